@@ -1,0 +1,84 @@
+"""Generate the golden fixtures that pin the CPU oracle.
+
+The reference (Swift over mlx-swift) cannot run on the machines this library is built
+on, and it ships no golden vectors.  These fixtures therefore come from HuggingFace
+``transformers``' MoonshineStreamingForConditionalGeneration -- an independent
+implementation of the same architecture that loads the same checkpoint layout -- run
+in float64 with eager attention on seeded random-init weights and seeded synthetic
+audio.  They cover the frontend, the sliding-window encoder, memory preparation and
+teacher-forced decoder logits with an fp32 KV cache.
+
+Run from the repository root:  python tests/golden/make_golden.py
+"""
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "moonshine-mlx_b200"))
+
+from moonshine_b200 import synth  # noqa: E402
+
+# (name, arch, overrides, weight seed, audio samples, audio seed, teacher-forced ids)
+CASES = [
+    ("hf_tiny", "tiny", {}, 0, 32000, 7, [1, 5, 900, 12384, 77, 2, 31000, 4]),
+    ("hf_small_v2048", "small", {"vocab_size": 2048, "max_position_embeddings": 512},
+     2, 24000, 8, [1, 9, 2047, 3, 2, 1000]),
+]
+
+N_PROBE = 256  # logits kept per step at fixed probe indices (keeps fixtures small)
+
+
+def run_case(name, arch, overrides, seed, n_samples, audio_seed, teacher):
+    import torch
+    from transformers import (MoonshineStreamingConfig,
+                              MoonshineStreamingForConditionalGeneration)
+
+    cfg = synth.make_config(arch, **overrides)
+    w = synth.make_weights(cfg, seed)
+    hcfg = dict(cfg)
+    enc = hcfg.pop("encoder_config")
+    hc = MoonshineStreamingConfig(encoder_config=enc, **{k: v for k, v in hcfg.items()
+                                                         if k not in ("model_type",)})
+    hc.num_key_value_heads = cfg["num_key_value_heads"]
+    hc._attn_implementation = "eager"
+    model = MoonshineStreamingForConditionalGeneration(hc).double().eval()
+    sd = {k: torch.from_numpy(np.asarray(v, dtype=np.float64)) for k, v in w.items()}
+    missing, unexpected = model.load_state_dict(sd, strict=False)
+    missing = [m for m in missing if not m.endswith("rotary_emb.inv_freq")]
+    assert not missing and not unexpected, (missing, unexpected)
+
+    audio = synth.synth_audio(n_samples, audio_seed)
+    with torch.no_grad():
+        x = torch.from_numpy(audio.astype(np.float64))[None]
+        # HF applies the per-layer sliding windows only when a padding mask is given
+        am = torch.ones(x.shape, dtype=torch.long)
+        enc_out = model.model.encoder(input_values=x, attention_mask=am).last_hidden_state
+        memory = enc_out[0].clone() + model.model.decoder.pos_emb.weight[: enc_out.shape[1]]
+        ids = torch.tensor([teacher], dtype=torch.long)
+        out = model(input_values=x, attention_mask=am, decoder_input_ids=ids, use_cache=False)
+        logits = out.logits[0].numpy()
+    V = logits.shape[1]
+    probe = np.random.Generator(np.random.PCG64(1234)).choice(V, size=N_PROBE, replace=False)
+    probe.sort()
+    np.savez_compressed(
+        os.path.join(HERE, f"{name}.npz"),
+        arch=arch, seed=seed, n_samples=n_samples, audio_seed=audio_seed,
+        overrides_vocab=overrides.get("vocab_size", 32768),
+        overrides_maxpos=overrides.get("max_position_embeddings", 4096),
+        teacher=np.asarray(teacher, dtype=np.int64),
+        memory=memory.numpy().astype(np.float32),
+        probe=probe.astype(np.int64),
+        logits_probe=logits[:, probe].astype(np.float64),
+        argmax=logits.argmax(axis=1).astype(np.int64),
+        lmax=logits.max(axis=1), lmin=logits.min(axis=1), lmean=logits.mean(axis=1),
+    )
+    print(name, "memory", tuple(memory.shape), "steps", logits.shape[0],
+          "argmax", logits.argmax(axis=1).tolist())
+
+
+if __name__ == "__main__":
+    for c in CASES:
+        run_case(*c)
