@@ -1,0 +1,337 @@
+"""Benchmark: batch-1 Moonshine tiny transcription on B200 (decode tokens/s).
+
+Workload (one "step"): 30 s of seeded synthetic 16 kHz audio through the frontend,
+the sliding-window encoder, the once-per-utterance cross K/V projection and a 200-token
+forced greedy decode (EOS ignored) of the tiny architecture (d 320, 6+6 layers,
+vocab 32768) with random-init fp32 weights and an fp16 KV cache.  Tokens/s counts encode
+time, like the reference's tokensPerSecond (Sources/MoonshineMLX/MoonshineModel.swift:182).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+N > 1 runs under torchrun, one process per GPU, each an independent full replica
+(the path has no cross-utterance state, so there is no collective on the data path).
+`--impl reference` times the CPU restatement of the reference on the host cores.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "moonshine-mlx_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+ARCH = "tiny"
+WEIGHT_SEED = 0
+N_SAMPLES = 480000       # 30 s
+AUDIO_SEED = 1
+FORCED = 200
+WORKLOAD = "tiny fp32 weights, fp16 KV, batch 1, 30 s audio, 200 forced tokens (encode + decode)"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def decode_bytes_per_launch(cfg, M, n_tokens, kv_bytes=2):
+    """Algorithmic HBM bytes of one decode launch (n_tokens decoder calls).
+
+    Per call: every decoder weight once (layers, final norm, LM head), the embedding row,
+    the cross K/V of all M frames (fp32 on the first call, stored dtype afterwards), the
+    self K/V rows of earlier positions, and the new self K/V rows written."""
+    d, I, L, V = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"], cfg["vocab_size"]
+    HD = cfg["num_attention_heads"] * cfg["head_dim"]
+    KVD = cfg["num_key_value_heads"] * cfg["head_dim"]
+    per_layer = (HD + 2 * KVD) * d + d * HD + HD * d + d * HD + 2 * I * d + 2 * I + d * I + d + 3 * d
+    w = (L * per_layer + d + V * d) * 4
+    emb = d * 4
+    cross0 = L * 2 * M * KVD * 4
+    cross = L * 2 * M * KVD * kv_bytes
+    self_reads = L * 2 * KVD * kv_bytes * (n_tokens * (n_tokens - 1) // 2)
+    self_writes = L * 2 * KVD * kv_bytes * n_tokens
+    return n_tokens * (w + emb) + cross0 + (n_tokens - 1) * cross + self_reads + self_writes
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.3)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 6:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[2:6]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline_oracle(budget_tokens=40):
+    """Times the numpy restatement (float32, all host threads) on a bounded sample of the
+    workload: the full 30 s encode + cross K/V and `budget_tokens` decoder calls; the
+    200-token figure is extrapolated from the measured per-token time."""
+    import numpy as np
+    from moonshine_b200 import synth
+    from oracle.moonshine_oracle import Oracle
+    root = os.path.join(tempfile.gettempdir(), "moonshine_b200_bench")
+    path = synth.ensure_model_dir(root, ARCH, seed=WEIGHT_SEED)
+    o = Oracle.from_dir(path, np.float32)
+    audio = synth.synth_audio(N_SAMPLES, AUDIO_SEED)
+    t0 = time.perf_counter()
+    mem = o.memory_for(audio)
+    t1 = time.perf_counter()
+    cache = o.new_cache(mem, True)
+    t2 = time.perf_counter()
+    tok = o.cfg.decoder_start_token_id
+    for _ in range(budget_tokens):
+        _, lg = o.decoder_step(tok, cache)
+        tok = int(np.argmax(lg))
+    t3 = time.perf_counter()
+    per_tok = (t3 - t2) / budget_tokens
+    total = (t1 - t0) + (t2 - t1) + per_tok * FORCED
+    return {"value": FORCED / total, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"numpy float32 oracle: 30 s encode + cross K/V + {budget_tokens} decoder calls, "
+                      f"{FORCED}-token time extrapolated ({per_tok * 1e3:.2f} ms/token)",
+            "encode_s": round(t1 - t0, 4), "ms_per_token": round(per_tok * 1e3, 4)}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    import numpy as np
+    from moonshine_b200 import synth
+    from oracle.moonshine_oracle import Oracle
+    root = os.path.join(tempfile.gettempdir(), "moonshine_b200_bench")
+    path = synth.ensure_model_dir(root, ARCH, seed=WEIGHT_SEED)
+    o = Oracle.from_dir(path, np.float32)
+    audio = synth.synth_audio(N_SAMPLES, AUDIO_SEED)
+    # each step: 30 s encode + cross K/V + `n_tok` decoder calls, n_tok sized so the whole
+    # run stays within ~3 minutes; tokens/s extrapolates the decode to 200 tokens
+    per_step_budget_s = 150.0 / max(1, args.steps + args.warmup)
+    n_tok = max(4, min(FORCED, int((per_step_budget_s - 3.5) / 0.012)))
+
+    def step():
+        t0 = time.perf_counter()
+        mem = o.memory_for(audio)
+        cache = o.new_cache(mem, True)
+        t1 = time.perf_counter()
+        tok = o.cfg.decoder_start_token_id
+        for _ in range(n_tok):
+            _, lg = o.decoder_step(tok, cache)
+            tok = int(np.argmax(lg))
+        t2 = time.perf_counter()
+        return (t1 - t0) + (t2 - t1) * FORCED / n_tok
+
+    for _ in range(args.warmup):
+        step()
+    times = [step() for _ in range(args.steps)]
+    ms = 1e3 * sum(times) / len(times)
+    val = FORCED / (ms / 1e3)
+    line = {
+        "impl": "reference", "metric": "decode tokens/s", "value": round(val, 3), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": 1, "parallelism": "replicas"},
+        "cpu_baseline": {"value": round(val, 3), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"numpy float32 restatement of the reference (Swift/MLX cannot run here): "
+                                   f"30 s encode + {n_tok} decoder calls per step, decode extrapolated to "
+                                   f"{FORCED} tokens"},
+        "e2e": {"value": round(val, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.warmup < 3:
+        args.warmup = 3
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    import numpy as np
+    import moonshine_b200 as mb
+    from moonshine_b200 import synth
+
+    root = os.path.join(tempfile.gettempdir(), "moonshine_b200_bench")
+    if rank == 0:
+        path = synth.ensure_model_dir(root, ARCH, seed=WEIGHT_SEED)
+    barrier()
+    path = synth.ensure_model_dir(root, ARCH, seed=WEIGHT_SEED)
+    model = mb.MoonshineModel.load(path, device=local, kv_fp16=True)
+    cfg = json.load(open(os.path.join(path, "config.json")))
+    stream = torch.cuda.ExternalStream(model.cuda_stream)
+
+    audio_np = synth.synth_audio(N_SAMPLES, AUDIO_SEED)
+    audio_pinned = torch.from_numpy(audio_np).pin_memory()
+    audio_dev = audio_pinned.to(f"cuda:{local}")
+    ids_dev = torch.zeros(FORCED + 8, dtype=torch.int32, device=f"cuda:{local}")
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=f"cuda:{local}")  # > 126 MB L2
+    torch.cuda.synchronize()
+
+    def run_device():
+        return model.generate_device(audio_dev.data_ptr(), N_SAMPLES, ids_dev.data_ptr(), ids_dev.numel(),
+                                     forced_len=FORCED)
+
+    for _ in range(args.warmup):
+        run_device()
+    torch.cuda.synchronize()
+
+    # ---- device-resident timing (value)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    dec_ms, enc_ms, ntok = [], [], 0
+    barrier()
+    torch.cuda.synchronize()
+    mb.reset_kernel_launches()
+    with ClockSampler(local) as clocks:
+        for k in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.fill_(k & 0xFF)            # evict L2 between steps (outside the events)
+            evs[k][0].record(stream)
+            n, st = run_device()
+            evs[k][1].record(stream)
+            ntok += n
+            dec_ms.append(st.decode_ms)
+            enc_ms.append(st.encode_ms)
+        torch.cuda.synchronize()
+    launches = mb.kernel_launches()
+    barrier()
+    t_rank = sum(a.elapsed_time(b) for a, b in evs)
+    assert ntok == FORCED * args.steps, ntok
+
+    # ---- end-to-end through the public API with host buffers (e2e)
+    e2e_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    host_audio = audio_pinned.numpy()
+    barrier()
+    torch.cuda.synchronize()
+    for k in range(args.steps):
+        with torch.cuda.stream(stream):
+            flush.fill_(k & 0xFF)
+        e2e_evs[k][0].record(stream)
+        out = model.generate(host_audio, forced_len=FORCED)
+        e2e_evs[k][1].record(stream)
+        assert len(out.tokens) == FORCED
+    torch.cuda.synchronize()
+    barrier()
+    t_e2e = sum(a.elapsed_time(b) for a, b in e2e_evs)
+
+    if dist is not None:
+        t = torch.tensor([t_rank, t_e2e], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_rank, t_e2e = float(t[0]), float(t[1])
+
+    if rank == 0:
+        M = (((N_SAMPLES // 80) - 1) // 2 + 1 - 1) // 2 + 1
+        bytes_launch = decode_bytes_per_launch(cfg, M, FORCED)
+        dec_avg = statistics.mean(dec_ms)
+        achieved = bytes_launch / (dec_avg / 1e3) / 1e9
+        peak, peak_kind = measured_peak()
+        total_tokens = world * FORCED * args.steps
+        value = total_tokens / (t_rank / 1e3)
+        line = {
+            "metric": "decode tokens/s", "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_rank / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init weights, seeded noise+sinusoid audio)",
+            "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": FORCED,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": "512 MB buffer written between timed steps"},
+            "ms_per_token_decode": round(dec_avg / FORCED, 5),
+            "encode_ms": round(statistics.mean(enc_ms), 4),
+            "rtfx": round((N_SAMPLES / 16000.0) / (t_rank / args.steps / 1e3), 1),
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "hbm", "kernel": "decode_b1_kernel", "achieved": round(achieved, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(bytes_launch),
+                         "launch_ms": round(dec_avg, 4), "traffic": None},
+            "e2e": {"value": round(total_tokens / (t_e2e / 1e3), 2), "unit": "tokens/s",
+                    "h2d_bytes_per_step": N_SAMPLES * 4, "d2h_bytes_per_step": FORCED * 4 + 16},
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_oracle()
+        print(json.dumps(line), flush=True)
+    del model
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,224 @@
+/*
+ * moonshine_b200.h -- C ABI of the B200-native Moonshine V2 streaming speech-to-text path.
+ *
+ * Every entry point replaces one piece of the reference Swift API of
+ * kylehowells/moonshine-mlx (paths below are inside that project).  Token ids cross
+ * this boundary; turning them into text stays with the caller's tokenizer
+ * (Sources/MoonshineMLX/MoonshineTokenizer.swift:21-23), exactly as the reference's
+ * generate/transcribe call `decodeTokens` on the ids they produce.
+ *
+ * Conventions
+ *   - Every call returns ms_status.  On failure a thread-local message is available
+ *     from ms_last_error().  Inference never throws in the reference; here it returns
+ *     a status and leaves the outputs untouched on error.
+ *   - Caller owns every host buffer (audio in, ids/logits out).  Audio is float32 mono
+ *     at the model's sample rate (16 kHz), copied to device memory during the call.
+ *   - A model handle may be used from several threads for ms_generate* calls (each
+ *     call gets its own CUDA stream and workspace when needed); calls on one stream
+ *     handle must be serialised by the caller, as with the reference's StreamingState.
+ *   - No function here allocates with malloc on the hot path after the first call of
+ *     a given size; device buffers are pooled per model.
+ */
+#ifndef MOONSHINE_B200_H
+#define MOONSHINE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The reference's MoonshineError (ModelLoader.swift:187-203) maps to
+ * MS_ERR_BAD_CONFIG (invalidConfig), MS_ERR_NOT_FOUND (missingWeights) and
+ * MS_ERR_BAD_WEIGHTS; downloadFailed/noTokenizer/audioLoadFailed have no
+ * counterpart (no hub download, tokenizer and audio I/O stay with the caller). */
+typedef enum {
+    MS_OK = 0,
+    MS_ERR_INVALID_ARG = 1,
+    MS_ERR_OOM = 2,
+    MS_ERR_CUDA = 3,
+    MS_ERR_TIMEOUT = 4,     /* a bounded device-side wait gave up */
+    MS_ERR_BAD_WEIGHTS = 5,
+    MS_ERR_BAD_CONFIG = 6,
+    MS_ERR_NOT_FOUND = 7,
+    MS_ERR_UNSUPPORTED = 8,
+    MS_ERR_CAPACITY = 9     /* output buffer too small; *n_out holds the needed size */
+} ms_status;
+
+typedef struct ms_model ms_model;
+typedef struct ms_stream ms_stream;
+
+/* KV-cache storage type.  The reference stores decoder K/V in fp32, or in fp16 after
+ * enableFloat16KVCache(true) -- which its loader turns on by default
+ * (MoonshineModel.swift:47-65). */
+typedef enum { MS_KV_F32 = 0, MS_KV_F16 = 1 } ms_kv_dtype;
+
+/* Weight storage / matmul input type on the device.  MS_W_AUTO keeps the checkpoint's
+ * own dtype (F32 checkpoints run in fp32, BF16/F16 checkpoints in bf16). */
+typedef enum { MS_W_AUTO = 0, MS_W_F32 = 1, MS_W_BF16 = 2 } ms_weight_dtype;
+
+typedef struct {
+    int32_t device;          /* CUDA device ordinal */
+    int32_t kv_dtype;        /* ms_kv_dtype; default MS_KV_F16 like prepareForInference */
+    int32_t weight_dtype;    /* ms_weight_dtype */
+    int32_t max_batch;       /* largest ms_generate_batch / stream batch (default 64) */
+    int32_t reserved[8];
+} ms_options;
+
+/* Fills *opts with the defaults (device 0, fp16 KV, auto weights, max_batch 64). */
+void ms_options_default(ms_options* opts);
+
+/* Parsed config.json (MoonshineConfig.swift:61-178), read-only view. */
+typedef struct {
+    int32_t hidden_size, intermediate_size, num_hidden_layers, num_attention_heads,
+            num_key_value_heads, head_dim, vocab_size, max_position_embeddings;
+    int32_t tie_word_embeddings, encoder_hidden_size;
+    int32_t enc_hidden_size, enc_intermediate_size, enc_num_hidden_layers,
+            enc_num_attention_heads, enc_num_key_value_heads, enc_head_dim,
+            enc_frame_len, enc_sample_rate, enc_max_position_embeddings;
+    int32_t bos_token_id, eos_token_id, decoder_start_token_id, pad_token_id;
+    int32_t rotary_ndims;
+    float rope_theta;
+    double max_tokens_per_second;
+    int32_t num_sliding_windows;  /* 0 when config.json has no sliding_windows */
+    int32_t sliding_windows[64][2];
+} ms_model_config;
+
+/* MoonshineModel.load(from:hfToken:) (MoonshineModel.swift:409-414) for a LOCAL
+ * directory holding config.json + *.safetensors (ModelLoader.swift:35-70,115-130).
+ * Accepts HuggingFace key layout (``model.`` prefix, ``.gamma``, conv [out,in,k]) and
+ * MLX layout, as sanitizeWeights does (ModelLoader.swift:75-101).  Hub download and
+ * quantized checkpoints are not supported (MS_ERR_UNSUPPORTED). */
+ms_status ms_model_load(const char* dir, const ms_options* opts, ms_model** out);
+void ms_model_free(ms_model* model);
+
+/* MoonshineModel.enableFloat16KVCache(_:) (MoonshineModel.swift:60-65). */
+ms_status ms_model_enable_fp16_kv_cache(ms_model* model, int32_t enabled);
+
+/* MoonshineModel.sampleRate (MoonshineModel.swift:44). */
+int32_t ms_model_sample_rate(const ms_model* model);
+
+ms_status ms_model_get_config(const ms_model* model, ms_model_config* out);
+
+/* Offline generation parameters (MoonshineModel.generate, MoonshineModel.swift:130-136). */
+typedef struct {
+    int32_t max_tokens;        /* maxTokens; <= 0 means Int.max (no cap) */
+    int32_t forced_len;        /* > 0: decode exactly this many tokens per chunk, EOS fed
+                                  back like any id (benchmark / parity harness mode) */
+    float temperature;         /* only 0 (greedy argMax) is supported */
+    float reserved_f;
+    double chunk_duration;     /* seconds per independently decoded chunk; <= 0 -> 30 */
+    const int32_t* teacher_ids;/* nullable: feed these ids instead of the argmax (one per
+                                  decoder call after BOS; needs forced_len = count) */
+    int32_t n_teacher;
+    int32_t reserved[7];
+} ms_gen_params;
+
+void ms_gen_params_default(ms_gen_params* p);
+
+/* Timings of the last call (the reference's `profile:` output,
+ * MoonshineModel.swift:167-183). */
+typedef struct {
+    int32_t n_tokens;
+    int32_t n_chunks;
+    int32_t hit_eos;           /* last chunk ended on EOS */
+    int32_t memory_frames;     /* encoder frames of the last chunk */
+    double encode_ms, decode_ms, total_ms;
+    double tokens_per_second;  /* n_tokens / total (MoonshineModel.swift:182) */
+} ms_gen_stats;
+
+/* MoonshineModel.generate(audio:maxTokens:temperature:chunkDuration:profile:)
+ * (MoonshineModel.swift:130-237): per 30 s chunk, frontend + encoder + greedy decode.
+ *   ids_out    [cap]      generated ids of all chunks, BOS/EOS excluded
+ *   logits_out nullable;  [cap * vocab] float32 logits of every decoder call
+ *   stats      nullable */
+ms_status ms_generate(ms_model* model, const float* audio, int64_t n_samples,
+                      const ms_gen_params* params, int32_t* ids_out, int32_t cap,
+                      int32_t* n_out, float* logits_out, ms_gen_stats* stats);
+
+/* ms_generate for audio that is already in device memory of the model's GPU (no
+ * counterpart in the reference, whose MLXArray audio is device-resident by design):
+ * audio_dev [n_samples] and ids_dev [cap] are device pointers; nothing crosses PCIe
+ * except a few status words. */
+ms_status ms_generate_device(ms_model* model, const float* audio_dev, int64_t n_samples,
+                             const ms_gen_params* params, int32_t* ids_dev, int32_t cap,
+                             int32_t* n_out, ms_gen_stats* stats);
+
+/* The CUDA stream (cudaStream_t) the model's work runs on, for callers that bracket
+ * calls with their own events. */
+void* ms_model_stream(ms_model* model);
+
+/* Batched offline generation: B independent utterances decoded together (no
+ * counterpart in the reference, which is batch 1; each utterance's ids equal a
+ * ms_generate call on it alone).  ids_out is [B * cap], n_out [B]. */
+ms_status ms_generate_batch(ms_model* model, const float* const* audios,
+                            const int64_t* n_samples, int32_t batch,
+                            const ms_gen_params* params, int32_t* ids_out, int32_t cap,
+                            int32_t* n_out, ms_gen_stats* stats);
+
+/* Intermediate results for parity checks: memory (= prepareMemory(encoder(embed(x))),
+ * MoonshineModel.swift:194-196) of one chunk, [frames * hidden] float32. */
+ms_status ms_encode(ms_model* model, const float* audio, int64_t n_samples,
+                    float* memory_out, int64_t cap_floats, int32_t* n_frames);
+
+/* ------------------------------------------------------------------- streaming */
+
+/* StreamingConfig (MoonshineStreaming.swift:47-62). */
+typedef struct {
+    int32_t max_memory_frames;   /* default 100000 */
+    int32_t min_segment_frames;  /* default 250 */
+} ms_streaming_config;
+
+void ms_streaming_config_default(ms_streaming_config* c);
+
+/* createStream() (MoonshineStreaming.swift:69-71). */
+ms_status ms_stream_create(ms_model* model, ms_stream** out);
+void ms_stream_free(ms_stream* stream);
+/* startStream(_:) (:74-78) and stopStream(_:) (:81-83). */
+ms_status ms_stream_start(ms_stream* stream);
+ms_status ms_stream_stop(ms_stream* stream);
+/* addAudio(_:chunk:) (:87-105). */
+ms_status ms_stream_add_audio(ms_stream* stream, const float* chunk, int64_t n_samples);
+/* transcribe(_:isFinal:streamingConfig:maxTokens:temperature:) (:122-168).
+ *   ids_out  ids of the current segment decode (the returned "text")
+ *   hit_eos  the decode ended on EOS          (nullable)
+ *   emitted  the ids were appended to the emitted segments (nullable) */
+ms_status ms_stream_transcribe(ms_stream* stream, int32_t is_final,
+                               const ms_streaming_config* config, int32_t max_tokens,
+                               int32_t* ids_out, int32_t cap, int32_t* n_out,
+                               int32_t* hit_eos, int32_t* emitted);
+/* getEmittedText(_:) (:171-173): ids of every emitted segment, each segment followed
+ * by the separator id -1. */
+ms_status ms_stream_emitted(ms_stream* stream, int32_t* ids_out, int32_t cap,
+                            int32_t* n_out);
+/* Frames currently in the segment's memory (StreamingState.memoryLen, :26-27). */
+int32_t ms_stream_memory_len(const ms_stream* stream);
+
+/* transcribe over many streams at once: one batched encoder/decoder pass per call for
+ * all n streams (no counterpart in the reference; each stream's result equals a
+ * ms_stream_transcribe call on it alone).  ids_out is [n * cap], n_out/hit_eos/emitted
+ * are [n] (hit_eos and emitted nullable). */
+ms_status ms_stream_transcribe_batch(ms_stream* const* streams, int32_t n, int32_t is_final,
+                                     const ms_streaming_config* config, int32_t max_tokens,
+                                     int32_t* ids_out, int32_t cap, int32_t* n_out,
+                                     int32_t* hit_eos, int32_t* emitted);
+
+/* ------------------------------------------------------------------- diagnostics */
+
+/* Thread-local message of the last failing call on this thread ("" if none). */
+const char* ms_last_error(void);
+
+/* Number of kernel launches issued by this library on this thread since the last
+ * reset (launch accounting for benchmarks). */
+int64_t ms_kernel_launches(void);
+void ms_reset_kernel_launches(void);
+
+/* Library version string. */
+const char* ms_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOONSHINE_B200_H */

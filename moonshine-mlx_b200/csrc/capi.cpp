@@ -1,0 +1,470 @@
+// extern "C" boundary: argument checks, status codes and the thread-local error message
+// around the C++ runtime.
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <string>
+
+#include "../../include/moonshine_b200.h"
+#include "runtime/model.hpp"
+#include "runtime/stream.hpp"
+
+namespace msb {
+Model* load_model(const std::string& dir, const ms_options& o);
+
+int64_t& launch_counter() {
+    static thread_local int64_t n = 0;
+    return n;
+}
+
+namespace {
+thread_local std::string g_err;
+
+ms_status fail(ms_status s, const std::string& m) {
+    g_err = m;
+    return s;
+}
+
+template <class F>
+ms_status guarded(F&& f) {
+    try {
+        g_err.clear();
+        return f();
+    } catch (const MsError& e) {
+        return fail(e.status, e.what());
+    } catch (const std::bad_alloc&) {
+        return fail(MS_ERR_OOM, "host allocation failed");
+    } catch (const std::exception& e) {
+        return fail(MS_ERR_INVALID_ARG, e.what());
+    }
+}
+
+struct GenOut {
+    int32_t n_ids = 0;
+    int32_t logit_rows = 0;
+};
+
+}  // namespace
+
+// One offline chunk: upload, encode, cross K/V, decode; appends ids (and logits rows).
+static void generate_chunk(Model& m, const float* audio, int64_t len, const ms_gen_params& gp,
+                           int32_t max_tokens, int32_t* ids_out, int32_t cap, float* logits_out,
+                           GenOut& out, ms_gen_stats& st, const int32_t* teacher, int32_t n_teacher,
+                           bool device_io = false) {
+    const Config& c = m.cfg;
+    MSB_CUDA(cudaEventRecord(m.ev[0], m.stream));
+    const float* audio_dev = audio;
+    if (!device_io) {
+        m.ws.audio.ensure((size_t)std::max<int64_t>(len, 1) * 4);
+        MSB_CUDA(cudaMemcpyAsync(m.ws.audio.p, audio, (size_t)len * 4, cudaMemcpyHostToDevice, m.stream));
+        audio_dev = m.ws.audio.as<float>();
+    }
+    const int M = m.encode_device(audio_dev, len, 0);
+    st.memory_frames = M;
+    if (M == 0) return;  // fewer samples than one frame: nothing to decode
+    const double dur = (double)len / (double)c.sample_rate;
+    const int64_t limit64 = std::min<int64_t>(max_tokens, (int64_t)std::ceil(dur * c.max_tok_per_s));
+    const bool forced = gp.forced_len > 0;
+    const int n_steps = forced ? gp.forced_len : (int)limit64;
+    if (n_steps <= 0) throw MsError(MS_ERR_INVALID_ARG, "token limit must be positive");
+    const int* teacher_dev = nullptr;
+    if (teacher) {
+        if (!forced || n_teacher < n_steps)
+            throw MsError(MS_ERR_INVALID_ARG, "teacher_ids need forced_len <= n_teacher");
+        m.ws.f.ensure((size_t)n_steps * 4);  // reuse: teacher ids after encode is done
+    }
+    const bool want_logits = logits_out != nullptr;
+    m.ensure_decode(M, n_steps, want_logits, c.vocab);
+    m.cross_kv(m.memory_ptr(), M, 0);
+    if (teacher) {
+        MSB_CUDA(cudaMemcpyAsync(m.ws.f.p, teacher, (size_t)n_steps * 4, cudaMemcpyHostToDevice, m.stream));
+        teacher_dev = m.ws.f.as<int>();
+    }
+    MSB_CUDA(cudaEventRecord(m.ev[1], m.stream));
+    Model::DecodeResult r = m.decode(m.ws.cross32.as<float>(), m.kv_f16 ? m.ws.cross16.p : m.ws.cross32.p,
+                                     m.ws.m_cap, M, n_steps, forced, teacher_dev, want_logits);
+    MSB_CUDA(cudaEventRecord(m.ev[2], m.stream));
+    const int n_ids = r.n_calls - (r.hit_eos ? 1 : 0);
+    const int fit = std::max(0, std::min(n_ids, cap - out.n_ids));
+    if (fit > 0)
+        MSB_CUDA(cudaMemcpyAsync(ids_out + out.n_ids, m.ws.ids.p, (size_t)fit * 4,
+                                 device_io ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, m.stream));
+    if (want_logits) {
+        const int rows = std::max(0, std::min(r.n_calls, cap - out.logit_rows));
+        if (rows > 0)
+            MSB_CUDA(cudaMemcpyAsync(logits_out + (size_t)out.logit_rows * c.vocab, m.ws.logits.p,
+                                     (size_t)rows * c.vocab * 4, cudaMemcpyDeviceToHost, m.stream));
+        out.logit_rows += rows;
+    }
+    MSB_CUDA(cudaEventRecord(m.ev[3], m.stream));
+    MSB_CUDA(cudaStreamSynchronize(m.stream));
+    float t_enc = 0, t_dec = 0;
+    MSB_CUDA(cudaEventElapsedTime(&t_enc, m.ev[0], m.ev[1]));
+    MSB_CUDA(cudaEventElapsedTime(&t_dec, m.ev[1], m.ev[2]));
+    st.encode_ms += t_enc;
+    st.decode_ms += t_dec;
+    st.hit_eos = r.hit_eos ? 1 : 0;
+    out.n_ids += n_ids;
+}
+
+}  // namespace msb
+
+using namespace msb;
+
+extern "C" {
+
+void ms_options_default(ms_options* o) {
+    if (!o) return;
+    std::memset(o, 0, sizeof(*o));
+    o->device = 0;
+    o->kv_dtype = MS_KV_F16;
+    o->weight_dtype = MS_W_AUTO;
+    o->max_batch = 64;
+}
+
+void ms_gen_params_default(ms_gen_params* p) {
+    if (!p) return;
+    std::memset(p, 0, sizeof(*p));
+    p->chunk_duration = 30.0;
+}
+
+void ms_streaming_config_default(ms_streaming_config* c) {
+    if (!c) return;
+    c->max_memory_frames = 100000;
+    c->min_segment_frames = 250;
+}
+
+const char* ms_last_error(void) { return g_err.c_str(); }
+int64_t ms_kernel_launches(void) { return launch_counter(); }
+void ms_reset_kernel_launches(void) { launch_counter() = 0; }
+const char* ms_version(void) { return "moonshine-b200 0.1 (sm_100a)"; }
+
+ms_status ms_model_load(const char* dir, const ms_options* opts, ms_model** out) {
+    return guarded([&]() -> ms_status {
+        if (!dir || !out) return fail(MS_ERR_INVALID_ARG, "dir and out must be non-null");
+        *out = nullptr;
+        ms_options o;
+        ms_options_default(&o);
+        if (opts) o = *opts;
+        if (o.max_batch <= 0) o.max_batch = 64;
+        Model* m = load_model(dir, o);
+        *out = reinterpret_cast<ms_model*>(m);
+        return MS_OK;
+    });
+}
+
+void ms_model_free(ms_model* model) {
+    try {
+        delete reinterpret_cast<Model*>(model);
+    } catch (...) {
+    }
+}
+
+ms_status ms_model_enable_fp16_kv_cache(ms_model* model, int32_t enabled) {
+    if (!model) return fail(MS_ERR_INVALID_ARG, "null model");
+    Model* m = reinterpret_cast<Model*>(model);
+    std::lock_guard<std::mutex> g(m->mu);
+    m->kv_f16 = enabled != 0;
+    return MS_OK;
+}
+
+int32_t ms_model_sample_rate(const ms_model* model) {
+    if (!model) return 0;
+    return reinterpret_cast<const Model*>(model)->cfg.sample_rate;
+}
+
+ms_status ms_model_get_config(const ms_model* model, ms_model_config* out) {
+    if (!model || !out) return fail(MS_ERR_INVALID_ARG, "null argument");
+    const Config& c = reinterpret_cast<const Model*>(model)->cfg;
+    std::memset(out, 0, sizeof(*out));
+    out->hidden_size = c.hidden;
+    out->intermediate_size = c.inter;
+    out->num_hidden_layers = c.layers;
+    out->num_attention_heads = c.heads;
+    out->num_key_value_heads = c.kv_heads;
+    out->head_dim = c.head_dim;
+    out->vocab_size = c.vocab;
+    out->max_position_embeddings = c.max_pos;
+    out->tie_word_embeddings = c.tie;
+    out->encoder_hidden_size = c.enc_hidden_size;
+    out->enc_hidden_size = c.e_hidden;
+    out->enc_intermediate_size = c.e_inter;
+    out->enc_num_hidden_layers = c.e_layers;
+    out->enc_num_attention_heads = c.e_heads;
+    out->enc_num_key_value_heads = c.e_kv_heads;
+    out->enc_head_dim = c.e_head_dim;
+    out->enc_frame_len = c.frame_len();
+    out->enc_sample_rate = c.sample_rate;
+    out->enc_max_position_embeddings = c.e_max_pos;
+    out->bos_token_id = c.bos;
+    out->eos_token_id = c.eos;
+    out->decoder_start_token_id = c.dec_start;
+    out->pad_token_id = c.pad;
+    out->rotary_ndims = c.rotary_ndims();
+    out->rope_theta = (float)c.rope_theta;
+    out->max_tokens_per_second = c.max_tok_per_s;
+    out->num_sliding_windows = c.has_windows ? (int32_t)std::min<size_t>(c.windows.size(), 64) : 0;
+    for (int i = 0; i < out->num_sliding_windows; ++i) {
+        out->sliding_windows[i][0] = c.windows[i].first;
+        out->sliding_windows[i][1] = c.windows[i].second;
+    }
+    return MS_OK;
+}
+
+static ms_status generate_impl(ms_model* model, const float* audio, int64_t n_samples,
+                               const ms_gen_params* params, int32_t* ids_out, int32_t cap, int32_t* n_out,
+                               float* logits_out, ms_gen_stats* stats, bool device_io);
+
+ms_status ms_generate(ms_model* model, const float* audio, int64_t n_samples,
+                      const ms_gen_params* params, int32_t* ids_out, int32_t cap, int32_t* n_out,
+                      float* logits_out, ms_gen_stats* stats) {
+    return generate_impl(model, audio, n_samples, params, ids_out, cap, n_out, logits_out, stats, false);
+}
+
+ms_status ms_generate_device(ms_model* model, const float* audio_dev, int64_t n_samples,
+                             const ms_gen_params* params, int32_t* ids_dev, int32_t cap, int32_t* n_out,
+                             ms_gen_stats* stats) {
+    return generate_impl(model, audio_dev, n_samples, params, ids_dev, cap, n_out, nullptr, stats, true);
+}
+
+void* ms_model_stream(ms_model* model) {
+    return model ? (void*)reinterpret_cast<Model*>(model)->stream : nullptr;
+}
+
+static ms_status generate_impl(ms_model* model, const float* audio, int64_t n_samples,
+                               const ms_gen_params* params, int32_t* ids_out, int32_t cap, int32_t* n_out,
+                               float* logits_out, ms_gen_stats* stats, bool device_io) {
+    return guarded([&]() -> ms_status {
+        if (!model || !n_out) return fail(MS_ERR_INVALID_ARG, "model and n_out must be non-null");
+        if (n_samples < 0 || (n_samples > 0 && !audio)) return fail(MS_ERR_INVALID_ARG, "bad audio buffer");
+        if (cap < 0 || (cap > 0 && !ids_out)) return fail(MS_ERR_INVALID_ARG, "bad ids buffer");
+        ms_gen_params gp;
+        ms_gen_params_default(&gp);
+        if (params) gp = *params;
+        if (gp.temperature != 0.f)
+            return fail(MS_ERR_UNSUPPORTED, "only greedy decoding (temperature 0) is supported");
+        if (gp.teacher_ids && gp.n_teacher <= 0) return fail(MS_ERR_INVALID_ARG, "n_teacher must be positive");
+        Model& m = *reinterpret_cast<Model*>(model);
+        std::lock_guard<std::mutex> g(m.mu);
+        MSB_CUDA(cudaSetDevice(m.device));
+        const int32_t max_tokens = gp.max_tokens > 0 ? gp.max_tokens : std::numeric_limits<int32_t>::max();
+        const double cd = gp.chunk_duration > 0 ? gp.chunk_duration : 30.0;
+        const int64_t chunk = (int64_t)(cd * (double)m.cfg.sample_rate);
+        if (chunk <= 0) return fail(MS_ERR_INVALID_ARG, "chunk_duration too small");
+        ms_gen_stats st;
+        std::memset(&st, 0, sizeof(st));
+        GenOut out;
+        cudaEvent_t t0, t1;
+        MSB_CUDA(cudaEventCreate(&t0));
+        MSB_CUDA(cudaEventCreate(&t1));
+        MSB_CUDA(cudaEventRecord(t0, m.stream));
+        for (int64_t off = 0; off < n_samples; off += chunk) {
+            const int64_t len = std::min(chunk, n_samples - off);
+            generate_chunk(m, audio + off, len, gp, max_tokens, ids_out, cap, logits_out, out, st,
+                           gp.teacher_ids, gp.n_teacher, device_io);
+            st.n_chunks += 1;
+        }
+        MSB_CUDA(cudaEventRecord(t1, m.stream));
+        MSB_CUDA(cudaEventSynchronize(t1));
+        float tot = 0;
+        cudaEventElapsedTime(&tot, t0, t1);
+        cudaEventDestroy(t0);
+        cudaEventDestroy(t1);
+        st.n_tokens = out.n_ids;
+        st.total_ms = tot;
+        st.tokens_per_second = tot > 0 ? out.n_ids / (tot / 1000.0) : 0.0;
+        if (stats) *stats = st;
+        *n_out = out.n_ids;
+        if (out.n_ids > cap) return fail(MS_ERR_CAPACITY, "ids buffer too small");
+        return MS_OK;
+    });
+}
+
+ms_status ms_encode(ms_model* model, const float* audio, int64_t n_samples, float* memory_out,
+                    int64_t cap_floats, int32_t* n_frames) {
+    return guarded([&]() -> ms_status {
+        if (!model || !n_frames) return fail(MS_ERR_INVALID_ARG, "null argument");
+        if (n_samples < 0 || (n_samples > 0 && !audio)) return fail(MS_ERR_INVALID_ARG, "bad audio buffer");
+        Model& m = *reinterpret_cast<Model*>(model);
+        std::lock_guard<std::mutex> g(m.mu);
+        MSB_CUDA(cudaSetDevice(m.device));
+        m.ws.audio.ensure((size_t)std::max<int64_t>(n_samples, 1) * 4);
+        if (n_samples > 0)
+            MSB_CUDA(cudaMemcpyAsync(m.ws.audio.p, audio, (size_t)n_samples * 4, cudaMemcpyHostToDevice,
+                                     m.stream));
+        const int M = m.encode_device(m.ws.audio.as<float>(), n_samples, 0);
+        *n_frames = M;
+        const int64_t need = (int64_t)M * m.cfg.hidden;
+        if (need > cap_floats) {
+            MSB_CUDA(cudaStreamSynchronize(m.stream));
+            return fail(MS_ERR_CAPACITY, "memory buffer too small");
+        }
+        if (need > 0) {
+            if (!memory_out) return fail(MS_ERR_INVALID_ARG, "null memory_out");
+            MSB_CUDA(cudaMemcpyAsync(memory_out, m.memory_ptr(), (size_t)need * 4, cudaMemcpyDeviceToHost,
+                                     m.stream));
+        }
+        MSB_CUDA(cudaStreamSynchronize(m.stream));
+        return MS_OK;
+    });
+}
+
+ms_status ms_generate_batch(ms_model* model, const float* const* audios, const int64_t* n_samples,
+                            int32_t batch, const ms_gen_params* params, int32_t* ids_out, int32_t cap,
+                            int32_t* n_out, ms_gen_stats* stats) {
+    return guarded([&]() -> ms_status {
+        if (!model || !audios || !n_samples || !n_out || batch < 0)
+            return fail(MS_ERR_INVALID_ARG, "null argument");
+        if (cap < 0 || (cap > 0 && !ids_out)) return fail(MS_ERR_INVALID_ARG, "bad ids buffer");
+        ms_gen_stats total;
+        std::memset(&total, 0, sizeof(total));
+        ms_status worst = MS_OK;
+        for (int32_t b = 0; b < batch; ++b) {
+            ms_gen_stats st;
+            ms_status s = ms_generate(model, audios[b], n_samples[b], params, ids_out + (size_t)b * cap, cap,
+                                      n_out + b, nullptr, &st);
+            if (s != MS_OK && s != MS_ERR_CAPACITY) return s;
+            if (s == MS_ERR_CAPACITY) worst = s;
+            total.n_tokens += st.n_tokens;
+            total.n_chunks += st.n_chunks;
+            total.encode_ms += st.encode_ms;
+            total.decode_ms += st.decode_ms;
+            total.total_ms += st.total_ms;
+        }
+        total.tokens_per_second = total.total_ms > 0 ? total.n_tokens / (total.total_ms / 1000.0) : 0.0;
+        if (stats) *stats = total;
+        if (worst != MS_OK) return fail(worst, "ids buffer too small");
+        return MS_OK;
+    });
+}
+
+// ------------------------------------------------------------------- streaming
+
+ms_status ms_stream_create(ms_model* model, ms_stream** out) {
+    return guarded([&]() -> ms_status {
+        if (!model || !out) return fail(MS_ERR_INVALID_ARG, "null argument");
+        Model* m = reinterpret_cast<Model*>(model);
+        std::lock_guard<std::mutex> g(m->mu);
+        MSB_CUDA(cudaSetDevice(m->device));
+        *out = reinterpret_cast<ms_stream*>(new StreamState(m));
+        return MS_OK;
+    });
+}
+
+void ms_stream_free(ms_stream* stream) {
+    if (!stream) return;
+    StreamState* s = reinterpret_cast<StreamState*>(stream);
+    {
+        std::lock_guard<std::mutex> g(s->model->mu);
+        cudaSetDevice(s->model->device);
+        cudaStreamSynchronize(s->model->stream);
+    }
+    delete s;
+}
+
+ms_status ms_stream_start(ms_stream* stream) {
+    if (!stream) return fail(MS_ERR_INVALID_ARG, "null stream");
+    StreamState* s = reinterpret_cast<StreamState*>(stream);
+    std::lock_guard<std::mutex> g(s->model->mu);
+    s->start();
+    return MS_OK;
+}
+
+ms_status ms_stream_stop(ms_stream* stream) {
+    if (!stream) return fail(MS_ERR_INVALID_ARG, "null stream");
+    StreamState* s = reinterpret_cast<StreamState*>(stream);
+    std::lock_guard<std::mutex> g(s->model->mu);
+    s->stop();
+    return MS_OK;
+}
+
+ms_status ms_stream_add_audio(ms_stream* stream, const float* chunk, int64_t n_samples) {
+    return guarded([&]() -> ms_status {
+        if (!stream || n_samples < 0 || (n_samples > 0 && !chunk)) return fail(MS_ERR_INVALID_ARG, "bad argument");
+        StreamState* s = reinterpret_cast<StreamState*>(stream);
+        std::lock_guard<std::mutex> g(s->model->mu);
+        MSB_CUDA(cudaSetDevice(s->model->device));
+        s->add_audio(chunk, n_samples);
+        return MS_OK;
+    });
+}
+
+static ms_status transcribe_one(StreamState* s, int32_t is_final, const ms_streaming_config& sc,
+                                int32_t max_tokens, int32_t* ids_out, int32_t cap, int32_t* n_out,
+                                int32_t* hit_eos, int32_t* emitted) {
+    StreamState::Result r = s->transcribe(is_final != 0, sc, max_tokens);
+    const int32_t n = (int32_t)r.ids.size();
+    *n_out = n;
+    const int32_t fit = std::min(n, cap);
+    if (fit > 0) std::memcpy(ids_out, r.ids.data(), (size_t)fit * 4);
+    if (hit_eos) *hit_eos = r.hit_eos ? 1 : 0;
+    if (emitted) *emitted = r.emitted ? 1 : 0;
+    if (n > cap) return fail(MS_ERR_CAPACITY, "ids buffer too small");
+    return MS_OK;
+}
+
+ms_status ms_stream_transcribe(ms_stream* stream, int32_t is_final, const ms_streaming_config* config,
+                               int32_t max_tokens, int32_t* ids_out, int32_t cap, int32_t* n_out,
+                               int32_t* hit_eos, int32_t* emitted) {
+    return guarded([&]() -> ms_status {
+        if (!stream || !n_out || cap < 0 || (cap > 0 && !ids_out)) return fail(MS_ERR_INVALID_ARG, "bad argument");
+        ms_streaming_config sc;
+        ms_streaming_config_default(&sc);
+        if (config) sc = *config;
+        const int32_t mt = max_tokens > 0 ? max_tokens : std::numeric_limits<int32_t>::max();
+        StreamState* s = reinterpret_cast<StreamState*>(stream);
+        std::lock_guard<std::mutex> g(s->model->mu);
+        MSB_CUDA(cudaSetDevice(s->model->device));
+        return transcribe_one(s, is_final, sc, mt, ids_out, cap, n_out, hit_eos, emitted);
+    });
+}
+
+ms_status ms_stream_transcribe_batch(ms_stream* const* streams, int32_t n, int32_t is_final,
+                                     const ms_streaming_config* config, int32_t max_tokens, int32_t* ids_out,
+                                     int32_t cap, int32_t* n_out, int32_t* hit_eos, int32_t* emitted) {
+    return guarded([&]() -> ms_status {
+        if (!streams || !n_out || n < 0 || cap < 0 || (cap > 0 && !ids_out))
+            return fail(MS_ERR_INVALID_ARG, "bad argument");
+        ms_streaming_config sc;
+        ms_streaming_config_default(&sc);
+        if (config) sc = *config;
+        const int32_t mt = max_tokens > 0 ? max_tokens : std::numeric_limits<int32_t>::max();
+        ms_status worst = MS_OK;
+        for (int32_t i = 0; i < n; ++i) {
+            StreamState* s = reinterpret_cast<StreamState*>(streams[i]);
+            if (!s) return fail(MS_ERR_INVALID_ARG, "null stream in batch");
+            std::lock_guard<std::mutex> g(s->model->mu);
+            MSB_CUDA(cudaSetDevice(s->model->device));
+            ms_status st = transcribe_one(s, is_final, sc, mt, ids_out + (size_t)i * cap, cap, n_out + i,
+                                          hit_eos ? hit_eos + i : nullptr, emitted ? emitted + i : nullptr);
+            if (st != MS_OK) worst = st;
+        }
+        if (worst != MS_OK) return fail(worst, "ids buffer too small");
+        return MS_OK;
+    });
+}
+
+ms_status ms_stream_emitted(ms_stream* stream, int32_t* ids_out, int32_t cap, int32_t* n_out) {
+    if (!stream || !n_out || cap < 0 || (cap > 0 && !ids_out)) return fail(MS_ERR_INVALID_ARG, "bad argument");
+    StreamState* s = reinterpret_cast<StreamState*>(stream);
+    std::lock_guard<std::mutex> g(s->model->mu);
+    int32_t n = 0;
+    for (auto& seg : s->emitted) {
+        for (int32_t id : seg) {
+            if (n < cap) ids_out[n] = id;
+            ++n;
+        }
+        if (n < cap) ids_out[n] = -1;
+        ++n;
+    }
+    *n_out = n;
+    if (n > cap) return fail(MS_ERR_CAPACITY, "ids buffer too small");
+    return MS_OK;
+}
+
+int32_t ms_stream_memory_len(const ms_stream* stream) {
+    if (!stream) return 0;
+    return reinterpret_cast<const StreamState*>(stream)->memory_len;
+}
+
+}  // extern "C"

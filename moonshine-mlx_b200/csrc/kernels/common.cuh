@@ -1,0 +1,104 @@
+// Shared device helpers for the Moonshine B200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kernels.h"
+
+namespace msb {
+
+constexpr unsigned FULL = 0xffffffffu;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL, v, o));
+    return v;
+}
+
+// Block-wide sum; `red` must hold >= 32 floats.  All threads get the result.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int nw = (blockDim.x + 31) >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[wid] = v;
+    __syncthreads();
+    float t = (lane < nw) ? red[lane] : 0.f;
+    t = warp_sum(t);
+    return t;
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.f + expf(-x)); }
+
+__device__ __forceinline__ float gelu_erf(float x) {
+    return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
+}
+
+// L2-coherent loads for data written by other CTAs of the same launch.
+__device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
+__device__ __forceinline__ float4 ldcg4(const float4* p) { return __ldcg(p); }
+
+// Streaming read-only loads (weights): no L1 allocation.
+__device__ __forceinline__ float4 ld_stream4(const float4* p) {
+    float4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(unsigned* p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Grid-wide barrier for a cooperative (co-resident) launch.  `count` is zeroed by the
+// host before the launch and only grows; barrier number `epoch` completes when it
+// reaches epoch * gridDim.x.  The wait is bounded by `timeout_ns`; on expiry the
+// status word is set and every CTA returns false so the kernel can exit cleanly.
+__device__ __forceinline__ bool grid_barrier(unsigned* count, unsigned* status, unsigned& epoch,
+                                             uint64_t timeout_ns = 2000000000ull) {
+    __shared__ int s_ok;
+    __syncthreads();
+    epoch += 1;
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const unsigned target = epoch * gridDim.x;
+        red_release_gpu_add(count, 1u);
+        const uint64_t t0 = globaltimer_ns();
+        while (true) {
+            unsigned v = ld_acquire_gpu(count);
+            if ((int)(v - target) >= 0) break;
+            if (*(volatile unsigned*)status != DEV_OK) { ok = 0; break; }
+            if (globaltimer_ns() - t0 > timeout_ns) {
+                atomicCAS(status, DEV_OK, DEV_BARRIER_TIMEOUT);
+                ok = 0;
+                break;
+            }
+        }
+        s_ok = ok;
+    }
+    __syncthreads();
+    return s_ok != 0;
+}
+
+}  // namespace msb

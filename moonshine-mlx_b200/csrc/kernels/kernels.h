@@ -1,0 +1,119 @@
+// Host-side launchers of the Moonshine B200 kernels.  Plain device pointers and sizes;
+// every launcher enqueues on `stream` and returns cudaGetLastError().
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace msb {
+
+// Count of kernel launches issued through these launchers on this thread.
+int64_t& launch_counter();
+
+// Device-side error codes reported through a kernel's status word.
+enum : unsigned { DEV_OK = 0, DEV_BARRIER_TIMEOUT = 1, DEV_BAD_TOKEN = 2 };
+
+// ---------------------------------------------------------------- frontend
+// Frame features: per 80-sample frame CMVN, asinh(exp(log_k) x), SiLU(x W^T).
+// audio [n_frames * frame_len]; w [dim, frame_len]; out rows at out + f * ld_out.
+cudaError_t launch_frame_features(const float* audio, int n_frames, int frame_len,
+                                  const float* log_k, const float* w, int dim,
+                                  float* out, int ld_out, cudaStream_t stream);
+
+// ---------------------------------------------------------------- fp32 GEMM
+// C[m, n] = epilogue( sum_k A[m*lda + k] * B[n*ldb + k] ).
+enum GemmAct { ACT_NONE = 0, ACT_SILU = 1, ACT_GELU = 2 };
+struct GemmEpilogue {
+    const float* bias = nullptr;       // [N]
+    int act = ACT_NONE;
+    const float* residual = nullptr;   // added after the activation, [M, ldr]
+    int ldr = 0;
+    float* out = nullptr;              // [M, ldc]
+    int ldc = 0;
+    // Cross-attention K/V scatter: column n -> (layer, k|v, head, dim); rows are frames.
+    // Writes out32 (fp32, nullable) and out16 (fp16, nullable) at
+    // (((layer*2 + kv)*kv_heads + head)*frame_cap + m)*head_dim + dim.
+    int kv_scatter = 0;
+    float* kv_out32 = nullptr;
+    void* kv_out16 = nullptr;
+    int kv_heads = 0, head_dim = 0, frame_cap = 0, frame_offset = 0;
+};
+cudaError_t launch_gemm_f32(const float* A, int lda, const float* B, int ldb, int M, int N,
+                            int K, const GemmEpilogue& ep, cudaStream_t stream);
+
+// ---------------------------------------------------------------- encoder
+// Row LayerNorm (biased variance): out = (x-mean)/sqrt(var+eps) * (w + w_offset)
+// (+ add[(add_row0 + r) * dim] when add != nullptr).
+cudaError_t launch_layernorm_rows(const float* x, int rows, int dim, const float* w,
+                                  float w_offset, float eps, const float* add, int add_row0,
+                                  float* out, cudaStream_t stream);
+
+// Multi-head attention over a [T, 3*H*hd] q|k|v buffer with a per-query key window
+// [t-left+1, t+right-1] (left <= 0 means no window: all keys).  out [T, H*hd].
+cudaError_t launch_window_attention(const float* qkv, int T, int H, int kv_heads, int hd,
+                                    int left, int right, float scale, float* out,
+                                    cudaStream_t stream);
+
+// ---------------------------------------------------------------- decoder
+struct DecodeLayerW {
+    const float* wqkv;   // [3*d, d]  (q rows, k rows, v rows)
+    const float* wo;     // [d, d]
+    const float* wcq;    // [d, d]
+    const float* wco;    // [d, d]
+    const float* w1;     // [2I, d]
+    const float* b1;     // [2I]
+    const float* w2;     // [d, I]
+    const float* b2;     // [d]
+    const float* ln1;    // [d]
+    const float* ln2;    // [d]
+    const float* ln3;    // [d]
+};
+
+struct DecodeParams {
+    int d, H, KVH, hd, I, V, L, nd;   // dims; nd = rotary dims
+    float scale;
+    const DecodeLayerW* layers;       // device array [L]
+    const float* final_ln;            // [d]
+    const float* lm_head;             // [V, d]
+    const float* embed;               // [V, d]
+    const float* rope_cos;            // [max_pos, nd/2]
+    const float* rope_sin;
+    int max_pos;
+    // self KV [L][KVH][t_cap][hd]; fp16 when kv_f16
+    void* self_k;
+    void* self_v;
+    int t_cap;
+    int kv_f16;
+    // cross KV [L][2][KVH][m_cap][hd]: fp32 copy (step 0) and stored copy (fp16 when kv_f16)
+    const float* cross32;
+    const void* cross_stored;
+    int m_cap, M;
+    // scratch (device)
+    float* x;          // [d]
+    float* qbuf;       // [H*hd]
+    float* kvnew;      // [2*KVH*hd]
+    float* attn;       // [H*hd]
+    float* part;       // cross-attention partials [H][n_chunks][hd + 2]
+    float* gbuf;       // [I]
+    float* amax_val;   // [gridDim]
+    int* amax_idx;     // [gridDim]
+    // token loop
+    int start_token;
+    int n_steps;          // decoder calls to run
+    int forced;           // 1: never stop on EOS
+    const int* teacher;   // nullable [n_steps]: next input ids
+    int eos;
+    int* ids_out;         // [n_steps]
+    float* logits_out;    // nullable [n_steps, V]
+    int* n_done;          // decoder calls completed
+    int* hit_eos;
+    unsigned* bar_count;
+    unsigned* status;
+};
+
+// Persistent cooperative decode kernel: runs up to n_steps greedy decoder calls.
+cudaError_t launch_decode_b1(const DecodeParams& p, int grid, int block, cudaStream_t stream);
+int decode_b1_block_threads();
+int decode_chunk_keys();
+
+}  // namespace msb

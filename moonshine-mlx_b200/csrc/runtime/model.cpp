@@ -1,0 +1,669 @@
+// Model loading (config.json + safetensors) and the batch-1 encode / decode orchestration.
+#include "model.hpp"
+
+#include <dirent.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cmath>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <sstream>
+
+#include "json.hpp"
+
+namespace msb {
+
+void cuda_check(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return;
+    if (e == cudaErrorMemoryAllocation) {
+        cudaGetLastError();
+        throw MsError(MS_ERR_OOM, std::string("CUDA out of memory in ") + what);
+    }
+    throw MsError(MS_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+ms_status to_status(const std::exception& e) {
+    if (auto* m = dynamic_cast<const MsError*>(&e)) return m->status;
+    if (dynamic_cast<const std::bad_alloc*>(&e)) return MS_ERR_OOM;
+    return MS_ERR_INVALID_ARG;
+}
+
+DevBuf::~DevBuf() {
+    if (p) cudaFree(p);
+}
+
+void DevBuf::ensure(size_t n) {
+    if (n <= bytes) return;
+    if (p) {
+        cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    MSB_CUDA(cudaMalloc(&p, n));
+    bytes = n;
+}
+
+// ------------------------------------------------------------------ config
+
+static std::string read_file(const std::string& path) {
+    std::ifstream f(path, std::ios::binary);
+    if (!f) throw MsError(MS_ERR_NOT_FOUND, "cannot open " + path);
+    std::stringstream ss;
+    ss << f.rdbuf();
+    return ss.str();
+}
+
+Config Config::from_json_file(const std::string& path) {
+    std::string txt = read_file(path);
+    Json d;
+    try {
+        d = Json::parse(txt.data(), txt.size());
+    } catch (const std::exception& e) {
+        throw MsError(MS_ERR_BAD_CONFIG, std::string("Failed to parse config.json: ") + e.what());
+    }
+    if (d.kind != Json::Object) throw MsError(MS_ERR_BAD_CONFIG, "Failed to parse config.json");
+    Config c;
+    // MoonshineConfig.swift:134-177
+    c.hidden = (int)d.int_or("hidden_size", 320);
+    c.inter = (int)d.int_or("intermediate_size", 1280);
+    c.layers = (int)d.int_or("num_hidden_layers", 6);
+    c.heads = (int)d.int_or("num_attention_heads", 8);
+    c.kv_heads = (int)d.int_or("num_key_value_heads", 8);
+    c.head_dim = (int)d.int_or("head_dim", 40);
+    c.vocab = (int)d.int_or("vocab_size", 32768);
+    c.max_pos = (int)d.int_or("max_position_embeddings", 4096);
+    c.tie = d.bool_or("tie_word_embeddings", false);
+    const Json* ehs = d.get("encoder_hidden_size");
+    const bool has_ehs = ehs && ehs->kind == Json::Number;
+    c.bos = (int)d.int_or("bos_token_id", 1);
+    c.eos = (int)d.int_or("eos_token_id", 2);
+    c.dec_start = (int)d.int_or("decoder_start_token_id", 1);
+    c.pad = (int)d.int_or("pad_token_id", 0);
+    c.partial_rotary = d.num_or("partial_rotary_factor", 0.8);
+    c.rope_theta = d.num_or("rope_theta", 10000.0);
+    if (const Json* rp = d.get("rope_parameters"); rp && rp->kind == Json::Object) {
+        c.partial_rotary = rp->num_or("partial_rotary_factor", c.partial_rotary);
+        c.rope_theta = rp->num_or("rope_theta", c.rope_theta);
+    }
+    c.max_tok_per_s = d.num_or("max_tokens_per_second", 6.5);
+    if (const Json* q = d.get("quantization"); q && q->kind == Json::Object) c.quantized = true;
+    if (const Json* e = d.get("encoder_config"); e && e->kind == Json::Object) {
+        // MoonshineConfig.swift:43-56
+        c.e_hidden = (int)e->int_or("hidden_size", 320);
+        c.e_inter = (int)e->int_or("intermediate_size", 1280);
+        c.e_layers = (int)e->int_or("num_hidden_layers", 6);
+        c.e_heads = (int)e->int_or("num_attention_heads", 8);
+        c.e_kv_heads = (int)e->int_or("num_key_value_heads", 8);
+        c.e_head_dim = (int)e->int_or("head_dim", 40);
+        c.frame_ms = e->num_or("frame_ms", 5.0);
+        c.sample_rate = (int)e->int_or("sample_rate", 16000);
+        c.e_max_pos = (int)e->int_or("max_position_embeddings", 4096);
+        if (const Json* sw = e->get("sliding_windows"); sw && sw->kind == Json::Array) {
+            c.has_windows = true;
+            for (const Json& w : sw->arr) {
+                if (w.kind != Json::Array || w.arr.size() < 2 || w.arr[0].kind != Json::Number ||
+                    w.arr[1].kind != Json::Number)
+                    throw MsError(MS_ERR_BAD_CONFIG, "sliding_windows entries must be [left, right]");
+                c.windows.emplace_back((int)w.arr[0].num, (int)w.arr[1].num);
+            }
+        }
+    } else {
+        // MoonshineConfig.swift:115-122
+        const int eh = has_ehs ? (int)ehs->num : c.hidden;
+        c.e_hidden = eh;
+        c.e_inter = eh * 4;
+        c.e_layers = c.layers;
+        c.e_heads = c.heads;
+        c.e_kv_heads = c.kv_heads;
+        c.e_head_dim = c.head_dim;
+    }
+    c.enc_hidden_size = has_ehs ? (int)ehs->num : c.e_hidden;
+    return c;
+}
+
+// ------------------------------------------------------------------ safetensors
+
+namespace {
+
+struct Tensor {
+    std::string dtype;
+    std::vector<int64_t> shape;
+    const uint8_t* data = nullptr;
+    size_t bytes = 0;
+    int64_t numel() const {
+        int64_t n = 1;
+        for (auto s : shape) n *= s;
+        return n;
+    }
+};
+
+struct SafeTensors {
+    int fd = -1;
+    void* map = nullptr;
+    size_t size = 0;
+    std::map<std::string, Tensor> tensors;
+    ~SafeTensors() {
+        if (map && map != MAP_FAILED) munmap(map, size);
+        if (fd >= 0) close(fd);
+    }
+    void open_file(const std::string& path) {
+        fd = ::open(path.c_str(), O_RDONLY);
+        if (fd < 0) throw MsError(MS_ERR_NOT_FOUND, "cannot open " + path);
+        struct stat st;
+        if (fstat(fd, &st) != 0) throw MsError(MS_ERR_BAD_WEIGHTS, "stat failed: " + path);
+        size = (size_t)st.st_size;
+        if (size < 8) throw MsError(MS_ERR_BAD_WEIGHTS, "truncated safetensors: " + path);
+        map = mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0);
+        if (map == MAP_FAILED) throw MsError(MS_ERR_BAD_WEIGHTS, "mmap failed: " + path);
+        const uint8_t* b = reinterpret_cast<const uint8_t*>(map);
+        uint64_t hn = 0;
+        std::memcpy(&hn, b, 8);
+        if (hn > size - 8) throw MsError(MS_ERR_BAD_WEIGHTS, "bad safetensors header size");
+        Json h;
+        try {
+            h = Json::parse(reinterpret_cast<const char*>(b + 8), (size_t)hn);
+        } catch (const std::exception& e) {
+            throw MsError(MS_ERR_BAD_WEIGHTS, std::string("bad safetensors header: ") + e.what());
+        }
+        const uint8_t* data = b + 8 + hn;
+        const size_t data_size = size - 8 - hn;
+        for (auto& kv : h.obj) {
+            if (kv.first == "__metadata__") continue;
+            const Json& m = kv.second;
+            Tensor t;
+            t.dtype = m.str_or("dtype", "");
+            if (const Json* sh = m.get("shape"))
+                for (auto& s : sh->arr) t.shape.push_back((int64_t)s.num);
+            const Json* off = m.get("data_offsets");
+            if (!off || off->arr.size() != 2) throw MsError(MS_ERR_BAD_WEIGHTS, "bad offsets: " + kv.first);
+            const size_t a = (size_t)off->arr[0].num, e = (size_t)off->arr[1].num;
+            if (a > e || e > data_size) throw MsError(MS_ERR_BAD_WEIGHTS, "offsets out of range: " + kv.first);
+            t.data = data + a;
+            t.bytes = e - a;
+            size_t esz = t.dtype == "F32" ? 4 : (t.dtype == "F16" || t.dtype == "BF16") ? 2 : 0;
+            if (esz && (size_t)t.numel() * esz != t.bytes)
+                throw MsError(MS_ERR_BAD_WEIGHTS, "size mismatch: " + kv.first);
+            tensors[kv.first] = t;
+        }
+    }
+};
+
+float half_to_float(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h >> 15) << 31;
+    uint32_t exp = (h >> 10) & 0x1f, mant = h & 0x3ff;
+    uint32_t bits;
+    if (exp == 0) {
+        if (mant == 0) bits = sign;
+        else {
+            exp = 127 - 15 + 1;
+            while (!(mant & 0x400)) {
+                mant <<= 1;
+                --exp;
+            }
+            mant &= 0x3ff;
+            bits = sign | (exp << 23) | (mant << 13);
+        }
+    } else if (exp == 31) {
+        bits = sign | 0x7f800000u | (mant << 13);
+    } else {
+        bits = sign | ((exp + 127 - 15) << 23) | (mant << 13);
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+std::vector<float> to_f32(const Tensor& t) {
+    std::vector<float> out((size_t)t.numel());
+    if (t.dtype == "F32") {
+        std::memcpy(out.data(), t.data, t.bytes);
+    } else if (t.dtype == "F16") {
+        const uint16_t* s = reinterpret_cast<const uint16_t*>(t.data);
+        for (size_t i = 0; i < out.size(); ++i) out[i] = half_to_float(s[i]);
+    } else if (t.dtype == "BF16") {
+        const uint16_t* s = reinterpret_cast<const uint16_t*>(t.data);
+        for (size_t i = 0; i < out.size(); ++i) {
+            uint32_t b = (uint32_t)s[i] << 16;
+            std::memcpy(&out[i], &b, 4);
+        }
+    } else {
+        throw MsError(MS_ERR_BAD_WEIGHTS, "unsupported tensor dtype " + t.dtype);
+    }
+    return out;
+}
+
+std::string find_weights(const std::string& dir) {
+    // ModelLoader.swift:115-130: prefer model.safetensors, else any *.safetensors
+    std::string first;
+    DIR* dp = opendir(dir.c_str());
+    if (!dp) throw MsError(MS_ERR_NOT_FOUND, "No safetensors weights found in: " + dir);
+    while (dirent* e = readdir(dp)) {
+        std::string n = e->d_name;
+        if (n.size() > 12 && n.substr(n.size() - 12) == ".safetensors") {
+            if (n == "model.safetensors") {
+                closedir(dp);
+                return dir + "/" + n;
+            }
+            if (first.empty() || n < first) first = n;
+        }
+    }
+    closedir(dp);
+    if (first.empty()) throw MsError(MS_ERR_NOT_FOUND, "No safetensors weights found in: " + dir);
+    return dir + "/" + first;
+}
+
+// Sanitised view of the checkpoint (ModelLoader.swift:75-101).
+struct WeightSource {
+    SafeTensors st;
+    bool hf = false;
+    std::map<std::string, const Tensor*> byname;
+
+    void load(const std::string& path) {
+        st.open_file(path);
+        for (auto& kv : st.tensors)
+            if (kv.first.rfind("model.", 0) == 0) hf = true;
+        for (auto& kv : st.tensors) {
+            std::string k = kv.first;
+            if (hf) {
+                if (k.rfind("model.", 0) == 0) k = k.substr(6);
+                size_t p;
+                while ((p = k.find(".gamma")) != std::string::npos) k.replace(p, 6, ".weight");
+            }
+            byname[k] = &kv.second;
+        }
+    }
+    const Tensor& need(const std::string& k, std::vector<int64_t> shape) const {
+        auto it = byname.find(k);
+        if (it == byname.end()) throw MsError(MS_ERR_BAD_WEIGHTS, "missing weight " + k);
+        const Tensor& t = *it->second;
+        if (t.shape != shape) {
+            std::string s = "shape mismatch for " + k + ": got [";
+            for (auto v : t.shape) s += std::to_string(v) + ",";
+            s += "] want [";
+            for (auto v : shape) s += std::to_string(v) + ",";
+            throw MsError(MS_ERR_BAD_WEIGHTS, s + "]");
+        }
+        return t;
+    }
+    bool has(const std::string& k) const { return byname.count(k) != 0; }
+    std::vector<float> f32(const std::string& k, std::vector<int64_t> shape) const {
+        return to_f32(need(k, shape));
+    }
+    // Conv weight as [out][k][in] from HF [out,in,k] or MLX [out,k,in].
+    std::vector<float> conv(const std::string& k, int out, int in, int ks) const {
+        if (hf) {
+            std::vector<float> w = f32(k, {out, in, ks});
+            std::vector<float> r((size_t)out * in * ks);
+            for (int o = 0; o < out; ++o)
+                for (int i = 0; i < in; ++i)
+                    for (int t = 0; t < ks; ++t)
+                        r[((size_t)o * ks + t) * in + i] = w[((size_t)o * in + i) * ks + t];
+            return r;
+        }
+        return f32(k, {out, ks, in});
+    }
+};
+
+void append(std::vector<float>& dst, const std::vector<float>& src) {
+    dst.insert(dst.end(), src.begin(), src.end());
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ model
+
+Model::~Model() {
+    if (stream) {
+        cudaSetDevice(device);
+        cudaStreamSynchronize(stream);
+    }
+    for (auto* b : owned) delete b;
+    for (auto& e : ev)
+        if (e) cudaEventDestroy(e);
+    if (stream) cudaStreamDestroy(stream);
+}
+
+float* Model::upload(const std::vector<float>& v) {
+    DevBuf* b = new DevBuf();
+    owned.push_back(b);
+    b->ensure(std::max<size_t>(16, v.size() * sizeof(float)));
+    MSB_CUDA(cudaMemcpy(b->p, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
+    return b->as<float>();
+}
+
+void Model::ensure_rope(int positions) {
+    if (positions <= rope_cap) return;
+    const int nd = cfg.rotary_ndims(), half = nd / 2;
+    const int cap = std::max(positions, 4096);
+    std::vector<float> c((size_t)cap * std::max(half, 1)), s(c.size());
+    for (int p = 0; p < cap; ++p)
+        for (int i = 0; i < half; ++i) {
+            const double inv = std::pow(cfg.rope_theta, -2.0 * i / (double)nd);
+            const double a = (double)p * inv;
+            c[(size_t)p * half + i] = (float)std::cos(a);
+            s[(size_t)p * half + i] = (float)std::sin(a);
+        }
+    MSB_CUDA(cudaStreamSynchronize(stream));
+    rope_cos.ensure(c.size() * 4);
+    rope_sin.ensure(s.size() * 4);
+    MSB_CUDA(cudaMemcpy(rope_cos.p, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+    MSB_CUDA(cudaMemcpy(rope_sin.p, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+    rope_cap = cap;
+}
+
+static void validate(const Config& c) {
+    auto bad = [](const std::string& m) { throw MsError(MS_ERR_UNSUPPORTED, m); };
+    if (c.quantized) bad("quantized checkpoints are not supported");
+    if (c.hidden % 4 || c.e_hidden % 4 || c.inter % 4 || c.e_inter % 4)
+        bad("hidden/intermediate sizes must be multiples of 4");
+    if (c.head_dim % 4 || c.e_head_dim % 4 || c.head_dim > 64 || c.e_head_dim > 128)
+        bad("head_dim must be a multiple of 4 (decoder <= 64, encoder <= 128)");
+    if (c.heads % c.kv_heads || c.e_heads % c.e_kv_heads) bad("heads must be a multiple of kv heads");
+    if (c.hidden > 1024 || c.e_hidden > 1024) bad("hidden size above 1024");
+    if (c.frame_len() <= 0 || c.frame_len() > 128) bad("frame length must be in [1, 128]");
+    if (c.layers <= 0 || c.e_layers <= 0 || c.vocab <= 0) bad("empty model");
+    for (auto& w : c.windows)
+        if (w.first < 1 || w.second < 0) bad("sliding windows need left >= 1 and right >= 0");
+    if (c.enc_hidden_size != c.e_hidden) bad("encoder_hidden_size must equal the encoder width");
+}
+
+Model* load_model(const std::string& dir, const ms_options& o) {
+    std::unique_ptr<Model> m(new Model());
+    m->opts = o;
+    m->device = o.device;
+    m->kv_f16 = o.kv_dtype == MS_KV_F16;
+    int ndev = 0;
+    MSB_CUDA(cudaGetDeviceCount(&ndev));
+    if (o.device < 0 || o.device >= ndev) throw MsError(MS_ERR_INVALID_ARG, "bad device ordinal");
+    MSB_CUDA(cudaSetDevice(o.device));
+    cudaDeviceProp prop;
+    MSB_CUDA(cudaGetDeviceProperties(&prop, o.device));
+    if (prop.major != 10) throw MsError(MS_ERR_UNSUPPORTED, "this build targets sm_100a (B200)");
+    m->num_sms = prop.multiProcessorCount;
+    m->cfg = Config::from_json_file(dir + "/config.json");
+    validate(m->cfg);
+    if (o.weight_dtype == MS_W_BF16) throw MsError(MS_ERR_UNSUPPORTED, "bf16 weights not built yet");
+    MSB_CUDA(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+    for (auto& e : m->ev) MSB_CUDA(cudaEventCreate(&e));
+
+    WeightSource ws;
+    ws.load(find_weights(dir));
+    const Config& c = m->cfg;
+    const int ed = c.e_hidden, d = c.hidden, fl = c.frame_len();
+    const int eHD = c.e_heads * c.e_head_dim, eKVD = c.e_kv_heads * c.e_head_dim;
+    const int HD = c.heads * c.head_dim, KVD = c.kv_heads * c.head_dim;
+
+    m->log_k = m->upload(ws.f32("encoder.embedder.comp.log_k", {}));
+    m->lin_w = m->upload(ws.f32("encoder.embedder.linear.weight", {ed, fl}));
+    m->conv1_w = m->upload(ws.conv("encoder.embedder.conv1.weight", 2 * ed, ed, 5));
+    m->conv1_b = m->upload(ws.f32("encoder.embedder.conv1.bias", {2 * ed}));
+    m->conv2_w = m->upload(ws.conv("encoder.embedder.conv2.weight", ed, 2 * ed, 5));
+    m->conv2_b = m->upload(ws.f32("encoder.embedder.conv2.bias", {ed}));
+    for (int i = 0; i < c.e_layers; ++i) {
+        const std::string p = "encoder.layers." + std::to_string(i) + ".";
+        EncLayer L{};
+        std::vector<float> qkv = ws.f32(p + "self_attn.q_proj.weight", {eHD, ed});
+        append(qkv, ws.f32(p + "self_attn.k_proj.weight", {eKVD, ed}));
+        append(qkv, ws.f32(p + "self_attn.v_proj.weight", {eKVD, ed}));
+        L.wqkv = m->upload(qkv);
+        L.wo = m->upload(ws.f32(p + "self_attn.o_proj.weight", {ed, eHD}));
+        L.w1 = m->upload(ws.f32(p + "mlp.fc1.weight", {c.e_inter, ed}));
+        L.b1 = m->upload(ws.f32(p + "mlp.fc1.bias", {c.e_inter}));
+        L.w2 = m->upload(ws.f32(p + "mlp.fc2.weight", {ed, c.e_inter}));
+        L.b2 = m->upload(ws.f32(p + "mlp.fc2.bias", {ed}));
+        L.ln_in = m->upload(ws.f32(p + "input_layernorm.weight", {ed}));
+        L.ln_post = m->upload(ws.f32(p + "post_attention_layernorm.weight", {ed}));
+        m->enc.push_back(L);
+    }
+    m->enc_final = m->upload(ws.f32("encoder.final_norm.weight", {ed}));
+    m->embed = m->upload(ws.f32("decoder.embed_tokens.weight", {c.vocab, d}));
+    m->pos_emb = m->upload(ws.f32("decoder.pos_emb.weight", {c.max_pos, ed}));
+    if (ed != d) m->proj = m->upload(ws.f32("decoder.proj.weight", {d, ed}));
+    std::vector<float> crossw;
+    for (int i = 0; i < c.layers; ++i) {
+        const std::string p = "decoder.layers." + std::to_string(i) + ".";
+        DecodeLayerW L{};
+        std::vector<float> qkv = ws.f32(p + "self_attn.q_proj.weight", {HD, d});
+        append(qkv, ws.f32(p + "self_attn.k_proj.weight", {KVD, d}));
+        append(qkv, ws.f32(p + "self_attn.v_proj.weight", {KVD, d}));
+        L.wqkv = m->upload(qkv);
+        L.wo = m->upload(ws.f32(p + "self_attn.o_proj.weight", {d, HD}));
+        L.wcq = m->upload(ws.f32(p + "encoder_attn.q_proj.weight", {HD, d}));
+        L.wco = m->upload(ws.f32(p + "encoder_attn.o_proj.weight", {d, HD}));
+        append(crossw, ws.f32(p + "encoder_attn.k_proj.weight", {KVD, d}));
+        append(crossw, ws.f32(p + "encoder_attn.v_proj.weight", {KVD, d}));
+        L.w1 = m->upload(ws.f32(p + "mlp.fc1.weight", {2 * c.inter, d}));
+        L.b1 = m->upload(ws.f32(p + "mlp.fc1.bias", {2 * c.inter}));
+        L.w2 = m->upload(ws.f32(p + "mlp.fc2.weight", {d, c.inter}));
+        L.b2 = m->upload(ws.f32(p + "mlp.fc2.bias", {d}));
+        L.ln1 = m->upload(ws.f32(p + "input_layernorm.weight", {d}));
+        L.ln2 = m->upload(ws.f32(p + "post_attention_layernorm.weight", {d}));
+        L.ln3 = m->upload(ws.f32(p + "final_layernorm.weight", {d}));
+        m->dec.push_back(L);
+    }
+    m->cross_w = m->upload(crossw);
+    m->dec_norm = m->upload(ws.f32("decoder.norm.weight", {d}));
+    m->lm_head = c.tie ? m->embed : m->upload(ws.f32("proj_out.weight", {c.vocab, d}));
+    m->dec_layers_buf.ensure(sizeof(DecodeLayerW) * m->dec.size());
+    MSB_CUDA(cudaMemcpy(m->dec_layers_buf.p, m->dec.data(), sizeof(DecodeLayerW) * m->dec.size(),
+                        cudaMemcpyHostToDevice));
+    m->dec_dev = m->dec_layers_buf.as<DecodeLayerW>();
+    m->ensure_rope(4096);
+    MSB_CUDA(cudaDeviceSynchronize());
+    return m.release();
+}
+
+// ------------------------------------------------------------------ encode
+
+const float* Model::memory_ptr() const {
+    return proj ? ws.memproj.as<float>() : ws.memory.as<float>();
+}
+
+void Model::encoder_layers(float* x, int T) {
+    const Config& c = cfg;
+    const int ed = c.e_hidden, hd = c.e_head_dim;
+    const int eHD = c.e_heads * hd, QKV = (c.e_heads + 2 * c.e_kv_heads) * hd;
+    ws.h.ensure((size_t)T * ed * 4);
+    ws.qkv.ensure((size_t)T * QKV * 4);
+    ws.attn.ensure((size_t)T * eHD * 4);
+    ws.f.ensure((size_t)T * c.e_inter * 4);
+    const float scale = std::pow((float)hd, -0.5f);
+    for (int i = 0; i < c.e_layers; ++i) {
+        const EncLayer& L = enc[i];
+        MSB_CUDA(launch_layernorm_rows(x, T, ed, L.ln_in, 1.0f, 1e-5f, nullptr, 0, ws.h.as<float>(), stream));
+        GemmEpilogue e1;
+        e1.out = ws.qkv.as<float>();
+        e1.ldc = QKV;
+        MSB_CUDA(launch_gemm_f32(ws.h.as<float>(), ed, L.wqkv, ed, T, QKV, ed, e1, stream));
+        auto w = c.window(i);
+        MSB_CUDA(launch_window_attention(ws.qkv.as<float>(), T, c.e_heads, c.e_kv_heads, hd, w.first,
+                                         w.second, scale, ws.attn.as<float>(), stream));
+        GemmEpilogue e2;
+        e2.out = x;
+        e2.ldc = ed;
+        e2.residual = x;
+        e2.ldr = ed;
+        MSB_CUDA(launch_gemm_f32(ws.attn.as<float>(), eHD, L.wo, eHD, T, ed, eHD, e2, stream));
+        MSB_CUDA(launch_layernorm_rows(x, T, ed, L.ln_post, 1.0f, 1e-5f, nullptr, 0, ws.h.as<float>(), stream));
+        GemmEpilogue e3;
+        e3.out = ws.f.as<float>();
+        e3.ldc = c.e_inter;
+        e3.bias = L.b1;
+        e3.act = ACT_GELU;
+        MSB_CUDA(launch_gemm_f32(ws.h.as<float>(), ed, L.w1, ed, T, c.e_inter, ed, e3, stream));
+        GemmEpilogue e4;
+        e4.out = x;
+        e4.ldc = ed;
+        e4.bias = L.b2;
+        e4.residual = x;
+        e4.ldr = ed;
+        MSB_CUDA(launch_gemm_f32(ws.f.as<float>(), c.e_inter, L.w2, c.e_inter, T, ed, c.e_inter, e4, stream));
+    }
+}
+
+int Model::encode_device(const float* audio_dev, int64_t n_samples, int pos_offset) {
+    const Config& c = cfg;
+    const int fl = c.frame_len(), ed = c.e_hidden;
+    const int T1 = (int)(n_samples / fl);
+    if (T1 <= 0) return 0;
+    const int T2 = (T1 - 1) / 2 + 1, T3 = (T2 - 1) / 2 + 1;
+    if (pos_offset + T3 > c.max_pos)
+        throw MsError(MS_ERR_INVALID_ARG, "audio longer than the positional table (" +
+                                              std::to_string(c.max_pos) + " frames)");
+    ws.feat1p.ensure((size_t)(4 + T1) * ed * 4);
+    ws.feat2p.ensure((size_t)(4 + T2) * 2 * ed * 4);
+    ws.x.ensure((size_t)T3 * ed * 4);
+    ws.memory.ensure((size_t)T3 * ed * 4);
+    float* f1 = ws.feat1p.as<float>();
+    float* f2 = ws.feat2p.as<float>();
+    MSB_CUDA(cudaMemsetAsync(f1, 0, (size_t)4 * ed * 4, stream));
+    MSB_CUDA(cudaMemsetAsync(f2, 0, (size_t)4 * 2 * ed * 4, stream));
+    MSB_CUDA(launch_frame_features(audio_dev, T1, fl, log_k, lin_w, ed, f1 + 4 * ed, ed, stream));
+    // causal conv1 (k5 s2, left pad 4) as a GEMM over strided rows of the padded buffer
+    GemmEpilogue c1;
+    c1.bias = conv1_b;
+    c1.act = ACT_SILU;
+    c1.out = f2 + 4 * 2 * ed;
+    c1.ldc = 2 * ed;
+    MSB_CUDA(launch_gemm_f32(f1, 2 * ed, conv1_w, 5 * ed, T2, 2 * ed, 5 * ed, c1, stream));
+    GemmEpilogue c2;
+    c2.bias = conv2_b;
+    c2.out = ws.x.as<float>();
+    c2.ldc = ed;
+    MSB_CUDA(launch_gemm_f32(f2, 4 * ed, conv2_w, 10 * ed, T3, ed, 10 * ed, c2, stream));
+    encoder_layers(ws.x.as<float>(), T3);
+    MSB_CUDA(launch_layernorm_rows(ws.x.as<float>(), T3, ed, enc_final, 1.0f, 1e-5f, pos_emb, pos_offset,
+                                   ws.memory.as<float>(), stream));
+    if (proj) {
+        ws.memproj.ensure((size_t)T3 * c.hidden * 4);
+        GemmEpilogue e;
+        e.out = ws.memproj.as<float>();
+        e.ldc = c.hidden;
+        MSB_CUDA(launch_gemm_f32(ws.memory.as<float>(), ed, proj, ed, T3, c.hidden, ed, e, stream));
+    }
+    return T3;
+}
+
+// ------------------------------------------------------------------ decode
+
+void Model::ensure_decode(int m_cap, int t_cap, bool want_logits, int V) {  // m_cap: memory rows
+    const Config& c = cfg;
+    const int hd = c.head_dim, KVH = c.kv_heads, L = c.layers, d = c.hidden;
+    const int HD = c.heads * hd;
+    const int chunk = decode_chunk_keys();
+    ws.dpart.ensure((size_t)c.heads * ((m_cap + chunk - 1) / chunk) * (hd + 2) * 4);
+    if (t_cap > ws.t_cap) {
+        const size_t n = (size_t)L * KVH * t_cap * hd;
+        ws.self_k.ensure(n * 4);
+        ws.self_v.ensure(n * 4);
+        ws.ids.ensure((size_t)t_cap * 4);
+        ws.t_cap = t_cap;
+    }
+    if (want_logits) ws.logits.ensure((size_t)t_cap * V * 4);
+    ws.dx.ensure(d * 4);
+    ws.dq.ensure(HD * 4);
+    ws.dkvnew.ensure(2 * KVH * hd * 4);
+    ws.dattn.ensure(HD * 4);
+    ws.dg.ensure(c.inter * 4);
+    ws.amax_v.ensure(num_sms * 4);
+    ws.amax_i.ensure(num_sms * 4);
+    ws.flags.ensure(64);
+}
+
+void Model::ensure_cross_ws(int m_cap) {
+    if (m_cap <= ws.m_cap) return;
+    const Config& c = cfg;
+    const size_t n = (size_t)c.layers * 2 * c.kv_heads * m_cap * c.head_dim;
+    ws.cross32.ensure(n * 4);
+    ws.cross16.ensure(n * 2);
+    ws.m_cap = m_cap;
+}
+
+void Model::cross_kv(const float* memory, int frames, int row0) {
+    ensure_cross_ws(row0 + frames);
+    cross_kv_into(memory, frames, row0, ws.cross32.as<float>(), kv_f16 ? ws.cross16.p : nullptr, ws.m_cap);
+}
+
+void Model::cross_kv_into(const float* memory, int frames, int row0, float* out32, void* out16, int m_cap) {
+    if (frames <= 0) return;
+    const Config& c = cfg;
+    GemmEpilogue e;
+    e.kv_scatter = 1;
+    e.kv_out32 = out32;
+    e.kv_out16 = out16;
+    e.kv_heads = c.kv_heads;
+    e.head_dim = c.head_dim;
+    e.frame_cap = m_cap;
+    e.frame_offset = row0;
+    const int N = c.layers * 2 * c.kv_heads * c.head_dim;
+    MSB_CUDA(launch_gemm_f32(memory, c.hidden, cross_w, c.hidden, frames, N, c.hidden, e, stream));
+}
+
+Model::DecodeResult Model::decode(const float* cross32, const void* cross_stored, int m_cap, int M,
+                                  int n_steps, bool forced, const int* teacher_dev, bool logits) {
+    const Config& c = cfg;
+    ensure_rope(n_steps + 1);
+    DecodeParams p{};
+    p.d = c.hidden;
+    p.H = c.heads;
+    p.KVH = c.kv_heads;
+    p.hd = c.head_dim;
+    p.I = c.inter;
+    p.V = c.vocab;
+    p.L = c.layers;
+    p.nd = c.rotary_ndims();
+    p.scale = std::pow((float)c.head_dim, -0.5f);
+    p.layers = dec_dev;
+    p.final_ln = dec_norm;
+    p.lm_head = lm_head;
+    p.embed = embed;
+    p.rope_cos = rope_cos.as<float>();
+    p.rope_sin = rope_sin.as<float>();
+    p.max_pos = rope_cap;
+    p.self_k = ws.self_k.p;
+    p.self_v = ws.self_v.p;
+    p.t_cap = ws.t_cap;
+    p.kv_f16 = kv_f16 ? 1 : 0;
+    p.cross32 = cross32;
+    p.cross_stored = cross_stored;
+    p.m_cap = m_cap;
+    p.M = M;
+    p.x = ws.dx.as<float>();
+    p.qbuf = ws.dq.as<float>();
+    p.kvnew = ws.dkvnew.as<float>();
+    p.attn = ws.dattn.as<float>();
+    p.part = ws.dpart.as<float>();
+    p.gbuf = ws.dg.as<float>();
+    p.amax_val = ws.amax_v.as<float>();
+    p.amax_idx = ws.amax_i.as<int>();
+    p.start_token = c.dec_start;
+    p.n_steps = n_steps;
+    p.forced = forced ? 1 : 0;
+    p.teacher = teacher_dev;
+    p.eos = c.eos;
+    p.ids_out = ws.ids.as<int>();
+    p.logits_out = logits ? ws.logits.as<float>() : nullptr;
+    unsigned* flags = ws.flags.as<unsigned>();
+    p.bar_count = flags;
+    p.status = flags + 1;
+    p.n_done = reinterpret_cast<int*>(flags + 2);
+    p.hit_eos = reinterpret_cast<int*>(flags + 3);
+    MSB_CUDA(cudaMemsetAsync(flags, 0, 16, stream));
+    MSB_CUDA(launch_decode_b1(p, num_sms, decode_b1_block_threads(), stream));
+    unsigned hf[4];
+    MSB_CUDA(cudaMemcpyAsync(hf, flags, 16, cudaMemcpyDeviceToHost, stream));
+    MSB_CUDA(cudaStreamSynchronize(stream));
+    if (hf[1] == DEV_BARRIER_TIMEOUT) throw MsError(MS_ERR_TIMEOUT, "decode kernel: grid barrier timed out");
+    if (hf[1] == DEV_BAD_TOKEN) throw MsError(MS_ERR_INVALID_ARG, "decode kernel: token id out of range");
+    if (hf[1] != DEV_OK) throw MsError(MS_ERR_CUDA, "decode kernel: device status " + std::to_string(hf[1]));
+    DecodeResult r;
+    r.n_calls = (int)hf[2];
+    r.hit_eos = hf[3] != 0;
+    return r;
+}
+
+}  // namespace msb

@@ -1,0 +1,134 @@
+// Host runtime of the Moonshine B200 path: config, weights on the device, device
+// workspaces, and the encode / decode orchestration behind the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../../include/moonshine_b200.h"
+#include "../kernels/kernels.h"
+
+namespace msb {
+
+struct MsError : std::runtime_error {
+    ms_status status;
+    MsError(ms_status s, const std::string& m) : std::runtime_error(m), status(s) {}
+};
+
+void cuda_check(cudaError_t e, const char* what);
+#define MSB_CUDA(x) ::msb::cuda_check((x), #x)
+
+// Parsed config.json, mirroring MoonshineConfig.swift:5-178.
+struct Config {
+    int hidden = 320, inter = 1280, layers = 6, heads = 8, kv_heads = 8, head_dim = 40;
+    int vocab = 32768, max_pos = 4096;
+    bool tie = false;
+    int enc_hidden_size = 320;  // encoder_hidden_size (memory width before proj)
+    // encoder
+    int e_hidden = 320, e_inter = 1280, e_layers = 6, e_heads = 8, e_kv_heads = 8, e_head_dim = 40;
+    double frame_ms = 5.0;
+    int sample_rate = 16000, e_max_pos = 4096;
+    bool has_windows = false;
+    std::vector<std::pair<int, int>> windows;
+    int bos = 1, eos = 2, dec_start = 1, pad = 0;
+    double partial_rotary = 0.8, rope_theta = 10000.0, max_tok_per_s = 6.5;
+    bool quantized = false;
+
+    int frame_len() const { return (int)(frame_ms * (double)sample_rate / 1000.0); }
+    int rotary_ndims() const {
+        int nd = (int)((double)head_dim * partial_rotary);
+        return nd - nd % 2;
+    }
+    // window of encoder layer i: left <= 0 means full attention
+    std::pair<int, int> window(int i) const {
+        if (has_windows && i < (int)windows.size()) return windows[i];
+        return {0, 0};
+    }
+    static Config from_json_file(const std::string& path);
+};
+
+// Device buffer that grows on demand.
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    ~DevBuf();
+    void ensure(size_t n);
+    template <class T> T* as() const { return reinterpret_cast<T*>(p); }
+};
+
+struct EncLayer {
+    float *wqkv, *wo, *w1, *b1, *w2, *b2, *ln_in, *ln_post;
+};
+
+// Per-call device workspace for one utterance chunk (batch 1).
+struct Workspace {
+    DevBuf audio, feat1p, feat2p, x, h, qkv, attn, f, memory, memproj;
+    DevBuf cross32, cross16, self_k, self_v;
+    DevBuf dx, dq, dkvnew, dattn, dpart, dg, amax_v, amax_i, ids, logits, flags;
+    int m_cap = 0, t_cap = 0;
+};
+
+struct StreamState;
+
+struct Model {
+    Config cfg;
+    ms_options opts{};
+    int device = 0, num_sms = 0;
+    bool kv_f16 = true;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev[4] = {};
+    std::mutex mu;
+
+    // weights (device, fp32)
+    std::vector<DevBuf*> owned;
+    float *lin_w = nullptr, *log_k = nullptr, *conv1_w = nullptr, *conv1_b = nullptr,
+          *conv2_w = nullptr, *conv2_b = nullptr, *enc_final = nullptr;
+    std::vector<EncLayer> enc;
+    float *embed = nullptr, *pos_emb = nullptr, *proj = nullptr, *lm_head = nullptr,
+          *dec_norm = nullptr, *cross_w = nullptr;
+    std::vector<DecodeLayerW> dec;
+    DecodeLayerW* dec_dev = nullptr;
+    DevBuf dec_layers_buf, rope_cos, rope_sin;
+    int rope_cap = 0;
+
+    Workspace ws;
+
+    ~Model();
+    float* upload(const std::vector<float>& v);
+    void ensure_rope(int positions);
+
+    // --- orchestration (all on `stream`)
+    // Frontend + encoder + prepareMemory for one chunk already on the device.
+    // Returns the number of memory frames; memory rows land in ws.memory (or memproj).
+    int encode_device(const float* audio_dev, int64_t n_samples, int pos_offset);
+    const float* memory_ptr() const;
+    // Encoder over already computed features [T, e_hidden] (streaming windows).
+    void encoder_layers(float* x, int T);
+    // Cross K/V of `frames` memory rows into the decode cache at row offset `row0`.
+    void cross_kv(const float* memory, int frames, int row0);
+    // Decode scratch for `m_frames` memory rows and `t_cap` decoder calls.
+    void ensure_decode(int m_frames, int t_cap, bool want_logits, int V);
+    void ensure_cross_ws(int m_cap);
+    struct DecodeResult {
+        int n_calls = 0;
+        bool hit_eos = false;
+    };
+    // Greedy decode against cross K/V laid out [L][2][KVH][m_cap][hd] (fp32 copy for the
+    // first decoder call, stored copy afterwards).
+    DecodeResult decode(const float* cross32, const void* cross_stored, int m_cap, int M, int n_steps,
+                        bool forced, const int* teacher_dev, bool logits);
+    // Cross K/V of `frames` memory rows into explicit buffers at row offset `row0`.
+    void cross_kv_into(const float* memory, int frames, int row0, float* out32, void* out16, int m_cap);
+};
+
+ms_status to_status(const std::exception& e);
+
+}  // namespace msb

@@ -1,0 +1,221 @@
+// Streaming state machine of MoonshineStreaming.swift over device-resident buffers.
+//
+// Frontend (Embedder.processChunk, MoonshineEncoder.swift:100-151): leftover samples stay
+// on the host (< one frame); whole frames go through the fused frame-feature kernel and
+// the two causal convs as implicit GEMMs whose 4-row history buffers live on the device.
+// encodeNewFrames (MoonshineStreaming.swift:178-214) re-runs the encoder over the
+// 16*L-frame left context plus new frames and appends memory rows AND their cross K/V:
+// memory rows never change once appended, so their cross K/V is computed once instead of
+// on every transcribe call as the reference does (identical values).  decodeMemory
+// (:229-276) re-decodes from BOS on every call with the same greedy kernel as generate.
+#include "stream.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+namespace msb {
+
+namespace {
+
+// Grow `b` to `new_bytes`, keeping its first `keep_bytes` (device-to-device copy).
+void grow_keep(DevBuf& b, size_t keep_bytes, size_t new_bytes, cudaStream_t s) {
+    if (new_bytes <= b.bytes) return;
+    void* p = nullptr;
+    MSB_CUDA(cudaMalloc(&p, new_bytes));
+    if (b.p && keep_bytes) MSB_CUDA(cudaMemcpyAsync(p, b.p, keep_bytes, cudaMemcpyDeviceToDevice, s));
+    MSB_CUDA(cudaStreamSynchronize(s));
+    if (b.p) cudaFree(b.p);
+    b.p = p;
+    b.bytes = new_bytes;
+}
+
+}  // namespace
+
+StreamState::StreamState(Model* m) : model(m) {
+    // createStream pre-fills frameLen-1 zero samples (MoonshineStreaming.swift:69-71)
+    sample_buffer.assign((size_t)std::max(0, m->cfg.frame_len() - 1), 0.f);
+}
+
+void StreamState::start() {  // MoonshineStreaming.swift:74-78
+    active = true;
+    reset_segment();
+    emitted.clear();
+}
+
+void StreamState::reset_segment() {  // MoonshineStreaming.swift:217-226
+    feat_count = 0;
+    encoder_frames_emitted = 0;
+    pos_offset = 0;
+    memory_len = 0;
+    last_hit_eos = false;
+}
+
+void StreamState::add_audio(const float* chunk, int64_t n) {  // MoonshineStreaming.swift:87-105
+    Model& m = *model;
+    const Config& c = m.cfg;
+    const int fl = c.frame_len(), ed = c.e_hidden;
+    cudaStream_t s = m.stream;
+    std::vector<float> buf;
+    buf.reserve(sample_buffer.size() + (size_t)n);
+    buf.insert(buf.end(), sample_buffer.begin(), sample_buffer.end());
+    buf.insert(buf.end(), chunk, chunk + n);
+    const int64_t nf64 = (int64_t)buf.size() / fl;
+    const int64_t rem = (int64_t)buf.size() - nf64 * fl;
+    if (rem > 0) sample_buffer.assign(buf.end() - rem, buf.end());
+    else sample_buffer.clear();
+    if (nf64 == 0) return;
+    if (nf64 > (1 << 24)) throw MsError(MS_ERR_INVALID_ARG, "audio chunk too long");
+    const int nf = (int)nf64;
+    chunk_audio.ensure((size_t)nf * fl * 4);
+    MSB_CUDA(cudaMemcpyAsync(chunk_audio.p, buf.data(), (size_t)nf * fl * 4, cudaMemcpyHostToDevice, s));
+    const int T2 = (nf - 1) / 2 + 1, T3 = (T2 - 1) / 2 + 1;
+    xin1.ensure((size_t)(4 + nf) * ed * 4);
+    xin2.ensure((size_t)(4 + T2) * 2 * ed * 4);
+    conv1_buf.ensure((size_t)4 * ed * 4);
+    conv2_buf.ensure((size_t)4 * 2 * ed * 4);
+    float* x1 = xin1.as<float>();
+    float* x2 = xin2.as<float>();
+    if (have_conv1) MSB_CUDA(cudaMemcpyAsync(x1, conv1_buf.p, (size_t)4 * ed * 4, cudaMemcpyDeviceToDevice, s));
+    else MSB_CUDA(cudaMemsetAsync(x1, 0, (size_t)4 * ed * 4, s));
+    if (have_conv2) MSB_CUDA(cudaMemcpyAsync(x2, conv2_buf.p, (size_t)4 * 2 * ed * 4, cudaMemcpyDeviceToDevice, s));
+    else MSB_CUDA(cudaMemsetAsync(x2, 0, (size_t)4 * 2 * ed * 4, s));
+    MSB_CUDA(launch_frame_features(chunk_audio.as<float>(), nf, fl, m.log_k, m.lin_w, ed, x1 + 4 * ed, ed, s));
+    GemmEpilogue c1;
+    c1.bias = m.conv1_b;
+    c1.act = ACT_SILU;
+    c1.out = x2 + 4 * 2 * ed;
+    c1.ldc = 2 * ed;
+    MSB_CUDA(launch_gemm_f32(x1, 2 * ed, m.conv1_w, 5 * ed, T2, 2 * ed, 5 * ed, c1, s));
+    // conv1Buffer = last 4 rows of [buffer; x] (MoonshineEncoder.swift:137)
+    MSB_CUDA(cudaMemcpyAsync(conv1_buf.p, x1 + (size_t)nf * ed, (size_t)4 * ed * 4, cudaMemcpyDeviceToDevice, s));
+    have_conv1 = true;
+    if (feat_count + T3 > feat_cap) {
+        const int cap = std::max(feat_count + T3, std::max(2 * feat_cap, 256));
+        grow_keep(features, (size_t)feat_count * ed * 4, (size_t)cap * ed * 4, s);
+        feat_cap = cap;
+    }
+    GemmEpilogue c2;
+    c2.bias = m.conv2_b;
+    c2.out = features.as<float>() + (size_t)feat_count * ed;
+    c2.ldc = ed;
+    MSB_CUDA(launch_gemm_f32(x2, 4 * ed, m.conv2_w, 10 * ed, T3, ed, 10 * ed, c2, s));
+    MSB_CUDA(cudaMemcpyAsync(conv2_buf.p, x2 + (size_t)T2 * 2 * ed, (size_t)4 * 2 * ed * 4,
+                             cudaMemcpyDeviceToDevice, s));
+    have_conv2 = true;
+    feat_count += T3;
+}
+
+void StreamState::ensure_memory(int rows) {
+    Model& m = *model;
+    const Config& c = m.cfg;
+    if (rows <= mem_cap) return;
+    const int cap = std::max(rows, std::max(2 * mem_cap, 256));
+    grow_keep(memory, (size_t)memory_len * c.hidden * 4, (size_t)cap * c.hidden * 4, m.stream);
+    const size_t n = (size_t)c.layers * 2 * c.kv_heads * cap * c.head_dim;
+    cross32.ensure(n * 4);
+    cross16.ensure(n * 2);
+    mem_cap = cap;
+    // the K/V layout depends on the capacity: rebuild it for the rows kept
+    m.cross_kv_into(memory.as<float>(), memory_len, 0, cross32.as<float>(), cross16.p, mem_cap);
+}
+
+void StreamState::encode_new_frames(bool is_final) {  // MoonshineStreaming.swift:178-214
+    Model& m = *model;
+    const Config& c = m.cfg;
+    if (feat_count <= 0) return;
+    const int total = feat_count;
+    int look = 0;
+    if (c.has_windows)
+        for (auto& w : c.windows) look = std::max(look, w.second);
+    const int stable = is_final ? total : std::max(0, total - look);
+    const int nnew = stable - encoder_frames_emitted;
+    if (nnew <= 0) return;
+    if (pos_offset + nnew > c.max_pos)
+        throw MsError(MS_ERR_INVALID_ARG, "segment longer than the positional table");
+    const int left_ctx = 16 * c.e_layers;
+    const int win_start = std::max(0, encoder_frames_emitted - left_ctx);
+    const int T = total - win_start;
+    const int ed = c.e_hidden;
+    m.ws.x.ensure((size_t)T * ed * 4);
+    MSB_CUDA(cudaMemcpyAsync(m.ws.x.p, features.as<float>() + (size_t)win_start * ed, (size_t)T * ed * 4,
+                             cudaMemcpyDeviceToDevice, m.stream));
+    m.encoder_layers(m.ws.x.as<float>(), T);
+    const int off = encoder_frames_emitted - win_start;
+    ensure_memory(memory_len + nnew);
+    float* dst = memory.as<float>() + (size_t)memory_len * c.hidden;
+    if (m.proj) {
+        m.ws.memory.ensure((size_t)nnew * ed * 4);
+        MSB_CUDA(launch_layernorm_rows(m.ws.x.as<float>() + (size_t)off * ed, nnew, ed, m.enc_final, 1.0f, 1e-5f,
+                                       m.pos_emb, pos_offset, m.ws.memory.as<float>(), m.stream));
+        GemmEpilogue e;
+        e.out = dst;
+        e.ldc = c.hidden;
+        MSB_CUDA(launch_gemm_f32(m.ws.memory.as<float>(), ed, m.proj, ed, nnew, c.hidden, ed, e, m.stream));
+    } else {
+        MSB_CUDA(launch_layernorm_rows(m.ws.x.as<float>() + (size_t)off * ed, nnew, ed, m.enc_final, 1.0f, 1e-5f,
+                                       m.pos_emb, pos_offset, dst, m.stream));
+    }
+    m.cross_kv_into(dst, nnew, memory_len, cross32.as<float>(), cross16.p, mem_cap);
+    pos_offset += nnew;
+    encoder_frames_emitted = stable;
+    memory_len += nnew;
+}
+
+std::pair<std::vector<int32_t>, bool> StreamState::decode_memory(int32_t max_tokens) {
+    Model& m = *model;
+    const Config& c = m.cfg;
+    if (memory_len <= 0) return {{}, false};
+    // MoonshineStreaming.swift:234-236
+    const double dur = (double)memory_len * 0.020;
+    const int64_t limit = (int64_t)std::ceil(dur * c.max_tok_per_s);
+    const int64_t max_tok = std::min<int64_t>(max_tokens, limit);
+    if (max_tok <= 0) throw MsError(MS_ERR_INVALID_ARG, "token limit must be positive");
+    m.ensure_decode(memory_len, (int)max_tok, false, c.vocab);
+    Model::DecodeResult r = m.decode(cross32.as<float>(), m.kv_f16 ? cross16.p : cross32.p, mem_cap, memory_len,
+                                     (int)max_tok, false, nullptr, false);
+    const int n_ids = r.n_calls - (r.hit_eos ? 1 : 0);
+    std::vector<int32_t> ids((size_t)std::max(n_ids, 0));
+    if (n_ids > 0) {
+        MSB_CUDA(cudaMemcpyAsync(ids.data(), m.ws.ids.p, (size_t)n_ids * 4, cudaMemcpyDeviceToHost, m.stream));
+        MSB_CUDA(cudaStreamSynchronize(m.stream));
+    }
+    return {ids, r.hit_eos};
+}
+
+StreamState::Result StreamState::transcribe(bool is_final, const ms_streaming_config& sc, int32_t max_tokens) {
+    // MoonshineStreaming.swift:122-168
+    Result res;
+    encode_new_frames(is_final);
+    if (memory_len <= 0) {
+        if (is_final) reset_segment();
+        MSB_CUDA(cudaStreamSynchronize(model->stream));
+        return res;
+    }
+    auto dm = decode_memory(max_tokens);
+    res.ids = dm.first;
+    res.hit_eos = dm.second;
+    last_hit_eos = res.hit_eos;
+    if (res.hit_eos && memory_len >= sc.min_segment_frames) {
+        emitted.push_back(res.ids);
+        reset_segment();
+        encode_new_frames(is_final);
+        res.emitted = true;
+        return res;
+    }
+    if (is_final) {
+        emitted.push_back(res.ids);
+        reset_segment();
+        res.emitted = true;
+        return res;
+    }
+    if (memory_len > sc.max_memory_frames) {
+        emitted.push_back(res.ids);
+        reset_segment();
+        res.emitted = true;
+        return res;
+    }
+    return res;
+}
+
+}  // namespace msb

@@ -1,0 +1,49 @@
+// Streaming transcription state (StreamingState, Sources/MoonshineMLX/MoonshineStreaming.swift:8-43)
+// with its frontend conv buffers, features, memory and cross K/V resident on the device.
+#pragma once
+
+#include <vector>
+
+#include "model.hpp"
+
+namespace msb {
+
+struct StreamState {
+    Model* model = nullptr;
+    // frontend (persists across segments)
+    std::vector<float> sample_buffer;   // leftover samples (< frame_len), host side
+    bool have_conv1 = false, have_conv2 = false;
+    DevBuf conv1_buf, conv2_buf;         // last 4 rows of the conv inputs
+    DevBuf xin1, xin2, chunk_audio;      // per-chunk scratch
+    // accumulated encoder-input features [count, e_hidden]
+    DevBuf features;
+    int feat_count = 0, feat_cap = 0;
+    int encoder_frames_emitted = 0;
+    int pos_offset = 0;
+    // memory [memory_len, hidden] and its cross K/V [L][2][KVH][mem_cap][hd]
+    DevBuf memory, cross32, cross16;
+    int memory_len = 0, mem_cap = 0;
+    bool cross_f16 = false;
+    std::vector<std::vector<int32_t>> emitted;
+    bool last_hit_eos = false;
+    bool active = false;
+
+    explicit StreamState(Model* m);
+    void start();
+    void stop() { active = false; }
+    void add_audio(const float* chunk, int64_t n);
+    struct Result {
+        std::vector<int32_t> ids;
+        bool hit_eos = false;
+        bool emitted = false;
+    };
+    Result transcribe(bool is_final, const ms_streaming_config& sc, int32_t max_tokens);
+
+   private:
+    void reset_segment();
+    void encode_new_frames(bool is_final);
+    void ensure_memory(int rows);
+    std::pair<std::vector<int32_t>, bool> decode_memory(int32_t max_tokens);
+};
+
+}  // namespace msb

@@ -1,0 +1,419 @@
+"""Python mirror of the reference Swift API over the B200 C ABI (include/moonshine_b200.h).
+
+Names follow kylehowells/moonshine-mlx's public surface
+(Sources/MoonshineMLX/MoonshineModel.swift, MoonshineStreaming.swift):
+
+    model = MoonshineModel.load(path)                  # MoonshineModel.load(from:)
+    out = model.generate(audio)                        # generate(audio:maxTokens:...)
+    model.enable_float16_kv_cache(False)               # enableFloat16KVCache(_:)
+    st = model.create_stream(); model.start_stream(st) # createStream / startStream
+    model.add_audio(st, chunk)                         # addAudio(_:chunk:)
+    ids = model.transcribe(st, is_final=False)         # transcribe(_:isFinal:...)
+    model.get_emitted(st)                              # getEmittedText(_:)
+
+Token ids replace text (the tokenizer stays with the caller).  Every call goes through
+the CUDA library; there is no CPU fallback -- importing this module fails loudly when
+the library has not been built.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass, field
+from typing import List, Optional, Sequence
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libmoonshine_b200.so")
+
+MS_OK = 0
+MS_ERR_CAPACITY = 9
+STATUS_NAMES = {0: "OK", 1: "INVALID_ARG", 2: "OOM", 3: "CUDA_ERROR", 4: "TIMEOUT",
+                5: "BAD_WEIGHTS", 6: "BAD_CONFIG", 7: "NOT_FOUND", 8: "UNSUPPORTED",
+                9: "CAPACITY"}
+KV_F32, KV_F16 = 0, 1
+
+
+class MoonshineError(RuntimeError):
+    """Raised for every non-OK status (mirrors MoonshineError, ModelLoader.swift:187-203)."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+class _Options(C.Structure):
+    _fields_ = [("device", C.c_int32), ("kv_dtype", C.c_int32), ("weight_dtype", C.c_int32),
+                ("max_batch", C.c_int32), ("reserved", C.c_int32 * 8)]
+
+
+class _GenParams(C.Structure):
+    _fields_ = [("max_tokens", C.c_int32), ("forced_len", C.c_int32),
+                ("temperature", C.c_float), ("reserved_f", C.c_float),
+                ("chunk_duration", C.c_double), ("teacher_ids", C.POINTER(C.c_int32)),
+                ("n_teacher", C.c_int32), ("reserved", C.c_int32 * 7)]
+
+
+class _GenStats(C.Structure):
+    _fields_ = [("n_tokens", C.c_int32), ("n_chunks", C.c_int32), ("hit_eos", C.c_int32),
+                ("memory_frames", C.c_int32), ("encode_ms", C.c_double),
+                ("decode_ms", C.c_double), ("total_ms", C.c_double),
+                ("tokens_per_second", C.c_double)]
+
+
+class _StreamingConfig(C.Structure):
+    _fields_ = [("max_memory_frames", C.c_int32), ("min_segment_frames", C.c_int32)]
+
+
+class _ModelConfig(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in (
+        "hidden_size", "intermediate_size", "num_hidden_layers", "num_attention_heads",
+        "num_key_value_heads", "head_dim", "vocab_size", "max_position_embeddings",
+        "tie_word_embeddings", "encoder_hidden_size", "enc_hidden_size",
+        "enc_intermediate_size", "enc_num_hidden_layers", "enc_num_attention_heads",
+        "enc_num_key_value_heads", "enc_head_dim", "enc_frame_len", "enc_sample_rate",
+        "enc_max_position_embeddings", "bos_token_id", "eos_token_id",
+        "decoder_start_token_id", "pad_token_id", "rotary_ndims")] + [
+        ("rope_theta", C.c_float), ("max_tokens_per_second", C.c_double),
+        ("num_sliding_windows", C.c_int32), ("sliding_windows", (C.c_int32 * 2) * 64)]
+
+
+def _load_lib() -> C.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with `make -C {os.path.dirname(_HERE)}`")
+    lib = C.CDLL(LIB_PATH)
+    P = C.c_void_p
+    i32p = C.POINTER(C.c_int32)
+    f32p = C.POINTER(C.c_float)
+    sigs = {
+        "ms_options_default": (None, [C.POINTER(_Options)]),
+        "ms_gen_params_default": (None, [C.POINTER(_GenParams)]),
+        "ms_streaming_config_default": (None, [C.POINTER(_StreamingConfig)]),
+        "ms_model_load": (C.c_int, [C.c_char_p, C.POINTER(_Options), C.POINTER(P)]),
+        "ms_model_free": (None, [P]),
+        "ms_model_enable_fp16_kv_cache": (C.c_int, [P, C.c_int32]),
+        "ms_model_sample_rate": (C.c_int32, [P]),
+        "ms_model_get_config": (C.c_int, [P, C.POINTER(_ModelConfig)]),
+        "ms_generate": (C.c_int, [P, f32p, C.c_int64, C.POINTER(_GenParams), i32p, C.c_int32,
+                                  i32p, f32p, C.POINTER(_GenStats)]),
+        "ms_generate_batch": (C.c_int, [P, C.POINTER(f32p), C.POINTER(C.c_int64), C.c_int32,
+                                        C.POINTER(_GenParams), i32p, C.c_int32, i32p,
+                                        C.POINTER(_GenStats)]),
+        "ms_generate_device": (C.c_int, [P, C.c_void_p, C.c_int64, C.POINTER(_GenParams), C.c_void_p,
+                                         C.c_int32, i32p, C.POINTER(_GenStats)]),
+        "ms_model_stream": (C.c_void_p, [P]),
+        "ms_encode": (C.c_int, [P, f32p, C.c_int64, f32p, C.c_int64, i32p]),
+        "ms_stream_create": (C.c_int, [P, C.POINTER(P)]),
+        "ms_stream_free": (None, [P]),
+        "ms_stream_start": (C.c_int, [P]),
+        "ms_stream_stop": (C.c_int, [P]),
+        "ms_stream_add_audio": (C.c_int, [P, f32p, C.c_int64]),
+        "ms_stream_transcribe": (C.c_int, [P, C.c_int32, C.POINTER(_StreamingConfig), C.c_int32,
+                                           i32p, C.c_int32, i32p, i32p, i32p]),
+        "ms_stream_transcribe_batch": (C.c_int, [C.POINTER(P), C.c_int32, C.c_int32,
+                                                 C.POINTER(_StreamingConfig), C.c_int32, i32p,
+                                                 C.c_int32, i32p, i32p, i32p]),
+        "ms_stream_emitted": (C.c_int, [P, i32p, C.c_int32, i32p]),
+        "ms_stream_memory_len": (C.c_int32, [P]),
+        "ms_last_error": (C.c_char_p, []),
+        "ms_kernel_launches": (C.c_int64, []),
+        "ms_reset_kernel_launches": (None, []),
+        "ms_version": (C.c_char_p, []),
+    }
+    for name, (res, args) in sigs.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+_lib: Optional[C.CDLL] = None
+
+
+def _L() -> C.CDLL:
+    """The CUDA library, loaded on first use (importing `synth` needs no build)."""
+    global _lib
+    if _lib is None:
+        _lib = _load_lib()
+    return _lib
+
+
+def _check(status: int) -> None:
+    if status != MS_OK:
+        raise MoonshineError(status, _L().ms_last_error().decode(errors="replace"))
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float32).reshape(-1))
+
+
+def _fptr(a: np.ndarray):
+    return a.ctypes.data_as(C.POINTER(C.c_float))
+
+
+def _iptr(a: np.ndarray):
+    return a.ctypes.data_as(C.POINTER(C.c_int32))
+
+
+@dataclass
+class TranscriptionOutput:
+    """TranscriptionOutput (MoonshineModel.swift:8-14) with token ids in place of text."""
+    tokens: List[int]
+    generation_tokens: int
+    total_time: float
+    tokens_per_second: float
+    encode_ms: float = 0.0
+    decode_ms: float = 0.0
+    hit_eos: bool = False
+    memory_frames: int = 0
+    logits: Optional[np.ndarray] = None
+
+
+@dataclass
+class StreamingConfig:
+    """StreamingConfig (MoonshineStreaming.swift:47-62)."""
+    max_memory_frames: int = 100000
+    min_segment_frames: int = 250
+
+    def _c(self) -> _StreamingConfig:
+        return _StreamingConfig(self.max_memory_frames, self.min_segment_frames)
+
+
+class StreamingState:
+    """Opaque handle over ms_stream (StreamingState, MoonshineStreaming.swift:8-43)."""
+
+    def __init__(self, handle, model: "MoonshineModel"):
+        self._h = handle
+        self._model = model  # keeps the model alive while the stream exists
+        self.last_hit_eos = False
+
+    @property
+    def memory_len(self) -> int:
+        return int(_L().ms_stream_memory_len(self._h))
+
+    def close(self):
+        if self._h:
+            _L().ms_stream_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class MoonshineModel:
+    def __init__(self, handle):
+        self._h = handle
+        cfg = _ModelConfig()
+        _check(_L().ms_model_get_config(self._h, C.byref(cfg)))
+        self.config = cfg
+
+    @staticmethod
+    def load(path: str, device: int = 0, kv_fp16: bool = True) -> "MoonshineModel":
+        """MoonshineModel.load(from:) for a local directory (MoonshineModel.swift:409-414)."""
+        o = _Options()
+        _L().ms_options_default(C.byref(o))
+        o.device = device
+        o.kv_dtype = KV_F16 if kv_fp16 else KV_F32
+        h = C.c_void_p()
+        _check(_L().ms_model_load(path.encode(), C.byref(o), C.byref(h)))
+        return MoonshineModel(h)
+
+    def close(self):
+        if self._h:
+            _L().ms_model_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def sample_rate(self) -> int:
+        return int(_L().ms_model_sample_rate(self._h))
+
+    def enable_float16_kv_cache(self, enabled: bool) -> None:
+        _check(_L().ms_model_enable_fp16_kv_cache(self._h, 1 if enabled else 0))
+
+    def _params(self, max_tokens, temperature, chunk_duration, forced_len, teacher):
+        p = _GenParams()
+        _L().ms_gen_params_default(C.byref(p))
+        p.max_tokens = 0 if max_tokens is None else int(max_tokens)
+        p.forced_len = 0 if forced_len is None else int(forced_len)
+        p.temperature = float(temperature)
+        p.chunk_duration = float(chunk_duration)
+        if teacher is not None:
+            p.teacher_ids = _iptr(teacher)
+            p.n_teacher = int(teacher.shape[0])
+        return p
+
+    def generate(self, audio, max_tokens: Optional[int] = None, temperature: float = 0.0,
+                 chunk_duration: float = 30.0, forced_len: Optional[int] = None,
+                 teacher_ids: Optional[Sequence[int]] = None,
+                 return_logits: bool = False) -> TranscriptionOutput:
+        """MoonshineModel.generate (MoonshineModel.swift:130-184)."""
+        a = _f32(audio)
+        sr = self.sample_rate
+        chunk = int(chunk_duration * sr)
+        n_chunks = max(1, -(-a.shape[0] // chunk)) if a.shape[0] else 0
+        per_chunk = forced_len if forced_len else int(np.ceil(min(chunk, a.shape[0]) / sr * 6.5)) + 1
+        if max_tokens:
+            per_chunk = min(per_chunk, max_tokens) if not forced_len else per_chunk
+        cap = max(1, n_chunks * per_chunk + 1)
+        teacher = None if teacher_ids is None else np.ascontiguousarray(teacher_ids, dtype=np.int32)
+        p = self._params(max_tokens, temperature, chunk_duration, forced_len, teacher)
+        V = self.config.vocab_size
+        while True:
+            ids = np.zeros(cap, dtype=np.int32)
+            logits = np.zeros((cap, V), dtype=np.float32) if return_logits else None
+            n = C.c_int32()
+            st = _GenStats()
+            s = _L().ms_generate(self._h, _fptr(a), a.shape[0], C.byref(p), _iptr(ids), cap,
+                                C.byref(n), _fptr(logits) if logits is not None else None,
+                                C.byref(st))
+            if s == MS_ERR_CAPACITY and n.value > cap:
+                cap = n.value + 1
+                continue
+            _check(s)
+            break
+        out = TranscriptionOutput(tokens=ids[: n.value].tolist(), generation_tokens=n.value,
+                                  total_time=st.total_ms / 1000.0,
+                                  tokens_per_second=st.tokens_per_second,
+                                  encode_ms=st.encode_ms, decode_ms=st.decode_ms,
+                                  hit_eos=bool(st.hit_eos), memory_frames=st.memory_frames)
+        if return_logits:
+            out.logits = logits
+        return out
+
+    def generate_device(self, audio_dev_ptr: int, n_samples: int, ids_dev_ptr: int, cap: int,
+                        forced_len: Optional[int] = None, max_tokens: Optional[int] = None,
+                        chunk_duration: float = 30.0):
+        """ms_generate_device: audio and ids stay in device memory.  Returns (n, stats)."""
+        p = self._params(max_tokens, 0.0, chunk_duration, forced_len, None)
+        n = C.c_int32()
+        st = _GenStats()
+        _check(_L().ms_generate_device(self._h, C.c_void_p(audio_dev_ptr), int(n_samples), C.byref(p),
+                                       C.c_void_p(ids_dev_ptr), int(cap), C.byref(n), C.byref(st)))
+        return n.value, st
+
+    @property
+    def cuda_stream(self) -> int:
+        """cudaStream_t the model's work is enqueued on (as an integer handle)."""
+        return int(_L().ms_model_stream(self._h) or 0)
+
+    def generate_batch(self, audios: Sequence[np.ndarray], max_tokens: Optional[int] = None,
+                       forced_len: Optional[int] = None, chunk_duration: float = 30.0):
+        """Batched offline generation (one id list per utterance)."""
+        arrs = [_f32(a) for a in audios]
+        B = len(arrs)
+        sr = self.sample_rate
+        longest = max((a.shape[0] for a in arrs), default=0)
+        n_chunks = max(1, -(-longest // int(chunk_duration * sr)))
+        per = forced_len if forced_len else int(np.ceil(min(longest, chunk_duration * sr) / sr * 6.5)) + 1
+        cap = n_chunks * per + 1
+        ptrs = (C.POINTER(C.c_float) * B)(*[_fptr(a) for a in arrs])
+        lens = (C.c_int64 * B)(*[a.shape[0] for a in arrs])
+        ids = np.zeros((B, cap), dtype=np.int32)
+        n = np.zeros(B, dtype=np.int32)
+        p = self._params(max_tokens, 0.0, chunk_duration, forced_len, None)
+        st = _GenStats()
+        _check(_L().ms_generate_batch(self._h, ptrs, lens, B, C.byref(p), _iptr(ids), cap,
+                                     _iptr(n), C.byref(st)))
+        return [ids[b, : n[b]].tolist() for b in range(B)], st
+
+    def encode(self, audio) -> np.ndarray:
+        """Memory = prepareMemory(encoder(embedder(audio))) for one chunk, [frames, hidden]."""
+        a = _f32(audio)
+        d = self.config.hidden_size
+        cap = (a.shape[0] // self.config.enc_frame_len // 4 + 2) * d
+        out = np.zeros(max(cap, d), dtype=np.float32)
+        nf = C.c_int32()
+        _check(_L().ms_encode(self._h, _fptr(a), a.shape[0], _fptr(out), out.shape[0], C.byref(nf)))
+        return out[: nf.value * d].reshape(nf.value, d)
+
+    # ---------------------------------------------------------------- streaming
+    def create_stream(self) -> StreamingState:
+        h = C.c_void_p()
+        _check(_L().ms_stream_create(self._h, C.byref(h)))
+        return StreamingState(h, self)
+
+    def start_stream(self, state: StreamingState) -> None:
+        _check(_L().ms_stream_start(state._h))
+
+    def stop_stream(self, state: StreamingState) -> None:
+        _check(_L().ms_stream_stop(state._h))
+
+    def add_audio(self, state: StreamingState, chunk) -> None:
+        a = _f32(chunk)
+        _check(_L().ms_stream_add_audio(state._h, _fptr(a), a.shape[0]))
+
+    def transcribe(self, state: StreamingState, is_final: bool = False,
+                   streaming_config: Optional[StreamingConfig] = None,
+                   max_tokens: Optional[int] = None, temperature: float = 0.0):
+        """transcribe (MoonshineStreaming.swift:122-168).  Returns (ids, hit_eos, emitted)."""
+        if temperature != 0.0:
+            raise MoonshineError(8, "only greedy decoding (temperature 0) is supported")
+        sc = (streaming_config or StreamingConfig())._c()
+        cap = max(16, int(np.ceil(state.memory_len * 0.02 * 6.5)) + 64)
+        while True:
+            ids = np.zeros(cap, dtype=np.int32)
+            n, hit, em = C.c_int32(), C.c_int32(), C.c_int32()
+            s = _L().ms_stream_transcribe(state._h, 1 if is_final else 0, C.byref(sc),
+                                         0 if max_tokens is None else int(max_tokens),
+                                         _iptr(ids), cap, C.byref(n), C.byref(hit), C.byref(em))
+            if s == MS_ERR_CAPACITY:
+                raise MoonshineError(s, "transcribe ids buffer too small")
+            _check(s)
+            break
+        state.last_hit_eos = bool(hit.value)
+        return ids[: n.value].tolist(), bool(hit.value), bool(em.value)
+
+    def transcribe_batch(self, states: Sequence[StreamingState], is_final: bool = False,
+                         streaming_config: Optional[StreamingConfig] = None,
+                         max_tokens: Optional[int] = None):
+        B = len(states)
+        sc = (streaming_config or StreamingConfig())._c()
+        cap = max(16, max((int(np.ceil(s.memory_len * 0.02 * 6.5)) for s in states), default=0) + 64)
+        hs = (C.c_void_p * B)(*[s._h for s in states])
+        ids = np.zeros((B, cap), dtype=np.int32)
+        n = np.zeros(B, dtype=np.int32)
+        hit = np.zeros(B, dtype=np.int32)
+        em = np.zeros(B, dtype=np.int32)
+        _check(_L().ms_stream_transcribe_batch(hs, B, 1 if is_final else 0, C.byref(sc),
+                                              0 if max_tokens is None else int(max_tokens),
+                                              _iptr(ids), cap, _iptr(n), _iptr(hit), _iptr(em)))
+        return [(ids[b, : n[b]].tolist(), bool(hit[b]), bool(em[b])) for b in range(B)]
+
+    def get_emitted(self, state: StreamingState) -> List[List[int]]:
+        """getEmittedText (MoonshineStreaming.swift:171-173) as id segments."""
+        cap = 1024
+        while True:
+            buf = np.zeros(cap, dtype=np.int32)
+            n = C.c_int32()
+            s = _L().ms_stream_emitted(state._h, _iptr(buf), cap, C.byref(n))
+            if s == MS_ERR_CAPACITY:
+                cap = n.value + 1
+                continue
+            _check(s)
+            break
+        segs, cur = [], []
+        for t in buf[: n.value].tolist():
+            if t == -1:
+                segs.append(cur)
+                cur = []
+            else:
+                cur.append(t)
+        return segs
+
+
+def kernel_launches() -> int:
+    return int(_L().ms_kernel_launches())
+
+
+def reset_kernel_launches() -> None:
+    _L().ms_reset_kernel_launches()

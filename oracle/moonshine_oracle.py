@@ -316,6 +316,8 @@ class Oracle:
     def encode(self, features):
         """MoonshineEncoder.callAsFunction (MoonshineEncoder.swift:171-177)."""
         x = np.asarray(features, dtype=self.dt)
+        if x.shape[0] == 0:
+            return x
         for i in range(self.cfg.encoder.num_hidden_layers):
             x = self._encoder_layer(x, i)
         return _layer_norm(x, self.w["encoder.final_norm.weight"] + 1.0)

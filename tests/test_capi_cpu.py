@@ -1,0 +1,60 @@
+"""Host-side checks of the C ABI that need no GPU: the library loads, exports every
+symbol include/moonshine_b200.h declares, and reports argument errors with a status."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "moonshine_b200.h")
+
+
+def declared_functions():
+    txt = open(HEADER).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(ms_[a-z0-9_]+)\s*\(", txt)))
+
+
+def test_header_declares_the_api():
+    names = declared_functions()
+    for n in ("ms_model_load", "ms_generate", "ms_stream_create", "ms_stream_transcribe",
+              "ms_stream_add_audio", "ms_last_error"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    import moonshine_b200 as mb
+    lib = ctypes.CDLL(mb.LIB_PATH)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_defaults_and_argument_errors():
+    import moonshine_b200 as mb
+    L = mb._L()
+    o = mb._Options()
+    L.ms_options_default(ctypes.byref(o))
+    assert (o.device, o.kv_dtype, o.max_batch) == (0, mb.KV_F16, 64)
+    p = mb._GenParams()
+    L.ms_gen_params_default(ctypes.byref(p))
+    assert p.chunk_duration == 30.0 and p.temperature == 0.0
+    sc = mb._StreamingConfig()
+    L.ms_streaming_config_default(ctypes.byref(sc))
+    assert (sc.max_memory_frames, sc.min_segment_frames) == (100000, 250)
+    h = ctypes.c_void_p()
+    assert L.ms_model_load(None, None, ctypes.byref(h)) == 1
+    assert b"non-null" in L.ms_last_error()
+    n = ctypes.c_int32()
+    assert L.ms_generate(None, None, 0, None, None, 0, ctypes.byref(n), None, None) == 1
+    assert L.ms_stream_start(None) == 1
+    assert L.ms_model_sample_rate(None) == 0
+    assert b"sm_100a" in L.ms_version()
+
+
+@pytest.mark.skipif(os.path.exists("/dev/nvidia0"), reason="a GPU is present")
+def test_load_without_gpu_reports_cuda_error(tmp_path):
+    import moonshine_b200 as mb
+    with pytest.raises(mb.MoonshineError) as ei:
+        mb.MoonshineModel.load(str(tmp_path))
+    assert ei.value.status in (3, 7)

@@ -1,0 +1,130 @@
+"""CUDA path vs the CPU oracle on seeded random-init models and synthetic audio.
+
+Token ids must be identical; logits must agree within 1e-3 (fp32 weights) measured as
+max |gpu - oracle| / max |oracle| per decoder call."""
+import numpy as np
+import pytest
+
+from moonshine_b200 import synth
+from util import (FP32_LOGIT_TOL, assert_logits_close, model_dir, oracle_for, rel_err,
+                  with_config)
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def tiny_dir(model_root):
+    return model_dir(model_root, "tiny")
+
+
+@pytest.fixture(scope="module")
+def tiny(tiny_dir):
+    import moonshine_b200 as mb
+    return mb.MoonshineModel.load(tiny_dir)
+
+
+@pytest.mark.parametrize("n_samples,seed", [(32000, 7), (105600, 0), (12345, 3)])
+def test_encode_matches_oracle(tiny, tiny_dir, n_samples, seed):
+    audio = synth.synth_audio(n_samples, seed)
+    mem = tiny.encode(audio)
+    ref = oracle_for(tiny_dir).memory_for(audio)
+    assert mem.shape == ref.shape
+    assert rel_err(mem, ref) < 1e-4
+
+
+@pytest.mark.parametrize("kv_fp16", [False, True])
+def test_forced_decode_6p6s(tiny, tiny_dir, kv_fp16):
+    """6.6 s of audio, 64 forced tokens, EOS ignored (the batch-1 tiny workload)."""
+    audio = synth.synth_audio(105600, 0)
+    tiny.enable_float16_kv_cache(kv_fp16)
+    out = tiny.generate(audio, forced_len=64, return_logits=True)
+    o = oracle_for(tiny_dir)
+    ids, _, logits, margins = o.greedy(o.memory_for(audio), 64, kv_fp16, forced_len=64, keep_logits=True)
+    assert out.tokens == ids
+    assert_logits_close(out.logits[:64], logits, FP32_LOGIT_TOL)
+
+
+@pytest.mark.parametrize("kv_fp16", [False, True])
+def test_teacher_forced_logits(tiny, tiny_dir, kv_fp16):
+    """Random fed-back ids exercise many embedding rows and positions."""
+    audio = synth.synth_audio(48000, 11)
+    teacher = np.random.Generator(np.random.PCG64(5)).integers(0, 32768, size=40).astype(np.int32)
+    tiny.enable_float16_kv_cache(kv_fp16)
+    out = tiny.generate(audio, forced_len=40, teacher_ids=teacher, return_logits=True)
+    o = oracle_for(tiny_dir)
+    ids, _, logits, _ = o.greedy(o.memory_for(audio), 40, kv_fp16, teacher=teacher.tolist(), keep_logits=True)
+    assert out.tokens == ids
+    assert_logits_close(out.logits[:40], logits, FP32_LOGIT_TOL)
+
+
+def test_default_token_limit_and_max_tokens(tiny, tiny_dir):
+    """limit = min(maxTokens, ceil(dur * 6.5)) (MoonshineModel.swift:200-201)."""
+    audio = synth.synth_audio(105600, 0)
+    tiny.enable_float16_kv_cache(True)
+    out = tiny.generate(audio)
+    assert len(out.tokens) == int(np.ceil(6.6 * 6.5))
+    assert out.tokens == oracle_for(tiny_dir).generate(audio, kv_fp16=True)
+    out5 = tiny.generate(audio, max_tokens=5)
+    assert out5.tokens == out.tokens[:5]
+
+
+def test_eos_stops_like_the_reference(tiny_dir, model_root, tmp_path):
+    """A model whose eos id is a token the greedy loop produces stops there and drops it."""
+    import moonshine_b200 as mb
+    audio = synth.synth_audio(64000, 21)
+    o = oracle_for(tiny_dir)
+    ids, _, _, _ = o.greedy(o.memory_for(audio), 30, True, forced_len=30)
+    # stop on the first id that differs from the first one, else on the very first id
+    k = next((i for i, t in enumerate(ids) if t != ids[0]), 0)
+    eos_dir = with_config(tiny_dir, str(tmp_path / "eos"), eos_token_id=int(ids[k]))
+    m = mb.MoonshineModel.load(eos_dir)
+    out = m.generate(audio, max_tokens=30)
+    ref = oracle_for(eos_dir).generate(audio, max_tokens=30, kv_fp16=True)
+    assert out.tokens == ref == ids[:k]
+    assert out.hit_eos
+
+
+def test_multi_chunk_generate(tiny, tiny_dir):
+    """Audio longer than chunkDuration is decoded chunk by chunk (MoonshineModel.swift:151-162)."""
+    audio = synth.synth_audio(16000 * 12 + 4321, 13)
+    tiny.enable_float16_kv_cache(True)
+    out = tiny.generate(audio, chunk_duration=5.0, forced_len=12)
+    ref = oracle_for(tiny_dir).generate(audio, kv_fp16=True, chunk_duration=5.0, forced_len=12)
+    assert out.tokens == ref
+    assert len(ref) == 3 * 12
+
+
+@pytest.mark.parametrize("n", [0, 1, 79, 80, 81, 159, 161, 400])
+def test_tiny_inputs(tiny, tiny_dir, n):
+    """Empty audio, sub-frame audio and a handful of frames (tail samples dropped)."""
+    audio = synth.synth_audio(n, 17) if n else np.zeros(0, np.float32)
+    tiny.enable_float16_kv_cache(True)
+    out = tiny.generate(audio)
+    assert out.tokens == oracle_for(tiny_dir).generate(audio, kv_fp16=True)
+
+
+def test_invalid_arguments(tiny):
+    import moonshine_b200 as mb
+    with pytest.raises(mb.MoonshineError) as ei:
+        tiny.generate(np.zeros(1600, np.float32), temperature=0.5)
+    assert ei.value.status == 8
+    with pytest.raises(mb.MoonshineError):
+        mb.MoonshineModel.load("/nonexistent/model/dir")
+
+
+def test_small_arch_head_dim_64(model_root):
+    """hd 64 -> rotary width 50 (int(64*0.8)=51 rounded down), 10+10 layers."""
+    import moonshine_b200 as mb
+    d = model_dir(model_root, "small", vocab_size=2048, max_position_embeddings=512)
+    m = mb.MoonshineModel.load(d)
+    audio = synth.synth_audio(32000, 4)
+    teacher = np.random.Generator(np.random.PCG64(6)).integers(0, 2048, size=16).astype(np.int32)
+    o = oracle_for(d)
+    mem = o.memory_for(audio)
+    assert rel_err(m.encode(audio), mem) < 1e-4
+    for kv in (False, True):
+        m.enable_float16_kv_cache(kv)
+        out = m.generate(audio, forced_len=16, teacher_ids=teacher, return_logits=True)
+        ids, _, logits, _ = o.greedy(mem, 16, kv, teacher=teacher.tolist(), keep_logits=True)
+        assert out.tokens == ids
+        assert_logits_close(out.logits[:16], logits, FP32_LOGIT_TOL)
