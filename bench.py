@@ -202,7 +202,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seconds", type=float, default=30.0, help="audio length (profiling cases)")
+    ap.add_argument("--tokens", type=int, default=200, help="forced decode length (profiling cases)")
     args = ap.parse_args()
+    global N_SAMPLES, FORCED, WORKLOAD
+    if args.seconds != 30.0 or args.tokens != 200:
+        N_SAMPLES = int(args.seconds * 16000) // 80 * 80
+        FORCED = args.tokens
+        WORKLOAD = (f"tiny fp32 weights, fp16 KV, batch 1, {args.seconds:g} s audio, "
+                    f"{FORCED} forced tokens (encode + decode)")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -214,6 +214,13 @@ const char* ms_last_error(void);
 int64_t ms_kernel_launches(void);
 void ms_reset_kernel_launches(void);
 
+/* Phase trace of the batch-1 decode kernel (the device-side counterpart of the
+ * reference's `profile:` timings, MoonshineModel.swift:167-175): when enabled, the next
+ * decode records a %globaltimer stamp (ns) at its start and after every grid-wide phase
+ * barrier; ms_decode_trace copies the stamps of the last decode. */
+ms_status ms_enable_decode_trace(ms_model* model, int32_t enabled);
+ms_status ms_decode_trace(ms_model* model, uint64_t* stamps_out, int32_t cap, int32_t* n_out);
+
 /* Library version string. */
 const char* ms_version(void);
 

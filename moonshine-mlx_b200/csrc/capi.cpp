@@ -139,6 +139,25 @@ int64_t ms_kernel_launches(void) { return launch_counter(); }
 void ms_reset_kernel_launches(void) { launch_counter() = 0; }
 const char* ms_version(void) { return "moonshine-b200 0.1 (sm_100a)"; }
 
+ms_status ms_enable_decode_trace(ms_model* model, int32_t enabled) {
+    if (!model) return fail(MS_ERR_INVALID_ARG, "null model");
+    Model* m = reinterpret_cast<Model*>(model);
+    std::lock_guard<std::mutex> g(m->mu);
+    m->trace_enabled = enabled != 0;
+    return MS_OK;
+}
+
+ms_status ms_decode_trace(ms_model* model, uint64_t* stamps_out, int32_t cap, int32_t* n_out) {
+    if (!model || !n_out || cap < 0 || (cap > 0 && !stamps_out)) return fail(MS_ERR_INVALID_ARG, "bad argument");
+    Model* m = reinterpret_cast<Model*>(model);
+    std::lock_guard<std::mutex> g(m->mu);
+    const int32_t n = (int32_t)m->last_trace.size();
+    *n_out = n;
+    for (int32_t i = 0; i < n && i < cap; ++i) stamps_out[i] = m->last_trace[i];
+    if (n > cap) return fail(MS_ERR_CAPACITY, "stamps buffer too small");
+    return MS_OK;
+}
+
 ms_status ms_model_load(const char* dir, const ms_options* opts, ms_model** out) {
     return guarded([&]() -> ms_status {
         if (!dir || !out) return fail(MS_ERR_INVALID_ARG, "dir and out must be non-null");

@@ -89,12 +89,15 @@ struct DecodeParams {
     const void* cross_stored;
     int m_cap, M;
     // scratch (device)
-    float* x;          // [d]
-    float* qbuf;       // [H*hd]
-    float* kvnew;      // [2*KVH*hd]
-    float* attn;       // [H*hd]
-    float* part;       // cross-attention partials [H][n_chunks][hd + 2]
-    float* gbuf;       // [I]
+    float* xb;         // [2][d] residual stream, ping-pong across layers
+    float* qbuf;       // [H*hd] self-attention query (after RoPE)
+    float* qc;         // [H*hd] cross-attention query
+    float* kvnew;      // [2*KVH*hd] this step's K/V (fp32)
+    float* x1;         // [d] residual after self-attention
+    float* x2;         // [d] residual after cross-attention
+    float* spart;      // [H * self_chunks][hd + 2] self-attention chunk partials
+    float* cpart;      // [rounds][grid][8][hd + 2] cross-attention per-CTA partials
+    float* gbuf;       // [I] SwiGLU output
     float* amax_val;   // [gridDim]
     int* amax_idx;     // [gridDim]
     // token loop
@@ -109,11 +112,18 @@ struct DecodeParams {
     int* hit_eos;
     unsigned* bar_count;
     unsigned* status;
+    unsigned long long* trace;  // nullable: %globaltimer stamps (start + after each barrier)
+    int trace_cap;
+    int region_bytes;           // per-warp prefetch region (set by the launcher)
 };
 
 // Persistent cooperative decode kernel: runs up to n_steps greedy decoder calls.
-cudaError_t launch_decode_b1(const DecodeParams& p, int grid, int block, cudaStream_t stream);
+cudaError_t launch_decode_b1(const DecodeParams& p, int grid, cudaStream_t stream);
 int decode_b1_block_threads();
+bool decode_b1_supports_head_dim(int hd);
 int decode_chunk_keys();
+// Scratch sizes (floats) the decode kernel needs for `grid` CTAs.
+size_t decode_b1_spart_floats(int H, int hd, int t_cap);
+size_t decode_b1_cpart_floats(int H, int hd, int m_cap, int grid);
 
 }  // namespace msb

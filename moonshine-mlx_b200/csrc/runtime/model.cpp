@@ -290,6 +290,11 @@ struct WeightSource {
         return t;
     }
     bool has(const std::string& k) const { return byname.count(k) != 0; }
+    const Tensor& need_any(const std::string& k) const {
+        auto it = byname.find(k);
+        if (it == byname.end()) throw MsError(MS_ERR_BAD_WEIGHTS, "missing weight " + k);
+        return *it->second;
+    }
     std::vector<float> f32(const std::string& k, std::vector<int64_t> shape) const {
         return to_f32(need(k, shape));
     }
@@ -363,6 +368,8 @@ static void validate(const Config& c) {
     if (c.head_dim % 4 || c.e_head_dim % 4 || c.head_dim > 64 || c.e_head_dim > 128)
         bad("head_dim must be a multiple of 4 (decoder <= 64, encoder <= 128)");
     if (c.heads % c.kv_heads || c.e_heads % c.e_kv_heads) bad("heads must be a multiple of kv heads");
+    if (!decode_b1_supports_head_dim(c.head_dim)) bad("decoder head_dim must be 32, 40, 48 or 64");
+    if (c.heads > 16) bad("at most 16 decoder heads");
     if (c.hidden > 1024 || c.e_hidden > 1024) bad("hidden size above 1024");
     if (c.frame_len() <= 0 || c.frame_len() > 128) bad("frame length must be in [1, 128]");
     if (c.layers <= 0 || c.e_layers <= 0 || c.vocab <= 0) bad("empty model");
@@ -397,7 +404,11 @@ Model* load_model(const std::string& dir, const ms_options& o) {
     const int eHD = c.e_heads * c.e_head_dim, eKVD = c.e_kv_heads * c.e_head_dim;
     const int HD = c.heads * c.head_dim, KVD = c.kv_heads * c.head_dim;
 
-    m->log_k = m->upload(ws.f32("encoder.embedder.comp.log_k", {}));
+    // log_k is a scalar; writers store it as shape [] or [1]
+    m->log_k = m->upload(ws.has("encoder.embedder.comp.log_k") &&
+                                 ws.need_any("encoder.embedder.comp.log_k").numel() == 1
+                             ? to_f32(ws.need_any("encoder.embedder.comp.log_k"))
+                             : ws.f32("encoder.embedder.comp.log_k", {}));
     m->lin_w = m->upload(ws.f32("encoder.embedder.linear.weight", {ed, fl}));
     m->conv1_w = m->upload(ws.conv("encoder.embedder.conv1.weight", 2 * ed, ed, 5));
     m->conv1_b = m->upload(ws.f32("encoder.embedder.conv1.bias", {2 * ed}));
@@ -552,10 +563,8 @@ int Model::encode_device(const float* audio_dev, int64_t n_samples, int pos_offs
 
 void Model::ensure_decode(int m_cap, int t_cap, bool want_logits, int V) {  // m_cap: memory rows
     const Config& c = cfg;
-    const int hd = c.head_dim, KVH = c.kv_heads, L = c.layers, d = c.hidden;
-    const int HD = c.heads * hd;
-    const int chunk = decode_chunk_keys();
-    ws.dpart.ensure((size_t)c.heads * ((m_cap + chunk - 1) / chunk) * (hd + 2) * 4);
+    const int hd = c.head_dim, KVH = c.kv_heads, L = c.layers, d = c.hidden, H = c.heads;
+    const int HD = H * hd;
     if (t_cap > ws.t_cap) {
         const size_t n = (size_t)L * KVH * t_cap * hd;
         ws.self_k.ensure(n * 4);
@@ -564,11 +573,15 @@ void Model::ensure_decode(int m_cap, int t_cap, bool want_logits, int V) {  // m
         ws.t_cap = t_cap;
     }
     if (want_logits) ws.logits.ensure((size_t)t_cap * V * 4);
-    ws.dx.ensure(d * 4);
-    ws.dq.ensure(HD * 4);
-    ws.dkvnew.ensure(2 * KVH * hd * 4);
-    ws.dattn.ensure(HD * 4);
-    ws.dg.ensure(c.inter * 4);
+    ws.dx.ensure((size_t)2 * d * 4);
+    ws.dq.ensure((size_t)HD * 4);
+    ws.dqc.ensure((size_t)HD * 4);
+    ws.dkvnew.ensure((size_t)2 * KVH * hd * 4);
+    ws.dps.ensure((size_t)H * d * 4);
+    ws.dpc.ensure((size_t)H * d * 4);
+    ws.dspart.ensure(decode_b1_spart_floats(H, hd, ws.t_cap) * 4);
+    ws.dpart.ensure(decode_b1_cpart_floats(H, hd, m_cap, num_sms) * 4);
+    ws.dg.ensure((size_t)c.inter * 4);
     ws.amax_v.ensure(num_sms * 4);
     ws.amax_i.ensure(num_sms * 4);
     ws.flags.ensure(64);
@@ -632,11 +645,14 @@ Model::DecodeResult Model::decode(const float* cross32, const void* cross_stored
     p.cross_stored = cross_stored;
     p.m_cap = m_cap;
     p.M = M;
-    p.x = ws.dx.as<float>();
+    p.xb = ws.dx.as<float>();
     p.qbuf = ws.dq.as<float>();
+    p.qc = ws.dqc.as<float>();
     p.kvnew = ws.dkvnew.as<float>();
-    p.attn = ws.dattn.as<float>();
-    p.part = ws.dpart.as<float>();
+    p.x1 = ws.dps.as<float>();
+    p.x2 = ws.dpc.as<float>();
+    p.spart = ws.dspart.as<float>();
+    p.cpart = ws.dpart.as<float>();
     p.gbuf = ws.dg.as<float>();
     p.amax_val = ws.amax_v.as<float>();
     p.amax_idx = ws.amax_i.as<int>();
@@ -652,10 +668,23 @@ Model::DecodeResult Model::decode(const float* cross32, const void* cross_stored
     p.status = flags + 1;
     p.n_done = reinterpret_cast<int*>(flags + 2);
     p.hit_eos = reinterpret_cast<int*>(flags + 3);
+    int trace_n = 0;
+    if (trace_enabled) {
+        trace_n = 2 + n_steps * (c.layers * 8 * 4 + 4);
+        trace_buf.ensure((size_t)trace_n * 8);
+        MSB_CUDA(cudaMemsetAsync(trace_buf.p, 0, (size_t)trace_n * 8, stream));
+        p.trace = trace_buf.as<unsigned long long>();
+        p.trace_cap = trace_n;
+    }
     MSB_CUDA(cudaMemsetAsync(flags, 0, 16, stream));
-    MSB_CUDA(launch_decode_b1(p, num_sms, decode_b1_block_threads(), stream));
+    MSB_CUDA(launch_decode_b1(p, num_sms, stream));
     unsigned hf[4];
     MSB_CUDA(cudaMemcpyAsync(hf, flags, 16, cudaMemcpyDeviceToHost, stream));
+    if (trace_n) {
+        last_trace.resize(trace_n);
+        MSB_CUDA(cudaMemcpyAsync(last_trace.data(), trace_buf.p, (size_t)trace_n * 8, cudaMemcpyDeviceToHost,
+                                 stream));
+    }
     MSB_CUDA(cudaStreamSynchronize(stream));
     if (hf[1] == DEV_BARRIER_TIMEOUT) throw MsError(MS_ERR_TIMEOUT, "decode kernel: grid barrier timed out");
     if (hf[1] == DEV_BAD_TOKEN) throw MsError(MS_ERR_INVALID_ARG, "decode kernel: token id out of range");

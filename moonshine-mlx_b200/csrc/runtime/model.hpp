@@ -72,7 +72,7 @@ struct EncLayer {
 struct Workspace {
     DevBuf audio, feat1p, feat2p, x, h, qkv, attn, f, memory, memproj;
     DevBuf cross32, cross16, self_k, self_v;
-    DevBuf dx, dq, dkvnew, dattn, dpart, dg, amax_v, amax_i, ids, logits, flags;
+    DevBuf dx, dq, dqc, dkvnew, dps, dpc, dspart, dpart, dg, amax_v, amax_i, ids, logits, flags;
     int m_cap = 0, t_cap = 0;
 };
 
@@ -100,6 +100,9 @@ struct Model {
     int rope_cap = 0;
 
     Workspace ws;
+    bool trace_enabled = false;
+    DevBuf trace_buf;
+    std::vector<unsigned long long> last_trace;
 
     ~Model();
     float* upload(const std::vector<float>& v);

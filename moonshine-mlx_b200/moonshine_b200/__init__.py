@@ -116,6 +116,8 @@ def _load_lib() -> C.CDLL:
                                                  C.c_int32, i32p, i32p, i32p]),
         "ms_stream_emitted": (C.c_int, [P, i32p, C.c_int32, i32p]),
         "ms_stream_memory_len": (C.c_int32, [P]),
+        "ms_enable_decode_trace": (C.c_int, [P, C.c_int32]),
+        "ms_decode_trace": (C.c_int, [P, C.POINTER(C.c_uint64), C.c_int32, i32p]),
         "ms_last_error": (C.c_char_p, []),
         "ms_kernel_launches": (C.c_int64, []),
         "ms_reset_kernel_launches": (None, []),
@@ -300,6 +302,18 @@ class MoonshineModel:
         _check(_L().ms_generate_device(self._h, C.c_void_p(audio_dev_ptr), int(n_samples), C.byref(p),
                                        C.c_void_p(ids_dev_ptr), int(cap), C.byref(n), C.byref(st)))
         return n.value, st
+
+    def enable_decode_trace(self, enabled: bool = True) -> None:
+        _check(_L().ms_enable_decode_trace(self._h, 1 if enabled else 0))
+
+    def decode_trace(self) -> np.ndarray:
+        """%globaltimer stamps (ns) of the last traced decode: start, then one per barrier."""
+        n = C.c_int32()
+        _L().ms_decode_trace(self._h, None, 0, C.byref(n))
+        buf = np.zeros(max(n.value, 1), dtype=np.uint64)
+        _check(_L().ms_decode_trace(self._h, buf.ctypes.data_as(C.POINTER(C.c_uint64)), buf.shape[0],
+                                    C.byref(n)))
+        return buf[: n.value]
 
     @property
     def cuda_stream(self) -> int:
