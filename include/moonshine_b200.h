@@ -162,6 +162,27 @@ ms_status ms_generate_batch(ms_model* model, const float* const* audios,
 ms_status ms_encode(ms_model* model, const float* audio, int64_t n_samples,
                     float* memory_out, int64_t cap_floats, int32_t* n_frames);
 
+/* Greedy decode that allocates no device memory.  No counterpart in the reference: it
+ * exists for callers that cannot call cudaMalloc once they are running -- a real-time
+ * audio callback, where an allocation can block and synchronise the device past the
+ * callback's deadline, or a host that runs inside a fixed, pre-reserved GPU memory budget.
+ *
+ * The caller passes encoder memory rows already in device memory of the model's GPU
+ * (memory_dev, [frames * hidden] float32, 16-byte aligned; e.g. ms_encode's output copied
+ * to the device) and a device buffer ids_dev of n_tokens int32.  The call runs up to
+ * n_tokens decoder calls from BOS (forced != 0: exactly n_tokens, EOS fed back like any
+ * id), writes the ids to ids_dev and their count to *n_out (host), like ms_generate_device
+ * for one chunk.  The cross-attention K/V, the self-attention K/V cache and the decode
+ * working buffers live in one static 16 MiB device array that every GPU loading this
+ * library holds until the process exits: with the tiny model that covers 500 memory frames
+ * (10 s of audio) and 128 decoder calls; larger requests fail with MS_ERR_CAPACITY and a
+ * message giving the bytes needed.  The first call on a device looks up the array's device
+ * address; make that first call before any stream capture.  Every call reuses the array:
+ * calls whose GPU work overlaps race on it (calls through this library are serialised). */
+ms_status ms_decode_memory_static(ms_model* model, const float* memory_dev, int32_t frames,
+                                  int32_t n_tokens, int32_t forced, int32_t* ids_dev,
+                                  int32_t* n_out, int32_t* hit_eos);
+
 /* ------------------------------------------------------------------- streaming */
 
 /* StreamingConfig (MoonshineStreaming.swift:47-62). */

@@ -24,6 +24,11 @@ ms_status fail(ms_status s, const std::string& m) {
     g_err = m;
     return s;
 }
+}  // namespace
+
+void set_last_error(const std::string& m) { g_err = m; }
+
+namespace {
 
 template <class F>
 ms_status guarded(F&& f) {

@@ -133,5 +133,7 @@ struct Model {
 };
 
 ms_status to_status(const std::exception& e);
+// Sets the thread-local message returned by ms_last_error().
+void set_last_error(const std::string& m);
 
 }  // namespace msb

@@ -103,6 +103,8 @@ def _load_lib() -> C.CDLL:
         "ms_generate_device": (C.c_int, [P, C.c_void_p, C.c_int64, C.POINTER(_GenParams), C.c_void_p,
                                          C.c_int32, i32p, C.POINTER(_GenStats)]),
         "ms_model_stream": (C.c_void_p, [P]),
+        "ms_decode_memory_static": (C.c_int, [P, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
+                                              i32p, i32p]),
         "ms_encode": (C.c_int, [P, f32p, C.c_int64, f32p, C.c_int64, i32p]),
         "ms_stream_create": (C.c_int, [P, C.POINTER(P)]),
         "ms_stream_free": (None, [P]),
@@ -314,6 +316,16 @@ class MoonshineModel:
         _check(_L().ms_decode_trace(self._h, buf.ctypes.data_as(C.POINTER(C.c_uint64)), buf.shape[0],
                                     C.byref(n)))
         return buf[: n.value]
+
+    def decode_memory_static(self, memory_dev_ptr: int, frames: int, ids_dev_ptr: int, n_tokens: int,
+                             forced: bool = True):
+        """ms_decode_memory_static: decode without any device allocation, from memory rows
+        in device memory into a device ids buffer.  Returns (n_ids, hit_eos)."""
+        n, hit = C.c_int32(), C.c_int32()
+        _check(_L().ms_decode_memory_static(self._h, C.c_void_p(memory_dev_ptr), int(frames), int(n_tokens),
+                                            1 if forced else 0, C.c_void_p(ids_dev_ptr), C.byref(n),
+                                            C.byref(hit)))
+        return n.value, bool(hit.value)
 
     @property
     def cuda_stream(self) -> int:
