@@ -57,6 +57,17 @@ def decode_bytes_per_launch(cfg, M, n_tokens, kv_bytes=2):
     return n_tokens * (w + emb) + cross0 + (n_tokens - 1) * cross + self_reads + self_writes
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode launch (16 decoder calls, 1500
+# memory frames, fp16 KV) from an ncu capture; per-call traffic is flat after the first call.
+NCU_DECODE_BYTES_16CALLS_1500F = 830.744e6 + 5.621e6
+
+
+def decode_traffic_per_launch(M, n_tokens):
+    if M != 1500:
+        return None
+    return int(NCU_DECODE_BYTES_16CALLS_1500F * n_tokens / 16)
+
+
 def measured_peak():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -204,6 +215,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seconds", type=float, default=30.0, help="audio length (profiling cases)")
     ap.add_argument("--tokens", type=int, default=200, help="forced decode length (profiling cases)")
+    ap.add_argument("--flush-mb", type=int, default=512, help="L2-flush buffer written between steps")
     args = ap.parse_args()
     global N_SAMPLES, FORCED, WORKLOAD
     if args.seconds != 30.0 or args.tokens != 200:
@@ -251,7 +263,8 @@ def main():
     audio_pinned = torch.from_numpy(audio_np).pin_memory()
     audio_dev = audio_pinned.to(f"cuda:{local}")
     ids_dev = torch.zeros(FORCED + 8, dtype=torch.int32, device=f"cuda:{local}")
-    flush = torch.empty(512 << 20, dtype=torch.uint8, device=f"cuda:{local}")  # > 126 MB L2
+    # > 126 MB L2; profiling captures may shrink it (less device memory to save/restore)
+    flush = torch.empty(max(1, args.flush_mb) << 20, dtype=torch.uint8, device=f"cuda:{local}")
     torch.cuda.synchronize()
 
     def run_device():
@@ -320,7 +333,7 @@ def main():
             "data": "synthetic (seeded random-init weights, seeded noise+sinusoid audio)",
             "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": FORCED,
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                       "l2": "512 MB buffer written between timed steps"},
+                       "l2": f"{args.flush_mb} MB buffer written between timed steps"},
             "ms_per_token_decode": round(dec_avg / FORCED, 5),
             "encode_ms": round(statistics.mean(enc_ms), 4),
             "rtfx": round((N_SAMPLES / 16000.0) / (t_rank / args.steps / 1e3), 1),
@@ -328,7 +341,9 @@ def main():
             "roofline": {"bound": "hbm", "kernel": "decode_b1_kernel", "achieved": round(achieved, 1),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(bytes_launch),
-                         "launch_ms": round(dec_avg, 4), "traffic": None},
+                         "launch_ms": round(dec_avg, 4), "traffic": decode_traffic_per_launch(M, FORCED),
+                         "traffic_source": "ncu dram__bytes of a 16-call launch at 1500 frames, scaled by "
+                                           "decoder calls (profiles/decode_b1_tiny_30s_16tok.md)"},
             "e2e": {"value": round(total_tokens / (t_e2e / 1e3), 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": N_SAMPLES * 4, "d2h_bytes_per_step": FORCED * 4 + 16},
             "clocks": clocks.summary(),
