@@ -1,0 +1,330 @@
+// bf16 tensor-core GEMM for sm_100a: TMA -> shared memory -> tcgen05.mma -> TMEM -> fused
+// epilogue.  C[m, n] = epi( sum_k A[m, k] * B[n, k] ), A and B K-major bf16, fp32 accumulate.
+//
+// One CTA computes a 128 x BN output tile with four warps:
+//   warp 0 (one lane)  TMA producer: STAGES-deep ring of 128x64 A / BNx64 B tiles, 128-byte
+//                      swizzled, completion tracked by mbarrier transaction counts
+//   warp 1 (one lane)  MMA issuer: 4 x tcgen05.mma (K = 16 each) per 64-wide k-block into a
+//                      128 x BN fp32 accumulator in tensor memory; tcgen05.commit frees the
+//                      stage and, after the last k-block, signals the epilogue
+//   all four warps     epilogue: tcgen05.ld of their 32 accumulator lanes (= rows), then
+//                      bias / activation / residual / bf16 or fp32 store / K-V scatter
+//
+// A is addressed through a 3-D tensor map (k, y, z) so a causal stride-2 convolution runs as
+// `taps` accumulated GEMMs: tap t reads A at (k, y_t, m + z_t) and B at column t*K_tap + k.
+// For a plain GEMM taps = 1, y = z = 0.
+//
+// Every mbarrier wait is bounded; a timeout records an error code and the CTA drains its
+// in-flight copies (again bounded), frees its tensor memory and exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace msb {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;         // bf16: 128 bytes = one 128B-swizzle row
+constexpr int STAGES = 4;
+constexpr int TC_THREADS = 128;
+constexpr uint32_t WAIT_LIMIT = 1u << 22;   // polls of a bounded mbarrier wait
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// Bounded parity wait; returns false after WAIT_LIMIT polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major tile of 128-byte rows with the 128B swizzle, 8-row
+// groups 1024 bytes apart (stride byte offset), leading byte offset unused (1), version 1.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor for kind::f16: bf16 A and B (K-major), fp32 accumulate, M x N.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int BN>
+struct alignas(1024) TcSmem {
+    __nv_bfloat16 a[STAGES][BM * BK];
+    __nv_bfloat16 b[STAGES][BN * BK];
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t done;
+    uint32_t tmem_base;
+};
+
+__device__ __forceinline__ void store_out(const TcGemmArgs& g, int m, int n, float v) {
+    const GemmEpilogue& ep = g.ep;
+    if (ep.bias) v += ep.bias[n];
+    if (ep.act == ACT_SILU) v = silu(v);
+    else if (ep.act == ACT_GELU) v = gelu_erf(v);
+    if (ep.residual) v += ep.residual[(size_t)m * ep.ldr + n];
+    if (ep.kv_scatter) {
+        const int kvdim = ep.kv_heads * ep.head_dim;
+        const int layer = n / (2 * kvdim);
+        const int rem = n - layer * 2 * kvdim;
+        const int kv = rem / kvdim;
+        const int c = rem - kv * kvdim;
+        const int head = c / ep.head_dim;
+        const int dim = c - head * ep.head_dim;
+        const size_t idx = ((((size_t)layer * 2 + kv) * ep.kv_heads + head) * ep.frame_cap +
+                            (size_t)(m + ep.frame_offset)) * ep.head_dim + dim;
+        if (ep.kv_out32) ep.kv_out32[idx] = v;
+        if (ep.kv_out16) reinterpret_cast<__half*>(ep.kv_out16)[idx] = __float2half_rn(v);
+        return;
+    }
+    if (ep.out) ep.out[(size_t)m * ep.ldc + n] = v;
+    if (g.out_bf16) g.out_bf16[(size_t)m * g.ldc_bf16 + n] = __float2bfloat16_rn(v);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+               TcGemmArgs g) {
+    extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
+    TcSmem<BN>& s = *reinterpret_cast<TcSmem<BN>*>(
+        (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int nkb = g.taps * g.kb_per_tap;
+    constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
+    __shared__ int s_fail;
+
+    if (threadIdx.x == 0) {
+        s_fail = 0;
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&s.full[i], 1);
+            mbar_init(&s.empty[i], 1);
+        }
+        mbar_init(&s.done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {  // tensor memory: BN fp32 columns x 128 lanes
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s.tmem_base)),
+                     "r"((uint32_t)BN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = s.tmem_base;
+
+    int issued = 0;  // producer: k-blocks whose copies were issued
+    if (warp == 0 && lane == 0) {
+        for (int kb = 0; kb < nkb; ++kb) {
+            const int st = kb % STAGES;
+            if (kb >= STAGES && !mbar_wait(&s.empty[st], ((kb / STAGES) - 1) & 1)) {
+                atomicCAS(g.status, 0u, 5u);
+                s_fail = 1;
+                break;
+            }
+            const int tap = kb / g.kb_per_tap;
+            const int k0 = (kb - tap * g.kb_per_tap) * BK;
+            mbar_expect_tx(&s.full[st], A_BYTES + B_BYTES);
+            tma_load_3d(s.a[st], &tmap_a, &s.full[st], k0, g.tap_y[tap], m0 + g.tap_z[tap]);
+            tma_load_2d(s.b[st], &tmap_b, &s.full[st], tap * g.k_per_tap + k0, n0);
+            issued = kb + 1;
+        }
+    } else if (warp == 1 && lane == 0) {
+        const uint32_t idesc = idesc_bf16(BM, BN);
+        for (int kb = 0; kb < nkb; ++kb) {
+            const int st = kb % STAGES;
+            if (!mbar_wait(&s.full[st], (kb / STAGES) & 1)) {
+                atomicCAS(g.status, 0u, 5u);
+                s_fail = 1;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a_addr = smem_u32(s.a[st]), b_addr = smem_u32(s.b[st]);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {  // 16 bf16 = 32 bytes per MMA along K
+                mma_bf16(tmem, smem_desc_sw128(a_addr + k * 32), smem_desc_sw128(b_addr + k * 32), idesc,
+                         (kb > 0 || k > 0) ? 1u : 0u);
+            }
+            mma_commit(&s.empty[st]);
+        }
+        mma_commit(&s.done);
+    }
+    __syncwarp();
+    __syncthreads();  // role loops finished; s_fail is final
+
+    // epilogue: warp w owns accumulator lanes (rows) 32w .. 32w+31
+    bool ok = mbar_wait(&s.done, 0);
+    if (!ok) atomicCAS(g.status, 0u, 5u);
+    ok = __all_sync(FULL, ok) && !s_fail;  // tcgen05.ld below is warp-collective
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (ok) {
+        const int m = m0 + warp * 32 + lane;
+        const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+        for (int c0 = 0; c0 < BN; c0 += 8) {
+            float v[8];
+            tmem_ld8(lane_addr + c0, v);
+            if (m < g.M) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int n = n0 + c0 + i;
+                    if (n < g.N) store_out(g, m, n, v[i]);
+                }
+            }
+        }
+    }
+    // drain copies still in flight after a failure (bounded), then free tensor memory
+    if (warp == 0 && lane == 0 && s_fail) {
+        for (int kb = (issued > STAGES ? issued - STAGES : 0); kb < issued; ++kb)
+            mbar_wait(&s.full[kb % STAGES], (kb / STAGES) & 1);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN)
+                     : "memory");
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void* p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+}  // namespace
+
+bool tc_make_map_3d(CUtensorMap* map, const void* base, uint64_t dim_k, uint64_t dim_y, uint64_t dim_z,
+                    uint64_t stride_y_bytes, uint64_t stride_z_bytes, uint32_t box_z) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[3] = {dim_k, dim_y, dim_z};
+    const cuuint64_t strides[2] = {stride_y_bytes, stride_z_bytes};
+    const cuuint32_t box[3] = {(cuuint32_t)BK, 1, box_z};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool tc_make_map_2d(CUtensorMap* map, const void* base, uint64_t dim_k, uint64_t rows, uint64_t row_stride_bytes,
+                    uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {dim_k, rows};
+    const cuuint64_t strides[1] = {row_stride_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t launch_gemm_tc(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcGemmArgs& g, int bn,
+                           cudaStream_t stream) {
+    if (g.M <= 0 || g.N <= 0) return cudaSuccess;
+    if (g.taps < 1 || g.taps > 8 || g.kb_per_tap < 1 || !g.status) return cudaErrorInvalidValue;
+    const dim3 grid((g.N + bn - 1) / bn, (g.M + BM - 1) / BM);
+    ++launch_counter();
+    if (bn == 128) {
+        const size_t smem = sizeof(TcSmem<128>) + 1024;
+        static bool set128 = false;
+        if (!set128) {
+            cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem);
+            if (e != cudaSuccess) return e;
+            set128 = true;
+        }
+        gemm_tc_kernel<128><<<grid, TC_THREADS, smem, stream>>>(map_a, map_b, g);
+    } else if (bn == 64) {
+        const size_t smem = sizeof(TcSmem<64>) + 1024;
+        static bool set64 = false;
+        if (!set64) {
+            cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem);
+            if (e != cudaSuccess) return e;
+            set64 = true;
+        }
+        gemm_tc_kernel<64><<<grid, TC_THREADS, smem, stream>>>(map_a, map_b, g);
+    } else {
+        return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace msb

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
 #include <stdint.h>
 
 namespace msb {
@@ -40,6 +41,32 @@ struct GemmEpilogue {
 };
 cudaError_t launch_gemm_f32(const float* A, int lda, const float* B, int ldb, int M, int N,
                             int K, const GemmEpilogue& ep, cudaStream_t stream);
+
+// ---------------------------------------------------------------- bf16 tensor-core GEMM
+// C = epi(A * B^T) with A [M, K] and B [N, K] bf16 (K-major), fp32 accumulation in TMEM.
+// A goes through a 3-D tensor map (k, y, z); k-block kb belongs to tap kb / kb_per_tap and
+// reads A at (k, tap_y[tap], m + tap_z[tap]) and B at column tap * k_per_tap + k.
+struct TcGemmArgs {
+    int M = 0, N = 0;
+    int taps = 1, kb_per_tap = 0, k_per_tap = 0;
+    int tap_y[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int tap_z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    GemmEpilogue ep;                      // fp32 outputs / scatter (as the fp32 GEMM)
+    __nv_bfloat16* out_bf16 = nullptr;    // optional bf16 copy of the output [M, ldc_bf16]
+    int ldc_bf16 = 0;
+    unsigned* status = nullptr;           // device word; 5 = a bounded wait gave up
+};
+}  // namespace msb
+struct CUtensorMap_st;
+namespace msb {
+// Tensor maps (128B swizzle, 64-element k boxes).  A: dims (k, y, z) with byte strides of
+// y and z, box z rows; B: dims (k, rows) with a row stride, box `box_rows` rows.
+bool tc_make_map_3d(CUtensorMap_st* map, const void* base, uint64_t dim_k, uint64_t dim_y, uint64_t dim_z,
+                    uint64_t stride_y_bytes, uint64_t stride_z_bytes, uint32_t box_z);
+bool tc_make_map_2d(CUtensorMap_st* map, const void* base, uint64_t dim_k, uint64_t rows, uint64_t row_stride_bytes,
+                    uint32_t box_rows);
+cudaError_t launch_gemm_tc(const CUtensorMap_st& map_a, const CUtensorMap_st& map_b, const TcGemmArgs& g, int bn,
+                           cudaStream_t stream);
 
 // ---------------------------------------------------------------- encoder
 // Row LayerNorm (biased variance): out = (x-mean)/sqrt(var+eps) * (w + w_offset)
