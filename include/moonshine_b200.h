@@ -112,7 +112,10 @@ typedef struct {
     const int32_t* teacher_ids;/* nullable: feed these ids instead of the argmax (one per
                                   decoder call after BOS; needs forced_len = count) */
     int32_t n_teacher;
-    int32_t reserved[7];
+    int32_t reserved_i;
+    float* batch_logits;       /* nullable, ms_generate_batch only: [batch][cap][vocab]
+                                  logits of every decoder call */
+    int32_t reserved[4];
 } ms_gen_params;
 
 void ms_gen_params_default(ms_gen_params* p);
@@ -149,9 +152,12 @@ ms_status ms_generate_device(ms_model* model, const float* audio_dev, int64_t n_
  * calls with their own events. */
 void* ms_model_stream(ms_model* model);
 
-/* Batched offline generation: B independent utterances decoded together (no
- * counterpart in the reference, which is batch 1; each utterance's ids equal a
- * ms_generate call on it alone).  ids_out is [B * cap], n_out [B]. */
+/* Batched offline generation: B independent utterances decoded together (no counterpart
+ * in the reference, which is batch 1).  Utterances of at most one chunk (chunk_duration)
+ * are decoded in lockstep: every projection is one bf16 tensor-core GEMM over all B rows
+ * (fp32 accumulation, residual stream and softmax), so logits agree with a per-utterance
+ * ms_generate to bf16 precision.  Longer utterances fall back to per-utterance decoding.
+ * ids_out is [B * cap], n_out [B]; temperature and teacher ids are not supported. */
 ms_status ms_generate_batch(ms_model* model, const float* const* audios,
                             const int64_t* n_samples, int32_t batch,
                             const ms_gen_params* params, int32_t* ids_out, int32_t cap,

@@ -7,6 +7,7 @@
 
 #include "../../include/moonshine_b200.h"
 #include "runtime/model.hpp"
+#include "runtime/batch.hpp"
 #include "runtime/stream.hpp"
 
 namespace msb {
@@ -343,6 +344,77 @@ ms_status ms_generate_batch(ms_model* model, const float* const* audios, const i
         ms_gen_stats total;
         std::memset(&total, 0, sizeof(total));
         ms_status worst = MS_OK;
+        ms_gen_params gp;
+        ms_gen_params_default(&gp);
+        if (params) gp = *params;
+        if (gp.temperature != 0.f)
+            return fail(MS_ERR_UNSUPPORTED, "only greedy decoding (temperature 0) is supported");
+        Model& m = *reinterpret_cast<Model*>(model);
+        const double cd = gp.chunk_duration > 0 ? gp.chunk_duration : 30.0;
+        const int64_t chunk = (int64_t)(cd * (double)m.cfg.sample_rate);
+        bool one_chunk = batch > 0 && !gp.teacher_ids;
+        for (int32_t b = 0; b < batch && one_chunk; ++b)
+            one_chunk = audios[b] && n_samples[b] >= m.cfg.frame_len() && n_samples[b] <= chunk;
+        if (one_chunk) {
+            // lockstep decode of the whole batch on the tensor-core engine
+            std::lock_guard<std::mutex> g(m.mu);
+            MSB_CUDA(cudaSetDevice(m.device));
+            const int32_t max_tokens = gp.max_tokens > 0 ? gp.max_tokens : std::numeric_limits<int32_t>::max();
+            std::vector<int> limits(batch);
+            for (int32_t b = 0; b < batch; ++b) {
+                const double dur = (double)n_samples[b] / (double)m.cfg.sample_rate;
+                limits[b] = gp.forced_len > 0 ? gp.forced_len
+                                              : (int)std::min<int64_t>(max_tokens,
+                                                                       (int64_t)std::ceil(dur * m.cfg.max_tok_per_s));
+                if (limits[b] <= 0) return fail(MS_ERR_INVALID_ARG, "token limit must be positive");
+            }
+            int64_t total_samples = 0;
+            std::vector<int64_t> offs(batch);
+            for (int32_t b = 0; b < batch; ++b) {
+                offs[b] = total_samples;
+                total_samples += (n_samples[b] + 63) / 64 * 64;  // keep every utterance 256-byte aligned
+            }
+            m.ws.audio.ensure((size_t)total_samples * 4);
+            std::vector<const float*> dev(batch);
+            std::vector<int64_t> lens(n_samples, n_samples + batch);
+            for (int32_t b = 0; b < batch; ++b) {
+                dev[b] = m.ws.audio.as<float>() + offs[b];
+                MSB_CUDA(cudaMemcpyAsync(const_cast<float*>(dev[b]), audios[b], (size_t)n_samples[b] * 4,
+                                         cudaMemcpyHostToDevice, m.stream));
+            }
+            if (!m.batch) m.batch.reset(new BatchEngine(m));
+            cudaEvent_t t0, t1;
+            MSB_CUDA(cudaEventCreate(&t0));
+            MSB_CUDA(cudaEventCreate(&t1));
+            MSB_CUDA(cudaEventRecord(t0, m.stream));
+            BatchEngine::Result r = m.batch->run(dev, lens, limits, gp.forced_len > 0, gp.batch_logits != nullptr);
+            MSB_CUDA(cudaEventRecord(t1, m.stream));
+            MSB_CUDA(cudaEventSynchronize(t1));
+            float tot = 0;
+            cudaEventElapsedTime(&tot, t0, t1);
+            cudaEventDestroy(t0);
+            cudaEventDestroy(t1);
+            const int V = m.cfg.vocab;
+            for (int32_t b = 0; b < batch; ++b) {
+                const int n = r.counts[b];
+                n_out[b] = n;
+                if (n > cap) worst = MS_ERR_CAPACITY;
+                for (int i = 0; i < std::min(n, cap); ++i) ids_out[(size_t)b * cap + i] = r.ids[(size_t)b * r.t_cap + i];
+                if (gp.batch_logits)
+                    for (int st = 0; st < std::min(r.steps, cap); ++st)
+                        std::memcpy(gp.batch_logits + ((size_t)b * cap + st) * V,
+                                    r.logits.data() + ((size_t)st * batch + b) * V, (size_t)V * 4);
+                total.n_tokens += n;
+            }
+            total.n_chunks = batch;
+            total.encode_ms = r.encode_ms;
+            total.decode_ms = r.decode_ms;
+            total.total_ms = tot;
+            total.tokens_per_second = tot > 0 ? total.n_tokens / (tot / 1000.0) : 0.0;
+            if (stats) *stats = total;
+            if (worst != MS_OK) return fail(worst, "ids buffer too small");
+            return MS_OK;
+        }
         for (int32_t b = 0; b < batch; ++b) {
             ms_gen_stats st;
             ms_status s = ms_generate(model, audios[b], n_samples[b], params, ids_out + (size_t)b * cap, cap,

@@ -1,0 +1,317 @@
+// Batched greedy decode (B independent utterances in lockstep): the non-GEMM kernels of one
+// decoder step.  The projections run on the tcgen05 GEMM (gemm_tc.cu) with bf16 weights
+// and bf16 activations at the GEMM inputs; the residual stream, attention and softmax stay
+// in fp32.  Row b of every [B, ...] buffer is utterance b.
+//
+//   embed_rows          x[b] = embed[next_id[b]]
+//   ln_bf16             LayerNorm (no bias, eps 1e-5) of fp32 rows -> bf16 GEMM input
+//   self_attn_batch     one warp per (b, head): keys 0..t, cached rows below t (fp16|fp32),
+//                       this step's fp32 K/V at t (MoonshineLayers.swift:106-125)
+//   cross_attn_batch    (b, head, 32-key chunk) partials over utterance b's own frames
+//   cross_combine       merge the chunk partials -> bf16 attention rows
+//   step_finalize       per-row argmax -> ids, EOS / limit bookkeeping, next ids, t + 1
+#include "common.cuh"
+#include "kernels.h"
+
+namespace msb {
+
+namespace {
+
+constexpr int CHB = 32;
+constexpr int MAXHD_B = 64;
+
+__global__ void embed_rows_kernel(const int* __restrict__ ids, const float* __restrict__ embed, int d, int B,
+                                  int V, float* __restrict__ x, unsigned* status) {
+    const int b = blockIdx.x;
+    if (b >= B) return;
+    int id = ids[b];
+    if (id < 0 || id >= V) {
+        if (threadIdx.x == 0) atomicCAS(status, 0u, (unsigned)DEV_BAD_TOKEN);
+        id = 0;
+    }
+    const float* e = embed + (size_t)id * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) x[(size_t)b * d + i] = e[i];
+}
+
+__global__ void ln_bf16_kernel(const float* __restrict__ x, int rows, int d, const float* __restrict__ w,
+                               __nv_bfloat16* __restrict__ out) {
+    __shared__ float red[32];
+    const int r = blockIdx.x;
+    if (r >= rows) return;
+    const float* xr = x + (size_t)r * d;
+    float s = 0.f;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) s += xr[i];
+    const float mean = block_sum(s, red) / (float)d;
+    float q = 0.f;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        const float c = xr[i] - mean;
+        q += c * c;
+    }
+    const float rstd = rsqrtf(block_sum(q, red) / (float)d + 1e-5f);
+    for (int i = threadIdx.x; i < d; i += blockDim.x)
+        out[(size_t)r * d + i] = __float2bfloat16_rn((xr[i] - mean) * rstd * w[i]);
+}
+
+__device__ __forceinline__ float load_kv(const void* base, size_t idx, int f16) {
+    return f16 ? __half2float(reinterpret_cast<const __half*>(base)[idx]) : reinterpret_cast<const float*>(base)[idx];
+}
+
+// One warp per (b, h).  Lanes own keys for the scores, dims (2c, 2c+1) for the V sum.
+__global__ void self_attn_batch_kernel(const float* __restrict__ q, const float* __restrict__ kv_new,
+                                       const void* __restrict__ kc, const void* __restrict__ vc, int kv_f16,
+                                       const int* __restrict__ pos, int B, int H, int KVH, int hd, int t_cap,
+                                       float scale, __nv_bfloat16* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (item >= B * H) return;
+    const int b = item / H, h = item - b * H;
+    const int kvh = h / (H / KVH);
+    const int t = *pos;
+    const int HD = H * hd, KVD = KVH * hd;
+    const float* qr = q + (size_t)b * HD + h * hd;
+    const float* fk = kv_new + (size_t)b * 2 * KVD + kvh * hd;
+    const float* fv = fk + KVD;
+    const size_t cb = ((size_t)b * KVH + kvh) * t_cap * hd;
+    float m = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f;
+    for (int j0 = 0; j0 <= t; j0 += CHB) {
+        const int nk = min(CHB, t + 1 - j0);
+        const int j = j0 + lane;
+        float s = -INFINITY;
+        if (lane < nk) {
+            float dot = 0.f;
+            for (int c = 0; c < hd; ++c)
+                dot = fmaf(qr[c], (j == t) ? fk[c] : load_kv(kc, cb + (size_t)j * hd + c, kv_f16), dot);
+            s = dot * scale;
+        }
+        const float mc = warp_max(s);
+        const float mn = fmaxf(m, mc);
+        const float p = (lane < nk) ? expf(s - mn) : 0.f;
+        const float corr = (m == -INFINITY) ? 0.f : expf(m - mn);
+        l = l * corr + warp_sum(p);
+        a0 *= corr;
+        a1 *= corr;
+        for (int jj = 0; jj < nk; ++jj) {
+            const float pp = __shfl_sync(FULL, p, jj);
+            const int row = j0 + jj;
+            const int c = 2 * lane;
+            if (c < hd) {
+                float v0, v1;
+                if (row == t) {
+                    v0 = fv[c];
+                    v1 = fv[c + 1];
+                } else {
+                    v0 = load_kv(vc, cb + (size_t)row * hd + c, kv_f16);
+                    v1 = load_kv(vc, cb + (size_t)row * hd + c + 1, kv_f16);
+                }
+                a0 = fmaf(pp, v0, a0);
+                a1 = fmaf(pp, v1, a1);
+            }
+        }
+        m = mn;
+    }
+    const int c = 2 * lane;
+    if (c < hd) {
+        out[(size_t)b * HD + h * hd + c] = __float2bfloat16_rn(a0 / l);
+        out[(size_t)b * HD + h * hd + c + 1] = __float2bfloat16_rn(a1 / l);
+    }
+}
+
+// One warp per (b, h, chunk); partial (m, l, o[hd]) at part[((b*H + h)*max_chunks + c)].
+__global__ void cross_attn_batch_kernel(const float* __restrict__ qc, const float* __restrict__ cross32,
+                                        const void* __restrict__ cross_st, int st_f16, const int* __restrict__ pos,
+                                        const int* __restrict__ frame_off, const int* __restrict__ frames, int B,
+                                        int H, int KVH, int hd, int m_cap, int layer, int max_chunks, float scale,
+                                        float* __restrict__ part) {
+    const int lane = threadIdx.x & 31;
+    const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (item >= B * H * max_chunks) return;
+    const int c = item % max_chunks;
+    const int bh = item / max_chunks;
+    const int b = bh / H, h = bh - b * H;
+    const int kvh = h / (H / KVH);
+    const int M = frames[b];
+    float* out = part + (size_t)item * (hd + 2);
+    const int j0 = c * CHB;
+    if (j0 >= M) {
+        if (lane == 0) {
+            out[0] = -INFINITY;
+            out[1] = 0.f;
+        }
+        return;
+    }
+    const int nk = min(CHB, M - j0);
+    const bool first = (*pos == 0);
+    const int f16 = first ? 0 : st_f16;
+    const void* src = first ? (const void*)cross32 : cross_st;
+    const int HD = H * hd;
+    const float* qr = qc + (size_t)b * HD + h * hd;
+    const size_t kb = ((((size_t)layer * 2 + 0) * KVH + kvh) * m_cap + frame_off[b]) * hd;
+    const size_t vb = ((((size_t)layer * 2 + 1) * KVH + kvh) * m_cap + frame_off[b]) * hd;
+    float s = -INFINITY;
+    if (lane < nk) {
+        float dot = 0.f;
+        const size_t kr = kb + (size_t)(j0 + lane) * hd;
+        for (int e = 0; e < hd; ++e) dot = fmaf(qr[e], load_kv(src, kr + e, f16), dot);
+        s = dot * scale;
+    }
+    const float mc = warp_max(s);
+    const float p = (lane < nk) ? expf(s - mc) : 0.f;
+    const float l = warp_sum(p);
+    float a0 = 0.f, a1 = 0.f;
+    for (int jj = 0; jj < nk; ++jj) {
+        const float pp = __shfl_sync(FULL, p, jj);
+        const int e = 2 * lane;
+        if (e < hd) {
+            const size_t vr = vb + (size_t)(j0 + jj) * hd + e;
+            a0 = fmaf(pp, load_kv(src, vr, f16), a0);
+            a1 = fmaf(pp, load_kv(src, vr + 1, f16), a1);
+        }
+    }
+    if (lane == 0) {
+        out[0] = mc;
+        out[1] = l;
+    }
+    const int e = 2 * lane;
+    if (e < hd) {
+        out[2 + e] = a0;
+        out[2 + e + 1] = a1;
+    }
+}
+
+__global__ void cross_combine_kernel(const float* __restrict__ part, int B, int H, int hd, int max_chunks,
+                                     __nv_bfloat16* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (item >= B * H) return;
+    const float* base = part + (size_t)item * max_chunks * (hd + 2);
+    float M = -INFINITY;
+    for (int k = lane; k < max_chunks; k += 32) M = fmaxf(M, base[(size_t)k * (hd + 2)]);
+    M = warp_max(M);
+    float L = 0.f;
+    for (int k = lane; k < max_chunks; k += 32) {
+        const float mk = base[(size_t)k * (hd + 2)];
+        if (mk != -INFINITY) L += base[(size_t)k * (hd + 2) + 1] * expf(mk - M);
+    }
+    L = warp_sum(L);
+    const int b = item / H, h = item - b * H;
+    for (int e = lane; e < hd; e += 32) {
+        float O = 0.f;
+        for (int k = 0; k < max_chunks; ++k) {
+            const float mk = base[(size_t)k * (hd + 2)];
+            if (mk != -INFINITY) O += base[(size_t)k * (hd + 2) + 2 + e] * expf(mk - M);
+        }
+        out[(size_t)b * H * hd + h * hd + e] = __float2bfloat16_rn(O / L);
+    }
+}
+
+// One thread per row b.  Decodes the packed argmax, applies the greedy-loop rules of
+// MoonshineModel.swift:204-232 per utterance, and advances the step counter.
+__global__ void step_finalize_kernel(unsigned long long* amax, int B, int* pos, int* next_ids, int* ids_out,
+                                     int t_cap, int* counts, const int* limits, int* done, int* hit_eos, int eos,
+                                     int forced) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) {
+        const int id = (int)(0xFFFFFFFFu - (uint32_t)(amax[b] & 0xFFFFFFFFull));
+        amax[b] = 0ull;
+        next_ids[b] = id;
+        if (!done[b]) {
+            if (!forced && id == eos) {
+                done[b] = 1;
+                hit_eos[b] = 1;
+            } else {
+                ids_out[(size_t)b * t_cap + counts[b]] = id;
+                counts[b] += 1;
+                if (counts[b] >= limits[b]) done[b] = 1;
+            }
+        }
+    }
+    __syncthreads();
+    if (blockIdx.x == 0 && threadIdx.x == 0) *pos += 1;
+}
+
+}  // namespace
+
+cudaError_t launch_embed_rows(const int* ids, const float* embed, int d, int B, int V, float* x, unsigned* status,
+                              cudaStream_t s) {
+    ++launch_counter();
+    embed_rows_kernel<<<B, 128, 0, s>>>(ids, embed, d, B, V, x, status);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv_bfloat16* out, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    ++launch_counter();
+    ln_bf16_kernel<<<rows, 128, 0, s>>>(x, rows, d, w, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const void* kc, const void* vc, int kv_f16,
+                                   const int* pos, int B, int H, int KVH, int hd, int t_cap, float scale,
+                                   __nv_bfloat16* out, cudaStream_t s) {
+    if (hd > MAXHD_B || (hd & 1)) return cudaErrorInvalidValue;
+    ++launch_counter();
+    const int items = B * H;
+    self_attn_batch_kernel<<<(items + 7) / 8, 256, 0, s>>>(q, kv_new, kc, vc, kv_f16, pos, B, H, KVH, hd, t_cap,
+                                                           scale, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const void* cross_st, int st_f16,
+                                    const int* pos, const int* frame_off, const int* frames, int B, int H, int KVH,
+                                    int hd, int m_cap, int layer, int max_frames, float scale, float* part,
+                                    __nv_bfloat16* out, cudaStream_t s) {
+    if (hd > MAXHD_B || (hd & 1)) return cudaErrorInvalidValue;
+    const int max_chunks = (max_frames + CHB - 1) / CHB;
+    const int items = B * H * max_chunks;
+    launch_counter() += 2;
+    cross_attn_batch_kernel<<<(items + 7) / 8, 256, 0, s>>>(qc, cross32, cross_st, st_f16, pos, frame_off, frames, B,
+                                                            H, KVH, hd, m_cap, layer, max_chunks, scale, part);
+    cross_combine_kernel<<<(B * H + 7) / 8, 256, 0, s>>>(part, B, H, hd, max_chunks, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_step_finalize(unsigned long long* amax, int B, int* pos, int* next_ids, int* ids_out, int t_cap,
+                                 int* counts, const int* limits, int* done, int* hit_eos, int eos, int forced,
+                                 cudaStream_t s) {
+    if (B > 1024) return cudaErrorInvalidValue;
+    ++launch_counter();
+    step_finalize_kernel<<<1, ((B + 31) / 32) * 32, 0, s>>>(amax, B, pos, next_ids, ids_out, t_cap, counts, limits,
+                                                            done, hit_eos, eos, forced);
+    return cudaGetLastError();
+}
+
+namespace {
+// dst row r = src row r (interleave == 0) or, for the SwiGLU fc1, dst row 2j = src row j
+// (value) and dst row 2j+1 = src row j + interleave (gate).
+__global__ void f32_to_bf16_rows_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, int rows,
+                                        int K, int interleave) {
+    const int r = blockIdx.x;
+    if (r >= rows) return;
+    const int sr = interleave ? ((r & 1) ? interleave + (r >> 1) : (r >> 1)) : r;
+    for (int k = threadIdx.x; k < K; k += blockDim.x)
+        dst[(size_t)r * K + k] = __float2bfloat16_rn(src[(size_t)sr * K + k]);
+}
+__global__ void interleave_f32_kernel(const float* __restrict__ src, float* __restrict__ dst, int n2, int half) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r < n2) dst[r] = (r & 1) ? src[half + (r >> 1)] : src[r >> 1];
+}
+}  // namespace
+
+cudaError_t launch_f32_to_bf16_rows(const float* src, __nv_bfloat16* dst, int rows, int K, int interleave,
+                                    cudaStream_t s) {
+    ++launch_counter();
+    f32_to_bf16_rows_kernel<<<rows, 256, 0, s>>>(src, dst, rows, K, interleave);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_interleave_f32(const float* src, float* dst, int n2, int half, cudaStream_t s) {
+    ++launch_counter();
+    interleave_f32_kernel<<<(n2 + 255) / 256, 256, 0, s>>>(src, dst, n2, half);
+    return cudaGetLastError();
+}
+
+size_t cross_batch_part_floats(int B, int H, int hd, int max_frames) {
+    return (size_t)B * H * ((max_frames + CHB - 1) / CHB) * (hd + 2);
+}
+
+}  // namespace msb

@@ -150,6 +150,98 @@ __device__ __forceinline__ void store_out(const TcGemmArgs& g, int m, int n, flo
     if (g.out_bf16) g.out_bf16[(size_t)m * g.ldc_bf16 + n] = __float2bfloat16_rn(v);
 }
 
+__device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // order-preserving as unsigned
+    return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n);
+}
+
+// Epilogue of 8 consecutive accumulator columns [nb, nb+8) of row m.
+__device__ __forceinline__ void epilogue8(const TcGemmArgs& g, int m, int nb, float (&v)[8], float& best,
+                                          int& bestn) {
+    switch (g.mode) {
+        case TC_EPI_ROPE_KV: {
+            const TcRopeKv& r = g.rope;
+            const int HD = r.H * r.hd, KVD = r.KVH * r.hd;
+            const int t = *r.pos;
+#pragma unroll
+            for (int i = 0; i < 8; i += 2) {
+                const int n = nb + i;
+                if (n >= g.N) break;
+                float a0 = v[i], a1 = v[i + 1];
+                const bool isq = n < HD, isk = !isq && n < HD + KVD;
+                const int c = (isq ? n : (isk ? n - HD : n - HD - KVD)) % r.hd;
+                if ((isq || isk) && c < r.nd) {
+                    const float cs = r.cos_t[(size_t)t * (r.nd >> 1) + (c >> 1)];
+                    const float sn = r.sin_t[(size_t)t * (r.nd >> 1) + (c >> 1)];
+                    const float b0 = a0 * cs - a1 * sn, b1 = a0 * sn + a1 * cs;
+                    a0 = b0;
+                    a1 = b1;
+                }
+                if (isq) {
+                    r.q[(size_t)m * HD + n] = a0;
+                    r.q[(size_t)m * HD + n + 1] = a1;
+                } else {
+                    const int j = n - HD;
+                    r.kv_new[(size_t)m * 2 * KVD + j] = a0;
+                    r.kv_new[(size_t)m * 2 * KVD + j + 1] = a1;
+                    const int kv = j / KVD, c2 = j - kv * KVD;
+                    const int head = c2 / r.hd, dim = c2 - head * r.hd;
+                    const size_t idx = (((size_t)m * r.KVH + head) * r.t_cap + t) * r.hd + dim;
+                    void* base = kv ? r.v_cache : r.k_cache;
+                    if (r.kv_f16) {
+                        reinterpret_cast<__half*>(base)[idx] = __float2half_rn(a0);
+                        reinterpret_cast<__half*>(base)[idx + 1] = __float2half_rn(a1);
+                    } else {
+                        reinterpret_cast<float*>(base)[idx] = a0;
+                        reinterpret_cast<float*>(base)[idx + 1] = a1;
+                    }
+                }
+            }
+            break;
+        }
+        case TC_EPI_SWIGLU: {
+#pragma unroll
+            for (int i = 0; i < 8; i += 2) {
+                const int n = nb + i;
+                if (n >= g.N) break;
+                const float val = v[i] + (g.ep.bias ? g.ep.bias[n] : 0.f);
+                const float gate = v[i + 1] + (g.ep.bias ? g.ep.bias[n + 1] : 0.f);
+                g.out_bf16[(size_t)m * g.ldc_bf16 + (n >> 1)] = __float2bfloat16_rn(val * silu(gate));
+            }
+            break;
+        }
+        case TC_EPI_ARGMAX: {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int n = nb + i;
+                if (n >= g.N) break;
+                if (v[i] > best) {
+                    best = v[i];
+                    bestn = n;
+                }
+                if (g.ep.out) g.ep.out[(size_t)m * g.ep.ldc + n] = v[i];
+            }
+            break;
+        }
+        case TC_EPI_ACCUM: {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int n = nb + i;
+                if (n >= g.N) break;
+                float a = v[i];
+                if (blockIdx.z == 0 && g.ep.bias) a += g.ep.bias[n];
+                atomicAdd(g.ep.out + (size_t)m * g.ep.ldc + n, a);
+            }
+            break;
+        }
+        default:
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (nb + i < g.N) store_out(g, m, nb + i, v[i]);
+    }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -159,7 +251,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-    const int nkb = g.taps * g.kb_per_tap;
+    // this CTA's k-blocks: split blockIdx.z of g.splits
+    const int nkb_all = g.taps * g.kb_per_tap;
+    const int per_split = (nkb_all + g.splits - 1) / g.splits;
+    const int kb_lo = blockIdx.z * per_split;
+    const int nkb = max(0, min(nkb_all, kb_lo + per_split) - kb_lo);
     constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
     __shared__ int s_fail;
 
@@ -192,8 +288,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                 s_fail = 1;
                 break;
             }
-            const int tap = kb / g.kb_per_tap;
-            const int k0 = (kb - tap * g.kb_per_tap) * BK;
+            const int gkb = kb_lo + kb;
+            const int tap = gkb / g.kb_per_tap;
+            const int k0 = (gkb - tap * g.kb_per_tap) * BK;
             mbar_expect_tx(&s.full[st], A_BYTES + B_BYTES);
             tma_load_3d(s.a[st], &tmap_a, &s.full[st], k0, g.tap_y[tap], m0 + g.tap_z[tap]);
             tma_load_2d(s.b[st], &tmap_b, &s.full[st], tap * g.k_per_tap + k0, n0);
@@ -217,30 +314,28 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             }
             mma_commit(&s.empty[st]);
         }
-        mma_commit(&s.done);
+        if (nkb > 0) mma_commit(&s.done);
     }
     __syncwarp();
     __syncthreads();  // role loops finished; s_fail is final
 
     // epilogue: warp w owns accumulator lanes (rows) 32w .. 32w+31
-    bool ok = mbar_wait(&s.done, 0);
-    if (!ok) atomicCAS(g.status, 0u, 5u);
+    bool ok = nkb > 0 && mbar_wait(&s.done, 0);  // an empty k-split contributes nothing
+    if (nkb > 0 && !ok) atomicCAS(g.status, 0u, 5u);
     ok = __all_sync(FULL, ok) && !s_fail;  // tcgen05.ld below is warp-collective
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (ok) {
         const int m = m0 + warp * 32 + lane;
         const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+        float best = -INFINITY;
+        int bestn = 0;
         for (int c0 = 0; c0 < BN; c0 += 8) {
             float v[8];
             tmem_ld8(lane_addr + c0, v);
-            if (m < g.M) {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int n = n0 + c0 + i;
-                    if (n < g.N) store_out(g, m, n, v[i]);
-                }
-            }
+            if (m < g.M) epilogue8(g, m, n0 + c0, v, best, bestn);
         }
+        if (g.mode == TC_EPI_ARGMAX && m < g.M && best > -INFINITY)
+            atomicMax(g.argmax + m, argmax_key(best, bestn));
     }
     // drain copies still in flight after a failure (bounded), then free tensor memory
     if (warp == 0 && lane == 0 && s_fail) {
@@ -299,7 +394,9 @@ cudaError_t launch_gemm_tc(const CUtensorMap& map_a, const CUtensorMap& map_b, c
                            cudaStream_t stream) {
     if (g.M <= 0 || g.N <= 0) return cudaSuccess;
     if (g.taps < 1 || g.taps > 8 || g.kb_per_tap < 1 || !g.status) return cudaErrorInvalidValue;
-    const dim3 grid((g.N + bn - 1) / bn, (g.M + BM - 1) / BM);
+    if (g.splits < 1 || (g.splits > 1 && g.mode != TC_EPI_ACCUM)) return cudaErrorInvalidValue;
+    if ((g.mode == TC_EPI_ROPE_KV || g.mode == TC_EPI_SWIGLU) && (g.N & 1)) return cudaErrorInvalidValue;
+    const dim3 grid((g.N + bn - 1) / bn, (g.M + BM - 1) / BM, g.splits);
     ++launch_counter();
     if (bn == 128) {
         const size_t smem = sizeof(TcSmem<128>) + 1024;

@@ -46,14 +46,39 @@ cudaError_t launch_gemm_f32(const float* A, int lda, const float* B, int ldb, in
 // C = epi(A * B^T) with A [M, K] and B [N, K] bf16 (K-major), fp32 accumulation in TMEM.
 // A goes through a 3-D tensor map (k, y, z); k-block kb belongs to tap kb / kb_per_tap and
 // reads A at (k, tap_y[tap], m + tap_z[tap]) and B at column tap * k_per_tap + k.
+enum TcEpiMode {
+    TC_EPI_STD = 0,      // bias / activation / residual / fp32 + bf16 stores / K-V scatter
+    TC_EPI_ROPE_KV = 1,  // decoder q|k|v: partial interleaved RoPE, K/V appended to the cache
+    TC_EPI_SWIGLU = 2,   // interleaved (value, gate) columns -> bf16 value * silu(gate)
+    TC_EPI_ARGMAX = 3,   // per-row argmax (ties -> lowest column) + optional fp32 logits
+    TC_EPI_ACCUM = 4,    // out += acc (+ bias on k-split 0), fp32 atomics: split-K safe
+};
+
+// Decoder q|k|v epilogue parameters (row m = batch slot b).
+struct TcRopeKv {
+    const int* pos = nullptr;       // device: position of this step
+    const float* cos_t = nullptr;   // [pos][nd/2]
+    const float* sin_t = nullptr;
+    int nd = 0, hd = 0, H = 0, KVH = 0;
+    float* q = nullptr;             // [M, H*hd] fp32
+    float* kv_new = nullptr;        // [M, 2*KVH*hd] fp32 (k then v)
+    void* k_cache = nullptr;        // [M][KVH][t_cap][hd]
+    void* v_cache = nullptr;
+    int t_cap = 0, kv_f16 = 0;
+};
+
 struct TcGemmArgs {
     int M = 0, N = 0;
     int taps = 1, kb_per_tap = 0, k_per_tap = 0;
     int tap_y[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     int tap_z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int splits = 1;                       // k-splits over blockIdx.z (TC_EPI_ACCUM only)
+    int mode = TC_EPI_STD;
     GemmEpilogue ep;                      // fp32 outputs / scatter (as the fp32 GEMM)
     __nv_bfloat16* out_bf16 = nullptr;    // optional bf16 copy of the output [M, ldc_bf16]
     int ldc_bf16 = 0;
+    TcRopeKv rope;
+    unsigned long long* argmax = nullptr; // [M] packed (ordered value, ~column) maxima
     unsigned* status = nullptr;           // device word; 5 = a bounded wait gave up
 };
 }  // namespace msb
@@ -143,6 +168,25 @@ struct DecodeParams {
     int trace_cap;
     int region_bytes;           // per-warp prefetch region (set by the launcher)
 };
+
+// ---------------------------------------------------------------- batched decode step
+cudaError_t launch_embed_rows(const int* ids, const float* embed, int d, int B, int V, float* x, unsigned* status,
+                              cudaStream_t s);
+cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv_bfloat16* out, cudaStream_t s);
+cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const void* kc, const void* vc, int kv_f16,
+                                   const int* pos, int B, int H, int KVH, int hd, int t_cap, float scale,
+                                   __nv_bfloat16* out, cudaStream_t s);
+cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const void* cross_st, int st_f16,
+                                    const int* pos, const int* frame_off, const int* frames, int B, int H, int KVH,
+                                    int hd, int m_cap, int layer, int max_frames, float scale, float* part,
+                                    __nv_bfloat16* out, cudaStream_t s);
+cudaError_t launch_step_finalize(unsigned long long* amax, int B, int* pos, int* next_ids, int* ids_out, int t_cap,
+                                 int* counts, const int* limits, int* done, int* hit_eos, int eos, int forced,
+                                 cudaStream_t s);
+cudaError_t launch_f32_to_bf16_rows(const float* src, __nv_bfloat16* dst, int rows, int K, int interleave,
+                                    cudaStream_t s);
+cudaError_t launch_interleave_f32(const float* src, float* dst, int n2, int half, cudaStream_t s);
+size_t cross_batch_part_floats(int B, int H, int hd, int max_frames);
 
 // Persistent cooperative decode kernel: runs up to n_steps greedy decoder calls.
 cudaError_t launch_decode_b1(const DecodeParams& p, int grid, cudaStream_t stream);

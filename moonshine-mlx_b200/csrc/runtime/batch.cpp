@@ -1,0 +1,347 @@
+// Batched greedy decode: B utterances step in lockstep; every projection is one tcgen05 GEMM
+// over all B rows (bf16 weights and GEMM inputs, fp32 accumulation and residual stream).
+// Step 0 runs eagerly, the remaining steps replay one captured CUDA graph of the step.
+#include "batch.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+namespace msb {
+
+namespace {
+constexpr int kBnNarrow = 64;   // q|k|v and cross-q projections (more CTAs for small N)
+constexpr int kBnWide = 128;
+
+void make_b_map(CUtensorMap* map, const __nv_bfloat16* w, int N, int K, int bn) {
+    if (!tc_make_map_2d(map, w, (uint64_t)K, (uint64_t)N, (uint64_t)K * 2, (uint32_t)bn))
+        throw MsError(MS_ERR_CUDA, "cuTensorMapEncodeTiled failed for a weight matrix");
+}
+
+void make_a_map(CUtensorMap* map, const __nv_bfloat16* a, int rows, int K) {
+    if (!tc_make_map_3d(map, a, (uint64_t)K, 1, (uint64_t)rows, (uint64_t)K * 2, (uint64_t)K * 2, 128))
+        throw MsError(MS_ERR_CUDA, "cuTensorMapEncodeTiled failed for an activation matrix");
+}
+}  // namespace
+
+BatchEngine::~BatchEngine() {
+    for (auto* b : own) delete b;
+}
+
+template <class T>
+T* BatchEngine::alloc(size_t n) {
+    DevBuf* b = new DevBuf();
+    own.push_back(b);
+    b->ensure(std::max<size_t>(n * sizeof(T), 256));
+    return b->as<T>();
+}
+
+void BatchEngine::ensure_weights() {
+    if (weights_ready) return;
+    const Config& c = m.cfg;
+    const int d = c.hidden, HD = c.heads * c.head_dim, KVD = c.kv_heads * c.head_dim, I = c.inter;
+    cudaStream_t s = m.stream;
+    layers.resize(c.layers);
+    for (int l = 0; l < c.layers; ++l) {
+        const DecodeLayerW& W = m.dec[l];
+        LayerB& B = layers[l];
+        B.wqkv = alloc<__nv_bfloat16>((size_t)(HD + 2 * KVD) * d);
+        B.wo = alloc<__nv_bfloat16>((size_t)d * HD);
+        B.wcq = alloc<__nv_bfloat16>((size_t)HD * d);
+        B.wco = alloc<__nv_bfloat16>((size_t)d * HD);
+        B.w1i = alloc<__nv_bfloat16>((size_t)2 * I * d);
+        B.w2 = alloc<__nv_bfloat16>((size_t)d * I);
+        B.b1i = alloc<float>((size_t)2 * I);
+        MSB_CUDA(launch_f32_to_bf16_rows(W.wqkv, B.wqkv, HD + 2 * KVD, d, 0, s));
+        MSB_CUDA(launch_f32_to_bf16_rows(W.wo, B.wo, d, HD, 0, s));
+        MSB_CUDA(launch_f32_to_bf16_rows(W.wcq, B.wcq, HD, d, 0, s));
+        MSB_CUDA(launch_f32_to_bf16_rows(W.wco, B.wco, d, HD, 0, s));
+        MSB_CUDA(launch_f32_to_bf16_rows(W.w1, B.w1i, 2 * I, d, I, s));
+        MSB_CUDA(launch_f32_to_bf16_rows(W.w2, B.w2, d, I, 0, s));
+        MSB_CUDA(launch_interleave_f32(W.b1, B.b1i, 2 * I, I, s));
+        make_b_map(&B.m_qkv, B.wqkv, HD + 2 * KVD, d, kBnNarrow);
+        make_b_map(&B.m_o, B.wo, d, HD, kBnWide);
+        make_b_map(&B.m_cq, B.wcq, HD, d, kBnNarrow);
+        make_b_map(&B.m_co, B.wco, d, HD, kBnWide);
+        make_b_map(&B.m_w1, B.w1i, 2 * I, d, kBnWide);
+        make_b_map(&B.m_w2, B.w2, d, I, kBnWide);
+    }
+    lm = alloc<__nv_bfloat16>((size_t)c.vocab * d);
+    MSB_CUDA(launch_f32_to_bf16_rows(m.lm_head, lm, c.vocab, d, 0, s));
+    make_b_map(&m_lm, lm, c.vocab, d, kBnWide);
+    MSB_CUDA(cudaStreamSynchronize(s));
+    weights_ready = true;
+}
+
+void BatchEngine::ensure_ws(int B, int T, int Mtot, int maxM) {
+    const Config& c = m.cfg;
+    const int d = c.hidden, HD = c.heads * c.head_dim, KVD = c.kv_heads * c.head_dim, I = c.inter;
+    const size_t kvsz = m.kv_f16 ? 2 : 4;
+    bool remap = false;
+    if (B > Bc) {
+        Bc = B;
+        remap = true;
+        x.ensure((size_t)Bc * d * 4);
+        hb.ensure((size_t)Bc * d * 2);
+        attn.ensure((size_t)Bc * HD * 2);
+        g.ensure((size_t)Bc * I * 2);
+        q.ensure((size_t)Bc * HD * 4);
+        qc.ensure((size_t)Bc * HD * 4);
+        kvnew.ensure((size_t)Bc * 2 * KVD * 4);
+        amax.ensure((size_t)Bc * 8);
+        next_ids.ensure((size_t)Bc * 4);
+        counts.ensure((size_t)Bc * 4);
+        limits_d.ensure((size_t)Bc * 4);
+        done.ensure((size_t)Bc * 4);
+        hit.ensure((size_t)Bc * 4);
+        frame_off.ensure((size_t)Bc * 4);
+        frames.ensure((size_t)Bc * 4);
+    }
+    if (T > Tc || remap) {
+        Tc = std::max(Tc, T);
+        kcache.ensure((size_t)c.layers * Bc * KVD * Tc * 4);  // fp32-sized: the KV dtype may change
+        vcache.ensure((size_t)c.layers * Bc * KVD * Tc * 4);
+        ids.ensure((size_t)Bc * Tc * 4);
+    }
+    (void)kvsz;
+    if (Mtot > Mc) {
+        Mc = Mtot;
+        const size_t n = (size_t)c.layers * 2 * KVD * Mc;
+        cross32.ensure(n * 4);
+        cross16.ensure(n * 2);
+        memory.ensure((size_t)Mc * d * 4);
+    }
+    if (maxM > Fc || remap) {
+        Fc = std::max(Fc, maxM);
+        part.ensure(cross_batch_part_floats(Bc, c.heads, c.head_dim, Fc) * 4);
+    }
+    status.ensure(16);
+    pos.ensure(16);
+    if (remap) {
+        make_a_map(&a_hb, hb.as<__nv_bfloat16>(), Bc, d);
+        make_a_map(&a_attn, attn.as<__nv_bfloat16>(), Bc, HD);
+        make_a_map(&a_g, g.as<__nv_bfloat16>(), Bc, I);
+    }
+}
+
+void BatchEngine::gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& ga, int K, int bn) {
+    ga.taps = 1;
+    ga.kb_per_tap = (K + 63) / 64;
+    ga.k_per_tap = K;
+    ga.status = status.as<unsigned>();
+    if (ga.mode == TC_EPI_ACCUM) {
+        const int tiles = ((ga.N + bn - 1) / bn) * ((ga.M + 127) / 128);
+        ga.splits = std::max(1, std::min(ga.kb_per_tap, m.num_sms / std::max(tiles, 1)));
+    }
+    MSB_CUDA(launch_gemm_tc(a, b, ga, bn, m.stream));
+}
+
+void BatchEngine::enqueue_step(int B, int max_frames, bool forced, float* logits) {
+    const Config& c = m.cfg;
+    const int d = c.hidden, H = c.heads, KVH = c.kv_heads, hd = c.head_dim, I = c.inter;
+    const int HD = H * hd, KVD = KVH * hd;
+    const float scale = std::pow((float)hd, -0.5f);
+    const size_t kvsz = m.kv_f16 ? 2 : 4;
+    cudaStream_t s = m.stream;
+    const int* posp = pos.as<int>();
+    float* X = x.as<float>();
+    MSB_CUDA(launch_embed_rows(next_ids.as<int>(), m.embed, d, B, c.vocab, X, status.as<unsigned>(), s));
+    for (int l = 0; l < c.layers; ++l) {
+        const DecodeLayerW& W = m.dec[l];
+        LayerB& L = layers[l];
+        char* kc = kcache.as<char>() + (size_t)l * Bc * KVD * Tc * kvsz;
+        char* vc = vcache.as<char>() + (size_t)l * Bc * KVD * Tc * kvsz;
+        // self-attention block
+        MSB_CUDA(launch_ln_bf16(X, B, d, W.ln1, hb.as<__nv_bfloat16>(), s));
+        {
+            TcGemmArgs ga;
+            ga.M = B;
+            ga.N = HD + 2 * KVD;
+            ga.mode = TC_EPI_ROPE_KV;
+            ga.rope.pos = posp;
+            ga.rope.cos_t = m.rope_cos.as<float>();
+            ga.rope.sin_t = m.rope_sin.as<float>();
+            ga.rope.nd = c.rotary_ndims();
+            ga.rope.hd = hd;
+            ga.rope.H = H;
+            ga.rope.KVH = KVH;
+            ga.rope.q = q.as<float>();
+            ga.rope.kv_new = kvnew.as<float>();
+            ga.rope.k_cache = kc;
+            ga.rope.v_cache = vc;
+            ga.rope.t_cap = Tc;
+            ga.rope.kv_f16 = m.kv_f16 ? 1 : 0;
+            gemm(a_hb, L.m_qkv, ga, d, kBnNarrow);
+        }
+        MSB_CUDA(launch_self_attn_batch(q.as<float>(), kvnew.as<float>(), kc, vc, m.kv_f16 ? 1 : 0, posp, B, H, KVH,
+                                        hd, Tc, scale, attn.as<__nv_bfloat16>(), s));
+        {
+            TcGemmArgs ga;
+            ga.M = B;
+            ga.N = d;
+            ga.mode = TC_EPI_ACCUM;
+            ga.ep.out = X;
+            ga.ep.ldc = d;
+            gemm(a_attn, L.m_o, ga, HD, kBnWide);
+        }
+        // cross-attention block
+        MSB_CUDA(launch_ln_bf16(X, B, d, W.ln2, hb.as<__nv_bfloat16>(), s));
+        {
+            TcGemmArgs ga;
+            ga.M = B;
+            ga.N = HD;
+            ga.ep.out = qc.as<float>();
+            ga.ep.ldc = HD;
+            gemm(a_hb, L.m_cq, ga, d, kBnNarrow);
+        }
+        MSB_CUDA(launch_cross_attn_batch(qc.as<float>(), cross32.as<float>(), m.kv_f16 ? cross16.p : cross32.p,
+                                         m.kv_f16 ? 1 : 0, posp, frame_off.as<int>(), frames.as<int>(), B, H, KVH,
+                                         hd, Mc, l, max_frames, scale, part.as<float>(), attn.as<__nv_bfloat16>(),
+                                         s));
+        {
+            TcGemmArgs ga;
+            ga.M = B;
+            ga.N = d;
+            ga.mode = TC_EPI_ACCUM;
+            ga.ep.out = X;
+            ga.ep.ldc = d;
+            gemm(a_attn, L.m_co, ga, HD, kBnWide);
+        }
+        // SwiGLU MLP
+        MSB_CUDA(launch_ln_bf16(X, B, d, W.ln3, hb.as<__nv_bfloat16>(), s));
+        {
+            TcGemmArgs ga;
+            ga.M = B;
+            ga.N = 2 * I;
+            ga.mode = TC_EPI_SWIGLU;
+            ga.ep.bias = L.b1i;
+            ga.out_bf16 = g.as<__nv_bfloat16>();
+            ga.ldc_bf16 = I;
+            gemm(a_hb, L.m_w1, ga, d, kBnWide);
+        }
+        {
+            TcGemmArgs ga;
+            ga.M = B;
+            ga.N = d;
+            ga.mode = TC_EPI_ACCUM;
+            ga.ep.out = X;
+            ga.ep.ldc = d;
+            ga.ep.bias = W.b2;
+            gemm(a_g, L.m_w2, ga, I, kBnWide);
+        }
+    }
+    MSB_CUDA(launch_ln_bf16(X, B, d, m.dec_norm, hb.as<__nv_bfloat16>(), s));
+    {
+        TcGemmArgs ga;
+        ga.M = B;
+        ga.N = c.vocab;
+        ga.mode = TC_EPI_ARGMAX;
+        ga.argmax = amax.as<unsigned long long>();
+        ga.ep.out = logits;
+        ga.ep.ldc = c.vocab;
+        gemm(a_hb, m_lm, ga, d, kBnWide);
+    }
+    MSB_CUDA(launch_step_finalize(amax.as<unsigned long long>(), B, pos.as<int>(), next_ids.as<int>(), ids.as<int>(),
+                                  Tc, counts.as<int>(), limits_d.as<int>(), done.as<int>(), hit.as<int>(), c.eos,
+                                  forced ? 1 : 0, s));
+}
+
+BatchEngine::Result BatchEngine::run(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
+                                     const std::vector<int>& limits, bool forced, bool want_logits) {
+    const Config& c = m.cfg;
+    const int B = (int)audio_dev.size();
+    cudaStream_t s = m.stream;
+    Result res;
+    ensure_weights();
+    MSB_CUDA(cudaEventRecord(m.ev[0], s));
+    // encode every utterance, gather the memory rows [Mtot, d]
+    std::vector<int> off(B), fr(B);
+    std::vector<float*> staged;
+    int Mtot = 0, maxM = 0;
+    // first pass: frame counts
+    for (int b = 0; b < B; ++b) {
+        const int fl = c.frame_len();
+        const int T1 = (int)(n_samples[b] / fl);
+        const int T2 = T1 > 0 ? (T1 - 1) / 2 + 1 : 0;
+        fr[b] = T2 > 0 ? (T2 - 1) / 2 + 1 : 0;
+        if (fr[b] <= 0) throw MsError(MS_ERR_INVALID_ARG, "an utterance has fewer samples than one frame");
+        off[b] = Mtot;
+        Mtot += fr[b];
+        maxM = std::max(maxM, fr[b]);
+    }
+    const int T = *std::max_element(limits.begin(), limits.end());
+    ensure_ws(B, T, Mtot, maxM);
+    for (int b = 0; b < B; ++b) {
+        const int M = m.encode_device(audio_dev[b], n_samples[b], 0);
+        if (M != fr[b]) throw MsError(MS_ERR_CUDA, "frame count mismatch");
+        MSB_CUDA(cudaMemcpyAsync(memory.as<float>() + (size_t)off[b] * c.hidden, m.memory_ptr(),
+                                 (size_t)M * c.hidden * 4, cudaMemcpyDeviceToDevice, s));
+    }
+    m.cross_kv_into(memory.as<float>(), Mtot, 0, cross32.as<float>(), m.kv_f16 ? cross16.p : nullptr, Mc);
+    MSB_CUDA(cudaEventRecord(m.ev[1], s));
+    // step state
+    std::vector<int> bos(B, c.dec_start);
+    MSB_CUDA(cudaMemcpyAsync(next_ids.p, bos.data(), (size_t)B * 4, cudaMemcpyHostToDevice, s));
+    MSB_CUDA(cudaMemcpyAsync(limits_d.p, limits.data(), (size_t)B * 4, cudaMemcpyHostToDevice, s));
+    MSB_CUDA(cudaMemcpyAsync(frame_off.p, off.data(), (size_t)B * 4, cudaMemcpyHostToDevice, s));
+    MSB_CUDA(cudaMemcpyAsync(frames.p, fr.data(), (size_t)B * 4, cudaMemcpyHostToDevice, s));
+    MSB_CUDA(cudaMemsetAsync(counts.p, 0, (size_t)B * 4, s));
+    MSB_CUDA(cudaMemsetAsync(done.p, 0, (size_t)B * 4, s));
+    MSB_CUDA(cudaMemsetAsync(hit.p, 0, (size_t)B * 4, s));
+    MSB_CUDA(cudaMemsetAsync(amax.p, 0, (size_t)B * 8, s));
+    MSB_CUDA(cudaMemsetAsync(pos.p, 0, 16, s));
+    MSB_CUDA(cudaMemsetAsync(status.p, 0, 16, s));
+    DevBuf logit_buf;
+    if (want_logits) logit_buf.ensure((size_t)T * B * c.vocab * 4);
+    auto logits_at = [&](int step) -> float* {
+        return want_logits ? logit_buf.as<float>() + (size_t)step * B * c.vocab : nullptr;
+    };
+    enqueue_step(B, maxM, forced, logits_at(0));
+    if (want_logits) {
+        for (int st = 1; st < T; ++st) enqueue_step(B, maxM, forced, logits_at(st));
+    } else if (T > 1) {
+        cudaGraph_t graph = nullptr;
+        cudaGraphExec_t exec = nullptr;
+        MSB_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        try {
+            enqueue_step(B, maxM, forced, nullptr);
+        } catch (...) {
+            cudaStreamEndCapture(s, &graph);
+            if (graph) cudaGraphDestroy(graph);
+            throw;
+        }
+        MSB_CUDA(cudaStreamEndCapture(s, &graph));
+        MSB_CUDA(cudaGraphInstantiate(&exec, graph, 0));
+        for (int st = 1; st < T; ++st) MSB_CUDA(cudaGraphLaunch(exec, s));
+        MSB_CUDA(cudaStreamSynchronize(s));
+        cudaGraphExecDestroy(exec);
+        cudaGraphDestroy(graph);
+    }
+    MSB_CUDA(cudaEventRecord(m.ev[2], s));
+    res.t_cap = Tc;
+    res.steps = T;
+    res.ids.resize((size_t)B * Tc);
+    res.counts.resize(B);
+    res.hit_eos.resize(B);
+    unsigned st_word = 0;
+    MSB_CUDA(cudaMemcpyAsync(res.ids.data(), ids.p, (size_t)B * Tc * 4, cudaMemcpyDeviceToHost, s));
+    MSB_CUDA(cudaMemcpyAsync(res.counts.data(), counts.p, (size_t)B * 4, cudaMemcpyDeviceToHost, s));
+    MSB_CUDA(cudaMemcpyAsync(res.hit_eos.data(), hit.p, (size_t)B * 4, cudaMemcpyDeviceToHost, s));
+    MSB_CUDA(cudaMemcpyAsync(&st_word, status.p, 4, cudaMemcpyDeviceToHost, s));
+    if (want_logits) {
+        res.logits.resize((size_t)T * B * c.vocab);
+        MSB_CUDA(cudaMemcpyAsync(res.logits.data(), logit_buf.p, res.logits.size() * 4, cudaMemcpyDeviceToHost, s));
+    }
+    MSB_CUDA(cudaStreamSynchronize(s));
+    if (st_word == 5) throw MsError(MS_ERR_TIMEOUT, "batched decode: a GEMM pipeline wait timed out");
+    if (st_word == DEV_BAD_TOKEN) throw MsError(MS_ERR_INVALID_ARG, "batched decode: token id out of range");
+    if (st_word != 0) throw MsError(MS_ERR_CUDA, "batched decode: device status " + std::to_string(st_word));
+    float te = 0, td = 0;
+    cudaEventElapsedTime(&te, m.ev[0], m.ev[1]);
+    cudaEventElapsedTime(&td, m.ev[1], m.ev[2]);
+    res.encode_ms = te;
+    res.decode_ms = td;
+    return res;
+}
+
+}  // namespace msb

@@ -13,6 +13,7 @@
 #include <map>
 #include <sstream>
 
+#include "batch.hpp"
 #include "json.hpp"
 
 namespace msb {

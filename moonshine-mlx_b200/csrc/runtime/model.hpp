@@ -77,6 +77,7 @@ struct Workspace {
 };
 
 struct StreamState;
+struct BatchEngine;
 
 struct Model {
     Config cfg;
@@ -100,6 +101,7 @@ struct Model {
     int rope_cap = 0;
 
     Workspace ws;
+    std::unique_ptr<BatchEngine> batch;  // batched bf16 tensor-core decode, built on first use
     bool trace_enabled = false;
     DevBuf trace_buf;
     std::vector<unsigned long long> last_trace;

@@ -52,7 +52,8 @@ class _GenParams(C.Structure):
     _fields_ = [("max_tokens", C.c_int32), ("forced_len", C.c_int32),
                 ("temperature", C.c_float), ("reserved_f", C.c_float),
                 ("chunk_duration", C.c_double), ("teacher_ids", C.POINTER(C.c_int32)),
-                ("n_teacher", C.c_int32), ("reserved", C.c_int32 * 7)]
+                ("n_teacher", C.c_int32), ("reserved_i", C.c_int32),
+                ("batch_logits", C.POINTER(C.c_float)), ("reserved", C.c_int32 * 4)]
 
 
 class _GenStats(C.Structure):
@@ -333,8 +334,10 @@ class MoonshineModel:
         return int(_L().ms_model_stream(self._h) or 0)
 
     def generate_batch(self, audios: Sequence[np.ndarray], max_tokens: Optional[int] = None,
-                       forced_len: Optional[int] = None, chunk_duration: float = 30.0):
-        """Batched offline generation (one id list per utterance)."""
+                       forced_len: Optional[int] = None, chunk_duration: float = 30.0,
+                       return_logits: bool = False):
+        """Batched offline generation.  Returns (ids per utterance, stats[, logits
+        [B, cap, vocab] of every decoder call])."""
         arrs = [_f32(a) for a in audios]
         B = len(arrs)
         sr = self.sample_rate
@@ -347,10 +350,15 @@ class MoonshineModel:
         ids = np.zeros((B, cap), dtype=np.int32)
         n = np.zeros(B, dtype=np.int32)
         p = self._params(max_tokens, 0.0, chunk_duration, forced_len, None)
+        logits = None
+        if return_logits:
+            logits = np.zeros((B, cap, self.config.vocab_size), dtype=np.float32)
+            p.batch_logits = _fptr(logits)
         st = _GenStats()
         _check(_L().ms_generate_batch(self._h, ptrs, lens, B, C.byref(p), _iptr(ids), cap,
                                      _iptr(n), C.byref(st)))
-        return [ids[b, : n[b]].tolist() for b in range(B)], st
+        out = [ids[b, : n[b]].tolist() for b in range(B)]
+        return (out, st, logits) if return_logits else (out, st)
 
     def encode(self, audio) -> np.ndarray:
         """Memory = prepareMemory(encoder(embedder(audio))) for one chunk, [frames, hidden]."""

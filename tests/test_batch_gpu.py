@@ -1,0 +1,70 @@
+"""Batched lockstep decode (bf16 tcgen05 GEMMs) vs the CPU oracle, per utterance.
+
+GEMM inputs are bf16, so logits are compared with the bf16 tolerance (2e-2, max-abs
+relative per decoder call); token ids must match the oracle's greedy ids."""
+import numpy as np
+import pytest
+
+from moonshine_b200 import synth
+from util import BF16_LOGIT_TOL, assert_logits_close, model_dir, oracle_for, with_config
+
+pytestmark = pytest.mark.gpu
+
+
+def _check_batch(path, audios, forced, kv_fp16=True, max_tokens=None):
+    import moonshine_b200 as mb
+    m = mb.MoonshineModel.load(path, kv_fp16=kv_fp16)
+    ids, st, logits = m.generate_batch(audios, forced_len=forced, max_tokens=max_tokens, return_logits=True)
+    o = oracle_for(path)
+    for b, a in enumerate(audios):
+        mem = o.memory_for(a)
+        if forced:
+            ref, _, ref_logits, margins = o.greedy(mem, forced, kv_fp16, forced_len=forced, keep_logits=True)
+        else:
+            limit = o.token_limit(len(a), max_tokens)
+            ref, _, ref_logits, margins = o.greedy(mem, limit, kv_fp16, keep_logits=True)
+        # Greedy ids may only part at a near-tie: a step whose top-2 logit margin is within
+        # the bf16 tolerance.  Logits are compared up to and including that step (its
+        # inputs are still identical on both sides).
+        k = next((i for i, (x, y) in enumerate(zip(ids[b], ref)) if x != y), None)
+        if k is None:
+            assert len(ids[b]) == len(ref), f"utterance {b}"
+            k = len(ref_logits) - 1
+        else:
+            scale = float(np.max(np.abs(ref_logits[k])))
+            assert margins[k] <= BF16_LOGIT_TOL * scale, (
+                f"utterance {b}: ids part at step {k} with margin {margins[k]:.4f} (scale {scale:.3f})")
+        assert_logits_close(logits[b, : k + 1], ref_logits[: k + 1], BF16_LOGIT_TOL)
+    return st
+
+
+@pytest.mark.parametrize("kv_fp16", [True, False])
+def test_batch_tiny_forced(model_root, kv_fp16):
+    d = model_dir(model_root, "tiny")
+    audios = [synth.synth_audio(n, 60 + i) for i, n in enumerate([16000, 40000, 23456, 32000])]
+    _check_batch(d, audios, 12, kv_fp16=kv_fp16)
+
+
+def test_batch_small_bf16_checkpoint(model_root):
+    d = model_dir(model_root, "small", dtype="bfloat16", vocab_size=2048, max_position_embeddings=512)
+    audios = [synth.synth_audio(n, 70 + i) for i, n in enumerate([24000, 17777, 32000])]
+    _check_batch(d, audios, 8)
+
+
+def test_batch_limits_and_eos(model_root, tmp_path):
+    base = model_dir(model_root, "tiny")
+    o = oracle_for(base)
+    audios = [synth.synth_audio(n, 80 + i) for i, n in enumerate([8000, 12000, 20000])]
+    first = o.greedy(o.memory_for(audios[1]), 3, True, forced_len=3)[0]
+    eos_dir = with_config(base, str(tmp_path / "eos"), eos_token_id=int(first[1]))
+    _check_batch(eos_dir, audios, None)            # per-utterance limits, EOS stops
+    _check_batch(base, audios, None, max_tokens=4)
+
+
+def test_batch_of_one_equals_generate(model_root):
+    import moonshine_b200 as mb
+    d = model_dir(model_root, "tiny")
+    m = mb.MoonshineModel.load(d)
+    a = synth.synth_audio(48000, 90)
+    ids, _ = m.generate_batch([a], forced_len=20)
+    assert ids[0] == m.generate(a, forced_len=20).tokens
