@@ -204,6 +204,124 @@ __global__ void cross_combine_kernel(const float* __restrict__ part, int B, int 
     }
 }
 
+// Cross attention of one (utterance b, head h) per CTA: warp w takes the 32-key chunks
+// w, w+8, ... of utterance b's frames with an online softmax (lane = key for the scores,
+// lane c = dims 2c, 2c+1 for the weighted V sum, 128-bit K row loads, coalesced V rows),
+// then the eight warp states are merged in shared memory and written as bf16.
+template <int HDT, bool F16>
+__global__ void __launch_bounds__(256) cross_attn_cta_kernel(const float* __restrict__ qc, const void* __restrict__ src,
+                                                           const int* __restrict__ frame_off,
+                                                           const int* __restrict__ frames, int H, int KVH, int m_cap,
+                                                           int layer, float scale, __nv_bfloat16* __restrict__ out) {
+    __shared__ __align__(16) float qs[HDT];
+    __shared__ float wm[8], wl[8];
+    __shared__ float wacc[8][HDT];
+    __shared__ float pw[8][CHB];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int b = blockIdx.x / H, h = blockIdx.x - (blockIdx.x / H) * H;
+    const int kvh = h / (H / KVH);
+    const int M = frames[b];
+    const int HD = H * HDT;
+    for (int i = threadIdx.x; i < HDT; i += blockDim.x) qs[i] = qc[(size_t)b * HD + h * HDT + i];
+    __syncthreads();
+    const size_t kb = ((((size_t)layer * 2 + 0) * KVH + kvh) * m_cap + frame_off[b]) * HDT;
+    const size_t vb = ((((size_t)layer * 2 + 1) * KVH + kvh) * m_cap + frame_off[b]) * HDT;
+    float m = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f;
+    for (int j0 = wid * CHB; j0 < M; j0 += 8 * CHB) {
+        const int nk = min(CHB, M - j0);
+        float s = -INFINITY;
+        if (lane < nk) {
+            float dot = 0.f;
+            if (F16) {
+                const uint4* kr = reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(src) + kb +
+                                                                 (size_t)(j0 + lane) * HDT);
+                uint4 u[HDT / 8];
+#pragma unroll
+                for (int e = 0; e < HDT / 8; ++e) u[e] = __ldg(kr + e);
+#pragma unroll
+                for (int e = 0; e < HDT / 8; ++e) {
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&u[e]);
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        const float2 kf = __half22float2(h2[t]);
+                        dot = fmaf(qs[8 * e + 2 * t], kf.x, fmaf(qs[8 * e + 2 * t + 1], kf.y, dot));
+                    }
+                }
+            } else {
+                const float4* kr = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + kb +
+                                                                   (size_t)(j0 + lane) * HDT);
+                float4 u[HDT / 4];
+#pragma unroll
+                for (int e = 0; e < HDT / 4; ++e) u[e] = __ldg(kr + e);
+#pragma unroll
+                for (int e = 0; e < HDT / 4; ++e)
+                    dot = fmaf(qs[4 * e], u[e].x,
+                               fmaf(qs[4 * e + 1], u[e].y, fmaf(qs[4 * e + 2], u[e].z, fmaf(qs[4 * e + 3], u[e].w, dot))));
+            }
+            s = dot * scale;
+        }
+        const float mc = warp_max(s);
+        const float mn = fmaxf(m, mc);
+        const float p = (lane < nk) ? expf(s - mn) : 0.f;
+        const float corr = (m == -INFINITY) ? 0.f : expf(m - mn);
+        l = l * corr + warp_sum(p);
+        a0 *= corr;
+        a1 *= corr;
+        pw[wid][lane] = p;
+        __syncwarp();
+        if (2 * lane < HDT) {
+            float v0[CHB], v1[CHB];
+#pragma unroll
+            for (int jj = 0; jj < CHB; ++jj) {
+                if (jj < nk) {
+                    const size_t vr = vb + (size_t)(j0 + jj) * HDT + 2 * lane;
+                    if (F16) {
+                        const float2 vf = __half22float2(__ldg(reinterpret_cast<const __half2*>(
+                            reinterpret_cast<const __half*>(src) + vr)));
+                        v0[jj] = vf.x;
+                        v1[jj] = vf.y;
+                    } else {
+                        const float2 vf = __ldg(reinterpret_cast<const float2*>(reinterpret_cast<const float*>(src) + vr));
+                        v0[jj] = vf.x;
+                        v1[jj] = vf.y;
+                    }
+                }
+            }
+#pragma unroll
+            for (int jj = 0; jj < CHB; ++jj) {
+                if (jj < nk) {
+                    const float pp = pw[wid][jj];
+                    a0 = fmaf(pp, v0[jj], a0);
+                    a1 = fmaf(pp, v1[jj], a1);
+                }
+            }
+        }
+        __syncwarp();
+        m = mn;
+    }
+    if (lane == 0) {
+        wm[wid] = m;
+        wl[wid] = l;
+    }
+    if (2 * lane < HDT) {
+        wacc[wid][2 * lane] = a0;
+        wacc[wid][2 * lane + 1] = a1;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < HDT; e += blockDim.x) {
+        float Mx = -INFINITY;
+        for (int w = 0; w < 8; ++w) Mx = fmaxf(Mx, wm[w]);
+        float L = 0.f, O = 0.f;
+        for (int w = 0; w < 8; ++w) {
+            if (wm[w] == -INFINITY) continue;
+            const float f = expf(wm[w] - Mx);
+            L = fmaf(wl[w], f, L);
+            O = fmaf(wacc[w][e], f, O);
+        }
+        out[(size_t)b * HD + h * HDT + e] = __float2bfloat16_rn(O / L);
+    }
+}
+
 // One thread per row b.  Decodes the packed argmax, applies the greedy-loop rules of
 // MoonshineModel.swift:204-232 per utterance, and advances the step counter.
 __global__ void step_finalize_kernel(unsigned long long* amax, int B, int* pos, int* next_ids, int* ids_out,
@@ -259,8 +377,28 @@ cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const vo
 cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const void* cross_st, int st_f16,
                                     const int* pos, const int* frame_off, const int* frames, int B, int H, int KVH,
                                     int hd, int m_cap, int layer, int max_frames, float scale, float* part,
-                                    __nv_bfloat16* out, cudaStream_t s) {
+                                    __nv_bfloat16* out, int first_step, cudaStream_t s) {
     if (hd > MAXHD_B || (hd & 1)) return cudaErrorInvalidValue;
+    if (first_step >= 0) {
+        // one CTA per (utterance, head); the first decoder call reads the fp32 copy
+        const void* src = first_step ? (const void*)cross32 : cross_st;
+        const bool f16 = !first_step && st_f16;
+        ++launch_counter();
+#define MSB_CROSS(HDV)                                                                                          \
+    if (hd == HDV) {                                                                                            \
+        if (f16) cross_attn_cta_kernel<HDV, true><<<B * H, 256, 0, s>>>(qc, src, frame_off, frames, H, KVH, m_cap, \
+                                                                        layer, scale, out);                      \
+        else cross_attn_cta_kernel<HDV, false><<<B * H, 256, 0, s>>>(qc, src, frame_off, frames, H, KVH, m_cap,   \
+                                                                     layer, scale, out);                         \
+        return cudaGetLastError();                                                                              \
+    }
+        MSB_CROSS(32)
+        MSB_CROSS(40)
+        MSB_CROSS(48)
+        MSB_CROSS(64)
+#undef MSB_CROSS
+    }
+    // generic head_dim: chunk partials + combine, fp32/stored copy chosen on the device
     const int max_chunks = (max_frames + CHB - 1) / CHB;
     const int items = B * H * max_chunks;
     launch_counter() += 2;

@@ -7,8 +7,10 @@
 //   warp 1 (one lane)  MMA issuer: 4 x tcgen05.mma (K = 16 each) per 64-wide k-block into a
 //                      128 x BN fp32 accumulator in tensor memory; tcgen05.commit frees the
 //                      stage and, after the last k-block, signals the epilogue
-//   all four warps     epilogue: tcgen05.ld of their 32 accumulator lanes (= rows), then
-//                      bias / activation / residual / bf16 or fp32 store / K-V scatter
+//   all four warps     epilogue: tcgen05.ld of their 32 accumulator lanes (= rows) into the
+//                      idle stage buffers, then row by row (lanes along columns, so global
+//                      accesses coalesce) bias / activation / residual / bf16 or fp32 store /
+//                      K-V scatter / RoPE / SwiGLU / argmax / split-K atomics
 //
 // A is addressed through a 3-D tensor map (k, y, z) so a causal stride-2 convolution runs as
 // `taps` accumulated GEMMs: tap t reads A at (k, y_t, m + z_t) and B at column t*K_tap + k.
@@ -156,89 +158,76 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
     return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n);
 }
 
-// Epilogue of 8 consecutive accumulator columns [nb, nb+8) of row m.
-__device__ __forceinline__ void epilogue8(const TcGemmArgs& g, int m, int nb, float (&v)[8], float& best,
-                                          int& bestn) {
+// Epilogue of the accumulator column pair (n, n+1) of row m; n is even and has1 says
+// whether column n+1 exists.  ROPE_KV and SWIGLU need even N, so their pairs are whole.
+__device__ __forceinline__ void epilogue2(const TcGemmArgs& g, int m, int n, float a0, float a1, bool has1,
+                                          float& best, int& bestn) {
     switch (g.mode) {
         case TC_EPI_ROPE_KV: {
             const TcRopeKv& r = g.rope;
             const int HD = r.H * r.hd, KVD = r.KVH * r.hd;
             const int t = *r.pos;
-#pragma unroll
-            for (int i = 0; i < 8; i += 2) {
-                const int n = nb + i;
-                if (n >= g.N) break;
-                float a0 = v[i], a1 = v[i + 1];
-                const bool isq = n < HD, isk = !isq && n < HD + KVD;
-                const int c = (isq ? n : (isk ? n - HD : n - HD - KVD)) % r.hd;
-                if ((isq || isk) && c < r.nd) {
-                    const float cs = r.cos_t[(size_t)t * (r.nd >> 1) + (c >> 1)];
-                    const float sn = r.sin_t[(size_t)t * (r.nd >> 1) + (c >> 1)];
-                    const float b0 = a0 * cs - a1 * sn, b1 = a0 * sn + a1 * cs;
-                    a0 = b0;
-                    a1 = b1;
-                }
-                if (isq) {
-                    r.q[(size_t)m * HD + n] = a0;
-                    r.q[(size_t)m * HD + n + 1] = a1;
+            const bool isq = n < HD, isk = !isq && n < HD + KVD;
+            const int c = (isq ? n : (isk ? n - HD : n - HD - KVD)) % r.hd;
+            if ((isq || isk) && c < r.nd) {
+                const float cs = r.cos_t[(size_t)t * (r.nd >> 1) + (c >> 1)];
+                const float sn = r.sin_t[(size_t)t * (r.nd >> 1) + (c >> 1)];
+                const float b0 = a0 * cs - a1 * sn, b1 = a0 * sn + a1 * cs;
+                a0 = b0;
+                a1 = b1;
+            }
+            if (isq) {
+                r.q[(size_t)m * HD + n] = a0;
+                r.q[(size_t)m * HD + n + 1] = a1;
+            } else {
+                const int j = n - HD;
+                r.kv_new[(size_t)m * 2 * KVD + j] = a0;
+                r.kv_new[(size_t)m * 2 * KVD + j + 1] = a1;
+                const int kv = j / KVD, c2 = j - kv * KVD;
+                const int head = c2 / r.hd, dim = c2 - head * r.hd;
+                const size_t idx = (((size_t)m * r.KVH + head) * r.t_cap + t) * r.hd + dim;
+                void* base = kv ? r.v_cache : r.k_cache;
+                if (r.kv_f16) {
+                    reinterpret_cast<__half*>(base)[idx] = __float2half_rn(a0);
+                    reinterpret_cast<__half*>(base)[idx + 1] = __float2half_rn(a1);
                 } else {
-                    const int j = n - HD;
-                    r.kv_new[(size_t)m * 2 * KVD + j] = a0;
-                    r.kv_new[(size_t)m * 2 * KVD + j + 1] = a1;
-                    const int kv = j / KVD, c2 = j - kv * KVD;
-                    const int head = c2 / r.hd, dim = c2 - head * r.hd;
-                    const size_t idx = (((size_t)m * r.KVH + head) * r.t_cap + t) * r.hd + dim;
-                    void* base = kv ? r.v_cache : r.k_cache;
-                    if (r.kv_f16) {
-                        reinterpret_cast<__half*>(base)[idx] = __float2half_rn(a0);
-                        reinterpret_cast<__half*>(base)[idx + 1] = __float2half_rn(a1);
-                    } else {
-                        reinterpret_cast<float*>(base)[idx] = a0;
-                        reinterpret_cast<float*>(base)[idx + 1] = a1;
-                    }
+                    reinterpret_cast<float*>(base)[idx] = a0;
+                    reinterpret_cast<float*>(base)[idx + 1] = a1;
                 }
             }
             break;
         }
         case TC_EPI_SWIGLU: {
-#pragma unroll
-            for (int i = 0; i < 8; i += 2) {
-                const int n = nb + i;
-                if (n >= g.N) break;
-                const float val = v[i] + (g.ep.bias ? g.ep.bias[n] : 0.f);
-                const float gate = v[i + 1] + (g.ep.bias ? g.ep.bias[n + 1] : 0.f);
-                g.out_bf16[(size_t)m * g.ldc_bf16 + (n >> 1)] = __float2bfloat16_rn(val * silu(gate));
-            }
+            const float val = a0 + (g.ep.bias ? g.ep.bias[n] : 0.f);
+            const float gate = a1 + (g.ep.bias ? g.ep.bias[n + 1] : 0.f);
+            g.out_bf16[(size_t)m * g.ldc_bf16 + (n >> 1)] = __float2bfloat16_rn(val * silu(gate));
             break;
         }
         case TC_EPI_ARGMAX: {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int n = nb + i;
-                if (n >= g.N) break;
-                if (v[i] > best) {
-                    best = v[i];
-                    bestn = n;
-                }
-                if (g.ep.out) g.ep.out[(size_t)m * g.ep.ldc + n] = v[i];
+            if (a0 > best) {  // columns arrive in increasing order per lane: strict > keeps the lowest
+                best = a0;
+                bestn = n;
+            }
+            if (has1 && a1 > best) {
+                best = a1;
+                bestn = n + 1;
+            }
+            if (g.ep.out) {
+                g.ep.out[(size_t)m * g.ep.ldc + n] = a0;
+                if (has1) g.ep.out[(size_t)m * g.ep.ldc + n + 1] = a1;
             }
             break;
         }
         case TC_EPI_ACCUM: {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int n = nb + i;
-                if (n >= g.N) break;
-                float a = v[i];
-                if (blockIdx.z == 0 && g.ep.bias) a += g.ep.bias[n];
-                atomicAdd(g.ep.out + (size_t)m * g.ep.ldc + n, a);
-            }
+            const bool add_bias = blockIdx.z == 0 && g.ep.bias;
+            float* o = g.ep.out + (size_t)m * g.ep.ldc + n;
+            atomicAdd(o, a0 + (add_bias ? g.ep.bias[n] : 0.f));
+            if (has1) atomicAdd(o + 1, a1 + (add_bias ? g.ep.bias[n + 1] : 0.f));
             break;
         }
         default:
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                if (nb + i < g.N) store_out(g, m, nb + i, v[i]);
+            store_out(g, m, n, a0);
+            if (has1) store_out(g, m, n + 1, a1);
     }
 }
 
@@ -324,18 +313,48 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     if (nkb > 0 && !ok) atomicCAS(g.status, 0u, 5u);
     ok = __all_sync(FULL, ok) && !s_fail;  // tcgen05.ld below is warp-collective
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    // The accumulator tile goes through shared memory (the idle stage buffers) so that the
+    // epilogue walks rows with lanes along columns: every global store / atomic of a warp
+    // then touches one contiguous row segment instead of 32 rows.
+    constexpr int LDS = BN + 1;  // +1: rows written by the 32 lanes of a warp hit distinct banks
+    float* tile = reinterpret_cast<float*>(&s.a[0][0]);
+    static_assert(sizeof(float) * BM * LDS <= sizeof(s.a) + sizeof(s.b), "epilogue tile must fit the stages");
     if (ok) {
-        const int m = m0 + warp * 32 + lane;
         const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-        float best = -INFINITY;
-        int bestn = 0;
+        float* my = tile + (size_t)(warp * 32 + lane) * LDS;
         for (int c0 = 0; c0 < BN; c0 += 8) {
             float v[8];
             tmem_ld8(lane_addr + c0, v);
-            if (m < g.M) epilogue8(g, m, n0 + c0, v, best, bestn);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) my[c0 + i] = v[i];
         }
-        if (g.mode == TC_EPI_ARGMAX && m < g.M && best > -INFINITY)
-            atomicMax(g.argmax + m, argmax_key(best, bestn));
+    }
+    __syncthreads();
+    if (ok) {
+        const int rows = min(BM, g.M - m0);
+        for (int r = warp; r < rows; r += TC_THREADS / 32) {
+            const int m = m0 + r;
+            const float* row = tile + (size_t)r * LDS;
+            float best = -INFINITY;
+            int bestn = 0x7fffffff;
+            for (int c = 2 * lane; c < BN; c += 64) {
+                const int n = n0 + c;
+                if (n >= g.N) break;
+                epilogue2(g, m, n, row[c], row[c + 1], n + 1 < g.N, best, bestn);
+            }
+            if (g.mode == TC_EPI_ARGMAX) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float bo = __shfl_xor_sync(FULL, best, o);
+                    const int no = __shfl_xor_sync(FULL, bestn, o);
+                    if (bo > best || (bo == best && no < bestn)) {
+                        best = bo;
+                        bestn = no;
+                    }
+                }
+                if (lane == 0 && best > -INFINITY) atomicMax(g.argmax + m, argmax_key(best, bestn));
+            }
+        }
     }
     // drain copies still in flight after a failure (bounded), then free tensor memory
     if (warp == 0 && lane == 0 && s_fail) {

@@ -136,7 +136,7 @@ void BatchEngine::gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& g
     MSB_CUDA(launch_gemm_tc(a, b, ga, bn, m.stream));
 }
 
-void BatchEngine::enqueue_step(int B, int max_frames, bool forced, float* logits) {
+void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, float* logits) {
     const Config& c = m.cfg;
     const int d = c.hidden, H = c.heads, KVH = c.kv_heads, hd = c.head_dim, I = c.inter;
     const int HD = H * hd, KVD = KVH * hd;
@@ -197,7 +197,7 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, float* logits
         MSB_CUDA(launch_cross_attn_batch(qc.as<float>(), cross32.as<float>(), m.kv_f16 ? cross16.p : cross32.p,
                                          m.kv_f16 ? 1 : 0, posp, frame_off.as<int>(), frames.as<int>(), B, H, KVH,
                                          hd, Mc, l, max_frames, scale, part.as<float>(), attn.as<__nv_bfloat16>(),
-                                         s));
+                                         first ? 1 : 0, s));
         {
             TcGemmArgs ga;
             ga.M = B;
@@ -296,15 +296,15 @@ BatchEngine::Result BatchEngine::run(const std::vector<const float*>& audio_dev,
     auto logits_at = [&](int step) -> float* {
         return want_logits ? logit_buf.as<float>() + (size_t)step * B * c.vocab : nullptr;
     };
-    enqueue_step(B, maxM, forced, logits_at(0));
+    enqueue_step(B, maxM, forced, true, logits_at(0));
     if (want_logits) {
-        for (int st = 1; st < T; ++st) enqueue_step(B, maxM, forced, logits_at(st));
+        for (int st = 1; st < T; ++st) enqueue_step(B, maxM, forced, false, logits_at(st));
     } else if (T > 1) {
         cudaGraph_t graph = nullptr;
         cudaGraphExec_t exec = nullptr;
         MSB_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
         try {
-            enqueue_step(B, maxM, forced, nullptr);
+            enqueue_step(B, maxM, forced, false, nullptr);
         } catch (...) {
             cudaStreamEndCapture(s, &graph);
             if (graph) cudaGraphDestroy(graph);

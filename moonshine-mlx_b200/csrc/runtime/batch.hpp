@@ -46,7 +46,7 @@ struct BatchEngine {
     template <class T> T* alloc(size_t n);
     void ensure_weights();
     void ensure_ws(int B, int T, int Mtot, int maxM);
-    void enqueue_step(int B, int max_frames, bool forced, float* logits);
+    void enqueue_step(int B, int max_frames, bool forced, bool first, float* logits);
     void gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& g, int K, int bn);
 };
 
