@@ -7,9 +7,13 @@
 //   ln_bf16             LayerNorm (no bias, eps 1e-5) of fp32 rows -> bf16 GEMM input
 //   self_attn_batch     one warp per (b, head): keys 0..t, cached rows below t (fp16|fp32),
 //                       this step's fp32 K/V at t (MoonshineLayers.swift:106-125)
-//   cross_attn_batch    (b, head, 32-key chunk) partials over utterance b's own frames
+//   cross_attn_stream   one CTA per (b, head): bulk-copy ring of K/V chunks of utterance b's
+//                       own frames through shared memory, online softmax -> bf16 rows
+//   cross_attn_batch    generic head_dim: (b, head, 32-key chunk) partials over b's frames
 //   cross_combine       merge the chunk partials -> bf16 attention rows
 //   step_finalize       per-row argmax -> ids, EOS / limit bookkeeping, next ids, t + 1
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -204,104 +208,153 @@ __global__ void cross_combine_kernel(const float* __restrict__ part, int B, int 
     }
 }
 
-// Cross attention of one (utterance b, head h) per CTA: warp w takes the 32-key chunks
-// w, w+8, ... of utterance b's frames with an online softmax (lane = key for the scores,
-// lane c = dims 2c, 2c+1 for the weighted V sum, 128-bit K row loads, coalesced V rows),
-// then the eight warp states are merged in shared memory and written as bf16.
+// Cross attention of one (utterance b, head h) per CTA, streamed through shared memory.
+// K rows and V rows of one head are contiguous over frames, so thread 0 keeps a ring of
+// XS_STAGES chunks of CH keys in flight as two bulk copies per chunk completing on one
+// mbarrier.  Warp w scores keys [w*KW, (w+1)*KW) of each chunk with G lanes per key (16
+// bytes of the row per lane, the matching q slice in registers, shuffle sum inside the
+// group), keeps an online softmax, and accumulates V with lane c owning dims 2c, 2c+1.  The
+// four warp states are merged in shared memory and written as bf16.  Semantics as the
+// cross branch of MoonshineLayers.swift:150-160 (scale hd^-1/2, no mask over the frames).
 template <int HDT, bool F16>
-__global__ void __launch_bounds__(256) cross_attn_cta_kernel(const float* __restrict__ qc, const void* __restrict__ src,
-                                                           const int* __restrict__ frame_off,
-                                                           const int* __restrict__ frames, int H, int KVH, int m_cap,
-                                                           int layer, float scale, __nv_bfloat16* __restrict__ out) {
-    __shared__ __align__(16) float qs[HDT];
-    __shared__ float wm[8], wl[8];
-    __shared__ float wacc[8][HDT];
-    __shared__ float pw[8][CHB];
+struct XsShape {
+    static constexpr int ESZ = F16 ? 2 : 4;
+    static constexpr int ROWB = HDT * ESZ;                        // bytes of one key row
+    static constexpr int NE = ROWB / 16;                          // 16-byte pieces per row
+    static constexpr int EP = 16 / ESZ;                           // elements per piece
+    static constexpr int G = NE <= 4 ? 4 : (NE <= 8 ? 8 : 16);    // lanes per key
+    static constexpr int KPP = 32 / G;                            // keys per warp pass
+    static constexpr int CH = F16 ? 64 : 32;                      // keys per stage
+    static constexpr int KW = CH / 4;                             // keys per warp per stage
+    static constexpr int STAGE_ELEMS = CH * HDT;                  // per tensor
+    static_assert(NE * 16 == ROWB && NE <= 16, "key rows must be whole 16-byte pieces");
+    static_assert(KW % KPP == 0 && KW <= 32, "warp slice must be whole passes");
+};
+constexpr int XS_STAGES = 3;
+constexpr int XS_THREADS = 128;
+
+template <int HDT, bool F16>
+constexpr size_t xs_smem_bytes() {
+    return 2 * (size_t)XS_STAGES * XsShape<HDT, F16>::STAGE_ELEMS * XsShape<HDT, F16>::ESZ;
+}
+
+template <int HDT, bool F16>
+__global__ void __launch_bounds__(XS_THREADS) cross_attn_stream_kernel(
+    const float* __restrict__ qc, const void* __restrict__ src, const int* __restrict__ frame_off,
+    const int* __restrict__ frames, int H, int KVH, int m_cap, int layer, float scale,
+    __nv_bfloat16* __restrict__ out, unsigned* status) {
+    using S = XsShape<HDT, F16>;
+    using E = typename std::conditional<F16, __half, float>::type;
+    extern __shared__ __align__(128) unsigned char xs_raw[];
+    E* ks = reinterpret_cast<E*>(xs_raw);
+    E* vs = ks + XS_STAGES * S::STAGE_ELEMS;
+    __shared__ __align__(8) uint64_t full[XS_STAGES];
+    __shared__ float sc[4][S::KW];  // scores, then probabilities, of each warp's slice
+    __shared__ float wm[4], wl[4];
+    __shared__ float wacc[4][HDT];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int b = blockIdx.x / H, h = blockIdx.x - (blockIdx.x / H) * H;
     const int kvh = h / (H / KVH);
     const int M = frames[b];
-    const int HD = H * HDT;
-    for (int i = threadIdx.x; i < HDT; i += blockDim.x) qs[i] = qc[(size_t)b * HD + h * HDT + i];
-    __syncthreads();
-    const size_t kb = ((((size_t)layer * 2 + 0) * KVH + kvh) * m_cap + frame_off[b]) * HDT;
-    const size_t vb = ((((size_t)layer * 2 + 1) * KVH + kvh) * m_cap + frame_off[b]) * HDT;
-    float m = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f;
-    for (int j0 = wid * CHB; j0 < M; j0 += 8 * CHB) {
-        const int nk = min(CHB, M - j0);
-        float s = -INFINITY;
-        if (lane < nk) {
+    const int nchunks = (M + S::CH - 1) / S::CH;
+    const E* kg = reinterpret_cast<const E*>(src) +
+                  ((((size_t)layer * 2 + 0) * KVH + kvh) * m_cap + frame_off[b]) * HDT;
+    const E* vg = reinterpret_cast<const E*>(src) +
+                  ((((size_t)layer * 2 + 1) * KVH + kvh) * m_cap + frame_off[b]) * HDT;
+    auto issue = [&](int c) {
+        const int st = c % XS_STAGES;
+        const uint32_t bytes = (uint32_t)min(S::CH, M - c * S::CH) * S::ROWB;
+        mbar_expect_tx(&full[st], 2 * bytes);
+        bulk_load(ks + (size_t)st * S::STAGE_ELEMS, kg + (size_t)c * S::STAGE_ELEMS, bytes, &full[st]);
+        bulk_load(vs + (size_t)st * S::STAGE_ELEMS, vg + (size_t)c * S::STAGE_ELEMS, bytes, &full[st]);
+    };
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < XS_STAGES; ++i) mbar_init(&full[i], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int c = 0; c < min(nchunks, XS_STAGES); ++c) issue(c);
+    }
+    __syncthreads();  // the barriers are initialised before any thread waits on them
+    // q slice of this lane's piece (lanes with sub >= NE only pad their group)
+    const int g = lane / S::G, sub = lane - (lane / S::G) * S::G;
+    float qr[S::EP];
+    const float* qrow = qc + (size_t)b * H * HDT + h * HDT;
+#pragma unroll
+    for (int e = 0; e < S::EP; ++e) qr[e] = (sub < S::NE) ? qrow[sub * S::EP + e] : 0.f;
+
+    float m_run = -INFINITY, l_run = 0.f, a0 = 0.f, a1 = 0.f;
+    int failed_at = -1;
+    for (int c = 0; c < nchunks; ++c) {
+        const int st = c % XS_STAGES;
+        const bool ok = mbar_wait(&full[st], (c / XS_STAGES) & 1);
+        // every warp is past chunk c-1 here, so its stage can be refilled
+        if (!__syncthreads_and(ok)) {
+            failed_at = c;
+            break;
+        }
+        if (threadIdx.x == 0 && c >= 1 && c - 1 + XS_STAGES < nchunks) issue(c - 1 + XS_STAGES);
+        const int nk = min(S::CH, M - c * S::CH);
+        const int k0 = wid * S::KW;
+        const int kw = max(0, min(S::KW, nk - k0));
+        const E* kst = ks + (size_t)st * S::STAGE_ELEMS + (size_t)k0 * HDT;
+        const E* vst = vs + (size_t)st * S::STAGE_ELEMS + (size_t)k0 * HDT;
+#pragma unroll
+        for (int p = 0; p < S::KW / S::KPP; ++p) {
+            const int j = p * S::KPP + g;
             float dot = 0.f;
-            if (F16) {
-                const uint4* kr = reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(src) + kb +
-                                                                 (size_t)(j0 + lane) * HDT);
-                uint4 u[HDT / 8];
-#pragma unroll
-                for (int e = 0; e < HDT / 8; ++e) u[e] = __ldg(kr + e);
-#pragma unroll
-                for (int e = 0; e < HDT / 8; ++e) {
-                    const __half2* h2 = reinterpret_cast<const __half2*>(&u[e]);
+            if (j < kw && sub < S::NE) {
+                const uint4 u = *reinterpret_cast<const uint4*>(kst + (size_t)j * HDT + sub * S::EP);
+                if constexpr (F16) {
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
                     for (int t = 0; t < 4; ++t) {
-                        const float2 kf = __half22float2(h2[t]);
-                        dot = fmaf(qs[8 * e + 2 * t], kf.x, fmaf(qs[8 * e + 2 * t + 1], kf.y, dot));
+                        const float2 f = __half22float2(h2[t]);
+                        dot = fmaf(qr[2 * t], f.x, fmaf(qr[2 * t + 1], f.y, dot));
                     }
+                } else {
+                    const float* f = reinterpret_cast<const float*>(&u);
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) dot = fmaf(qr[t], f[t], dot);
                 }
-            } else {
-                const float4* kr = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + kb +
-                                                                   (size_t)(j0 + lane) * HDT);
-                float4 u[HDT / 4];
-#pragma unroll
-                for (int e = 0; e < HDT / 4; ++e) u[e] = __ldg(kr + e);
-#pragma unroll
-                for (int e = 0; e < HDT / 4; ++e)
-                    dot = fmaf(qs[4 * e], u[e].x,
-                               fmaf(qs[4 * e + 1], u[e].y, fmaf(qs[4 * e + 2], u[e].z, fmaf(qs[4 * e + 3], u[e].w, dot))));
             }
-            s = dot * scale;
+#pragma unroll
+            for (int o = S::G / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(FULL, dot, o);
+            if (sub == 0) sc[wid][j] = (j < kw) ? dot * scale : -INFINITY;
         }
-        const float mc = warp_max(s);
-        const float mn = fmaxf(m, mc);
-        const float p = (lane < nk) ? expf(s - mn) : 0.f;
-        const float corr = (m == -INFINITY) ? 0.f : expf(m - mn);
-        l = l * corr + warp_sum(p);
+        __syncwarp();
+        const float sv = lane < S::KW ? sc[wid][lane] : -INFINITY;
+        const float mn = fmaxf(m_run, warp_max(sv));
+        const float pv = (sv == -INFINITY) ? 0.f : expf(sv - mn);
+        const float corr = (m_run == -INFINITY) ? 0.f : expf(m_run - mn);
+        l_run = l_run * corr + warp_sum(pv);
         a0 *= corr;
         a1 *= corr;
-        pw[wid][lane] = p;
+        __syncwarp();
+        if (lane < S::KW) sc[wid][lane] = pv;
         __syncwarp();
         if (2 * lane < HDT) {
-            float v0[CHB], v1[CHB];
-#pragma unroll
-            for (int jj = 0; jj < CHB; ++jj) {
-                if (jj < nk) {
-                    const size_t vr = vb + (size_t)(j0 + jj) * HDT + 2 * lane;
-                    if (F16) {
-                        const float2 vf = __half22float2(__ldg(reinterpret_cast<const __half2*>(
-                            reinterpret_cast<const __half*>(src) + vr)));
-                        v0[jj] = vf.x;
-                        v1[jj] = vf.y;
-                    } else {
-                        const float2 vf = __ldg(reinterpret_cast<const float2*>(reinterpret_cast<const float*>(src) + vr));
-                        v0[jj] = vf.x;
-                        v1[jj] = vf.y;
-                    }
-                }
-            }
-#pragma unroll
-            for (int jj = 0; jj < CHB; ++jj) {
-                if (jj < nk) {
-                    const float pp = pw[wid][jj];
-                    a0 = fmaf(pp, v0[jj], a0);
-                    a1 = fmaf(pp, v1[jj], a1);
-                }
+#pragma unroll 4
+            for (int j = 0; j < kw; ++j) {
+                const float pj = sc[wid][j];
+                float2 v;
+                if constexpr (F16) v = __half22float2(*reinterpret_cast<const __half2*>(vst + (size_t)j * HDT + 2 * lane));
+                else v = *reinterpret_cast<const float2*>(vst + (size_t)j * HDT + 2 * lane);
+                a0 = fmaf(pj, v.x, a0);
+                a1 = fmaf(pj, v.y, a1);
             }
         }
-        __syncwarp();
-        m = mn;
+        m_run = mn;
+    }
+    if (failed_at >= 0) {  // uniform across the CTA (decided by __syncthreads_and)
+        if (threadIdx.x == 0) {
+            atomicCAS(status, 0u, (unsigned)DEV_WAIT_TIMEOUT);
+            const int issued = min(nchunks, failed_at == 0 ? XS_STAGES : failed_at - 1 + XS_STAGES);
+            for (int c = failed_at; c < issued; ++c) mbar_wait(&full[c % XS_STAGES], (c / XS_STAGES) & 1);
+        }
+        return;
     }
     if (lane == 0) {
-        wm[wid] = m;
-        wl[wid] = l;
+        wm[wid] = m_run;
+        wl[wid] = l_run;
     }
     if (2 * lane < HDT) {
         wacc[wid][2 * lane] = a0;
@@ -310,16 +363,42 @@ __global__ void __launch_bounds__(256) cross_attn_cta_kernel(const float* __rest
     __syncthreads();
     for (int e = threadIdx.x; e < HDT; e += blockDim.x) {
         float Mx = -INFINITY;
-        for (int w = 0; w < 8; ++w) Mx = fmaxf(Mx, wm[w]);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) Mx = fmaxf(Mx, wm[w]);
         float L = 0.f, O = 0.f;
-        for (int w = 0; w < 8; ++w) {
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
             if (wm[w] == -INFINITY) continue;
             const float f = expf(wm[w] - Mx);
             L = fmaf(wl[w], f, L);
             O = fmaf(wacc[w][e], f, O);
         }
-        out[(size_t)b * HD + h * HDT + e] = __float2bfloat16_rn(O / L);
+        out[(size_t)b * H * HDT + h * HDT + e] = __float2bfloat16_rn(O / L);
     }
+}
+
+template <int HDT>
+cudaError_t launch_cross_stream(bool f16, const float* qc, const void* src, const int* frame_off, const int* frames,
+                                int B, int H, int KVH, int m_cap, int layer, float scale, __nv_bfloat16* out,
+                                unsigned* status, cudaStream_t s) {
+    static bool attr_set = false;
+    if (!attr_set) {  // both variants at once: the fp16 one is first launched inside a graph capture
+        cudaError_t e = cudaFuncSetAttribute(cross_attn_stream_kernel<HDT, true>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)xs_smem_bytes<HDT, true>());
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(cross_attn_stream_kernel<HDT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)xs_smem_bytes<HDT, false>());
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    if (f16)
+        cross_attn_stream_kernel<HDT, true><<<B * H, XS_THREADS, xs_smem_bytes<HDT, true>(), s>>>(
+            qc, src, frame_off, frames, H, KVH, m_cap, layer, scale, out, status);
+    else
+        cross_attn_stream_kernel<HDT, false><<<B * H, XS_THREADS, xs_smem_bytes<HDT, false>(), s>>>(
+            qc, src, frame_off, frames, H, KVH, m_cap, layer, scale, out, status);
+    return cudaGetLastError();
 }
 
 // One thread per row b.  Decodes the packed argmax, applies the greedy-loop rules of
@@ -377,26 +456,20 @@ cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const vo
 cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const void* cross_st, int st_f16,
                                     const int* pos, const int* frame_off, const int* frames, int B, int H, int KVH,
                                     int hd, int m_cap, int layer, int max_frames, float scale, float* part,
-                                    __nv_bfloat16* out, int first_step, cudaStream_t s) {
+                                    __nv_bfloat16* out, int first_step, unsigned* status, cudaStream_t s) {
     if (hd > MAXHD_B || (hd & 1)) return cudaErrorInvalidValue;
-    if (first_step >= 0) {
+    if (first_step >= 0 && (hd == 32 || hd == 40 || hd == 48 || hd == 64)) {
         // one CTA per (utterance, head); the first decoder call reads the fp32 copy
         const void* src = first_step ? (const void*)cross32 : cross_st;
         const bool f16 = !first_step && st_f16;
+        if ((reinterpret_cast<uintptr_t>(src) & 15) != 0 || !status) return cudaErrorInvalidValue;
         ++launch_counter();
-#define MSB_CROSS(HDV)                                                                                          \
-    if (hd == HDV) {                                                                                            \
-        if (f16) cross_attn_cta_kernel<HDV, true><<<B * H, 256, 0, s>>>(qc, src, frame_off, frames, H, KVH, m_cap, \
-                                                                        layer, scale, out);                      \
-        else cross_attn_cta_kernel<HDV, false><<<B * H, 256, 0, s>>>(qc, src, frame_off, frames, H, KVH, m_cap,   \
-                                                                     layer, scale, out);                         \
-        return cudaGetLastError();                                                                              \
-    }
-        MSB_CROSS(32)
-        MSB_CROSS(40)
-        MSB_CROSS(48)
-        MSB_CROSS(64)
-#undef MSB_CROSS
+        switch (hd) {
+            case 32: return launch_cross_stream<32>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s);
+            case 40: return launch_cross_stream<40>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s);
+            case 48: return launch_cross_stream<48>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s);
+            default: return launch_cross_stream<64>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s);
+        }
     }
     // generic head_dim: chunk partials + combine, fp32/stored copy chosen on the device
     const int max_chunks = (max_frames + CHB - 1) / CHB;

@@ -32,37 +32,6 @@ constexpr int BM = 128;
 constexpr int BK = 64;         // bf16: 128 bytes = one 128B-swizzle row
 constexpr int STAGES = 4;
 constexpr int TC_THREADS = 128;
-constexpr uint32_t WAIT_LIMIT = 1u << 22;   // polls of a bounded mbarrier wait
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-
-// Bounded parity wait; returns false after WAIT_LIMIT polls.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    const uint32_t a = smem_u32(bar);
-    for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(a), "r"(parity)
-            : "memory");
-        if (ok) return true;
-    }
-    return false;
-}
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2) {
@@ -108,14 +77,15 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
-    uint32_t r[8];
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+// 32 consecutive accumulator columns of this thread's lane, one wait.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
                  : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 template <int BN>
@@ -128,110 +98,177 @@ struct alignas(1024) TcSmem {
     uint32_t tmem_base;
 };
 
-__device__ __forceinline__ void store_out(const TcGemmArgs& g, int m, int n, float v) {
-    const GemmEpilogue& ep = g.ep;
-    if (ep.bias) v += ep.bias[n];
-    if (ep.act == ACT_SILU) v = silu(v);
-    else if (ep.act == ACT_GELU) v = gelu_erf(v);
-    if (ep.residual) v += ep.residual[(size_t)m * ep.ldr + n];
-    if (ep.kv_scatter) {
-        const int kvdim = ep.kv_heads * ep.head_dim;
-        const int layer = n / (2 * kvdim);
-        const int rem = n - layer * 2 * kvdim;
-        const int kv = rem / kvdim;
-        const int c = rem - kv * kvdim;
-        const int head = c / ep.head_dim;
-        const int dim = c - head * ep.head_dim;
-        const size_t idx = ((((size_t)layer * 2 + kv) * ep.kv_heads + head) * ep.frame_cap +
-                            (size_t)(m + ep.frame_offset)) * ep.head_dim + dim;
-        if (ep.kv_out32) ep.kv_out32[idx] = v;
-        if (ep.kv_out16) reinterpret_cast<__half*>(ep.kv_out16)[idx] = __float2half_rn(v);
-        return;
-    }
-    if (ep.out) ep.out[(size_t)m * ep.ldc + n] = v;
-    if (g.out_bf16) g.out_bf16[(size_t)m * g.ldc_bf16 + n] = __float2bfloat16_rn(v);
-}
-
 __device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
     uint32_t u = __float_as_uint(v);
     u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // order-preserving as unsigned
     return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n);
 }
 
-// Epilogue of the accumulator column pair (n, n+1) of row m; n is even and has1 says
-// whether column n+1 exists.  ROPE_KV and SWIGLU need even N, so their pairs are whole.
-__device__ __forceinline__ void epilogue2(const TcGemmArgs& g, int m, int n, float a0, float a1, bool has1,
-                                          float& best, int& bestn) {
-    switch (g.mode) {
-        case TC_EPI_ROPE_KV: {
-            const TcRopeKv& r = g.rope;
-            const int HD = r.H * r.hd, KVD = r.KVH * r.hd;
-            const int t = *r.pos;
-            const bool isq = n < HD, isk = !isq && n < HD + KVD;
-            const int c = (isq ? n : (isk ? n - HD : n - HD - KVD)) % r.hd;
-            if ((isq || isk) && c < r.nd) {
-                const float cs = r.cos_t[(size_t)t * (r.nd >> 1) + (c >> 1)];
-                const float sn = r.sin_t[(size_t)t * (r.nd >> 1) + (c >> 1)];
-                const float b0 = a0 * cs - a1 * sn, b1 = a0 * sn + a1 * cs;
-                a0 = b0;
-                a1 = b1;
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+    return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+
+__device__ __forceinline__ void st_bf16x4(__nv_bfloat16* p, float4 v) {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&lo);
+    u.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(p) = u;
+}
+
+__device__ __forceinline__ void st_f16x4(__half* p, float4 v) {
+    __half2 lo = __floats2half2_rn(v.x, v.y), hi = __floats2half2_rn(v.z, v.w);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&lo);
+    u.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(p) = u;
+}
+
+// Row stride (floats) of the accumulator tile staged in shared memory: a multiple of 4 for
+// 128-bit accesses, and 4 mod 32 so the 8 lanes of one 128-bit store phase hit distinct banks.
+template <int BN>
+__host__ __device__ constexpr int tile_ld() { return BN + 4; }
+
+// Epilogue of a staged 128 x BN accumulator tile.  Thread t owns the four columns
+// n = n0 + 4 (t mod BN/4) .. n + 3 for every row it visits, so column-only terms (bias,
+// RoPE angles, K/V scatter base) are loaded once, and the BN/4 threads of a row write one
+// contiguous row segment with 128-bit accesses.  N is a multiple of 4 (checked at launch).
+template <int BN, int MODE>
+__device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* tile, int m0, int n0) {
+    constexpr int TPR = BN / 4;            // threads per row
+    constexpr int RPP = TC_THREADS / TPR;  // rows per pass
+    constexpr int LDS = tile_ld<BN>();
+    const int t = threadIdx.x;
+    const int c = (t % TPR) * 4;
+    const int n = n0 + c;
+    const bool col_ok = n < g.N;
+    const int r0 = t / TPR;
+    const int rows = min(BM, g.M - m0);
+    const int passes = (rows + RPP - 1) / RPP;
+    const GemmEpilogue& ep = g.ep;
+
+    float4 bias = make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (MODE == TC_EPI_STD || MODE == TC_EPI_SWIGLU || MODE == TC_EPI_ACCUM) {
+        const bool use = ep.bias && col_ok && (MODE != TC_EPI_ACCUM || blockIdx.z == 0);
+        if (use) bias = *reinterpret_cast<const float4*>(ep.bias + n);
+    }
+    // K/V scatter: column part of the cache index (the four columns share one head)
+    size_t kv_col = 0;
+    if constexpr (MODE == TC_EPI_STD) {
+        if (ep.kv_scatter && col_ok) {
+            const int kvdim = ep.kv_heads * ep.head_dim;
+            const int layer = n / (2 * kvdim);
+            const int rem = n - layer * 2 * kvdim;
+            const int kv = rem / kvdim;
+            const int cc = rem - kv * kvdim;
+            const int head = cc / ep.head_dim;
+            const int dim = cc - head * ep.head_dim;
+            kv_col = (((size_t)layer * 2 + kv) * ep.kv_heads + head) * ep.frame_cap * ep.head_dim + dim;
+        }
+    }
+    // RoPE: region of the four columns and the angles of their two pairs
+    int region = 0, rdim = 0;  // region 0 = q, 1 = k, 2 = v; rdim = column inside the region
+    float cs0 = 1.f, sn0 = 0.f, cs1 = 1.f, sn1 = 0.f;
+    int t_pos = 0;
+    if constexpr (MODE == TC_EPI_ROPE_KV) {
+        const TcRopeKv& r = g.rope;
+        const int HD = r.H * r.hd, KVD = r.KVH * r.hd;
+        region = n < HD ? 0 : (n < HD + KVD ? 1 : 2);
+        rdim = region == 0 ? n : (region == 1 ? n - HD : n - HD - KVD);
+        t_pos = *r.pos;
+        const int ch = rdim % r.hd;
+        if (col_ok && region < 2) {
+            const float* cr = r.cos_t + (size_t)t_pos * (r.nd >> 1);
+            const float* sr = r.sin_t + (size_t)t_pos * (r.nd >> 1);
+            if (ch < r.nd) {
+                cs0 = cr[ch >> 1];
+                sn0 = sr[ch >> 1];
             }
-            if (isq) {
-                r.q[(size_t)m * HD + n] = a0;
-                r.q[(size_t)m * HD + n + 1] = a1;
-            } else {
-                const int j = n - HD;
-                r.kv_new[(size_t)m * 2 * KVD + j] = a0;
-                r.kv_new[(size_t)m * 2 * KVD + j + 1] = a1;
-                const int kv = j / KVD, c2 = j - kv * KVD;
-                const int head = c2 / r.hd, dim = c2 - head * r.hd;
-                const size_t idx = (((size_t)m * r.KVH + head) * r.t_cap + t) * r.hd + dim;
-                void* base = kv ? r.v_cache : r.k_cache;
-                if (r.kv_f16) {
-                    reinterpret_cast<__half*>(base)[idx] = __float2half_rn(a0);
-                    reinterpret_cast<__half*>(base)[idx + 1] = __float2half_rn(a1);
+            if (ch + 2 < r.nd) {
+                cs1 = cr[(ch >> 1) + 1];
+                sn1 = sr[(ch >> 1) + 1];
+            }
+        }
+    }
+
+#pragma unroll 2
+    for (int p = 0; p < passes; ++p) {
+        const int r = r0 + p * RPP;
+        const bool ok = col_ok && r < rows;
+        const int m = m0 + r;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (ok) v = *reinterpret_cast<const float4*>(tile + (size_t)r * LDS + c);
+        if constexpr (MODE == TC_EPI_STD) {
+            if (ok) {
+                v = add4(v, bias);
+                if (ep.act == ACT_SILU) v = make_float4(silu(v.x), silu(v.y), silu(v.z), silu(v.w));
+                else if (ep.act == ACT_GELU)
+                    v = make_float4(gelu_erf(v.x), gelu_erf(v.y), gelu_erf(v.z), gelu_erf(v.w));
+                if (ep.residual) v = add4(v, *reinterpret_cast<const float4*>(ep.residual + (size_t)m * ep.ldr + n));
+                if (ep.kv_scatter) {
+                    const size_t idx = kv_col + (size_t)(m + ep.frame_offset) * ep.head_dim;
+                    if (ep.kv_out32) *reinterpret_cast<float4*>(ep.kv_out32 + idx) = v;
+                    if (ep.kv_out16) st_f16x4(reinterpret_cast<__half*>(ep.kv_out16) + idx, v);
                 } else {
-                    reinterpret_cast<float*>(base)[idx] = a0;
-                    reinterpret_cast<float*>(base)[idx + 1] = a1;
+                    if (ep.out) *reinterpret_cast<float4*>(ep.out + (size_t)m * ep.ldc + n) = v;
+                    if (g.out_bf16) st_bf16x4(g.out_bf16 + (size_t)m * g.ldc_bf16 + n, v);
                 }
             }
-            break;
-        }
-        case TC_EPI_SWIGLU: {
-            const float val = a0 + (g.ep.bias ? g.ep.bias[n] : 0.f);
-            const float gate = a1 + (g.ep.bias ? g.ep.bias[n + 1] : 0.f);
-            g.out_bf16[(size_t)m * g.ldc_bf16 + (n >> 1)] = __float2bfloat16_rn(val * silu(gate));
-            break;
-        }
-        case TC_EPI_ARGMAX: {
-            if (a0 > best) {  // columns arrive in increasing order per lane: strict > keeps the lowest
-                best = a0;
-                bestn = n;
+        } else if constexpr (MODE == TC_EPI_ACCUM) {
+            if (ok) atomicAdd(reinterpret_cast<float4*>(ep.out + (size_t)m * ep.ldc + n), add4(v, bias));
+        } else if constexpr (MODE == TC_EPI_SWIGLU) {
+            if (ok) {  // columns (value, gate, value, gate) -> two outputs
+                v = add4(v, bias);
+                const __nv_bfloat162 o = __floats2bfloat162_rn(v.x * silu(v.y), v.z * silu(v.w));
+                *reinterpret_cast<__nv_bfloat162*>(g.out_bf16 + (size_t)m * g.ldc_bf16 + (n >> 1)) = o;
             }
-            if (has1 && a1 > best) {
-                best = a1;
-                bestn = n + 1;
+        } else if constexpr (MODE == TC_EPI_ROPE_KV) {
+            if (ok) {
+                const TcRopeKv& rp = g.rope;
+                if (region < 2) {
+                    const float x0 = v.x * cs0 - v.y * sn0, y0 = v.x * sn0 + v.y * cs0;
+                    const float x1 = v.z * cs1 - v.w * sn1, y1 = v.z * sn1 + v.w * cs1;
+                    v = make_float4(x0, y0, x1, y1);
+                }
+                if (region == 0) {
+                    *reinterpret_cast<float4*>(rp.q + (size_t)m * rp.H * rp.hd + rdim) = v;
+                } else {
+                    const int KVD = rp.KVH * rp.hd;
+                    const int j = (region - 1) * KVD + rdim;
+                    *reinterpret_cast<float4*>(rp.kv_new + (size_t)m * 2 * KVD + j) = v;
+                    const int head = rdim / rp.hd, dim = rdim - head * rp.hd;
+                    const size_t idx = (((size_t)m * rp.KVH + head) * rp.t_cap + t_pos) * rp.hd + dim;
+                    void* base = region == 2 ? rp.v_cache : rp.k_cache;
+                    if (rp.kv_f16) st_f16x4(reinterpret_cast<__half*>(base) + idx, v);
+                    else *reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + idx) = v;
+                }
             }
-            if (g.ep.out) {
-                g.ep.out[(size_t)m * g.ep.ldc + n] = a0;
-                if (has1) g.ep.out[(size_t)m * g.ep.ldc + n + 1] = a1;
+        } else {  // TC_EPI_ARGMAX: the TPR threads of a row lie in one warp
+            float best = -INFINITY;
+            int bestn = 0x7fffffff;
+            if (ok) {
+                if (ep.out) *reinterpret_cast<float4*>(ep.out + (size_t)m * ep.ldc + n) = v;
+                // increasing column order with strict > keeps the lowest index on ties
+                if (v.x > best) { best = v.x; bestn = n; }
+                if (v.y > best) { best = v.y; bestn = n + 1; }
+                if (v.z > best) { best = v.z; bestn = n + 2; }
+                if (v.w > best) { best = v.w; bestn = n + 3; }
             }
-            break;
+#pragma unroll
+            for (int o = TPR / 2; o > 0; o >>= 1) {
+                const float bo = __shfl_xor_sync(FULL, best, o);
+                const int no = __shfl_xor_sync(FULL, bestn, o);
+                if (bo > best || (bo == best && no < bestn)) {
+                    best = bo;
+                    bestn = no;
+                }
+            }
+            if ((t % TPR) == 0 && r < rows && best > -INFINITY) atomicMax(g.argmax + m, argmax_key(best, bestn));
         }
-        case TC_EPI_ACCUM: {
-            const bool add_bias = blockIdx.z == 0 && g.ep.bias;
-            float* o = g.ep.out + (size_t)m * g.ep.ldc + n;
-            atomicAdd(o, a0 + (add_bias ? g.ep.bias[n] : 0.f));
-            if (has1) atomicAdd(o + 1, a1 + (add_bias ? g.ep.bias[n + 1] : 0.f));
-            break;
-        }
-        default:
-            store_out(g, m, n, a0);
-            if (has1) store_out(g, m, n + 1, a1);
     }
 }
 
-template <int BN>
+template <int BN, int MODE>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                TcGemmArgs g) {
@@ -273,7 +310,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         for (int kb = 0; kb < nkb; ++kb) {
             const int st = kb % STAGES;
             if (kb >= STAGES && !mbar_wait(&s.empty[st], ((kb / STAGES) - 1) & 1)) {
-                atomicCAS(g.status, 0u, 5u);
+                atomicCAS(g.status, 0u, (unsigned)DEV_WAIT_TIMEOUT);
                 s_fail = 1;
                 break;
             }
@@ -290,7 +327,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         for (int kb = 0; kb < nkb; ++kb) {
             const int st = kb % STAGES;
             if (!mbar_wait(&s.full[st], (kb / STAGES) & 1)) {
-                atomicCAS(g.status, 0u, 5u);
+                atomicCAS(g.status, 0u, (unsigned)DEV_WAIT_TIMEOUT);
                 s_fail = 1;
                 break;
             }
@@ -308,53 +345,30 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     __syncwarp();
     __syncthreads();  // role loops finished; s_fail is final
 
-    // epilogue: warp w owns accumulator lanes (rows) 32w .. 32w+31
+    // epilogue: warp w owns accumulator lanes (rows) 32w .. 32w+31.  The tile goes through
+    // shared memory (the idle stage buffers) so the global side is row-contiguous.
     bool ok = nkb > 0 && mbar_wait(&s.done, 0);  // an empty k-split contributes nothing
-    if (nkb > 0 && !ok) atomicCAS(g.status, 0u, 5u);
-    ok = __all_sync(FULL, ok) && !s_fail;  // tcgen05.ld below is warp-collective
+    if (nkb > 0 && !ok) atomicCAS(g.status, 0u, (unsigned)DEV_WAIT_TIMEOUT);
+    ok = __syncthreads_and(ok && !s_fail);      // uniform: the epilogue crosses warps
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    // The accumulator tile goes through shared memory (the idle stage buffers) so that the
-    // epilogue walks rows with lanes along columns: every global store / atomic of a warp
-    // then touches one contiguous row segment instead of 32 rows.
-    constexpr int LDS = BN + 1;  // +1: rows written by the 32 lanes of a warp hit distinct banks
+    constexpr int LDS = tile_ld<BN>();
     float* tile = reinterpret_cast<float*>(&s.a[0][0]);
     static_assert(sizeof(float) * BM * LDS <= sizeof(s.a) + sizeof(s.b), "epilogue tile must fit the stages");
     if (ok) {
-        const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-        float* my = tile + (size_t)(warp * 32 + lane) * LDS;
-        for (int c0 = 0; c0 < BN; c0 += 8) {
-            float v[8];
-            tmem_ld8(lane_addr + c0, v);
+        if (warp * 32 < g.M - m0) {  // warp-uniform: lanes of rows past M hold nothing
+            const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+            float* my = tile + (size_t)(warp * 32 + lane) * LDS;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                float v[32];
+                tmem_ld32(lane_addr + c0, v);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) my[c0 + i] = v[i];
-        }
-    }
-    __syncthreads();
-    if (ok) {
-        const int rows = min(BM, g.M - m0);
-        for (int r = warp; r < rows; r += TC_THREADS / 32) {
-            const int m = m0 + r;
-            const float* row = tile + (size_t)r * LDS;
-            float best = -INFINITY;
-            int bestn = 0x7fffffff;
-            for (int c = 2 * lane; c < BN; c += 64) {
-                const int n = n0 + c;
-                if (n >= g.N) break;
-                epilogue2(g, m, n, row[c], row[c + 1], n + 1 < g.N, best, bestn);
-            }
-            if (g.mode == TC_EPI_ARGMAX) {
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const float bo = __shfl_xor_sync(FULL, best, o);
-                    const int no = __shfl_xor_sync(FULL, bestn, o);
-                    if (bo > best || (bo == best && no < bestn)) {
-                        best = bo;
-                        bestn = no;
-                    }
-                }
-                if (lane == 0 && best > -INFINITY) atomicMax(g.argmax + m, argmax_key(best, bestn));
+                for (int i = 0; i < 32; i += 4)
+                    *reinterpret_cast<float4*>(my + c0 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
             }
         }
+        __syncthreads();
+        epilogue_tile<BN, MODE>(g, tile, m0, n0);
     }
     // drain copies still in flight after a failure (bounded), then free tensor memory
     if (warp == 0 && lane == 0 && s_fail) {
@@ -409,38 +423,80 @@ bool tc_make_map_2d(CUtensorMap* map, const void* base, uint64_t dim_k, uint64_t
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+namespace {
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+template <int BN, int MODE>
+cudaError_t launch_tc(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcGemmArgs& g, cudaStream_t stream) {
+    const size_t smem = sizeof(TcSmem<BN>) + 1024;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e =
+            cudaFuncSetAttribute(gemm_tc_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    const dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.splits);
+    gemm_tc_kernel<BN, MODE><<<grid, TC_THREADS, smem, stream>>>(map_a, map_b, g);
+    return cudaGetLastError();
+}
+
+template <int BN>
+cudaError_t launch_tc_mode(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcGemmArgs& g,
+                           cudaStream_t stream) {
+    switch (g.mode) {
+        case TC_EPI_STD: return launch_tc<BN, TC_EPI_STD>(map_a, map_b, g, stream);
+        case TC_EPI_ROPE_KV: return launch_tc<BN, TC_EPI_ROPE_KV>(map_a, map_b, g, stream);
+        case TC_EPI_SWIGLU: return launch_tc<BN, TC_EPI_SWIGLU>(map_a, map_b, g, stream);
+        case TC_EPI_ARGMAX: return launch_tc<BN, TC_EPI_ARGMAX>(map_a, map_b, g, stream);
+        case TC_EPI_ACCUM: return launch_tc<BN, TC_EPI_ACCUM>(map_a, map_b, g, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// The epilogue moves four columns per thread with 128-bit (fp32) / 64-bit (bf16, fp16)
+// accesses: every output it touches must allow that.
+bool epilogue_layout_ok(const TcGemmArgs& g) {
+    const GemmEpilogue& ep = g.ep;
+    if (g.N % 4) return false;
+    switch (g.mode) {
+        case TC_EPI_STD:
+            if (ep.bias && !aligned(ep.bias, 16)) return false;
+            if (ep.residual && (ep.ldr % 4 || !aligned(ep.residual, 16))) return false;
+            if (ep.kv_scatter)
+                return ep.head_dim % 4 == 0 && (!ep.kv_out32 || aligned(ep.kv_out32, 16)) &&
+                       (!ep.kv_out16 || aligned(ep.kv_out16, 8));
+            if (ep.out && (ep.ldc % 4 || !aligned(ep.out, 16))) return false;
+            if (g.out_bf16 && (g.ldc_bf16 % 4 || !aligned(g.out_bf16, 8))) return false;
+            return true;
+        case TC_EPI_ACCUM:
+            return ep.out && ep.ldc % 4 == 0 && aligned(ep.out, 16) && (!ep.bias || aligned(ep.bias, 16));
+        case TC_EPI_SWIGLU:
+            return g.out_bf16 && g.ldc_bf16 % 2 == 0 && aligned(g.out_bf16, 4) && (!ep.bias || aligned(ep.bias, 16));
+        case TC_EPI_ROPE_KV: {
+            const TcRopeKv& r = g.rope;
+            return r.hd % 4 == 0 && aligned(r.q, 16) && aligned(r.kv_new, 16) &&
+                   aligned(r.k_cache, r.kv_f16 ? 8 : 16) && aligned(r.v_cache, r.kv_f16 ? 8 : 16) &&
+                   g.N == (r.H + 2 * r.KVH) * r.hd;
+        }
+        case TC_EPI_ARGMAX:
+            return g.argmax && (!ep.out || (ep.ldc % 4 == 0 && aligned(ep.out, 16)));
+        default:
+            return false;
+    }
+}
+}  // namespace
+
 cudaError_t launch_gemm_tc(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcGemmArgs& g, int bn,
                            cudaStream_t stream) {
     if (g.M <= 0 || g.N <= 0) return cudaSuccess;
     if (g.taps < 1 || g.taps > 8 || g.kb_per_tap < 1 || !g.status) return cudaErrorInvalidValue;
     if (g.splits < 1 || (g.splits > 1 && g.mode != TC_EPI_ACCUM)) return cudaErrorInvalidValue;
-    if ((g.mode == TC_EPI_ROPE_KV || g.mode == TC_EPI_SWIGLU) && (g.N & 1)) return cudaErrorInvalidValue;
-    const dim3 grid((g.N + bn - 1) / bn, (g.M + BM - 1) / BM, g.splits);
+    if (!epilogue_layout_ok(g)) return cudaErrorInvalidValue;
     ++launch_counter();
-    if (bn == 128) {
-        const size_t smem = sizeof(TcSmem<128>) + 1024;
-        static bool set128 = false;
-        if (!set128) {
-            cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)smem);
-            if (e != cudaSuccess) return e;
-            set128 = true;
-        }
-        gemm_tc_kernel<128><<<grid, TC_THREADS, smem, stream>>>(map_a, map_b, g);
-    } else if (bn == 64) {
-        const size_t smem = sizeof(TcSmem<64>) + 1024;
-        static bool set64 = false;
-        if (!set64) {
-            cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)smem);
-            if (e != cudaSuccess) return e;
-            set64 = true;
-        }
-        gemm_tc_kernel<64><<<grid, TC_THREADS, smem, stream>>>(map_a, map_b, g);
-    } else {
-        return cudaErrorInvalidValue;
-    }
-    return cudaGetLastError();
+    if (bn == 128) return launch_tc_mode<128>(map_a, map_b, g, stream);
+    if (bn == 64) return launch_tc_mode<64>(map_a, map_b, g, stream);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace msb

@@ -12,7 +12,7 @@ namespace msb {
 int64_t& launch_counter();
 
 // Device-side error codes reported through a kernel's status word.
-enum : unsigned { DEV_OK = 0, DEV_BARRIER_TIMEOUT = 1, DEV_BAD_TOKEN = 2 };
+enum : unsigned { DEV_OK = 0, DEV_BARRIER_TIMEOUT = 1, DEV_BAD_TOKEN = 2, DEV_WAIT_TIMEOUT = 5 };
 
 // ---------------------------------------------------------------- frontend
 // Frame features: per 80-sample frame CMVN, asinh(exp(log_k) x), SiLU(x W^T).
@@ -179,7 +179,7 @@ cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const vo
 cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const void* cross_st, int st_f16,
                                     const int* pos, const int* frame_off, const int* frames, int B, int H, int KVH,
                                     int hd, int m_cap, int layer, int max_frames, float scale, float* part,
-                                    __nv_bfloat16* out, int first_step, cudaStream_t s);
+                                    __nv_bfloat16* out, int first_step, unsigned* status, cudaStream_t s);
 cudaError_t launch_step_finalize(unsigned long long* amax, int B, int* pos, int* next_ids, int* ids_out, int t_cap,
                                  int* counts, const int* limits, int* done, int* hit_eos, int eos, int forced,
                                  cudaStream_t s);

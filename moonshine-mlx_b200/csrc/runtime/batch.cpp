@@ -197,7 +197,7 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
         MSB_CUDA(launch_cross_attn_batch(qc.as<float>(), cross32.as<float>(), m.kv_f16 ? cross16.p : cross32.p,
                                          m.kv_f16 ? 1 : 0, posp, frame_off.as<int>(), frames.as<int>(), B, H, KVH,
                                          hd, Mc, l, max_frames, scale, part.as<float>(), attn.as<__nv_bfloat16>(),
-                                         first ? 1 : 0, s));
+                                         first ? 1 : 0, status.as<unsigned>(), s));
         {
             TcGemmArgs ga;
             ga.M = B;
