@@ -63,8 +63,13 @@ typedef struct {
     int32_t kv_dtype;        /* ms_kv_dtype; default MS_KV_F16 like prepareForInference */
     int32_t weight_dtype;    /* ms_weight_dtype */
     int32_t max_batch;       /* largest ms_generate_batch / stream batch (default 64) */
-    int32_t reserved[8];
+    int32_t decode_kernel;   /* batch-1 decode kernel: MS_DECODE_AUTO (head-clustered when the
+                                dims and the GPU allow it) or MS_DECODE_GRID (single-grid
+                                persistent kernel).  Both compute the same greedy loop. */
+    int32_t reserved[7];
 } ms_options;
+
+enum { MS_DECODE_AUTO = 0, MS_DECODE_GRID = 1 };
 
 /* Fills *opts with the defaults (device 0, fp16 KV, auto weights, max_batch 64). */
 void ms_options_default(ms_options* opts);

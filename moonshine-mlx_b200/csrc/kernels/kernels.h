@@ -188,6 +188,25 @@ cudaError_t launch_f32_to_bf16_rows(const float* src, __nv_bfloat16* dst, int ro
 cudaError_t launch_interleave_f32(const float* src, float* dst, int n2, int half, cudaStream_t s);
 size_t cross_batch_part_floats(int B, int H, int hd, int max_frames);
 
+// Head-clustered batch-1 decode (one 8-CTA cluster per head, packed per-CTA weight streams).
+struct ClusterGeom {
+    int rq = 0, ro = 0, rcq = 0, gr = 0, rlm = 0;  // rows per CTA: q|k|v, out-proj, cross q, SwiGLU, vocab
+    int slot_bytes = 0;                           // weight-stream ring slot
+    int skv_keys = 0;                             // cached self keys per CTA (ceil(t_cap / 8))
+    size_t cta_floats = 0;                        // packed stream length per CTA
+    const float* packed = nullptr;                // [H * 8][cta_floats]
+    unsigned long long* part = nullptr;           // tagged exchange words: [2][H][d] partial sums, then
+                                                  // [H * 8][2] per-CTA argmax; zeroed before each launch
+    size_t part_words = 0;
+};
+// false when the dims do not fit the clustered kernel (the caller keeps decode_b1)
+bool cluster_geom(int d, int H, int KVH, int hd, int I, int V, int L, int t_cap, ClusterGeom* g);
+int cluster_ctas(int H);
+cudaError_t pack_cluster_weights(const ClusterGeom& g, const DecodeLayerW* layers_host, int L, const float* lm_head,
+                                 const float* final_ln, int d, int H, int hd, int I, int V, float* packed,
+                                 cudaStream_t s);
+cudaError_t launch_decode_cluster(const DecodeParams& p, const ClusterGeom& g, cudaStream_t stream);
+
 // Persistent cooperative decode kernel: runs up to n_steps greedy decoder calls.
 cudaError_t launch_decode_b1(const DecodeParams& p, int grid, cudaStream_t stream);
 int decode_b1_block_threads();

@@ -617,6 +617,24 @@ void Model::cross_kv_into(const float* memory, int frames, int row0, float* out3
     MSB_CUDA(launch_gemm_f32(memory, c.hidden, cross_w, c.hidden, frames, N, c.hidden, e, stream));
 }
 
+bool Model::prepare_cluster_decode() {
+    if (cl_tried) return cl_ok;
+    cl_tried = true;
+    const Config& c = cfg;
+    ClusterGeom g;
+    if (!cluster_geom(c.hidden, c.heads, c.kv_heads, c.head_dim, c.inter, c.vocab, c.layers, 0, &g)) return false;
+    cl_packed.ensure((size_t)cluster_ctas(c.heads) * g.cta_floats * 4);
+    g.part_words = (size_t)2 * c.heads * c.hidden + (size_t)2 * cluster_ctas(c.heads);
+    cl_part.ensure(g.part_words * 8);
+    MSB_CUDA(pack_cluster_weights(g, dec.data(), c.layers, lm_head, dec_norm, c.hidden, c.heads, c.head_dim, c.inter,
+                                  c.vocab, cl_packed.as<float>(), stream));
+    g.packed = cl_packed.as<float>();
+    g.part = cl_part.as<unsigned long long>();
+    cl_geom = g;
+    cl_ok = true;
+    return true;
+}
+
 Model::DecodeResult Model::decode(const float* cross32, const void* cross_stored, int m_cap, int M,
                                   int n_steps, bool forced, const int* teacher_dev, bool logits) {
     const Config& c = cfg;
@@ -678,7 +696,20 @@ Model::DecodeResult Model::decode(const float* cross32, const void* cross_stored
         p.trace_cap = trace_n;
     }
     MSB_CUDA(cudaMemsetAsync(flags, 0, 16, stream));
-    MSB_CUDA(launch_decode_b1(p, num_sms, stream));
+    bool launched = false;
+    if (opts.decode_kernel == MS_DECODE_AUTO && prepare_cluster_decode()) {
+        ClusterGeom g = cl_geom;
+        ClusterGeom sized;
+        if (cluster_geom(c.hidden, c.heads, c.kv_heads, c.head_dim, c.inter, c.vocab, c.layers, ws.t_cap, &sized)) {
+            g.skv_keys = sized.skv_keys;
+            MSB_CUDA(cudaMemsetAsync(g.part, 0, g.part_words * 8, stream));  // no stale exchange word
+            const cudaError_t e = launch_decode_cluster(p, g, stream);
+            if (e == cudaSuccess) launched = true;
+            else if (e == cudaErrorCooperativeLaunchTooLarge) (void)cudaGetLastError();  // not all clusters fit
+            else MSB_CUDA(e);
+        }
+    }
+    if (!launched) MSB_CUDA(launch_decode_b1(p, num_sms, stream));
     unsigned hf[4];
     MSB_CUDA(cudaMemcpyAsync(hf, flags, 16, cudaMemcpyDeviceToHost, stream));
     if (trace_n) {

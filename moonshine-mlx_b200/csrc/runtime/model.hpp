@@ -101,6 +101,11 @@ struct Model {
     int rope_cap = 0;
 
     Workspace ws;
+    // head-clustered batch-1 decode: packed per-CTA weight streams, built on first use
+    bool cl_tried = false, cl_ok = false;
+    ClusterGeom cl_geom;
+    DevBuf cl_packed, cl_part;
+    bool prepare_cluster_decode();
     std::unique_ptr<BatchEngine> batch;  // batched bf16 tensor-core decode, built on first use
     bool trace_enabled = false;
     DevBuf trace_buf;

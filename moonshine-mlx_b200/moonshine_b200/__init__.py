@@ -45,7 +45,7 @@ class MoonshineError(RuntimeError):
 
 class _Options(C.Structure):
     _fields_ = [("device", C.c_int32), ("kv_dtype", C.c_int32), ("weight_dtype", C.c_int32),
-                ("max_batch", C.c_int32), ("reserved", C.c_int32 * 8)]
+                ("max_batch", C.c_int32), ("decode_kernel", C.c_int32), ("reserved", C.c_int32 * 7)]
 
 
 class _GenParams(C.Structure):
@@ -217,12 +217,18 @@ class MoonshineModel:
         self.config = cfg
 
     @staticmethod
-    def load(path: str, device: int = 0, kv_fp16: bool = True) -> "MoonshineModel":
-        """MoonshineModel.load(from:) for a local directory (MoonshineModel.swift:409-414)."""
+    def load(path: str, device: int = 0, kv_fp16: bool = True, decode_kernel: str = "auto") -> "MoonshineModel":
+        """MoonshineModel.load(from:) for a local directory (MoonshineModel.swift:409-414).
+
+        ``decode_kernel`` picks the batch-1 decode kernel: "auto" (head-clustered when the
+        dims and the GPU allow it) or "grid" (single-grid persistent kernel)."""
+        if decode_kernel not in ("auto", "grid"):
+            raise ValueError("decode_kernel must be 'auto' or 'grid'")
         o = _Options()
         _L().ms_options_default(C.byref(o))
         o.device = device
         o.kv_dtype = KV_F16 if kv_fp16 else KV_F32
+        o.decode_kernel = 0 if decode_kernel == "auto" else 1
         h = C.c_void_p()
         _check(_L().ms_model_load(path.encode(), C.byref(o), C.byref(h)))
         return MoonshineModel(h)

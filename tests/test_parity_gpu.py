@@ -128,3 +128,17 @@ def test_small_arch_head_dim_64(model_root):
         ids, _, logits, _ = o.greedy(mem, 16, kv, teacher=teacher.tolist(), keep_logits=True)
         assert out.tokens == ids
         assert_logits_close(out.logits[:16], logits, FP32_LOGIT_TOL)
+
+
+@pytest.mark.parametrize("kernel", ["grid", "auto"])
+def test_both_decode_kernels_30s(tiny_dir, kernel):
+    """30 s of audio (1500 memory frames), fp16 KV, 48 forced tokens through each batch-1
+    decode kernel: the single-grid one and the head-clustered one ("auto" on a B200)."""
+    import moonshine_b200 as mb
+    m = mb.MoonshineModel.load(tiny_dir, decode_kernel=kernel)
+    audio = synth.synth_audio(480000, 1)
+    out = m.generate(audio, forced_len=48, return_logits=True)
+    o = oracle_for(tiny_dir)
+    ids, _, logits, _ = o.greedy(o.memory_for(audio), 48, True, forced_len=48, keep_logits=True)
+    assert out.tokens == ids
+    assert_logits_close(out.logits[:48], logits, FP32_LOGIT_TOL)
