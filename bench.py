@@ -58,14 +58,20 @@ def decode_bytes_per_launch(cfg, M, n_tokens, kv_bytes=2):
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode launch (16 decoder calls, 1500
-# memory frames, fp16 KV) from an ncu capture; per-call traffic is flat after the first call.
-NCU_DECODE_BYTES_16CALLS_1500F = 830.744e6 + 5.621e6
+# memory frames, fp16 KV) from an ncu capture of each batch-1 kernel; per-call traffic is
+# flat after the first call.
+NCU_DECODE_BYTES_16CALLS_1500F = {
+    "cluster": (1462431488 + 3375360, "profiles/decode_cluster_tiny_30s_16tok.md"),
+    "grid": (830.744e6 + 5.621e6, "profiles/decode_b1_tiny_30s_16tok.md"),
+}
+DECODE_KERNEL_SYMBOL = {"cluster": "decode_cluster_kernel<40>", "grid": "decode_b1_kernel<40>"}
 
 
-def decode_traffic_per_launch(M, n_tokens):
-    if M != 1500:
-        return None
-    return int(NCU_DECODE_BYTES_16CALLS_1500F * n_tokens / 16)
+def decode_traffic_per_launch(M, n_tokens, kernel):
+    if M != 1500 or kernel not in NCU_DECODE_BYTES_16CALLS_1500F:
+        return None, None
+    b, src = NCU_DECODE_BYTES_16CALLS_1500F[kernel]
+    return int(b * n_tokens / 16), src
 
 
 def measured_peak():
@@ -277,7 +283,7 @@ def main():
 
     # ---- device-resident timing (value)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    dec_ms, enc_ms, ntok = [], [], 0
+    dec_ms, enc_ms, ntok, kernels = [], [], 0, set()
     barrier()
     torch.cuda.synchronize()
     mb.reset_kernel_launches()
@@ -289,6 +295,7 @@ def main():
             n, st = run_device()
             evs[k][1].record(stream)
             ntok += n
+            kernels.add(mb.DECODE_KERNEL_NAMES.get(st.decode_kernel, "?"))
             dec_ms.append(st.decode_ms)
             enc_ms.append(st.encode_ms)
         torch.cuda.synchronize()
@@ -326,6 +333,8 @@ def main():
         peak, peak_kind = measured_peak()
         total_tokens = world * FORCED * args.steps
         value = total_tokens / (t_rank / 1e3)
+        kern = kernels.pop() if len(kernels) == 1 else "mixed"
+        traffic, traffic_src = decode_traffic_per_launch(M, FORCED, kern)
         line = {
             "metric": "decode tokens/s", "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_rank / args.steps, 4),
@@ -338,12 +347,13 @@ def main():
             "encode_ms": round(statistics.mean(enc_ms), 4),
             "rtfx": round((N_SAMPLES / 16000.0) / (t_rank / args.steps / 1e3), 1),
             "gpu_launches": int(launches),
-            "roofline": {"bound": "hbm", "kernel": "decode_b1_kernel", "achieved": round(achieved, 1),
+            "roofline": {"bound": "hbm", "kernel": DECODE_KERNEL_SYMBOL.get(kern, kern),
+                         "achieved": round(achieved, 1),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(bytes_launch),
-                         "launch_ms": round(dec_avg, 4), "traffic": decode_traffic_per_launch(M, FORCED),
-                         "traffic_source": "ncu dram__bytes of a 16-call launch at 1500 frames, scaled by "
-                                           "decoder calls (profiles/decode_b1_tiny_30s_16tok.md)"},
+                         "launch_ms": round(dec_avg, 4), "traffic": traffic,
+                         "traffic_source": (f"ncu dram__bytes of a 16-call launch at 1500 frames, scaled by "
+                                            f"decoder calls ({traffic_src})") if traffic_src else None},
             "e2e": {"value": round(total_tokens / (t_e2e / 1e3), 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": N_SAMPLES * 4, "d2h_bytes_per_step": FORCED * 4 + 16},
             "clocks": clocks.summary(),

@@ -69,7 +69,7 @@ typedef struct {
     int32_t reserved[7];
 } ms_options;
 
-enum { MS_DECODE_AUTO = 0, MS_DECODE_GRID = 1 };
+enum { MS_DECODE_AUTO = 0, MS_DECODE_GRID = 1, MS_DECODE_CLUSTER = 2 };
 
 /* Fills *opts with the defaults (device 0, fp16 KV, auto weights, max_batch 64). */
 void ms_options_default(ms_options* opts);
@@ -132,6 +132,7 @@ typedef struct {
     int32_t n_chunks;
     int32_t hit_eos;           /* last chunk ended on EOS */
     int32_t memory_frames;     /* encoder frames of the last chunk */
+    int32_t decode_kernel;     /* batch-1 kernel of the last chunk: MS_DECODE_GRID or MS_DECODE_CLUSTER */
     double encode_ms, decode_ms, total_ms;
     double tokens_per_second;  /* n_tokens / total (MoonshineModel.swift:182) */
 } ms_gen_stats;

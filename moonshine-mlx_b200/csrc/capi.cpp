@@ -110,6 +110,7 @@ static void generate_chunk(Model& m, const float* audio, int64_t len, const ms_g
     st.encode_ms += t_enc;
     st.decode_ms += t_dec;
     st.hit_eos = r.hit_eos ? 1 : 0;
+    st.decode_kernel = r.kernel;
     out.n_ids += n_ids;
 }
 

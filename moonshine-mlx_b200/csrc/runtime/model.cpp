@@ -724,6 +724,7 @@ Model::DecodeResult Model::decode(const float* cross32, const void* cross_stored
     DecodeResult r;
     r.n_calls = (int)hf[2];
     r.hit_eos = hf[3] != 0;
+    r.kernel = launched ? MS_DECODE_CLUSTER : MS_DECODE_GRID;
     return r;
 }
 

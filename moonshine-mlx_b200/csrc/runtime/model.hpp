@@ -130,6 +130,7 @@ struct Model {
     struct DecodeResult {
         int n_calls = 0;
         bool hit_eos = false;
+        int kernel = MS_DECODE_GRID;  // which batch-1 kernel ran
     };
     // Greedy decode against cross K/V laid out [L][2][KVH][m_cap][hd] (fp32 copy for the
     // first decoder call, stored copy afterwards).

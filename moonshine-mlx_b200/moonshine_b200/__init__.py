@@ -56,9 +56,12 @@ class _GenParams(C.Structure):
                 ("batch_logits", C.POINTER(C.c_float)), ("reserved", C.c_int32 * 4)]
 
 
+DECODE_KERNEL_NAMES = {1: "grid", 2: "cluster"}
+
+
 class _GenStats(C.Structure):
     _fields_ = [("n_tokens", C.c_int32), ("n_chunks", C.c_int32), ("hit_eos", C.c_int32),
-                ("memory_frames", C.c_int32), ("encode_ms", C.c_double),
+                ("memory_frames", C.c_int32), ("decode_kernel", C.c_int32), ("encode_ms", C.c_double),
                 ("decode_ms", C.c_double), ("total_ms", C.c_double),
                 ("tokens_per_second", C.c_double)]
 
@@ -172,6 +175,7 @@ class TranscriptionOutput:
     decode_ms: float = 0.0
     hit_eos: bool = False
     memory_frames: int = 0
+    decode_kernel: str = ""   # batch-1 kernel of the last chunk: "grid" or "cluster"
     logits: Optional[np.ndarray] = None
 
 
@@ -296,7 +300,8 @@ class MoonshineModel:
                                   total_time=st.total_ms / 1000.0,
                                   tokens_per_second=st.tokens_per_second,
                                   encode_ms=st.encode_ms, decode_ms=st.decode_ms,
-                                  hit_eos=bool(st.hit_eos), memory_frames=st.memory_frames)
+                                  hit_eos=bool(st.hit_eos), memory_frames=st.memory_frames,
+                                  decode_kernel=DECODE_KERNEL_NAMES.get(st.decode_kernel, ""))
         if return_logits:
             out.logits = logits
         return out
