@@ -26,6 +26,44 @@ void make_a_map(CUtensorMap* map, const __nv_bfloat16* a, int rows, int K) {
 
 BatchEngine::~BatchEngine() {
     for (auto* b : own) delete b;
+    for (auto& l : lanes) {
+        if (l->stream) cudaStreamDestroy(l->stream);
+        if (l->done) cudaEventDestroy(l->done);
+    }
+    if (ev_start) cudaEventDestroy(ev_start);
+}
+
+// Encode every utterance into memory rows [off[b], off[b] + frames) of the batch memory.
+// Utterance b runs on lane b % K; the model stream waits for all lanes at the end.
+void BatchEngine::encode_all(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
+                             const std::vector<int>& off) {
+    constexpr int kLanes = 8;
+    const int B = (int)audio_dev.size();
+    const int K = std::min(B, kLanes);
+    if (!ev_start) MSB_CUDA(cudaEventCreateWithFlags(&ev_start, cudaEventDisableTiming));
+    while ((int)lanes.size() < K) {
+        auto l = std::make_unique<EncLane>();
+        MSB_CUDA(cudaStreamCreateWithFlags(&l->stream, cudaStreamNonBlocking));
+        MSB_CUDA(cudaEventCreateWithFlags(&l->done, cudaEventDisableTiming));
+        lanes.push_back(std::move(l));
+    }
+    const int64_t longest = *std::max_element(n_samples.begin(), n_samples.end());
+    for (int k = 0; k < K; ++k) m.reserve_encoder(lanes[k]->bufs(), longest);  // before any lane runs
+    MSB_CUDA(cudaEventRecord(ev_start, m.stream));
+    for (int k = 0; k < K; ++k) MSB_CUDA(cudaStreamWaitEvent(lanes[k]->stream, ev_start, 0));
+    const int hidden = m.cfg.hidden;
+    for (int b = 0; b < B; ++b) {
+        EncLane& l = *lanes[b % K];
+        const EncBufs eb = l.bufs();
+        const int M = m.encode_into(eb, audio_dev[b], n_samples[b], 0, l.stream);
+        if (M <= 0) throw MsError(MS_ERR_CUDA, "frame count mismatch");
+        MSB_CUDA(cudaMemcpyAsync(memory.as<float>() + (size_t)off[b] * hidden, m.memory_of(eb),
+                                 (size_t)M * hidden * 4, cudaMemcpyDeviceToDevice, l.stream));
+    }
+    for (int k = 0; k < K; ++k) {
+        MSB_CUDA(cudaEventRecord(lanes[k]->done, lanes[k]->stream));
+        MSB_CUDA(cudaStreamWaitEvent(m.stream, lanes[k]->done, 0));
+    }
 }
 
 template <class T>
@@ -271,12 +309,7 @@ BatchEngine::Result BatchEngine::run(const std::vector<const float*>& audio_dev,
     }
     const int T = *std::max_element(limits.begin(), limits.end());
     ensure_ws(B, T, Mtot, maxM);
-    for (int b = 0; b < B; ++b) {
-        const int M = m.encode_device(audio_dev[b], n_samples[b], 0);
-        if (M != fr[b]) throw MsError(MS_ERR_CUDA, "frame count mismatch");
-        MSB_CUDA(cudaMemcpyAsync(memory.as<float>() + (size_t)off[b] * c.hidden, m.memory_ptr(),
-                                 (size_t)M * c.hidden * 4, cudaMemcpyDeviceToDevice, s));
-    }
+    encode_all(audio_dev, n_samples, off);
     m.cross_kv_into(memory.as<float>(), Mtot, 0, cross32.as<float>(), m.kv_f16 ? cross16.p : nullptr, Mc);
     MSB_CUDA(cudaEventRecord(m.ev[1], s));
     // step state

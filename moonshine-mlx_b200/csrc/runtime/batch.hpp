@@ -3,6 +3,7 @@
 
 #include <cuda.h>
 
+#include <memory>
 #include <vector>
 
 #include "model.hpp"
@@ -42,6 +43,19 @@ struct BatchEngine {
     DevBuf x, hb, attn, g, q, qc, kvnew, kcache, vcache, part, amax, ids, next_ids, counts, limits_d, done, hit,
         pos, frame_off, frames, cross32, cross16, memory, status;
     CUtensorMap a_hb, a_attn, a_g;
+
+    // Concurrent encoder lanes: each has its own scratch buffers and stream, so independent
+    // utterances' (latency-bound) encoders overlap on the GPU.
+    struct EncLane {
+        DevBuf feat1p, feat2p, x, h, qkv, attn, f, memory, memproj;
+        cudaStream_t stream = nullptr;
+        cudaEvent_t done = nullptr;
+        EncBufs bufs() { return {&feat1p, &feat2p, &x, &h, &qkv, &attn, &f, &memory, &memproj}; }
+    };
+    std::vector<std::unique_ptr<EncLane>> lanes;
+    cudaEvent_t ev_start = nullptr;
+    void encode_all(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
+                    const std::vector<int>& off);
 
     template <class T> T* alloc(size_t n);
     void ensure_weights();

@@ -471,53 +471,84 @@ Model* load_model(const std::string& dir, const ms_options& o) {
 
 // ------------------------------------------------------------------ encode
 
-const float* Model::memory_ptr() const {
-    return proj ? ws.memproj.as<float>() : ws.memory.as<float>();
+EncBufs Model::own_enc_bufs() {
+    return {&ws.feat1p, &ws.feat2p, &ws.x, &ws.h, &ws.qkv, &ws.attn, &ws.f, &ws.memory, &ws.memproj};
 }
 
-void Model::encoder_layers(float* x, int T) {
+const float* Model::memory_ptr() const { return proj ? ws.memproj.as<float>() : ws.memory.as<float>(); }
+
+const float* Model::memory_of(const EncBufs& b) const {
+    return proj ? b.memproj->as<float>() : b.memory->as<float>();
+}
+
+void Model::encoder_layers(float* x, int T) { encoder_layers_on(own_enc_bufs(), x, T, stream); }
+
+int Model::encode_device(const float* audio_dev, int64_t n_samples, int pos_offset) {
+    return encode_into(own_enc_bufs(), audio_dev, n_samples, pos_offset, stream);
+}
+
+void Model::encoder_layers_on(const EncBufs& b, float* x, int T, cudaStream_t s) {
     const Config& c = cfg;
     const int ed = c.e_hidden, hd = c.e_head_dim;
     const int eHD = c.e_heads * hd, QKV = (c.e_heads + 2 * c.e_kv_heads) * hd;
-    ws.h.ensure((size_t)T * ed * 4);
-    ws.qkv.ensure((size_t)T * QKV * 4);
-    ws.attn.ensure((size_t)T * eHD * 4);
-    ws.f.ensure((size_t)T * c.e_inter * 4);
+    b.h->ensure((size_t)T * ed * 4);
+    b.qkv->ensure((size_t)T * QKV * 4);
+    b.attn->ensure((size_t)T * eHD * 4);
+    b.f->ensure((size_t)T * c.e_inter * 4);
+    float *h = b.h->as<float>(), *qkv = b.qkv->as<float>(), *attn = b.attn->as<float>(), *f = b.f->as<float>();
     const float scale = std::pow((float)hd, -0.5f);
     for (int i = 0; i < c.e_layers; ++i) {
         const EncLayer& L = enc[i];
-        MSB_CUDA(launch_layernorm_rows(x, T, ed, L.ln_in, 1.0f, 1e-5f, nullptr, 0, ws.h.as<float>(), stream));
+        MSB_CUDA(launch_layernorm_rows(x, T, ed, L.ln_in, 1.0f, 1e-5f, nullptr, 0, h, s));
         GemmEpilogue e1;
-        e1.out = ws.qkv.as<float>();
+        e1.out = qkv;
         e1.ldc = QKV;
-        MSB_CUDA(launch_gemm_f32(ws.h.as<float>(), ed, L.wqkv, ed, T, QKV, ed, e1, stream));
+        MSB_CUDA(launch_gemm_f32(h, ed, L.wqkv, ed, T, QKV, ed, e1, s));
         auto w = c.window(i);
-        MSB_CUDA(launch_window_attention(ws.qkv.as<float>(), T, c.e_heads, c.e_kv_heads, hd, w.first,
-                                         w.second, scale, ws.attn.as<float>(), stream));
+        MSB_CUDA(launch_window_attention(qkv, T, c.e_heads, c.e_kv_heads, hd, w.first, w.second, scale, attn, s));
         GemmEpilogue e2;
         e2.out = x;
         e2.ldc = ed;
         e2.residual = x;
         e2.ldr = ed;
-        MSB_CUDA(launch_gemm_f32(ws.attn.as<float>(), eHD, L.wo, eHD, T, ed, eHD, e2, stream));
-        MSB_CUDA(launch_layernorm_rows(x, T, ed, L.ln_post, 1.0f, 1e-5f, nullptr, 0, ws.h.as<float>(), stream));
+        MSB_CUDA(launch_gemm_f32(attn, eHD, L.wo, eHD, T, ed, eHD, e2, s));
+        MSB_CUDA(launch_layernorm_rows(x, T, ed, L.ln_post, 1.0f, 1e-5f, nullptr, 0, h, s));
         GemmEpilogue e3;
-        e3.out = ws.f.as<float>();
+        e3.out = f;
         e3.ldc = c.e_inter;
         e3.bias = L.b1;
         e3.act = ACT_GELU;
-        MSB_CUDA(launch_gemm_f32(ws.h.as<float>(), ed, L.w1, ed, T, c.e_inter, ed, e3, stream));
+        MSB_CUDA(launch_gemm_f32(h, ed, L.w1, ed, T, c.e_inter, ed, e3, s));
         GemmEpilogue e4;
         e4.out = x;
         e4.ldc = ed;
         e4.bias = L.b2;
         e4.residual = x;
         e4.ldr = ed;
-        MSB_CUDA(launch_gemm_f32(ws.f.as<float>(), c.e_inter, L.w2, c.e_inter, T, ed, c.e_inter, e4, stream));
+        MSB_CUDA(launch_gemm_f32(f, c.e_inter, L.w2, c.e_inter, T, ed, c.e_inter, e4, s));
     }
 }
 
-int Model::encode_device(const float* audio_dev, int64_t n_samples, int pos_offset) {
+void Model::reserve_encoder(const EncBufs& b, int64_t max_samples) {
+    const Config& c = cfg;
+    const int ed = c.e_hidden;
+    const int T1 = (int)(max_samples / c.frame_len());
+    if (T1 <= 0) return;
+    const int T2 = (T1 - 1) / 2 + 1, T3 = (T2 - 1) / 2 + 1;
+    const int QKV = (c.e_heads + 2 * c.e_kv_heads) * c.e_head_dim;
+    b.feat1p->ensure((size_t)(4 + T1) * ed * 4);
+    b.feat2p->ensure((size_t)(4 + T2) * 2 * ed * 4);
+    b.x->ensure((size_t)T3 * ed * 4);
+    b.memory->ensure((size_t)T3 * ed * 4);
+    b.h->ensure((size_t)T3 * ed * 4);
+    b.qkv->ensure((size_t)T3 * QKV * 4);
+    b.attn->ensure((size_t)T3 * c.e_heads * c.e_head_dim * 4);
+    b.f->ensure((size_t)T3 * c.e_inter * 4);
+    if (proj) b.memproj->ensure((size_t)T3 * c.hidden * 4);
+}
+
+int Model::encode_into(const EncBufs& b, const float* audio_dev, int64_t n_samples, int pos_offset,
+                       cudaStream_t s) {
     const Config& c = cfg;
     const int fl = c.frame_len(), ed = c.e_hidden;
     const int T1 = (int)(n_samples / fl);
@@ -526,36 +557,36 @@ int Model::encode_device(const float* audio_dev, int64_t n_samples, int pos_offs
     if (pos_offset + T3 > c.max_pos)
         throw MsError(MS_ERR_INVALID_ARG, "audio longer than the positional table (" +
                                               std::to_string(c.max_pos) + " frames)");
-    ws.feat1p.ensure((size_t)(4 + T1) * ed * 4);
-    ws.feat2p.ensure((size_t)(4 + T2) * 2 * ed * 4);
-    ws.x.ensure((size_t)T3 * ed * 4);
-    ws.memory.ensure((size_t)T3 * ed * 4);
-    float* f1 = ws.feat1p.as<float>();
-    float* f2 = ws.feat2p.as<float>();
-    MSB_CUDA(cudaMemsetAsync(f1, 0, (size_t)4 * ed * 4, stream));
-    MSB_CUDA(cudaMemsetAsync(f2, 0, (size_t)4 * 2 * ed * 4, stream));
-    MSB_CUDA(launch_frame_features(audio_dev, T1, fl, log_k, lin_w, ed, f1 + 4 * ed, ed, stream));
+    b.feat1p->ensure((size_t)(4 + T1) * ed * 4);
+    b.feat2p->ensure((size_t)(4 + T2) * 2 * ed * 4);
+    b.x->ensure((size_t)T3 * ed * 4);
+    b.memory->ensure((size_t)T3 * ed * 4);
+    float* f1 = b.feat1p->as<float>();
+    float* f2 = b.feat2p->as<float>();
+    float* x = b.x->as<float>();
+    MSB_CUDA(cudaMemsetAsync(f1, 0, (size_t)4 * ed * 4, s));
+    MSB_CUDA(cudaMemsetAsync(f2, 0, (size_t)4 * 2 * ed * 4, s));
+    MSB_CUDA(launch_frame_features(audio_dev, T1, fl, log_k, lin_w, ed, f1 + 4 * ed, ed, s));
     // causal conv1 (k5 s2, left pad 4) as a GEMM over strided rows of the padded buffer
     GemmEpilogue c1;
     c1.bias = conv1_b;
     c1.act = ACT_SILU;
     c1.out = f2 + 4 * 2 * ed;
     c1.ldc = 2 * ed;
-    MSB_CUDA(launch_gemm_f32(f1, 2 * ed, conv1_w, 5 * ed, T2, 2 * ed, 5 * ed, c1, stream));
+    MSB_CUDA(launch_gemm_f32(f1, 2 * ed, conv1_w, 5 * ed, T2, 2 * ed, 5 * ed, c1, s));
     GemmEpilogue c2;
     c2.bias = conv2_b;
-    c2.out = ws.x.as<float>();
+    c2.out = x;
     c2.ldc = ed;
-    MSB_CUDA(launch_gemm_f32(f2, 4 * ed, conv2_w, 10 * ed, T3, ed, 10 * ed, c2, stream));
-    encoder_layers(ws.x.as<float>(), T3);
-    MSB_CUDA(launch_layernorm_rows(ws.x.as<float>(), T3, ed, enc_final, 1.0f, 1e-5f, pos_emb, pos_offset,
-                                   ws.memory.as<float>(), stream));
+    MSB_CUDA(launch_gemm_f32(f2, 4 * ed, conv2_w, 10 * ed, T3, ed, 10 * ed, c2, s));
+    encoder_layers_on(b, x, T3, s);
+    MSB_CUDA(launch_layernorm_rows(x, T3, ed, enc_final, 1.0f, 1e-5f, pos_emb, pos_offset, b.memory->as<float>(), s));
     if (proj) {
-        ws.memproj.ensure((size_t)T3 * c.hidden * 4);
+        b.memproj->ensure((size_t)T3 * c.hidden * 4);
         GemmEpilogue e;
-        e.out = ws.memproj.as<float>();
+        e.out = b.memproj->as<float>();
         e.ldc = c.hidden;
-        MSB_CUDA(launch_gemm_f32(ws.memory.as<float>(), ed, proj, ed, T3, c.hidden, ed, e, stream));
+        MSB_CUDA(launch_gemm_f32(b.memory->as<float>(), ed, proj, ed, T3, c.hidden, ed, e, s));
     }
     return T3;
 }

@@ -68,6 +68,12 @@ struct EncLayer {
     float *wqkv, *wo, *w1, *b1, *w2, *b2, *ln_in, *ln_post;
 };
 
+// Encoder scratch of one utterance (the model's own set lives in Workspace; the batched
+// engine keeps extra sets to encode several utterances concurrently).
+struct EncBufs {
+    DevBuf *feat1p, *feat2p, *x, *h, *qkv, *attn, *f, *memory, *memproj;
+};
+
 // Per-call device workspace for one utterance chunk (batch 1).
 struct Workspace {
     DevBuf audio, feat1p, feat2p, x, h, qkv, attn, f, memory, memproj;
@@ -122,6 +128,13 @@ struct Model {
     const float* memory_ptr() const;
     // Encoder over already computed features [T, e_hidden] (streaming windows).
     void encoder_layers(float* x, int T);
+    // The same on explicit scratch buffers and stream (concurrent encodes).
+    EncBufs own_enc_bufs();
+    int encode_into(const EncBufs& b, const float* audio_dev, int64_t n_samples, int pos_offset, cudaStream_t s);
+    const float* memory_of(const EncBufs& b) const;
+    void encoder_layers_on(const EncBufs& b, float* x, int T, cudaStream_t s);
+    // Grow `b` once for utterances of up to max_samples (no reallocation while encoding).
+    void reserve_encoder(const EncBufs& b, int64_t max_samples);
     // Cross K/V of `frames` memory rows into the decode cache at row offset `row0`.
     void cross_kv(const float* memory, int frames, int row0);
     // Decode scratch for `m_frames` memory rows and `t_cap` decoder calls.
