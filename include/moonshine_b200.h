@@ -197,10 +197,14 @@ ms_status ms_decode_memory_static(ms_model* model, const float* memory_dev, int3
 
 /* ------------------------------------------------------------------- streaming */
 
-/* StreamingConfig (MoonshineStreaming.swift:47-62). */
+/* StreamingConfig (MoonshineStreaming.swift:47-62), plus one field of this build. */
 typedef struct {
     int32_t max_memory_frames;   /* default 100000 */
     int32_t min_segment_frames;  /* default 250 */
+    int32_t batch_decode;        /* ms_stream_transcribe_batch only (default 0): 1 decodes all
+                                    streams of one model in lockstep on bf16 tensor cores;
+                                    ids then match a per-stream decode except where the top
+                                    two logits are closer than bf16 precision */
 } ms_streaming_config;
 
 void ms_streaming_config_default(ms_streaming_config* c);
@@ -228,10 +232,11 @@ ms_status ms_stream_emitted(ms_stream* stream, int32_t* ids_out, int32_t cap,
 /* Frames currently in the segment's memory (StreamingState.memoryLen, :26-27). */
 int32_t ms_stream_memory_len(const ms_stream* stream);
 
-/* transcribe over many streams at once: one batched encoder/decoder pass per call for
- * all n streams (no counterpart in the reference; each stream's result equals a
- * ms_stream_transcribe call on it alone).  ids_out is [n * cap], n_out/hit_eos/emitted
- * are [n] (hit_eos and emitted nullable). */
+/* transcribe over many streams at once (no counterpart in the reference).  Each stream's
+ * new frames are encoded on its own; with config->batch_decode == 0 each stream is then
+ * decoded on its own (results equal ms_stream_transcribe on it alone), with 1 the
+ * decodes of all streams that share one model run in lockstep (see batch_decode).
+ * ids_out is [n * cap], n_out/hit_eos/emitted are [n] (hit_eos and emitted nullable). */
 ms_status ms_stream_transcribe_batch(ms_stream* const* streams, int32_t n, int32_t is_final,
                                      const ms_streaming_config* config, int32_t max_tokens,
                                      int32_t* ids_out, int32_t cap, int32_t* n_out,

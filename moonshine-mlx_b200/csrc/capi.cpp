@@ -139,6 +139,7 @@ void ms_streaming_config_default(ms_streaming_config* c) {
     if (!c) return;
     c->max_memory_frames = 100000;
     c->min_segment_frames = 250;
+    c->batch_decode = 0;
 }
 
 const char* ms_last_error(void) { return g_err.c_str(); }
@@ -527,9 +528,55 @@ ms_status ms_stream_transcribe_batch(ms_stream* const* streams, int32_t n, int32
         if (config) sc = *config;
         const int32_t mt = max_tokens > 0 ? max_tokens : std::numeric_limits<int32_t>::max();
         ms_status worst = MS_OK;
+        for (int32_t i = 0; i < n; ++i)
+            if (!streams[i]) return fail(MS_ERR_INVALID_ARG, "null stream in batch");
+        Model* shared = n > 0 ? reinterpret_cast<StreamState*>(streams[0])->model : nullptr;
+        for (int32_t i = 1; i < n && shared; ++i)
+            if (reinterpret_cast<StreamState*>(streams[i])->model != shared) shared = nullptr;
+        if (sc.batch_decode && shared) {
+            // encode each stream's new frames, decode every segment with memory in lockstep
+            std::lock_guard<std::mutex> g(shared->mu);
+            MSB_CUDA(cudaSetDevice(shared->device));
+            std::vector<StreamState::Result> res(n);
+            std::vector<int64_t> lim(n);
+            std::vector<BatchEngine::CrossSrc> src;
+            std::vector<int> limits, rows;
+            const int lanes = std::min<int32_t>(n, 8);  // concurrent incremental encoders
+            shared->fork_lanes(lanes);
+            for (int32_t i = 0; i < n; ++i) {
+                StreamState* s = reinterpret_cast<StreamState*>(streams[i]);
+                lim[i] = s->begin(is_final != 0, mt, &res[i], &shared->enc_lane(i % lanes));
+                if (lim[i] > 0) {
+                    src.push_back({s->cross32.as<float>(), s->cross16.p, s->mem_cap, s->memory_len});
+                    limits.push_back((int)lim[i]);
+                    rows.push_back(i);
+                }
+            }
+            shared->join_lanes(lanes);
+            if (!src.empty()) {
+                if (!shared->batch) shared->batch.reset(new BatchEngine(*shared));
+                BatchEngine::Result r = shared->batch->run_cross(src, limits, false);
+                for (size_t k = 0; k < rows.size(); ++k) {
+                    const int32_t i = rows[k];
+                    std::vector<int32_t> ids(r.ids.begin() + (size_t)k * r.t_cap,
+                                             r.ids.begin() + (size_t)k * r.t_cap + r.counts[k]);
+                    res[i] = reinterpret_cast<StreamState*>(streams[i])->finish(std::move(ids), r.hit_eos[k] != 0,
+                                                                                  is_final != 0, sc);
+                }
+            }
+            for (int32_t i = 0; i < n; ++i) {
+                const int32_t cnt = (int32_t)res[i].ids.size();
+                n_out[i] = cnt;
+                for (int32_t j = 0; j < std::min(cnt, cap); ++j) ids_out[(size_t)i * cap + j] = res[i].ids[j];
+                if (hit_eos) hit_eos[i] = res[i].hit_eos ? 1 : 0;
+                if (emitted) emitted[i] = res[i].emitted ? 1 : 0;
+                if (cnt > cap) worst = MS_ERR_CAPACITY;
+            }
+            if (worst != MS_OK) return fail(worst, "ids buffer too small");
+            return MS_OK;
+        }
         for (int32_t i = 0; i < n; ++i) {
             StreamState* s = reinterpret_cast<StreamState*>(streams[i]);
-            if (!s) return fail(MS_ERR_INVALID_ARG, "null stream in batch");
             std::lock_guard<std::mutex> g(s->model->mu);
             MSB_CUDA(cudaSetDevice(s->model->device));
             ms_status st = transcribe_one(s, is_final, sc, mt, ids_out + (size_t)i * cap, cap, n_out + i,

@@ -492,6 +492,40 @@ cudaError_t launch_step_finalize(unsigned long long* amax, int B, int* pos, int*
 }
 
 namespace {
+// Block (segment s, row b): copy row b's M[b] frames of segment s of its own cross K/V
+// ([segs][mcap[b]][hd], fp32 and optional fp16 copy) to frames off[b].. of segment s of
+// the concatenated layout [segs][m_cap][hd].  Rows of hd elements are whole 16-byte units.
+__global__ void gather_cross_kernel(const float* const* __restrict__ src32, const __half* const* __restrict__ src16,
+                                    const int* __restrict__ mcap, const int* __restrict__ frames,
+                                    const int* __restrict__ off, int hd, int m_cap, float* __restrict__ dst32,
+                                    __half* __restrict__ dst16) {
+    const int seg = blockIdx.x, b = blockIdx.y;
+    const size_t n = (size_t)frames[b] * hd;
+    const size_t so = (size_t)seg * mcap[b] * hd, dof = ((size_t)seg * m_cap + off[b]) * hd;
+    const uint4* s32 = reinterpret_cast<const uint4*>(src32[b] + so);
+    uint4* d32 = reinterpret_cast<uint4*>(dst32 + dof);
+    for (size_t i = threadIdx.x; i < n / 4; i += blockDim.x) d32[i] = s32[i];
+    if (dst16 && src16[b]) {
+        const uint4* s16 = reinterpret_cast<const uint4*>(src16[b] + so);
+        uint4* d16 = reinterpret_cast<uint4*>(dst16 + dof);
+        for (size_t i = threadIdx.x; i < n / 8; i += blockDim.x) d16[i] = s16[i];
+    }
+}
+}  // namespace
+
+cudaError_t launch_gather_cross(const float* const* src32, const void* const* src16, const int* mcap,
+                                const int* frames, const int* off, int B, int segs, int hd, int m_cap, float* dst32,
+                                void* dst16, cudaStream_t s) {
+    if (B <= 0 || segs <= 0) return cudaSuccess;
+    if (hd & 7) return cudaErrorInvalidValue;
+    ++launch_counter();
+    gather_cross_kernel<<<dim3(segs, B), 256, 0, s>>>(src32, reinterpret_cast<const __half* const*>(src16), mcap,
+                                                       frames, off, hd, m_cap, dst32,
+                                                       reinterpret_cast<__half*>(dst16));
+    return cudaGetLastError();
+}
+
+namespace {
 // dst row r = src row r (interleave == 0) or, for the SwiGLU fc1, dst row 2j = src row j
 // (value) and dst row 2j+1 = src row j + interleave (gate).
 __global__ void f32_to_bf16_rows_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, int rows,

@@ -187,6 +187,11 @@ cudaError_t launch_f32_to_bf16_rows(const float* src, __nv_bfloat16* dst, int ro
                                     cudaStream_t s);
 cudaError_t launch_interleave_f32(const float* src, float* dst, int n2, int half, cudaStream_t s);
 size_t cross_batch_part_floats(int B, int H, int hd, int max_frames);
+// Per-row cross K/V ([segs][mcap[b]][hd] at src32[b] / src16[b], device pointer arrays) into
+// the concatenated layout [segs][m_cap][hd] at frame offset off[b]; src16 entries may be null.
+cudaError_t launch_gather_cross(const float* const* src32, const void* const* src16, const int* mcap,
+                                const int* frames, const int* off, int B, int segs, int hd, int m_cap, float* dst32,
+                                void* dst16, cudaStream_t s);
 
 // Head-clustered batch-1 decode (one 8-CTA cluster per head, packed per-CTA weight streams).
 struct ClusterGeom {

@@ -26,11 +26,6 @@ void make_a_map(CUtensorMap* map, const __nv_bfloat16* a, int rows, int K) {
 
 BatchEngine::~BatchEngine() {
     for (auto* b : own) delete b;
-    for (auto& l : lanes) {
-        if (l->stream) cudaStreamDestroy(l->stream);
-        if (l->done) cudaEventDestroy(l->done);
-    }
-    if (ev_start) cudaEventDestroy(ev_start);
 }
 
 // Encode every utterance into memory rows [off[b], off[b] + frames) of the batch memory.
@@ -40,30 +35,19 @@ void BatchEngine::encode_all(const std::vector<const float*>& audio_dev, const s
     constexpr int kLanes = 8;
     const int B = (int)audio_dev.size();
     const int K = std::min(B, kLanes);
-    if (!ev_start) MSB_CUDA(cudaEventCreateWithFlags(&ev_start, cudaEventDisableTiming));
-    while ((int)lanes.size() < K) {
-        auto l = std::make_unique<EncLane>();
-        MSB_CUDA(cudaStreamCreateWithFlags(&l->stream, cudaStreamNonBlocking));
-        MSB_CUDA(cudaEventCreateWithFlags(&l->done, cudaEventDisableTiming));
-        lanes.push_back(std::move(l));
-    }
     const int64_t longest = *std::max_element(n_samples.begin(), n_samples.end());
-    for (int k = 0; k < K; ++k) m.reserve_encoder(lanes[k]->bufs(), longest);  // before any lane runs
-    MSB_CUDA(cudaEventRecord(ev_start, m.stream));
-    for (int k = 0; k < K; ++k) MSB_CUDA(cudaStreamWaitEvent(lanes[k]->stream, ev_start, 0));
+    for (int k = 0; k < K; ++k) m.reserve_encoder(m.enc_lane(k).bufs(), longest);  // before any lane runs
+    m.fork_lanes(K);
     const int hidden = m.cfg.hidden;
     for (int b = 0; b < B; ++b) {
-        EncLane& l = *lanes[b % K];
+        EncLane& l = m.enc_lane(b % K);
         const EncBufs eb = l.bufs();
         const int M = m.encode_into(eb, audio_dev[b], n_samples[b], 0, l.stream);
         if (M <= 0) throw MsError(MS_ERR_CUDA, "frame count mismatch");
         MSB_CUDA(cudaMemcpyAsync(memory.as<float>() + (size_t)off[b] * hidden, m.memory_of(eb),
                                  (size_t)M * hidden * 4, cudaMemcpyDeviceToDevice, l.stream));
     }
-    for (int k = 0; k < K; ++k) {
-        MSB_CUDA(cudaEventRecord(lanes[k]->done, lanes[k]->stream));
-        MSB_CUDA(cudaStreamWaitEvent(m.stream, lanes[k]->done, 0));
-    }
+    m.join_lanes(K);
 }
 
 template <class T>
@@ -312,6 +296,55 @@ BatchEngine::Result BatchEngine::run(const std::vector<const float*>& audio_dev,
     encode_all(audio_dev, n_samples, off);
     m.cross_kv_into(memory.as<float>(), Mtot, 0, cross32.as<float>(), m.kv_f16 ? cross16.p : nullptr, Mc);
     MSB_CUDA(cudaEventRecord(m.ev[1], s));
+    return decode_prepared(B, T, maxM, off, fr, limits, forced, want_logits);
+}
+
+BatchEngine::Result BatchEngine::run_cross(const std::vector<CrossSrc>& src, const std::vector<int>& limits,
+                                           bool forced) {
+    const Config& c = m.cfg;
+    const int B = (int)src.size();
+    cudaStream_t s = m.stream;
+    ensure_weights();
+    MSB_CUDA(cudaEventRecord(m.ev[0], s));
+    std::vector<int> off(B), fr(B), mcap(B);
+    int Mtot = 0, maxM = 0;
+    for (int b = 0; b < B; ++b) {
+        fr[b] = src[b].frames;
+        mcap[b] = src[b].m_cap;
+        if (fr[b] <= 0 || fr[b] > mcap[b]) throw MsError(MS_ERR_INVALID_ARG, "a stream has no memory to decode");
+        off[b] = Mtot;
+        Mtot += fr[b];
+        maxM = std::max(maxM, fr[b]);
+    }
+    const int T = *std::max_element(limits.begin(), limits.end());
+    ensure_ws(B, T, Mtot, maxM);
+    // pointer tables: src32[B], src16[B], then mcap[B]
+    std::vector<const void*> ptrs(2 * (size_t)B);
+    for (int b = 0; b < B; ++b) {
+        ptrs[b] = src[b].c32;
+        ptrs[B + b] = m.kv_f16 ? src[b].c16 : nullptr;
+    }
+    xsrc.ensure((size_t)2 * B * sizeof(void*) + (size_t)B * 4);
+    char* tab = reinterpret_cast<char*>(xsrc.p);
+    MSB_CUDA(cudaMemcpyAsync(tab, ptrs.data(), ptrs.size() * sizeof(void*), cudaMemcpyHostToDevice, s));
+    MSB_CUDA(cudaMemcpyAsync(tab + 2 * B * sizeof(void*), mcap.data(), (size_t)B * 4, cudaMemcpyHostToDevice, s));
+    MSB_CUDA(cudaMemcpyAsync(frame_off.p, off.data(), (size_t)B * 4, cudaMemcpyHostToDevice, s));
+    MSB_CUDA(cudaMemcpyAsync(frames.p, fr.data(), (size_t)B * 4, cudaMemcpyHostToDevice, s));
+    MSB_CUDA(launch_gather_cross(reinterpret_cast<const float* const*>(tab),
+                                 reinterpret_cast<const void* const*>(tab + B * sizeof(void*)),
+                                 reinterpret_cast<const int*>(tab + 2 * B * sizeof(void*)), frames.as<int>(),
+                                 frame_off.as<int>(), B, c.layers * 2 * c.kv_heads, c.head_dim, Mc,
+                                 cross32.as<float>(), m.kv_f16 ? cross16.p : nullptr, s));
+    MSB_CUDA(cudaEventRecord(m.ev[1], s));
+    return decode_prepared(B, T, maxM, off, fr, limits, forced, false);
+}
+
+BatchEngine::Result BatchEngine::decode_prepared(int B, int T, int maxM, const std::vector<int>& off,
+                                                 const std::vector<int>& fr, const std::vector<int>& limits,
+                                                 bool forced, bool want_logits) {
+    const Config& c = m.cfg;
+    cudaStream_t s = m.stream;
+    Result res;
     // step state
     std::vector<int> bos(B, c.dec_start);
     MSB_CUDA(cudaMemcpyAsync(next_ids.p, bos.data(), (size_t)B * 4, cudaMemcpyHostToDevice, s));
@@ -366,7 +399,7 @@ BatchEngine::Result BatchEngine::run(const std::vector<const float*>& audio_dev,
         MSB_CUDA(cudaMemcpyAsync(res.logits.data(), logit_buf.p, res.logits.size() * 4, cudaMemcpyDeviceToHost, s));
     }
     MSB_CUDA(cudaStreamSynchronize(s));
-    if (st_word == 5) throw MsError(MS_ERR_TIMEOUT, "batched decode: a GEMM pipeline wait timed out");
+    if (st_word == DEV_WAIT_TIMEOUT) throw MsError(MS_ERR_TIMEOUT, "batched decode: a pipeline wait timed out");
     if (st_word == DEV_BAD_TOKEN) throw MsError(MS_ERR_INVALID_ARG, "batched decode: token id out of range");
     if (st_word != 0) throw MsError(MS_ERR_CUDA, "batched decode: device status " + std::to_string(st_word));
     float te = 0, td = 0;

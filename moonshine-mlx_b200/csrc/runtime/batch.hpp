@@ -27,6 +27,15 @@ struct BatchEngine {
     Result run(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
                const std::vector<int>& limits, bool forced, bool want_logits);
 
+    // Decode rows whose cross K/V already exist (streaming segments): row b's layout is
+    // [L][2][KVH][m_cap][hd] with `frames` valid rows, fp32 plus the fp16 copy.
+    struct CrossSrc {
+        const float* c32;
+        const void* c16;
+        int m_cap, frames;
+    };
+    Result run_cross(const std::vector<CrossSrc>& src, const std::vector<int>& limits, bool forced);
+
    private:
     struct LayerB {
         __nv_bfloat16 *wqkv, *wo, *wcq, *wco, *w1i, *w2;
@@ -44,21 +53,15 @@ struct BatchEngine {
         pos, frame_off, frames, cross32, cross16, memory, status;
     CUtensorMap a_hb, a_attn, a_g;
 
-    // Concurrent encoder lanes: each has its own scratch buffers and stream, so independent
-    // utterances' (latency-bound) encoders overlap on the GPU.
-    struct EncLane {
-        DevBuf feat1p, feat2p, x, h, qkv, attn, f, memory, memproj;
-        cudaStream_t stream = nullptr;
-        cudaEvent_t done = nullptr;
-        EncBufs bufs() { return {&feat1p, &feat2p, &x, &h, &qkv, &attn, &f, &memory, &memproj}; }
-    };
-    std::vector<std::unique_ptr<EncLane>> lanes;
-    cudaEvent_t ev_start = nullptr;
+    // Utterances are encoded concurrently on the model's encoder lanes.
     void encode_all(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
                     const std::vector<int>& off);
 
     template <class T> T* alloc(size_t n);
     void ensure_weights();
+    Result decode_prepared(int B, int T, int maxM, const std::vector<int>& off, const std::vector<int>& fr,
+                           const std::vector<int>& limits, bool forced, bool want_logits);
+    DevBuf xsrc;  // device pointer tables of run_cross
     void ensure_ws(int B, int T, int Mtot, int maxM);
     void enqueue_step(int B, int max_frames, bool forced, bool first, float* logits);
     void gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& g, int K, int bn);

@@ -323,6 +323,8 @@ void append(std::vector<float>& dst, const std::vector<float>& src) {
 // ------------------------------------------------------------------ model
 
 Model::~Model() {
+    enc_lanes.clear();
+    if (lanes_fork) cudaEventDestroy(lanes_fork);
     if (stream) {
         cudaSetDevice(device);
         cudaStreamSynchronize(stream);
@@ -633,7 +635,37 @@ void Model::cross_kv(const float* memory, int frames, int row0) {
     cross_kv_into(memory, frames, row0, ws.cross32.as<float>(), kv_f16 ? ws.cross16.p : nullptr, ws.m_cap);
 }
 
-void Model::cross_kv_into(const float* memory, int frames, int row0, float* out32, void* out16, int m_cap) {
+EncLane::~EncLane() {
+    if (stream) cudaStreamDestroy(stream);
+    if (done) cudaEventDestroy(done);
+}
+
+EncLane& Model::enc_lane(int k) {
+    while ((int)enc_lanes.size() <= k) {
+        auto l = std::make_unique<EncLane>();
+        MSB_CUDA(cudaStreamCreateWithFlags(&l->stream, cudaStreamNonBlocking));
+        MSB_CUDA(cudaEventCreateWithFlags(&l->done, cudaEventDisableTiming));
+        enc_lanes.push_back(std::move(l));
+    }
+    return *enc_lanes[k];
+}
+
+void Model::fork_lanes(int k) {
+    if (!lanes_fork) MSB_CUDA(cudaEventCreateWithFlags(&lanes_fork, cudaEventDisableTiming));
+    MSB_CUDA(cudaEventRecord(lanes_fork, stream));
+    for (int i = 0; i < k; ++i) MSB_CUDA(cudaStreamWaitEvent(enc_lane(i).stream, lanes_fork, 0));
+}
+
+void Model::join_lanes(int k) {
+    for (int i = 0; i < k; ++i) {
+        EncLane& l = enc_lane(i);
+        MSB_CUDA(cudaEventRecord(l.done, l.stream));
+        MSB_CUDA(cudaStreamWaitEvent(stream, l.done, 0));
+    }
+}
+
+void Model::cross_kv_into(const float* memory, int frames, int row0, float* out32, void* out16, int m_cap,
+                          cudaStream_t s) {
     if (frames <= 0) return;
     const Config& c = cfg;
     GemmEpilogue e;
@@ -645,7 +677,7 @@ void Model::cross_kv_into(const float* memory, int frames, int row0, float* out3
     e.frame_cap = m_cap;
     e.frame_offset = row0;
     const int N = c.layers * 2 * c.kv_heads * c.head_dim;
-    MSB_CUDA(launch_gemm_f32(memory, c.hidden, cross_w, c.hidden, frames, N, c.hidden, e, stream));
+    MSB_CUDA(launch_gemm_f32(memory, c.hidden, cross_w, c.hidden, frames, N, c.hidden, e, s ? s : stream));
 }
 
 bool Model::prepare_cluster_decode() {

@@ -74,6 +74,15 @@ struct EncBufs {
     DevBuf *feat1p, *feat2p, *x, *h, *qkv, *attn, *f, *memory, *memproj;
 };
 
+// A concurrent encoder lane: its own scratch set and CUDA stream.
+struct EncLane {
+    DevBuf feat1p, feat2p, x, h, qkv, attn, f, memory, memproj;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t done = nullptr;
+    EncBufs bufs() { return {&feat1p, &feat2p, &x, &h, &qkv, &attn, &f, &memory, &memproj}; }
+    ~EncLane();
+};
+
 // Per-call device workspace for one utterance chunk (batch 1).
 struct Workspace {
     DevBuf audio, feat1p, feat2p, x, h, qkv, attn, f, memory, memproj;
@@ -150,7 +159,15 @@ struct Model {
     DecodeResult decode(const float* cross32, const void* cross_stored, int m_cap, int M, int n_steps,
                         bool forced, const int* teacher_dev, bool logits);
     // Cross K/V of `frames` memory rows into explicit buffers at row offset `row0`.
-    void cross_kv_into(const float* memory, int frames, int row0, float* out32, void* out16, int m_cap);
+    void cross_kv_into(const float* memory, int frames, int row0, float* out32, void* out16, int m_cap,
+                       cudaStream_t s = nullptr);
+    // Encoder lanes 0..k-1 (created on first use); `fork` makes them wait for the work
+    // queued so far on the model stream, `join` makes the model stream wait for them.
+    std::vector<std::unique_ptr<EncLane>> enc_lanes;
+    cudaEvent_t lanes_fork = nullptr;
+    EncLane& enc_lane(int k);
+    void fork_lanes(int k);
+    void join_lanes(int k);
 };
 
 ms_status to_status(const std::exception& e);

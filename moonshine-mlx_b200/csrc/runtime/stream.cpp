@@ -106,23 +106,25 @@ void StreamState::add_audio(const float* chunk, int64_t n) {  // MoonshineStream
     feat_count += T3;
 }
 
-void StreamState::ensure_memory(int rows) {
+void StreamState::ensure_memory(int rows, cudaStream_t s) {
     Model& m = *model;
     const Config& c = m.cfg;
     if (rows <= mem_cap) return;
     const int cap = std::max(rows, std::max(2 * mem_cap, 256));
-    grow_keep(memory, (size_t)memory_len * c.hidden * 4, (size_t)cap * c.hidden * 4, m.stream);
+    grow_keep(memory, (size_t)memory_len * c.hidden * 4, (size_t)cap * c.hidden * 4, s);
     const size_t n = (size_t)c.layers * 2 * c.kv_heads * cap * c.head_dim;
     cross32.ensure(n * 4);
     cross16.ensure(n * 2);
     mem_cap = cap;
     // the K/V layout depends on the capacity: rebuild it for the rows kept
-    m.cross_kv_into(memory.as<float>(), memory_len, 0, cross32.as<float>(), cross16.p, mem_cap);
+    m.cross_kv_into(memory.as<float>(), memory_len, 0, cross32.as<float>(), cross16.p, mem_cap, s);
 }
 
-void StreamState::encode_new_frames(bool is_final) {  // MoonshineStreaming.swift:178-214
+void StreamState::encode_new_frames(bool is_final, EncLane* lane) {  // MoonshineStreaming.swift:178-214
     Model& m = *model;
     const Config& c = m.cfg;
+    const EncBufs eb = lane ? lane->bufs() : m.own_enc_bufs();
+    const cudaStream_t s = lane ? lane->stream : m.stream;
     if (feat_count <= 0) return;
     const int total = feat_count;
     int look = 0;
@@ -137,26 +139,27 @@ void StreamState::encode_new_frames(bool is_final) {  // MoonshineStreaming.swif
     const int win_start = std::max(0, encoder_frames_emitted - left_ctx);
     const int T = total - win_start;
     const int ed = c.e_hidden;
-    m.ws.x.ensure((size_t)T * ed * 4);
-    MSB_CUDA(cudaMemcpyAsync(m.ws.x.p, features.as<float>() + (size_t)win_start * ed, (size_t)T * ed * 4,
-                             cudaMemcpyDeviceToDevice, m.stream));
-    m.encoder_layers(m.ws.x.as<float>(), T);
+    eb.x->ensure((size_t)T * ed * 4);
+    float* x = eb.x->as<float>();
+    MSB_CUDA(cudaMemcpyAsync(x, features.as<float>() + (size_t)win_start * ed, (size_t)T * ed * 4,
+                             cudaMemcpyDeviceToDevice, s));
+    m.encoder_layers_on(eb, x, T, s);
     const int off = encoder_frames_emitted - win_start;
-    ensure_memory(memory_len + nnew);
+    ensure_memory(memory_len + nnew, s);
     float* dst = memory.as<float>() + (size_t)memory_len * c.hidden;
     if (m.proj) {
-        m.ws.memory.ensure((size_t)nnew * ed * 4);
-        MSB_CUDA(launch_layernorm_rows(m.ws.x.as<float>() + (size_t)off * ed, nnew, ed, m.enc_final, 1.0f, 1e-5f,
-                                       m.pos_emb, pos_offset, m.ws.memory.as<float>(), m.stream));
+        eb.memory->ensure((size_t)nnew * ed * 4);
+        MSB_CUDA(launch_layernorm_rows(x + (size_t)off * ed, nnew, ed, m.enc_final, 1.0f, 1e-5f, m.pos_emb,
+                                       pos_offset, eb.memory->as<float>(), s));
         GemmEpilogue e;
         e.out = dst;
         e.ldc = c.hidden;
-        MSB_CUDA(launch_gemm_f32(m.ws.memory.as<float>(), ed, m.proj, ed, nnew, c.hidden, ed, e, m.stream));
+        MSB_CUDA(launch_gemm_f32(eb.memory->as<float>(), ed, m.proj, ed, nnew, c.hidden, ed, e, s));
     } else {
-        MSB_CUDA(launch_layernorm_rows(m.ws.x.as<float>() + (size_t)off * ed, nnew, ed, m.enc_final, 1.0f, 1e-5f,
-                                       m.pos_emb, pos_offset, dst, m.stream));
+        MSB_CUDA(launch_layernorm_rows(x + (size_t)off * ed, nnew, ed, m.enc_final, 1.0f, 1e-5f, m.pos_emb,
+                                       pos_offset, dst, s));
     }
-    m.cross_kv_into(dst, nnew, memory_len, cross32.as<float>(), cross16.p, mem_cap);
+    m.cross_kv_into(dst, nnew, memory_len, cross32.as<float>(), cross16.p, mem_cap, s);
     pos_offset += nnew;
     encoder_frames_emitted = stable;
     memory_len += nnew;
@@ -183,18 +186,29 @@ std::pair<std::vector<int32_t>, bool> StreamState::decode_memory(int32_t max_tok
     return {ids, r.hit_eos};
 }
 
-StreamState::Result StreamState::transcribe(bool is_final, const ms_streaming_config& sc, int32_t max_tokens) {
-    // MoonshineStreaming.swift:122-168
-    Result res;
-    encode_new_frames(is_final);
+int64_t StreamState::begin(bool is_final, int32_t max_tokens, Result* done_early, EncLane* lane) {
+    // MoonshineStreaming.swift:122-131
+    encode_new_frames(is_final, lane);
     if (memory_len <= 0) {
         if (is_final) reset_segment();
-        MSB_CUDA(cudaStreamSynchronize(model->stream));
-        return res;
+        MSB_CUDA(cudaStreamSynchronize(lane ? lane->stream : model->stream));
+        *done_early = Result();
+        return 0;
     }
-    auto dm = decode_memory(max_tokens);
-    res.ids = dm.first;
-    res.hit_eos = dm.second;
+    // MoonshineStreaming.swift:234-236
+    const double dur = (double)memory_len * 0.020;
+    const int64_t limit = (int64_t)std::ceil(dur * model->cfg.max_tok_per_s);
+    const int64_t max_tok = std::min<int64_t>(max_tokens, limit);
+    if (max_tok <= 0) throw MsError(MS_ERR_INVALID_ARG, "token limit must be positive");
+    return max_tok;
+}
+
+StreamState::Result StreamState::finish(std::vector<int32_t> ids, bool hit_eos, bool is_final,
+                                        const ms_streaming_config& sc) {
+    // MoonshineStreaming.swift:133-168
+    Result res;
+    res.ids = std::move(ids);
+    res.hit_eos = hit_eos;
     last_hit_eos = res.hit_eos;
     if (res.hit_eos && memory_len >= sc.min_segment_frames) {
         emitted.push_back(res.ids);
@@ -203,19 +217,20 @@ StreamState::Result StreamState::transcribe(bool is_final, const ms_streaming_co
         res.emitted = true;
         return res;
     }
-    if (is_final) {
+    if (is_final || memory_len > sc.max_memory_frames) {
         emitted.push_back(res.ids);
         reset_segment();
         res.emitted = true;
-        return res;
-    }
-    if (memory_len > sc.max_memory_frames) {
-        emitted.push_back(res.ids);
-        reset_segment();
-        res.emitted = true;
-        return res;
     }
     return res;
+}
+
+StreamState::Result StreamState::transcribe(bool is_final, const ms_streaming_config& sc, int32_t max_tokens) {
+    Result early;
+    const int64_t max_tok = begin(is_final, max_tokens, &early);
+    if (max_tok <= 0) return early;
+    auto dm = decode_memory(max_tokens);
+    return finish(std::move(dm.first), dm.second, is_final, sc);
 }
 
 }  // namespace msb

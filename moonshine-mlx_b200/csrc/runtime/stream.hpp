@@ -38,11 +38,17 @@ struct StreamState {
         bool emitted = false;
     };
     Result transcribe(bool is_final, const ms_streaming_config& sc, int32_t max_tokens);
+    // transcribe in two halves around an external decode of the segment's memory:
+    // begin() encodes the new frames and returns the decode limit (0: nothing to decode,
+    // the call is already complete); finish() applies the segment rules to the ids.
+    // `lane` (nullable) runs the encoder on that lane's scratch and stream.
+    int64_t begin(bool is_final, int32_t max_tokens, Result* done_early, EncLane* lane = nullptr);
+    Result finish(std::vector<int32_t> ids, bool hit_eos, bool is_final, const ms_streaming_config& sc);
 
    private:
     void reset_segment();
-    void encode_new_frames(bool is_final);
-    void ensure_memory(int rows);
+    void encode_new_frames(bool is_final, EncLane* lane = nullptr);
+    void ensure_memory(int rows, cudaStream_t s);
     std::pair<std::vector<int32_t>, bool> decode_memory(int32_t max_tokens);
 };
 

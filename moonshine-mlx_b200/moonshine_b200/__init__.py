@@ -67,7 +67,8 @@ class _GenStats(C.Structure):
 
 
 class _StreamingConfig(C.Structure):
-    _fields_ = [("max_memory_frames", C.c_int32), ("min_segment_frames", C.c_int32)]
+    _fields_ = [("max_memory_frames", C.c_int32), ("min_segment_frames", C.c_int32),
+                ("batch_decode", C.c_int32)]
 
 
 class _ModelConfig(C.Structure):
@@ -184,9 +185,10 @@ class StreamingConfig:
     """StreamingConfig (MoonshineStreaming.swift:47-62)."""
     max_memory_frames: int = 100000
     min_segment_frames: int = 250
+    batch_decode: bool = False   # transcribe_batch: lockstep bf16 decode of all streams
 
     def _c(self) -> _StreamingConfig:
-        return _StreamingConfig(self.max_memory_frames, self.min_segment_frames)
+        return _StreamingConfig(self.max_memory_frames, self.min_segment_frames, 1 if self.batch_decode else 0)
 
 
 class StreamingState:

@@ -90,3 +90,49 @@ def test_stream_batch_equals_single(model_root):
         got = m.transcribe_batch(streams, max_tokens=16)
         want = [m.transcribe(s, max_tokens=16) for s in singles]
         assert got == want
+
+
+def test_stream_batch_decode_lockstep(model_root):
+    """transcribe_batch with batch_decode: 4 streams fed 80 ms chunks, every call's segment
+    decoded in lockstep on bf16 tensor cores.  Per call and stream the ids follow the
+    oracle's decodeMemory (MoonshineStreaming.swift:229-276) up to the first step whose
+    top-2 logit margin is within the bf16 tolerance; the memories stay equal throughout."""
+    import moonshine_b200 as mb
+    from oracle.moonshine_oracle import OracleStream, StreamingConfig
+    from util import BF16_LOGIT_TOL
+    d = model_dir(model_root, "tiny")
+    m = mb.MoonshineModel.load(d)
+    o = oracle_for(d)
+    n_streams, chunk, n_chunks, max_tokens = 4, 1280, 10, 16
+    audios = [synth.synth_audio(chunk * n_chunks, 70 + i) for i in range(n_streams)]
+    streams = [m.create_stream() for _ in range(n_streams)]
+    refs = [OracleStream(o, kv_fp16=True) for _ in range(n_streams)]
+    for s, r in zip(streams, refs):
+        m.start_stream(s)
+        r.start()
+    sc = mb.StreamingConfig(batch_decode=True)
+    checked = 0
+    for k in range(n_chunks):
+        for i in range(n_streams):
+            piece = audios[i][k * chunk:(k + 1) * chunk]
+            m.add_audio(streams[i], piece)
+            refs[i].add_audio(piece)
+        got = m.transcribe_batch(streams, streaming_config=sc, max_tokens=max_tokens)
+        for i in range(n_streams):
+            r = refs[i]
+            r._encode_new_frames(False)
+            assert streams[i].memory_len == r.memory_len
+            if r.memory_len == 0:
+                assert got[i] == ([], False, False)
+                continue
+            limit = min(max_tokens, int(np.ceil(r.memory_len * 0.020 * o.cfg.max_tokens_per_second)))
+            ref, hit, ref_logits, margins = o.greedy(r.memory, limit, True, keep_logits=True)
+            ids = got[i][0]
+            j = next((t for t, (x, y) in enumerate(zip(ids, ref)) if x != y), None)
+            if j is None:
+                assert ids == ref and got[i][1] == hit, f"stream {i} chunk {k}"
+            else:
+                scale = float(np.max(np.abs(ref_logits[j])))
+                assert margins[j] <= BF16_LOGIT_TOL * scale, f"stream {i} chunk {k}: ids part at step {j}"
+            checked += 1
+    assert checked >= n_streams * (n_chunks - 2)
