@@ -242,6 +242,19 @@ ms_status ms_stream_transcribe_batch(ms_stream* const* streams, int32_t n, int32
                                      int32_t* ids_out, int32_t cap, int32_t* n_out,
                                      int32_t* hit_eos, int32_t* emitted);
 
+/* generateLong(audio:streamingConfig:) (MoonshineStreaming.swift:287-376): the whole
+ * audio is encoded in one pass, then decoded in segments of at most max_memory_frames
+ * memory rows with EOS-driven advance (an early EOS in a segment longer than
+ * min_segment_frames moves the start by max(min_segment_frames, tokens / 6.5 * 50) frames).
+ * ids_out receives the ids of every segment that produced tokens, each followed by the
+ * separator -1 (the reference joins the non-empty segment texts).  stats->n_chunks is the
+ * number of segments; stats->tokens_per_second holds audio seconds per wall second, as
+ * the reference's generateLong reports it.  The audio's memory must fit the positional
+ * table (max_position_embeddings frames). */
+ms_status ms_generate_long(ms_model* model, const float* audio, int64_t n_samples,
+                           const ms_streaming_config* config, int32_t* ids_out, int32_t cap,
+                           int32_t* n_out, ms_gen_stats* stats);
+
 /* ------------------------------------------------------------------- diagnostics */
 
 /* Thread-local message of the last failing call on this thread ("" if none). */

@@ -254,6 +254,97 @@ ms_status ms_generate_device(ms_model* model, const float* audio_dev, int64_t n_
     return generate_impl(model, audio_dev, n_samples, params, ids_dev, cap, n_out, nullptr, stats, true);
 }
 
+ms_status ms_generate_long(ms_model* model, const float* audio, int64_t n_samples,
+                           const ms_streaming_config* config, int32_t* ids_out, int32_t cap, int32_t* n_out,
+                           ms_gen_stats* stats) {
+    return guarded([&]() -> ms_status {
+        if (!model || !n_out) return fail(MS_ERR_INVALID_ARG, "model and n_out must be non-null");
+        if (n_samples < 0 || (n_samples > 0 && !audio)) return fail(MS_ERR_INVALID_ARG, "bad audio buffer");
+        if (cap < 0 || (cap > 0 && !ids_out)) return fail(MS_ERR_INVALID_ARG, "bad ids buffer");
+        ms_streaming_config sc;
+        ms_streaming_config_default(&sc);
+        if (config) sc = *config;
+        if (sc.max_memory_frames <= 0) return fail(MS_ERR_INVALID_ARG, "max_memory_frames must be positive");
+        Model& m = *reinterpret_cast<Model*>(model);
+        std::lock_guard<std::mutex> g(m.mu);
+        MSB_CUDA(cudaSetDevice(m.device));
+        const Config& c = m.cfg;
+        ms_gen_stats st;
+        std::memset(&st, 0, sizeof(st));
+        cudaEvent_t t0, t1, t2;
+        MSB_CUDA(cudaEventCreate(&t0));
+        MSB_CUDA(cudaEventCreate(&t1));
+        MSB_CUDA(cudaEventCreate(&t2));
+        MSB_CUDA(cudaEventRecord(t0, m.stream));
+        // one full encode (MoonshineStreaming.swift:297-301) and the cross K/V of every row
+        m.ws.audio.ensure((size_t)std::max<int64_t>(n_samples, 1) * 4);
+        if (n_samples > 0)
+            MSB_CUDA(cudaMemcpyAsync(m.ws.audio.p, audio, (size_t)n_samples * 4, cudaMemcpyHostToDevice, m.stream));
+        const int total = m.encode_device(m.ws.audio.as<float>(), n_samples, 0);
+        st.memory_frames = total;
+        if (total > 0) m.cross_kv(m.memory_ptr(), total, 0);
+        MSB_CUDA(cudaEventRecord(t1, m.stream));
+        int32_t n = 0;
+        auto put = [&](int32_t id) {
+            if (n < cap) ids_out[n] = id;
+            ++n;
+        };
+        int mem_start = 0;
+        while (mem_start < total) {  // :312-360
+            const int mem_end = std::min(mem_start + sc.max_memory_frames, total);
+            const int frames = mem_end - mem_start;
+            const int tok_limit = (int)std::ceil((double)frames * 0.02 * c.max_tok_per_s);
+            if (tok_limit <= 0) break;
+            m.ensure_decode(m.ws.m_cap, tok_limit, false, c.vocab);
+            // a segment is a row slice of the cross K/V: same layout, base moved by mem_start rows
+            const float* c32 = m.ws.cross32.as<float>() + (size_t)mem_start * c.head_dim;
+            const char* cst = reinterpret_cast<const char*>(m.kv_f16 ? m.ws.cross16.p : m.ws.cross32.p) +
+                              (size_t)mem_start * c.head_dim * (m.kv_f16 ? 2 : 4);
+            Model::DecodeResult r = m.decode(c32, cst, m.ws.m_cap, frames, tok_limit, false, nullptr, false);
+            const int n_ids = r.n_calls - (r.hit_eos ? 1 : 0);
+            std::vector<int32_t> seg((size_t)std::max(n_ids, 0));
+            if (n_ids > 0) {
+                MSB_CUDA(cudaMemcpyAsync(seg.data(), m.ws.ids.p, (size_t)n_ids * 4, cudaMemcpyDeviceToHost, m.stream));
+                MSB_CUDA(cudaStreamSynchronize(m.stream));
+            }
+            // the reference's hitEOS is set only by an EOS before the last decoder call
+            const bool hit = r.hit_eos && r.n_calls < tok_limit;
+            if (!seg.empty()) {
+                for (int32_t id : seg) put(id);
+                put(-1);
+                st.n_chunks += 1;
+            }
+            st.n_tokens += (int32_t)seg.size();
+            st.hit_eos = hit ? 1 : 0;
+            st.decode_kernel = r.kernel;
+            if (hit && frames > sc.min_segment_frames) {  // :354-359 (tokens include the start token)
+                const int used = std::max(sc.min_segment_frames,
+                                          (int)((double)(seg.size() + 1) / c.max_tok_per_s * 50.0));
+                mem_start += std::min(used, frames);
+            } else {
+                mem_start = mem_end;
+            }
+        }
+        MSB_CUDA(cudaEventRecord(t2, m.stream));
+        MSB_CUDA(cudaEventSynchronize(t2));
+        float te = 0, tt = 0;
+        cudaEventElapsedTime(&te, t0, t1);
+        cudaEventElapsedTime(&tt, t0, t2);
+        cudaEventDestroy(t0);
+        cudaEventDestroy(t1);
+        cudaEventDestroy(t2);
+        st.encode_ms = te;
+        st.decode_ms = tt - te;
+        st.total_ms = tt;
+        const double dur = (double)n_samples / (double)c.sample_rate;
+        st.tokens_per_second = tt > 0 ? dur / (tt / 1000.0) : 0.0;
+        if (stats) *stats = st;
+        *n_out = n;
+        if (n > cap) return fail(MS_ERR_CAPACITY, "ids buffer too small");
+        return MS_OK;
+    });
+}
+
 void* ms_model_stream(ms_model* model) {
     return model ? (void*)reinterpret_cast<Model*>(model)->stream : nullptr;
 }

@@ -102,6 +102,8 @@ def _load_lib() -> C.CDLL:
         "ms_model_get_config": (C.c_int, [P, C.POINTER(_ModelConfig)]),
         "ms_generate": (C.c_int, [P, f32p, C.c_int64, C.POINTER(_GenParams), i32p, C.c_int32,
                                   i32p, f32p, C.POINTER(_GenStats)]),
+        "ms_generate_long": (C.c_int, [P, f32p, C.c_int64, C.POINTER(_StreamingConfig), i32p, C.c_int32,
+                                       i32p, C.POINTER(_GenStats)]),
         "ms_generate_batch": (C.c_int, [P, C.POINTER(f32p), C.POINTER(C.c_int64), C.c_int32,
                                         C.POINTER(_GenParams), i32p, C.c_int32, i32p,
                                         C.POINTER(_GenStats)]),
@@ -307,6 +309,39 @@ class MoonshineModel:
         if return_logits:
             out.logits = logits
         return out
+
+    def generate_long(self, audio, streaming_config: Optional["StreamingConfig"] = None):
+        """generateLong (MoonshineStreaming.swift:287-376): returns (segments, output) where
+        segments are the id lists of the segments that produced tokens and output carries
+        the timings (its tokens_per_second is audio seconds per wall second, as in the
+        reference)."""
+        a = _f32(audio)
+        sc = (streaming_config or StreamingConfig())._c()
+        cap = max(16, int(np.ceil(a.shape[0] / self.sample_rate * 6.5)) * 4 + 64)
+        while True:
+            ids = np.zeros(cap, dtype=np.int32)
+            n = C.c_int32()
+            st = _GenStats()
+            s = _L().ms_generate_long(self._h, _fptr(a), a.shape[0], C.byref(sc), _iptr(ids), cap,
+                                      C.byref(n), C.byref(st))
+            if s == MS_ERR_CAPACITY and n.value > cap:
+                cap = n.value + 1
+                continue
+            _check(s)
+            break
+        segments, cur = [], []
+        for t in ids[: n.value].tolist():
+            if t == -1:
+                segments.append(cur)
+                cur = []
+            else:
+                cur.append(t)
+        out = TranscriptionOutput(tokens=[t for seg in segments for t in seg], generation_tokens=len(segments),
+                                  total_time=st.total_ms / 1000.0, tokens_per_second=st.tokens_per_second,
+                                  encode_ms=st.encode_ms, decode_ms=st.decode_ms, hit_eos=bool(st.hit_eos),
+                                  memory_frames=st.memory_frames,
+                                  decode_kernel=DECODE_KERNEL_NAMES.get(st.decode_kernel, ""))
+        return segments, out
 
     def generate_device(self, audio_dev_ptr: int, n_samples: int, ids_dev_ptr: int, cap: int,
                         forced_len: Optional[int] = None, max_tokens: Optional[int] = None,

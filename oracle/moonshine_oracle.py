@@ -474,6 +474,33 @@ class Oracle:
             ids.extend(out)
         return ids
 
+    def generate_long(self, audio, max_memory_frames: int = 100000, min_segment_frames: int = 250,
+                      kv_fp16: bool = True) -> List[List[int]]:
+        """generateLong (MoonshineStreaming.swift:287-376): one full encode, then segments of at
+        most max_memory_frames memory rows with EOS-driven advance.  Returns the ids of every
+        segment that produced tokens (the reference keeps the non-empty segment texts)."""
+        mem = self.memory_for(np.asarray(audio, dtype=np.float32).reshape(-1))
+        total = mem.shape[0]
+        segments: List[List[int]] = []
+        start = 0
+        while start < total:  # :312
+            end = min(start + max_memory_frames, total)
+            frames = end - start
+            limit = int(math.ceil(frames * 0.02 * self.cfg.max_tokens_per_second))  # :317
+            ids, hit, _, _ = self.greedy(mem[start:end], limit, kv_fp16)
+            # :324-345: the loop runs limit - 1 more calls and only an EOS inside it sets hitEOS;
+            # an EOS from the last call is dropped without setting it
+            calls = len(ids) + (1 if hit else 0)
+            hit = hit and calls < limit
+            if ids:
+                segments.append(ids)
+            if hit and frames > min_segment_frames:  # :354-359, tokens include the start token
+                used = max(min_segment_frames, int((len(ids) + 1) / self.cfg.max_tokens_per_second * 50.0))
+                start += min(used, frames)
+            else:
+                start = end
+        return segments
+
 
 class DecoderCache:
     """Per-layer self and cross K/V (MoonshineDecoder.swift:90-98) for one utterance."""

@@ -67,3 +67,16 @@ def test_sanitize_mlx_layout_roundtrip():
     assert set(a) == set(b)
     for k in a:
         np.testing.assert_array_equal(a[k], b[k])
+
+
+def test_generate_long_single_segment_equals_generate(tmp_path):
+    """With the memory cap above the audio's frame count, generateLong is one greedy decode
+    of the whole memory: the same ids as generate on one chunk (CPU, oracle only)."""
+    from moonshine_b200 import synth
+    from oracle.moonshine_oracle import Oracle
+    d = synth.ensure_model_dir(str(tmp_path), "tiny", vocab_size=512)
+    o = Oracle.from_dir(d)
+    audio = synth.synth_audio(16000, 5)
+    segs = o.generate_long(audio, max_memory_frames=10000, min_segment_frames=5)
+    ref = o.generate(audio)
+    assert [t for s in segs for t in s] == ref

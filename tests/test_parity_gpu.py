@@ -142,3 +142,32 @@ def test_both_decode_kernels_30s(tiny_dir, kernel):
     ids, _, logits, _ = o.greedy(o.memory_for(audio), 48, True, forced_len=48, keep_logits=True)
     assert out.tokens == ids
     assert_logits_close(out.logits[:48], logits, FP32_LOGIT_TOL)
+
+
+def test_generate_long_memory_cap(tiny, tiny_dir):
+    """generateLong (MoonshineStreaming.swift:287-376) with a 100-frame memory cap: 6.6 s of
+    audio (330 frames) decodes as 4 segments over slices of one full encode."""
+    import moonshine_b200 as mb
+    audio = synth.synth_audio(105600, 0)
+    tiny.enable_float16_kv_cache(True)
+    segs, out = tiny.generate_long(audio, mb.StreamingConfig(max_memory_frames=100, min_segment_frames=20))
+    ref = oracle_for(tiny_dir).generate_long(audio, max_memory_frames=100, min_segment_frames=20)
+    assert segs == ref
+    assert len(ref) == 4 and out.generation_tokens == 4
+
+
+def test_generate_long_eos_advance(model_root, tmp_path):
+    """An EOS inside a segment longer than min_segment_frames moves the next segment's start
+    by max(min_segment_frames, tokens / 6.5 * 50) frames instead of the full segment.  The
+    weight seed 5 model's greedy ids vary within a segment; its eos id is set to one of
+    them (16128, the sixth id of the first segment) so segments end early."""
+    import moonshine_b200 as mb
+    d = model_dir(model_root, "tiny", seed=5)
+    audio = synth.synth_audio(105600, 0)
+    eos_dir = with_config(d, str(tmp_path / "eos_long"), eos_token_id=16128)
+    m = mb.MoonshineModel.load(eos_dir)
+    sc = mb.StreamingConfig(max_memory_frames=120, min_segment_frames=10)
+    segs, _ = m.generate_long(audio, sc)
+    ref = oracle_for(eos_dir).generate_long(audio, max_memory_frames=120, min_segment_frames=10)
+    assert segs == ref
+    assert len(ref) >= 6  # 330 frames in 120-frame caps would give 3 segments
