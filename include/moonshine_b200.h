@@ -111,13 +111,16 @@ typedef struct {
     int32_t max_tokens;        /* maxTokens; <= 0 means Int.max (no cap) */
     int32_t forced_len;        /* > 0: decode exactly this many tokens per chunk, EOS fed
                                   back like any id (benchmark / parity harness mode) */
-    float temperature;         /* only 0 (greedy argMax) is supported */
+    float temperature;         /* 0: greedy argMax; > 0: each token is a draw from
+                                  softmax(logits / temperature) (MLXRandom.categorical,
+                                  MoonshineModel.swift:211-213), by the Gumbel-max trick */
     float reserved_f;
     double chunk_duration;     /* seconds per independently decoded chunk; <= 0 -> 30 */
     const int32_t* teacher_ids;/* nullable: feed these ids instead of the argmax (one per
                                   decoder call after BOS; needs forced_len = count) */
     int32_t n_teacher;
-    int32_t reserved_i;
+    int32_t seed;              /* temperature > 0: a draw depends only on (seed, chunk, step,
+                                  vocabulary index; plus the row in ms_generate_batch) */
     float* batch_logits;       /* nullable, ms_generate_batch only: [batch][cap][vocab]
                                   logits of every decoder call */
     int32_t reserved[4];
@@ -163,7 +166,7 @@ void* ms_model_stream(ms_model* model);
  * are decoded in lockstep: every projection is one bf16 tensor-core GEMM over all B rows
  * (fp32 accumulation, residual stream and softmax), so logits agree with a per-utterance
  * ms_generate to bf16 precision.  Longer utterances fall back to per-utterance decoding.
- * ids_out is [B * cap], n_out [B]; temperature and teacher ids are not supported. */
+ * ids_out is [B * cap], n_out [B]; teacher ids are not supported. */
 ms_status ms_generate_batch(ms_model* model, const float* const* audios,
                             const int64_t* n_samples, int32_t batch,
                             const ms_gen_params* params, int32_t* ids_out, int32_t cap,

@@ -56,7 +56,7 @@ struct GenOut {
 static void generate_chunk(Model& m, const float* audio, int64_t len, const ms_gen_params& gp,
                            int32_t max_tokens, int32_t* ids_out, int32_t cap, float* logits_out,
                            GenOut& out, ms_gen_stats& st, const int32_t* teacher, int32_t n_teacher,
-                           bool device_io = false) {
+                           bool device_io, unsigned chunk_index) {
     const Config& c = m.cfg;
     MSB_CUDA(cudaEventRecord(m.ev[0], m.stream));
     const float* audio_dev = audio;
@@ -87,8 +87,9 @@ static void generate_chunk(Model& m, const float* audio, int64_t len, const ms_g
         teacher_dev = m.ws.f.as<int>();
     }
     MSB_CUDA(cudaEventRecord(m.ev[1], m.stream));
+    const unsigned seed = (unsigned)gp.seed ^ (chunk_index * 0x9E3779B9u);  // chunks draw independently
     Model::DecodeResult r = m.decode(m.ws.cross32.as<float>(), m.kv_f16 ? m.ws.cross16.p : m.ws.cross32.p,
-                                     m.ws.m_cap, M, n_steps, forced, teacher_dev, want_logits);
+                                     m.ws.m_cap, M, n_steps, forced, teacher_dev, want_logits, gp.temperature, seed);
     MSB_CUDA(cudaEventRecord(m.ev[2], m.stream));
     const int n_ids = r.n_calls - (r.hit_eos ? 1 : 0);
     const int fit = std::max(0, std::min(n_ids, cap - out.n_ids));
@@ -359,8 +360,7 @@ static ms_status generate_impl(ms_model* model, const float* audio, int64_t n_sa
         ms_gen_params gp;
         ms_gen_params_default(&gp);
         if (params) gp = *params;
-        if (gp.temperature != 0.f)
-            return fail(MS_ERR_UNSUPPORTED, "only greedy decoding (temperature 0) is supported");
+        if (!(gp.temperature >= 0.f)) return fail(MS_ERR_INVALID_ARG, "temperature must be >= 0");
         if (gp.teacher_ids && gp.n_teacher <= 0) return fail(MS_ERR_INVALID_ARG, "n_teacher must be positive");
         Model& m = *reinterpret_cast<Model*>(model);
         std::lock_guard<std::mutex> g(m.mu);
@@ -379,7 +379,7 @@ static ms_status generate_impl(ms_model* model, const float* audio, int64_t n_sa
         for (int64_t off = 0; off < n_samples; off += chunk) {
             const int64_t len = std::min(chunk, n_samples - off);
             generate_chunk(m, audio + off, len, gp, max_tokens, ids_out, cap, logits_out, out, st,
-                           gp.teacher_ids, gp.n_teacher, device_io);
+                           gp.teacher_ids, gp.n_teacher, device_io, (unsigned)st.n_chunks);
             st.n_chunks += 1;
         }
         MSB_CUDA(cudaEventRecord(t1, m.stream));
@@ -440,8 +440,7 @@ ms_status ms_generate_batch(ms_model* model, const float* const* audios, const i
         ms_gen_params gp;
         ms_gen_params_default(&gp);
         if (params) gp = *params;
-        if (gp.temperature != 0.f)
-            return fail(MS_ERR_UNSUPPORTED, "only greedy decoding (temperature 0) is supported");
+        if (!(gp.temperature >= 0.f)) return fail(MS_ERR_INVALID_ARG, "temperature must be >= 0");
         Model& m = *reinterpret_cast<Model*>(model);
         const double cd = gp.chunk_duration > 0 ? gp.chunk_duration : 30.0;
         const int64_t chunk = (int64_t)(cd * (double)m.cfg.sample_rate);
@@ -480,7 +479,8 @@ ms_status ms_generate_batch(ms_model* model, const float* const* audios, const i
             MSB_CUDA(cudaEventCreate(&t0));
             MSB_CUDA(cudaEventCreate(&t1));
             MSB_CUDA(cudaEventRecord(t0, m.stream));
-            BatchEngine::Result r = m.batch->run(dev, lens, limits, gp.forced_len > 0, gp.batch_logits != nullptr);
+            BatchEngine::Result r = m.batch->run(dev, lens, limits, gp.forced_len > 0, gp.batch_logits != nullptr,
+                                                 gp.temperature, (unsigned)gp.seed);
             MSB_CUDA(cudaEventRecord(t1, m.stream));
             MSB_CUDA(cudaEventSynchronize(t1));
             float tot = 0;

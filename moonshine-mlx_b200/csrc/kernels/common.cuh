@@ -108,6 +108,20 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         : "memory");
 }
 
+// Gumbel(0, 1) noise for temperature sampling by the Gumbel-max trick (the argmax of
+// logit / T + g over the vocabulary is a draw from softmax(logit / T); Gumbel 1954, used
+// for sampling by Maddison, Tarlow and Minka 2014).  The uniform comes from a counter-based
+// hash of (seed, stream, index) with the SplitMix64 finalizer (Steele, Lea and Flood 2014),
+// so a draw depends only on those three numbers.
+__device__ __forceinline__ float gumbel_noise(uint32_t seed, uint32_t stream, uint32_t idx) {
+    uint64_t z = (((uint64_t)seed << 32) | stream) + (uint64_t)(idx + 1) * 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    const float u = ((float)(z >> 40) + 0.5f) * (1.0f / 16777216.0f);  // (0, 1), 24 bits
+    return -logf(-logf(u));
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

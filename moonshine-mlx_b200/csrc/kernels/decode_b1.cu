@@ -720,8 +720,11 @@ __global__ void __launch_bounds__(NT, 1) decode_b1_kernel(DecodeParams p) {
                 const float* rows = reg + (size_t)(k % 3) * 4 * d;
                 for (int r = 0; r < nr; ++r) {
                     const float v = sdot(rows + (size_t)r * d, hs, d, lane);
-                    if (v > bv) {
-                        bv = v;
+                    const float key = p.inv_temp > 0.f
+                                          ? v * p.inv_temp + gumbel_noise(p.seed, (unsigned)step, (unsigned)(r0 + r))
+                                          : v;
+                    if (key > bv) {
+                        bv = key;
                         bi = r0 + r;
                     }
                     if (p.logits_out && lane == 0) p.logits_out[(size_t)step * V + r0 + r] = v;

@@ -834,8 +834,10 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
             for (int i = tid; i < nr; i += NT) {
                 const float v = gres[i];
                 const int row = lm_row0 + row0 + i;
-                if (v > bv) {  // a thread sees its rows in increasing order: ties keep the lowest
-                    bv = v;
+                const float key =
+                    p.inv_temp > 0.f ? v * p.inv_temp + gumbel_noise(p.seed, (unsigned)step, (unsigned)row) : v;
+                if (key > bv) {  // a thread sees its rows in increasing order: ties keep the lowest
+                    bv = key;
                     bi = row;
                 }
                 if (p.logits_out) p.logits_out[(size_t)step * V + row] = v;

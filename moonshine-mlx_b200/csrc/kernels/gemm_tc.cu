@@ -248,11 +248,19 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* 
             int bestn = 0x7fffffff;
             if (ok) {
                 if (ep.out) *reinterpret_cast<float4*>(ep.out + (size_t)m * ep.ldc + n) = v;
+                float4 k = v;
+                if (g.inv_temp > 0.f) {  // temperature sampling: Gumbel-max keys
+                    const unsigned st = (unsigned)(*g.step) + ((unsigned)m << 20);
+                    k = make_float4(v.x * g.inv_temp + gumbel_noise(g.seed, st, (unsigned)n),
+                                    v.y * g.inv_temp + gumbel_noise(g.seed, st, (unsigned)n + 1),
+                                    v.z * g.inv_temp + gumbel_noise(g.seed, st, (unsigned)n + 2),
+                                    v.w * g.inv_temp + gumbel_noise(g.seed, st, (unsigned)n + 3));
+                }
                 // increasing column order with strict > keeps the lowest index on ties
-                if (v.x > best) { best = v.x; bestn = n; }
-                if (v.y > best) { best = v.y; bestn = n + 1; }
-                if (v.z > best) { best = v.z; bestn = n + 2; }
-                if (v.w > best) { best = v.w; bestn = n + 3; }
+                if (k.x > best) { best = k.x; bestn = n; }
+                if (k.y > best) { best = k.y; bestn = n + 1; }
+                if (k.z > best) { best = k.z; bestn = n + 2; }
+                if (k.w > best) { best = k.w; bestn = n + 3; }
             }
 #pragma unroll
             for (int o = TPR / 2; o > 0; o >>= 1) {
@@ -480,7 +488,7 @@ bool epilogue_layout_ok(const TcGemmArgs& g) {
                    g.N == (r.H + 2 * r.KVH) * r.hd;
         }
         case TC_EPI_ARGMAX:
-            return g.argmax && (!ep.out || (ep.ldc % 4 == 0 && aligned(ep.out, 16)));
+            return g.argmax && (!ep.out || (ep.ldc % 4 == 0 && aligned(ep.out, 16))) && (g.inv_temp <= 0.f || g.step);
         default:
             return false;
     }

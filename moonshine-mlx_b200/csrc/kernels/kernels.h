@@ -79,6 +79,9 @@ struct TcGemmArgs {
     int ldc_bf16 = 0;
     TcRopeKv rope;
     unsigned long long* argmax = nullptr; // [M] packed (ordered value, ~column) maxima
+    float inv_temp = 0.f;                 // ARGMAX: 0 greedy, else maxima of logit * inv_temp + Gumbel
+    unsigned seed = 0;                    //   noise of (seed, step + (row << 20), column);
+    const int* step = nullptr;            //   step from this device word
     unsigned* status = nullptr;           // device word; 5 = a bounded wait gave up
 };
 }  // namespace msb
@@ -156,6 +159,8 @@ struct DecodeParams {
     int start_token;
     int n_steps;          // decoder calls to run
     int forced;           // 1: never stop on EOS
+    float inv_temp;       // 0: greedy argmax; else sample softmax(logit * inv_temp) (Gumbel-max)
+    unsigned seed;        // sampling: noise of (seed, step, vocabulary index)
     const int* teacher;   // nullable [n_steps]: next input ids
     int eos;
     int* ids_out;         // [n_steps]

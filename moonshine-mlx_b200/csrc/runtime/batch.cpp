@@ -261,6 +261,9 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
         ga.argmax = amax.as<unsigned long long>();
         ga.ep.out = logits;
         ga.ep.ldc = c.vocab;
+        ga.inv_temp = inv_temp;
+        ga.seed = seed;
+        ga.step = pos.as<int>();
         gemm(a_hb, m_lm, ga, d, kBnWide);
     }
     MSB_CUDA(launch_step_finalize(amax.as<unsigned long long>(), B, pos.as<int>(), next_ids.as<int>(), ids.as<int>(),
@@ -269,7 +272,10 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
 }
 
 BatchEngine::Result BatchEngine::run(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
-                                     const std::vector<int>& limits, bool forced, bool want_logits) {
+                                     const std::vector<int>& limits, bool forced, bool want_logits, float temperature,
+                                     unsigned seed_) {
+    inv_temp = temperature > 0.f ? 1.f / temperature : 0.f;
+    seed = seed_;
     const Config& c = m.cfg;
     const int B = (int)audio_dev.size();
     cudaStream_t s = m.stream;
@@ -301,6 +307,7 @@ BatchEngine::Result BatchEngine::run(const std::vector<const float*>& audio_dev,
 
 BatchEngine::Result BatchEngine::run_cross(const std::vector<CrossSrc>& src, const std::vector<int>& limits,
                                            bool forced) {
+    inv_temp = 0.f;
     const Config& c = m.cfg;
     const int B = (int)src.size();
     cudaStream_t s = m.stream;

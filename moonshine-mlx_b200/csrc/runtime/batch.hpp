@@ -24,8 +24,10 @@ struct BatchEngine {
     };
     // Encode each utterance (one chunk each), project all cross K/V at once, then run the
     // step loop.  limits[b] decoder calls at most per utterance (forced: exactly).
+    // temperature > 0 samples each row's tokens (Gumbel-max keys of (seed, step, row, column)).
     Result run(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
-               const std::vector<int>& limits, bool forced, bool want_logits);
+               const std::vector<int>& limits, bool forced, bool want_logits, float temperature = 0.f,
+               unsigned seed = 0);
 
     // Decode rows whose cross K/V already exist (streaming segments): row b's layout is
     // [L][2][KVH][m_cap][hd] with `frames` valid rows, fp32 plus the fp16 copy.
@@ -64,6 +66,8 @@ struct BatchEngine {
     DevBuf xsrc;  // device pointer tables of run_cross
     void ensure_ws(int B, int T, int Mtot, int maxM);
     void enqueue_step(int B, int max_frames, bool forced, bool first, float* logits);
+    float inv_temp = 0.f;  // sampling state of the current run
+    unsigned seed = 0;
     void gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& g, int K, int bn);
 };
 

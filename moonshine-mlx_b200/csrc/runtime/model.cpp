@@ -699,7 +699,8 @@ bool Model::prepare_cluster_decode() {
 }
 
 Model::DecodeResult Model::decode(const float* cross32, const void* cross_stored, int m_cap, int M,
-                                  int n_steps, bool forced, const int* teacher_dev, bool logits) {
+                                  int n_steps, bool forced, const int* teacher_dev, bool logits, float temperature,
+                                  unsigned seed) {
     const Config& c = cfg;
     ensure_rope(n_steps + 1);
     DecodeParams p{};
@@ -741,6 +742,8 @@ Model::DecodeResult Model::decode(const float* cross32, const void* cross_stored
     p.start_token = c.dec_start;
     p.n_steps = n_steps;
     p.forced = forced ? 1 : 0;
+    p.inv_temp = temperature > 0.f ? 1.f / temperature : 0.f;
+    p.seed = seed;
     p.teacher = teacher_dev;
     p.eos = c.eos;
     p.ids_out = ws.ids.as<int>();

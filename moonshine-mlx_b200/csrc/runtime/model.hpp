@@ -154,10 +154,11 @@ struct Model {
         bool hit_eos = false;
         int kernel = MS_DECODE_GRID;  // which batch-1 kernel ran
     };
-    // Greedy decode against cross K/V laid out [L][2][KVH][m_cap][hd] (fp32 copy for the
-    // first decoder call, stored copy afterwards).
+    // Greedy (temperature 0) or sampled decode against cross K/V laid out
+    // [L][2][KVH][m_cap][hd] (fp32 copy for the first decoder call, stored copy afterwards).
     DecodeResult decode(const float* cross32, const void* cross_stored, int m_cap, int M, int n_steps,
-                        bool forced, const int* teacher_dev, bool logits);
+                        bool forced, const int* teacher_dev, bool logits, float temperature = 0.f,
+                        unsigned seed = 0);
     // Cross K/V of `frames` memory rows into explicit buffers at row offset `row0`.
     void cross_kv_into(const float* memory, int frames, int row0, float* out32, void* out16, int m_cap,
                        cudaStream_t s = nullptr);

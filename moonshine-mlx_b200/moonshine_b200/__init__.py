@@ -52,7 +52,7 @@ class _GenParams(C.Structure):
     _fields_ = [("max_tokens", C.c_int32), ("forced_len", C.c_int32),
                 ("temperature", C.c_float), ("reserved_f", C.c_float),
                 ("chunk_duration", C.c_double), ("teacher_ids", C.POINTER(C.c_int32)),
-                ("n_teacher", C.c_int32), ("reserved_i", C.c_int32),
+                ("n_teacher", C.c_int32), ("seed", C.c_int32),
                 ("batch_logits", C.POINTER(C.c_float)), ("reserved", C.c_int32 * 4)]
 
 
@@ -259,12 +259,13 @@ class MoonshineModel:
     def enable_float16_kv_cache(self, enabled: bool) -> None:
         _check(_L().ms_model_enable_fp16_kv_cache(self._h, 1 if enabled else 0))
 
-    def _params(self, max_tokens, temperature, chunk_duration, forced_len, teacher):
+    def _params(self, max_tokens, temperature, chunk_duration, forced_len, teacher, seed=0):
         p = _GenParams()
         _L().ms_gen_params_default(C.byref(p))
         p.max_tokens = 0 if max_tokens is None else int(max_tokens)
         p.forced_len = 0 if forced_len is None else int(forced_len)
         p.temperature = float(temperature)
+        p.seed = int(seed) & 0x7FFFFFFF
         p.chunk_duration = float(chunk_duration)
         if teacher is not None:
             p.teacher_ids = _iptr(teacher)
@@ -274,8 +275,9 @@ class MoonshineModel:
     def generate(self, audio, max_tokens: Optional[int] = None, temperature: float = 0.0,
                  chunk_duration: float = 30.0, forced_len: Optional[int] = None,
                  teacher_ids: Optional[Sequence[int]] = None,
-                 return_logits: bool = False) -> TranscriptionOutput:
-        """MoonshineModel.generate (MoonshineModel.swift:130-184)."""
+                 return_logits: bool = False, seed: int = 0) -> TranscriptionOutput:
+        """MoonshineModel.generate (MoonshineModel.swift:130-184); temperature > 0 samples
+        (MLXRandom.categorical of logits / temperature) with draws keyed by ``seed``."""
         a = _f32(audio)
         sr = self.sample_rate
         chunk = int(chunk_duration * sr)
@@ -285,7 +287,7 @@ class MoonshineModel:
             per_chunk = min(per_chunk, max_tokens) if not forced_len else per_chunk
         cap = max(1, n_chunks * per_chunk + 1)
         teacher = None if teacher_ids is None else np.ascontiguousarray(teacher_ids, dtype=np.int32)
-        p = self._params(max_tokens, temperature, chunk_duration, forced_len, teacher)
+        p = self._params(max_tokens, temperature, chunk_duration, forced_len, teacher, seed)
         V = self.config.vocab_size
         while True:
             ids = np.zeros(cap, dtype=np.int32)
@@ -383,7 +385,7 @@ class MoonshineModel:
 
     def generate_batch(self, audios: Sequence[np.ndarray], max_tokens: Optional[int] = None,
                        forced_len: Optional[int] = None, chunk_duration: float = 30.0,
-                       return_logits: bool = False):
+                       return_logits: bool = False, temperature: float = 0.0, seed: int = 0):
         """Batched offline generation.  Returns (ids per utterance, stats[, logits
         [B, cap, vocab] of every decoder call])."""
         arrs = [_f32(a) for a in audios]
@@ -397,7 +399,7 @@ class MoonshineModel:
         lens = (C.c_int64 * B)(*[a.shape[0] for a in arrs])
         ids = np.zeros((B, cap), dtype=np.int32)
         n = np.zeros(B, dtype=np.int32)
-        p = self._params(max_tokens, 0.0, chunk_duration, forced_len, None)
+        p = self._params(max_tokens, temperature, chunk_duration, forced_len, None, seed)
         logits = None
         if return_logits:
             logits = np.zeros((B, cap, self.config.vocab_size), dtype=np.float32)

@@ -106,8 +106,8 @@ def test_tiny_inputs(tiny, tiny_dir, n):
 def test_invalid_arguments(tiny):
     import moonshine_b200 as mb
     with pytest.raises(mb.MoonshineError) as ei:
-        tiny.generate(np.zeros(1600, np.float32), temperature=0.5)
-    assert ei.value.status == 8
+        tiny.generate(np.zeros(1600, np.float32), temperature=-0.5)
+    assert ei.value.status == 1
     with pytest.raises(mb.MoonshineError):
         mb.MoonshineModel.load("/nonexistent/model/dir")
 
@@ -171,3 +171,59 @@ def test_generate_long_eos_advance(model_root, tmp_path):
     ref = oracle_for(eos_dir).generate_long(audio, max_memory_frames=120, min_segment_frames=10)
     assert segs == ref
     assert len(ref) >= 6  # 330 frames in 120-frame caps would give 3 segments
+
+
+def _first_token_probs(d, audio, T):
+    o = oracle_for(d)
+    _, _, logits, _ = o.greedy(o.memory_for(audio), 1, True, forced_len=1, keep_logits=True)
+    z = np.asarray(logits[0], np.float64) / T
+    p = np.exp(z - z.max())
+    return p / p.sum()
+
+
+def _chi2(counts, p):
+    n = counts.sum()
+    keep = p * n >= 5
+    return float(np.sum((counts[keep] - n * p[keep]) ** 2 / (n * p[keep])))
+
+
+@pytest.mark.parametrize("kernel", ["grid", "auto"])
+def test_temperature_sampling_distribution(model_root, kernel):
+    """temperature > 0 draws each token from softmax(logits / T) (MLXRandom.categorical,
+    MoonshineModel.swift:211-213).  The random streams cannot match MLX's, so the test is
+    distributional: 4000 seeds on a 16-token vocabulary against the oracle's softmax of the
+    first decoder call (chi-square well above its 0.1 % point would fail), plus a fixed
+    seed giving the same draws twice."""
+    import moonshine_b200 as mb
+    d = model_dir(model_root, "tiny", vocab_size=16)
+    m = mb.MoonshineModel.load(d, decode_kernel=kernel)
+    audio = synth.synth_audio(32000, 9)
+    T = 0.7
+    p = _first_token_probs(d, audio, T)
+    counts = np.zeros(16)
+    for seed in range(4000):
+        out = m.generate(audio, forced_len=1, temperature=T, seed=seed)
+        counts[out.tokens[0]] += 1
+    chi2 = _chi2(counts, p)
+    assert chi2 < 45.0, (chi2, counts, 4000 * p)
+    a = m.generate(audio, max_tokens=20, temperature=T, seed=123)
+    b = m.generate(audio, max_tokens=20, temperature=T, seed=123)
+    assert a.tokens == b.tokens
+
+
+def test_temperature_sampling_batch(model_root):
+    """The batched engine samples per row: the first tokens of 16 x 256 rows of one utterance
+    follow the same softmax (bf16 logits, well inside the chi-square margin)."""
+    import moonshine_b200 as mb
+    d = model_dir(model_root, "tiny", vocab_size=16)
+    m = mb.MoonshineModel.load(d)
+    audio = synth.synth_audio(32000, 9)
+    T = 0.7
+    p = _first_token_probs(d, audio, T)
+    counts = np.zeros(16)
+    for seed in range(16):
+        ids, _ = m.generate_batch([audio] * 256, forced_len=1, temperature=T, seed=seed)
+        for r in ids:
+            counts[r[0]] += 1
+    chi2 = _chi2(counts, p)
+    assert chi2 < 45.0, (chi2, counts, counts.sum() * p)
