@@ -91,7 +91,11 @@ Config Config::from_json_file(const std::string& path) {
         c.rope_theta = rp->num_or("rope_theta", c.rope_theta);
     }
     c.max_tok_per_s = d.num_or("max_tokens_per_second", 6.5);
-    if (const Json* q = d.get("quantization"); q && q->kind == Json::Object) c.quantized = true;
+    if (const Json* q = d.get("quantization"); q && q->kind == Json::Object) {
+        c.quantized = true;
+        c.q_group = (int)q->int_or("group_size", 64);
+        c.q_bits = (int)q->int_or("bits", 8);
+    }
     if (const Json* e = d.get("encoder_config"); e && e->kind == Json::Object) {
         // MoonshineConfig.swift:43-56
         c.e_hidden = (int)e->int_or("hidden_size", 320);
@@ -185,7 +189,7 @@ struct SafeTensors {
             if (a > e || e > data_size) throw MsError(MS_ERR_BAD_WEIGHTS, "offsets out of range: " + kv.first);
             t.data = data + a;
             t.bytes = e - a;
-            size_t esz = t.dtype == "F32" ? 4 : (t.dtype == "F16" || t.dtype == "BF16") ? 2 : 0;
+            size_t esz = (t.dtype == "F32" || t.dtype == "U32") ? 4 : (t.dtype == "F16" || t.dtype == "BF16") ? 2 : 0;
             if (esz && (size_t)t.numel() * esz != t.bytes)
                 throw MsError(MS_ERR_BAD_WEIGHTS, "size mismatch: " + kv.first);
             tensors[kv.first] = t;
@@ -296,8 +300,36 @@ struct WeightSource {
         if (it == byname.end()) throw MsError(MS_ERR_BAD_WEIGHTS, "missing weight " + k);
         return *it->second;
     }
+    // Affine quantization of Linear weights (MLX format): a uint32 `.weight` of packed
+    // `q_bits`-bit codes, lowest bits first, with per-group `.scales` / `.biases`.
+    int q_group = 0, q_bits = 0;
     std::vector<float> f32(const std::string& k, std::vector<int64_t> shape) const {
+        auto it = byname.find(k);
+        if (it != byname.end() && it->second->dtype == "U32" && q_bits > 0 && shape.size() == 2)
+            return dequantize(k, shape[0], shape[1]);
         return to_f32(need(k, shape));
+    }
+    // w = scale * q + bias per group of q_group inputs: the matrix quantized_matmul multiplies by
+    // (ModelLoader.swift:47-49,103-111).
+    std::vector<float> dequantize(const std::string& k, int64_t out, int64_t in) const {
+        const std::string base = k.substr(0, k.size() - std::string(".weight").size());
+        if (k.size() < 7 || k.compare(k.size() - 7, 7, ".weight") != 0 || in % q_group)
+            throw MsError(MS_ERR_BAD_WEIGHTS, "unexpected quantized tensor " + k);
+        const int per = 32 / q_bits;
+        const Tensor& packed = need(k, {out, in / per});
+        const std::vector<float> sc = to_f32(need(base + ".scales", {out, in / q_group}));
+        const std::vector<float> bi = to_f32(need(base + ".biases", {out, in / q_group}));
+        const uint32_t* q = reinterpret_cast<const uint32_t*>(packed.data);
+        const uint32_t mask = (1u << q_bits) - 1u;
+        std::vector<float> w((size_t)out * in);
+        for (int64_t o = 0; o < out; ++o)
+            for (int64_t i = 0; i < in; ++i) {
+                const uint32_t word = q[(size_t)o * (in / per) + i / per];
+                const float code = (float)((word >> ((i % per) * q_bits)) & mask);
+                const size_t gi = (size_t)o * (in / q_group) + i / q_group;
+                w[(size_t)o * in + i] = sc[gi] * code + bi[gi];
+            }
+        return w;
     }
     // Conv weight as [out][k][in] from HF [out,in,k] or MLX [out,k,in].
     std::vector<float> conv(const std::string& k, int out, int in, int ks) const {
@@ -365,7 +397,9 @@ void Model::ensure_rope(int positions) {
 
 static void validate(const Config& c) {
     auto bad = [](const std::string& m) { throw MsError(MS_ERR_UNSUPPORTED, m); };
-    if (c.quantized) bad("quantized checkpoints are not supported");
+    if (c.quantized && !(c.q_bits == 2 || c.q_bits == 4 || c.q_bits == 8))
+        bad("quantized checkpoints need bits 2, 4 or 8");
+    if (c.quantized && (c.q_group < 8 || c.q_group % 8)) bad("quantization group_size must be a multiple of 8");
     if (c.hidden % 4 || c.e_hidden % 4 || c.inter % 4 || c.e_inter % 4)
         bad("hidden/intermediate sizes must be multiples of 4");
     if (c.head_dim % 4 || c.e_head_dim % 4 || c.head_dim > 64 || c.e_head_dim > 128)
@@ -401,6 +435,10 @@ Model* load_model(const std::string& dir, const ms_options& o) {
     for (auto& e : m->ev) MSB_CUDA(cudaEventCreate(&e));
 
     WeightSource ws;
+    if (m->cfg.quantized) {
+        ws.q_group = m->cfg.q_group;
+        ws.q_bits = m->cfg.q_bits;
+    }
     ws.load(find_weights(dir));
     const Config& c = m->cfg;
     const int ed = c.e_hidden, d = c.hidden, fl = c.frame_len();

@@ -37,7 +37,8 @@ struct Config {
     std::vector<std::pair<int, int>> windows;
     int bos = 1, eos = 2, dec_start = 1, pad = 0;
     double partial_rotary = 0.8, rope_theta = 10000.0, max_tok_per_s = 6.5;
-    bool quantized = false;
+    bool quantized = false;  // config.json "quantization" (MoonshineConfig.swift:147-153)
+    int q_group = 64, q_bits = 8;
 
     int frame_len() const { return (int)(frame_ms * (double)sample_rate / 1000.0); }
     int rotary_ndims() const {

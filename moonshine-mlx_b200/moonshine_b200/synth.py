@@ -189,6 +189,116 @@ def write_model_dir(path: str, cfg: dict, weights: Dict[str, np.ndarray],
     return path
 
 
+# Linear layers of the MLX module tree: the ones the reference quantizes when their input
+# width is a multiple of the group size (ModelLoader.swift:103-111).  Embeddings, convs and
+# norms stay floating point.
+_LINEAR_SUFFIXES = ("_proj.weight", "mlp.fc1.weight", "mlp.fc2.weight", "embedder.linear.weight",
+                    "decoder.proj.weight", "proj_out.weight")
+
+
+def is_quantizable_linear(key: str, shape: tuple, group_size: int) -> bool:
+    return key.endswith(_LINEAR_SUFFIXES) and len(shape) == 2 and shape[1] % group_size == 0
+
+
+def quantize_affine(w: np.ndarray, group_size: int, bits: int):
+    """MLX affine quantization of a [out, in] matrix (mlx.core.quantize, published format):
+    per group of ``group_size`` consecutive inputs, w ~ scale * q + bias with q an unsigned
+    ``bits``-bit integer; q values packed into uint32 words lowest bits first.  Returns
+    (packed [out, in * bits / 32] uint32, scales [out, in / group], biases [out, in / group])."""
+    out_dim, in_dim = w.shape
+    levels = (1 << bits) - 1
+    g = w.reshape(out_dim, in_dim // group_size, group_size).astype(np.float64)
+    lo, hi = g.min(axis=-1), g.max(axis=-1)
+    scale = np.where(hi > lo, (hi - lo) / levels, 1.0)
+    q = np.clip(np.rint((g - lo[..., None]) / scale[..., None]), 0, levels).astype(np.uint32)
+    q = q.reshape(out_dim, in_dim)
+    per = 32 // bits
+    q = q.reshape(out_dim, in_dim // per, per)
+    packed = np.zeros((out_dim, in_dim // per), dtype=np.uint32)
+    for j in range(per):
+        packed |= q[:, :, j] << np.uint32(j * bits)
+    return packed, scale.astype(np.float32), lo.astype(np.float32)
+
+
+def dequantize_affine(packed: np.ndarray, scales: np.ndarray, biases: np.ndarray, group_size: int,
+                      bits: int) -> np.ndarray:
+    """Inverse of quantize_affine: w = scale * q + bias per group (float32)."""
+    per = 32 // bits
+    out_dim = packed.shape[0]
+    in_dim = packed.shape[1] * per
+    mask = np.uint32((1 << bits) - 1)
+    q = np.stack([(packed >> np.uint32(j * bits)) & mask for j in range(per)], axis=-1).reshape(out_dim, in_dim)
+    s = np.repeat(np.asarray(scales, np.float32), group_size, axis=1)
+    b = np.repeat(np.asarray(biases, np.float32), group_size, axis=1)
+    return (s * q.astype(np.float32) + b).astype(np.float32)
+
+
+def to_mlx_layout(weights: Dict[str, np.ndarray]) -> Dict[str, np.ndarray]:
+    """HuggingFace keys -> the MLX module layout (ModelLoader.swift:75-101 in reverse):
+    no ``model.`` prefix, ``.gamma`` -> ``.weight``, conv weights [out, k, in]."""
+    out = {}
+    for k, v in weights.items():
+        if k.startswith("model."):
+            k = k[6:]
+        k = k.replace(".gamma", ".weight")
+        if "conv" in k and k.endswith(".weight") and v.ndim == 3:
+            v = np.transpose(v, (0, 2, 1))
+        out[k] = np.ascontiguousarray(v)
+    return out
+
+
+def write_quantized_model_dir(path: str, cfg: dict, weights: Dict[str, np.ndarray], group_size: int = 64,
+                              bits: int = 8, scale_dtype: str = "float16") -> str:
+    """A quantized checkpoint as MLX saves one: MLX key layout, config.json
+    "quantization": {group_size, bits}, and for every quantizable Linear a uint32
+    ``.weight`` with ``.scales`` / ``.biases`` (stored in ``scale_dtype``)."""
+    os.makedirs(path, exist_ok=True)
+    cfg = dict(cfg)
+    cfg["quantization"] = {"group_size": group_size, "bits": bits}
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(cfg, f, indent=1)
+    tensors = {}
+    for k, v in to_mlx_layout(weights).items():
+        if is_quantizable_linear(k, v.shape, group_size):
+            packed, sc, bi = quantize_affine(v, group_size, bits)
+            base = k[: -len(".weight")]
+            tensors[k] = packed
+            tensors[base + ".scales"] = sc
+            tensors[base + ".biases"] = bi
+        else:
+            tensors[k] = np.ascontiguousarray(v, dtype=np.float32)
+    _save_tensors(os.path.join(path, "model.safetensors"), tensors,
+                  {k for k in tensors if k.endswith((".scales", ".biases"))}, scale_dtype)
+    return path
+
+
+def _save_tensors(fn: str, tensors: Dict[str, np.ndarray], reduced: set, reduced_dtype: str) -> None:
+    """safetensors writer for float32 / uint32 tensors, ``reduced`` keys stored as f16/bf16."""
+    header = {}
+    blobs = []
+    off = 0
+    for k in sorted(tensors):
+        v = tensors[k]
+        if v.dtype == np.uint32:
+            raw, tag = np.ascontiguousarray(v).tobytes(), "U32"
+        elif k in reduced and reduced_dtype == "float16":
+            raw, tag = np.ascontiguousarray(v, np.float32).astype(np.float16).tobytes(), "F16"
+        elif k in reduced and reduced_dtype == "bfloat16":
+            raw, tag = f32_to_bf16_bits(v).tobytes(), "BF16"
+        else:
+            raw, tag = np.ascontiguousarray(v, np.float32).tobytes(), "F32"
+        header[k] = {"dtype": tag, "shape": list(v.shape), "data_offsets": [off, off + len(raw)]}
+        blobs.append(raw)
+        off += len(raw)
+    hb = json.dumps(header).encode()
+    hb += b" " * ((8 - len(hb) % 8) % 8)
+    with open(fn, "wb") as f:
+        f.write(np.uint64(len(hb)).tobytes())
+        f.write(hb)
+        for b in blobs:
+            f.write(b)
+
+
 def _save_reduced(path: str, weights: Dict[str, np.ndarray], dtype: str) -> None:
     """safetensors writer for bf16/f16 (numpy has no bfloat16): round-to-nearest-even."""
     header = {}
@@ -248,11 +358,14 @@ def utterance_lengths(n: int, lo_s: float, hi_s: float, seed: int) -> np.ndarray
 
 
 def ensure_model_dir(root: str, arch: str = "tiny", seed: Optional[int] = None,
-                     dtype: str = "float32", **overrides) -> str:
-    """Create (once) and return a seeded model directory under ``root``."""
+                     dtype: str = "float32", quant: Optional[tuple] = None, **overrides) -> str:
+    """Create (once) and return a seeded model directory under ``root``.  ``quant`` =
+    (group_size, bits) writes an MLX affine-quantized checkpoint of the same weights."""
     if seed is None:
         seed = default_seed(arch)
     tag = f"{arch}_s{seed}_{dtype}"
+    if quant:
+        tag += f"_q{quant[0]}b{quant[1]}"
     if overrides:
         tag += "_" + "_".join(f"{k}{v}" for k, v in sorted(overrides.items())
                               if not isinstance(v, list))
@@ -262,7 +375,10 @@ def ensure_model_dir(root: str, arch: str = "tiny", seed: Optional[int] = None,
     cfg = make_config(arch, **overrides)
     w = make_weights(cfg, seed)
     tmp = path + ".tmp%d" % os.getpid()
-    write_model_dir(tmp, cfg, w, dtype=dtype)
+    if quant:
+        write_quantized_model_dir(tmp, cfg, w, group_size=quant[0], bits=quant[1])
+    else:
+        write_model_dir(tmp, cfg, w, dtype=dtype)
     try:
         os.replace(tmp, path)
     except OSError:

@@ -154,11 +154,37 @@ def sanitize_weights(w: Dict[str, np.ndarray]) -> Dict[str, np.ndarray]:
     return out
 
 
+def dequantize_weights(w: Dict[str, np.ndarray], group_size: int, bits: int) -> Dict[str, np.ndarray]:
+    """Quantized Linear layers (ModelLoader.swift:47-49,103-111, MLX affine format): a uint32
+    ``.weight`` of packed ``bits``-bit codes (lowest bits first) with per-group ``.scales``
+    and ``.biases`` becomes w = scale * q + bias, which is what quantized_matmul multiplies
+    by.  Everything else passes through."""
+    out = {}
+    per = 32 // bits
+    mask = (1 << bits) - 1
+    for k, v in w.items():
+        if k.endswith((".scales", ".biases")):
+            continue
+        base = k[: -len(".weight")] if k.endswith(".weight") else None
+        if base is not None and v.dtype == np.uint32 and base + ".scales" in w:
+            q = np.stack([(v >> np.uint32(j * bits)) & np.uint32(mask) for j in range(per)], axis=-1)
+            q = q.reshape(v.shape[0], v.shape[1] * per).astype(np.float32)
+            sc = np.repeat(w[base + ".scales"].astype(np.float32), group_size, axis=1)
+            bi = np.repeat(w[base + ".biases"].astype(np.float32), group_size, axis=1)
+            out[k] = sc * q + bi
+        else:
+            out[k] = v
+    return out
+
+
 def load_model_dir(path: str) -> Tuple[ModelConfig, Dict[str, np.ndarray]]:
-    from safetensors.numpy import load_file
     with open(os.path.join(path, "config.json")) as f:
-        cfg = ModelConfig.from_dict(json.load(f))
+        raw_cfg = json.load(f)
+    cfg = ModelConfig.from_dict(raw_cfg)
     raw = _load_safetensors_any(os.path.join(path, "model.safetensors"))
+    qc = raw_cfg.get("quantization")
+    if isinstance(qc, dict):  # MoonshineConfig.swift:147-153 (defaults 64, 8)
+        raw = dequantize_weights(raw, int(qc.get("group_size", 64)), int(qc.get("bits", 8)))
     return cfg, sanitize_weights(raw)
 
 
@@ -183,6 +209,8 @@ def _load_safetensors_any(fn: str) -> Dict[str, np.ndarray]:
             v = buf.view(np.float16).astype(np.float32)
         elif dt == "BF16":
             v = (buf.view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+        elif dt == "U32":
+            v = buf.view(np.uint32)
         else:
             raise ValueError(f"unsupported dtype {dt} for {k}")
         out[k] = v.reshape(shape).copy()

@@ -80,3 +80,19 @@ def test_generate_long_single_segment_equals_generate(tmp_path):
     segs = o.generate_long(audio, max_memory_frames=10000, min_segment_frames=5)
     ref = o.generate(audio)
     assert [t for s in segs for t in s] == ref
+
+
+@pytest.mark.parametrize("bits", [8, 4, 2])
+def test_affine_quantization_roundtrip(bits):
+    """MLX affine format (codes packed lowest bits first in uint32, per-group scale and
+    bias): the writer's codes dequantize back within half a quantization step, and the
+    oracle's loader reads the packed words the same way."""
+    from oracle.moonshine_oracle import dequantize_weights
+    rng = np.random.default_rng(bits)
+    w = (rng.standard_normal((48, 128)) * 0.02).astype(np.float32)
+    packed, sc, bi = synth.quantize_affine(w, 64, bits)
+    assert packed.dtype == np.uint32 and packed.shape == (48, 128 * bits // 32)
+    d1 = synth.dequantize_affine(packed, sc, bi, 64, bits)
+    assert np.all(np.abs(d1 - w) <= np.repeat(sc, 64, axis=1) * 0.5 + 1e-7)
+    d2 = dequantize_weights({"x.weight": packed, "x.scales": sc, "x.biases": bi}, 64, bits)["x.weight"]
+    np.testing.assert_array_equal(d1, d2)

@@ -227,3 +227,20 @@ def test_temperature_sampling_batch(model_root):
             counts[r[0]] += 1
     chi2 = _chi2(counts, p)
     assert chi2 < 45.0, (chi2, counts, counts.sum() * p)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_quantized_checkpoint(model_root, bits):
+    """MLX affine-quantized checkpoints (ModelLoader.swift:47-49,103-111; config.json
+    "quantization": group_size 64): every Linear whose input width divides by 64 is stored as
+    packed codes + scales + biases.  The library dequantizes them at load; ids and logits
+    match the oracle on the same checkpoint at the fp32 tolerance."""
+    import moonshine_b200 as mb
+    d = model_dir(model_root, "tiny", quant=(64, bits))
+    m = mb.MoonshineModel.load(d)
+    audio = synth.synth_audio(105600, 0)
+    out = m.generate(audio, forced_len=32, return_logits=True)
+    o = oracle_for(d)
+    ids, _, logits, _ = o.greedy(o.memory_for(audio), 32, True, forced_len=32, keep_logits=True)
+    assert out.tokens == ids
+    assert_logits_close(out.logits[:32], logits, FP32_LOGIT_TOL)
