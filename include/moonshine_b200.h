@@ -198,6 +198,62 @@ ms_status ms_decode_memory_static(ms_model* model, const float* memory_dev, int3
                                   int32_t n_tokens, int32_t forced, int32_t* ids_dev,
                                   int32_t* n_out, int32_t* hit_eos);
 
+/* ------------------------------------------------------------------- word timestamps */
+
+/* Outputs of ms_generate_alignment.  The caller sets the buffers and capacities; the call
+ * sets the counts. */
+typedef struct {
+    int32_t* ids;              /* [cap] generated ids, BOS/EOS excluded (the reference's gen) */
+    float* token_probs;        /* [cap] softmax probability of each decoder call's chosen id
+                                  (tokenProbs, MoonshineModel.swift:278-283; the EOS call included) */
+    int32_t* jump_frames;      /* [cap] jumpTimes (MoonshineTimestamps.swift:176-184): the memory
+                                  frame at which the DTW path enters each call's row */
+    int32_t cap;               /* capacity of ids, token_probs and jump_frames */
+    int32_t reserved0;
+    float* attn_rows;          /* nullable [attn_cap]: per decoder call, the mean over layers and
+                                  heads of the cross-attention softmax over memory frames,
+                                  row-major [n_steps][n_frames] (:106-130) */
+    float* attn_filtered;      /* nullable [attn_cap]: the same rows z-scored and median-filtered
+                                  (:132-146); the DTW cost is their negation */
+    int64_t attn_cap;          /* floats in each of attn_rows / attn_filtered */
+    int32_t n_tokens;          /* out: ids */
+    int32_t n_steps;           /* out: decoder calls = attention rows = jump frames
+                                  (n_tokens, plus one when the last call produced EOS) */
+    int32_t n_frames;          /* out: memory frames (numFrames) */
+    int32_t hit_eos;           /* out */
+} ms_alignment;
+
+/* generateWithWordTimestamps(audio:maxTokens:timeOffset:) (MoonshineModel.swift:241-316) up
+ * to the tokenizer: the whole audio is encoded in one pass, then greedy decoding of up to
+ * min(max_tokens, ceil(seconds * 6.5)) decoder calls stops at EOS (max_tokens <= 0: no
+ * cap).  Every call's cross-attention queries are kept on the device; afterwards the GPU
+ * rebuilds the attention rows, z-scores and median-filters them (medfilt_width, the
+ * reference's 7; <= 1 disables the filter, at most 63), and the DTW path over them gives
+ * jump_frames.  Grouping ids into words needs the tokenizer and stays with the caller, who
+ * passes the word boundaries to ms_word_timings.  The audio's memory must fit the
+ * positional table (max_position_embeddings frames). */
+ms_status ms_generate_alignment(ms_model* model, const float* audio, int64_t n_samples,
+                                int32_t max_tokens, int32_t medfilt_width, ms_alignment* out,
+                                ms_gen_stats* stats);
+
+/* The DTW step of findAlignment on rows the caller holds (host only, no GPU work): dtw
+ * (MoonshineTimestamps.swift:20-65) over cost = -filtered ([n_rows][n_frames], row-major),
+ * then the jump extraction (:176-184).  jump_frames_out receives n_rows frames. */
+ms_status ms_alignment_jump_frames(const float* filtered, int32_t n_rows, int32_t n_frames,
+                                   int32_t* jump_frames_out);
+
+/* Word timings of findAlignment (MoonshineTimestamps.swift:186-239) for words given by the
+ * index of their first token (word_first, ascending; word w covers tokens
+ * [word_first[w], word_first[w+1]) and the last word ends at n_tokens; the reference starts
+ * a word at every token whose piece begins with U+2581).  start_out/end_out are seconds
+ * (time_offset + frame * 0.02, rounded to 1 ms; overlapping neighbours meet at the rounded
+ * midpoint), prob_out the mean token probability rounded to 1e-4.  Each output is
+ * [n_words]; *n_out receives the number of words written. */
+ms_status ms_word_timings(const int32_t* jump_frames, int32_t n_jumps, const float* token_probs,
+                          int32_t n_probs, const int32_t* word_first, int32_t n_words,
+                          int32_t n_tokens, int32_t n_frames, double time_offset,
+                          double* start_out, double* end_out, double* prob_out, int32_t* n_out);
+
 /* ------------------------------------------------------------------- streaming */
 
 /* StreamingConfig (MoonshineStreaming.swift:47-62), plus one field of this build. */

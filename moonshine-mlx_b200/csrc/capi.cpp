@@ -6,6 +6,7 @@
 #include <string>
 
 #include "../../include/moonshine_b200.h"
+#include "runtime/alignment.hpp"
 #include "runtime/model.hpp"
 #include "runtime/batch.hpp"
 #include "runtime/stream.hpp"
@@ -342,6 +343,160 @@ ms_status ms_generate_long(ms_model* model, const float* audio, int64_t n_sample
         if (stats) *stats = st;
         *n_out = n;
         if (n > cap) return fail(MS_ERR_CAPACITY, "ids buffer too small");
+        return MS_OK;
+    });
+}
+
+ms_status ms_generate_alignment(ms_model* model, const float* audio, int64_t n_samples, int32_t max_tokens,
+                                int32_t medfilt_width, ms_alignment* out, ms_gen_stats* stats) {
+    return guarded([&]() -> ms_status {
+        if (!model || !out) return fail(MS_ERR_INVALID_ARG, "model and out must be non-null");
+        if (n_samples < 0 || (n_samples > 0 && !audio)) return fail(MS_ERR_INVALID_ARG, "bad audio buffer");
+        if (out->cap < 0 || (out->cap > 0 && (!out->ids || !out->token_probs || !out->jump_frames)))
+            return fail(MS_ERR_INVALID_ARG, "ids, token_probs and jump_frames must hold cap entries");
+        if (out->attn_cap < 0) return fail(MS_ERR_INVALID_ARG, "attn_cap must be >= 0");
+        if (medfilt_width > alignment_max_median_width())
+            return fail(MS_ERR_INVALID_ARG, "medfilt_width must be at most " +
+                                                std::to_string(alignment_max_median_width()));
+        Model& m = *reinterpret_cast<Model*>(model);
+        std::lock_guard<std::mutex> g(m.mu);
+        MSB_CUDA(cudaSetDevice(m.device));
+        const Config& c = m.cfg;
+        out->n_tokens = out->n_steps = out->n_frames = out->hit_eos = 0;
+        ms_gen_stats st;
+        std::memset(&st, 0, sizeof(st));
+        cudaEvent_t t0, t1, t2;
+        MSB_CUDA(cudaEventCreate(&t0));
+        MSB_CUDA(cudaEventCreate(&t1));
+        MSB_CUDA(cudaEventCreate(&t2));
+        MSB_CUDA(cudaEventRecord(t0, m.stream));
+        // one encode of the whole audio (MoonshineModel.swift:253-256)
+        m.ws.audio.ensure((size_t)std::max<int64_t>(n_samples, 1) * 4);
+        if (n_samples > 0)
+            MSB_CUDA(cudaMemcpyAsync(m.ws.audio.p, audio, (size_t)n_samples * 4, cudaMemcpyHostToDevice, m.stream));
+        const int M = m.encode_device(m.ws.audio.as<float>(), n_samples, 0);
+        st.memory_frames = M;
+        out->n_frames = M;
+        const double dur = (double)n_samples / (double)c.sample_rate;
+        int limit = (int)std::ceil(dur * c.max_tok_per_s);  // :258-259
+        if (max_tokens > 0) limit = std::min(limit, (int)max_tokens);
+        std::vector<int32_t> ids;
+        std::vector<float> probs, filt;
+        int n_steps = 0;
+        if (M > 0 && limit > 0) {
+            m.cross_kv(m.memory_ptr(), M, 0);
+            MSB_CUDA(cudaEventRecord(t1, m.stream));
+            m.ensure_decode(m.ws.m_cap, limit, true, c.vocab);
+            const int HD = c.heads * c.head_dim;
+            m.ws.qtrace.ensure((size_t)limit * c.layers * HD * 4);
+            const void* cst = m.kv_f16 ? m.ws.cross16.p : m.ws.cross32.p;
+            Model::DecodeResult r = m.decode(m.ws.cross32.as<float>(), cst, m.ws.m_cap, M, limit, false, nullptr,
+                                             true, 0.f, 0, m.ws.qtrace.as<float>());
+            n_steps = r.n_calls;
+            st.decode_kernel = r.kernel;
+            st.hit_eos = r.hit_eos ? 1 : 0;
+            if (n_steps > 0) {
+                m.ws.apart.ensure(alignment_part_floats(n_steps, c.layers, M) * 4);
+                m.ws.arows.ensure((size_t)n_steps * M * 4);
+                m.ws.afilt.ensure((size_t)n_steps * M * 4);
+                m.ws.aprobs.ensure((size_t)n_steps * 4);
+                MSB_CUDA(launch_alignment_rows(m.ws.qtrace.as<float>(), m.ws.cross32.as<float>(), cst,
+                                               m.kv_f16 ? 1 : 0, n_steps, c.layers, c.heads, c.kv_heads,
+                                               c.head_dim, m.ws.m_cap, M, std::pow((float)c.head_dim, -0.5f),
+                                               m.ws.logits.as<float>(), m.ws.ids.as<int>(), c.vocab,
+                                               std::max(1, (int)medfilt_width), m.ws.apart.as<float>(),
+                                               m.ws.arows.as<float>(), m.ws.afilt.as<float>(),
+                                               m.ws.aprobs.as<float>(), m.stream));
+                ids.resize(n_steps);
+                probs.resize(n_steps);
+                filt.resize((size_t)n_steps * M);
+                MSB_CUDA(cudaMemcpyAsync(ids.data(), m.ws.ids.p, (size_t)n_steps * 4, cudaMemcpyDeviceToHost,
+                                         m.stream));
+                MSB_CUDA(cudaMemcpyAsync(probs.data(), m.ws.aprobs.p, (size_t)n_steps * 4,
+                                         cudaMemcpyDeviceToHost, m.stream));
+                MSB_CUDA(cudaMemcpyAsync(filt.data(), m.ws.afilt.p, filt.size() * 4, cudaMemcpyDeviceToHost,
+                                         m.stream));
+                const size_t rows_floats = (size_t)n_steps * M;
+                if (out->attn_rows && (int64_t)rows_floats <= out->attn_cap)
+                    MSB_CUDA(cudaMemcpyAsync(out->attn_rows, m.ws.arows.p, rows_floats * 4, cudaMemcpyDeviceToHost,
+                                             m.stream));
+            }
+        } else {
+            MSB_CUDA(cudaEventRecord(t1, m.stream));
+        }
+        MSB_CUDA(cudaStreamSynchronize(m.stream));
+        const int n_tok = n_steps - (st.hit_eos ? 1 : 0);
+        // the reference's DTW and jump extraction (MoonshineTimestamps.swift:148-184)
+        const std::vector<int32_t> jumps = n_tok > 0 ? dtw_jump_frames(filt.data(), n_steps, M)
+                                                     : std::vector<int32_t>();
+        MSB_CUDA(cudaEventRecord(t2, m.stream));
+        MSB_CUDA(cudaEventSynchronize(t2));
+        float te = 0, tt = 0;
+        cudaEventElapsedTime(&te, t0, t1);
+        cudaEventElapsedTime(&tt, t0, t2);
+        cudaEventDestroy(t0);
+        cudaEventDestroy(t1);
+        cudaEventDestroy(t2);
+        out->n_tokens = std::max(n_tok, 0);
+        out->n_steps = n_steps;
+        out->hit_eos = st.hit_eos;
+        const size_t rows_floats = (size_t)n_steps * M;
+        if (out->attn_filtered && (int64_t)rows_floats <= out->attn_cap)
+            std::memcpy(out->attn_filtered, filt.data(), rows_floats * 4);
+        if (n_steps > out->cap) return fail(MS_ERR_CAPACITY, "ids / token_probs / jump_frames hold fewer than " +
+                                                              std::to_string(n_steps) + " entries");
+        for (int k = 0; k < out->n_tokens; ++k) out->ids[k] = ids[k];
+        for (int k = 0; k < n_steps; ++k) out->token_probs[k] = probs[k];
+        for (size_t k = 0; k < jumps.size(); ++k) out->jump_frames[k] = jumps[k];
+        st.n_tokens = out->n_tokens;
+        st.n_chunks = 1;
+        st.encode_ms = te;
+        st.decode_ms = tt - te;
+        st.total_ms = tt;
+        st.tokens_per_second = tt > 0 ? out->n_tokens / (tt / 1000.0) : 0.0;
+        if (stats) *stats = st;
+        if ((out->attn_rows || out->attn_filtered) && (int64_t)rows_floats > out->attn_cap)
+            return fail(MS_ERR_CAPACITY, "attention buffers hold fewer than " + std::to_string(rows_floats) +
+                                             " floats");
+        return MS_OK;
+    });
+}
+
+ms_status ms_alignment_jump_frames(const float* filtered, int32_t n_rows, int32_t n_frames,
+                                   int32_t* jump_frames_out) {
+    return guarded([&]() -> ms_status {
+        if (n_rows < 0 || n_frames < 0) return fail(MS_ERR_INVALID_ARG, "negative size");
+        if (n_rows > 0 && n_frames > 0 && (!filtered || !jump_frames_out))
+            return fail(MS_ERR_INVALID_ARG, "null buffer");
+        const std::vector<int32_t> j = dtw_jump_frames(filtered, n_rows, n_frames);
+        for (size_t k = 0; k < j.size(); ++k) jump_frames_out[k] = j[k];
+        return MS_OK;
+    });
+}
+
+ms_status ms_word_timings(const int32_t* jump_frames, int32_t n_jumps, const float* token_probs, int32_t n_probs,
+                          const int32_t* word_first, int32_t n_words, int32_t n_tokens, int32_t n_frames,
+                          double time_offset, double* start_out, double* end_out, double* prob_out,
+                          int32_t* n_out) {
+    return guarded([&]() -> ms_status {
+        if (n_jumps < 0 || n_probs < 0 || n_words < 0 || n_tokens < 0 || !n_out)
+            return fail(MS_ERR_INVALID_ARG, "negative count or null n_out");
+        if ((n_jumps && !jump_frames) || (n_probs && !token_probs) || (n_words && !word_first) ||
+            (n_words && (!start_out || !end_out || !prob_out)))
+            return fail(MS_ERR_INVALID_ARG, "null buffer");
+        for (int w = 0; w < n_words; ++w)
+            if (word_first[w] < 0 || word_first[w] >= n_tokens || (w && word_first[w] <= word_first[w - 1]))
+                return fail(MS_ERR_INVALID_ARG, "word_first must ascend strictly within [0, n_tokens)");
+        *n_out = 0;
+        if (n_tokens == 0) return MS_OK;  // the reference returns no words without tokens (:104)
+        const std::vector<WordTime> wt = word_times(jump_frames, n_jumps, token_probs, n_probs, word_first, n_words,
+                                                    n_tokens, n_frames, time_offset);
+        for (size_t k = 0; k < wt.size(); ++k) {
+            start_out[k] = wt[k].start;
+            end_out[k] = wt[k].end;
+            prob_out[k] = wt[k].probability;
+        }
+        *n_out = (int32_t)wt.size();
         return MS_OK;
     });
 }

@@ -544,7 +544,10 @@ __global__ void __launch_bounds__(NT, 1) decode_b1_kernel(DecodeParams p) {
                 int k = 0;
                 for (int r = gw; r < HD; r += NW, ++k) {
                     const float v = sdot(reg + (size_t)k * d, hs, d, lane);
-                    if (lane == 0) p.qc[r] = v;
+                    if (lane == 0) {
+                        p.qc[r] = v;
+                        if (p.qc_trace) p.qc_trace[((size_t)step * L + l) * HD + r] = v;
+                    }
                 }
             }
             __syncwarp();

@@ -735,6 +735,9 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
                     const int i = e / CL, q = e - (e / CL) * CL;
                     st_dsmem(mapa_rank(qc_a + 4 * (r * gm.rcq + row0 + i), q), gres[i]);
                 }
+                if (p.qc_trace)
+                    for (int i = tid; i < nr; i += NT)
+                        p.qc_trace[((size_t)step * L + l) * H * HDT + c * HDT + r * gm.rcq + row0 + i] = gres[i];
             });
             cbar();
             stamp();

@@ -165,6 +165,7 @@ struct DecodeParams {
     int eos;
     int* ids_out;         // [n_steps]
     float* logits_out;    // nullable [n_steps, V]
+    float* qc_trace;      // nullable [n_steps][L][H*hd]: every decoder call's cross-attention queries
     int* n_done;          // decoder calls completed
     int* hit_eos;
     unsigned* bar_count;
@@ -216,6 +217,17 @@ cudaError_t pack_cluster_weights(const ClusterGeom& g, const DecodeLayerW* layer
                                  const float* final_ln, int d, int H, int hd, int I, int V, float* packed,
                                  cudaStream_t s);
 cudaError_t launch_decode_cluster(const DecodeParams& p, const ClusterGeom& g, cudaStream_t stream);
+
+// Word-timestamp alignment rows from the cross queries a decode stored (qc_trace) and the
+// cross K it read: raw_out (nullable) and filt_out [n_steps][M] are the head/layer-mean
+// softmax rows and their z-scored, median-filtered (width) form; probs [n_steps] the softmax
+// probability of ids[s] under logits [n_steps][V].  part: alignment_part_floats scratch.
+int alignment_max_median_width();
+size_t alignment_part_floats(int n_steps, int L, int M);
+cudaError_t launch_alignment_rows(const float* qc_trace, const float* cross32, const void* cross_stored, int st_f16,
+                                  int n_steps, int L, int H, int KVH, int hd, int m_cap, int M, float scale,
+                                  const float* logits, const int* ids, int V, int width, float* part, float* raw_out,
+                                  float* filt_out, float* probs, cudaStream_t s);
 
 // Persistent cooperative decode kernel: runs up to n_steps greedy decoder calls.
 cudaError_t launch_decode_b1(const DecodeParams& p, int grid, cudaStream_t stream);

@@ -738,7 +738,7 @@ bool Model::prepare_cluster_decode() {
 
 Model::DecodeResult Model::decode(const float* cross32, const void* cross_stored, int m_cap, int M,
                                   int n_steps, bool forced, const int* teacher_dev, bool logits, float temperature,
-                                  unsigned seed) {
+                                  unsigned seed, float* qc_trace) {
     const Config& c = cfg;
     ensure_rope(n_steps + 1);
     DecodeParams p{};
@@ -786,6 +786,7 @@ Model::DecodeResult Model::decode(const float* cross32, const void* cross_stored
     p.eos = c.eos;
     p.ids_out = ws.ids.as<int>();
     p.logits_out = logits ? ws.logits.as<float>() : nullptr;
+    p.qc_trace = qc_trace;
     unsigned* flags = ws.flags.as<unsigned>();
     p.bar_count = flags;
     p.status = flags + 1;

@@ -89,6 +89,7 @@ struct Workspace {
     DevBuf audio, feat1p, feat2p, x, h, qkv, attn, f, memory, memproj;
     DevBuf cross32, cross16, self_k, self_v;
     DevBuf dx, dq, dqc, dkvnew, dps, dpc, dspart, dpart, dg, amax_v, amax_i, ids, logits, flags;
+    DevBuf qtrace, apart, arows, afilt, aprobs;  // word-timestamp alignment
     int m_cap = 0, t_cap = 0;
 };
 
@@ -159,7 +160,7 @@ struct Model {
     // [L][2][KVH][m_cap][hd] (fp32 copy for the first decoder call, stored copy afterwards).
     DecodeResult decode(const float* cross32, const void* cross_stored, int m_cap, int M, int n_steps,
                         bool forced, const int* teacher_dev, bool logits, float temperature = 0.f,
-                        unsigned seed = 0);
+                        unsigned seed = 0, float* qc_trace = nullptr);
     // Cross K/V of `frames` memory rows into explicit buffers at row offset `row0`.
     void cross_kv_into(const float* memory, int frames, int row0, float* out32, void* out16, int m_cap,
                        cudaStream_t s = nullptr);

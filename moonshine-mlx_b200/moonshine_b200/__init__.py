@@ -20,7 +20,7 @@ from __future__ import annotations
 import ctypes as C
 import os
 from dataclasses import dataclass, field
-from typing import List, Optional, Sequence
+from typing import Callable, List, Optional, Sequence
 
 import numpy as np
 
@@ -71,6 +71,14 @@ class _StreamingConfig(C.Structure):
                 ("batch_decode", C.c_int32)]
 
 
+class _Alignment(C.Structure):
+    _fields_ = [("ids", C.POINTER(C.c_int32)), ("token_probs", C.POINTER(C.c_float)),
+                ("jump_frames", C.POINTER(C.c_int32)), ("cap", C.c_int32), ("reserved0", C.c_int32),
+                ("attn_rows", C.POINTER(C.c_float)), ("attn_filtered", C.POINTER(C.c_float)),
+                ("attn_cap", C.c_int64), ("n_tokens", C.c_int32), ("n_steps", C.c_int32),
+                ("n_frames", C.c_int32), ("hit_eos", C.c_int32)]
+
+
 class _ModelConfig(C.Structure):
     _fields_ = [(n, C.c_int32) for n in (
         "hidden_size", "intermediate_size", "num_hidden_layers", "num_attention_heads",
@@ -109,6 +117,12 @@ def _load_lib() -> C.CDLL:
                                         C.POINTER(_GenStats)]),
         "ms_generate_device": (C.c_int, [P, C.c_void_p, C.c_int64, C.POINTER(_GenParams), C.c_void_p,
                                          C.c_int32, i32p, C.POINTER(_GenStats)]),
+        "ms_generate_alignment": (C.c_int, [P, f32p, C.c_int64, C.c_int32, C.c_int32, C.POINTER(_Alignment),
+                                            C.POINTER(_GenStats)]),
+        "ms_word_timings": (C.c_int, [i32p, C.c_int32, f32p, C.c_int32, i32p, C.c_int32, C.c_int32, C.c_int32,
+                                      C.c_double, C.POINTER(C.c_double), C.POINTER(C.c_double),
+                                      C.POINTER(C.c_double), i32p]),
+        "ms_alignment_jump_frames": (C.c_int, [f32p, C.c_int32, C.c_int32, i32p]),
         "ms_model_stream": (C.c_void_p, [P]),
         "ms_decode_memory_static": (C.c_int, [P, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
                                               i32p, i32p]),
@@ -180,6 +194,96 @@ class TranscriptionOutput:
     memory_frames: int = 0
     decode_kernel: str = ""   # batch-1 kernel of the last chunk: "grid" or "cluster"
     logits: Optional[np.ndarray] = None
+    text: str = ""            # generate_with_word_timestamps: decoded text (caller's tokenizer)
+    segments: list = field(default_factory=list)
+
+
+@dataclass
+class WordTiming:
+    """WordTiming (MoonshineTimestamps.swift:9-15)."""
+    word: str
+    tokens: List[int]
+    start: float
+    end: float
+    probability: float
+
+
+@dataclass
+class TranscriptionSegment:
+    """TranscriptionSegment (MoonshineModel.swift:16-21)."""
+    text: str
+    start: float
+    end: float
+    words: List[WordTiming] = field(default_factory=list)
+
+
+@dataclass
+class Alignment:
+    """Everything ms_generate_alignment returns: ids (EOS excluded), one probability and
+    one jump frame per decoder call, and optionally the attention rows."""
+    ids: List[int]
+    token_probs: np.ndarray
+    jump_frames: np.ndarray
+    n_frames: int
+    hit_eos: bool
+    attn_rows: Optional[np.ndarray] = None
+    attn_filtered: Optional[np.ndarray] = None
+    stats: Optional[object] = None
+
+
+def _default_piece(t: int) -> str:
+    return ""
+
+
+def _default_decode(ids: Sequence[int]) -> str:
+    # the reference's decodeTokens without a tokenizer (MoonshineModel.swift:320-327)
+    return "".join(chr(t) if t < 128 else f"<{t}>" for t in ids)
+
+
+def alignment_jump_frames(filtered: np.ndarray) -> np.ndarray:
+    """DTW jump frames of z-scored, median-filtered attention rows [n_rows, n_frames]
+    (host-side step of findAlignment, MoonshineTimestamps.swift:148-184)."""
+    f = np.ascontiguousarray(filtered, dtype=np.float32)
+    n, m = (f.shape if f.ndim == 2 else (0, 0))
+    out = np.zeros(max(n, 1), dtype=np.int32)
+    _check(_L().ms_alignment_jump_frames(_fptr(f), n, m, _iptr(out)))
+    return out[: (n if m > 0 else 0)]
+
+
+def word_timings(alignment: "Alignment", token_to_string: Optional[Callable[[int], Optional[str]]] = None,
+                 decode_tokens: Optional[Callable[[Sequence[int]], str]] = None,
+                 time_offset: float = 0.0) -> List[WordTiming]:
+    """Word grouping of findAlignment (MoonshineTimestamps.swift:154-173): a word starts at
+    every token whose piece begins with U+2581; the timing arithmetic runs in the library
+    (ms_word_timings)."""
+    piece = token_to_string or _default_piece
+    dec = decode_tokens or _default_decode
+    toks = alignment.ids
+    if not toks:
+        return []
+    first: List[int] = []
+    for i, t in enumerate(toks):
+        p = piece(t) or ""
+        if not first or (p.startswith("\u2581") and i > first[-1]):
+            first.append(i)
+    nw = len(first)
+    wf = np.asarray(first, dtype=np.int32)
+    jf = np.ascontiguousarray(alignment.jump_frames, dtype=np.int32)
+    pr = np.ascontiguousarray(alignment.token_probs, dtype=np.float32)
+    st, en, pb = (np.zeros(nw, dtype=np.float64) for _ in range(3))
+    n = C.c_int32()
+    dp = C.POINTER(C.c_double)
+    _check(_L().ms_word_timings(_iptr(jf), jf.shape[0], _fptr(pr), pr.shape[0], _iptr(wf), nw, len(toks),
+                                int(alignment.n_frames), float(time_offset), st.ctypes.data_as(dp),
+                                en.ctypes.data_as(dp), pb.ctypes.data_as(dp), C.byref(n)))
+    out = []
+    for w in range(n.value):
+        lo = first[w]
+        hi = first[w + 1] if w + 1 < nw else len(toks)
+        ids = toks[lo:hi]
+        out.append(WordTiming(word=dec(ids).strip(" "), tokens=list(ids), start=float(st[w]), end=float(en[w]),
+                              probability=float(pb[w])))
+    return out
 
 
 @dataclass
@@ -409,6 +513,61 @@ class MoonshineModel:
                                      _iptr(n), C.byref(st)))
         out = [ids[b, : n[b]].tolist() for b in range(B)]
         return (out, st, logits) if return_logits else (out, st)
+
+    def generate_alignment(self, audio, max_tokens: Optional[int] = None, medfilt_width: int = 7,
+                           return_attention: bool = False) -> Alignment:
+        """The GPU part of generateWithWordTimestamps (MoonshineModel.swift:241-316): one
+        encode of the whole audio, greedy decode keeping every call's cross-attention
+        queries, the attention rows (z-scored and median-filtered) and their DTW jump frames."""
+        a = _f32(audio)
+        sr = self.sample_rate
+        cap = int(np.ceil(a.shape[0] / sr * self.config.max_tokens_per_second)) + 2
+        if max_tokens:
+            cap = min(cap, int(max_tokens) + 2)
+        cap = max(cap, 1)
+        frames = a.shape[0] // self.config.enc_frame_len // 4 + 2
+        ids = np.zeros(cap, dtype=np.int32)
+        probs = np.zeros(cap, dtype=np.float32)
+        jumps = np.zeros(cap, dtype=np.int32)
+        al = _Alignment()
+        al.ids, al.token_probs, al.jump_frames, al.cap = _iptr(ids), _fptr(probs), _iptr(jumps), cap
+        rows = filt = None
+        if return_attention:
+            rows = np.zeros(cap * frames, dtype=np.float32)
+            filt = np.zeros(cap * frames, dtype=np.float32)
+            al.attn_rows, al.attn_filtered, al.attn_cap = _fptr(rows), _fptr(filt), rows.shape[0]
+        st = _GenStats()
+        _check(_L().ms_generate_alignment(self._h, _fptr(a), a.shape[0], 0 if max_tokens is None else int(max_tokens),
+                                          int(medfilt_width), C.byref(al), C.byref(st)))
+        ns, M = al.n_steps, al.n_frames
+        out = Alignment(ids=ids[: al.n_tokens].tolist(), token_probs=probs[:ns].copy(),
+                        jump_frames=jumps[: (ns if al.n_tokens else 0)].copy(), n_frames=M,
+                        hit_eos=bool(al.hit_eos), stats=st)
+        if return_attention:
+            out.attn_rows = rows[: ns * M].reshape(ns, M).copy()
+            out.attn_filtered = filt[: ns * M].reshape(ns, M).copy()
+        return out
+
+    def generate_with_word_timestamps(self, audio, max_tokens: Optional[int] = None, time_offset: float = 0.0,
+                                      token_to_string: Optional[Callable[[int], Optional[str]]] = None,
+                                      decode_tokens: Optional[Callable[[Sequence[int]], str]] = None):
+        """generateWithWordTimestamps(audio:maxTokens:timeOffset:) (MoonshineModel.swift:241-316).
+        Returns (TranscriptionOutput, [WordTiming]); the output's ``segments`` holds one
+        TranscriptionSegment over the whole audio."""
+        a = _f32(audio)
+        al = self.generate_alignment(a, max_tokens)
+        words = word_timings(al, token_to_string, decode_tokens, time_offset)
+        dec = decode_tokens or _default_decode
+        text = dec(al.ids).strip(" ")
+        st = al.stats
+        dur = a.shape[0] / float(self.sample_rate)
+        out = TranscriptionOutput(tokens=al.ids, generation_tokens=len(al.ids), total_time=st.total_ms / 1000.0,
+                                  tokens_per_second=st.tokens_per_second, encode_ms=st.encode_ms,
+                                  decode_ms=st.decode_ms, hit_eos=al.hit_eos, memory_frames=al.n_frames,
+                                  decode_kernel=DECODE_KERNEL_NAMES.get(st.decode_kernel, ""))
+        out.text = text
+        out.segments = [TranscriptionSegment(text=text, start=0.0, end=dur, words=words)]
+        return out, words
 
     def encode(self, audio) -> np.ndarray:
         """Memory = prepareMemory(encoder(embedder(audio))) for one chunk, [frames, hidden]."""

@@ -379,10 +379,12 @@ class Oracle:
     def new_cache(self, memory, kv_fp16: bool):
         return DecoderCache(self, memory, kv_fp16)
 
-    def decoder_step(self, token: int, cache: "DecoderCache"):
+    def decoder_step(self, token: int, cache: "DecoderCache", cross_qk: Optional[list] = None):
         """One decoder call for a single token (MoonshineDecoder.swift:55-85 with
         DecoderLayer MoonshineLayers.swift:350-379); returns final hidden state and
-        logits (MoonshineModel.swift:71-85)."""
+        logits (MoonshineModel.swift:71-85).  ``cross_qk`` (a list) receives each layer's
+        cross-attention scores q.K^T * scale, [H, M] (returnCrossQK,
+        MoonshineDecoder.swift:65-81, MoonshineLayers.swift:150-154)."""
         cfg, w = self.cfg, self.w
         H, hd = cfg.num_attention_heads, cfg.head_dim
         KVH = cfg.num_key_value_heads
@@ -415,6 +417,9 @@ class Oracle:
             else:
                 Kc, Vc = cache.cross_k[i], cache.cross_v[i]
             oc = self._attend(qc, Kc, Vc, rep)
+            if cross_qk is not None:
+                Kr = np.repeat(Kc, rep, axis=0) if rep > 1 else Kc
+                cross_qk.append(np.einsum("hd,hsd->hs", qc, Kr) * self.scale)
             x = x + oc @ w[p + "encoder_attn.o_proj.weight"].T
             # SwiGLU MLP: first half value, second half gate (KernelFusion.swift:90-113)
             h = _layer_norm(x, w[p + "final_layernorm.weight"])
@@ -528,6 +533,169 @@ class Oracle:
             else:
                 start = end
         return segments
+
+    # ------------------------------------------------------------ word timestamps (f2)
+    def generate_with_alignment(self, audio, max_tokens: Optional[int] = None, kv_fp16: bool = True,
+                                medfilt_width: int = 7):
+        """generateWithWordTimestamps (MoonshineModel.swift:241-316) up to the tokenizer: one
+        encode of the whole audio, greedy decoding with every call's cross scores kept, EOS
+        break after the call's probability is recorded.  Returns a dict with ids (EOS
+        excluded), token_probs (one per call), attn_rows (layer/head-mean softmax rows),
+        filtered (z-scored + median-filtered rows), jump_frames and n_frames."""
+        a = np.asarray(audio, dtype=np.float32).reshape(-1)
+        mem = self.memory_for(a)
+        M = mem.shape[0]
+        limit = self.token_limit(a.shape[0], max_tokens)  # :258-259
+        cfg = self.cfg
+        ids: List[int] = []
+        probs: List[float] = []
+        qk_steps: List[list] = []
+        hit = False
+        if M > 0:
+            cache = self.new_cache(mem, kv_fp16)
+            tok = cfg.decoder_start_token_id
+            for _ in range(limit):  # :266-287
+                qk: list = []
+                _, lg = self.decoder_step(tok, cache, cross_qk=qk)
+                qk_steps.append(qk)
+                nt = int(np.argmax(lg))
+                probs.append(float(_softmax(lg)[nt]))
+                if nt == cfg.eos_token_id:
+                    hit = True
+                    break
+                ids.append(nt)
+                tok = nt
+        rows = attention_rows(qk_steps, M)
+        filt = median_filter_rows(zscore_rows(rows), medfilt_width)
+        jumps = dtw_jump_frames(-filt) if ids and M > 0 else np.zeros(0, dtype=np.int64)
+        return {"ids": ids, "token_probs": np.asarray(probs), "attn_rows": rows, "filtered": filt,
+                "jump_frames": jumps, "n_frames": M, "hit_eos": hit}
+
+
+def attention_rows(qk_steps: List[list], n_frames: int) -> np.ndarray:
+    """findAlignment :106-130: per decoder call, the mean over layers of the head-mean
+    softmax over frames of each layer's cross scores."""
+    out = np.zeros((len(qk_steps), n_frames))
+    for s, layers in enumerate(qk_steps):
+        acc = np.zeros(n_frames)
+        for qk in layers:
+            acc += _softmax(np.asarray(qk, dtype=np.float64), axis=-1).mean(axis=0)[:n_frames]
+        if layers:
+            acc /= len(layers)
+        out[s] = acc
+    return out
+
+
+def zscore_rows(rows: np.ndarray) -> np.ndarray:
+    """findAlignment :132-139: (row - mean) / (population std + 1e-6) per row."""
+    rows = np.asarray(rows, dtype=np.float64)
+    if rows.size == 0:
+        return rows.copy()
+    mean = rows.mean(axis=1, keepdims=True)
+    std = np.sqrt(((rows - mean) ** 2).mean(axis=1, keepdims=True)) + 1e-6
+    return (rows - mean) / std
+
+
+def median_filter_1d(x: np.ndarray, width: int) -> np.ndarray:
+    """medianFilter1D (MoonshineTimestamps.swift:68-80): window clipped at the ends, element
+    count/2 of the sorted window (the upper median of an even window)."""
+    x = np.asarray(x)
+    if width <= 1 or x.size == 0:
+        return x.copy()
+    half = width // 2
+    out = np.empty_like(x)
+    n = x.shape[0]
+    for i in range(n):
+        w = np.sort(x[max(0, i - half):min(n - 1, i + half) + 1])
+        out[i] = w[w.shape[0] // 2]
+    return out
+
+
+def median_filter_rows(rows: np.ndarray, width: int) -> np.ndarray:
+    return np.stack([median_filter_1d(r, width) for r in rows]) if len(rows) else np.asarray(rows).copy()
+
+
+def dtw_path(cost: np.ndarray) -> Tuple[List[int], List[int]]:
+    """dtw (MoonshineTimestamps.swift:20-65) in float32: diagonal wins ties, then vertical
+    (skip text), then horizontal (skip time); backtrace from (N, M)."""
+    cost = np.asarray(cost, dtype=np.float32)
+    N, M = cost.shape
+    if N == 0 or M == 0:
+        return [], []
+    inf = np.float32(np.inf)
+    D = np.full((N + 1, M + 1), inf, dtype=np.float32)
+    T = np.full((N + 1, M + 1), -1, dtype=np.int8)
+    D[0, 0] = 0.0
+    for i in range(1, N + 1):  # row order gives the same costs as the reference's column order
+        for j in range(1, M + 1):
+            c0, c1, c2 = D[i - 1, j - 1], D[i - 1, j], D[i, j - 1]
+            if c0 <= c1 and c0 <= c2:
+                c, t = c0, 0
+            elif c1 <= c2:
+                c, t = c1, 1
+            else:
+                c, t = c2, 2
+            D[i, j] = np.float32(cost[i - 1, j - 1] + c)
+            T[i, j] = t
+    T[0, :] = 2
+    T[:, 0] = 1
+    i, j = N, M
+    path = []
+    while i > 0 or j > 0:
+        path.append((i - 1, j - 1))
+        t = T[i, j]
+        if t == 0:
+            i, j = i - 1, j - 1
+        elif t == 1:
+            i -= 1
+        else:
+            j -= 1
+    path.reverse()
+    return [p[0] for p in path], [p[1] for p in path]
+
+
+def dtw_jump_frames(cost: np.ndarray) -> np.ndarray:
+    """findAlignment :148-184: DTW path, then the time index at each change of text index."""
+    text, time = dtw_path(cost)
+    jumps = [time[k] for k in range(len(text)) if k == 0 or text[k] != text[k - 1]]
+    return np.asarray(jumps, dtype=np.int64)
+
+
+def word_timings(jump_frames, token_probs, word_first: List[int], n_tokens: int, n_frames: int,
+                 time_offset: float = 0.0) -> List[Tuple[float, float, float]]:
+    """findAlignment :186-239 for words given by their first token index: (start, end,
+    probability) with the reference's rounding (Swift .rounded(): half away from zero) and
+    the midpoint fix of overlapping neighbours."""
+    def rnd(x, unit):
+        v = abs(x) * unit
+        f = math.floor(v)
+        r = f + 1 if v - f >= 0.5 else f
+        return (r if x >= 0 else -r) / unit
+
+    jumps = [int(j) for j in jump_frames]
+    probs = [float(p) for p in token_probs]
+    out = []
+    if n_tokens == 0:
+        return out
+    for w, first in enumerate(word_first):
+        last = (word_first[w + 1] if w + 1 < len(word_first) else n_tokens) - 1
+        sf = jumps[first] if first < len(jumps) else (jumps[-1] if jumps else 0)
+        ef = jumps[last + 1] if last + 1 < len(jumps) else (jumps[-1] if jumps else n_frames)
+        ps = np.float32(0.0)
+        cnt = 0
+        for k in range(first, last + 1):
+            if k < len(probs):
+                ps = np.float32(ps + np.float32(probs[k]))
+                cnt += 1
+        avg = float(ps) / cnt if cnt else 1.0
+        out.append([rnd(time_offset + sf * 0.02, 1000.0), rnd(time_offset + ef * 0.02, 1000.0),
+                    rnd(avg, 10000.0)])
+    for k in range(1, len(out)):
+        if out[k - 1][1] > out[k][0]:
+            mid = rnd((out[k - 1][1] + out[k][0]) / 2.0, 1000.0)
+            out[k - 1][1] = mid
+            out[k][0] = mid
+    return [tuple(o) for o in out]
 
 
 class DecoderCache:
