@@ -219,6 +219,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-timestamps", action="store_true", help="skip the word-timestamp leg")
     ap.add_argument("--seconds", type=float, default=30.0, help="audio length (profiling cases)")
     ap.add_argument("--tokens", type=int, default=200, help="forced decode length (profiling cases)")
     ap.add_argument("--flush-mb", type=int, default=512, help="L2-flush buffer written between steps")
@@ -320,6 +321,30 @@ def main():
     barrier()
     t_e2e = sum(a.elapsed_time(b) for a, b in e2e_evs)
 
+    # ---- word timestamps (generateWithWordTimestamps) on the same audio, host buffers: the
+    # greedy decode with the cross queries kept, the attention-row kernels and the host DTW,
+    # against a plain greedy generate of the same number of decoder calls
+    ts = None
+    if not args.no_timestamps:
+        al = model.generate_alignment(host_audio)
+        n_calls = len(al.token_probs)
+        t_al, t_gen = [], []
+        for k in range(3):
+            for fn, acc in ((lambda: model.generate_alignment(host_audio), t_al),
+                            (lambda: model.generate(host_audio, forced_len=n_calls), t_gen)):
+                with torch.cuda.stream(stream):
+                    flush.fill_(k & 0xFF)
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                fn()
+                torch.cuda.synchronize()
+                acc.append((time.perf_counter() - t0) * 1e3)
+        ts = {"decoder_calls": n_calls, "memory_frames": al.n_frames,
+              "ms_per_call": round(statistics.median(t_al), 3),
+              "generate_same_calls_ms": round(statistics.median(t_gen), 3),
+              "overhead_ms": round(statistics.median(t_al) - statistics.median(t_gen), 3),
+              "timing": "host wall clock around the public call (median of 3), L2 flushed before each"}
+
     if dist is not None:
         t = torch.tensor([t_rank, t_e2e], dtype=torch.float64, device=f"cuda:{local}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -358,6 +383,8 @@ def main():
                     "h2d_bytes_per_step": N_SAMPLES * 4, "d2h_bytes_per_step": FORCED * 4 + 16},
             "clocks": clocks.summary(),
         }
+        if ts is not None:
+            line["word_timestamps"] = ts
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_oracle()
         print(json.dumps(line), flush=True)

@@ -63,9 +63,10 @@ typedef struct {
     int32_t kv_dtype;        /* ms_kv_dtype; default MS_KV_F16 like prepareForInference */
     int32_t weight_dtype;    /* ms_weight_dtype */
     int32_t max_batch;       /* largest ms_generate_batch / stream batch (default 64) */
-    int32_t decode_kernel;   /* batch-1 decode kernel: MS_DECODE_AUTO (head-clustered when the
-                                dims and the GPU allow it) or MS_DECODE_GRID (single-grid
-                                persistent kernel).  Both compute the same greedy loop. */
+    int32_t decode_kernel;   /* batch-1 decode kernel: MS_DECODE_AUTO or MS_DECODE_CLUSTER
+                                (head-clustered when the dims and the GPU allow it, else
+                                single-grid) or MS_DECODE_GRID (single-grid persistent kernel).
+                                Both compute the same greedy loop. */
     int32_t reserved[7];
 } ms_options;
 

@@ -108,6 +108,23 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         : "memory");
 }
 
+// bulk_load with an L2 eviction-priority policy (from make_l2_policy) attached.
+__device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                               uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+        "%4;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// L2 policy: a fraction `keep` of the accessed lines evict_last, the others evict_first.
+__device__ __forceinline__ uint64_t make_l2_policy(float keep) {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.L2::evict_first.b64 %0, %1;" : "=l"(pol) : "f"(keep));
+    return pol;
+}
+
 // Gumbel(0, 1) noise for temperature sampling by the Gumbel-max trick (the argmax of
 // logit / T + g over the vocabulary is a draw from softmax(logit / T); Gumbel 1954, used
 // for sampling by Maddison, Tarlow and Minka 2014).  The uniform comes from a counter-based

@@ -36,6 +36,7 @@
 #include <algorithm>
 #include <type_traits>
 
+#include "cluster_common.cuh"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -44,197 +45,8 @@ namespace msb {
 namespace {
 
 constexpr int CL = 8;         // CTAs per cluster (one cluster per head)
-constexpr int NW = 8;         // warps per CTA
-constexpr int NT = NW * 32;   // threads per CTA
 constexpr int NSLOT = 3;      // weight-stream ring slots
 constexpr uint64_t GSYNC_TIMEOUT_NS = 2000000000ull;
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t cluster_index() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t mapa_rank(uint32_t local, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ void st_dsmem(uint32_t addr, float v) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-__device__ __forceinline__ void st_dsmem_i(uint32_t addr, int v) {
-    asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
-}
-__device__ __forceinline__ float ld_dsmem(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-    return v;
-}
-// 64-bit exchange words: (tag << 32) | payload.  One aligned 8-byte access is single-copy
-// atomic, so a reader that sees the expected tag also sees its payload; no fence is needed.
-__device__ __forceinline__ void st_tagged(unsigned long long* p, unsigned tag, uint32_t payload) {
-    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(((unsigned long long)tag << 32) | payload)
-                 : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void cluster_barrier() {
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cp16(void* s, const void* g) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(s)), "l"(g) : "memory");
-}
-
-// res[i] = rows[i][0 : rf) . vec for i < nr (nr <= 64, row i at rows + i * rs).  Long rows
-// split their columns over the eight warps with lanes owning rows (rs / 4 odd, so the eight
-// lanes of one 128-bit phase read eight different bank groups) and a per-row sum of the
-// warp partials in fixed order; short rows take one thread each.  Ends with a barrier.
-__device__ __noinline__ void block_gemv(const float* rows, int nr, int rf, int rs, const float* vec, float* part,
-                                        float* res) {
-    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-    const int c4 = rf >> 2;
-    const float4* v4 = reinterpret_cast<const float4*>(vec);
-    if (c4 >= 4 * NW) {
-        const int per = (c4 + NW - 1) / NW;
-        const int k0 = w * per, k1 = min(c4, k0 + per);
-        for (int i = lane; i < nr; i += 32) {
-            const float4* row = reinterpret_cast<const float4*>(rows + (size_t)i * rs);
-            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-            int k = k0;
-#pragma unroll 2
-            for (; k + 1 < k1; k += 2) {
-                const float4 x = row[k], y = row[k + 1], u = v4[k], v = v4[k + 1];
-                a0 = fmaf(x.x, u.x, a0);
-                a1 = fmaf(x.y, u.y, a1);
-                a2 = fmaf(x.z, u.z, a2);
-                a3 = fmaf(x.w, u.w, a3);
-                a0 = fmaf(y.x, v.x, a0);
-                a1 = fmaf(y.y, v.y, a1);
-                a2 = fmaf(y.z, v.z, a2);
-                a3 = fmaf(y.w, v.w, a3);
-            }
-            if (k < k1) {
-                const float4 x = row[k], u = v4[k];
-                a0 = fmaf(x.x, u.x, a0);
-                a1 = fmaf(x.y, u.y, a1);
-                a2 = fmaf(x.z, u.z, a2);
-                a3 = fmaf(x.w, u.w, a3);
-            }
-            part[w * 64 + i] = (a0 + a1) + (a2 + a3);
-        }
-        __syncthreads();
-        for (int i = tid; i < nr; i += NT) {
-            float sum = 0.f;
-#pragma unroll
-            for (int q = 0; q < NW; ++q) sum += part[q * 64 + i];
-            res[i] = sum;
-        }
-    } else {
-        for (int i = tid; i < nr; i += NT) {
-            const float4* row = reinterpret_cast<const float4*>(rows + (size_t)i * rs);
-            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-            for (int k = 0; k < c4; ++k) {
-                const float4 x = row[k], u = v4[k];
-                a0 = fmaf(x.x, u.x, a0);
-                a1 = fmaf(x.y, u.y, a1);
-                a2 = fmaf(x.z, u.z, a2);
-                a3 = fmaf(x.w, u.w, a3);
-            }
-            res[i] = (a0 + a1) + (a2 + a3);
-        }
-    }
-    __syncthreads();
-}
-
-// Cross-attention key scoring layout (as the batched streaming kernel): G lanes per key,
-// 16 bytes of the key row per lane.
-template <int HDT, bool F16>
-struct KeyShape {
-    static constexpr int ESZ = F16 ? 2 : 4;
-    static constexpr int NE = HDT * ESZ / 16;
-    static constexpr int EP = 16 / ESZ;
-    static constexpr int G = NE <= 4 ? 4 : (NE <= 8 ? 8 : 16);
-    static constexpr int KPP = 32 / G;
-};
-
-// One warp's pass over keys [k0, k1) of a shared-memory K/V block (rows of HDT elements):
-// scores with the grouped-lane layout, online softmax into (m, l), V accumulation into
-// (a0, a1) = dims (2 lane, 2 lane + 1).  `qr` is this lane's q slice, `sc` 32 floats.
-struct QSlice {
-    float v[8];
-};
-
-template <int HDT, bool F16>
-__device__ __noinline__ float4 attend_keys(const void* kblk, const void* vblk, int k0, int k1, QSlice q,
-                                           float scale, float* sc, float4 st, int lane) {
-    const float* qr = q.v;
-    float m = st.x, l = st.y, a0 = st.z, a1 = st.w;
-    using S = KeyShape<HDT, F16>;
-    using E = typename std::conditional<F16, __half, float>::type;
-    const E* kb = reinterpret_cast<const E*>(kblk);
-    const E* vb = reinterpret_cast<const E*>(vblk);
-    const int g = lane / S::G, sub = lane - (lane / S::G) * S::G;
-    for (int c0 = k0; c0 < k1; c0 += 32) {
-        const int nk = min(32, k1 - c0);
-        for (int p = 0; p < 32 / S::KPP; ++p) {
-            const int j = p * S::KPP + g;
-            if (p * S::KPP >= nk) break;  // warp-uniform
-            float dot = 0.f;
-            if (j < nk && sub < S::NE) {
-                const uint4 u = *reinterpret_cast<const uint4*>(kb + (size_t)(c0 + j) * HDT + sub * S::EP);
-                if constexpr (F16) {
-                    const __half2* h2 = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-                    for (int t = 0; t < 4; ++t) {
-                        const float2 f = __half22float2(h2[t]);
-                        dot = fmaf(qr[2 * t], f.x, fmaf(qr[2 * t + 1], f.y, dot));
-                    }
-                } else {
-                    const float* f = reinterpret_cast<const float*>(&u);
-#pragma unroll
-                    for (int t = 0; t < 4; ++t) dot = fmaf(qr[t], f[t], dot);
-                }
-            }
-#pragma unroll
-            for (int o = S::G / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(FULL, dot, o);
-            if (sub == 0) sc[j] = (j < nk) ? dot * scale : -INFINITY;
-        }
-        __syncwarp();
-        const float sv = lane < nk ? sc[lane] : -INFINITY;
-        const float mn = fmaxf(m, warp_max(sv));
-        const float pv = (sv == -INFINITY) ? 0.f : expf(sv - mn);
-        const float corr = (m == -INFINITY) ? 0.f : expf(m - mn);
-        l = l * corr + warp_sum(pv);
-        a0 *= corr;
-        a1 *= corr;
-        __syncwarp();
-        sc[lane] = pv;
-        __syncwarp();
-        if (2 * lane < HDT) {
-#pragma unroll 4
-            for (int j = 0; j < nk; ++j) {
-                const float pj = sc[j];
-                float2 v;
-                if constexpr (F16) v = __half22float2(*reinterpret_cast<const __half2*>(vb + (size_t)(c0 + j) * HDT + 2 * lane));
-                else v = *reinterpret_cast<const float2*>(vb + (size_t)(c0 + j) * HDT + 2 * lane);
-                a0 = fmaf(pj, v.x, a0);
-                a1 = fmaf(pj, v.y, a1);
-            }
-        }
-        __syncwarp();
-        m = mn;
-    }
-    return make_float4(m, l, a0, a1);
-}
 
 // ---------------------------------------------------------------- packed stream layout
 // Per CTA and layer, segments in consumption order; each is [header][rows] (GEMV rows padded
@@ -248,7 +60,6 @@ __device__ __noinline__ float4 attend_keys(const void* kblk, const void* vblk, i
 // then after the last layer LM [final_ln (d)][rlm rows x d].
 // GEMV rows are stored rf + 4 floats apart (rf % 8 == 0): an odd number of 16-byte units,
 // so lanes that own consecutive rows read distinct shared-memory bank groups.
-__host__ __device__ inline int row_stride(int rf) { return rf + 4; }
 
 struct Segs {
     size_t qkv, o, cq, co, fc1, fc2, layer;
@@ -266,17 +77,6 @@ __host__ __device__ inline Segs make_segs(const ClusterGeom& g, int d, int hd) {
     s.fc2 = s.fc1 + (size_t)d + 2 * g.gr + (size_t)2 * g.gr * sd;
     s.layer = s.fc2 + (size_t)s.ro4 + (size_t)d * g.gr;
     return s;
-}
-
-// Rows of the next block of a segment (header + rows of rf floats, at most 64 rows, split at
-// whole multiples of `gran` rows, the header only in the first block), or -1 when the
-// segment is exhausted.
-__host__ __device__ inline int next_block_rows(int hdr, int nrows, int rf, int gran, int slot_floats, int row0,
-                                               bool first) {
-    if (!(first && hdr > 0) && row0 >= nrows) return -1;
-    const int cap = slot_floats - (first ? hdr : 0);
-    const int per = max(gran, min(64, cap / rf) / gran * gran);
-    return min(nrows - row0, per);
 }
 
 enum SegId { SEG_QKV = 0, SEG_O, SEG_CQ, SEG_XKV, SEG_CO, SEG_FC1, SEG_FC2, SEG_LM };
@@ -333,11 +133,6 @@ __host__ __device__ inline int blocks_per_step(const ClusterGeom& g, const Segs&
     return n;
 }
 
-struct BlockEnt {
-    const void* s0;
-    const void* s1;
-    uint32_t b0, b1;
-};
 
 template <int HDT>
 __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, ClusterGeom gm) {
@@ -436,14 +231,21 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
     const uint32_t nb0 = (uint32_t)s_nb[0], nb1 = (uint32_t)s_nb[1];
     const uint32_t n_total = p.n_steps > 0 ? nb0 + (uint32_t)(p.n_steps - 1) * nb1 : 0u;
     // issue block n_iss of the whole launch (thread 0; nothing once failed or exhausted)
+    const bool hint = gm.l2_keep > 0.f;
+    const uint64_t l2pol = hint ? make_l2_policy(fminf(gm.l2_keep, 1.f)) : 0ull;
     auto issue_next = [&]() {
         if (n_iss >= n_total || s_failed) return;
         const BlockEnt e = n_iss < nb0 ? s_tab[0][n_iss] : s_tab[1][(n_iss - nb0) % nb1];
         const int slot = n_iss % NSLOT;
         mbar_expect_tx(&full[slot], e.b0 + e.b1);
         unsigned char* dst = ring + (size_t)slot * slot_bytes;
-        bulk_load(dst, e.s0, e.b0, &full[slot]);
-        if (e.b1) bulk_load(dst + e.b0, e.s1, e.b1, &full[slot]);
+        if (hint) {
+            bulk_load_hint(dst, e.s0, e.b0, &full[slot], l2pol);
+            if (e.b1) bulk_load_hint(dst + e.b0, e.s1, e.b1, &full[slot], l2pol);
+        } else {
+            bulk_load(dst, e.s0, e.b0, &full[slot]);
+            if (e.b1) bulk_load(dst + e.b0, e.s1, e.b1, &full[slot]);
+        }
         ++n_iss;
     };
     if (tid == 0)

@@ -209,6 +209,9 @@ struct ClusterGeom {
     unsigned long long* part = nullptr;           // tagged exchange words: [2][H][d] partial sums, then
                                                   // [H * 8][2] per-CTA argmax; zeroed before each launch
     size_t part_words = 0;
+    float l2_keep = 0.f;                          // > 0: this fraction of the streamed weight and
+                                                  // cross K/V lines is loaded L2 evict_last, the rest
+                                                  // evict_first (the stream is re-read every token)
 };
 // false when the dims do not fit the clustered kernel (the caller keeps decode_b1)
 bool cluster_geom(int d, int H, int KVH, int hd, int I, int V, int L, int t_cap, ClusterGeom* g);

@@ -332,15 +332,17 @@ class MoonshineModel:
     def load(path: str, device: int = 0, kv_fp16: bool = True, decode_kernel: str = "auto") -> "MoonshineModel":
         """MoonshineModel.load(from:) for a local directory (MoonshineModel.swift:409-414).
 
-        ``decode_kernel`` picks the batch-1 decode kernel: "auto" (head-clustered when the
-        dims and the GPU allow it) or "grid" (single-grid persistent kernel)."""
-        if decode_kernel not in ("auto", "grid"):
-            raise ValueError("decode_kernel must be 'auto' or 'grid'")
+        ``decode_kernel`` picks the batch-1 decode kernel: "auto" or "cluster" (one 8-CTA
+        cluster per head when the dims and the GPU allow it, else single-grid) or "grid"
+        (single-grid persistent kernel)."""
+        kinds = {"auto": 0, "grid": 1, "cluster": 2}
+        if decode_kernel not in kinds:
+            raise ValueError("decode_kernel must be one of " + ", ".join(kinds))
         o = _Options()
         _L().ms_options_default(C.byref(o))
         o.device = device
         o.kv_dtype = KV_F16 if kv_fp16 else KV_F32
-        o.decode_kernel = 0 if decode_kernel == "auto" else 1
+        o.decode_kernel = kinds[decode_kernel]
         h = C.c_void_p()
         _check(_L().ms_model_load(path.encode(), C.byref(o), C.byref(h)))
         return MoonshineModel(h)

@@ -47,10 +47,10 @@ def _check_against_oracle(al, ref, width=7):
     assert dist.mean() <= 2.0, dist
 
 
-@pytest.mark.parametrize("kernel,kv_fp16", [("grid", True), ("auto", True), ("auto", False), ("grid", False)])
+@pytest.mark.parametrize("kernel,kv_fp16", [("grid", True), ("cluster", True), ("cluster", False), ("grid", False)])
 def test_alignment_matches_oracle(varied_dir, kernel, kv_fp16):
-    """6.6 s of audio: 330 memory frames, ceil(6.6 * 6.5) = 43 decoder calls, through both
-    batch-1 decode kernels (both store the cross queries) and both K/V cache dtypes."""
+    """6.6 s of audio: 330 memory frames, ceil(6.6 * 6.5) = 43 decoder calls, through every
+    batch-1 decode kernel (each stores the cross queries) and both K/V cache dtypes."""
     import moonshine_b200 as mb
     m = mb.MoonshineModel.load(varied_dir, decode_kernel=kernel)
     m.enable_float16_kv_cache(kv_fp16)

@@ -130,14 +130,16 @@ def test_small_arch_head_dim_64(model_root):
         assert_logits_close(out.logits[:16], logits, FP32_LOGIT_TOL)
 
 
-@pytest.mark.parametrize("kernel", ["grid", "auto"])
-def test_both_decode_kernels_30s(tiny_dir, kernel):
+@pytest.mark.parametrize("kernel", ["grid", "cluster", "auto"])
+def test_every_decode_kernel_30s(tiny_dir, kernel):
     """30 s of audio (1500 memory frames), fp16 KV, 48 forced tokens through each batch-1
-    decode kernel: the single-grid one and the head-clustered one ("auto" on a B200)."""
+    decode kernel: single-grid and one 8-CTA cluster per head ("auto" picks the latter on a
+    B200)."""
     import moonshine_b200 as mb
     m = mb.MoonshineModel.load(tiny_dir, decode_kernel=kernel)
     audio = synth.synth_audio(480000, 1)
     out = m.generate(audio, forced_len=48, return_logits=True)
+    assert out.decode_kernel == ("cluster" if kernel == "auto" else kernel)
     o = oracle_for(tiny_dir)
     ids, _, logits, _ = o.greedy(o.memory_for(audio), 48, True, forced_len=48, keep_logits=True)
     assert out.tokens == ids
@@ -187,7 +189,7 @@ def _chi2(counts, p):
     return float(np.sum((counts[keep] - n * p[keep]) ** 2 / (n * p[keep])))
 
 
-@pytest.mark.parametrize("kernel", ["grid", "auto"])
+@pytest.mark.parametrize("kernel", ["grid", "cluster"])
 def test_temperature_sampling_distribution(model_root, kernel):
     """temperature > 0 draws each token from softmax(logits / T) (MLXRandom.categorical,
     MoonshineModel.swift:211-213).  The random streams cannot match MLX's, so the test is
