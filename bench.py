@@ -61,7 +61,7 @@ def decode_bytes_per_launch(cfg, M, n_tokens, kv_bytes=2):
 # memory frames, fp16 KV) from an ncu capture of each batch-1 kernel; per-call traffic is
 # flat after the first call.
 NCU_DECODE_BYTES_16CALLS_1500F = {
-    "cluster": (1462431488 + 3375360, "profiles/decode_cluster_tiny_30s_16tok.md"),
+    "cluster": (854506752 + 3145984, "profiles/decode_cluster_tiny_30s_16tok.md"),
     "grid": (830.744e6 + 5.621e6, "profiles/decode_b1_tiny_30s_16tok.md"),
 }
 DECODE_KERNEL_SYMBOL = {"cluster": "decode_cluster_kernel<40>", "grid": "decode_b1_kernel<40>"}
