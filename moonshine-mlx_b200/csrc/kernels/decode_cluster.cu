@@ -325,6 +325,45 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
         for (int q = 0; q < 16; ++q)
             if (q < n) out[q] = (uint32_t)v[q];
     };
+    // wait_tagged for 8 words at srcA[q * stride] and nb <= 2 at srcB[q * stride], all loads of
+    // both groups in flight together (one L2 round trip when the words are already there)
+    auto wait_tagged_82 = [&](const unsigned long long* srcA, const unsigned long long* srcB, int nb,
+                              size_t stride, unsigned tag, uint32_t* outA, uint32_t* outB) {
+        unsigned long long va[8], vb[2];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) va[q] = ld_tagged(srcA + q * stride);
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+            if (q < nb) vb[q] = ld_tagged(srcB + q * stride);
+        const long long c0 = tr0 ? clock64() : 0;
+        uint64_t t0 = 0;
+        for (;;) {
+            bool done = true;
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                if ((unsigned)(va[q] >> 32) != tag) {
+                    done = false;
+                    va[q] = ld_tagged(srcA + q * stride);
+                }
+#pragma unroll
+            for (int q = 0; q < 2; ++q)
+                if (q < nb && (unsigned)(vb[q] >> 32) != tag) {
+                    done = false;
+                    vb[q] = ld_tagged(srcB + q * stride);
+                }
+            if (done || s_failed) break;
+            if (t0 == 0) t0 = globaltimer_ns();
+            else if (globaltimer_ns() - t0 > GSYNC_TIMEOUT_NS) {
+                fail(DEV_BARRIER_TIMEOUT);
+                break;
+            }
+        }
+        if (tr0) cyc_poll += clock64() - c0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) outA[q] = (uint32_t)va[q];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) outB[q] = q < nb ? (uint32_t)vb[q] : 0u;
+    };
     auto layer_norm = [&](const float* wln) {  // xl = LN(xs) * wln (wln in shared memory)
         float s = 0.f;
         for (int k = lane; k < d; k += 32) s += xs[k];
@@ -342,12 +381,30 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
     // xs += sum over clusters (fixed order) of partial[par][.] of exchange `epoch`
     auto add_partials = [&]() {
         const unsigned long long* pb = gm.part + (size_t)par * H * d;
-        for (int k = tid; k < d; k += NT) {
-            uint32_t u[16];
-            wait_tagged(pb + k, d, H, epoch, u);
-            float v = xs[k];
-            for (int q = 0; q < H; ++q) v += __uint_as_float(u[q]);
-            xs[k] = v;
+        if (H == 8 && d > NT && d - NT <= NT / 4) {
+            // one round of polls: element tid (8 words) and a quarter of element NT + tid / 4
+            // (words 2 (tid % 4), +1), whose four pair sums meet by shuffles in fixed order
+            const int e = d - NT, xi = tid >> 2, qq = (tid & 3) * 2;
+            const bool hasx = xi < e;
+            uint32_t ua[8], ub[2];
+            wait_tagged_82(pb + tid, pb + NT + min(xi, e - 1) + (size_t)qq * d, hasx ? 2 : 0, d, epoch, ua, ub);
+            float v = xs[tid];
+            for (int q = 0; q < 8; ++q) v += __uint_as_float(ua[q]);
+            xs[tid] = v;
+            const float s2 = __uint_as_float(ub[0]) + __uint_as_float(ub[1]);
+            const float o1 = __shfl_xor_sync(FULL, s2, 1);
+            const float pr = (tid & 1) ? o1 + s2 : s2 + o1;  // words 0-3 / 4-7 of the element
+            const float o2 = __shfl_xor_sync(FULL, pr, 2);
+            const float tot = (tid & 2) ? o2 + pr : pr + o2;
+            if (hasx && (tid & 3) == 0) xs[NT + xi] += tot;
+        } else {
+            for (int k = tid; k < d; k += NT) {
+                uint32_t u[16];
+                wait_tagged(pb + k, d, H, epoch, u);
+                float v = xs[k];
+                for (int q = 0; q < H; ++q) v += __uint_as_float(u[q]);
+                xs[k] = v;
+            }
         }
         par ^= 1;
         __syncthreads();
