@@ -257,7 +257,8 @@ ms_status ms_word_timings(const int32_t* jump_frames, int32_t n_jumps, const flo
 
 /* ------------------------------------------------------------------- streaming */
 
-/* StreamingConfig (MoonshineStreaming.swift:47-62), plus one field of this build. */
+/* StreamingConfig (MoonshineStreaming.swift:47-62), plus fields of this build: transcribe's
+ * temperature argument and the seed of its draws. */
 typedef struct {
     int32_t max_memory_frames;   /* default 100000 */
     int32_t min_segment_frames;  /* default 250 */
@@ -265,6 +266,12 @@ typedef struct {
                                     streams of one model in lockstep on bf16 tensor cores;
                                     ids then match a per-stream decode except where the top
                                     two logits are closer than bf16 precision */
+    float temperature;           /* transcribe(temperature:) (:122-128): 0 greedy (default);
+                                    > 0 draws each token from softmax(logits / temperature)
+                                    (decodeMemory, :238-268) by the Gumbel-max trick */
+    int32_t seed;                /* temperature > 0: a draw depends only on (seed, the stream's
+                                    number of transcribe calls so far, step, vocabulary index;
+                                    plus the stream's row in a lockstep batch) */
 } ms_streaming_config;
 
 void ms_streaming_config_default(ms_streaming_config* c);

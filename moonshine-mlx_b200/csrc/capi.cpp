@@ -142,6 +142,8 @@ void ms_streaming_config_default(ms_streaming_config* c) {
     c->max_memory_frames = 100000;
     c->min_segment_frames = 250;
     c->batch_decode = 0;
+    c->temperature = 0.f;
+    c->seed = 0;
 }
 
 const char* ms_last_error(void) { return g_err.c_str(); }
@@ -755,6 +757,7 @@ ms_status ms_stream_transcribe(ms_stream* stream, int32_t is_final, const ms_str
         ms_streaming_config sc;
         ms_streaming_config_default(&sc);
         if (config) sc = *config;
+        if (!(sc.temperature >= 0.f)) return fail(MS_ERR_INVALID_ARG, "temperature must be >= 0");
         const int32_t mt = max_tokens > 0 ? max_tokens : std::numeric_limits<int32_t>::max();
         StreamState* s = reinterpret_cast<StreamState*>(stream);
         std::lock_guard<std::mutex> g(s->model->mu);
@@ -772,6 +775,7 @@ ms_status ms_stream_transcribe_batch(ms_stream* const* streams, int32_t n, int32
         ms_streaming_config sc;
         ms_streaming_config_default(&sc);
         if (config) sc = *config;
+        if (!(sc.temperature >= 0.f)) return fail(MS_ERR_INVALID_ARG, "temperature must be >= 0");
         const int32_t mt = max_tokens > 0 ? max_tokens : std::numeric_limits<int32_t>::max();
         ms_status worst = MS_OK;
         for (int32_t i = 0; i < n; ++i)
@@ -801,7 +805,11 @@ ms_status ms_stream_transcribe_batch(ms_stream* const* streams, int32_t n, int32
             shared->join_lanes(lanes);
             if (!src.empty()) {
                 if (!shared->batch) shared->batch.reset(new BatchEngine(*shared));
-                BatchEngine::Result r = shared->batch->run_cross(src, limits, false);
+                // one seed for the lockstep batch: the rows (stream positions) separate the draws
+                unsigned seed = (unsigned)sc.seed;
+                if (sc.temperature > 0.f)
+                    seed = mix_seed(seed, reinterpret_cast<StreamState*>(streams[rows[0]])->calls - 1);
+                BatchEngine::Result r = shared->batch->run_cross(src, limits, false, sc.temperature, seed);
                 for (size_t k = 0; k < rows.size(); ++k) {
                     const int32_t i = rows[k];
                     std::vector<int32_t> ids(r.ids.begin() + (size_t)k * r.t_cap,

@@ -306,8 +306,9 @@ BatchEngine::Result BatchEngine::run(const std::vector<const float*>& audio_dev,
 }
 
 BatchEngine::Result BatchEngine::run_cross(const std::vector<CrossSrc>& src, const std::vector<int>& limits,
-                                           bool forced) {
-    inv_temp = 0.f;
+                                           bool forced, float temperature, unsigned seed_) {
+    inv_temp = temperature > 0.f ? 1.f / temperature : 0.f;
+    seed = seed_;
     const Config& c = m.cfg;
     const int B = (int)src.size();
     cudaStream_t s = m.stream;

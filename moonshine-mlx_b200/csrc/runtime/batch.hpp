@@ -36,7 +36,8 @@ struct BatchEngine {
         const void* c16;
         int m_cap, frames;
     };
-    Result run_cross(const std::vector<CrossSrc>& src, const std::vector<int>& limits, bool forced);
+    Result run_cross(const std::vector<CrossSrc>& src, const std::vector<int>& limits, bool forced,
+                     float temperature = 0.f, unsigned seed = 0);
 
    private:
     struct LayerB {

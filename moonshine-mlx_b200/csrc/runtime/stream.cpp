@@ -165,7 +165,8 @@ void StreamState::encode_new_frames(bool is_final, EncLane* lane) {  // Moonshin
     memory_len += nnew;
 }
 
-std::pair<std::vector<int32_t>, bool> StreamState::decode_memory(int32_t max_tokens) {
+std::pair<std::vector<int32_t>, bool> StreamState::decode_memory(int32_t max_tokens, float temperature,
+                                                                   unsigned seed) {
     Model& m = *model;
     const Config& c = m.cfg;
     if (memory_len <= 0) return {{}, false};
@@ -176,7 +177,7 @@ std::pair<std::vector<int32_t>, bool> StreamState::decode_memory(int32_t max_tok
     if (max_tok <= 0) throw MsError(MS_ERR_INVALID_ARG, "token limit must be positive");
     m.ensure_decode(memory_len, (int)max_tok, false, c.vocab);
     Model::DecodeResult r = m.decode(cross32.as<float>(), m.kv_f16 ? cross16.p : cross32.p, mem_cap, memory_len,
-                                     (int)max_tok, false, nullptr, false);
+                                     (int)max_tok, false, nullptr, false, temperature, seed);
     const int n_ids = r.n_calls - (r.hit_eos ? 1 : 0);
     std::vector<int32_t> ids((size_t)std::max(n_ids, 0));
     if (n_ids > 0) {
@@ -188,6 +189,7 @@ std::pair<std::vector<int32_t>, bool> StreamState::decode_memory(int32_t max_tok
 
 int64_t StreamState::begin(bool is_final, int32_t max_tokens, Result* done_early, EncLane* lane) {
     // MoonshineStreaming.swift:122-131
+    ++calls;
     encode_new_frames(is_final, lane);
     if (memory_len <= 0) {
         if (is_final) reset_segment();
@@ -229,7 +231,7 @@ StreamState::Result StreamState::transcribe(bool is_final, const ms_streaming_co
     Result early;
     const int64_t max_tok = begin(is_final, max_tokens, &early);
     if (max_tok <= 0) return early;
-    auto dm = decode_memory(max_tokens);
+    auto dm = decode_memory(max_tokens, sc.temperature, mix_seed((unsigned)sc.seed, calls - 1));
     return finish(std::move(dm.first), dm.second, is_final, sc);
 }
 

@@ -8,6 +8,9 @@
 
 namespace msb {
 
+// Seed of a sampled decode: the caller's seed mixed with a call counter.
+inline unsigned mix_seed(unsigned seed, uint32_t call) { return seed ^ (call * 0x9E3779B9u); }
+
 struct StreamState {
     Model* model = nullptr;
     // frontend (persists across segments)
@@ -27,6 +30,7 @@ struct StreamState {
     std::vector<std::vector<int32_t>> emitted;
     bool last_hit_eos = false;
     bool active = false;
+    uint32_t calls = 0;  // transcribe calls so far (separates the draws of successive calls)
 
     explicit StreamState(Model* m);
     void start();
@@ -49,7 +53,7 @@ struct StreamState {
     void reset_segment();
     void encode_new_frames(bool is_final, EncLane* lane = nullptr);
     void ensure_memory(int rows, cudaStream_t s);
-    std::pair<std::vector<int32_t>, bool> decode_memory(int32_t max_tokens);
+    std::pair<std::vector<int32_t>, bool> decode_memory(int32_t max_tokens, float temperature, unsigned seed);
 };
 
 }  // namespace msb

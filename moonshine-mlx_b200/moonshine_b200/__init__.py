@@ -68,7 +68,7 @@ class _GenStats(C.Structure):
 
 class _StreamingConfig(C.Structure):
     _fields_ = [("max_memory_frames", C.c_int32), ("min_segment_frames", C.c_int32),
-                ("batch_decode", C.c_int32)]
+                ("batch_decode", C.c_int32), ("temperature", C.c_float), ("seed", C.c_int32)]
 
 
 class _Alignment(C.Structure):
@@ -293,8 +293,9 @@ class StreamingConfig:
     min_segment_frames: int = 250
     batch_decode: bool = False   # transcribe_batch: lockstep bf16 decode of all streams
 
-    def _c(self) -> _StreamingConfig:
-        return _StreamingConfig(self.max_memory_frames, self.min_segment_frames, 1 if self.batch_decode else 0)
+    def _c(self, temperature: float = 0.0, seed: int = 0) -> _StreamingConfig:
+        return _StreamingConfig(self.max_memory_frames, self.min_segment_frames, 1 if self.batch_decode else 0,
+                                float(temperature), int(seed) & 0x7FFFFFFF)
 
 
 class StreamingState:
@@ -599,11 +600,11 @@ class MoonshineModel:
 
     def transcribe(self, state: StreamingState, is_final: bool = False,
                    streaming_config: Optional[StreamingConfig] = None,
-                   max_tokens: Optional[int] = None, temperature: float = 0.0):
-        """transcribe (MoonshineStreaming.swift:122-168).  Returns (ids, hit_eos, emitted)."""
-        if temperature != 0.0:
-            raise MoonshineError(8, "only greedy decoding (temperature 0) is supported")
-        sc = (streaming_config or StreamingConfig())._c()
+                   max_tokens: Optional[int] = None, temperature: float = 0.0, seed: int = 0):
+        """transcribe (MoonshineStreaming.swift:122-168).  Returns (ids, hit_eos, emitted);
+        temperature > 0 samples (MLXRandom.categorical of logits / temperature) with draws
+        keyed by ``seed`` and the stream's call count."""
+        sc = (streaming_config or StreamingConfig())._c(temperature, seed)
         cap = max(16, int(np.ceil(state.memory_len * 0.02 * 6.5)) + 64)
         while True:
             ids = np.zeros(cap, dtype=np.int32)
@@ -620,9 +621,9 @@ class MoonshineModel:
 
     def transcribe_batch(self, states: Sequence[StreamingState], is_final: bool = False,
                          streaming_config: Optional[StreamingConfig] = None,
-                         max_tokens: Optional[int] = None):
+                         max_tokens: Optional[int] = None, temperature: float = 0.0, seed: int = 0):
         B = len(states)
-        sc = (streaming_config or StreamingConfig())._c()
+        sc = (streaming_config or StreamingConfig())._c(temperature, seed)
         cap = max(16, max((int(np.ceil(s.memory_len * 0.02 * 6.5)) for s in states), default=0) + 64)
         hs = (C.c_void_p * B)(*[s._h for s in states])
         ids = np.zeros((B, cap), dtype=np.int32)

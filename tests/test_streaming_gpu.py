@@ -136,3 +136,81 @@ def test_stream_batch_decode_lockstep(model_root):
                 assert margins[j] <= BF16_LOGIT_TOL * scale, f"stream {i} chunk {k}: ids part at step {j}"
             checked += 1
     assert checked >= n_streams * (n_chunks - 2)
+
+
+def _stream_first_token_probs(o, audio, T, chunk=1280):
+    """Softmax(logits / T) of the first decoder call on the oracle stream's memory after
+    feeding `audio` in chunks (the memory a non-final transcribe decodes against)."""
+    from oracle.moonshine_oracle import OracleStream
+    os_ = OracleStream(o, kv_fp16=True)
+    os_.start()
+    for off in range(0, len(audio), chunk):
+        os_.add_audio(audio[off:off + chunk])
+    os_._encode_new_frames(False)
+    cache = o.new_cache(os_.memory, True)
+    _, lg = o.decoder_step(o.cfg.decoder_start_token_id, cache)
+    z = np.asarray(lg, np.float64) / T
+    p = np.exp(z - z.max())
+    return p / p.sum(), os_.memory_len
+
+
+def _chi2(counts, p):
+    n = counts.sum()
+    keep = p * n >= 5
+    return float(np.sum((counts[keep] - n * p[keep]) ** 2 / (n * p[keep])))
+
+
+def test_stream_temperature_sampling(model_root):
+    """transcribe(temperature:) (MoonshineStreaming.swift:122-128, decodeMemory :238-268):
+    each non-final call decodes from BOS against the same memory, so 3000 one-token calls
+    draw from softmax(logits / T) of its first decoder call; a repeated (seed, call) sequence
+    repeats its draws.  The lockstep batch samples per stream row."""
+    import moonshine_b200 as mb
+    d = model_dir(model_root, "tiny", vocab_size=16)
+    o = oracle_for(d)
+    audio = synth.synth_audio(16000, 41)
+    T = 0.7
+    p, mem_len = _stream_first_token_probs(o, audio, T)
+    eos = o.cfg.eos_token_id
+    m = mb.MoonshineModel.load(d)
+
+    def fed_stream():
+        st = m.create_stream()
+        m.start_stream(st)
+        for off in range(0, len(audio), 1280):
+            m.add_audio(st, audio[off:off + 1280])
+        return st
+
+    st = fed_stream()
+    counts = np.zeros(16)
+    for _ in range(3000):
+        ids, hit, emitted = m.transcribe(st, max_tokens=1, temperature=T, seed=7)
+        assert not emitted
+        if ids:
+            counts[ids[0]] += 1
+        elif hit and eos < 16:
+            counts[eos] += 1
+    assert st.memory_len == mem_len
+    assert counts.sum() > 2900
+    chi2 = _chi2(counts, p)
+    assert chi2 < 45.0, (chi2, counts, counts.sum() * p)
+
+    a, b = fed_stream(), fed_stream()
+    seq_a = [m.transcribe(a, max_tokens=8, temperature=T, seed=11)[0] for _ in range(5)]
+    seq_b = [m.transcribe(b, max_tokens=8, temperature=T, seed=11)[0] for _ in range(5)]
+    assert seq_a == seq_b and len({tuple(x) for x in seq_a}) > 1
+
+    streams = [fed_stream() for _ in range(64)]
+    counts = np.zeros(16)
+    sc = mb.StreamingConfig(batch_decode=True)
+    for _ in range(32):
+        for ids, hit, _ in m.transcribe_batch(streams, streaming_config=sc, max_tokens=1, temperature=T, seed=3):
+            if ids:
+                counts[ids[0]] += 1
+            elif hit and eos < 16:
+                counts[eos] += 1
+    chi2 = _chi2(counts, p)
+    assert chi2 < 45.0, (chi2, counts, counts.sum() * p)
+
+    with pytest.raises(mb.MoonshineError):
+        m.transcribe(st, temperature=-1.0)
