@@ -815,7 +815,12 @@ bool cluster_geom(int d, int H, int KVH, int hd, int I, int V, int L, int t_cap,
     r.rcq = (hd + CL - 1) / CL;
     r.gr = I / (H * CL);
     r.rlm = (V + H * CL - 1) / (H * CL);
-    r.slot_bytes = 52 * 1024;
+    // ring slot: at least 52 KB, and large enough that a CTA's whole fc1 segment (header and
+    // every (value, gate) row pair, at most 64 rows) is one block
+    {
+        const size_t fc1 = ((size_t)d + 2 * r.gr + (size_t)std::min(2 * r.gr, 64) * row_stride(d)) * 4;
+        r.slot_bytes = (int)std::max<size_t>(52 * 1024, (fc1 + 127) / 128 * 128);
+    }
     r.skv_keys = (t_cap + CL - 1) / CL;
     const Segs s = make_segs(r, d, hd);
     r.cta_floats = (size_t)L * s.layer + (size_t)d + (size_t)r.rlm * row_stride(d);
