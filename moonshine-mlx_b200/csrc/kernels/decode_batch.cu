@@ -38,7 +38,7 @@ __global__ void embed_rows_kernel(const int* __restrict__ ids, const float* __re
 }
 
 __global__ void ln_bf16_kernel(const float* __restrict__ x, int rows, int d, const float* __restrict__ w,
-                               __nv_bfloat16* __restrict__ out) {
+                               float w_offset, __nv_bfloat16* __restrict__ out) {
     __shared__ float red[32];
     const int r = blockIdx.x;
     if (r >= rows) return;
@@ -53,7 +53,7 @@ __global__ void ln_bf16_kernel(const float* __restrict__ x, int rows, int d, con
     }
     const float rstd = rsqrtf(block_sum(q, red) / (float)d + 1e-5f);
     for (int i = threadIdx.x; i < d; i += blockDim.x)
-        out[(size_t)r * d + i] = __float2bfloat16_rn((xr[i] - mean) * rstd * w[i]);
+        out[(size_t)r * d + i] = __float2bfloat16_rn((xr[i] - mean) * rstd * (w[i] + w_offset));
 }
 
 __device__ __forceinline__ float load_kv(const void* base, size_t idx, int f16) {
@@ -435,10 +435,11 @@ cudaError_t launch_embed_rows(const int* ids, const float* embed, int d, int B, 
     return cudaGetLastError();
 }
 
-cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv_bfloat16* out, cudaStream_t s) {
+cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv_bfloat16* out, cudaStream_t s,
+                          float w_offset) {
     if (rows <= 0) return cudaSuccess;
     ++launch_counter();
-    ln_bf16_kernel<<<rows, 128, 0, s>>>(x, rows, d, w, out);
+    ln_bf16_kernel<<<rows, 128, 0, s>>>(x, rows, d, w, w_offset, out);
     return cudaGetLastError();
 }
 

@@ -17,10 +17,14 @@ namespace {
 constexpr int FF_WARPS = 8;
 constexpr int MAX_FRAME = 128;
 
+__device__ __forceinline__ void store_feature(float* p, float v) { *p = v; }
+__device__ __forceinline__ void store_feature(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+template <class OutT>
 __global__ void __launch_bounds__(FF_WARPS * 32)
 frame_features_kernel(const float* __restrict__ audio, int n_frames, int frame_len,
                       const float* __restrict__ log_k, const float* __restrict__ w, int dim,
-                      float* __restrict__ out, int ld_out) {
+                      OutT* __restrict__ out, int ld_out) {
     __shared__ float fr[FF_WARPS][MAX_FRAME];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int f = blockIdx.x * FF_WARPS + wid;
@@ -42,7 +46,7 @@ frame_features_kernel(const float* __restrict__ audio, int n_frames, int frame_l
         const float* wr = w + (size_t)o * frame_len;
         float acc = 0.f;
         for (int i = 0; i < frame_len; ++i) acc = fmaf(fr[wid][i], __ldg(wr + i), acc);
-        out[(size_t)f * ld_out + o] = silu(acc);
+        store_feature(out + (size_t)f * ld_out + o, silu(acc));
     }
 }
 
@@ -91,7 +95,8 @@ constexpr int WA_MAXHD = 128;
 // One warp per (query, head).  Keys are visited 32 at a time with an online softmax.
 __global__ void window_attention_kernel(const float* __restrict__ qkv, int T, int H, int KVH,
                                         int hd, int left, int right, float scale,
-                                        float* __restrict__ out) {
+                                        float* __restrict__ out, int seg_rows, const int* __restrict__ seg_len,
+                                        __nv_bfloat16* __restrict__ out_bf16) {
     const int lane = threadIdx.x & 31;
     const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (item >= T * H) return;
@@ -101,10 +106,26 @@ __global__ void window_attention_kernel(const float* __restrict__ qkv, int T, in
     const float* q = qkv + (size_t)t * ld + h * hd;
     const float* kbase = qkv + H * hd + kvh * hd;
     const float* vbase = qkv + (H + KVH) * hd + kvh * hd;
-    int lo = 0, hi = T;
+    // segments: rows [s * seg_rows, s * seg_rows + seg_len[s]) are one utterance; a query sees
+    // keys of its own utterance only, and rows past its length are written as zeros
+    int base = 0, len = T, tl = t;
+    if (seg_rows > 0) {
+        const int sgi = t / seg_rows;
+        base = sgi * seg_rows;
+        len = seg_len[sgi];
+        tl = t - base;
+        if (tl >= len) {
+            for (int d = lane; d < hd; d += 32) {
+                if (out) out[(size_t)t * (H * hd) + h * hd + d] = 0.f;
+                if (out_bf16) out_bf16[(size_t)t * (H * hd) + h * hd + d] = __float2bfloat16_rn(0.f);
+            }
+            return;
+        }
+    }
+    int lo = base, hi = base + len;
     if (left > 0) {
-        lo = max(0, t - left + 1);
-        hi = min(T, t + (right > 0 ? right : 1));
+        lo = base + max(0, tl - left + 1);
+        hi = base + min(len, tl + (right > 0 ? right : 1));
     }
     float m = -INFINITY, l = 0.f;
     float acc[WA_MAXHD / 32];
@@ -145,12 +166,88 @@ __global__ void window_attention_kernel(const float* __restrict__ qkv, int T, in
         }
         m = mn;
     }
-    float* o = out + (size_t)t * (H * hd) + h * hd;
+    const size_t o = (size_t)t * (H * hd) + h * hd;
     const float inv = 1.f / l;
 #pragma unroll
     for (int c = 0; c < WA_MAXHD / 32; ++c) {
         const int d = lane + 32 * c;
-        if (d < hd) o[d] = acc[c] * inv;
+        if (d < hd) {
+            if (out) out[o + d] = acc[c] * inv;
+            if (out_bf16) out_bf16[o + d] = __float2bfloat16_rn(acc[c] * inv);
+        }
+    }
+}
+
+// CMVN + asinh of the 80-sample frames of a batch in segment-row layout: row r holds frame
+// r % seg_rows - 4 of utterance r / seg_rows (bf16, frame_len values), or zeros where there is
+// none (the causal padding in front and the tail), so the following Linear + SiLU GEMM
+// writes exact zeros there.
+__global__ void frame_norm_rows_kernel(const float* const* __restrict__ audio, const int* __restrict__ n_frames,
+                                       int rows, int seg_rows, int frame_len, const float* __restrict__ log_k,
+                                       __nv_bfloat16* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    const int sgi = r / seg_rows, f = r - sgi * seg_rows - 4;
+    __nv_bfloat16* o = out + (size_t)r * frame_len;
+    if (f < 0 || f >= n_frames[sgi]) {
+        for (int i = lane; i < frame_len; i += 32) o[i] = __float2bfloat16_rn(0.f);
+        return;
+    }
+    const float* a = audio[sgi] + (size_t)f * frame_len;
+    float s = 0.f;
+    for (int i = lane; i < frame_len; i += 32) s += a[i];
+    const float mean = warp_sum(s) / (float)frame_len;
+    float v = 0.f;
+    for (int i = lane; i < frame_len; i += 32) {
+        const float c = a[i] - mean;
+        v += c * c;
+    }
+    const float rms = sqrtf(warp_sum(v) / (float)frame_len + 1e-6f);
+    const float k = expf(*log_k);
+    for (int i = lane; i < frame_len; i += 32) o[i] = __float2bfloat16_rn(asinhf(k * ((a[i] - mean) / rms)));
+}
+
+// Final encoder LayerNorm of segment rows (rows [s * seg_rows, s * seg_rows + len[s]) hold
+// utterance s) plus pos_emb[t], gathered to memory rows off[s] + t (fp32 and bf16).
+__global__ void ln_gather_rows_kernel(const float* __restrict__ x, int rows, int seg_rows, int dim,
+                                      const float* __restrict__ w, float w_offset, float eps,
+                                      const float* __restrict__ pos_emb, const int* __restrict__ len,
+                                      const int* __restrict__ off, float* __restrict__ out,
+                                      __nv_bfloat16* __restrict__ out_bf16) {
+    const int lane = threadIdx.x & 31;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    const int sgi = r / seg_rows, t = r - sgi * seg_rows;
+    if (t >= len[sgi]) return;
+    const float* xr = x + (size_t)r * dim;
+    float v[LN_MAXV];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < LN_MAXV; ++j) {
+        const int i = lane + 32 * j;
+        v[j] = (i < dim) ? xr[i] : 0.f;
+        s += v[j];
+    }
+    const float mean = warp_sum(s) / (float)dim;
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < LN_MAXV; ++j) {
+        const int i = lane + 32 * j;
+        const float c = (i < dim) ? v[j] - mean : 0.f;
+        q += c * c;
+    }
+    const float rstd = rsqrtf(warp_sum(q) / (float)dim + eps);
+    const size_t orow = (size_t)(off[sgi] + t) * dim;
+    const float* pe = pos_emb + (size_t)t * dim;
+#pragma unroll
+    for (int j = 0; j < LN_MAXV; ++j) {
+        const int i = lane + 32 * j;
+        if (i < dim) {
+            const float y = (v[j] - mean) * rstd * (w[i] + w_offset) + pe[i];
+            out[orow + i] = y;
+            out_bf16[orow + i] = __float2bfloat16_rn(y);
+        }
     }
 }
 
@@ -162,7 +259,18 @@ cudaError_t launch_frame_features(const float* audio, int n_frames, int frame_le
     if (n_frames <= 0) return cudaSuccess;
     if (frame_len > MAX_FRAME) return cudaErrorInvalidValue;
     ++launch_counter();
-    frame_features_kernel<<<(n_frames + FF_WARPS - 1) / FF_WARPS, FF_WARPS * 32, 0, stream>>>(
+    frame_features_kernel<float><<<(n_frames + FF_WARPS - 1) / FF_WARPS, FF_WARPS * 32, 0, stream>>>(
+        audio, n_frames, frame_len, log_k, w, dim, out, ld_out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_frame_features_bf16(const float* audio, int n_frames, int frame_len, const float* log_k,
+                                       const float* w, int dim, __nv_bfloat16* out, int ld_out,
+                                       cudaStream_t stream) {
+    if (n_frames <= 0) return cudaSuccess;
+    if (frame_len > MAX_FRAME) return cudaErrorInvalidValue;
+    ++launch_counter();
+    frame_features_kernel<__nv_bfloat16><<<(n_frames + FF_WARPS - 1) / FF_WARPS, FF_WARPS * 32, 0, stream>>>(
         audio, n_frames, frame_len, log_k, w, dim, out, ld_out);
     return cudaGetLastError();
 }
@@ -181,14 +289,39 @@ cudaError_t launch_layernorm_rows(const float* x, int rows, int dim, const float
 
 cudaError_t launch_window_attention(const float* qkv, int T, int H, int kv_heads, int hd,
                                     int left, int right, float scale, float* out,
-                                    cudaStream_t stream) {
+                                    cudaStream_t stream, int seg_rows, const int* seg_len,
+                                    __nv_bfloat16* out_bf16) {
     if (T <= 0) return cudaSuccess;
     if (hd > WA_MAXHD || (hd & 3) || H % kv_heads) return cudaErrorInvalidValue;
+    if ((seg_rows > 0) != (seg_len != nullptr) || (!out && !out_bf16)) return cudaErrorInvalidValue;
     ++launch_counter();
     const int wpb = 8;
     const int items = T * H;
     window_attention_kernel<<<(items + wpb - 1) / wpb, wpb * 32, 0, stream>>>(
-        qkv, T, H, kv_heads, hd, left, right, scale, out);
+        qkv, T, H, kv_heads, hd, left, right, scale, out, seg_rows, seg_len, out_bf16);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_frame_norm_rows(const float* const* audio, const int* n_frames, int rows, int seg_rows,
+                                   int frame_len, const float* log_k, __nv_bfloat16* out, cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    if (seg_rows <= 4) return cudaErrorInvalidValue;
+    ++launch_counter();
+    const int wpb = 8;
+    frame_norm_rows_kernel<<<(rows + wpb - 1) / wpb, wpb * 32, 0, stream>>>(audio, n_frames, rows, seg_rows,
+                                                                          frame_len, log_k, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ln_gather_rows(const float* x, int rows, int seg_rows, int dim, const float* w, float w_offset,
+                                  float eps, const float* pos_emb, const int* len, const int* off, float* out,
+                                  __nv_bfloat16* out_bf16, cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    if (dim > 32 * LN_MAXV || seg_rows <= 0) return cudaErrorInvalidValue;
+    ++launch_counter();
+    const int wpb = 8;
+    ln_gather_rows_kernel<<<(rows + wpb - 1) / wpb, wpb * 32, 0, stream>>>(x, rows, seg_rows, dim, w, w_offset, eps,
+                                                                         pos_emb, len, off, out, out_bf16);
     return cudaGetLastError();
 }
 

@@ -105,9 +105,27 @@ cudaError_t launch_layernorm_rows(const float* x, int rows, int dim, const float
 
 // Multi-head attention over a [T, 3*H*hd] q|k|v buffer with a per-query key window
 // [t-left+1, t+right-1] (left <= 0 means no window: all keys).  out [T, H*hd].
+// Segments (seg_rows > 0): rows [s * seg_rows, s * seg_rows + seg_len[s]) are one utterance;
+// queries see keys of their own utterance, rows past its length get zeros.  out and
+// out_bf16 are each nullable (not both).
 cudaError_t launch_window_attention(const float* qkv, int T, int H, int kv_heads, int hd,
                                     int left, int right, float scale, float* out,
-                                    cudaStream_t stream);
+                                    cudaStream_t stream, int seg_rows = 0, const int* seg_len = nullptr,
+                                    __nv_bfloat16* out_bf16 = nullptr);
+// CMVN + asinh of every frame of a batch into segment rows (row r: frame r % seg_rows - 4 of
+// utterance r / seg_rows, zeros where there is none), bf16 [rows][frame_len]: the input of
+// the frame Linear as one GEMM.  audio / n_frames: device arrays of the utterances.
+cudaError_t launch_frame_norm_rows(const float* const* audio, const int* n_frames, int rows, int seg_rows,
+                                   int frame_len, const float* log_k, __nv_bfloat16* out, cudaStream_t stream);
+// Frame features written as bf16 (same math as launch_frame_features).
+cudaError_t launch_frame_features_bf16(const float* audio, int n_frames, int frame_len, const float* log_k,
+                                       const float* w, int dim, __nv_bfloat16* out, int ld_out,
+                                       cudaStream_t stream);
+// Final encoder LayerNorm of segment rows + pos_emb[t], gathered to rows off[s] + t of out
+// (fp32) and out_bf16 for t < len[s].
+cudaError_t launch_ln_gather_rows(const float* x, int rows, int seg_rows, int dim, const float* w, float w_offset,
+                                  float eps, const float* pos_emb, const int* len, const int* off, float* out,
+                                  __nv_bfloat16* out_bf16, cudaStream_t stream);
 
 // ---------------------------------------------------------------- decoder
 struct DecodeLayerW {
@@ -178,7 +196,8 @@ struct DecodeParams {
 // ---------------------------------------------------------------- batched decode step
 cudaError_t launch_embed_rows(const int* ids, const float* embed, int d, int B, int V, float* x, unsigned* status,
                               cudaStream_t s);
-cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv_bfloat16* out, cudaStream_t s);
+cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv_bfloat16* out, cudaStream_t s,
+                          float w_offset = 0.f);
 cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const void* kc, const void* vc, int kv_f16,
                                    const int* pos, int B, int H, int KVH, int hd, int t_cap, float scale,
                                    __nv_bfloat16* out, cudaStream_t s);

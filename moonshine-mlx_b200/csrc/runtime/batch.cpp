@@ -271,6 +271,230 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
                                   forced ? 1 : 0, s));
 }
 
+void BatchEngine::ensure_enc_weights() {
+    if (enc_weights_ready) return;
+    const Config& c = m.cfg;
+    const int ed = c.e_hidden, hd = c.e_head_dim, EI = c.e_inter;
+    const int eHD = c.e_heads * hd, QKV = (c.e_heads + 2 * c.e_kv_heads) * hd;
+    const int NKV = c.layers * 2 * c.kv_heads * c.head_dim;
+    cudaStream_t s = m.stream;
+    elin = alloc<__nv_bfloat16>((size_t)ed * c.frame_len());
+    MSB_CUDA(launch_f32_to_bf16_rows(m.lin_w, elin, ed, c.frame_len(), 0, s));
+    make_b_map(&m_lin, elin, ed, c.frame_len(), kBnWide);
+    econv1 = alloc<__nv_bfloat16>((size_t)2 * ed * 5 * ed);
+    econv2 = alloc<__nv_bfloat16>((size_t)ed * 10 * ed);
+    MSB_CUDA(launch_f32_to_bf16_rows(m.conv1_w, econv1, 2 * ed, 5 * ed, 0, s));
+    MSB_CUDA(launch_f32_to_bf16_rows(m.conv2_w, econv2, ed, 10 * ed, 0, s));
+    make_b_map(&m_conv1, econv1, 2 * ed, 5 * ed, kBnWide);
+    make_b_map(&m_conv2, econv2, ed, 10 * ed, kBnWide);
+    elayers.resize(c.e_layers);
+    for (int i = 0; i < c.e_layers; ++i) {
+        const EncLayer& L = m.enc[i];
+        EncLayerB& E = elayers[i];
+        E.wqkv = alloc<__nv_bfloat16>((size_t)QKV * ed);
+        E.wo = alloc<__nv_bfloat16>((size_t)ed * eHD);
+        E.w1 = alloc<__nv_bfloat16>((size_t)EI * ed);
+        E.w2 = alloc<__nv_bfloat16>((size_t)ed * EI);
+        MSB_CUDA(launch_f32_to_bf16_rows(L.wqkv, E.wqkv, QKV, ed, 0, s));
+        MSB_CUDA(launch_f32_to_bf16_rows(L.wo, E.wo, ed, eHD, 0, s));
+        MSB_CUDA(launch_f32_to_bf16_rows(L.w1, E.w1, EI, ed, 0, s));
+        MSB_CUDA(launch_f32_to_bf16_rows(L.w2, E.w2, ed, EI, 0, s));
+        make_b_map(&E.m_qkv, E.wqkv, QKV, ed, kBnWide);
+        make_b_map(&E.m_o, E.wo, ed, eHD, kBnWide);
+        make_b_map(&E.m_w1, E.w1, EI, ed, kBnWide);
+        make_b_map(&E.m_w2, E.w2, ed, EI, kBnWide);
+    }
+    ecross = alloc<__nv_bfloat16>((size_t)NKV * c.hidden);
+    MSB_CUDA(launch_f32_to_bf16_rows(m.cross_w, ecross, NKV, c.hidden, 0, s));
+    make_b_map(&m_ecross, ecross, NKV, c.hidden, kBnWide);
+    MSB_CUDA(cudaStreamSynchronize(s));
+    enc_weights_ready = true;
+}
+
+bool BatchEngine::encode_tc(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
+                            const std::vector<int>& off, const std::vector<int>& fr) {
+    const Config& c = m.cfg;
+    const int ed = c.e_hidden, fl = c.frame_len(), d = c.hidden, hd = c.e_head_dim, EI = c.e_inter;
+    const int eHD = c.e_heads * hd, QKV = (c.e_heads + 2 * c.e_kv_heads) * hd;
+    if (m.proj || ed != d || ed % 64 || eHD % 64 || EI % 64 || ed > 1024 || hd > 128 || (hd & 3) || (fl & 7) ||
+        fl > 128)
+        return false;
+    const int B = (int)audio_dev.size();
+    int T1max = 0;
+    std::vector<int> T1(B);
+    for (int b = 0; b < B; ++b) {
+        T1[b] = (int)(n_samples[b] / fl);
+        T1max = std::max(T1max, T1[b]);
+    }
+    // rows per utterance: R in the conv1 input (4 zero rows + frames), R/2 in the conv2 input
+    // (4 zero rows + conv1 outputs), R/4 in the encoder layers
+    const int T3max = *std::max_element(fr.begin(), fr.end());
+    if (T3max > c.max_pos)
+        throw MsError(MS_ERR_INVALID_ARG, "audio longer than the positional table (" + std::to_string(c.max_pos) +
+                                              " frames)");
+    const int R = (T1max + 9 + 3) / 4 * 4, R2 = R / 2, R3 = R / 4;
+    const size_t rows1 = (size_t)B * R, rows2 = (size_t)B * R2 + 4, rows3 = (size_t)B * R3;
+    ensure_enc_weights();
+    cudaStream_t s = m.stream;
+    enorm.ensure(rows1 * fl * 2);
+    eaud.ensure((size_t)B * sizeof(float*));
+    epad1.ensure(rows1 * ed * 2);
+    epad2.ensure(rows2 * 2 * ed * 2);
+    ex.ensure(rows3 * ed * 4);
+    eh.ensure(rows3 * ed * 2);
+    eqkv.ensure(rows3 * QKV * 4);
+    eattn.ensure(rows3 * eHD * 2);
+    ef.ensure(rows3 * EI * 2);
+    emem16.ensure((size_t)Mc * d * 2);
+    eseg.ensure((size_t)3 * B * 4);
+    __nv_bfloat16* pad1 = epad1.as<__nv_bfloat16>();
+    __nv_bfloat16* pad2 = epad2.as<__nv_bfloat16>();
+    float* X = ex.as<float>();
+    int* seg_len = eseg.as<int>();
+    int* seg_off = seg_len + B;
+    {
+        std::vector<int> host(2 * (size_t)B);
+        for (int b = 0; b < B; ++b) {
+            host[b] = fr[b];
+            host[B + b] = off[b];
+        }
+        MSB_CUDA(cudaMemcpyAsync(seg_len, host.data(), host.size() * 4, cudaMemcpyHostToDevice, s));
+    }
+    // frontend: frames of utterance b at rows b*R + 4 + f, every other row zero (normalised
+    // frames of zeros give SiLU(0) = 0 out of the Linear)
+    {
+        std::vector<int> t1(T1);
+        int* t1_dev = seg_len + 2 * B;
+        MSB_CUDA(cudaMemcpyAsync(t1_dev, t1.data(), (size_t)B * 4, cudaMemcpyHostToDevice, s));
+        MSB_CUDA(cudaMemcpyAsync(eaud.p, audio_dev.data(), (size_t)B * sizeof(float*), cudaMemcpyHostToDevice, s));
+        MSB_CUDA(launch_frame_norm_rows(reinterpret_cast<const float* const*>(eaud.p), t1_dev, (int)rows1, R, fl,
+                                        m.log_k, enorm.as<__nv_bfloat16>(), s));
+        CUtensorMap a_norm;
+        if (!tc_make_map_3d(&a_norm, enorm.p, (uint64_t)fl, 1, (uint64_t)rows1, (uint64_t)fl * 2, (uint64_t)fl * 2,
+                            128))
+            throw MsError(MS_ERR_CUDA, "cuTensorMapEncodeTiled failed for the frames");
+        TcGemmArgs ga;
+        ga.M = (int)rows1;
+        ga.N = ed;
+        ga.ep.act = ACT_SILU;
+        ga.out_bf16 = pad1;
+        ga.ldc_bf16 = ed;
+        gemm(a_norm, m_lin, ga, fl, kBnWide);
+    }
+    // causal stride-2 convs as 5-tap GEMMs: output row m reads input rows 2m + tap, i.e.
+    // (y, z) = (tap & 1, m + tap / 2) of the input viewed as row pairs
+    auto conv = [&](const __nv_bfloat16* in, size_t in_rows, int cin, const CUtensorMap& wmap, int M, int N,
+                    TcGemmArgs& ga) {
+        CUtensorMap amap;
+        if (!tc_make_map_3d(&amap, in, (uint64_t)cin, 2, (uint64_t)(in_rows / 2), (uint64_t)cin * 2,
+                            (uint64_t)cin * 4, 128))
+            throw MsError(MS_ERR_CUDA, "cuTensorMapEncodeTiled failed for a conv input");
+        ga.M = M;
+        ga.N = N;
+        ga.taps = 5;
+        ga.kb_per_tap = cin / 64;
+        ga.k_per_tap = cin;
+        for (int t = 0; t < 5; ++t) {
+            ga.tap_y[t] = t & 1;
+            ga.tap_z[t] = t >> 1;
+        }
+        ga.mode = TC_EPI_STD;
+        ga.status = status.as<unsigned>();
+        MSB_CUDA(launch_gemm_tc(amap, wmap, ga, kBnWide, s));
+    };
+    {
+        TcGemmArgs ga;
+        ga.ep.bias = m.conv1_b;
+        ga.ep.act = ACT_SILU;
+        ga.out_bf16 = pad2 + (size_t)4 * 2 * ed;  // utterance b's conv1 outputs at rows b*R2 + 4 + t
+        ga.ldc_bf16 = 2 * ed;
+        conv(pad1, rows1, ed, m_conv1, B * R2, 2 * ed, ga);
+    }
+    // the 4 rows in front of every utterance took the previous one's tail outputs: back to zero
+    MSB_CUDA(cudaMemset2DAsync(pad2, (size_t)R2 * 2 * ed * 2, 0, (size_t)4 * 2 * ed * 2, B, s));
+    {
+        TcGemmArgs ga;
+        ga.ep.bias = m.conv2_b;
+        ga.ep.out = X;
+        ga.ep.ldc = ed;
+        conv(pad2, rows2, 2 * ed, m_conv2, B * R3, ed, ga);
+    }
+    // encoder layers over all B * R3 rows; attention stays inside each utterance's rows
+    CUtensorMap a_h, a_attn, a_f;
+    make_a_map(&a_h, eh.as<__nv_bfloat16>(), (int)rows3, ed);
+    make_a_map(&a_attn, eattn.as<__nv_bfloat16>(), (int)rows3, eHD);
+    make_a_map(&a_f, ef.as<__nv_bfloat16>(), (int)rows3, EI);
+    const float scale = std::pow((float)hd, -0.5f);
+    for (int i = 0; i < c.e_layers; ++i) {
+        const EncLayer& L = m.enc[i];
+        const EncLayerB& E = elayers[i];
+        MSB_CUDA(launch_ln_bf16(X, (int)rows3, ed, L.ln_in, eh.as<__nv_bfloat16>(), s, 1.0f));
+        {
+            TcGemmArgs ga;
+            ga.M = (int)rows3;
+            ga.N = QKV;
+            ga.ep.out = eqkv.as<float>();
+            ga.ep.ldc = QKV;
+            gemm(a_h, E.m_qkv, ga, ed, kBnWide);
+        }
+        const auto w = c.window(i);
+        MSB_CUDA(launch_window_attention(eqkv.as<float>(), (int)rows3, c.e_heads, c.e_kv_heads, hd, w.first, w.second,
+                                         scale, nullptr, s, R3, seg_len, eattn.as<__nv_bfloat16>()));
+        {
+            TcGemmArgs ga;
+            ga.M = (int)rows3;
+            ga.N = ed;
+            ga.ep.out = X;
+            ga.ep.ldc = ed;
+            ga.ep.residual = X;
+            ga.ep.ldr = ed;
+            gemm(a_attn, E.m_o, ga, eHD, kBnWide);
+        }
+        MSB_CUDA(launch_ln_bf16(X, (int)rows3, ed, L.ln_post, eh.as<__nv_bfloat16>(), s, 1.0f));
+        {
+            TcGemmArgs ga;
+            ga.M = (int)rows3;
+            ga.N = EI;
+            ga.ep.bias = L.b1;
+            ga.ep.act = ACT_GELU;
+            ga.out_bf16 = ef.as<__nv_bfloat16>();
+            ga.ldc_bf16 = EI;
+            gemm(a_h, E.m_w1, ga, ed, kBnWide);
+        }
+        {
+            TcGemmArgs ga;
+            ga.M = (int)rows3;
+            ga.N = ed;
+            ga.ep.bias = L.b2;
+            ga.ep.out = X;
+            ga.ep.ldc = ed;
+            ga.ep.residual = X;
+            ga.ep.ldr = ed;
+            gemm(a_f, E.m_w2, ga, EI, kBnWide);
+        }
+    }
+    // prepareMemory: final norm + positions, gathered to the batch memory rows
+    MSB_CUDA(launch_ln_gather_rows(X, (int)rows3, R3, ed, m.enc_final, 1.0f, 1e-5f, m.pos_emb, seg_len, seg_off,
+                                   memory.as<float>(), emem16.as<__nv_bfloat16>(), s));
+    // cross K/V of every memory row in one GEMM (scatter epilogue: fp32 copy + fp16 store)
+    int Mtot = 0;
+    for (int b = 0; b < B; ++b) Mtot = std::max(Mtot, off[b] + fr[b]);
+    CUtensorMap a_mem;
+    make_a_map(&a_mem, emem16.as<__nv_bfloat16>(), Mtot, d);
+    TcGemmArgs ga;
+    ga.M = Mtot;
+    ga.N = c.layers * 2 * c.kv_heads * c.head_dim;
+    ga.ep.kv_scatter = 1;
+    ga.ep.kv_out32 = cross32.as<float>();
+    ga.ep.kv_out16 = m.kv_f16 ? cross16.p : nullptr;
+    ga.ep.kv_heads = c.kv_heads;
+    ga.ep.head_dim = c.head_dim;
+    ga.ep.frame_cap = Mc;
+    ga.ep.frame_offset = 0;
+    gemm(a_mem, m_ecross, ga, d, kBnWide);
+    return true;
+}
+
 BatchEngine::Result BatchEngine::run(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
                                      const std::vector<int>& limits, bool forced, bool want_logits, float temperature,
                                      unsigned seed_) {
@@ -299,8 +523,10 @@ BatchEngine::Result BatchEngine::run(const std::vector<const float*>& audio_dev,
     }
     const int T = *std::max_element(limits.begin(), limits.end());
     ensure_ws(B, T, Mtot, maxM);
-    encode_all(audio_dev, n_samples, off);
-    m.cross_kv_into(memory.as<float>(), Mtot, 0, cross32.as<float>(), m.kv_f16 ? cross16.p : nullptr, Mc);
+    if (!(m.enc_bf16 && encode_tc(audio_dev, n_samples, off, fr))) {
+        encode_all(audio_dev, n_samples, off);
+        m.cross_kv_into(memory.as<float>(), Mtot, 0, cross32.as<float>(), m.kv_f16 ? cross16.p : nullptr, Mc);
+    }
     MSB_CUDA(cudaEventRecord(m.ev[1], s));
     return decode_prepared(B, T, maxM, off, fr, limits, forced, want_logits);
 }

@@ -59,6 +59,22 @@ struct BatchEngine {
     // Utterances are encoded concurrently on the model's encoder lanes.
     void encode_all(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
                     const std::vector<int>& off);
+    // All utterances in one pass of bf16 tcgen05 GEMMs (model.enc_bf16): each utterance owns a
+    // fixed number of rows (its padded length), so the causal convs are 5-tap GEMMs over the
+    // whole batch and every encoder projection is one GEMM; also the cross K/V of all memory
+    // rows.  false when the dims do not fit (the caller keeps the per-utterance path).
+    bool encode_tc(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
+                   const std::vector<int>& off, const std::vector<int>& fr);
+    struct EncLayerB {
+        __nv_bfloat16 *wqkv, *wo, *w1, *w2;
+        CUtensorMap m_qkv, m_o, m_w1, m_w2;
+    };
+    bool enc_weights_ready = false;
+    std::vector<EncLayerB> elayers;
+    __nv_bfloat16 *elin = nullptr, *econv1 = nullptr, *econv2 = nullptr, *ecross = nullptr;
+    CUtensorMap m_lin, m_conv1, m_conv2, m_ecross;
+    DevBuf enorm, epad1, epad2, ex, eh, eqkv, eattn, ef, emem16, eseg, eaud;
+    void ensure_enc_weights();
 
     template <class T> T* alloc(size_t n);
     void ensure_weights();

@@ -430,7 +430,6 @@ Model* load_model(const std::string& dir, const ms_options& o) {
     m->num_sms = prop.multiProcessorCount;
     m->cfg = Config::from_json_file(dir + "/config.json");
     validate(m->cfg);
-    if (o.weight_dtype == MS_W_BF16) throw MsError(MS_ERR_UNSUPPORTED, "bf16 weights not built yet");
     MSB_CUDA(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
     for (auto& e : m->ev) MSB_CUDA(cudaEventCreate(&e));
 
@@ -440,6 +439,13 @@ Model* load_model(const std::string& dir, const ms_options& o) {
         ws.q_bits = m->cfg.q_bits;
     }
     ws.load(find_weights(dir));
+    {
+        // bf16 tensor-core encoder for batches: bf16 / f16 checkpoints (MS_W_AUTO) or on request
+        const std::string k = "encoder.layers.0.mlp.fc1.weight";
+        const std::string dt = ws.has(k) ? ws.need_any(k).dtype : "";
+        m->enc_bf16 = o.weight_dtype == MS_W_BF16 ||
+                      (o.weight_dtype == MS_W_AUTO && (dt == "BF16" || dt == "F16"));
+    }
     const Config& c = m->cfg;
     const int ed = c.e_hidden, d = c.hidden, fl = c.frame_len();
     const int eHD = c.e_heads * c.e_head_dim, eKVD = c.e_kv_heads * c.e_head_dim;

@@ -101,6 +101,7 @@ struct Model {
     ms_options opts{};
     int device = 0, num_sms = 0;
     bool kv_f16 = true;
+    bool enc_bf16 = false;  // batched encodes run on bf16 tensor cores (bf16 / f16 checkpoint or MS_W_BF16)
     cudaStream_t stream = nullptr;
     cudaEvent_t ev[4] = {};
     std::mutex mu;
