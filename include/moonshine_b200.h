@@ -54,8 +54,11 @@ typedef struct ms_stream ms_stream;
  * (MoonshineModel.swift:47-65). */
 typedef enum { MS_KV_F32 = 0, MS_KV_F16 = 1 } ms_kv_dtype;
 
-/* Weight storage / matmul input type on the device.  MS_W_AUTO keeps the checkpoint's
- * own dtype (F32 checkpoints run in fp32, BF16/F16 checkpoints in bf16). */
+/* Matmul input type of the encoder in batched generation.  The batch-1 kernels always
+ * compute in fp32 from the checkpoint's values and the batched decode always runs bf16
+ * tensor-core GEMMs; the batched encoder runs bf16 tensor-core GEMMs for BF16/F16
+ * checkpoints under MS_W_AUTO or for any checkpoint under MS_W_BF16, and fp32 CUDA-core
+ * GEMMs otherwise (MS_W_F32, or an F32 checkpoint under MS_W_AUTO). */
 typedef enum { MS_W_AUTO = 0, MS_W_F32 = 1, MS_W_BF16 = 2 } ms_weight_dtype;
 
 typedef struct {
