@@ -19,6 +19,11 @@ int64_t& launch_counter() {
     return n;
 }
 
+bool& pdl_launches() {
+    static thread_local bool on = false;
+    return on;
+}
+
 namespace {
 thread_local std::string g_err;
 

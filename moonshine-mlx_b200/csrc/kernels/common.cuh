@@ -65,6 +65,15 @@ __device__ __forceinline__ void red_release_gpu_add(unsigned* p, unsigned v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A grid launched with programmatic stream serialization (launch_kernel under pdl_launches())
+// may be scheduled while its predecessor in the stream still runs: it must call pdl_wait()
+// before it reads anything the predecessor writes (the wait returns once that grid has
+// completed and its writes are visible; without the launch attribute it returns at once).
+// pdl_trigger() lets the next such grid start launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- mbarriers and bulk copies
 constexpr uint32_t WAIT_LIMIT = 1u << 22;  // polls of a bounded mbarrier wait
 

@@ -26,6 +26,8 @@ constexpr int MAXHD_B = 64;
 
 __global__ void embed_rows_kernel(const int* __restrict__ ids, const float* __restrict__ embed, int d, int B,
                                   int V, float* __restrict__ x, unsigned* status) {
+    pdl_wait();
+    pdl_trigger();
     const int b = blockIdx.x;
     if (b >= B) return;
     int id = ids[b];
@@ -39,6 +41,8 @@ __global__ void embed_rows_kernel(const int* __restrict__ ids, const float* __re
 
 __global__ void ln_bf16_kernel(const float* __restrict__ x, int rows, int d, const float* __restrict__ w,
                                float w_offset, __nv_bfloat16* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float red[32];
     const int r = blockIdx.x;
     if (r >= rows) return;
@@ -65,6 +69,8 @@ __global__ void self_attn_batch_kernel(const float* __restrict__ q, const float*
                                        const void* __restrict__ kc, const void* __restrict__ vc, int kv_f16,
                                        const int* __restrict__ pos, int B, int H, int KVH, int hd, int t_cap,
                                        float scale, __nv_bfloat16* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (item >= B * H) return;
@@ -243,6 +249,8 @@ __global__ void __launch_bounds__(XS_THREADS) cross_attn_stream_kernel(
     const float* __restrict__ qc, const void* __restrict__ src, const int* __restrict__ frame_off,
     const int* __restrict__ frames, int H, int KVH, int m_cap, int layer, float scale,
     __nv_bfloat16* __restrict__ out, unsigned* status) {
+    pdl_wait();
+    pdl_trigger();
     using S = XsShape<HDT, F16>;
     using E = typename std::conditional<F16, __half, float>::type;
     extern __shared__ __align__(128) unsigned char xs_raw[];
@@ -393,12 +401,12 @@ cudaError_t launch_cross_stream(bool f16, const float* qc, const void* src, cons
         attr_set = true;
     }
     if (f16)
-        cross_attn_stream_kernel<HDT, true><<<B * H, XS_THREADS, xs_smem_bytes<HDT, true>(), s>>>(
-            qc, src, frame_off, frames, H, KVH, m_cap, layer, scale, out, status);
-    else
-        cross_attn_stream_kernel<HDT, false><<<B * H, XS_THREADS, xs_smem_bytes<HDT, false>(), s>>>(
-            qc, src, frame_off, frames, H, KVH, m_cap, layer, scale, out, status);
-    return cudaGetLastError();
+        return launch_kernel(cross_attn_stream_kernel<HDT, true>, dim3(B * H), dim3(XS_THREADS),
+                             xs_smem_bytes<HDT, true>(), s, qc, src, frame_off, frames, H, KVH, m_cap, layer, scale,
+                             out, status);
+    return launch_kernel(cross_attn_stream_kernel<HDT, false>, dim3(B * H), dim3(XS_THREADS),
+                         xs_smem_bytes<HDT, false>(), s, qc, src, frame_off, frames, H, KVH, m_cap, layer, scale,
+                         out, status);
 }
 
 // One thread per row b.  Decodes the packed argmax, applies the greedy-loop rules of
@@ -406,6 +414,8 @@ cudaError_t launch_cross_stream(bool f16, const float* qc, const void* src, cons
 __global__ void step_finalize_kernel(unsigned long long* amax, int B, int* pos, int* next_ids, int* ids_out,
                                      int t_cap, int* counts, const int* limits, int* done, int* hit_eos, int eos,
                                      int forced) {
+    pdl_wait();
+    pdl_trigger();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b < B) {
         const int id = (int)(0xFFFFFFFFu - (uint32_t)(amax[b] & 0xFFFFFFFFull));
@@ -431,16 +441,14 @@ __global__ void step_finalize_kernel(unsigned long long* amax, int B, int* pos, 
 cudaError_t launch_embed_rows(const int* ids, const float* embed, int d, int B, int V, float* x, unsigned* status,
                               cudaStream_t s) {
     ++launch_counter();
-    embed_rows_kernel<<<B, 128, 0, s>>>(ids, embed, d, B, V, x, status);
-    return cudaGetLastError();
+    return launch_kernel(embed_rows_kernel, dim3(B), dim3(128), 0, s, ids, embed, d, B, V, x, status);
 }
 
 cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv_bfloat16* out, cudaStream_t s,
                           float w_offset) {
     if (rows <= 0) return cudaSuccess;
     ++launch_counter();
-    ln_bf16_kernel<<<rows, 128, 0, s>>>(x, rows, d, w, w_offset, out);
-    return cudaGetLastError();
+    return launch_kernel(ln_bf16_kernel, dim3(rows), dim3(128), 0, s, x, rows, d, w, w_offset, out);
 }
 
 cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const void* kc, const void* vc, int kv_f16,
@@ -449,9 +457,8 @@ cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const vo
     if (hd > MAXHD_B || (hd & 1)) return cudaErrorInvalidValue;
     ++launch_counter();
     const int items = B * H;
-    self_attn_batch_kernel<<<(items + 7) / 8, 256, 0, s>>>(q, kv_new, kc, vc, kv_f16, pos, B, H, KVH, hd, t_cap,
-                                                           scale, out);
-    return cudaGetLastError();
+    return launch_kernel(self_attn_batch_kernel, dim3((items + 7) / 8), dim3(256), 0, s, q, kv_new, kc, vc, kv_f16,
+                         pos, B, H, KVH, hd, t_cap, scale, out);
 }
 
 cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const void* cross_st, int st_f16,
@@ -487,9 +494,8 @@ cudaError_t launch_step_finalize(unsigned long long* amax, int B, int* pos, int*
                                  cudaStream_t s) {
     if (B > 1024) return cudaErrorInvalidValue;
     ++launch_counter();
-    step_finalize_kernel<<<1, ((B + 31) / 32) * 32, 0, s>>>(amax, B, pos, next_ids, ids_out, t_cap, counts, limits,
-                                                            done, hit_eos, eos, forced);
-    return cudaGetLastError();
+    return launch_kernel(step_finalize_kernel, dim3(1), dim3(((B + 31) / 32) * 32), 0, s, amax, B, pos, next_ids,
+                         ids_out, t_cap, counts, limits, done, hit_eos, eos, forced);
 }
 
 namespace {

@@ -313,6 +313,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = s.tmem_base;
 
+    // B (the weights) does not come from the previous kernel: the first stages' B tiles are
+    // requested before waiting for it (programmatic dependent launch), A after
+    const int pre = min(nkb, STAGES);
+    if (warp == 0 && lane == 0)
+        for (int kb = 0; kb < pre; ++kb) {
+            const int gkb = kb_lo + kb;
+            const int tap = gkb / g.kb_per_tap;
+            const int k0 = (gkb - tap * g.kb_per_tap) * BK;
+            mbar_expect_tx(&s.full[kb], A_BYTES + B_BYTES);
+            tma_load_2d(s.b[kb], &tmap_b, &s.full[kb], tap * g.k_per_tap + k0, n0);
+        }
+    pdl_wait();
+    pdl_trigger();
+
     int issued = 0;  // producer: k-blocks whose copies were issued
     if (warp == 0 && lane == 0) {
         for (int kb = 0; kb < nkb; ++kb) {
@@ -325,9 +339,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             const int gkb = kb_lo + kb;
             const int tap = gkb / g.kb_per_tap;
             const int k0 = (gkb - tap * g.kb_per_tap) * BK;
-            mbar_expect_tx(&s.full[st], A_BYTES + B_BYTES);
+            if (kb >= pre) {
+                mbar_expect_tx(&s.full[st], A_BYTES + B_BYTES);
+                tma_load_2d(s.b[st], &tmap_b, &s.full[st], tap * g.k_per_tap + k0, n0);
+            }
             tma_load_3d(s.a[st], &tmap_a, &s.full[st], k0, g.tap_y[tap], m0 + g.tap_z[tap]);
-            tma_load_2d(s.b[st], &tmap_b, &s.full[st], tap * g.k_per_tap + k0, n0);
             issued = kb + 1;
         }
     } else if (warp == 1 && lane == 0) {
@@ -445,8 +461,7 @@ cudaError_t launch_tc(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
         attr_set = true;
     }
     const dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.splits);
-    gemm_tc_kernel<BN, MODE><<<grid, TC_THREADS, smem, stream>>>(map_a, map_b, g);
-    return cudaGetLastError();
+    return launch_kernel(gemm_tc_kernel<BN, MODE>, grid, dim3(TC_THREADS), smem, stream, map_a, map_b, g);
 }
 
 template <int BN>

@@ -2,6 +2,8 @@
 // every launcher enqueues on `stream` and returns cudaGetLastError().
 #pragma once
 
+#include <utility>
+
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -10,6 +12,26 @@ namespace msb {
 
 // Count of kernel launches issued through these launchers on this thread.
 int64_t& launch_counter();
+
+// Launches of the kernels that call pdl_wait() (the batched decode step's) carry the
+// programmatic-stream-serialization attribute while this thread-local flag is set, so each
+// can launch while its predecessor finishes (CUDA graphs keep the programmatic edges).
+bool& pdl_launches();
+template <class... Params, class... Args>
+cudaError_t launch_kernel(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_launches() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Device-side error codes reported through a kernel's status word.
 enum : unsigned { DEV_OK = 0, DEV_BARRIER_TIMEOUT = 1, DEV_BAD_TOKEN = 2, DEV_WAIT_TIMEOUT = 5 };

@@ -158,7 +158,19 @@ void BatchEngine::gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& g
     MSB_CUDA(launch_gemm_tc(a, b, ga, bn, m.stream));
 }
 
+namespace {
+// Programmatic dependent launches for the kernels of one decode step (each waits for its
+// predecessor before reading its results; a weight GEMM prefetches its first weight tiles
+// while the previous kernel finishes).
+struct PdlScope {
+    bool prev;
+    PdlScope() : prev(pdl_launches()) { pdl_launches() = true; }
+    ~PdlScope() { pdl_launches() = prev; }
+};
+}  // namespace
+
 void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, float* logits) {
+    PdlScope pdl;
     const Config& c = m.cfg;
     const int d = c.hidden, H = c.heads, KVH = c.kv_heads, hd = c.head_dim, I = c.inter;
     const int HD = H * hd, KVD = KVH * hd;
