@@ -54,11 +54,14 @@ typedef struct ms_stream ms_stream;
  * (MoonshineModel.swift:47-65). */
 typedef enum { MS_KV_F32 = 0, MS_KV_F16 = 1 } ms_kv_dtype;
 
-/* Matmul input type of the encoder in batched generation.  The batch-1 kernels always
- * compute in fp32 from the checkpoint's values and the batched decode always runs bf16
- * tensor-core GEMMs; the batched encoder runs bf16 tensor-core GEMMs for BF16/F16
- * checkpoints under MS_W_AUTO or for any checkpoint under MS_W_BF16, and fp32 CUDA-core
- * GEMMs otherwise (MS_W_F32, or an F32 checkpoint under MS_W_AUTO). */
+/* Matmul input type of the encoder in batched generation, and the weight rows of
+ * quantized checkpoints in the batch-1 decode.  The batch-1 kernels compute in fp32 from
+ * the checkpoint's values and the batched decode always runs bf16 tensor-core GEMMs; the
+ * batched encoder runs bf16 tensor-core GEMMs for BF16/F16 checkpoints under MS_W_AUTO or
+ * for any checkpoint under MS_W_BF16, and fp32 CUDA-core GEMMs otherwise (MS_W_F32, or an
+ * F32 checkpoint under MS_W_AUTO).  For a quantized checkpoint the clustered batch-1 kernel
+ * streams the quantized codes of its row-split weights (ms_model_decode_weight_bits) except
+ * under MS_W_F32, which streams them dequantized to fp32. */
 typedef enum { MS_W_AUTO = 0, MS_W_F32 = 1, MS_W_BF16 = 2 } ms_weight_dtype;
 
 typedef struct {
@@ -97,10 +100,18 @@ typedef struct {
 /* MoonshineModel.load(from:hfToken:) (MoonshineModel.swift:409-414) for a LOCAL
  * directory holding config.json + *.safetensors (ModelLoader.swift:35-70,115-130).
  * Accepts HuggingFace key layout (``model.`` prefix, ``.gamma``, conv [out,in,k]) and
- * MLX layout, as sanitizeWeights does (ModelLoader.swift:75-101).  Hub download and
- * quantized checkpoints are not supported (MS_ERR_UNSUPPORTED). */
+ * MLX layout, as sanitizeWeights does (ModelLoader.swift:75-101), and MLX affine-quantized
+ * checkpoints (config.json "quantization", 2/4/8 bits, ModelLoader.swift:47-49,103-111).
+ * Hub download is not supported. */
 ms_status ms_model_load(const char* dir, const ms_options* opts, ms_model** out);
 void ms_model_free(ms_model* model);
+
+/* Code width of the weight rows the clustered batch-1 decode kernel streams for q|k|v,
+ * cross q and fc1 of a quantized checkpoint (2, 4 or 8: the checkpoint's codes with their
+ * per-group scale and bias, multiplied in the kernel), or 0 when it streams fp32 rows
+ * (unquantized checkpoints, MS_W_F32, or dims the quantized rows do not fit).  *lm_bits (nullable)
+ * receives the same for the LM head (0 when it is tied to the embedding). */
+int32_t ms_model_decode_weight_bits(const ms_model* model, int32_t* lm_bits);
 
 /* MoonshineModel.enableFloat16KVCache(_:) (MoonshineModel.swift:60-65). */
 ms_status ms_model_enable_fp16_kv_cache(ms_model* model, int32_t enabled);

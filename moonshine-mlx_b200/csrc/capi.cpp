@@ -152,6 +152,12 @@ void ms_streaming_config_default(ms_streaming_config* c) {
 }
 
 const char* ms_last_error(void) { return g_err.c_str(); }
+int32_t ms_model_decode_weight_bits(const ms_model* model, int32_t* lm_bits) {
+    const Model* m = reinterpret_cast<const Model*>(model);
+    if (lm_bits) *lm_bits = m ? m->cl_lm_qbits : 0;
+    return m ? m->cl_qbits : 0;
+}
+
 int64_t ms_kernel_launches(void) { return launch_counter(); }
 void ms_reset_kernel_launches(void) { launch_counter() = 0; }
 const char* ms_version(void) { return "moonshine-b200 0.1 (sm_100a)"; }

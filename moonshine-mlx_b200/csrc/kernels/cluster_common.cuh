@@ -59,6 +59,10 @@ __device__ __forceinline__ void cp16(void* s, const void* g) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(s)), "l"(g) : "memory");
 }
 
+// GEMV rows of the packed streams are stored rf + 4 floats apart (rf % 8 == 0): an odd
+// number of 16-byte units, so lanes that own consecutive rows read distinct bank groups.
+__host__ __device__ inline int row_stride(int rf) { return rf + 4; }
+
 // res[i] = rows[i][0 : rf) . vec for i < nr (nr <= 64, row i at rows + i * rs).  Long rows
 // split their columns over the eight warps with lanes owning rows (rs / 4 odd, so the eight
 // lanes of one 128-bit phase read eight different bank groups) and a per-row sum of the
@@ -118,6 +122,121 @@ __device__ __noinline__ void block_gemv(const float* rows, int nr, int rf, int r
         }
     }
     __syncthreads();
+}
+
+// Dot product of one word of BITS-bit codes (lowest bits first) with its 32 / BITS inputs.
+// A code field is turned into a float without a conversion instruction: OR-ing it into the
+// mantissa of 2^23 and subtracting 2^23 gives field * 2^s exactly, s being the field's bit
+// offset inside its 16-bit half of the word; x holds the inputs pre-scaled by 2^-s, so each
+// product equals code * input exactly before the fused add.
+template <int BITS>
+__device__ __forceinline__ float dot_code_word(uint32_t wd, const float4* x4) {
+    constexpr int PER = 32 / BITS;
+    const uint32_t hi = wd >> 16;
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int q = 0; q < PER / 4; ++q) {
+        const float4 t = x4[q];
+        const float xv[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int o = (4 * q + e) * BITS;
+            const uint32_t src = o < 16 ? wd : hi;
+            const uint32_t m = ((1u << BITS) - 1u) << (o & 15);
+            const float f = __uint_as_float((src & m) | 0x4B000000u) - 8388608.f;
+            if (e & 1) a1 = fmaf(f, xv[e], a1);
+            else a0 = fmaf(f, xv[e], a0);
+        }
+    }
+    return a0 + a1;
+}
+
+// Scale of input j of a row of BITS-bit codes in the pre-scaled vector block_gemv_q reads
+// (2^-s, s = the bit offset of j's code field inside its 16-bit half word; exact).
+__device__ __forceinline__ float quant_input_scale(int j, int bits) {
+    const int sh = ((j % (32 / bits)) * bits) & 15;
+    return __uint_as_float((uint32_t)(127 - sh) << 23);
+}
+
+// The vector block_gemv_q reads, from vec [rf] (rf % 64 == 0): xq[j] = vec[j] *
+// quant_input_scale(j), then xq[rf + j / 16] = the sum of vec over inputs j .. j + 15.
+// Thread t handles inputs t, t + NT, ... (whole warps per iteration); no barrier.
+__device__ __noinline__ void quant_vector(const float* vec, float* xq, int rf, int bits) {
+    const int lane = threadIdx.x & 31;
+    for (int k = threadIdx.x; k < rf; k += NT) {
+        const float v = vec[k];
+        xq[k] = v * quant_input_scale(k, bits);
+        float t = v + __shfl_xor_sync(0xffffffffu, v, 8);
+        t += __shfl_xor_sync(0xffffffffu, t, 4);
+        t += __shfl_xor_sync(0xffffffffu, t, 2);
+        t += __shfl_xor_sync(0xffffffffu, t, 1);
+        if ((lane & 15) == 0) xq[rf + (k >> 4)] = t;
+    }
+}
+
+// res[i] = W[i] . vec for a block of nr <= NT affine-quantized rows of rf inputs (the MLX
+// layout w = scale * q + bias per group of gs inputs).  Row i is a record at rows + i * rs
+// words: rf * BITS / 32 code words, then (scale, bias) float pairs per group.  The sum is
+// taken as sum over 16-byte code chunks k of scale_g * (q . vec)_k + bias_g * (sum of vec)_k.
+// The vector comes prepared (by the LayerNorm that produced it): xq[j] = vec[j] *
+// quant_input_scale(j), then at xq + rf the sums of vec over each 16 inputs.  Lanes own
+// rows; the eight warps split into 8 / T' row groups of 32 (T' = the number of 32-row groups
+// rounded up to a power of two) and each group's warps take the chunks round robin, their
+// partials summed per row in fixed order.  Ends with a barrier.
+template <int BITS>
+__device__ __noinline__ void block_gemv_q(const uint32_t* rows, int nr, int rf, int rs, int gs, const float* xq,
+                                          float* part, float* res) {
+    constexpr int PER = 32 / BITS;  // codes per word
+    constexpr int CC = 4 * PER;     // inputs per 16-byte chunk of codes
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int nch = rf / CC;
+    const float* x16 = xq + rf;
+    const int T = (nr + 31) >> 5;
+    const int Tp = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;
+    const int S = NW / Tp;  // warps per 32-row group
+    const int rg = w / S, sp = w - rg * S;
+    const int i = rg * 32 + lane;
+    float acc = 0.f;
+    if (i < nr) {
+        const uint32_t* row = rows + (size_t)i * rs;
+        const float2* sb = reinterpret_cast<const float2*>(row + rf / PER);
+        for (int k = sp; k < nch; k += S) {
+            const uint4 cw = *reinterpret_cast<const uint4*>(row + 4 * k);
+            const float4* x4 = reinterpret_cast<const float4*>(xq + k * CC);
+            float a0 = dot_code_word<BITS>(cw.x, x4);
+            float a1 = dot_code_word<BITS>(cw.y, x4 + PER / 4);
+            a0 += dot_code_word<BITS>(cw.z, x4 + 2 * (PER / 4));
+            a1 += dot_code_word<BITS>(cw.w, x4 + 3 * (PER / 4));
+            float xs = x16[k * (CC / 16)];
+#pragma unroll
+            for (int t = 1; t < CC / 16; ++t) xs += x16[k * (CC / 16) + t];
+            const float2 g = sb[(k * CC) / gs];
+            acc = fmaf(g.x, a0 + a1, fmaf(g.y, xs, acc));
+        }
+    }
+    if (S == 1) {
+        if (i < nr) res[i] = acc;
+    } else {
+        part[sp * (32 * Tp) + i] = acc;
+        __syncthreads();
+        for (int q = tid; q < nr; q += NT) {
+            float v = 0.f;
+            for (int t = 0; t < S; ++t) v += part[t * (32 * Tp) + q];
+            res[q] = v;
+        }
+    }
+    __syncthreads();
+}
+
+// block_gemv_q for qcode = bits | group size << 4 | row stride << 16 (xq = res + NT).
+__device__ __noinline__ void block_gemv_qrows(const float* rows, int nr, int rf, int qcode, float* part,
+                                              float* res) {
+    const int bits = qcode & 15, gs = (qcode >> 4) & 0xfff, rs = qcode >> 16;
+    const uint32_t* qr = reinterpret_cast<const uint32_t*>(rows);
+    const float* xq = res + NT;
+    if (bits == 4) block_gemv_q<4>(qr, nr, rf, rs, gs, xq, part, res);
+    else if (bits == 8) block_gemv_q<8>(qr, nr, rf, rs, gs, xq, part, res);
+    else block_gemv_q<2>(qr, nr, rf, rs, gs, xq, part, res);
 }
 
 // Cross-attention key scoring layout (as the batched streaming kernel): G lanes per key,
@@ -201,18 +320,15 @@ __device__ __noinline__ float4 attend_keys(const void* kblk, const void* vblk, i
     return make_float4(m, l, a0, a1);
 }
 
-// GEMV rows of the packed streams are stored rf + 4 floats apart (rf % 8 == 0): an odd
-// number of 16-byte units, so lanes that own consecutive rows read distinct bank groups.
-__host__ __device__ inline int row_stride(int rf) { return rf + 4; }
 
-// Rows of the next block of a segment (header + rows of rf floats, at most 64 rows, split at
-// whole multiples of `gran` rows, the header only in the first block), or -1 when the
+// Rows of the next block of a segment (header + rows of rf floats, at most maxr rows, split
+// at whole multiples of `gran` rows, the header only in the first block), or -1 when the
 // segment is exhausted.
 __host__ __device__ inline int next_block_rows(int hdr, int nrows, int rf, int gran, int slot_floats, int row0,
-                                               bool first) {
+                                               bool first, int maxr) {
     if (!(first && hdr > 0) && row0 >= nrows) return -1;
     const int cap = slot_floats - (first ? hdr : 0);
-    const int per = max(gran, min(64, cap / rf) / gran * gran);
+    const int per = max(gran, min(maxr, cap / rf) / gran * gran);
     return min(nrows - row0, per);
 }
 

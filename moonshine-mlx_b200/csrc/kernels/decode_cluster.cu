@@ -59,15 +59,25 @@ constexpr uint64_t GSYNC_TIMEOUT_NS = 2000000000ull;
 //   FC2  [b2 slice (ro, padded)]     [d rows x gr  ]   W2[:, this CTA's gr columns]
 // then after the last layer LM [final_ln (d)][rlm rows x d].
 // GEMV rows are stored rf + 4 floats apart (rf % 8 == 0): an odd number of 16-byte units,
-// so lanes that own consecutive rows read distinct shared-memory bank groups.
+// so lanes that own consecutive rows read distinct shared-memory bank groups.  With
+// g.qbits the QKV, CQ and FC1 rows (with g.lm_qbits the LM rows) are quantized records
+// (quant_row_stride words: codes, then (scale, bias) pairs), at most NT rows per block.
+
+// stored row stride (words) of the QKV / CQ / FC1 rows and of the LM rows (cluster_geom);
+// QR = false: the geometry has fp32 rows only and the strides are row_stride(d)
+template <bool QR = true>
+__host__ __device__ inline int rows_stride_d(const ClusterGeom& g, int d) { return QR ? g.rs_rows : row_stride(d); }
+template <bool QR = true>
+__host__ __device__ inline int lm_stride(const ClusterGeom& g, int d) { return QR ? g.rs_lm : row_stride(d); }
 
 struct Segs {
     size_t qkv, o, cq, co, fc1, fc2, layer;
     int ro4;
 };
+template <bool QR = true>
 __host__ __device__ inline Segs make_segs(const ClusterGeom& g, int d, int hd) {
     Segs s;
-    const int sd = row_stride(d), sh = row_stride(hd);
+    const int sd = rows_stride_d<QR>(g, d), sh = row_stride(hd);
     s.ro4 = (g.ro + 3) & ~3;
     s.qkv = 0;
     s.o = s.qkv + (size_t)d + (size_t)g.rq * sd;
@@ -86,8 +96,10 @@ constexpr int MAXB = 192;  // blocks per step a CTA's schedule may have (checked
 struct SegPlan {
     size_t off;  // floats from the CTA's stream base
     int hdr, nrows, rf, gran;  // rf: stored row stride (floats)
+    int maxr;                  // rows per block at most
 };
 // Segment `seg` of `layer` for cluster rank r (CTA index cta); SEG_LM ignores `layer`.
+template <bool QR = true>
 __host__ __device__ inline SegPlan seg_plan(int seg, int layer, const ClusterGeom& g, const Segs& sg, int d, int hd,
                                            int L, int V, int r, int cta) {
     const size_t lw = (size_t)layer * sg.layer;
@@ -95,14 +107,15 @@ __host__ __device__ inline SegPlan seg_plan(int seg, int layer, const ClusterGeo
     const int no = max(0, min(g.ro, d - r * g.ro));
     const int ncq = max(0, min(g.rcq, hd - r * g.rcq));
     const int nlm = max(0, min(g.rlm, V - cta * g.rlm));
+    const int sd = rows_stride_d<QR>(g, d), mq = QR && g.qbits ? NT : 64;
     switch (seg) {
-        case SEG_QKV: return {lw + sg.qkv, d, nq, row_stride(d), 1};
-        case SEG_O: return {lw + sg.o, 0, no, row_stride(hd), 1};
-        case SEG_CQ: return {lw + sg.cq, d, ncq, row_stride(d), 1};
-        case SEG_CO: return {lw + sg.co, 0, no, row_stride(hd), 1};
-        case SEG_FC1: return {lw + sg.fc1, d + 2 * g.gr, 2 * g.gr, row_stride(d), 2};
-        case SEG_FC2: return {lw + sg.fc2, sg.ro4, d, g.gr, 1};
-        default: return {(size_t)L * sg.layer, d, nlm, row_stride(d), 1};
+        case SEG_QKV: return {lw + sg.qkv, d, nq, sd, 1, mq};
+        case SEG_O: return {lw + sg.o, 0, no, row_stride(hd), 1, 64};
+        case SEG_CQ: return {lw + sg.cq, d, ncq, sd, 1, mq};
+        case SEG_CO: return {lw + sg.co, 0, no, row_stride(hd), 1, 64};
+        case SEG_FC1: return {lw + sg.fc1, d + 2 * g.gr, 2 * g.gr, sd, 2, mq};
+        case SEG_FC2: return {lw + sg.fc2, sg.ro4, d, g.gr, 1, 64};
+        default: return {(size_t)L * sg.layer, d, nlm, lm_stride<QR>(g, d), 1, QR && g.lm_qbits ? NT : 64};
     }
 }
 
@@ -123,7 +136,7 @@ __host__ __device__ inline int blocks_per_step(const ClusterGeom& g, const Segs&
             int row0 = 0;
             bool first = true;
             for (;;) {
-                const int nr = next_block_rows(sp.hdr, sp.nrows, sp.rf, sp.gran, slot_floats, row0, first);
+                const int nr = next_block_rows(sp.hdr, sp.nrows, sp.rf, sp.gran, slot_floats, row0, first, sp.maxr);
                 if (nr < 0) break;
                 ++n;
                 row0 += nr;
@@ -134,7 +147,9 @@ __host__ __device__ inline int blocks_per_step(const ClusterGeom& g, const Segs&
 }
 
 
-template <int HDT>
+// QR: the geometry streams quantized rows (gm.qc_rows / gm.qc_lm); the fp32 instantiation
+// carries none of their code.
+template <int HDT, bool QR>
 __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, ClusterGeom gm) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t full[NSLOT];
@@ -150,7 +165,7 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
     const int c = (int)cluster_index(), r = (int)cluster_rank();
     const int cta = c * CL + r, ncta = H * CL;
     const int slot_bytes = gm.slot_bytes, slot_floats = slot_bytes / 4;
-    const Segs sg = make_segs(gm, d, HDT);
+    const Segs sg = make_segs<QR>(gm, d, HDT);
     const int nq = max(0, min(gm.rq, 3 * HDT - r * gm.rq));
     const int no = max(0, min(gm.ro, d - r * gm.ro));
     const int ncq = max(0, min(gm.rcq, HDT - r * gm.rcq));
@@ -177,7 +192,8 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
     float* b2_s = gb_s + 2 * gm.gr;                    // [ro4] b2 slice
     float* sc = b2_s + sg.ro4;                         // [NW][32]
     float* gpart = sc + NW * 32;                       // [NW][64] block_gemv warp partials
-    float* gres = gpart + NW * 64;                     // [64] block_gemv results
+    float* gres = gpart + NW * 64;                     // [64] block_gemv results ([NT], then
+                                                       // [d + d / 16] quantized GEMV input, when QR)
 
     if (tid == 0) {
         for (int i = 0; i < NSLOT; ++i) mbar_init(&full[i], 1);
@@ -211,11 +227,11 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
                         }
                         continue;
                     }
-                    const SegPlan sp = seg_plan(seg, l, gm, sg, d, HDT, L, V, r, cta);
+                    const SegPlan sp = seg_plan<QR>(seg, l, gm, sg, d, HDT, L, V, r, cta);
                     int row0 = 0;
                     bool first = true;
                     while (n < MAXB) {
-                        const int nr = next_block_rows(sp.hdr, sp.nrows, sp.rf, sp.gran, slot_floats, row0, first);
+                        const int nr = next_block_rows(sp.hdr, sp.nrows, sp.rf, sp.gran, slot_floats, row0, first, sp.maxr);
                         if (nr < 0) break;
                         const float* src = pbase + sp.off + (first ? 0 : sp.hdr + (size_t)row0 * sp.rf);
                         const uint32_t floats = (first ? sp.hdr : 0) + (uint32_t)nr * sp.rf;
@@ -275,11 +291,11 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
     auto release = [&]() { ++n_con; };
     // walk the blocks of one segment: body(block, rows, row0, nr, first)
     auto for_blocks = [&](int seg, int layer, auto&& body) {
-        const SegPlan sp = seg_plan(seg, layer, gm, sg, d, HDT, L, V, r, cta);
+        const SegPlan sp = seg_plan<QR>(seg, layer, gm, sg, d, HDT, L, V, r, cta);
         int row0 = 0;
         bool first = true;
         for (;;) {
-            const int nr = next_block_rows(sp.hdr, sp.nrows, sp.rf, sp.gran, slot_floats, row0, first);
+            const int nr = next_block_rows(sp.hdr, sp.nrows, sp.rf, sp.gran, slot_floats, row0, first, sp.maxr);
             if (nr < 0) break;
             const float* blk = take();
             body(blk, blk + (first ? sp.hdr : 0), row0, nr, first);
@@ -364,7 +380,11 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
 #pragma unroll
         for (int q = 0; q < 2; ++q) outB[q] = q < nb ? (uint32_t)vb[q] : 0u;
     };
-    auto layer_norm = [&](const float* wln) {  // xl = LN(xs) * wln (wln in shared memory)
+    // xl = LN(xs) * wln (wln in shared memory); for rows quantized to qb bits also the
+    // vector block_gemv_q reads: xl pre-scaled per input, then sums over each 16 inputs
+    // (d % 64 == 0 there, so every iteration below covers whole warps)
+    float* xq_s = gres + NT;
+    auto layer_norm = [&](const float* wln, int qb) {
         float s = 0.f;
         for (int k = lane; k < d; k += 32) s += xs[k];
         const float mean = warp_sum(s) / (float)d;
@@ -375,6 +395,8 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
         }
         const float rstd = rsqrtf(warp_sum(q) / (float)d + 1e-5f);
         for (int k = tid; k < d; k += NT) xl[k] = (xs[k] - mean) * rstd * wln[k];
+        if constexpr (QR)
+            if (qb) quant_vector(xl, xq_s, d, qb);  // reads only this thread's own xl elements
         __syncthreads();
     };
     int par = 0;
@@ -510,8 +532,9 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
             }
             // ---- LN1 + this CTA's q|k|v rows -> every CTA of the cluster
             for_blocks(SEG_QKV, l, [&](const float* blk, const float* rows, int row0, int nr, bool first) {
-                if (first) layer_norm(blk);
-                block_gemv(rows, nr, d, row_stride(d), xl, gpart, gres);
+                if (first) layer_norm(blk, gm.qbits);
+                if (QR && gm.qc_rows) block_gemv_qrows(rows, nr, d, gm.qc_rows, gpart, gres);
+                else block_gemv(rows, nr, d, row_stride(d), xl, gpart, gres);
                 for (int e = tid; e < nr * CL; e += NT) {  // row i -> rank q
                     const int i = e / CL, q = e - (e / CL) * CL;
                     st_dsmem(mapa_rank(qkv_a + 4 * (r * gm.rq + row0 + i), q), gres[i]);
@@ -588,8 +611,9 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
             add_partials();
             // ---- LN2 + cross q rows -> every CTA of the cluster
             for_blocks(SEG_CQ, l, [&](const float* blk, const float* rows, int row0, int nr, bool first) {
-                if (first) layer_norm(blk);
-                block_gemv(rows, nr, d, row_stride(d), xl, gpart, gres);
+                if (first) layer_norm(blk, gm.qbits);
+                if (QR && gm.qc_rows) block_gemv_qrows(rows, nr, d, gm.qc_rows, gpart, gres);
+                else block_gemv(rows, nr, d, row_stride(d), xl, gpart, gres);
                 for (int e = tid; e < nr * CL; e += NT) {
                     const int i = e / CL, q = e - (e / CL) * CL;
                     st_dsmem(mapa_rank(qc_a + 4 * (r * gm.rcq + row0 + i), q), gres[i]);
@@ -644,9 +668,10 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
             for_blocks(SEG_FC1, l, [&](const float* blk, const float* rows, int row0, int nr, bool first) {
                 if (first) {
                     for (int i = tid; i < 2 * gm.gr; i += NT) gb_s[i] = blk[d + i];
-                    layer_norm(blk);  // ends with a barrier: gb_s is visible too
+                    layer_norm(blk, gm.qbits);  // ends with a barrier: gb_s is visible too
                 }
-                block_gemv(rows, nr, d, row_stride(d), xl, gpart, gres);
+                if (QR && gm.qc_rows) block_gemv_qrows(rows, nr, d, gm.qc_rows, gpart, gres);
+                else block_gemv(rows, nr, d, row_stride(d), xl, gpart, gres);
                 for (int i = tid; i < (nr >> 1); i += NT) {  // row0 and nr even: whole pairs
                     const int pr = (row0 >> 1) + i;
                     const float val = gres[2 * i] + gb_s[2 * pr], gate = gres[2 * i + 1] + gb_s[2 * pr + 1];
@@ -691,8 +716,9 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
         int bi = 0x7fffffff;
         const int lm_row0 = cta * gm.rlm;
         for_blocks(SEG_LM, 0, [&](const float* blk, const float* rows, int row0, int nr, bool first) {
-            if (first) layer_norm(blk);
-            block_gemv(rows, nr, d, row_stride(d), xl, gpart, gres);
+            if (first) layer_norm(blk, gm.lm_qbits);
+            if (QR && gm.qc_lm) block_gemv_qrows(rows, nr, d, gm.qc_lm, gpart, gres);
+            else block_gemv(rows, nr, d, row_stride(d), xl, gpart, gres);
             for (int i = tid; i < nr; i += NT) {
                 const float v = gres[i];
                 const int row = lm_row0 + row0 + i;
@@ -801,32 +827,54 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
 size_t cluster_smem_bytes(const ClusterGeom& g, int d, int hd) {
     const int ro4 = (g.ro + 3) & ~3;
     const size_t floats = (size_t)2 * g.skv_keys * hd + 2 * d + 3 * hd + hd + 2 * CL * (hd + 4) + d + hd +
-                          NW * (hd + 4) + ((g.gr + 3) & ~3) + 2 * g.gr + ro4 + NW * 32 + NW * 64 + 64;
+                          NW * (hd + 4) + ((g.gr + 3) & ~3) + 2 * g.gr + ro4 + NW * 32 + NW * 64 +
+                          (g.qbits || g.lm_qbits ? NT + d + d / 16 + 4 : 64);
     return (size_t)NSLOT * g.slot_bytes + floats * 4;
 }
 
 }  // namespace
 
-bool cluster_geom(int d, int H, int KVH, int hd, int I, int V, int L, int t_cap, ClusterGeom* g) {
+bool cluster_quant_ok(int d, int bits, int gs) {
+    if (!(bits == 2 || bits == 4 || bits == 8) || gs <= 0 || d % gs) return false;
+    return gs % (128 / bits) == 0;  // a 16-byte chunk of codes lies inside one group
+}
+
+bool cluster_geom(int d, int H, int KVH, int hd, int I, int V, int L, int t_cap, ClusterGeom* g, int qbits,
+                  int lm_qbits, int qgroup) {
     if (KVH != H || (d & 7) || (hd & 7) || hd > 64 || I % (H * CL) || ((I / (H * CL)) & 3)) return false;
+    if ((qbits && !cluster_quant_ok(d, qbits, qgroup)) || (lm_qbits && !cluster_quant_ok(d, lm_qbits, qgroup)))
+        return false;
     ClusterGeom r{};
+    r.qbits = qbits;
+    r.lm_qbits = lm_qbits;
+    r.qgroup = qbits || lm_qbits ? qgroup : 0;
+    r.rs_rows = qbits ? quant_row_stride(d, qbits, qgroup) : row_stride(d);
+    r.rs_lm = lm_qbits ? quant_row_stride(d, lm_qbits, qgroup) : row_stride(d);
+    r.qc_rows = qbits ? qbits | qgroup << 4 | r.rs_rows << 16 : 0;
+    r.qc_lm = lm_qbits ? lm_qbits | qgroup << 4 | r.rs_lm << 16 : 0;
     r.rq = (3 * hd + CL - 1) / CL;
     r.ro = (d + CL - 1) / CL;
     r.rcq = (hd + CL - 1) / CL;
     r.gr = I / (H * CL);
     r.rlm = (V + H * CL - 1) / (H * CL);
+    const int sd = rows_stride_d(r, d), sl = lm_stride(r, d);
     // ring slot: at least 52 KB, and large enough that a CTA's whole fc1 segment (header and
-    // every (value, gate) row pair, at most 64 rows) is one block
+    // every (value, gate) row pair, at most 64 fp32 / NT quantized rows) is one block; with a
+    // quantized LM head, large enough for NT of its rows behind the final-norm header when
+    // that stays within 56 KB
     {
-        const size_t fc1 = ((size_t)d + 2 * r.gr + (size_t)std::min(2 * r.gr, 64) * row_stride(d)) * 4;
-        r.slot_bytes = (int)std::max<size_t>(52 * 1024, (fc1 + 127) / 128 * 128);
+        const size_t fc1 = ((size_t)d + 2 * r.gr + (size_t)std::min(2 * r.gr, qbits ? NT : 64) * sd) * 4;
+        size_t want = std::max<size_t>(52 * 1024, fc1);
+        const size_t lm = ((size_t)d + (size_t)std::min(r.rlm, NT) * sl) * 4;
+        if (lm_qbits && lm <= 56 * 1024) want = std::max(want, lm);
+        r.slot_bytes = (int)((want + 127) / 128 * 128);
     }
     r.skv_keys = (t_cap + CL - 1) / CL;
     const Segs s = make_segs(r, d, hd);
-    r.cta_floats = (size_t)L * s.layer + (size_t)d + (size_t)r.rlm * row_stride(d);
+    r.cta_floats = (size_t)L * s.layer + (size_t)d + (size_t)r.rlm * sl;
     // every segment's first block (header + one row group) and a fp32 K/V frame fit a slot
     const size_t slot_f = (size_t)r.slot_bytes / 4;
-    if ((size_t)d + row_stride(d) > slot_f || (size_t)d + 2 * r.gr + 2 * row_stride(d) > slot_f ||
+    if ((size_t)d + std::max(sd, sl) > slot_f || (size_t)d + 2 * r.gr + 2 * sd > slot_f ||
         (size_t)s.ro4 + r.gr > slot_f ||
         (size_t)2 * hd * 4 > slot_f)
         return false;
@@ -840,11 +888,17 @@ int cluster_ctas(int H) { return H * CL; }
 // Packed per-CTA stream of the decoder weights in consumption order (see make_segs):
 // device-to-device copies, once per model.
 cudaError_t pack_cluster_weights(const ClusterGeom& g, const DecodeLayerW* layers_host, int L, const float* lm_head,
-                                 const float* final_ln, int d, int H, int hd, int I, int V, float* packed,
-                                 cudaStream_t s) {
+                                 const uint32_t* lm_q, const float* final_ln, int d, int H, int hd, int I, int V,
+                                 float* packed, cudaStream_t s) {
     const Segs sg = make_segs(g, d, hd);
     const int HD = H * hd;
-    const int sd = row_stride(d), sh = row_stride(hd);
+    const int sd = rows_stride_d(g, d), sh = row_stride(hd), sl = lm_stride(g, d);
+    // source rows of d inputs: fp32 rows (pitch d, d floats copied) or quantized records
+    // (pitch and copied width sd words)
+    const int rw = g.qbits ? sd : d;
+    if ((g.qbits && (!layers_host[0].qkv_q || !layers_host[0].cq_q || !layers_host[0].w1_q)) ||
+        (g.lm_qbits && !lm_q))
+        return cudaErrorInvalidValue;
     cudaError_t e = cudaSuccess;
     auto copy_rows = [&](float* dst, const float* src, size_t row_floats, size_t src_pitch_floats, size_t nrows,
                          size_t dst_pitch_floats) {
@@ -864,10 +918,13 @@ cudaError_t pack_cluster_weights(const ClusterGeom& g, const DecodeLayerW* layer
                 float* lw = base + (size_t)l * sg.layer;
                 // QKV: ln1, then head c's q|k|v rows: local row i -> global (i / hd) * HD + c * hd + i % hd
                 copy_vec(lw + sg.qkv, W.ln1, d);
+                const float* qkv = g.qbits ? reinterpret_cast<const float*>(W.qkv_q) : W.wqkv;
+                const float* cq = g.qbits ? reinterpret_cast<const float*>(W.cq_q) : W.wcq;
+                const float* w1 = g.qbits ? reinterpret_cast<const float*>(W.w1_q) : W.w1;
                 for (int i = r * g.rq; i < std::min(3 * hd, (r + 1) * g.rq);) {
                     const int grp = i / hd, end = std::min(std::min(3 * hd, (r + 1) * g.rq), (grp + 1) * hd);
                     copy_rows(lw + sg.qkv + d + (size_t)(i - r * g.rq) * sd,
-                              W.wqkv + ((size_t)grp * HD + c * hd + i % hd) * d, d, d, end - i, sd);
+                              qkv + ((size_t)grp * HD + c * hd + i % hd) * rw, rw, rw, end - i, sd);
                     i = end;
                 }
                 const int r0o = r * g.ro, no = std::max(0, std::min(g.ro, d - r0o));
@@ -875,15 +932,15 @@ cudaError_t pack_cluster_weights(const ClusterGeom& g, const DecodeLayerW* layer
                 copy_rows(lw + sg.co, W.wco + (size_t)r0o * HD + c * hd, hd, HD, no, sh);
                 const int r0q = r * g.rcq, ncq = std::max(0, std::min(g.rcq, hd - r0q));
                 copy_vec(lw + sg.cq, W.ln2, d);
-                copy_rows(lw + sg.cq + d, W.wcq + ((size_t)c * hd + r0q) * d, d, d, ncq, sd);
+                copy_rows(lw + sg.cq + d, cq + ((size_t)c * hd + r0q) * rw, rw, rw, ncq, sd);
                 // FC1: ln3, (value, gate) bias pairs, (value, gate) row pairs
                 const int jb = c * g.gr * CL + r * g.gr;
                 float* f1 = lw + sg.fc1;
                 copy_vec(f1, W.ln3, d);
                 copy_rows(f1 + d, W.b1 + jb, 1, 1, g.gr, 2);
                 copy_rows(f1 + d + 1, W.b1 + I + jb, 1, 1, g.gr, 2);
-                copy_rows(f1 + d + 2 * g.gr, W.w1 + (size_t)jb * d, d, d, g.gr, 2 * sd);
-                copy_rows(f1 + d + 2 * g.gr + sd, W.w1 + ((size_t)I + jb) * d, d, d, g.gr, 2 * sd);
+                copy_rows(f1 + d + 2 * g.gr, w1 + (size_t)jb * rw, rw, rw, g.gr, 2 * sd);
+                copy_rows(f1 + d + 2 * g.gr + sd, w1 + ((size_t)I + jb) * rw, rw, rw, g.gr, 2 * sd);
                 // FC2: b2 slice of this rank's reduce-scatter range, then W2[:, jb .. jb + gr)
                 copy_vec(lw + sg.fc2, W.b2 + r0o, no);
                 copy_rows(lw + sg.fc2 + sg.ro4, W.w2 + jb, g.gr, I, d, g.gr);
@@ -891,18 +948,22 @@ cudaError_t pack_cluster_weights(const ClusterGeom& g, const DecodeLayerW* layer
             float* lm = base + (size_t)L * sg.layer;
             copy_vec(lm, final_ln, d);
             const int r0 = cta * g.rlm, nr = std::max(0, std::min(g.rlm, V - r0));
-            copy_rows(lm + d, lm_head + (size_t)r0 * d, d, d, nr, sd);
+            if (g.lm_qbits)
+                copy_rows(lm + d, reinterpret_cast<const float*>(lm_q) + (size_t)r0 * sl, sl, sl, nr, sl);
+            else
+                copy_rows(lm + d, lm_head + (size_t)r0 * d, d, d, nr, sl);
         }
     return e;
 }
 
 cudaError_t launch_decode_cluster(const DecodeParams& p, const ClusterGeom& g, cudaStream_t stream) {
     const void* fn = nullptr;
+    const bool qr = g.qc_rows || g.qc_lm;
     switch (p.hd) {
-        case 32: fn = (const void*)decode_cluster_kernel<32>; break;
-        case 40: fn = (const void*)decode_cluster_kernel<40>; break;
-        case 48: fn = (const void*)decode_cluster_kernel<48>; break;
-        case 64: fn = (const void*)decode_cluster_kernel<64>; break;
+        case 32: fn = qr ? (const void*)decode_cluster_kernel<32, true> : (const void*)decode_cluster_kernel<32, false>; break;
+        case 40: fn = qr ? (const void*)decode_cluster_kernel<40, true> : (const void*)decode_cluster_kernel<40, false>; break;
+        case 48: fn = qr ? (const void*)decode_cluster_kernel<48, true> : (const void*)decode_cluster_kernel<48, false>; break;
+        case 64: fn = qr ? (const void*)decode_cluster_kernel<64, true> : (const void*)decode_cluster_kernel<64, false>; break;
         default: return cudaErrorInvalidValue;
     }
     if (p.KVH != p.H || p.t_cap > g.skv_keys * CL || !g.packed || !g.part) return cudaErrorInvalidValue;

@@ -162,7 +162,23 @@ struct DecodeLayerW {
     const float* ln1;    // [d]
     const float* ln2;    // [d]
     const float* ln3;    // [d]
+    // Affine-quantized row records of q|k|v, cross q and fc1 (quant_row_stride words per row:
+    // the checkpoint's packed codes, then one (scale, bias) float pair per group), or null.
+    // Only the clustered batch-1 kernel reads them; every other kernel uses the fp32 rows.
+    const uint32_t* qkv_q;
+    const uint32_t* cq_q;
+    const uint32_t* w1_q;
 };
+
+// Words per quantized row record of rf inputs: rf * bits / 32 code words, then rf / gs
+// (scale, bias) float pairs, padded to an odd number of 16-byte units so that lanes owning
+// consecutive rows read distinct shared-memory bank groups.
+__host__ __device__ inline int quant_row_stride(int rf, int bits, int gs) {
+    const int words = rf * bits / 32 + 2 * (rf / gs);
+    int units = (words + 3) / 4;
+    if (!(units & 1)) ++units;
+    return units * 4;
+}
 
 struct DecodeParams {
     int d, H, KVH, hd, I, V, L, nd;   // dims; nd = rotary dims
@@ -253,13 +269,23 @@ struct ClusterGeom {
     float l2_keep = 0.f;                          // > 0: this fraction of the streamed weight and
                                                   // cross K/V lines is loaded L2 evict_last, the rest
                                                   // evict_first (the stream is re-read every token)
+    int qbits = 0, lm_qbits = 0, qgroup = 0;      // > 0: the q|k|v, cross q and fc1 rows (qbits) and
+                                                  // the LM-head rows (lm_qbits) are streamed as
+                                                  // quantized records (2, 4 or 8 bits, groups of qgroup)
+    int rs_rows = 0, rs_lm = 0;                   // stored row strides (words) of those rows
+    int qc_rows = 0, qc_lm = 0;                   // bits | group << 4 | stride << 16, 0 = fp32 rows
 };
+// Whether the clustered kernel can stream rows of d inputs quantized to `bits` in groups of
+// gs: every 16-byte chunk of codes must lie inside one group.
+bool cluster_quant_ok(int d, int bits, int gs);
 // false when the dims do not fit the clustered kernel (the caller keeps decode_b1)
-bool cluster_geom(int d, int H, int KVH, int hd, int I, int V, int L, int t_cap, ClusterGeom* g);
+bool cluster_geom(int d, int H, int KVH, int hd, int I, int V, int L, int t_cap, ClusterGeom* g, int qbits = 0,
+                  int lm_qbits = 0, int qgroup = 0);
 int cluster_ctas(int H);
+// lm_q: quantized LM-head records (when g.lm_qbits), else lm_head's fp32 rows are packed.
 cudaError_t pack_cluster_weights(const ClusterGeom& g, const DecodeLayerW* layers_host, int L, const float* lm_head,
-                                 const float* final_ln, int d, int H, int hd, int I, int V, float* packed,
-                                 cudaStream_t s);
+                                 const uint32_t* lm_q, const float* final_ln, int d, int H, int hd, int I, int V,
+                                 float* packed, cudaStream_t s);
 cudaError_t launch_decode_cluster(const DecodeParams& p, const ClusterGeom& g, cudaStream_t stream);
 
 // Word-timestamp alignment rows from the cross queries a decode stored (qc_trace) and the

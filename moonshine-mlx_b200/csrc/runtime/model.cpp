@@ -331,6 +331,34 @@ struct WeightSource {
             }
         return w;
     }
+    bool is_quantized(const std::string& k) const {
+        auto it = byname.find(k);
+        return q_bits > 0 && it != byname.end() && it->second->dtype == "U32";
+    }
+    // Rows of a quantized Linear as the clustered decode kernel streams them: per row its
+    // packed codes (in * q_bits / 32 words, as stored), then one (scale, bias) fp32 pair per
+    // group, zero padded to quant_row_stride words.
+    std::vector<uint32_t> quant_records(const std::string& k, int64_t out, int64_t in) const {
+        if (!is_quantized(k) || in % q_group)
+            throw MsError(MS_ERR_BAD_WEIGHTS, "unexpected quantized tensor " + k);
+        const std::string base = k.substr(0, k.size() - std::string(".weight").size());
+        const int per = 32 / q_bits;
+        const int64_t ng = in / q_group, cw = in / per;
+        const Tensor& packed = need(k, {out, cw});
+        const std::vector<float> sc = to_f32(need(base + ".scales", {out, ng}));
+        const std::vector<float> bi = to_f32(need(base + ".biases", {out, ng}));
+        const int rs = quant_row_stride((int)in, q_bits, q_group);
+        std::vector<uint32_t> r((size_t)out * rs, 0u);
+        for (int64_t o = 0; o < out; ++o) {
+            uint32_t* dst = r.data() + (size_t)o * rs;
+            std::memcpy(dst, packed.data + (size_t)o * cw * 4, (size_t)cw * 4);
+            for (int64_t g = 0; g < ng; ++g) {
+                std::memcpy(dst + cw + 2 * g, &sc[(size_t)o * ng + g], 4);
+                std::memcpy(dst + cw + 2 * g + 1, &bi[(size_t)o * ng + g], 4);
+            }
+        }
+        return r;
+    }
     // Conv weight as [out][k][in] from HF [out,in,k] or MLX [out,k,in].
     std::vector<float> conv(const std::string& k, int out, int in, int ks) const {
         if (hf) {
@@ -365,6 +393,14 @@ Model::~Model() {
     for (auto& e : ev)
         if (e) cudaEventDestroy(e);
     if (stream) cudaStreamDestroy(stream);
+}
+
+const uint32_t* Model::upload_words(const std::vector<uint32_t>& v) {
+    DevBuf* b = new DevBuf();
+    owned.push_back(b);
+    b->ensure(std::max<size_t>(16, v.size() * sizeof(uint32_t)));
+    MSB_CUDA(cudaMemcpy(b->p, v.data(), v.size() * sizeof(uint32_t), cudaMemcpyHostToDevice));
+    return reinterpret_cast<const uint32_t*>(b->p);
 }
 
 float* Model::upload(const std::vector<float>& v) {
@@ -481,10 +517,38 @@ Model* load_model(const std::string& dir, const ms_options& o) {
     m->embed = m->upload(ws.f32("decoder.embed_tokens.weight", {c.vocab, d}));
     m->pos_emb = m->upload(ws.f32("decoder.pos_emb.weight", {c.max_pos, ed}));
     if (ed != d) m->proj = m->upload(ws.f32("decoder.proj.weight", {d, ed}));
+    // Quantized checkpoints: unless fp32 weights or the single-grid kernel are asked for, the
+    // clustered batch-1 kernel streams the rows of d inputs it splits by rows (q|k|v, cross q,
+    // fc1, and an untied LM head) as the checkpoint's codes with their scales and biases, not
+    // as fp32 rows.
+    static const char* const kRowKeys[] = {"self_attn.q_proj.weight", "self_attn.k_proj.weight",
+                                           "self_attn.v_proj.weight", "encoder_attn.q_proj.weight",
+                                           "mlp.fc1.weight"};
+    if (c.quantized && o.weight_dtype != MS_W_F32 && o.decode_kernel != MS_DECODE_GRID &&
+        cluster_quant_ok(d, c.q_bits, c.q_group)) {
+        bool all = true;
+        for (int i = 0; i < c.layers; ++i)
+            for (const char* k : kRowKeys) all = all && ws.is_quantized("decoder.layers." + std::to_string(i) + "." + k);
+        m->cl_qbits = all ? c.q_bits : 0;
+        m->cl_lm_qbits = !c.tie && ws.is_quantized("proj_out.weight") ? c.q_bits : 0;
+    }
+    auto records = [&](const std::string& p, std::initializer_list<std::pair<const char*, int>> parts) {
+        std::vector<uint32_t> r;
+        for (const auto& kp : parts) {
+            const std::vector<uint32_t> x = ws.quant_records(p + kp.first, kp.second, d);
+            r.insert(r.end(), x.begin(), x.end());
+        }
+        return m->upload_words(r);
+    };
     std::vector<float> crossw;
     for (int i = 0; i < c.layers; ++i) {
         const std::string p = "decoder.layers." + std::to_string(i) + ".";
         DecodeLayerW L{};
+        if (m->cl_qbits) {
+            L.qkv_q = records(p, {{kRowKeys[0], HD}, {kRowKeys[1], KVD}, {kRowKeys[2], KVD}});
+            L.cq_q = records(p, {{kRowKeys[3], HD}});
+            L.w1_q = records(p, {{kRowKeys[4], 2 * c.inter}});
+        }
         std::vector<float> qkv = ws.f32(p + "self_attn.q_proj.weight", {HD, d});
         append(qkv, ws.f32(p + "self_attn.k_proj.weight", {KVD, d}));
         append(qkv, ws.f32(p + "self_attn.v_proj.weight", {KVD, d}));
@@ -506,6 +570,7 @@ Model* load_model(const std::string& dir, const ms_options& o) {
     m->cross_w = m->upload(crossw);
     m->dec_norm = m->upload(ws.f32("decoder.norm.weight", {d}));
     m->lm_head = c.tie ? m->embed : m->upload(ws.f32("proj_out.weight", {c.vocab, d}));
+    if (m->cl_lm_qbits) m->lm_q = records("", {{"proj_out.weight", c.vocab}});
     m->dec_layers_buf.ensure(sizeof(DecodeLayerW) * m->dec.size());
     MSB_CUDA(cudaMemcpy(m->dec_layers_buf.p, m->dec.data(), sizeof(DecodeLayerW) * m->dec.size(),
                         cudaMemcpyHostToDevice));
@@ -735,12 +800,14 @@ bool Model::prepare_cluster_decode() {
     cl_tried = true;
     const Config& c = cfg;
     ClusterGeom g;
-    if (!cluster_geom(c.hidden, c.heads, c.kv_heads, c.head_dim, c.inter, c.vocab, c.layers, 0, &g)) return false;
+    if (!cluster_geom(c.hidden, c.heads, c.kv_heads, c.head_dim, c.inter, c.vocab, c.layers, 0, &g, cl_qbits,
+                      cl_lm_qbits, c.q_group))
+        return false;
     cl_packed.ensure((size_t)cluster_ctas(c.heads) * g.cta_floats * 4);
     g.part_words = (size_t)2 * c.heads * c.hidden + (size_t)2 * cluster_ctas(c.heads);
     cl_part.ensure(g.part_words * 8);
-    MSB_CUDA(pack_cluster_weights(g, dec.data(), c.layers, lm_head, dec_norm, c.hidden, c.heads, c.head_dim, c.inter,
-                                  c.vocab, cl_packed.as<float>(), stream));
+    MSB_CUDA(pack_cluster_weights(g, dec.data(), c.layers, lm_head, lm_q, dec_norm, c.hidden, c.heads, c.head_dim,
+                                  c.inter, c.vocab, cl_packed.as<float>(), stream));
     g.packed = cl_packed.as<float>();
     g.part = cl_part.as<unsigned long long>();
     cl_geom = g;
@@ -819,7 +886,8 @@ Model::DecodeResult Model::decode(const float* cross32, const void* cross_stored
     if ((want == MS_DECODE_AUTO || want == MS_DECODE_CLUSTER) && prepare_cluster_decode()) {
         ClusterGeom g = cl_geom;
         ClusterGeom sized;
-        if (cluster_geom(c.hidden, c.heads, c.kv_heads, c.head_dim, c.inter, c.vocab, c.layers, ws.t_cap, &sized)) {
+        if (cluster_geom(c.hidden, c.heads, c.kv_heads, c.head_dim, c.inter, c.vocab, c.layers, ws.t_cap, &sized,
+                         cl_qbits, cl_lm_qbits, c.q_group)) {
             g.skv_keys = sized.skv_keys;
             g.l2_keep = kL2Keep;
             MSB_CUDA(cudaMemsetAsync(g.part, 0, g.part_words * 8, stream));  // no stale exchange word

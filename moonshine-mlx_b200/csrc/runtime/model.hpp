@@ -123,6 +123,10 @@ struct Model {
     bool cl_tried = false, cl_ok = false;
     ClusterGeom cl_geom;
     DevBuf cl_packed, cl_part;
+    // quantized checkpoints: bits of the quantized row records the clustered kernel streams
+    // for q|k|v, cross q and fc1 (DecodeLayerW::*_q) and for the LM head (lm_q); 0 = fp32 rows
+    int cl_qbits = 0, cl_lm_qbits = 0;
+    const uint32_t* lm_q = nullptr;
     bool prepare_cluster_decode();
     std::unique_ptr<BatchEngine> batch;  // batched bf16 tensor-core decode, built on first use
     bool trace_enabled = false;
@@ -131,6 +135,7 @@ struct Model {
 
     ~Model();
     float* upload(const std::vector<float>& v);
+    const uint32_t* upload_words(const std::vector<uint32_t>& v);
     void ensure_rope(int positions);
 
     // --- orchestration (all on `stream`)

@@ -20,7 +20,7 @@ from __future__ import annotations
 import ctypes as C
 import os
 from dataclasses import dataclass, field
-from typing import Callable, List, Optional, Sequence
+from typing import Callable, List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -107,6 +107,7 @@ def _load_lib() -> C.CDLL:
         "ms_model_free": (None, [P]),
         "ms_model_enable_fp16_kv_cache": (C.c_int, [P, C.c_int32]),
         "ms_model_sample_rate": (C.c_int32, [P]),
+        "ms_model_decode_weight_bits": (C.c_int32, [P, C.POINTER(C.c_int32)]),
         "ms_model_get_config": (C.c_int, [P, C.POINTER(_ModelConfig)]),
         "ms_generate": (C.c_int, [P, f32p, C.c_int64, C.POINTER(_GenParams), i32p, C.c_int32,
                                   i32p, f32p, C.POINTER(_GenStats)]),
@@ -330,20 +331,27 @@ class MoonshineModel:
         self.config = cfg
 
     @staticmethod
-    def load(path: str, device: int = 0, kv_fp16: bool = True, decode_kernel: str = "auto") -> "MoonshineModel":
+    def load(path: str, device: int = 0, kv_fp16: bool = True, decode_kernel: str = "auto",
+             weight_dtype: str = "auto") -> "MoonshineModel":
         """MoonshineModel.load(from:) for a local directory (MoonshineModel.swift:409-414).
 
         ``decode_kernel`` picks the batch-1 decode kernel: "auto" or "cluster" (one 8-CTA
         cluster per head when the dims and the GPU allow it, else single-grid) or "grid"
-        (single-grid persistent kernel)."""
+        (single-grid persistent kernel).  ``weight_dtype`` ("auto", "f32", "bf16") is
+        ms_weight_dtype: "f32" also makes the clustered kernel stream a quantized
+        checkpoint's rows dequantized instead of as codes."""
         kinds = {"auto": 0, "grid": 1, "cluster": 2}
         if decode_kernel not in kinds:
             raise ValueError("decode_kernel must be one of " + ", ".join(kinds))
+        wkinds = {"auto": 0, "f32": 1, "bf16": 2}
+        if weight_dtype not in wkinds:
+            raise ValueError("weight_dtype must be one of " + ", ".join(wkinds))
         o = _Options()
         _L().ms_options_default(C.byref(o))
         o.device = device
         o.kv_dtype = KV_F16 if kv_fp16 else KV_F32
         o.decode_kernel = kinds[decode_kernel]
+        o.weight_dtype = wkinds[weight_dtype]
         h = C.c_void_p()
         _check(_L().ms_model_load(path.encode(), C.byref(o), C.byref(h)))
         return MoonshineModel(h)
@@ -362,6 +370,14 @@ class MoonshineModel:
     @property
     def sample_rate(self) -> int:
         return int(_L().ms_model_sample_rate(self._h))
+
+    @property
+    def decode_weight_bits(self) -> Tuple[int, int]:
+        """(bits of the q|k|v / cross q / fc1 rows, bits of the LM-head rows) that the
+        clustered batch-1 kernel streams as quantized codes; 0 = fp32 rows."""
+        lm = C.c_int32()
+        rows = int(_L().ms_model_decode_weight_bits(self._h, C.byref(lm)))
+        return rows, int(lm.value)
 
     def enable_float16_kv_cache(self, enabled: bool) -> None:
         _check(_L().ms_model_enable_fp16_kv_cache(self._h, 1 if enabled else 0))

@@ -231,18 +231,32 @@ def test_temperature_sampling_batch(model_root):
     assert chi2 < 45.0, (chi2, counts, counts.sum() * p)
 
 
-@pytest.mark.parametrize("bits", [8, 4])
-def test_quantized_checkpoint(model_root, bits):
+@pytest.mark.parametrize("group,bits,streamed", [(64, 8, 8), (64, 4, 4), (64, 2, 2), (32, 4, 4), (32, 2, 0),
+                                                 (128, 4, 0)])
+def test_quantized_checkpoint(model_root, group, bits, streamed):
     """MLX affine-quantized checkpoints (ModelLoader.swift:47-49,103-111; config.json
-    "quantization": group_size 64): every Linear whose input width divides by 64 is stored as
-    packed codes + scales + biases.  The library dequantizes them at load; ids and logits
-    match the oracle on the same checkpoint at the fp32 tolerance."""
+    "quantization"): every Linear whose input width divides by the group size is stored as
+    packed codes + scales + biases.  The clustered batch-1 kernel streams the q|k|v, cross q,
+    fc1 and LM-head rows as those codes and multiplies them in the kernel (`streamed` bits;
+    0 where the rows are not quantized at d = 320 with groups of 128, or where a 16-byte
+    chunk of 2-bit codes would straddle two groups of 32); the single-grid kernel and
+    weight_dtype "f32" use the rows dequantized at load.  Ids and logits of all three match
+    the oracle on the same checkpoint at the fp32 tolerance, and the quantized stream's
+    logits match the dequantized stream's within 1e-4 relative (both fp32; the kernel factors
+    each group's scale out of its sum, a different rounding order that 32 dependent calls
+    compound to ~1e-5)."""
     import moonshine_b200 as mb
-    d = model_dir(model_root, "tiny", quant=(64, bits))
-    m = mb.MoonshineModel.load(d)
+    d = model_dir(model_root, "tiny", quant=(group, bits))
     audio = synth.synth_audio(105600, 0)
-    out = m.generate(audio, forced_len=32, return_logits=True)
     o = oracle_for(d)
     ids, _, logits, _ = o.greedy(o.memory_for(audio), 32, True, forced_len=32, keep_logits=True)
-    assert out.tokens == ids
-    assert_logits_close(out.logits[:32], logits, FP32_LOGIT_TOL)
+    outs = {}
+    for name, kw in (("cluster", {}), ("grid", {"decode_kernel": "grid"}), ("f32", {"weight_dtype": "f32"})):
+        m = mb.MoonshineModel.load(d, **kw)
+        assert m.decode_weight_bits == ((streamed, streamed) if name == "cluster" else (0, 0))
+        out = m.generate(audio, forced_len=32, return_logits=True)
+        assert out.tokens == ids, name
+        assert_logits_close(out.logits[:32], logits, FP32_LOGIT_TOL)
+        outs[name] = out.logits[:32]
+        m.close()
+    assert rel_err(outs["cluster"], outs["f32"]) < 1e-4
