@@ -61,10 +61,10 @@ def decode_bytes_per_launch(cfg, M, n_tokens, kv_bytes=2):
 # memory frames, fp16 KV) from an ncu capture of each batch-1 kernel; per-call traffic is
 # flat after the first call.
 NCU_DECODE_BYTES_16CALLS_1500F = {
-    "cluster": (854506752 + 3145984, "profiles/decode_cluster_tiny_30s_16tok.md"),
+    "cluster": (857855232 + 3086336, "profiles/decode_cluster_tiny_30s_16tok.md"),
     "grid": (830.744e6 + 5.621e6, "profiles/decode_b1_tiny_30s_16tok.md"),
 }
-DECODE_KERNEL_SYMBOL = {"cluster": "decode_cluster_kernel<40>", "grid": "decode_b1_kernel<40>"}
+DECODE_KERNEL_SYMBOL = {"cluster": "decode_cluster_kernel<40, 0>", "grid": "decode_b1_kernel<40>"}
 
 
 def decode_traffic_per_launch(M, n_tokens, kernel):
@@ -220,6 +220,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-timestamps", action="store_true", help="skip the word-timestamp leg")
+    ap.add_argument("--no-quantized", action="store_true", help="skip the 4-bit checkpoint leg")
     ap.add_argument("--seconds", type=float, default=30.0, help="audio length (profiling cases)")
     ap.add_argument("--tokens", type=int, default=200, help="forced decode length (profiling cases)")
     ap.add_argument("--flush-mb", type=int, default=512, help="L2-flush buffer written between steps")
@@ -345,6 +346,40 @@ def main():
               "overhead_ms": round(statistics.median(t_al) - statistics.median(t_gen), 3),
               "timing": "host wall clock around the public call (median of 3), L2 flushed before each"}
 
+    # ---- the same weights as an MLX affine 4-bit checkpoint (group 64), device-resident audio:
+    # the clustered kernel streams the LM head as codes (the default quant_stream)
+    qleg = None
+    if not args.no_quantized:
+        if rank == 0:
+            qpath = synth.ensure_model_dir(root, ARCH, seed=WEIGHT_SEED, quant=(64, 4))
+        barrier()
+        qpath = synth.ensure_model_dir(root, ARCH, seed=WEIGHT_SEED, quant=(64, 4))
+        qm = mb.MoonshineModel.load(qpath, device=local, kv_fp16=True)
+        qstream = torch.cuda.ExternalStream(qm.cuda_stream)
+        for _ in range(args.warmup):
+            qm.generate_device(audio_dev.data_ptr(), N_SAMPLES, ids_dev.data_ptr(), ids_dev.numel(), forced_len=FORCED)
+        q_evs, q_dec = [], []
+        torch.cuda.synchronize()
+        for k in range(min(args.steps, 8)):
+            with torch.cuda.stream(qstream):
+                flush.fill_(k & 0xFF)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(qstream)
+            n, st = qm.generate_device(audio_dev.data_ptr(), N_SAMPLES, ids_dev.data_ptr(), ids_dev.numel(),
+                                       forced_len=FORCED)
+            e1.record(qstream)
+            assert n == FORCED
+            q_evs.append((e0, e1))
+            q_dec.append(st.decode_ms)
+        torch.cuda.synchronize()
+        q_ms = statistics.mean(a.elapsed_time(b) for a, b in q_evs)
+        qleg = {"checkpoint": "MLX affine 4-bit, group 64 (same weights)", "streamed_bits": list(qm.decode_weight_bits),
+                "tokens_per_s": round(FORCED / (q_ms / 1e3), 2),
+                "ms_per_token_decode": round(statistics.mean(q_dec) / FORCED, 5),
+                "timing": "CUDA events per step (encode + decode), L2 flushed before each"}
+        del qm
+        barrier()
+
     if dist is not None:
         t = torch.tensor([t_rank, t_e2e], dtype=torch.float64, device=f"cuda:{local}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -385,6 +420,8 @@ def main():
         }
         if ts is not None:
             line["word_timestamps"] = ts
+        if qleg is not None:
+            line["quantized_4bit"] = qleg
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_oracle()
         print(json.dumps(line), flush=True)

@@ -73,10 +73,18 @@ typedef struct {
                                 (head-clustered when the dims and the GPU allow it, else
                                 single-grid) or MS_DECODE_GRID (single-grid persistent kernel).
                                 Both compute the same greedy loop. */
-    int32_t reserved[7];
+    int32_t quant_stream;    /* quantized checkpoints, clustered kernel: which weights stream as
+                                codes (MS_QSTREAM_*); ignored otherwise */
+    int32_t reserved[6];
 } ms_options;
 
 enum { MS_DECODE_AUTO = 0, MS_DECODE_GRID = 1, MS_DECODE_CLUSTER = 2 };
+
+/* MS_QSTREAM_ALL: q|k|v, cross q, fc1 and the LM head; MS_QSTREAM_LM: the LM head only;
+ * MS_QSTREAM_NONE: none (every row dequantized to fp32 at load); MS_QSTREAM_AUTO: the LM
+ * head only, which measured fastest for 2, 4 and 8 bits on the tiny model (ALL streams the
+ * fewest bytes but its small per-layer blocks cost more to dequantize than they save). */
+enum { MS_QSTREAM_AUTO = 0, MS_QSTREAM_ALL = 1, MS_QSTREAM_LM = 2, MS_QSTREAM_NONE = 3 };
 
 /* Fills *opts with the defaults (device 0, fp16 KV, auto weights, max_batch 64). */
 void ms_options_default(ms_options* opts);
@@ -109,8 +117,9 @@ void ms_model_free(ms_model* model);
 /* Code width of the weight rows the clustered batch-1 decode kernel streams for q|k|v,
  * cross q and fc1 of a quantized checkpoint (2, 4 or 8: the checkpoint's codes with their
  * per-group scale and bias, multiplied in the kernel), or 0 when it streams fp32 rows
- * (unquantized checkpoints, MS_W_F32, or dims the quantized rows do not fit).  *lm_bits (nullable)
- * receives the same for the LM head (0 when it is tied to the embedding). */
+ * (unquantized checkpoints, MS_W_F32, MS_DECODE_GRID, quant_stream other than
+ * MS_QSTREAM_ALL, or dims the quantized rows do not fit).  *lm_bits (nullable) receives the
+ * same for the LM head (0 when it is tied to the embedding or for MS_QSTREAM_NONE). */
 int32_t ms_model_decode_weight_bits(const ms_model* model, int32_t* lm_bits);
 
 /* MoonshineModel.enableFloat16KVCache(_:) (MoonshineModel.swift:60-65). */

@@ -158,20 +158,22 @@ __device__ __forceinline__ float quant_input_scale(int j, int bits) {
     return __uint_as_float((uint32_t)(127 - sh) << 23);
 }
 
-// The vector block_gemv_q reads, from vec [rf] (rf % 64 == 0): xq[j] = vec[j] *
-// quant_input_scale(j), then xq[rf + j / 16] = the sum of vec over inputs j .. j + 15.
-// Thread t handles inputs t, t + NT, ... (whole warps per iteration); no barrier.
-__device__ __noinline__ void quant_vector(const float* vec, float* xq, int rf, int bits) {
-    const int lane = threadIdx.x & 31;
-    for (int k = threadIdx.x; k < rf; k += NT) {
-        const float v = vec[k];
-        xq[k] = v * quant_input_scale(k, bits);
-        float t = v + __shfl_xor_sync(0xffffffffu, v, 8);
-        t += __shfl_xor_sync(0xffffffffu, t, 4);
-        t += __shfl_xor_sync(0xffffffffu, t, 2);
-        t += __shfl_xor_sync(0xffffffffu, t, 1);
-        if ((lane & 15) == 0) xq[rf + (k >> 4)] = t;
-    }
+#ifndef MSB_QGEMV_ATTR
+#define MSB_QGEMV_ATTR __noinline__
+#endif
+
+// Input k (value v) of the vector block_gemv_q reads, for rows of rf inputs (rf % 64 == 0):
+// xq[k] = v * quant_input_scale(k), and lane 16m of the warp stores xq[rf + k / 16] = the
+// sum of the 16 inputs its half warp holds.  Called by whole warps holding 32 consecutive
+// inputs (k = 32 w + lane).
+template <int BITS>
+__device__ __forceinline__ void quant_input(float v, int k, float* xq, int rf) {
+    xq[k] = v * quant_input_scale(k, BITS);
+    float t = v + __shfl_xor_sync(0xffffffffu, v, 8);
+    t += __shfl_xor_sync(0xffffffffu, t, 4);
+    t += __shfl_xor_sync(0xffffffffu, t, 2);
+    t += __shfl_xor_sync(0xffffffffu, t, 1);
+    if ((threadIdx.x & 15) == 0) xq[rf + (k >> 4)] = t;
 }
 
 // res[i] = W[i] . vec for a block of nr <= NT affine-quantized rows of rf inputs (the MLX
@@ -184,8 +186,8 @@ __device__ __noinline__ void quant_vector(const float* vec, float* xq, int rf, i
 // rounded up to a power of two) and each group's warps take the chunks round robin, their
 // partials summed per row in fixed order.  Ends with a barrier.
 template <int BITS>
-__device__ __noinline__ void block_gemv_q(const uint32_t* rows, int nr, int rf, int rs, int gs, const float* xq,
-                                          float* part, float* res) {
+__device__ MSB_QGEMV_ATTR void block_gemv_q(const uint32_t* rows, int nr, int rf, int rs, int gs, const float* xq,
+                                            float* part, float* res) {
     constexpr int PER = 32 / BITS;  // codes per word
     constexpr int CC = 4 * PER;     // inputs per 16-byte chunk of codes
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
@@ -226,17 +228,6 @@ __device__ __noinline__ void block_gemv_q(const uint32_t* rows, int nr, int rf, 
         }
     }
     __syncthreads();
-}
-
-// block_gemv_q for qcode = bits | group size << 4 | row stride << 16 (xq = res + NT).
-__device__ __noinline__ void block_gemv_qrows(const float* rows, int nr, int rf, int qcode, float* part,
-                                              float* res) {
-    const int bits = qcode & 15, gs = (qcode >> 4) & 0xfff, rs = qcode >> 16;
-    const uint32_t* qr = reinterpret_cast<const uint32_t*>(rows);
-    const float* xq = res + NT;
-    if (bits == 4) block_gemv_q<4>(qr, nr, rf, rs, gs, xq, part, res);
-    else if (bits == 8) block_gemv_q<8>(qr, nr, rf, rs, gs, xq, part, res);
-    else block_gemv_q<2>(qr, nr, rf, rs, gs, xq, part, res);
 }
 
 // Cross-attention key scoring layout (as the batched streaming kernel): G lanes per key,

@@ -147,10 +147,132 @@ __host__ __device__ inline int blocks_per_step(const ClusterGeom& g, const Segs&
 }
 
 
-// QR: the geometry streams quantized rows (gm.qc_rows / gm.qc_lm); the fp32 instantiation
-// carries none of their code.
-template <int HDT, bool QR>
+// xs[k] += the H clusters' partial words pb[q * d + k] of exchange `tag`, summed in cluster
+// order, for every k < d; each thread polls exactly the words it adds until their tags match
+// (or the CTA has failed; a wait past GSYNC_TIMEOUT_NS records DEV_BARRIER_TIMEOUT).  With
+// eight clusters and NT < d <= NT + NT / 4 it is one round of polls: element tid (8 words) and
+// a quarter of element NT + tid / 4 (words 2 (tid % 4), +1), all loads in flight together,
+// whose four pair sums meet by shuffles in fixed order.  Ends with a barrier; returns the
+// cycles spent polling.
+__device__ __forceinline__ long long add_cluster_partials(const unsigned long long* pb, float* xs, int d, int H,
+                                                          unsigned tag, volatile int* failed, unsigned* status) {
+    const int tid = threadIdx.x;
+    long long cyc = 0;
+    auto timed_out = [&](uint64_t& t0) {
+        if (t0 == 0) {
+            t0 = globaltimer_ns();
+        } else if (globaltimer_ns() - t0 > GSYNC_TIMEOUT_NS) {
+            atomicCAS(status, DEV_OK, DEV_BARRIER_TIMEOUT);
+            *failed = 1;
+            return true;
+        }
+        return false;
+    };
+    if (H == 8 && d > NT && d - NT <= NT / 4) {
+        const int e = d - NT, xi = tid >> 2, qq = (tid & 3) * 2;
+        const bool hasx = xi < e;
+        const int nb = hasx ? 2 : 0;
+        const unsigned long long* srcA = pb + tid;
+        const unsigned long long* srcB = pb + NT + min(xi, e - 1) + (size_t)qq * d;
+        unsigned long long va[8], vb[2] = {0ull, 0ull};
+#pragma unroll
+        for (int q = 0; q < 8; ++q) va[q] = ld_tagged(srcA + (size_t)q * d);
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+            if (q < nb) vb[q] = ld_tagged(srcB + (size_t)q * d);
+        const long long c0 = clock64();
+        uint64_t t0 = 0;
+        for (;;) {
+            bool done = true;
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                if ((unsigned)(va[q] >> 32) != tag) {
+                    done = false;
+                    va[q] = ld_tagged(srcA + (size_t)q * d);
+                }
+#pragma unroll
+            for (int q = 0; q < 2; ++q)
+                if (q < nb && (unsigned)(vb[q] >> 32) != tag) {
+                    done = false;
+                    vb[q] = ld_tagged(srcB + (size_t)q * d);
+                }
+            if (done || *failed || timed_out(t0)) break;
+        }
+        cyc = clock64() - c0;
+        float v = xs[tid];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v += __uint_as_float((uint32_t)va[q]);
+        xs[tid] = v;
+        const float s2 = __uint_as_float((uint32_t)vb[0]) + __uint_as_float((uint32_t)vb[1]);
+        const float o1 = __shfl_xor_sync(FULL, s2, 1);
+        const float pr = (tid & 1) ? o1 + s2 : s2 + o1;  // words 0-3 / 4-7 of the element
+        const float o2 = __shfl_xor_sync(FULL, pr, 2);
+        const float tot = (tid & 2) ? o2 + pr : pr + o2;
+        if (hasx && (tid & 3) == 0) xs[NT + xi] += tot;
+    } else {
+        for (int k = tid; k < d; k += NT) {
+            unsigned long long v[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+                if (q < H) v[q] = ld_tagged(pb + (size_t)q * d + k);
+            const long long c0 = clock64();
+            uint64_t t0 = 0;
+            for (;;) {
+                bool done = true;
+#pragma unroll
+                for (int q = 0; q < 16; ++q)
+                    if (q < H && (unsigned)(v[q] >> 32) != tag) {
+                        done = false;
+                        v[q] = ld_tagged(pb + (size_t)q * d + k);
+                    }
+                if (done || *failed || timed_out(t0)) break;
+            }
+            cyc += clock64() - c0;
+            float a = xs[k];
+            for (int q = 0; q < H; ++q) a += __uint_as_float((uint32_t)v[q]);
+            xs[k] = a;
+        }
+    }
+    __syncthreads();
+    return cyc;
+}
+// The same as one out-of-line copy: the quantized-row kernels (measured faster so; the fp32
+// kernel is faster with the body inlined at its three exchanges per layer).
+__device__ __noinline__ long long add_cluster_partials_call(const unsigned long long* pb, float* xs, int d, int H,
+                                                            unsigned tag, volatile int* failed, unsigned* status) {
+    return add_cluster_partials(pb, xs, d, H, tag, failed, status);
+}
+
+// xl = LN(xs) * wln over d inputs (every warp computes the statistics itself); for rows
+// quantized to qb (= QB) bits also the vector block_gemv_q reads (d % 64 == 0 there, so every
+// iteration covers whole warps).  One out-of-line copy serves every call site of the kernel,
+// so its instructions stay cached between the segments of a layer.  Ends with a barrier.
+template <int QB>
+__device__ __noinline__ void ln_vector(const float* xs, const float* wln, float* xl, int d, float* xq, int qb) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    float s = 0.f;
+    for (int k = lane; k < d; k += 32) s += xs[k];
+    const float mean = warp_sum(s) / (float)d;
+    float q = 0.f;
+    for (int k = lane; k < d; k += 32) {
+        const float e = xs[k] - mean;
+        q += e * e;
+    }
+    const float rstd = rsqrtf(warp_sum(q) / (float)d + 1e-5f);
+    for (int k = tid; k < d; k += NT) {
+        const float v = (xs[k] - mean) * rstd * wln[k];
+        xl[k] = v;
+        if constexpr (QB != 0)
+            if (qb) quant_input<QB>(v, k, xq, d);
+    }
+    __syncthreads();
+}
+
+// QB: code width of the quantized rows the geometry streams (gm.qbits / gm.lm_qbits, each QB
+// or 0); the fp32 instantiation (QB = 0) carries none of their code.
+template <int HDT, int QB>
 __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, ClusterGeom gm) {
+    constexpr bool QR = QB != 0;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t full[NSLOT];
     __shared__ int s_failed;
@@ -194,6 +316,7 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
     float* gpart = sc + NW * 32;                       // [NW][64] block_gemv warp partials
     float* gres = gpart + NW * 64;                     // [64] block_gemv results ([NT], then
                                                        // [d + d / 16] quantized GEMV input, when QR)
+    float* xq_s = gres + NT;
 
     if (tid == 0) {
         for (int i = 0; i < NSLOT; ++i) mbar_init(&full[i], 1);
@@ -304,6 +427,16 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
             first = false;
         }
     };
+    // block GEMV of rows of d inputs against xl: quantized records (rs words apart) or fp32 rows
+    auto rows_gemv = [&](const float* rows, int nr, bool quant, int rs) {
+        if constexpr (QR) {
+            if (quant) {
+                block_gemv_q<QB>(reinterpret_cast<const uint32_t*>(rows), nr, d, rs, gm.qgroup, xq_s, gpart, gres);
+                return;
+            }
+        }
+        block_gemv(rows, nr, d, row_stride(d), xl, gpart, gres);
+    };
     auto cbar = [&]() {
         const long long c0 = tr0 ? clock64() : 0;
         cluster_barrier();
@@ -341,95 +474,19 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
         for (int q = 0; q < 16; ++q)
             if (q < n) out[q] = (uint32_t)v[q];
     };
-    // wait_tagged for 8 words at srcA[q * stride] and nb <= 2 at srcB[q * stride], all loads of
-    // both groups in flight together (one L2 round trip when the words are already there)
-    auto wait_tagged_82 = [&](const unsigned long long* srcA, const unsigned long long* srcB, int nb,
-                              size_t stride, unsigned tag, uint32_t* outA, uint32_t* outB) {
-        unsigned long long va[8], vb[2];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) va[q] = ld_tagged(srcA + q * stride);
-#pragma unroll
-        for (int q = 0; q < 2; ++q)
-            if (q < nb) vb[q] = ld_tagged(srcB + q * stride);
-        const long long c0 = tr0 ? clock64() : 0;
-        uint64_t t0 = 0;
-        for (;;) {
-            bool done = true;
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-                if ((unsigned)(va[q] >> 32) != tag) {
-                    done = false;
-                    va[q] = ld_tagged(srcA + q * stride);
-                }
-#pragma unroll
-            for (int q = 0; q < 2; ++q)
-                if (q < nb && (unsigned)(vb[q] >> 32) != tag) {
-                    done = false;
-                    vb[q] = ld_tagged(srcB + q * stride);
-                }
-            if (done || s_failed) break;
-            if (t0 == 0) t0 = globaltimer_ns();
-            else if (globaltimer_ns() - t0 > GSYNC_TIMEOUT_NS) {
-                fail(DEV_BARRIER_TIMEOUT);
-                break;
-            }
-        }
-        if (tr0) cyc_poll += clock64() - c0;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) outA[q] = (uint32_t)va[q];
-#pragma unroll
-        for (int q = 0; q < 2; ++q) outB[q] = q < nb ? (uint32_t)vb[q] : 0u;
-    };
     // xl = LN(xs) * wln (wln in shared memory); for rows quantized to qb bits also the
     // vector block_gemv_q reads: xl pre-scaled per input, then sums over each 16 inputs
     // (d % 64 == 0 there, so every iteration below covers whole warps)
-    float* xq_s = gres + NT;
-    auto layer_norm = [&](const float* wln, int qb) {
-        float s = 0.f;
-        for (int k = lane; k < d; k += 32) s += xs[k];
-        const float mean = warp_sum(s) / (float)d;
-        float q = 0.f;
-        for (int k = lane; k < d; k += 32) {
-            const float e = xs[k] - mean;
-            q += e * e;
-        }
-        const float rstd = rsqrtf(warp_sum(q) / (float)d + 1e-5f);
-        for (int k = tid; k < d; k += NT) xl[k] = (xs[k] - mean) * rstd * wln[k];
-        if constexpr (QR)
-            if (qb) quant_vector(xl, xq_s, d, qb);  // reads only this thread's own xl elements
-        __syncthreads();
-    };
+    auto layer_norm = [&](const float* wln, int qb) { ln_vector<QB>(xs, wln, xl, d, xq_s, qb); };
     int par = 0;
     // xs += sum over clusters (fixed order) of partial[par][.] of exchange `epoch`
     auto add_partials = [&]() {
         const unsigned long long* pb = gm.part + (size_t)par * H * d;
-        if (H == 8 && d > NT && d - NT <= NT / 4) {
-            // one round of polls: element tid (8 words) and a quarter of element NT + tid / 4
-            // (words 2 (tid % 4), +1), whose four pair sums meet by shuffles in fixed order
-            const int e = d - NT, xi = tid >> 2, qq = (tid & 3) * 2;
-            const bool hasx = xi < e;
-            uint32_t ua[8], ub[2];
-            wait_tagged_82(pb + tid, pb + NT + min(xi, e - 1) + (size_t)qq * d, hasx ? 2 : 0, d, epoch, ua, ub);
-            float v = xs[tid];
-            for (int q = 0; q < 8; ++q) v += __uint_as_float(ua[q]);
-            xs[tid] = v;
-            const float s2 = __uint_as_float(ub[0]) + __uint_as_float(ub[1]);
-            const float o1 = __shfl_xor_sync(FULL, s2, 1);
-            const float pr = (tid & 1) ? o1 + s2 : s2 + o1;  // words 0-3 / 4-7 of the element
-            const float o2 = __shfl_xor_sync(FULL, pr, 2);
-            const float tot = (tid & 2) ? o2 + pr : pr + o2;
-            if (hasx && (tid & 3) == 0) xs[NT + xi] += tot;
-        } else {
-            for (int k = tid; k < d; k += NT) {
-                uint32_t u[16];
-                wait_tagged(pb + k, d, H, epoch, u);
-                float v = xs[k];
-                for (int q = 0; q < H; ++q) v += __uint_as_float(u[q]);
-                xs[k] = v;
-            }
-        }
+        long long cy;
+        if constexpr (QR) cy = add_cluster_partials_call(pb, xs, d, H, epoch, &s_failed, p.status);
+        else cy = add_cluster_partials(pb, xs, d, H, epoch, &s_failed, p.status);
+        if (tr0) cyc_poll += cy;
         par ^= 1;
-        __syncthreads();
     };
     // output-projection partial of head c: rows r*ro + i of W[:, head c] . attn_s
     auto out_proj = [&](int seg, int layer) {
@@ -533,8 +590,7 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
             // ---- LN1 + this CTA's q|k|v rows -> every CTA of the cluster
             for_blocks(SEG_QKV, l, [&](const float* blk, const float* rows, int row0, int nr, bool first) {
                 if (first) layer_norm(blk, gm.qbits);
-                if (QR && gm.qc_rows) block_gemv_qrows(rows, nr, d, gm.qc_rows, gpart, gres);
-                else block_gemv(rows, nr, d, row_stride(d), xl, gpart, gres);
+                rows_gemv(rows, nr, gm.qbits != 0, gm.rs_rows);
                 for (int e = tid; e < nr * CL; e += NT) {  // row i -> rank q
                     const int i = e / CL, q = e - (e / CL) * CL;
                     st_dsmem(mapa_rank(qkv_a + 4 * (r * gm.rq + row0 + i), q), gres[i]);
@@ -612,8 +668,7 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
             // ---- LN2 + cross q rows -> every CTA of the cluster
             for_blocks(SEG_CQ, l, [&](const float* blk, const float* rows, int row0, int nr, bool first) {
                 if (first) layer_norm(blk, gm.qbits);
-                if (QR && gm.qc_rows) block_gemv_qrows(rows, nr, d, gm.qc_rows, gpart, gres);
-                else block_gemv(rows, nr, d, row_stride(d), xl, gpart, gres);
+                rows_gemv(rows, nr, gm.qbits != 0, gm.rs_rows);
                 for (int e = tid; e < nr * CL; e += NT) {
                     const int i = e / CL, q = e - (e / CL) * CL;
                     st_dsmem(mapa_rank(qc_a + 4 * (r * gm.rcq + row0 + i), q), gres[i]);
@@ -670,8 +725,7 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
                     for (int i = tid; i < 2 * gm.gr; i += NT) gb_s[i] = blk[d + i];
                     layer_norm(blk, gm.qbits);  // ends with a barrier: gb_s is visible too
                 }
-                if (QR && gm.qc_rows) block_gemv_qrows(rows, nr, d, gm.qc_rows, gpart, gres);
-                else block_gemv(rows, nr, d, row_stride(d), xl, gpart, gres);
+                rows_gemv(rows, nr, gm.qbits != 0, gm.rs_rows);
                 for (int i = tid; i < (nr >> 1); i += NT) {  // row0 and nr even: whole pairs
                     const int pr = (row0 >> 1) + i;
                     const float val = gres[2 * i] + gb_s[2 * pr], gate = gres[2 * i + 1] + gb_s[2 * pr + 1];
@@ -717,8 +771,7 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
         const int lm_row0 = cta * gm.rlm;
         for_blocks(SEG_LM, 0, [&](const float* blk, const float* rows, int row0, int nr, bool first) {
             if (first) layer_norm(blk, gm.lm_qbits);
-            if (QR && gm.qc_lm) block_gemv_qrows(rows, nr, d, gm.qc_lm, gpart, gres);
-            else block_gemv(rows, nr, d, row_stride(d), xl, gpart, gres);
+            rows_gemv(rows, nr, gm.lm_qbits != 0, gm.rs_lm);
             for (int i = tid; i < nr; i += NT) {
                 const float v = gres[i];
                 const int row = lm_row0 + row0 + i;
@@ -850,8 +903,6 @@ bool cluster_geom(int d, int H, int KVH, int hd, int I, int V, int L, int t_cap,
     r.qgroup = qbits || lm_qbits ? qgroup : 0;
     r.rs_rows = qbits ? quant_row_stride(d, qbits, qgroup) : row_stride(d);
     r.rs_lm = lm_qbits ? quant_row_stride(d, lm_qbits, qgroup) : row_stride(d);
-    r.qc_rows = qbits ? qbits | qgroup << 4 | r.rs_rows << 16 : 0;
-    r.qc_lm = lm_qbits ? lm_qbits | qgroup << 4 | r.rs_lm << 16 : 0;
     r.rq = (3 * hd + CL - 1) / CL;
     r.ro = (d + CL - 1) / CL;
     r.rcq = (hd + CL - 1) / CL;
@@ -956,14 +1007,25 @@ cudaError_t pack_cluster_weights(const ClusterGeom& g, const DecodeLayerW* layer
     return e;
 }
 
+template <int HDT>
+const void* cluster_kernel_for(int qb) {
+    switch (qb) {
+        case 2: return (const void*)decode_cluster_kernel<HDT, 2>;
+        case 4: return (const void*)decode_cluster_kernel<HDT, 4>;
+        case 8: return (const void*)decode_cluster_kernel<HDT, 8>;
+        default: return (const void*)decode_cluster_kernel<HDT, 0>;
+    }
+}
+
 cudaError_t launch_decode_cluster(const DecodeParams& p, const ClusterGeom& g, cudaStream_t stream) {
     const void* fn = nullptr;
-    const bool qr = g.qc_rows || g.qc_lm;
+    const int qb = g.qbits ? g.qbits : g.lm_qbits;
+    if (g.qbits && g.lm_qbits && g.qbits != g.lm_qbits) return cudaErrorInvalidValue;
     switch (p.hd) {
-        case 32: fn = qr ? (const void*)decode_cluster_kernel<32, true> : (const void*)decode_cluster_kernel<32, false>; break;
-        case 40: fn = qr ? (const void*)decode_cluster_kernel<40, true> : (const void*)decode_cluster_kernel<40, false>; break;
-        case 48: fn = qr ? (const void*)decode_cluster_kernel<48, true> : (const void*)decode_cluster_kernel<48, false>; break;
-        case 64: fn = qr ? (const void*)decode_cluster_kernel<64, true> : (const void*)decode_cluster_kernel<64, false>; break;
+        case 32: fn = cluster_kernel_for<32>(qb); break;
+        case 40: fn = cluster_kernel_for<40>(qb); break;
+        case 48: fn = cluster_kernel_for<48>(qb); break;
+        case 64: fn = cluster_kernel_for<64>(qb); break;
         default: return cudaErrorInvalidValue;
     }
     if (p.KVH != p.H || p.t_cap > g.skv_keys * CL || !g.packed || !g.part) return cudaErrorInvalidValue;

@@ -273,7 +273,6 @@ struct ClusterGeom {
                                                   // the LM-head rows (lm_qbits) are streamed as
                                                   // quantized records (2, 4 or 8 bits, groups of qgroup)
     int rs_rows = 0, rs_lm = 0;                   // stored row strides (words) of those rows
-    int qc_rows = 0, qc_lm = 0;                   // bits | group << 4 | stride << 16, 0 = fp32 rows
 };
 // Whether the clustered kernel can stream rows of d inputs quantized to `bits` in groups of
 // gs: every 16-byte chunk of codes must lie inside one group.

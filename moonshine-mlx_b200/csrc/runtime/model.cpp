@@ -518,15 +518,20 @@ Model* load_model(const std::string& dir, const ms_options& o) {
     m->pos_emb = m->upload(ws.f32("decoder.pos_emb.weight", {c.max_pos, ed}));
     if (ed != d) m->proj = m->upload(ws.f32("decoder.proj.weight", {d, ed}));
     // Quantized checkpoints: unless fp32 weights or the single-grid kernel are asked for, the
-    // clustered batch-1 kernel streams the rows of d inputs it splits by rows (q|k|v, cross q,
-    // fc1, and an untied LM head) as the checkpoint's codes with their scales and biases, not
-    // as fp32 rows.
+    // clustered batch-1 kernel can stream the rows of d inputs it splits by rows (q|k|v, cross
+    // q, fc1, and an untied LM head) as the checkpoint's codes with their scales and biases
+    // instead of fp32 rows (ms_options.quant_stream).
     static const char* const kRowKeys[] = {"self_attn.q_proj.weight", "self_attn.k_proj.weight",
                                            "self_attn.v_proj.weight", "encoder_attn.q_proj.weight",
                                            "mlp.fc1.weight"};
+    if (o.quant_stream < MS_QSTREAM_AUTO || o.quant_stream > MS_QSTREAM_NONE)
+        throw MsError(MS_ERR_INVALID_ARG, "bad quant_stream");
     if (c.quantized && o.weight_dtype != MS_W_F32 && o.decode_kernel != MS_DECODE_GRID &&
-        cluster_quant_ok(d, c.q_bits, c.q_group)) {
-        bool all = true;
+        o.quant_stream != MS_QSTREAM_NONE && cluster_quant_ok(d, c.q_bits, c.q_group)) {
+        // AUTO streams the LM head only: on the tiny model at batch 1 that measured fastest for
+        // 2, 4 and 8 bits (the small per-layer row blocks gain less from fewer bytes than their
+        // in-kernel dequantization costs)
+        bool all = o.quant_stream == MS_QSTREAM_ALL;
         for (int i = 0; i < c.layers; ++i)
             for (const char* k : kRowKeys) all = all && ws.is_quantized("decoder.layers." + std::to_string(i) + "." + k);
         m->cl_qbits = all ? c.q_bits : 0;

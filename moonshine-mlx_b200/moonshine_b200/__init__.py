@@ -45,7 +45,8 @@ class MoonshineError(RuntimeError):
 
 class _Options(C.Structure):
     _fields_ = [("device", C.c_int32), ("kv_dtype", C.c_int32), ("weight_dtype", C.c_int32),
-                ("max_batch", C.c_int32), ("decode_kernel", C.c_int32), ("reserved", C.c_int32 * 7)]
+                ("max_batch", C.c_int32), ("decode_kernel", C.c_int32), ("quant_stream", C.c_int32),
+                ("reserved", C.c_int32 * 6)]
 
 
 class _GenParams(C.Structure):
@@ -332,14 +333,16 @@ class MoonshineModel:
 
     @staticmethod
     def load(path: str, device: int = 0, kv_fp16: bool = True, decode_kernel: str = "auto",
-             weight_dtype: str = "auto") -> "MoonshineModel":
+             weight_dtype: str = "auto", quant_stream: str = "auto") -> "MoonshineModel":
         """MoonshineModel.load(from:) for a local directory (MoonshineModel.swift:409-414).
 
         ``decode_kernel`` picks the batch-1 decode kernel: "auto" or "cluster" (one 8-CTA
         cluster per head when the dims and the GPU allow it, else single-grid) or "grid"
         (single-grid persistent kernel).  ``weight_dtype`` ("auto", "f32", "bf16") is
         ms_weight_dtype: "f32" also makes the clustered kernel stream a quantized
-        checkpoint's rows dequantized instead of as codes."""
+        checkpoint's rows dequantized instead of as codes.  ``quant_stream`` ("auto", "all",
+        "lm", "none") is MS_QSTREAM_*: which weights of a quantized checkpoint the clustered
+        kernel streams as codes."""
         kinds = {"auto": 0, "grid": 1, "cluster": 2}
         if decode_kernel not in kinds:
             raise ValueError("decode_kernel must be one of " + ", ".join(kinds))
@@ -352,6 +355,10 @@ class MoonshineModel:
         o.kv_dtype = KV_F16 if kv_fp16 else KV_F32
         o.decode_kernel = kinds[decode_kernel]
         o.weight_dtype = wkinds[weight_dtype]
+        qkinds = {"auto": 0, "all": 1, "lm": 2, "none": 3}
+        if quant_stream not in qkinds:
+            raise ValueError("quant_stream must be one of " + ", ".join(qkinds))
+        o.quant_stream = qkinds[quant_stream]
         h = C.c_void_p()
         _check(_L().ms_model_load(path.encode(), C.byref(o), C.byref(h)))
         return MoonshineModel(h)

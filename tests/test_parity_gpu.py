@@ -237,10 +237,11 @@ def test_quantized_checkpoint(model_root, group, bits, streamed):
     """MLX affine-quantized checkpoints (ModelLoader.swift:47-49,103-111; config.json
     "quantization"): every Linear whose input width divides by the group size is stored as
     packed codes + scales + biases.  The clustered batch-1 kernel streams the q|k|v, cross q,
-    fc1 and LM-head rows as those codes and multiplies them in the kernel (`streamed` bits;
+    fc1 and LM-head rows (quant_stream "all"; by default only the LM head) as those codes and
+    multiplies them in the kernel (`streamed` bits;
     0 where the rows are not quantized at d = 320 with groups of 128, or where a 16-byte
     chunk of 2-bit codes would straddle two groups of 32); the single-grid kernel and
-    weight_dtype "f32" use the rows dequantized at load.  Ids and logits of all three match
+    weight_dtype "f32" use the rows dequantized at load.  Ids and logits of all four match
     the oracle on the same checkpoint at the fp32 tolerance, and the quantized stream's
     logits match the dequantized stream's within 1e-4 relative (both fp32; the kernel factors
     each group's scale out of its sum, a different rounding order that 32 dependent calls
@@ -251,12 +252,15 @@ def test_quantized_checkpoint(model_root, group, bits, streamed):
     o = oracle_for(d)
     ids, _, logits, _ = o.greedy(o.memory_for(audio), 32, True, forced_len=32, keep_logits=True)
     outs = {}
-    for name, kw in (("cluster", {}), ("grid", {"decode_kernel": "grid"}), ("f32", {"weight_dtype": "f32"})):
+    expect = {"all": (streamed, streamed), "auto": (0, streamed), "grid": (0, 0), "f32": (0, 0)}
+    for name, kw in (("all", {"quant_stream": "all"}), ("auto", {}), ("grid", {"decode_kernel": "grid"}),
+                     ("f32", {"weight_dtype": "f32"})):
         m = mb.MoonshineModel.load(d, **kw)
-        assert m.decode_weight_bits == ((streamed, streamed) if name == "cluster" else (0, 0))
+        assert m.decode_weight_bits == expect[name], name
         out = m.generate(audio, forced_len=32, return_logits=True)
         assert out.tokens == ids, name
         assert_logits_close(out.logits[:32], logits, FP32_LOGIT_TOL)
         outs[name] = out.logits[:32]
         m.close()
-    assert rel_err(outs["cluster"], outs["f32"]) < 1e-4
+    assert rel_err(outs["all"], outs["f32"]) < 1e-4
+    assert rel_err(outs["auto"], outs["f32"]) < 1e-4
