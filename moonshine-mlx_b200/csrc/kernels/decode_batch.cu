@@ -60,6 +60,58 @@ __global__ void ln_bf16_kernel(const float* __restrict__ x, int rows, int d, con
         out[(size_t)r * d + i] = __float2bfloat16_rn((xr[i] - mean) * rstd * (w[i] + w_offset));
 }
 
+// The same LayerNorm with one warp per row for d % 4 == 0, d <= 32 * 4 * LNW_V4: the row
+// stays in registers (LNW_V4 float4 per lane) across the mean, variance and output passes,
+// reductions are warp shuffles only, LNW_ROWS rows per CTA.  x and w 16-byte aligned, out
+// 8-byte aligned.
+constexpr int LNW_ROWS = 8;
+constexpr int LNW_V4 = 8;
+__global__ void __launch_bounds__(LNW_ROWS * 32) ln_bf16_warp_kernel(const float* __restrict__ x, int rows, int d,
+                                                                     const float* __restrict__ w, float w_offset,
+                                                                     __nv_bfloat16* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
+    const int lane = threadIdx.x & 31;
+    const int r = blockIdx.x * LNW_ROWS + (threadIdx.x >> 5);
+    if (r >= rows) return;  // whole warps
+    const int n4 = d >> 2;
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)r * d);
+    float4 v[LNW_V4];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < LNW_V4; ++j) {
+        const int i = lane + 32 * j;
+        v[j] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+    }
+    const float mean = warp_sum(s) / (float)d;
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < LNW_V4; ++j)
+        if (lane + 32 * j < n4) {
+            const float a = v[j].x - mean, b = v[j].y - mean, c = v[j].z - mean, e = v[j].w - mean;
+            q += (a * a + b * b) + (c * c + e * e);
+        }
+    const float rstd = rsqrtf(warp_sum(q) / (float)d + 1e-5f);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(out + (size_t)r * d);
+#pragma unroll
+    for (int j = 0; j < LNW_V4; ++j) {
+        const int i = lane + 32 * j;
+        if (i < n4) {
+            const float4 g = w4[i];
+            const __nv_bfloat162 lo = __floats2bfloat162_rn((v[j].x - mean) * rstd * (g.x + w_offset),
+                                                            (v[j].y - mean) * rstd * (g.y + w_offset));
+            const __nv_bfloat162 hi = __floats2bfloat162_rn((v[j].z - mean) * rstd * (g.z + w_offset),
+                                                            (v[j].w - mean) * rstd * (g.w + w_offset));
+            uint2 pk;
+            pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+            pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+            *reinterpret_cast<uint2*>(o2 + 2 * i) = pk;
+        }
+    }
+}
+
 __device__ __forceinline__ float load_kv(const void* base, size_t idx, int f16) {
     return f16 ? __half2float(reinterpret_cast<const __half*>(base)[idx]) : reinterpret_cast<const float*>(base)[idx];
 }
@@ -448,6 +500,11 @@ cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv
                           float w_offset) {
     if (rows <= 0) return cudaSuccess;
     ++launch_counter();
+    const bool warp_rows = d % 4 == 0 && d <= 32 * 4 * LNW_V4 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+                           reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 8 == 0;
+    if (warp_rows)
+        return launch_kernel(ln_bf16_warp_kernel, dim3((rows + LNW_ROWS - 1) / LNW_ROWS), dim3(LNW_ROWS * 32), 0, s,
+                             x, rows, d, w, w_offset, out);
     return launch_kernel(ln_bf16_kernel, dim3(rows), dim3(128), 0, s, x, rows, d, w, w_offset, out);
 }
 
