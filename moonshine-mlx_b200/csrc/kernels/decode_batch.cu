@@ -116,7 +116,8 @@ __device__ __forceinline__ float load_kv(const void* base, size_t idx, int f16) 
     return f16 ? __half2float(reinterpret_cast<const __half*>(base)[idx]) : reinterpret_cast<const float*>(base)[idx];
 }
 
-// One warp per (b, h).  Lanes own keys for the scores, dims (2c, 2c+1) for the V sum.
+// One warp per (b, h), eight per CTA.  Lanes own keys for the scores (each reads its key row
+// in 16-byte loads against q staged in shared memory), dims (2c, 2c+1) for the V sum.
 __global__ void self_attn_batch_kernel(const float* __restrict__ q, const float* __restrict__ kv_new,
                                        const void* __restrict__ kc, const void* __restrict__ vc, int kv_f16,
                                        const int* __restrict__ pos, int B, int H, int KVH, int hd, int t_cap,
@@ -134,15 +135,46 @@ __global__ void self_attn_batch_kernel(const float* __restrict__ q, const float*
     const float* fk = kv_new + (size_t)b * 2 * KVD + kvh * hd;
     const float* fv = fk + KVD;
     const size_t cb = ((size_t)b * KVH + kvh) * t_cap * hd;
+    // this head's q, staged once per warp and read back as broadcast float4s
+    __shared__ __align__(16) float qsh[8][MAXHD_B];
+    float* qw = qsh[(threadIdx.x >> 5) & 7];
+    for (int c = lane; c < hd; c += 32) qw[c] = qr[c];
+    __syncwarp();
+    const float4* q4 = reinterpret_cast<const float4*>(qw);
     float m = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f;
     for (int j0 = 0; j0 <= t; j0 += CHB) {
         const int nk = min(CHB, t + 1 - j0);
         const int j = j0 + lane;
         float s = -INFINITY;
         if (lane < nk) {
+            // the lane's key row in 16-byte loads (hd % 8 == 0: rows start 16-byte aligned)
             float dot = 0.f;
-            for (int c = 0; c < hd; ++c)
-                dot = fmaf(qr[c], (j == t) ? fk[c] : load_kv(kc, cb + (size_t)j * hd + c, kv_f16), dot);
+            if (j == t) {
+                const float4* k4 = reinterpret_cast<const float4*>(fk);
+                for (int p = 0; p < hd / 4; ++p) {
+                    const float4 kv = k4[p], qq = q4[p];
+                    dot = fmaf(qq.x, kv.x, fmaf(qq.y, kv.y, fmaf(qq.z, kv.z, fmaf(qq.w, kv.w, dot))));
+                }
+            } else if (kv_f16) {
+                const uint4* k8 = reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(kc) + cb + (size_t)j * hd);
+#pragma unroll 4
+                for (int p = 0; p < hd / 8; ++p) {
+                    const uint4 u = k8[p];
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+                    const float4 qa = q4[2 * p], qb = q4[2 * p + 1];
+                    const float2 f0 = __half22float2(h2[0]), f1 = __half22float2(h2[1]);
+                    const float2 f2 = __half22float2(h2[2]), f3 = __half22float2(h2[3]);
+                    dot = fmaf(qa.x, f0.x, fmaf(qa.y, f0.y, fmaf(qa.z, f1.x, fmaf(qa.w, f1.y, dot))));
+                    dot = fmaf(qb.x, f2.x, fmaf(qb.y, f2.y, fmaf(qb.z, f3.x, fmaf(qb.w, f3.y, dot))));
+                }
+            } else {
+                const float4* k4 = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kc) + cb + (size_t)j * hd);
+#pragma unroll 4
+                for (int p = 0; p < hd / 4; ++p) {
+                    const float4 kv = k4[p], qq = q4[p];
+                    dot = fmaf(qq.x, kv.x, fmaf(qq.y, kv.y, fmaf(qq.z, kv.z, fmaf(qq.w, kv.w, dot))));
+                }
+            }
             s = dot * scale;
         }
         const float mc = warp_max(s);
@@ -161,9 +193,16 @@ __global__ void self_attn_batch_kernel(const float* __restrict__ q, const float*
                 if (row == t) {
                     v0 = fv[c];
                     v1 = fv[c + 1];
+                } else if (kv_f16) {
+                    const float2 f = __half22float2(
+                        *reinterpret_cast<const __half2*>(reinterpret_cast<const __half*>(vc) + cb + (size_t)row * hd + c));
+                    v0 = f.x;
+                    v1 = f.y;
                 } else {
-                    v0 = load_kv(vc, cb + (size_t)row * hd + c, kv_f16);
-                    v1 = load_kv(vc, cb + (size_t)row * hd + c + 1, kv_f16);
+                    const float2 f =
+                        *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(vc) + cb + (size_t)row * hd + c);
+                    v0 = f.x;
+                    v1 = f.y;
                 }
                 a0 = fmaf(pp, v0, a0);
                 a1 = fmaf(pp, v1, a1);
@@ -511,7 +550,7 @@ cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv
 cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const void* kc, const void* vc, int kv_f16,
                                    const int* pos, int B, int H, int KVH, int hd, int t_cap, float scale,
                                    __nv_bfloat16* out, cudaStream_t s) {
-    if (hd > MAXHD_B || (hd & 1)) return cudaErrorInvalidValue;
+    if (hd > MAXHD_B || (hd & 7)) return cudaErrorInvalidValue;
     ++launch_counter();
     const int items = B * H;
     return launch_kernel(self_attn_batch_kernel, dim3((items + 7) / 8), dim3(256), 0, s, q, kv_new, kc, vc, kv_f16,
