@@ -115,7 +115,7 @@ __host__ __device__ inline SegPlan seg_plan(int seg, int layer, const ClusterGeo
         case SEG_CO: return {lw + sg.co, 0, no, row_stride(hd), 1, 64};
         case SEG_FC1: return {lw + sg.fc1, d + 2 * g.gr, 2 * g.gr, sd, 2, mq};
         case SEG_FC2: return {lw + sg.fc2, sg.ro4, d, g.gr, 1, 64};
-        default: return {(size_t)L * sg.layer, d, nlm, lm_stride<QR>(g, d), 1, QR && g.lm_qbits ? NT : 64};
+        default: return {(size_t)L * sg.layer, d, nlm, lm_stride<QR>(g, d), 1, QR && g.lm_qbits ? NT : 32};
     }
 }
 
