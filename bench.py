@@ -374,7 +374,7 @@ def main():
         torch.cuda.synchronize()
         q_ms = statistics.mean(a.elapsed_time(b) for a, b in q_evs)
         qleg = {"checkpoint": "MLX affine 4-bit, group 64 (same weights)", "streamed_bits": list(qm.decode_weight_bits),
-                "tokens_per_s": round(FORCED / (q_ms / 1e3), 2),
+                "tokens_per_s_per_gpu": round(FORCED / (q_ms / 1e3), 2),
                 "ms_per_token_decode": round(statistics.mean(q_dec) / FORCED, 5),
                 "timing": "CUDA events per step (encode + decode), L2 flushed before each"}
         del qm
