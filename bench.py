@@ -221,6 +221,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-timestamps", action="store_true", help="skip the word-timestamp leg")
     ap.add_argument("--no-quantized", action="store_true", help="skip the 4-bit checkpoint leg")
+    ap.add_argument("--batched", action="store_true",
+                    help="add the batched leg: small architecture, bf16 weights, 64 utterances of 5-15 s, "
+                         "128 forced tokens each")
     ap.add_argument("--seconds", type=float, default=30.0, help="audio length (profiling cases)")
     ap.add_argument("--tokens", type=int, default=200, help="forced decode length (profiling cases)")
     ap.add_argument("--flush-mb", type=int, default=512, help="L2-flush buffer written between steps")
@@ -380,6 +383,37 @@ def main():
         del qm
         barrier()
 
+    # ---- batched generation (ms_generate_batch): small architecture, bf16 checkpoint, 64
+    # independent utterances of U(5, 15) s, 128 forced tokens each, host buffers in and out
+    bleg = None
+    if args.batched:
+        if rank == 0:
+            bpath = synth.ensure_model_dir(root, "small", seed=2, dtype="bfloat16")
+        barrier()
+        bpath = synth.ensure_model_dir(root, "small", seed=2, dtype="bfloat16")
+        brng = np.random.Generator(np.random.PCG64(7))
+        blens = (brng.uniform(5, 15, size=64) * 16000).astype(int) // 80 * 80
+        baudio = [synth.synth_audio(int(n), 100 + i) for i, n in enumerate(blens)]
+        bm = mb.MoonshineModel.load(bpath, device=local)
+        bm.generate_batch(baudio, forced_len=128)
+        b_enc, b_dec, b_wall = [], [], []
+        for _ in range(3):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            bids, bst = bm.generate_batch(baudio, forced_len=128)
+            b_wall.append((time.perf_counter() - t0) * 1e3)
+            assert all(len(r) == 128 for r in bids)
+            b_enc.append(bst.encode_ms)
+            b_dec.append(bst.decode_ms)
+        bleg = {"workload": "small bf16 weights, 64 utterances of U(5, 15) s, 128 forced tokens each",
+                "encode_ms": round(statistics.median(b_enc), 2), "decode_ms": round(statistics.median(b_dec), 2),
+                "wall_ms": round(statistics.median(b_wall), 2),
+                "tokens_per_s_per_gpu": round(64 * 128 / (statistics.median(b_wall) / 1e3), 1),
+                "audio_s": round(float(blens.sum()) / 16000.0, 2),
+                "timing": "host wall clock around the public call incl. host copies (median of 3)"}
+        del bm
+        barrier()
+
     if dist is not None:
         t = torch.tensor([t_rank, t_e2e], dtype=torch.float64, device=f"cuda:{local}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -422,6 +456,8 @@ def main():
             line["word_timestamps"] = ts
         if qleg is not None:
             line["quantized_4bit"] = qleg
+        if bleg is not None:
+            line["batched"] = bleg
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_oracle()
         print(json.dumps(line), flush=True)
