@@ -280,7 +280,7 @@ ms_status ms_word_timings(const int32_t* jump_frames, int32_t n_jumps, const flo
 
 /* ------------------------------------------------------------------- streaming */
 
-/* StreamingConfig (MoonshineStreaming.swift:47-62), plus fields of this build: transcribe's
+/* StreamingConfig (MoonshineStreaming.swift:47-62), plus fields of this library: transcribe's
  * temperature argument and the seed of its draws. */
 typedef struct {
     int32_t max_memory_frames;   /* default 100000 */

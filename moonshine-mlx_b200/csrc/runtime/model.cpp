@@ -462,7 +462,7 @@ Model* load_model(const std::string& dir, const ms_options& o) {
     MSB_CUDA(cudaSetDevice(o.device));
     cudaDeviceProp prop;
     MSB_CUDA(cudaGetDeviceProperties(&prop, o.device));
-    if (prop.major != 10) throw MsError(MS_ERR_UNSUPPORTED, "this build targets sm_100a (B200)");
+    if (prop.major != 10) throw MsError(MS_ERR_UNSUPPORTED, "this library targets sm_100a (B200)");
     m->num_sms = prop.multiProcessorCount;
     m->cfg = Config::from_json_file(dir + "/config.json");
     validate(m->cfg);

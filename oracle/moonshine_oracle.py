@@ -7,8 +7,8 @@ token loop and the streaming state machine.  Each function cites the reference
 file:line it follows (paths inside the reference project).
 
 Only the test suite, the smoke check and the CPU-baseline leg of the benchmark may
-import it, and only as the checker / the timed CPU restatement.  The product path never
-calls it.
+import it, and only as the outputs to compare against or as the timed CPU restatement.
+The product path never calls it.
 
 Parity status: UNPINNED against the reference itself.  The reference is a Swift package
 over mlx-swift 0.30.6 (Package.resolved:23-28); neither Swift nor MLX can run where this
