@@ -50,6 +50,17 @@ def test_defaults_and_argument_errors():
     assert L.ms_stream_start(None) == 1
     assert L.ms_model_sample_rate(None) == 0
     assert b"sm_100a" in L.ms_version()
+    assert (o.weight_dtype, o.decode_kernel, o.quant_stream) == (0, 0, 0)  # AUTO everywhere
+    lm = ctypes.c_int32(-1)
+    assert L.ms_model_decode_weight_bits(None, ctypes.byref(lm)) == 0 and lm.value == 0
+    assert L.ms_model_decode_weight_bits(None, None) == 0
+
+
+def test_python_load_rejects_unknown_options(tmp_path):
+    import moonshine_b200 as mb
+    for kw in ({"decode_kernel": "solo"}, {"weight_dtype": "f16"}, {"quant_stream": "some"}):
+        with pytest.raises(ValueError):
+            mb.MoonshineModel.load(str(tmp_path), **kw)
 
 
 @pytest.mark.skipif(os.path.exists("/dev/nvidia0"), reason="a GPU is present")
