@@ -158,10 +158,6 @@ __device__ __forceinline__ float quant_input_scale(int j, int bits) {
     return __uint_as_float((uint32_t)(127 - sh) << 23);
 }
 
-#ifndef MSB_QGEMV_ATTR
-#define MSB_QGEMV_ATTR __noinline__
-#endif
-
 // Input k (value v) of the vector block_gemv_q reads, for rows of rf inputs (rf % 64 == 0):
 // xq[k] = v * quant_input_scale(k), and lane 16m of the warp stores xq[rf + k / 16] = the
 // sum of the 16 inputs its half warp holds.  Called by whole warps holding 32 consecutive
@@ -186,8 +182,8 @@ __device__ __forceinline__ void quant_input(float v, int k, float* xq, int rf) {
 // rounded up to a power of two) and each group's warps take the chunks round robin, their
 // partials summed per row in fixed order.  Ends with a barrier.
 template <int BITS>
-__device__ MSB_QGEMV_ATTR void block_gemv_q(const uint32_t* rows, int nr, int rf, int rs, int gs, const float* xq,
-                                            float* part, float* res) {
+__device__ __noinline__ void block_gemv_q(const uint32_t* rows, int nr, int rf, int rs, int gs, const float* xq,
+                                          float* part, float* res) {
     constexpr int PER = 32 / BITS;  // codes per word
     constexpr int CC = 4 * PER;     // inputs per 16-byte chunk of codes
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
