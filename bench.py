@@ -1,18 +1,32 @@
-"""Benchmark: batch-1 Moonshine tiny transcription on B200 (decode tokens/s).
+"""Benchmark: batch-1 Moonshine tiny transcription on B200 (decode tokens/s), plus the
+batched, sharded and streaming workloads as extra keys of the same JSON line.
 
-Workload (one "step"): 30 s of seeded synthetic 16 kHz audio through the frontend,
+Headline workload (one "step"): 30 s of seeded synthetic 16 kHz audio through the frontend,
 the sliding-window encoder, the once-per-utterance cross K/V projection and a 200-token
-forced greedy decode (EOS ignored) of the tiny architecture (d 320, 6+6 layers,
-vocab 32768) with random-init fp32 weights and an fp16 KV cache.  Tokens/s counts encode
-time, like the reference's tokensPerSecond (Sources/MoonshineMLX/MoonshineModel.swift:182).
+forced greedy decode (EOS ignored) of the tiny architecture (d 320, 6+6 layers, vocab
+32768) with random-init fp32 weights and an fp16 KV cache.  Tokens/s counts encode time,
+like the reference's tokensPerSecond (Sources/MoonshineMLX/MoonshineModel.swift:182).
+
+Legs (keys of the same line; each can be skipped):
+  word_timestamps  generateWithWordTimestamps on the headline audio
+  quantized_4bit   the same weights as an MLX affine 4-bit checkpoint
+  batched          small bf16, 64 utterances of U(5, 15) s, 128 forced tokens (per GPU)
+  sharded          medium bf16, a fixed job of 256 utterances of U(2, 30) s, each decoding
+                   its own limit ceil(6.5 s) with EOS ignored, partitioned over the N GPUs
+                   (whole-box tokens/s, RTFx, per-rank imbalance)
+  streaming        512 tiny fp32 streams split over the N GPUs, 80 ms chunks,
+                   transcribe(isFinal: false, maxTokens: 16) after every chunk (aggregate
+                   tokens/s, p50 / p99 per-chunk latency)
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-N > 1 runs under torchrun, one process per GPU, each an independent full replica
-(the path has no cross-utterance state, so there is no collective on the data path).
-`--impl reference` times the CPU restatement of the reference on the host cores.
+N > 1 runs under torchrun, one process per GPU, each a full model replica (the path has no
+cross-utterance state, so there is no collective on the data path; NCCL carries only the
+timing barrier, the max-over-ranks reduction and the result gather).  `--impl reference`
+times the CPU restatement of the reference on the host cores.
 """
 import argparse
+import hashlib
 import json
 import math
 import os
@@ -57,21 +71,31 @@ def decode_bytes_per_launch(cfg, M, n_tokens, kv_bytes=2):
     return n_tokens * (w + emb) + cross0 + (n_tokens - 1) * cross + self_reads + self_writes
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one decode launch (16 decoder calls, 1500
-# memory frames, fp16 KV) from an ncu capture of each batch-1 kernel; per-call traffic is
-# flat after the first call.
-NCU_DECODE_BYTES_16CALLS_1500F = {
-    "cluster": (857855232 + 3086336, "profiles/decode_cluster_tiny_30s_16tok.md"),
-    "grid": (830.744e6 + 5.621e6, "profiles/decode_b1_tiny_30s_16tok.md"),
+# DRAM traffic of one decode launch measured by ncu (dram__bytes_read.sum +
+# dram__bytes_write.sum, 16 decoder calls at 1500 memory frames, fp16 KV), together with
+# the sha256 of the kernel's source files at capture time.  Reported only while the sources
+# are unchanged; otherwise the line carries traffic null.
+KERNEL_SOURCES = {
+    "cluster": ["csrc/kernels/decode_cluster.cu", "csrc/kernels/cluster_common.cuh", "csrc/kernels/common.cuh"],
+    "grid": ["csrc/kernels/decode_b1.cu", "csrc/kernels/common.cuh"],
 }
+NCU_DECODE_TRAFFIC_16CALLS_1500F = {}
 DECODE_KERNEL_SYMBOL = {"cluster": "decode_cluster_kernel<40, 0>", "grid": "decode_b1_kernel<40>"}
 
 
+def kernel_sources_sha256(kernel):
+    h = hashlib.sha256()
+    for rel in KERNEL_SOURCES.get(kernel, []):
+        with open(os.path.join(PKG, rel), "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()
+
+
 def decode_traffic_per_launch(M, n_tokens, kernel):
-    if M != 1500 or kernel not in NCU_DECODE_BYTES_16CALLS_1500F:
-        return None, None
-    b, src = NCU_DECODE_BYTES_16CALLS_1500F[kernel]
-    return int(b * n_tokens / 16), src
+    rec = NCU_DECODE_TRAFFIC_16CALLS_1500F.get(kernel)
+    if M != 1500 or rec is None or rec["sources_sha256"] != kernel_sources_sha256(kernel):
+        return None
+    return int(rec["bytes"] * n_tokens / 16)
 
 
 def measured_peak():
@@ -81,6 +105,13 @@ def measured_peak():
             return float(json.load(f)["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def bench_config(world):
+    """The `config` object of both arms' lines."""
+    return {"workload": WORKLOAD, "global_batch": world, "seq_len": FORCED,
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "l2": "512 MB buffer written between timed steps"}
 
 
 class ClockSampler:
@@ -137,79 +168,227 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline_oracle(budget_tokens=40):
-    """Times the numpy restatement (float32, all host threads) on a bounded sample of the
-    workload: the full 30 s encode + cross K/V and `budget_tokens` decoder calls; the
-    200-token figure is extrapolated from the measured per-token time."""
+# ------------------------------------------------------------------ CPU restatement
+
+def oracle_setup():
     import numpy as np
     from moonshine_b200 import synth
     from oracle.moonshine_oracle import Oracle
     root = os.path.join(tempfile.gettempdir(), "moonshine_b200_bench")
     path = synth.ensure_model_dir(root, ARCH, seed=WEIGHT_SEED)
-    o = Oracle.from_dir(path, np.float32)
-    audio = synth.synth_audio(N_SAMPLES, AUDIO_SEED)
+    return Oracle.from_dir(path, np.float32), synth.synth_audio(N_SAMPLES, AUDIO_SEED)
+
+
+def oracle_step(o, audio):
+    """One step of the headline workload on the numpy float32 restatement: the 30 s
+    encode, the cross K/V and all FORCED decoder calls with greedy feedback."""
+    import numpy as np
     t0 = time.perf_counter()
-    mem = o.memory_for(audio)
-    t1 = time.perf_counter()
-    cache = o.new_cache(mem, True)
-    t2 = time.perf_counter()
+    cache = o.new_cache(o.memory_for(audio), True)
     tok = o.cfg.decoder_start_token_id
-    for _ in range(budget_tokens):
+    for _ in range(FORCED):
         _, lg = o.decoder_step(tok, cache)
         tok = int(np.argmax(lg))
-    t3 = time.perf_counter()
-    per_tok = (t3 - t2) / budget_tokens
-    total = (t1 - t0) + (t2 - t1) + per_tok * FORCED
-    return {"value": FORCED / total, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"numpy float32 oracle: 30 s encode + cross K/V + {budget_tokens} decoder calls, "
-                      f"{FORCED}-token time extrapolated ({per_tok * 1e3:.2f} ms/token)",
-            "encode_s": round(t1 - t0, 4), "ms_per_token": round(per_tok * 1e3, 4)}
+    return time.perf_counter() - t0
+
+
+def cpu_baseline_oracle(n_steps=3):
+    """The numpy float32 restatement on all host threads, timed over `n_steps` whole steps of
+    the headline workload (median)."""
+    o, audio = oracle_setup()
+    times = [oracle_step(o, audio) for _ in range(n_steps)]
+    t = statistics.median(times)
+    return {"value": round(FORCED / t, 3), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"numpy float32 restatement of the reference (Swift/MLX cannot run here): "
+                      f"{n_steps} whole steps (30 s encode + cross K/V + {FORCED} decoder calls), median",
+            "s_per_step": round(t, 4)}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    import numpy as np
-    from moonshine_b200 import synth
-    from oracle.moonshine_oracle import Oracle
-    root = os.path.join(tempfile.gettempdir(), "moonshine_b200_bench")
-    path = synth.ensure_model_dir(root, ARCH, seed=WEIGHT_SEED)
-    o = Oracle.from_dir(path, np.float32)
-    audio = synth.synth_audio(N_SAMPLES, AUDIO_SEED)
-    # each step: 30 s encode + cross K/V + `n_tok` decoder calls, n_tok sized so the whole
-    # run stays within ~3 minutes; tokens/s extrapolates the decode to 200 tokens
-    per_step_budget_s = 150.0 / max(1, args.steps + args.warmup)
-    n_tok = max(4, min(FORCED, int((per_step_budget_s - 3.5) / 0.012)))
-
-    def step():
-        t0 = time.perf_counter()
-        mem = o.memory_for(audio)
-        cache = o.new_cache(mem, True)
-        t1 = time.perf_counter()
-        tok = o.cfg.decoder_start_token_id
-        for _ in range(n_tok):
-            _, lg = o.decoder_step(tok, cache)
-            tok = int(np.argmax(lg))
-        t2 = time.perf_counter()
-        return (t1 - t0) + (t2 - t1) * FORCED / n_tok
-
+    o, audio = oracle_setup()
     for _ in range(args.warmup):
-        step()
-    times = [step() for _ in range(args.steps)]
+        oracle_step(o, audio)
+    times = [oracle_step(o, audio) for _ in range(args.steps)]
     ms = 1e3 * sum(times) / len(times)
     val = FORCED / (ms / 1e3)
     line = {
         "impl": "reference", "metric": "decode tokens/s", "value": round(val, 3), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": 1, "parallelism": "replicas"},
+        "config": bench_config(world),
         "cpu_baseline": {"value": round(val, 3), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
                          "sample": f"numpy float32 restatement of the reference (Swift/MLX cannot run here): "
-                                   f"30 s encode + {n_tok} decoder calls per step, decode extrapolated to "
-                                   f"{FORCED} tokens"},
+                                   f"whole steps (30 s encode + cross K/V + {FORCED} decoder calls)"},
         "e2e": {"value": round(val, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU legs
+
+def _events(torch, stream):
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    return a, b
+
+
+def leg_batched(mb, synth, root, torch, barrier, rank, reps=3):
+    """ms_generate_batch on small bf16: 64 utterances of U(5, 15) s, 128 forced tokens each,
+    host buffers in and out; CUDA events on the model's stream around the public call."""
+    import numpy as np
+    if rank == 0:
+        synth.ensure_model_dir(root, "small", seed=2, dtype="bfloat16")
+    barrier()
+    bpath = synth.ensure_model_dir(root, "small", seed=2, dtype="bfloat16")
+    brng = np.random.Generator(np.random.PCG64(7))
+    blens = (brng.uniform(5, 15, size=64) * 16000).astype(int) // 80 * 80
+    baudio = [synth.synth_audio(int(n), 100 + i) for i, n in enumerate(blens)]
+    bm = mb.MoonshineModel.load(bpath)
+    s = torch.cuda.ExternalStream(bm.cuda_stream)
+    bm.generate_batch(baudio, forced_len=128)
+    b_enc, b_dec, b_ms = [], [], []
+    for _ in range(reps):
+        e0, e1 = _events(torch, s)
+        e0.record(s)
+        bids, bst = bm.generate_batch(baudio, forced_len=128)
+        e1.record(s)
+        torch.cuda.synchronize()
+        assert all(len(r) == 128 for r in bids)
+        b_ms.append(e0.elapsed_time(e1))
+        b_enc.append(bst.encode_ms)
+        b_dec.append(bst.decode_ms)
+    bm.close()
+    med = statistics.median(b_ms)
+    return {"workload": "small bf16 weights, 64 utterances of U(5, 15) s, 128 forced tokens each",
+            "encode_ms": round(statistics.median(b_enc), 2), "decode_ms": round(statistics.median(b_dec), 2),
+            "ms": round(med, 2), "ms_per_step_decode": round(statistics.median(b_dec) / 128, 4),
+            "tokens_per_s_per_gpu": round(64 * 128 / (med / 1e3), 1),
+            "audio_s": round(float(blens.sum()) / 16000.0, 2),
+            "timing": f"CUDA events on the model stream around the public call incl. host copies "
+                      f"(median of {reps})"}
+
+
+def leg_sharded(mb, synth, root, torch, dist, barrier, rank, world, local, reps=2, sub_batch=64):
+    """A fixed job of 256 medium bf16 utterances of U(2, 30) s, each decoding its own limit
+    ceil(6.5 s) with EOS ignored, partitioned by length over the ranks (shard.py).  Each rank
+    runs its share through ms_generate_batch in length-sorted groups of at most `sub_batch`
+    utterances; time per rank by CUDA events on its model stream, job time = max over ranks;
+    ids gathered on rank 0."""
+    import numpy as np
+    from moonshine_b200 import shard
+    if rank == 0:
+        synth.ensure_model_dir(root, "medium", seed=3, dtype="bfloat16")
+    barrier()
+    path = synth.ensure_model_dir(root, "medium", seed=3, dtype="bfloat16")
+    rng = np.random.Generator(np.random.PCG64(11))
+    lens = (rng.uniform(2, 30, size=256) * 16000).astype(int) // 80 * 80
+    share = shard.partition_by_length(lens.tolist(), world)[rank]
+    order = sorted(share, key=lambda i: -int(lens[i]))
+    groups = [order[k:k + sub_batch] for k in range(0, len(order), sub_batch)]
+    audio = {i: synth.synth_audio(int(lens[i]), 1000 + i) for i in share}
+    m = mb.MoonshineModel.load(path)
+    s = torch.cuda.ExternalStream(m.cuda_stream)
+    m.generate_batch([audio[i] for i in groups[0]], forced_len=-1)   # warm-up: weights, graphs
+    times, results = [], {}
+    for _ in range(reps):
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = _events(torch, s)
+        e0.record(s)
+        for g in groups:
+            ids, _ = m.generate_batch([audio[i] for i in g], forced_len=-1)
+            for i, r in zip(g, ids):
+                results[i] = r
+        e1.record(s)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) / 1e3)
+    m.close()
+    t_rank = statistics.median(times)
+    toks = sum(len(results[i]) for i in share)
+    expect = sum(int(math.ceil(lens[i] / 16000.0 * 6.5)) for i in share)
+    assert toks == expect, (toks, expect)
+    t_max, t_mean, tok_all = t_rank, t_rank, toks
+    if dist is not None:
+        t = torch.tensor([t_rank, t_rank, float(toks)], dtype=torch.float64, device=f"cuda:{local}")
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        t_max, t_mean, tok_all = float(mx[0]), float(t[1]) / world, int(t[2])
+    gathered = shard.gather_results([results[i] for i in share], share, len(lens))
+    if rank != 0:
+        return None
+    assert all(r is not None for r in gathered)
+    audio_s = float(lens.sum()) / 16000.0
+    return {"workload": "medium bf16 weights, 256 utterances of U(2, 30) s (a fixed job, partitioned by length "
+                        "over the GPUs), each decoding ceil(6.5 tokens per second) with EOS ignored",
+            "n_gpus": world, "tokens": tok_all, "audio_s": round(audio_s, 1),
+            "job_s": round(t_max, 4), "tokens_per_s": round(tok_all / t_max, 1),
+            "rtfx": round(audio_s / t_max, 1), "rank_imbalance": round(t_max / t_mean, 4),
+            "utterances_per_gpu_call": min(sub_batch, len(share)),
+            "timing": "CUDA events on each rank's model stream around its generate_batch calls (host buffers, "
+                      f"median of {reps}), job time = max over ranks"}
+
+
+def leg_streaming(mb, synth, torch, dist, barrier, rank, world, local, root, n_streams=512, n_chunks=125,
+                  chunk=1280, max_tokens=16):
+    """512 tiny fp32 streams (split over the ranks), 80 ms chunks, after every chunk
+    transcribe(isFinal: false, maxTokens: 16) of every stream of the rank (one
+    ms_stream_transcribe_batch per chunk, per-stream exact decode).  Per-chunk latency = the
+    time of that call for the rank's streams (CUDA events); p50 / p99 over chunks and ranks."""
+    import numpy as np
+    if rank == 0:
+        synth.ensure_model_dir(root, ARCH, seed=WEIGHT_SEED)
+    barrier()
+    path = synth.ensure_model_dir(root, ARCH, seed=WEIGHT_SEED)
+    mine = list(range(rank, n_streams, world))
+    m = mb.MoonshineModel.load(path, kv_fp16=True)
+    s = torch.cuda.ExternalStream(m.cuda_stream)
+    audio = {i: synth.synth_audio(n_chunks * chunk, 5000 + i) for i in mine}
+    states = [m.create_stream() for _ in mine]
+    for st in states:
+        m.start_stream(st)
+    lat, toks = [], 0
+    barrier()
+    torch.cuda.synchronize()
+    t_all0, t_all1 = _events(torch, s)
+    t_all0.record(s)
+    for k in range(n_chunks):
+        e0, e1 = _events(torch, s)
+        e0.record(s)
+        for st, i in zip(states, mine):
+            m.add_audio(st, audio[i][k * chunk:(k + 1) * chunk])
+        out = m.transcribe_batch(states, is_final=False, max_tokens=max_tokens)
+        e1.record(s)
+        toks += sum(len(o[0]) for o in out)
+        lat.append((e0, e1))
+    t_all1.record(s)
+    torch.cuda.synchronize()
+    lat_ms = [a.elapsed_time(b) for a, b in lat]
+    total_s = t_all0.elapsed_time(t_all1) / 1e3
+    for st in states:
+        st.close()
+    m.close()
+    all_lat = lat_ms
+    t_max, tok_all = total_s, toks
+    if dist is not None:
+        t = torch.tensor(lat_ms + [total_s, float(toks)], dtype=torch.float64, device=f"cuda:{local}")
+        got = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(got, t)
+        all_lat = [float(x) for g in got for x in g[:-2].tolist()]
+        t_max = max(float(g[-2]) for g in got)
+        tok_all = int(sum(float(g[-1]) for g in got))
+    if rank != 0:
+        return None
+    a = np.asarray(all_lat)
+    return {"workload": f"{n_streams} tiny fp32 streams (fp16 KV), {n_chunks} chunks of 80 ms each, "
+                        f"transcribe(isFinal: false, maxTokens: {max_tokens}) of every stream after every chunk "
+                        "(exact per-stream decode)",
+            "n_gpus": world, "streams_per_gpu": len(mine), "decoded_tokens": tok_all,
+            "tokens_per_s": round(tok_all / t_max, 1), "chunk_ms_p50": round(float(np.percentile(a, 50)), 3),
+            "chunk_ms_p99": round(float(np.percentile(a, 99)), 3), "job_s": round(t_max, 3),
+            "timing": "CUDA events on each rank's model stream around add_audio + transcribe_batch of its streams "
+                      "per chunk (host buffers); job time = max over ranks"}
 
 
 def main():
@@ -221,9 +400,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-timestamps", action="store_true", help="skip the word-timestamp leg")
     ap.add_argument("--no-quantized", action="store_true", help="skip the 4-bit checkpoint leg")
-    ap.add_argument("--batched", action="store_true",
-                    help="add the batched leg: small architecture, bf16 weights, 64 utterances of 5-15 s, "
-                         "128 forced tokens each")
+    ap.add_argument("--no-batched", action="store_true", help="skip the small-model batched leg")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the medium-model sharded job")
+    ap.add_argument("--no-streaming", action="store_true", help="skip the 512-stream leg")
+    ap.add_argument("--stream-chunks", type=int, default=125, help="80 ms chunks per stream")
     ap.add_argument("--seconds", type=float, default=30.0, help="audio length (profiling cases)")
     ap.add_argument("--tokens", type=int, default=200, help="forced decode length (profiling cases)")
     ap.add_argument("--flush-mb", type=int, default=512, help="L2-flush buffer written between steps")
@@ -250,14 +430,13 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
 
     def barrier():
         if dist is not None:
             dist.barrier()
 
-    import numpy as np
     import moonshine_b200 as mb
     from moonshine_b200 import synth
 
@@ -338,23 +517,25 @@ def main():
                             (lambda: model.generate(host_audio, forced_len=n_calls), t_gen)):
                 with torch.cuda.stream(stream):
                     flush.fill_(k & 0xFF)
-                torch.cuda.synchronize()
-                t0 = time.perf_counter()
+                e0, e1 = _events(torch, stream)
+                e0.record(stream)
                 fn()
+                e1.record(stream)
                 torch.cuda.synchronize()
-                acc.append((time.perf_counter() - t0) * 1e3)
+                acc.append(e0.elapsed_time(e1))
         ts = {"decoder_calls": n_calls, "memory_frames": al.n_frames,
               "ms_per_call": round(statistics.median(t_al), 3),
               "generate_same_calls_ms": round(statistics.median(t_gen), 3),
               "overhead_ms": round(statistics.median(t_al) - statistics.median(t_gen), 3),
-              "timing": "host wall clock around the public call (median of 3), L2 flushed before each"}
+              "timing": "CUDA events on the model stream around the public call (median of 3), L2 flushed "
+                        "before each"}
 
     # ---- the same weights as an MLX affine 4-bit checkpoint (group 64), device-resident audio:
     # the clustered kernel streams the LM head as codes (the default quant_stream)
     qleg = None
     if not args.no_quantized:
         if rank == 0:
-            qpath = synth.ensure_model_dir(root, ARCH, seed=WEIGHT_SEED, quant=(64, 4))
+            synth.ensure_model_dir(root, ARCH, seed=WEIGHT_SEED, quant=(64, 4))
         barrier()
         qpath = synth.ensure_model_dir(root, ARCH, seed=WEIGHT_SEED, quant=(64, 4))
         qm = mb.MoonshineModel.load(qpath, device=local, kv_fp16=True)
@@ -366,7 +547,7 @@ def main():
         for k in range(min(args.steps, 8)):
             with torch.cuda.stream(qstream):
                 flush.fill_(k & 0xFF)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0, e1 = _events(torch, qstream)
             e0.record(qstream)
             n, st = qm.generate_device(audio_dev.data_ptr(), N_SAMPLES, ids_dev.data_ptr(), ids_dev.numel(),
                                        forced_len=FORCED)
@@ -380,39 +561,17 @@ def main():
                 "tokens_per_s_per_gpu": round(FORCED / (q_ms / 1e3), 2),
                 "ms_per_token_decode": round(statistics.mean(q_dec) / FORCED, 5),
                 "timing": "CUDA events per step (encode + decode), L2 flushed before each"}
-        del qm
+        qm.close()
         barrier()
 
-    # ---- batched generation (ms_generate_batch): small architecture, bf16 checkpoint, 64
-    # independent utterances of U(5, 15) s, 128 forced tokens each, host buffers in and out
-    bleg = None
-    if args.batched:
-        if rank == 0:
-            bpath = synth.ensure_model_dir(root, "small", seed=2, dtype="bfloat16")
-        barrier()
-        bpath = synth.ensure_model_dir(root, "small", seed=2, dtype="bfloat16")
-        brng = np.random.Generator(np.random.PCG64(7))
-        blens = (brng.uniform(5, 15, size=64) * 16000).astype(int) // 80 * 80
-        baudio = [synth.synth_audio(int(n), 100 + i) for i, n in enumerate(blens)]
-        bm = mb.MoonshineModel.load(bpath, device=local)
-        bm.generate_batch(baudio, forced_len=128)
-        b_enc, b_dec, b_wall = [], [], []
-        for _ in range(3):
-            torch.cuda.synchronize()
-            t0 = time.perf_counter()
-            bids, bst = bm.generate_batch(baudio, forced_len=128)
-            b_wall.append((time.perf_counter() - t0) * 1e3)
-            assert all(len(r) == 128 for r in bids)
-            b_enc.append(bst.encode_ms)
-            b_dec.append(bst.decode_ms)
-        bleg = {"workload": "small bf16 weights, 64 utterances of U(5, 15) s, 128 forced tokens each",
-                "encode_ms": round(statistics.median(b_enc), 2), "decode_ms": round(statistics.median(b_dec), 2),
-                "wall_ms": round(statistics.median(b_wall), 2),
-                "tokens_per_s_per_gpu": round(64 * 128 / (statistics.median(b_wall) / 1e3), 1),
-                "audio_s": round(float(blens.sum()) / 16000.0, 2),
-                "timing": "host wall clock around the public call incl. host copies (median of 3)"}
-        del bm
-        barrier()
+    bleg = None if args.no_batched else leg_batched(mb, synth, root, torch, barrier, rank)
+    barrier()
+    sleg = None if args.no_sharded else leg_sharded(mb, synth, root, torch, dist, barrier, rank, world, local)
+    barrier()
+    stleg = None
+    if not args.no_streaming:
+        stleg = leg_streaming(mb, synth, torch, dist, barrier, rank, world, local, root, n_chunks=args.stream_chunks)
+    barrier()
 
     if dist is not None:
         t = torch.tensor([t_rank, t_e2e], dtype=torch.float64, device=f"cuda:{local}")
@@ -428,15 +587,13 @@ def main():
         total_tokens = world * FORCED * args.steps
         value = total_tokens / (t_rank / 1e3)
         kern = kernels.pop() if len(kernels) == 1 else "mixed"
-        traffic, traffic_src = decode_traffic_per_launch(M, FORCED, kern)
+        traffic = decode_traffic_per_launch(M, FORCED, kern)
         line = {
             "metric": "decode tokens/s", "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_rank / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init weights, seeded noise+sinusoid audio)",
-            "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": FORCED,
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                       "l2": f"{args.flush_mb} MB buffer written between timed steps"},
+            "config": bench_config(world),
             "ms_per_token_decode": round(dec_avg / FORCED, 5),
             "encode_ms": round(statistics.mean(enc_ms), 4),
             "rtfx": round((N_SAMPLES / 16000.0) / (t_rank / args.steps / 1e3), 1),
@@ -446,8 +603,8 @@ def main():
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(bytes_launch),
                          "launch_ms": round(dec_avg, 4), "traffic": traffic,
-                         "traffic_source": (f"ncu dram__bytes of a 16-call launch at 1500 frames, scaled by "
-                                            f"decoder calls ({traffic_src})") if traffic_src else None},
+                         "traffic_source": ("ncu dram__bytes of a 16-call launch at 1500 frames on the same kernel "
+                                            "sources, scaled by decoder calls") if traffic else None},
             "e2e": {"value": round(total_tokens / (t_e2e / 1e3), 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": N_SAMPLES * 4, "d2h_bytes_per_step": FORCED * 4 + 16},
             "clocks": clocks.summary(),
@@ -458,10 +615,14 @@ def main():
             line["quantized_4bit"] = qleg
         if bleg is not None:
             line["batched"] = bleg
+        if sleg is not None:
+            line["sharded"] = sleg
+        if stleg is not None:
+            line["streaming"] = stleg
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_oracle()
         print(json.dumps(line), flush=True)
-    del model
+    model.close()
     if dist is not None:
         dist.destroy_process_group()
 

@@ -134,7 +134,10 @@ ms_status ms_model_get_config(const ms_model* model, ms_model_config* out);
 typedef struct {
     int32_t max_tokens;        /* maxTokens; <= 0 means Int.max (no cap) */
     int32_t forced_len;        /* > 0: decode exactly this many tokens per chunk, EOS fed
-                                  back like any id (benchmark / parity harness mode) */
+                                  back like any id (benchmark / parity harness mode);
+                                  < 0: each chunk (ms_generate_batch: each utterance) decodes
+                                  exactly its own limit min(max_tokens, ceil(seconds * 6.5)),
+                                  EOS fed back like any id */
     float temperature;         /* 0: greedy argMax; > 0: each token is a draw from
                                   softmax(logits / temperature) (MLXRandom.categorical,
                                   MoonshineModel.swift:211-213), by the Gumbel-max trick */
@@ -208,16 +211,23 @@ ms_status ms_encode(ms_model* model, const float* audio, int64_t n_samples,
  *
  * The caller passes encoder memory rows already in device memory of the model's GPU
  * (memory_dev, [frames * hidden] float32, 16-byte aligned; e.g. ms_encode's output copied
- * to the device) and a device buffer ids_dev of n_tokens int32.  The call runs up to
+ * to the device) and a device buffer ids_dev of n_tokens int32.  The rows must be fully
+ * written before the call: the call's work runs on the model's own stream (ms_model_stream),
+ * which does not wait for other streams, so synchronise the stream that wrote them (or make
+ * the model's stream wait on an event recorded after the write).  The call runs up to
  * n_tokens decoder calls from BOS (forced != 0: exactly n_tokens, EOS fed back like any
  * id), writes the ids to ids_dev and their count to *n_out (host), like ms_generate_device
- * for one chunk.  The cross-attention K/V, the self-attention K/V cache and the decode
- * working buffers live in one static 16 MiB device array that every GPU loading this
- * library holds until the process exits: with the tiny model that covers 500 memory frames
- * (10 s of audio) and 128 decoder calls; larger requests fail with MS_ERR_CAPACITY and a
- * message giving the bytes needed.  The first call on a device looks up the array's device
- * address; make that first call before any stream capture.  Every call reuses the array:
- * calls whose GPU work overlaps race on it (calls through this library are serialised). */
+ * for one chunk.  It always uses the single-grid decode kernel; ms_generate_device may pick
+ * the head-clustered one, which sums in another order, so the two agree to rounding.
+ *
+ * The cross-attention K/V, the self-attention K/V cache and the decode working buffers
+ * live in one static 16 MiB device array that every GPU loading this library holds until
+ * the process exits: with the tiny model that covers 500 memory frames (10 s of audio) and
+ * 128 decoder calls; larger requests fail with MS_ERR_CAPACITY and a message giving the
+ * bytes needed.  ms_model_load reserves the array on its device and loads the kernels this
+ * call launches, so the call itself neither allocates nor loads code.  Every call reuses
+ * the array: two calls whose GPU work overlapped would race on it, which this library
+ * prevents by serialising the calls and waiting for each call's work before returning. */
 ms_status ms_decode_memory_static(ms_model* model, const float* memory_dev, int32_t frames,
                                   int32_t n_tokens, int32_t forced, int32_t* ids_dev,
                                   int32_t* n_out, int32_t* hit_eos);

@@ -76,12 +76,12 @@ static void generate_chunk(Model& m, const float* audio, int64_t len, const ms_g
     if (M == 0) return;  // fewer samples than one frame: nothing to decode
     const double dur = (double)len / (double)c.sample_rate;
     const int64_t limit64 = std::min<int64_t>(max_tokens, (int64_t)std::ceil(dur * c.max_tok_per_s));
-    const bool forced = gp.forced_len > 0;
-    const int n_steps = forced ? gp.forced_len : (int)limit64;
+    const bool forced = gp.forced_len != 0;  // < 0: this chunk's own limit, EOS ignored
+    const int n_steps = gp.forced_len > 0 ? gp.forced_len : (int)limit64;
     if (n_steps <= 0) throw MsError(MS_ERR_INVALID_ARG, "token limit must be positive");
     const int* teacher_dev = nullptr;
     if (teacher) {
-        if (!forced || n_teacher < n_steps)
+        if (gp.forced_len <= 0 || n_teacher < n_steps)
             throw MsError(MS_ERR_INVALID_ARG, "teacher_ids need forced_len <= n_teacher");
         m.ws.f.ensure((size_t)n_steps * 4);  // reuse: teacher ids after encode is done
     }
@@ -647,7 +647,7 @@ ms_status ms_generate_batch(ms_model* model, const float* const* audios, const i
             MSB_CUDA(cudaEventCreate(&t0));
             MSB_CUDA(cudaEventCreate(&t1));
             MSB_CUDA(cudaEventRecord(t0, m.stream));
-            BatchEngine::Result r = m.batch->run(dev, lens, limits, gp.forced_len > 0, gp.batch_logits != nullptr,
+            BatchEngine::Result r = m.batch->run(dev, lens, limits, gp.forced_len != 0, gp.batch_logits != nullptr,
                                                  gp.temperature, (unsigned)gp.seed);
             MSB_CUDA(cudaEventRecord(t1, m.stream));
             MSB_CUDA(cudaEventSynchronize(t1));

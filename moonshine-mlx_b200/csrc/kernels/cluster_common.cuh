@@ -40,6 +40,15 @@ __device__ __forceinline__ float ld_dsmem(uint32_t addr) {
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
     return v;
 }
+// 16-byte aligned address
+__device__ __forceinline__ float4 ld_dsmem4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
 // 64-bit exchange words: (tag << 32) | payload.  One aligned 8-byte access is single-copy
 // atomic, so a reader that sees the expected tag also sees its payload; no fence is needed.
 __device__ __forceinline__ void st_tagged(unsigned long long* p, unsigned tag, uint32_t payload) {

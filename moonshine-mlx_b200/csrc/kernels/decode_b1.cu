@@ -857,4 +857,15 @@ cudaError_t launch_decode_b1(const DecodeParams& p, int grid, cudaStream_t strea
 
 bool decode_b1_supports_head_dim(int hd) { return hd == 32 || hd == 40 || hd == 48 || hd == 64; }
 
+cudaError_t preload_decode_b1(int hd) {
+    cudaFuncAttributes a;
+    switch (hd) {
+        case 32: return cudaFuncGetAttributes(&a, decode_b1_kernel<32>);
+        case 40: return cudaFuncGetAttributes(&a, decode_b1_kernel<40>);
+        case 48: return cudaFuncGetAttributes(&a, decode_b1_kernel<48>);
+        case 64: return cudaFuncGetAttributes(&a, decode_b1_kernel<64>);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
 }  // namespace msb

@@ -91,7 +91,7 @@ __host__ __device__ inline Segs make_segs(const ClusterGeom& g, int d, int hd) {
 
 enum SegId { SEG_QKV = 0, SEG_O, SEG_CQ, SEG_XKV, SEG_CO, SEG_FC1, SEG_FC2, SEG_LM };
 
-constexpr int MAXB = 192;  // blocks per step a CTA's schedule may have (checked at launch)
+constexpr int MAXB = 320;  // blocks per step a CTA's schedule may have (checked at launch)
 
 struct SegPlan {
     size_t off;  // floats from the CTA's stream base
@@ -910,12 +910,14 @@ bool cluster_geom(int d, int H, int KVH, int hd, int I, int V, int L, int t_cap,
     r.rlm = (V + H * CL - 1) / (H * CL);
     const int sd = rows_stride_d(r, d), sl = lm_stride(r, d);
     // ring slot: at least 52 KB, and large enough that a CTA's whole fc1 segment (header and
-    // every (value, gate) row pair, at most 64 fp32 / NT quantized rows) is one block; with a
+    // every (value, gate) row pair, at most 64 fp32 / NT quantized rows) is one block when
+    // that stays within 56 KB (wider models take their fc1 rows in several blocks); with a
     // quantized LM head, large enough for NT of its rows behind the final-norm header when
     // that stays within 56 KB
     {
         const size_t fc1 = ((size_t)d + 2 * r.gr + (size_t)std::min(2 * r.gr, qbits ? NT : 64) * sd) * 4;
-        size_t want = std::max<size_t>(52 * 1024, fc1);
+        size_t want = 52 * 1024;
+        if (fc1 <= 56 * 1024) want = std::max(want, fc1);
         const size_t lm = ((size_t)d + (size_t)std::min(r.rlm, NT) * sl) * 4;
         if (lm_qbits && lm <= 56 * 1024) want = std::max(want, lm);
         r.slot_bytes = (int)((want + 127) / 128 * 128);
@@ -929,7 +931,7 @@ bool cluster_geom(int d, int H, int KVH, int hd, int I, int V, int L, int t_cap,
         (size_t)s.ro4 + r.gr > slot_f ||
         (size_t)2 * hd * 4 > slot_f)
         return false;
-    if (cluster_smem_bytes(r, d, hd) > 208 * 1024) return false;  // + ~10 KB of static shared memory
+    if (cluster_smem_bytes(r, d, hd) > 208 * 1024) return false;  // + ~16 KB of static shared memory
     *g = r;
     return true;
 }

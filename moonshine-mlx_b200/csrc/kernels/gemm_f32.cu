@@ -153,4 +153,10 @@ cudaError_t launch_gemm_f32(const float* A, int lda, const float* B, int ldb, in
     return cudaGetLastError();
 }
 
+cudaError_t preload_gemm_f32() {
+    cudaFuncAttributes a;
+    cudaError_t e = cudaFuncGetAttributes(&a, gemm_f32_kernel<64>);
+    return e != cudaSuccess ? e : cudaFuncGetAttributes(&a, gemm_f32_kernel<128>);
+}
+
 }  // namespace msb

@@ -10,7 +10,13 @@
 //   all four warps     epilogue: tcgen05.ld of their 32 accumulator lanes (= rows) into the
 //                      idle stage buffers, then row by row (lanes along columns, so global
 //                      accesses coalesce) bias / activation / residual / bf16 or fp32 store /
-//                      K-V scatter / RoPE / SwiGLU / argmax / split-K atomics
+//                      K-V scatter / RoPE / SwiGLU / argmax / residual update
+//
+// Split-K: the `splits` CTAs of one output tile (blockIdx.z) form a thread-block cluster.
+// Each stages its partial tile in its own shared memory; after a cluster barrier, split z
+// sums rows [z * R / S, (z + 1) * R / S) of all S partials in split order through
+// distributed shared memory and runs the epilogue on them.  The sum order is fixed, so
+// results do not depend on which split finishes first.
 //
 // A is addressed through a 3-D tensor map (k, y, z) so a causal stride-2 convolution runs as
 // `taps` accumulated GEMMs: tap t reads A at (k, y_t, m + z_t) and B at column t*K_tap + k.
@@ -21,6 +27,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include "cluster_common.cuh"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -133,8 +140,10 @@ __host__ __device__ constexpr int tile_ld() { return BN + 4; }
 // n = n0 + 4 (t mod BN/4) .. n + 3 for every row it visits, so column-only terms (bias,
 // RoPE angles, K/V scatter base) are loaded once, and the BN/4 threads of a row write one
 // contiguous row segment with 128-bit accesses.  N is a multiple of 4 (checked at launch).
+// Rows [r_lo, r_hi) of the tile.
 template <int BN, int MODE>
-__device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* tile, int m0, int n0) {
+__device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* tile, int m0, int n0, int r_lo,
+                                              int r_hi) {
     constexpr int TPR = BN / 4;            // threads per row
     constexpr int RPP = TC_THREADS / TPR;  // rows per pass
     constexpr int LDS = tile_ld<BN>();
@@ -142,15 +151,14 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* 
     const int c = (t % TPR) * 4;
     const int n = n0 + c;
     const bool col_ok = n < g.N;
-    const int r0 = t / TPR;
-    const int rows = min(BM, g.M - m0);
-    const int passes = (rows + RPP - 1) / RPP;
+    const int r0 = r_lo + t / TPR;
+    const int rows = r_hi;
+    const int passes = (r_hi - r_lo + RPP - 1) / RPP;
     const GemmEpilogue& ep = g.ep;
 
     float4 bias = make_float4(0.f, 0.f, 0.f, 0.f);
     if constexpr (MODE == TC_EPI_STD || MODE == TC_EPI_SWIGLU || MODE == TC_EPI_ACCUM) {
-        const bool use = ep.bias && col_ok && (MODE != TC_EPI_ACCUM || blockIdx.z == 0);
-        if (use) bias = *reinterpret_cast<const float4*>(ep.bias + n);
+        if (ep.bias && col_ok) bias = *reinterpret_cast<const float4*>(ep.bias + n);
     }
     // K/V scatter: column part of the cache index (the four columns share one head)
     size_t kv_col = 0;
@@ -215,7 +223,10 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* 
                 }
             }
         } else if constexpr (MODE == TC_EPI_ACCUM) {
-            if (ok) atomicAdd(reinterpret_cast<float4*>(ep.out + (size_t)m * ep.ldc + n), add4(v, bias));
+            if (ok) {
+                float4* o = reinterpret_cast<float4*>(ep.out + (size_t)m * ep.ldc + n);
+                *o = add4(*o, add4(v, bias));
+            }
         } else if constexpr (MODE == TC_EPI_SWIGLU) {
             if (ok) {  // columns (value, gate, value, gate) -> two outputs
                 v = add4(v, bias);
@@ -371,28 +382,56 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
 
     // epilogue: warp w owns accumulator lanes (rows) 32w .. 32w+31.  The tile goes through
     // shared memory (the idle stage buffers) so the global side is row-contiguous.
-    bool ok = nkb > 0 && mbar_wait(&s.done, 0);  // an empty k-split contributes nothing
+    bool ok = nkb > 0 && mbar_wait(&s.done, 0);  // an empty k-split stages zeros
     if (nkb > 0 && !ok) atomicCAS(g.status, 0u, (unsigned)DEV_WAIT_TIMEOUT);
     ok = __syncthreads_and(ok && !s_fail);      // uniform: the epilogue crosses warps
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     constexpr int LDS = tile_ld<BN>();
     float* tile = reinterpret_cast<float*>(&s.a[0][0]);
     static_assert(sizeof(float) * BM * LDS <= sizeof(s.a) + sizeof(s.b), "epilogue tile must fit the stages");
-    if (ok) {
-        if (warp * 32 < g.M - m0) {  // warp-uniform: lanes of rows past M hold nothing
-            const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-            float* my = tile + (size_t)(warp * 32 + lane) * LDS;
+    const int rows = min(BM, g.M - m0);
+    if (warp * 32 < rows) {  // warp-uniform: lanes of rows past M hold nothing
+        const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+        float* my = tile + (size_t)(warp * 32 + lane) * LDS;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
-                float v[32];
-                tmem_ld32(lane_addr + c0, v);
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            float v[32];
+            if (ok) tmem_ld32(lane_addr + c0, v);
+            else
 #pragma unroll
-                for (int i = 0; i < 32; i += 4)
-                    *reinterpret_cast<float4*>(my + c0 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                for (int i = 0; i < 32; ++i) v[i] = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+                *reinterpret_cast<float4*>(my + c0 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        }
+    }
+    __syncthreads();
+    const int S = (int)gridDim.z;
+    if (S == 1) {
+        if (ok) epilogue_tile<BN, MODE>(g, tile, m0, n0, 0, rows);
+    } else {
+        // every split of the tile has staged its partial (barriers taken by all CTAs, also
+        // after a failure, so none is left waiting)
+        cluster_barrier();
+        const int z = (int)blockIdx.z;
+        const int per = (rows + S - 1) / S;
+        const int lo = min(rows, z * per), hi = min(rows, lo + per);
+        const bool any_fail = *reinterpret_cast<volatile unsigned*>(g.status) != 0u;
+        if (!any_fail) {
+            // rows [lo, hi): sum of the S partials in split order, into this CTA's own tile
+            // (no other CTA reads these rows of it)
+            constexpr int C4 = BN / 4;
+            const uint32_t tile_a = smem_u32(tile);
+            for (int e = threadIdx.x; e < (hi - lo) * C4; e += TC_THREADS) {
+                const int r = lo + e / C4, c = (e % C4) * 4;
+                const uint32_t off = (uint32_t)((r * LDS + c) * 4);
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int q = 0; q < S; ++q) acc = add4(acc, ld_dsmem4(mapa_rank(tile_a + off, (uint32_t)q)));
+                *reinterpret_cast<float4*>(tile + (size_t)r * LDS + c) = acc;
             }
         }
-        __syncthreads();
-        epilogue_tile<BN, MODE>(g, tile, m0, n0);
+        cluster_barrier();  // every CTA has read the partials it needs from its peers
+        if (!any_fail) epilogue_tile<BN, MODE>(g, tile, m0, n0, lo, hi);
     }
     // drain copies still in flight after a failure (bounded), then free tensor memory
     if (warp == 0 && lane == 0 && s_fail) {
@@ -461,6 +500,9 @@ cudaError_t launch_tc(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
         attr_set = true;
     }
     const dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.splits);
+    if (g.splits > 1)
+        return launch_kernel_cluster_z(gemm_tc_kernel<BN, MODE>, grid, dim3(TC_THREADS), smem, stream, g.splits,
+                                       map_a, map_b, g);
     return launch_kernel(gemm_tc_kernel<BN, MODE>, grid, dim3(TC_THREADS), smem, stream, map_a, map_b, g);
 }
 
@@ -514,7 +556,7 @@ cudaError_t launch_gemm_tc(const CUtensorMap& map_a, const CUtensorMap& map_b, c
                            cudaStream_t stream) {
     if (g.M <= 0 || g.N <= 0) return cudaSuccess;
     if (g.taps < 1 || g.taps > 8 || g.kb_per_tap < 1 || !g.status) return cudaErrorInvalidValue;
-    if (g.splits < 1 || (g.splits > 1 && g.mode != TC_EPI_ACCUM)) return cudaErrorInvalidValue;
+    if (g.splits < 1 || g.splits > TC_MAX_SPLITS || g.splits > g.taps * g.kb_per_tap) return cudaErrorInvalidValue;
     if (!epilogue_layout_ok(g)) return cudaErrorInvalidValue;
     ++launch_counter();
     if (bn == 128) return launch_tc_mode<128>(map_a, map_b, g, stream);

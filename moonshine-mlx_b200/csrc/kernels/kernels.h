@@ -32,6 +32,26 @@ cudaError_t launch_kernel(void (*kernel)(Params...), dim3 grid, dim3 block, size
     cfg.numAttrs = pdl_launches() ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
+// The same with thread-block clusters of (1, 1, cluster_z) CTAs (cluster_z > 1).
+template <class... Params, class... Args>
+cudaError_t launch_kernel_cluster_z(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                                    cudaStream_t stream, int cluster_z, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = (unsigned)cluster_z;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_launches() ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Device-side error codes reported through a kernel's status word.
 enum : unsigned { DEV_OK = 0, DEV_BARRIER_TIMEOUT = 1, DEV_BAD_TOKEN = 2, DEV_WAIT_TIMEOUT = 5 };
@@ -73,7 +93,7 @@ enum TcEpiMode {
     TC_EPI_ROPE_KV = 1,  // decoder q|k|v: partial interleaved RoPE, K/V appended to the cache
     TC_EPI_SWIGLU = 2,   // interleaved (value, gate) columns -> bf16 value * silu(gate)
     TC_EPI_ARGMAX = 3,   // per-row argmax (ties -> lowest column) + optional fp32 logits
-    TC_EPI_ACCUM = 4,    // out += acc (+ bias on k-split 0), fp32 atomics: split-K safe
+    TC_EPI_ACCUM = 4,    // out += acc (+ bias): the residual update (one CTA finalises each element)
 };
 
 // Decoder q|k|v epilogue parameters (row m = batch slot b).
@@ -89,12 +109,16 @@ struct TcRopeKv {
     int t_cap = 0, kv_f16 = 0;
 };
 
+constexpr int TC_MAX_SPLITS = 8;  // portable cluster size
 struct TcGemmArgs {
     int M = 0, N = 0;
     int taps = 1, kb_per_tap = 0, k_per_tap = 0;
     int tap_y[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     int tap_z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    int splits = 1;                       // k-splits over blockIdx.z (TC_EPI_ACCUM only)
+    int splits = 1;                       // k-splits over blockIdx.z (<= TC_MAX_SPLITS): the splits
+                                          // of a tile form one thread-block cluster and sum their
+                                          // partial tiles in split order through distributed
+                                          // shared memory (deterministic), every mode
     int mode = TC_EPI_STD;
     GemmEpilogue ep;                      // fp32 outputs / scatter (as the fp32 GEMM)
     __nv_bfloat16* out_bf16 = nullptr;    // optional bf16 copy of the output [M, ldc_bf16]
@@ -302,6 +326,10 @@ cudaError_t launch_alignment_rows(const float* qc_trace, const float* cross32, c
 cudaError_t launch_decode_b1(const DecodeParams& p, int grid, cudaStream_t stream);
 int decode_b1_block_threads();
 bool decode_b1_supports_head_dim(int hd);
+// Load the code of decode_b1_kernel<hd> / both gemm_f32_kernel instantiations now (under lazy
+// module loading the first launch would otherwise do it, reserving device memory then).
+cudaError_t preload_decode_b1(int hd);
+cudaError_t preload_gemm_f32();
 int decode_chunk_keys();
 // Scratch sizes (floats) the decode kernel needs for `grid` CTAs.
 size_t decode_b1_spart_floats(int H, int hd, int t_cap);

@@ -9,10 +9,17 @@
 // (the cross-attention K/V of the memory rows, the self-attention K/V cache and the
 // decode kernel's working buffers) lives in one file-scope device array of a fixed size.
 //
-// That array exists once per device for the lifetime of the process.  Every call on a
-// device reuses it, so two calls whose work overlaps on the same GPU would race on it;
-// calls are serialised by a process-wide lock and each call waits for its own work, so
-// this only concerns callers that run several processes' work on one context.
+// That array exists once per device for the lifetime of the process (each process has its
+// own copy).  Model load does the one-time set-up on its device (noalloc_prepare): it looks
+// up the array's device address, which loads this file's module and so reserves the array,
+// and loads the kernels the call launches, so the call itself loads and reserves nothing.
+// Every call reuses the array; two calls whose GPU work overlapped would race on it.  Calls
+// through this library cannot overlap: a process-wide lock serialises them and each call
+// waits for its own GPU work before it returns.
+//
+// The decode always runs the single-grid kernel (decode_b1_kernel), whose scratch the
+// array holds.  ms_generate_device may pick the head-clustered kernel, which sums in a
+// different order, so the two agree to rounding (identical ids except at near-ties).
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -34,7 +41,7 @@ __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 std::mutex g_static_mu;
 unsigned char* g_static_ptr[kMaxDevices] = {};
 
-// Device address of the array for the current device (set up once per device).
+// Device address of the array on `device` (the current device), looked up once.
 unsigned char* static_scratch(int device) {
     if (device < 0 || device >= kMaxDevices) throw MsError(MS_ERR_INVALID_ARG, "device ordinal out of range");
     if (!g_static_ptr[device]) {
@@ -60,6 +67,14 @@ struct Carve {
 };
 
 }  // namespace
+
+void noalloc_prepare(int device, int head_dim) {
+    std::lock_guard<std::mutex> g(g_static_mu);
+    static_scratch(device);
+    MSB_CUDA(preload_decode_b1(head_dim));
+    MSB_CUDA(preload_gemm_f32());
+}
+
 }  // namespace msb
 
 using namespace msb;
@@ -135,7 +150,8 @@ extern "C" ms_status ms_decode_memory_static(ms_model* model, const float* memor
                                                " bytes for this model, frames and tokens; the limit is " +
                                                std::to_string(kStaticScratchBytes));
 
-        unsigned char* base = static_scratch(m.device);
+        unsigned char* base = m.device >= 0 && m.device < kMaxDevices ? g_static_ptr[m.device] : nullptr;
+        if (!base) throw MsError(MS_ERR_CUDA, "static scratch was not set up by model load on this device");
         DecodeParams p{};
         layout(base, &p);
         p.d = d;
@@ -177,8 +193,7 @@ extern "C" ms_status ms_decode_memory_static(ms_model* model, const float* memor
         unsigned hf[4];
         MSB_CUDA(cudaMemcpyAsync(hf, p.bar_count, sizeof(hf), cudaMemcpyDeviceToHost, m.stream));
         MSB_CUDA(cudaStreamSynchronize(m.stream));
-        if (hf[1] == DEV_BARRIER_TIMEOUT) throw MsError(MS_ERR_TIMEOUT, "decode kernel: grid barrier timed out");
-        if (hf[1] != DEV_OK) throw MsError(MS_ERR_CUDA, "decode kernel: device status " + std::to_string(hf[1]));
+        throw_device_status(hf[1], "decode kernel");
         const int calls = (int)hf[2];
         *n_out = calls - (hf[3] ? 1 : 0);
         if (hit_eos) *hit_eos = hf[3] ? 1 : 0;

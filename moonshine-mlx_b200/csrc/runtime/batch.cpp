@@ -151,10 +151,12 @@ void BatchEngine::gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& g
     ga.kb_per_tap = (K + 63) / 64;
     ga.k_per_tap = K;
     ga.status = status.as<unsigned>();
-    if (ga.mode == TC_EPI_ACCUM) {
-        const int tiles = ((ga.N + bn - 1) / bn) * ((ga.M + 127) / 128);
-        ga.splits = std::max(1, std::min(ga.kb_per_tap, m.num_sms / std::max(tiles, 1)));
-    }
+    // k-splits (one cluster per output tile, summed in split order) until the grid covers
+    // the SMs; every split keeps at least one k-block
+    const int tiles = ((ga.N + bn - 1) / bn) * ((ga.M + 127) / 128);
+    int sp = std::max(1, std::min({TC_MAX_SPLITS, ga.kb_per_tap, m.num_sms / std::max(tiles, 1)}));
+    const int per = (ga.kb_per_tap + sp - 1) / sp;
+    ga.splits = (ga.kb_per_tap + per - 1) / per;
     MSB_CUDA(launch_gemm_tc(a, b, ga, bn, m.stream));
 }
 
@@ -645,9 +647,7 @@ BatchEngine::Result BatchEngine::decode_prepared(int B, int T, int maxM, const s
         MSB_CUDA(cudaMemcpyAsync(res.logits.data(), logit_buf.p, res.logits.size() * 4, cudaMemcpyDeviceToHost, s));
     }
     MSB_CUDA(cudaStreamSynchronize(s));
-    if (st_word == DEV_WAIT_TIMEOUT) throw MsError(MS_ERR_TIMEOUT, "batched decode: a pipeline wait timed out");
-    if (st_word == DEV_BAD_TOKEN) throw MsError(MS_ERR_INVALID_ARG, "batched decode: token id out of range");
-    if (st_word != 0) throw MsError(MS_ERR_CUDA, "batched decode: device status " + std::to_string(st_word));
+    throw_device_status(st_word, "batched decode");
     float te = 0, td = 0;
     cudaEventElapsedTime(&te, m.ev[0], m.ev[1]);
     cudaEventElapsedTime(&td, m.ev[1], m.ev[2]);

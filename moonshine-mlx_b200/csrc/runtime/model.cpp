@@ -411,6 +411,17 @@ float* Model::upload(const std::vector<float>& v) {
     return b->as<float>();
 }
 
+void throw_device_status(unsigned code, const char* what) {
+    const std::string w(what);
+    switch (code) {
+        case DEV_OK: return;
+        case DEV_BARRIER_TIMEOUT: throw MsError(MS_ERR_TIMEOUT, w + ": grid exchange timed out");
+        case DEV_WAIT_TIMEOUT: throw MsError(MS_ERR_TIMEOUT, w + ": a pipeline wait timed out");
+        case DEV_BAD_TOKEN: throw MsError(MS_ERR_INVALID_ARG, w + ": token id out of range");
+        default: throw MsError(MS_ERR_CUDA, w + ": device status " + std::to_string(code));
+    }
+}
+
 void Model::ensure_rope(int positions) {
     if (positions <= rope_cap) return;
     const int nd = cfg.rotary_ndims(), half = nd / 2;
@@ -581,6 +592,7 @@ Model* load_model(const std::string& dir, const ms_options& o) {
                         cudaMemcpyHostToDevice));
     m->dec_dev = m->dec_layers_buf.as<DecodeLayerW>();
     m->ensure_rope(4096);
+    noalloc_prepare(o.device, c.head_dim);
     MSB_CUDA(cudaDeviceSynchronize());
     return m.release();
 }
@@ -916,9 +928,7 @@ Model::DecodeResult Model::decode(const float* cross32, const void* cross_stored
                                  stream));
     }
     MSB_CUDA(cudaStreamSynchronize(stream));
-    if (hf[1] == DEV_BARRIER_TIMEOUT) throw MsError(MS_ERR_TIMEOUT, "decode kernel: grid barrier timed out");
-    if (hf[1] == DEV_BAD_TOKEN) throw MsError(MS_ERR_INVALID_ARG, "decode kernel: token id out of range");
-    if (hf[1] != DEV_OK) throw MsError(MS_ERR_CUDA, "decode kernel: device status " + std::to_string(hf[1]));
+    throw_device_status(hf[1], "decode kernel");
     DecodeResult r;
     r.n_calls = (int)hf[2];
     r.hit_eos = hf[3] != 0;

@@ -179,6 +179,14 @@ struct Model {
     void join_lanes(int k);
 };
 
+// Throws the MsError that a decode kernel's device status word stands for (no-op for DEV_OK).
+void throw_device_status(unsigned code, const char* what);
+
+// Allocation-free decode (ms_decode_memory_static): looks up the device address of the
+// static scratch array on `device` (which must be current) and loads the kernels that path
+// launches, so that the calls themselves load and reserve nothing.  Called by model load.
+void noalloc_prepare(int device, int head_dim);
+
 ms_status to_status(const std::exception& e);
 // Sets the thread-local message returned by ms_last_error().
 void set_last_error(const std::string& m);

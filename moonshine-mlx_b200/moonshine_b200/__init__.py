@@ -412,7 +412,7 @@ class MoonshineModel:
         sr = self.sample_rate
         chunk = int(chunk_duration * sr)
         n_chunks = max(1, -(-a.shape[0] // chunk)) if a.shape[0] else 0
-        per_chunk = forced_len if forced_len else int(np.ceil(min(chunk, a.shape[0]) / sr * 6.5)) + 1
+        per_chunk = forced_len if forced_len and forced_len > 0 else int(np.ceil(min(chunk, a.shape[0]) / sr * 6.5)) + 1
         if max_tokens:
             per_chunk = min(per_chunk, max_tokens) if not forced_len else per_chunk
         cap = max(1, n_chunks * per_chunk + 1)
@@ -523,7 +523,7 @@ class MoonshineModel:
         sr = self.sample_rate
         longest = max((a.shape[0] for a in arrs), default=0)
         n_chunks = max(1, -(-longest // int(chunk_duration * sr)))
-        per = forced_len if forced_len else int(np.ceil(min(longest, chunk_duration * sr) / sr * 6.5)) + 1
+        per = forced_len if forced_len and forced_len > 0 else int(np.ceil(min(longest, chunk_duration * sr) / sr * 6.5)) + 1
         cap = n_chunks * per + 1
         ptrs = (C.POINTER(C.c_float) * B)(*[_fptr(a) for a in arrs])
         lens = (C.c_int64 * B)(*[a.shape[0] for a in arrs])

@@ -316,6 +316,24 @@ class Oracle:
             valid |= (diff < 0) & (-diff < right)
         return np.where(valid, 0.0, -1e9).astype(self.dt)
 
+    def _banded_attention(self, q, k, v, left: int, right: int):
+        """The windowed softmax of slidingMask (MoonshineLayers.swift:266-290) evaluated over
+        each query's band of keys [t - left + 1, t + right - 1] only.  The dense form adds
+        -1e9 to every key outside the band, whose exp is exactly 0 in float64, so the two
+        differ only in summation order; the float64 checker uses this form (the dense one
+        spends its time in exp underflow at 30 s of audio), the float32 restatement keeps the
+        reference's dense mask.  q, k, v [H, T, hd] -> [H, T, hd]."""
+        T = q.shape[1]
+        offs = np.arange(-(left - 1), max(right, 1))
+        idx = np.arange(T)[:, None] + offs[None, :]                   # [T, W]
+        valid = (idx >= 0) & (idx < T)
+        idx = np.clip(idx, 0, T - 1)
+        kb, vb = k[:, idx], v[:, idx]                                 # [H, T, W, hd]
+        s = np.einsum("htd,htwd->htw", q, kb) * self.enc_scale
+        s = np.where(valid[None], s, -np.inf)
+        p = _softmax(s)
+        return np.einsum("htw,htwd->htd", p, vb)
+
     def _encoder_layer(self, x, i):
         """EncoderLayer.callAsFunction (MoonshineLayers.swift:297-310)."""
         w = self.w
@@ -331,11 +349,15 @@ class Oracle:
         if rep > 1:
             k = np.repeat(k, rep, axis=0)
             v = np.repeat(v, rep, axis=0)
-        s = q @ k.transpose(0, 2, 1) * self.enc_scale
-        m = self._window_mask(i, T)
-        if m is not None:
-            s = s + m
-        o = (_softmax(s) @ v).transpose(1, 0, 2).reshape(T, H * hd)
+        sw = ec.sliding_windows
+        if self.dt == np.float64 and sw is not None and i < len(sw):
+            o = self._banded_attention(q, k, v, *sw[i]).transpose(1, 0, 2).reshape(T, H * hd)
+        else:
+            s = q @ k.transpose(0, 2, 1) * self.enc_scale
+            m = self._window_mask(i, T)
+            if m is not None:
+                s = s + m
+            o = (_softmax(s) @ v).transpose(1, 0, 2).reshape(T, H * hd)
         x = x + o @ w[p + "self_attn.o_proj.weight"].T
         h = _layer_norm(x, w[p + "post_attention_layernorm.weight"] + 1.0)
         f = _gelu_erf(h @ w[p + "mlp.fc1.weight"].T + w[p + "mlp.fc1.bias"])

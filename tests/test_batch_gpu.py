@@ -68,3 +68,56 @@ def test_batch_of_one_equals_generate(model_root):
     a = synth.synth_audio(48000, 90)
     ids, _ = m.generate_batch([a], forced_len=20)
     assert ids[0] == m.generate(a, forced_len=20).tokens
+
+
+def _config3_audio():
+    """The small-model batched workload: 64 utterances of U(5, 15) s (lengths from PCG64(7),
+    whole frames), audio seeds 100 + i."""
+    rng = np.random.Generator(np.random.PCG64(7))
+    lens = (rng.uniform(5, 15, size=64) * 16000).astype(int) // 80 * 80
+    seeds = [100 + i for i in range(64)]
+    return lens, seeds, [synth.synth_audio(int(n), s) for n, s in zip(lens, seeds)]
+
+
+def test_batch_config3_shape_against_oracle(model_root, tmp_path):
+    """Small architecture, bf16 checkpoint, vocabulary 32768, 64 utterances of U(5, 15) s,
+    128 forced tokens each -- the batched workload at its full shape.  Every utterance is
+    checked against the oracle (a pool of oracle processes): ids identical except where they
+    part at a near-tie, logits within the bf16 tolerance up to there.  A second run of the
+    same batch gives bit-identical ids (the split-K sums run in a fixed order)."""
+    import moonshine_b200 as mb
+    from oracle_pool import check_batch
+    d = model_dir(model_root, "small", dtype="bfloat16")
+    lens, seeds, audios = _config3_audio()
+    m = mb.MoonshineModel.load(d)
+    ids, st, logits = m.generate_batch(audios, forced_len=128, return_logits=True)
+    assert all(len(r) == 128 for r in ids)
+    ids2, _ = m.generate_batch(audios, forced_len=128)
+    assert ids2 == ids
+    res = check_batch(d, lens, seeds, 128, True, ids, logits[:, :128], tmp_path)
+    errs = [e for _, e, _, _, _ in res if e]
+    parted = [(r, k) for r, _, _, k, _ in res if k >= 0]
+    worst = max(w for _, _, w, _, _ in res)
+    print(f"config-3 shape: worst logits error {worst:.3e}, rows parting at a near-tie {parted}, "
+          f"smallest relative top-2 margin {min(mm for *_, mm in res):.2e}")
+    assert not errs, errs
+
+
+def test_batch_runs_are_bit_identical(model_root):
+    """The same batch twice: identical ids and bit-identical logits."""
+    import moonshine_b200 as mb
+    d = model_dir(model_root, "small", dtype="bfloat16", vocab_size=2048, max_position_embeddings=512)
+    audios = [synth.synth_audio(16000 + 4000 * (i % 5), 300 + i) for i in range(24)]
+    m = mb.MoonshineModel.load(d)
+    a_ids, _, a_lg = m.generate_batch(audios, forced_len=24, return_logits=True)
+    b_ids, _, b_lg = m.generate_batch(audios, forced_len=24, return_logits=True)
+    assert a_ids == b_ids
+    assert np.array_equal(a_lg, b_lg)
+
+
+def test_batch_medium_arch(model_root):
+    """Medium architecture (d 640, 10 heads of 64, 14 + 14 layers), bf16 checkpoint, three
+    utterances, 8 forced tokens, against the oracle."""
+    d = model_dir(model_root, "medium", dtype="bfloat16", max_position_embeddings=1024)
+    audios = [synth.synth_audio(n, 400 + i) for i, n in enumerate([32000, 45678, 20000])]
+    _check_batch(d, audios, 8)

@@ -2,6 +2,8 @@
 
 Token ids must be identical; logits must agree within 1e-3 (fp32 weights) measured as
 max |gpu - oracle| / max |oracle| per decoder call."""
+import functools
+
 import numpy as np
 import pytest
 
@@ -264,3 +266,50 @@ def test_quantized_checkpoint(model_root, group, bits, streamed):
         m.close()
     assert rel_err(outs["all"], outs["f32"]) < 1e-4
     assert rel_err(outs["auto"], outs["f32"]) < 1e-4
+
+
+@functools.lru_cache(maxsize=1)
+def _headline_reference(tiny_dir):
+    o = oracle_for(tiny_dir)
+    ids, _, logits, margins = o.greedy(o.memory_for(synth.synth_audio(480000, 1)), 200, True, forced_len=200,
+                                       keep_logits=True)
+    return ids, logits, margins
+
+
+@pytest.mark.parametrize("kernel", ["auto", "grid"])
+def test_headline_workload_200_tokens(tiny_dir, kernel):
+    """The benchmarked workload itself: tiny weights (seed 0), 30 s of audio (seed 1), fp16
+    KV cache, 200 forced decoder calls, through the default kernel ("auto": the head-clustered
+    one on a B200) and the single-grid one.  Ids identical to the float64 oracle's, logits
+    within 1e-3 per call; the smallest top-2 margin is printed."""
+    import moonshine_b200 as mb
+    m = mb.MoonshineModel.load(tiny_dir, decode_kernel=kernel, kv_fp16=True)
+    out = m.generate(synth.synth_audio(480000, 1), forced_len=200, return_logits=True)
+    assert out.decode_kernel == ("cluster" if kernel == "auto" else kernel)
+    ids, logits, margins = _headline_reference(tiny_dir)
+    assert out.tokens == ids
+    worst = assert_logits_close(out.logits[:200], logits, FP32_LOGIT_TOL)
+    rel = [mg / float(np.max(np.abs(lg))) for mg, lg in zip(margins, logits)]
+    print(f"headline workload ({out.decode_kernel}): worst logits error {worst:.2e}, smallest relative "
+          f"top-2 margin {min(rel):.3e} at call {int(np.argmin(rel))}")
+
+
+@pytest.mark.parametrize("kernel", ["auto", "grid"])
+def test_medium_arch_batch1(model_root, kernel):
+    """Medium architecture (d 640, 10 heads of 64 -> 10 head clusters, 14 + 14 layers), fp32,
+    both batch-1 kernels, fp16 KV: teacher-forced logits and free-running ids."""
+    import moonshine_b200 as mb
+    d = model_dir(model_root, "medium", max_position_embeddings=1024)
+    m = mb.MoonshineModel.load(d, decode_kernel=kernel, kv_fp16=True)
+    audio = synth.synth_audio(48000, 8)
+    o = oracle_for(d)
+    mem = o.memory_for(audio)
+    assert rel_err(m.encode(audio), mem) < 1e-4
+    teacher = np.random.Generator(np.random.PCG64(9)).integers(0, 32768, size=12).astype(np.int32)
+    out = m.generate(audio, forced_len=12, teacher_ids=teacher, return_logits=True)
+    assert out.decode_kernel == ("cluster" if kernel == "auto" else kernel)
+    ids, _, logits, _ = o.greedy(mem, 12, True, teacher=teacher.tolist(), keep_logits=True)
+    assert out.tokens == ids
+    assert_logits_close(out.logits[:12], logits, FP32_LOGIT_TOL)
+    free = m.generate(audio, forced_len=12)
+    assert free.tokens == o.greedy(mem, 12, True, forced_len=12)[0]
