@@ -403,7 +403,7 @@ def main():
     ap.add_argument("--no-batched", action="store_true", help="skip the small-model batched leg")
     ap.add_argument("--no-sharded", action="store_true", help="skip the medium-model sharded job")
     ap.add_argument("--no-streaming", action="store_true", help="skip the 512-stream leg")
-    ap.add_argument("--stream-chunks", type=int, default=125, help="80 ms chunks per stream")
+    ap.add_argument("--stream-chunks", type=int, default=25, help="80 ms chunks per stream (the timed sample)")
     ap.add_argument("--seconds", type=float, default=30.0, help="audio length (profiling cases)")
     ap.add_argument("--tokens", type=int, default=200, help="forced decode length (profiling cases)")
     ap.add_argument("--flush-mb", type=int, default=512, help="L2-flush buffer written between steps")

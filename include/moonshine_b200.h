@@ -188,6 +188,15 @@ ms_status ms_generate_device(ms_model* model, const float* audio_dev, int64_t n_
  * calls with their own events. */
 void* ms_model_stream(ms_model* model);
 
+/* Self-attention K/V pages of the batched engine (ms_generate_batch and the lockstep
+ * ms_stream_transcribe_batch; no counterpart in the reference, whose cache grows by
+ * concatenation, MoonshineLayers.swift:106-115).  Each call gives every row
+ * ceil(limit / page_positions) pages of page_positions positions (all layers, K and V), so a
+ * ragged batch holds the sum of its rows' needs rather than rows x the longest, and every
+ * page returns to the pool when the call ends.  *used: pages the last call assigned;
+ * *capacity: pages the pool holds (the largest call so far).  Any output may be null. */
+ms_status ms_model_batch_kv_pages(ms_model* model, int64_t* used, int64_t* capacity, int32_t* page_positions);
+
 /* Batched offline generation: B independent utterances decoded together (no counterpart
  * in the reference, which is batch 1).  Utterances of at most one chunk (chunk_duration)
  * are decoded in lockstep: every projection is one bf16 tensor-core GEMM over all B rows

@@ -518,6 +518,16 @@ void* ms_model_stream(ms_model* model) {
     return model ? (void*)reinterpret_cast<Model*>(model)->stream : nullptr;
 }
 
+ms_status ms_model_batch_kv_pages(ms_model* model, int64_t* used, int64_t* capacity, int32_t* page_positions) {
+    if (!model) return fail(MS_ERR_INVALID_ARG, "null model");
+    Model& m = *reinterpret_cast<Model*>(model);
+    std::lock_guard<std::mutex> g(m.mu);
+    if (used) *used = m.batch ? m.batch->pages_used : 0;
+    if (capacity) *capacity = m.batch ? m.batch->pages_capacity : 0;
+    if (page_positions) *page_positions = BatchEngine::kKvPage;
+    return MS_OK;
+}
+
 static ms_status generate_impl(ms_model* model, const float* audio, int64_t n_samples,
                                const ms_gen_params* params, int32_t* ids_out, int32_t cap, int32_t* n_out,
                                float* logits_out, ms_gen_stats* stats, bool device_io) {

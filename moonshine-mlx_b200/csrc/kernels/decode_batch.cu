@@ -117,10 +117,11 @@ __device__ __forceinline__ float load_kv(const void* base, size_t idx, int f16) 
 }
 
 // One warp per (b, h), eight per CTA.  Lanes own keys for the scores (each reads its key row
-// in 16-byte loads against q staged in shared memory), dims (2c, 2c+1) for the V sum.
+// in 16-byte loads against q staged in shared memory), dims (2c, 2c+1) for the V sum.  Keys
+// 0..t-1 come from row b's pages (a key without a page -- a row past its own limit -- is
+// skipped), key t is this step's fp32 K/V.
 __global__ void self_attn_batch_kernel(const float* __restrict__ q, const float* __restrict__ kv_new,
-                                       const void* __restrict__ kc, const void* __restrict__ vc, int kv_f16,
-                                       const int* __restrict__ pos, int B, int H, int KVH, int hd, int t_cap,
+                                       const PagedKv kv, const int* __restrict__ pos, int B, int H, int KVH, int hd,
                                        float scale, __nv_bfloat16* __restrict__ out) {
     pdl_wait();
     pdl_trigger();
@@ -134,7 +135,10 @@ __global__ void self_attn_batch_kernel(const float* __restrict__ q, const float*
     const float* qr = q + (size_t)b * HD + h * hd;
     const float* fk = kv_new + (size_t)b * 2 * KVD + kvh * hd;
     const float* fv = fk + KVD;
-    const size_t cb = ((size_t)b * KVH + kvh) * t_cap * hd;
+    // element offsets of this (layer, head)'s K and V inside a page
+    const size_t koff = (size_t)kv.layer_off + (size_t)kvh * kv.page * hd;
+    const size_t voff = koff + (size_t)KVH * kv.page * hd;
+    const int* tab = kv.table + (size_t)b * kv.table_stride;
     // this head's q, staged once per warp and read back as broadcast float4s
     __shared__ __align__(16) float qsh[8][MAXHD_B];
     float* qw = qsh[(threadIdx.x >> 5) & 7];
@@ -146,17 +150,24 @@ __global__ void self_attn_batch_kernel(const float* __restrict__ q, const float*
         const int nk = min(CHB, t + 1 - j0);
         const int j = j0 + lane;
         float s = -INFINITY;
-        if (lane < nk) {
+        // element offset of key j's row inside the pool (-1: no key)
+        long long rowe = -1;
+        if (lane < nk && j < t) {
+            const int lp = j / kv.page;
+            const int phys = lp < kv.table_stride ? tab[lp] : -1;
+            if (phys >= 0) rowe = (long long)phys * kv.page_elems + (long long)(j % kv.page) * hd;
+        }
+        if (lane < nk && (j == t || rowe >= 0)) {
             // the lane's key row in 16-byte loads (hd % 8 == 0: rows start 16-byte aligned)
             float dot = 0.f;
             if (j == t) {
                 const float4* k4 = reinterpret_cast<const float4*>(fk);
                 for (int p = 0; p < hd / 4; ++p) {
-                    const float4 kv = k4[p], qq = q4[p];
-                    dot = fmaf(qq.x, kv.x, fmaf(qq.y, kv.y, fmaf(qq.z, kv.z, fmaf(qq.w, kv.w, dot))));
+                    const float4 kk = k4[p], qq = q4[p];
+                    dot = fmaf(qq.x, kk.x, fmaf(qq.y, kk.y, fmaf(qq.z, kk.z, fmaf(qq.w, kk.w, dot))));
                 }
-            } else if (kv_f16) {
-                const uint4* k8 = reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(kc) + cb + (size_t)j * hd);
+            } else if (kv.kv_f16) {
+                const uint4* k8 = reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(kv.pool) + koff + rowe);
 #pragma unroll 4
                 for (int p = 0; p < hd / 8; ++p) {
                     const uint4 u = k8[p];
@@ -168,39 +179,39 @@ __global__ void self_attn_batch_kernel(const float* __restrict__ q, const float*
                     dot = fmaf(qb.x, f2.x, fmaf(qb.y, f2.y, fmaf(qb.z, f3.x, fmaf(qb.w, f3.y, dot))));
                 }
             } else {
-                const float4* k4 = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kc) + cb + (size_t)j * hd);
+                const float4* k4 = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kv.pool) + koff + rowe);
 #pragma unroll 4
                 for (int p = 0; p < hd / 4; ++p) {
-                    const float4 kv = k4[p], qq = q4[p];
-                    dot = fmaf(qq.x, kv.x, fmaf(qq.y, kv.y, fmaf(qq.z, kv.z, fmaf(qq.w, kv.w, dot))));
+                    const float4 kk = k4[p], qq = q4[p];
+                    dot = fmaf(qq.x, kk.x, fmaf(qq.y, kk.y, fmaf(qq.z, kk.z, fmaf(qq.w, kk.w, dot))));
                 }
             }
             s = dot * scale;
         }
         const float mc = warp_max(s);
         const float mn = fmaxf(m, mc);
-        const float p = (lane < nk) ? expf(s - mn) : 0.f;
+        const float p = (s != -INFINITY) ? expf(s - mn) : 0.f;
         const float corr = (m == -INFINITY) ? 0.f : expf(m - mn);
         l = l * corr + warp_sum(p);
         a0 *= corr;
         a1 *= corr;
         for (int jj = 0; jj < nk; ++jj) {
             const float pp = __shfl_sync(FULL, p, jj);
+            const long long re = __shfl_sync(FULL, rowe, jj);
             const int row = j0 + jj;
             const int c = 2 * lane;
-            if (c < hd) {
+            if (c < hd && (row == t || re >= 0)) {
                 float v0, v1;
                 if (row == t) {
                     v0 = fv[c];
                     v1 = fv[c + 1];
-                } else if (kv_f16) {
+                } else if (kv.kv_f16) {
                     const float2 f = __half22float2(
-                        *reinterpret_cast<const __half2*>(reinterpret_cast<const __half*>(vc) + cb + (size_t)row * hd + c));
+                        *reinterpret_cast<const __half2*>(reinterpret_cast<const __half*>(kv.pool) + voff + re + c));
                     v0 = f.x;
                     v1 = f.y;
                 } else {
-                    const float2 f =
-                        *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(vc) + cb + (size_t)row * hd + c);
+                    const float2 f = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(kv.pool) + voff + re + c);
                     v0 = f.x;
                     v1 = f.y;
                 }
@@ -547,14 +558,13 @@ cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv
     return launch_kernel(ln_bf16_kernel, dim3(rows), dim3(128), 0, s, x, rows, d, w, w_offset, out);
 }
 
-cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const void* kc, const void* vc, int kv_f16,
-                                   const int* pos, int B, int H, int KVH, int hd, int t_cap, float scale,
-                                   __nv_bfloat16* out, cudaStream_t s) {
-    if (hd > MAXHD_B || (hd & 7)) return cudaErrorInvalidValue;
+cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const PagedKv& kv, const int* pos, int B,
+                                   int H, int KVH, int hd, float scale, __nv_bfloat16* out, cudaStream_t s) {
+    if (hd > MAXHD_B || (hd & 7) || !kv.table || kv.page <= 0 || !kv.pool) return cudaErrorInvalidValue;
     ++launch_counter();
     const int items = B * H;
-    return launch_kernel(self_attn_batch_kernel, dim3((items + 7) / 8), dim3(256), 0, s, q, kv_new, kc, vc, kv_f16,
-                         pos, B, H, KVH, hd, t_cap, scale, out);
+    return launch_kernel(self_attn_batch_kernel, dim3((items + 7) / 8), dim3(256), 0, s, q, kv_new, kv, pos, B, H,
+                         KVH, hd, scale, out);
 }
 
 cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const void* cross_st, int st_f16,

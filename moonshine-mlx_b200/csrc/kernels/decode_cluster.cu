@@ -92,6 +92,12 @@ __host__ __device__ inline Segs make_segs(const ClusterGeom& g, int d, int hd) {
 enum SegId { SEG_QKV = 0, SEG_O, SEG_CQ, SEG_XKV, SEG_CO, SEG_FC1, SEG_FC2, SEG_LM };
 
 constexpr int MAXB = 320;  // blocks per step a CTA's schedule may have (checked at launch)
+#ifndef MSB_FC2_MAXR
+#define MSB_FC2_MAXR 1024
+#endif
+#ifndef MSB_PF_AHEAD
+#define MSB_PF_AHEAD 0
+#endif
 
 struct SegPlan {
     size_t off;  // floats from the CTA's stream base
@@ -114,7 +120,7 @@ __host__ __device__ inline SegPlan seg_plan(int seg, int layer, const ClusterGeo
         case SEG_CQ: return {lw + sg.cq, d, ncq, sd, 1, mq};
         case SEG_CO: return {lw + sg.co, 0, no, row_stride(hd), 1, 64};
         case SEG_FC1: return {lw + sg.fc1, d + 2 * g.gr, 2 * g.gr, sd, 2, mq};
-        case SEG_FC2: return {lw + sg.fc2, sg.ro4, d, g.gr, 1, 64};
+        case SEG_FC2: return {lw + sg.fc2, sg.ro4, d, g.gr, 1, MSB_FC2_MAXR};
         default: return {(size_t)L * sg.layer, d, nlm, lm_stride<QR>(g, d), 1, QR && g.lm_qbits ? NT : 32};
     }
 }
@@ -375,6 +381,12 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
     auto issue_next = [&]() {
         if (n_iss >= n_total || s_failed) return;
         const BlockEnt e = n_iss < nb0 ? s_tab[0][n_iss] : s_tab[1][(n_iss - nb0) % nb1];
+        if (MSB_PF_AHEAD > 0 && n_iss + MSB_PF_AHEAD < n_total) {
+            const uint32_t f = n_iss + MSB_PF_AHEAD;
+            const BlockEnt pe = f < nb0 ? s_tab[0][f] : s_tab[1][(f - nb0) % nb1];
+            bulk_prefetch_l2(pe.s0, pe.b0);
+            if (pe.b1) bulk_prefetch_l2(pe.s1, pe.b1);
+        }
         const int slot = n_iss % NSLOT;
         mbar_expect_tx(&full[slot], e.b0 + e.b1);
         unsigned char* dst = ring + (size_t)slot * slot_bytes;

@@ -248,10 +248,16 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* 
                     const int j = (region - 1) * KVD + rdim;
                     *reinterpret_cast<float4*>(rp.kv_new + (size_t)m * 2 * KVD + j) = v;
                     const int head = rdim / rp.hd, dim = rdim - head * rp.hd;
-                    const size_t idx = (((size_t)m * rp.KVH + head) * rp.t_cap + t_pos) * rp.hd + dim;
-                    void* base = region == 2 ? rp.v_cache : rp.k_cache;
-                    if (rp.kv_f16) st_f16x4(reinterpret_cast<__half*>(base) + idx, v);
-                    else *reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + idx) = v;
+                    const PagedKv& pk = rp.kv;
+                    const int lp = t_pos / pk.page;
+                    const int phys = lp < pk.table_stride ? pk.table[(size_t)m * pk.table_stride + lp] : -1;
+                    if (phys >= 0) {  // rows past their own limit have no page here
+                        const size_t idx = (size_t)phys * pk.page_elems + pk.layer_off +
+                                           ((size_t)(region - 1) * rp.KVH + head) * pk.page * rp.hd +
+                                           (size_t)(t_pos % pk.page) * rp.hd + dim;
+                        if (pk.kv_f16) st_f16x4(reinterpret_cast<__half*>(pk.pool) + idx, v);
+                        else *reinterpret_cast<float4*>(reinterpret_cast<float*>(pk.pool) + idx) = v;
+                    }
                 }
             }
         } else {  // TC_EPI_ARGMAX: the TPR threads of a row lie in one warp
@@ -540,8 +546,8 @@ bool epilogue_layout_ok(const TcGemmArgs& g) {
             return g.out_bf16 && g.ldc_bf16 % 2 == 0 && aligned(g.out_bf16, 4) && (!ep.bias || aligned(ep.bias, 16));
         case TC_EPI_ROPE_KV: {
             const TcRopeKv& r = g.rope;
-            return r.hd % 4 == 0 && aligned(r.q, 16) && aligned(r.kv_new, 16) &&
-                   aligned(r.k_cache, r.kv_f16 ? 8 : 16) && aligned(r.v_cache, r.kv_f16 ? 8 : 16) &&
+            return r.hd % 4 == 0 && aligned(r.q, 16) && aligned(r.kv_new, 16) && r.kv.table && r.kv.page > 0 &&
+                   aligned(r.kv.pool, 16) && r.kv.page_elems % 4 == 0 && r.kv.layer_off % 4 == 0 &&
                    g.N == (r.H + 2 * r.KVH) * r.hd;
         }
         case TC_EPI_ARGMAX:

@@ -96,6 +96,22 @@ enum TcEpiMode {
     TC_EPI_ACCUM = 4,    // out += acc (+ bias): the residual update (one CTA finalises each element)
 };
 
+// Paged self-attention K/V of the batched engine.  A page holds `page` consecutive positions
+// of one row for every layer, K and V: the element of (layer, k|v, kv head, position j, dim)
+// lives at pool + phys * page_elems + layer_off + kv * KVH * page * hd
+//                  + (head * page + j % page) * hd + dim   (elements of the KV dtype),
+// with phys = table[row * table_stride + j / page] the row's physical page (-1: no page; a
+// write there is dropped and a read sees no key).  layer_off selects the layer.
+struct PagedKv {
+    void* pool = nullptr;
+    const int* table = nullptr;
+    int table_stride = 0;         // logical pages per row in the table
+    int page = 16;                // positions per page
+    long long page_elems = 0;     // elements per page (all layers, K and V)
+    long long layer_off = 0;      // elements from a page's start to this layer's K
+    int kv_f16 = 0;
+};
+
 // Decoder q|k|v epilogue parameters (row m = batch slot b).
 struct TcRopeKv {
     const int* pos = nullptr;       // device: position of this step
@@ -104,9 +120,7 @@ struct TcRopeKv {
     int nd = 0, hd = 0, H = 0, KVH = 0;
     float* q = nullptr;             // [M, H*hd] fp32
     float* kv_new = nullptr;        // [M, 2*KVH*hd] fp32 (k then v)
-    void* k_cache = nullptr;        // [M][KVH][t_cap][hd]
-    void* v_cache = nullptr;
-    int t_cap = 0, kv_f16 = 0;
+    PagedKv kv;                     // this step's K/V go to position *pos of row m
 };
 
 constexpr int TC_MAX_SPLITS = 8;  // portable cluster size
@@ -260,9 +274,8 @@ cudaError_t launch_embed_rows(const int* ids, const float* embed, int d, int B, 
                               cudaStream_t s);
 cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv_bfloat16* out, cudaStream_t s,
                           float w_offset = 0.f);
-cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const void* kc, const void* vc, int kv_f16,
-                                   const int* pos, int B, int H, int KVH, int hd, int t_cap, float scale,
-                                   __nv_bfloat16* out, cudaStream_t s);
+cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const PagedKv& kv, const int* pos, int B,
+                                   int H, int KVH, int hd, float scale, __nv_bfloat16* out, cudaStream_t s);
 cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const void* cross_st, int st_f16,
                                     const int* pos, const int* frame_off, const int* frames, int B, int H, int KVH,
                                     int hd, int m_cap, int layer, int max_frames, float scale, float* part,

@@ -121,8 +121,6 @@ void BatchEngine::ensure_ws(int B, int T, int Mtot, int maxM) {
     }
     if (T > Tc || remap) {
         Tc = std::max(Tc, T);
-        kcache.ensure((size_t)c.layers * Bc * KVD * Tc * 4);  // fp32-sized: the KV dtype may change
-        vcache.ensure((size_t)c.layers * Bc * KVD * Tc * 4);
         ids.ensure((size_t)Bc * Tc * 4);
     }
     (void)kvsz;
@@ -146,6 +144,31 @@ void BatchEngine::ensure_ws(int B, int T, int Mtot, int maxM) {
     }
 }
 
+// Self-attention K/V pages for this call: row b gets ceil(limits[b] / kKvPage) pages (the
+// positions it can reach), numbered consecutively from 0; the pool grows to the largest call
+// seen and every page returns to it when the call ends.  Table entries past a row's pages
+// are -1 (rows that have reached their limit keep stepping in lockstep; their writes there
+// are dropped).
+void BatchEngine::assign_pages(int B, int T, const std::vector<int>& limits) {
+    const Config& c = m.cfg;
+    const int KVD = c.kv_heads * c.head_dim;
+    table_stride = (T + kKvPage - 1) / kKvPage;
+    std::vector<int> tab((size_t)B * table_stride, -1);
+    int64_t next = 0;
+    for (int b = 0; b < B; ++b) {
+        const int need = (std::max(limits[b], 1) + kKvPage - 1) / kKvPage;
+        for (int q = 0; q < need && q < table_stride; ++q) tab[(size_t)b * table_stride + q] = (int)next++;
+    }
+    const size_t page_bytes = (size_t)c.layers * 2 * KVD * kKvPage * 4;  // fp32-sized: the KV dtype may change
+    kvpool.ensure((size_t)std::max<int64_t>(next, 1) * page_bytes);
+    pages_used = next;
+    pages_capacity = (int64_t)(kvpool.bytes / page_bytes);
+    ptable.ensure(tab.size() * 4);
+    MSB_CUDA(cudaMemcpyAsync(ptable.p, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, m.stream));
+    // the host vector goes away at return: the copy must have read it
+    MSB_CUDA(cudaStreamSynchronize(m.stream));
+}
+
 void BatchEngine::gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& ga, int K, int bn) {
     ga.taps = 1;
     ga.kb_per_tap = (K + 63) / 64;
@@ -154,7 +177,13 @@ void BatchEngine::gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& g
     // k-splits (one cluster per output tile, summed in split order) until the grid covers
     // the SMs; every split keeps at least one k-block
     const int tiles = ((ga.N + bn - 1) / bn) * ((ga.M + 127) / 128);
-    int sp = std::max(1, std::min({TC_MAX_SPLITS, ga.kb_per_tap, m.num_sms / std::max(tiles, 1)}));
+#ifndef MSB_SPLIT_POLICY
+#define MSB_SPLIT_POLICY 2
+#endif
+    int cap_s = TC_MAX_SPLITS;
+    if (MSB_SPLIT_POLICY == 2 && ga.mode != TC_EPI_ACCUM) cap_s = 1;
+    if (MSB_SPLIT_POLICY == 3) cap_s = ga.mode != TC_EPI_ACCUM ? 1 : 4;
+    int sp = std::max(1, std::min({cap_s, ga.kb_per_tap, m.num_sms / std::max(tiles, 1)}));
     const int per = (ga.kb_per_tap + sp - 1) / sp;
     ga.splits = (ga.kb_per_tap + per - 1) / per;
     MSB_CUDA(launch_gemm_tc(a, b, ga, bn, m.stream));
@@ -177,7 +206,6 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
     const int d = c.hidden, H = c.heads, KVH = c.kv_heads, hd = c.head_dim, I = c.inter;
     const int HD = H * hd, KVD = KVH * hd;
     const float scale = std::pow((float)hd, -0.5f);
-    const size_t kvsz = m.kv_f16 ? 2 : 4;
     cudaStream_t s = m.stream;
     const int* posp = pos.as<int>();
     float* X = x.as<float>();
@@ -185,8 +213,14 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
     for (int l = 0; l < c.layers; ++l) {
         const DecodeLayerW& W = m.dec[l];
         LayerB& L = layers[l];
-        char* kc = kcache.as<char>() + (size_t)l * Bc * KVD * Tc * kvsz;
-        char* vc = vcache.as<char>() + (size_t)l * Bc * KVD * Tc * kvsz;
+        PagedKv pk;
+        pk.pool = kvpool.p;
+        pk.table = ptable.as<int>();
+        pk.table_stride = table_stride;
+        pk.page = kKvPage;
+        pk.page_elems = (long long)c.layers * 2 * KVD * kKvPage;
+        pk.layer_off = (long long)l * 2 * KVD * kKvPage;
+        pk.kv_f16 = m.kv_f16 ? 1 : 0;
         // self-attention block
         MSB_CUDA(launch_ln_bf16(X, B, d, W.ln1, hb.as<__nv_bfloat16>(), s));
         {
@@ -203,14 +237,11 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
             ga.rope.KVH = KVH;
             ga.rope.q = q.as<float>();
             ga.rope.kv_new = kvnew.as<float>();
-            ga.rope.k_cache = kc;
-            ga.rope.v_cache = vc;
-            ga.rope.t_cap = Tc;
-            ga.rope.kv_f16 = m.kv_f16 ? 1 : 0;
+            ga.rope.kv = pk;
             gemm(a_hb, L.m_qkv, ga, d, kBnNarrow);
         }
-        MSB_CUDA(launch_self_attn_batch(q.as<float>(), kvnew.as<float>(), kc, vc, m.kv_f16 ? 1 : 0, posp, B, H, KVH,
-                                        hd, Tc, scale, attn.as<__nv_bfloat16>(), s));
+        MSB_CUDA(launch_self_attn_batch(q.as<float>(), kvnew.as<float>(), pk, posp, B, H, KVH, hd, scale,
+                                        attn.as<__nv_bfloat16>(), s));
         {
             TcGemmArgs ga;
             ga.M = B;
@@ -593,6 +624,7 @@ BatchEngine::Result BatchEngine::decode_prepared(int B, int T, int maxM, const s
     const Config& c = m.cfg;
     cudaStream_t s = m.stream;
     Result res;
+    assign_pages(B, T, limits);
     // step state
     std::vector<int> bos(B, c.dec_start);
     MSB_CUDA(cudaMemcpyAsync(next_ids.p, bos.data(), (size_t)B * 4, cudaMemcpyHostToDevice, s));

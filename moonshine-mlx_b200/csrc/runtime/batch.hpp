@@ -14,6 +14,10 @@ struct BatchEngine {
     explicit BatchEngine(Model& model) : m(model) {}
     ~BatchEngine();
 
+    static constexpr int kKvPage = 16;  // positions per self-attention K/V page
+    int64_t pages_used = 0;             // pages the last call assigned
+    int64_t pages_capacity = 0;         // pages the pool holds
+
     struct Result {
         std::vector<int32_t> ids;      // [B][t_cap]
         std::vector<int32_t> counts;   // [B]
@@ -52,8 +56,12 @@ struct BatchEngine {
     __nv_bfloat16* lm = nullptr;
     CUtensorMap m_lm;
     int Bc = 0, Tc = 0, Mc = 0, Fc = 0;  // capacities: rows, steps, total frames, frames per row
-    DevBuf x, hb, attn, g, q, qc, kvnew, kcache, vcache, part, amax, ids, next_ids, counts, limits_d, done, hit,
+    DevBuf x, hb, attn, g, q, qc, kvnew, part, amax, ids, next_ids, counts, limits_d, done, hit,
         pos, frame_off, frames, cross32, cross16, memory, status;
+    // paged self-attention K/V: page pool and per-row page table of the current call
+    DevBuf kvpool, ptable;
+    int table_stride = 0;
+    void assign_pages(int B, int T, const std::vector<int>& limits);
     CUtensorMap a_hb, a_attn, a_g;
 
     // Utterances are encoded concurrently on the model's encoder lanes.

@@ -126,6 +126,7 @@ def _load_lib() -> C.CDLL:
                                       C.POINTER(C.c_double), i32p]),
         "ms_alignment_jump_frames": (C.c_int, [f32p, C.c_int32, C.c_int32, i32p]),
         "ms_model_stream": (C.c_void_p, [P]),
+        "ms_model_batch_kv_pages": (C.c_int, [P, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(C.c_int32)]),
         "ms_decode_memory_static": (C.c_int, [P, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
                                               i32p, i32p]),
         "ms_encode": (C.c_int, [P, f32p, C.c_int64, f32p, C.c_int64, i32p]),
@@ -507,6 +508,12 @@ class MoonshineModel:
                                             1 if forced else 0, C.c_void_p(ids_dev_ptr), C.byref(n),
                                             C.byref(hit)))
         return n.value, bool(hit.value)
+
+    def batch_kv_pages(self):
+        """(pages the last batched call assigned, pages the pool holds, positions per page)."""
+        u, c, p = C.c_int64(), C.c_int64(), C.c_int32()
+        _check(_L().ms_model_batch_kv_pages(self._h, C.byref(u), C.byref(c), C.byref(p)))
+        return u.value, c.value, p.value
 
     @property
     def cuda_stream(self) -> int:

@@ -11,9 +11,9 @@ from util import BF16_LOGIT_TOL, assert_logits_close, model_dir, oracle_for, wit
 pytestmark = pytest.mark.gpu
 
 
-def _check_batch(path, audios, forced, kv_fp16=True, max_tokens=None):
+def _check_batch(path, audios, forced, kv_fp16=True, max_tokens=None, model=None):
     import moonshine_b200 as mb
-    m = mb.MoonshineModel.load(path, kv_fp16=kv_fp16)
+    m = model or mb.MoonshineModel.load(path, kv_fp16=kv_fp16)
     ids, st, logits = m.generate_batch(audios, forced_len=forced, max_tokens=max_tokens, return_logits=True)
     o = oracle_for(path)
     for b, a in enumerate(audios):
@@ -121,3 +121,36 @@ def test_batch_medium_arch(model_root):
     d = model_dir(model_root, "medium", dtype="bfloat16", max_position_embeddings=1024)
     audios = [synth.synth_audio(n, 400 + i) for i, n in enumerate([32000, 45678, 20000])]
     _check_batch(d, audios, 8)
+
+
+def test_batch_kv_pages_ragged(model_root):
+    """Paged self-attention K/V: rows with limits 4, 26, 9 and 17 (ceil(6.5 s)) get 1, 2, 1
+    and 2 pages of 16 positions -- 6 pages in one pool instead of 4 rows x 2 -- and still
+    match the oracle; a smaller call afterwards takes fewer pages from the same pool, and
+    the lockstep streaming decode draws its pages from it too."""
+    import moonshine_b200 as mb
+    d = model_dir(model_root, "tiny")
+    m = mb.MoonshineModel.load(d)
+    lens = [8000, 64000, 20000, 40000]
+    audios = [synth.synth_audio(n, 500 + i) for i, n in enumerate(lens)]
+    _check_batch(d, audios, None, model=m)
+    used, cap, page = m.batch_kv_pages()
+    assert page == 16
+    assert used == sum(-(-int(np.ceil(n / 16000 * 6.5)) // page) for n in lens) == 6
+    assert cap >= used
+    _check_batch(d, audios[:1], None, model=m)
+    used2, cap2, _ = m.batch_kv_pages()
+    assert used2 == 1 and cap2 == cap
+    # lockstep streaming decode of three streams: pages per call, returned after it
+    states = [m.create_stream() for _ in range(3)]
+    for st in states:
+        m.start_stream(st)
+    sc = mb.StreamingConfig(batch_decode=True)
+    for k in range(6):
+        for i, st in enumerate(states):
+            m.add_audio(st, synth.synth_audio(1280 * (i + 1), 600 + 10 * k + i))
+        m.transcribe_batch(states, streaming_config=sc, max_tokens=16)
+        u, c, _ = m.batch_kv_pages()
+        assert 1 <= u <= 3 and c == cap
+    for st in states:
+        st.close()

@@ -294,20 +294,20 @@ def test_headline_workload_200_tokens(tiny_dir, kernel):
           f"top-2 margin {min(rel):.3e} at call {int(np.argmin(rel))}")
 
 
-@pytest.mark.parametrize("kernel", ["auto", "grid"])
-def test_medium_arch_batch1(model_root, kernel):
+def test_medium_arch_batch1(model_root):
     """Medium architecture (d 640, 10 heads of 64 -> 10 head clusters, 14 + 14 layers), fp32,
-    both batch-1 kernels, fp16 KV: teacher-forced logits and free-running ids."""
+    fp16 KV, on the head-clustered kernel (the single-grid kernel's per-warp staging does not
+    fit shared memory at d 640): teacher-forced logits and free-running ids."""
     import moonshine_b200 as mb
     d = model_dir(model_root, "medium", max_position_embeddings=1024)
-    m = mb.MoonshineModel.load(d, decode_kernel=kernel, kv_fp16=True)
+    m = mb.MoonshineModel.load(d, kv_fp16=True)
     audio = synth.synth_audio(48000, 8)
     o = oracle_for(d)
     mem = o.memory_for(audio)
     assert rel_err(m.encode(audio), mem) < 1e-4
     teacher = np.random.Generator(np.random.PCG64(9)).integers(0, 32768, size=12).astype(np.int32)
     out = m.generate(audio, forced_len=12, teacher_ids=teacher, return_logits=True)
-    assert out.decode_kernel == ("cluster" if kernel == "auto" else kernel)
+    assert out.decode_kernel == "cluster"
     ids, _, logits, _ = o.greedy(mem, 12, True, teacher=teacher.tolist(), keep_logits=True)
     assert out.tokens == ids
     assert_logits_close(out.logits[:12], logits, FP32_LOGIT_TOL)
