@@ -54,12 +54,13 @@ typedef struct ms_stream ms_stream;
  * (MoonshineModel.swift:47-65). */
 typedef enum { MS_KV_F32 = 0, MS_KV_F16 = 1 } ms_kv_dtype;
 
-/* Matmul input type of the encoder in batched generation, and the weight rows of
- * quantized checkpoints in the batch-1 decode.  The batch-1 kernels compute in fp32 from
- * the checkpoint's values and the batched decode always runs bf16 tensor-core GEMMs; the
- * batched encoder runs bf16 tensor-core GEMMs for BF16/F16 checkpoints under MS_W_AUTO or
- * for any checkpoint under MS_W_BF16, and fp32 CUDA-core GEMMs otherwise (MS_W_F32, or an
- * F32 checkpoint under MS_W_AUTO).  For a quantized checkpoint the clustered batch-1 kernel
+/* Matmul input type of batched generation, and the weight rows of quantized checkpoints in
+ * the batch-1 decode.  The batch-1 kernels compute in fp32 from the checkpoint's values.
+ * Batched generation runs tensor-core GEMMs: for BF16/F16 checkpoints under MS_W_AUTO, or
+ * any checkpoint under MS_W_BF16, on bf16 inputs (the encoder too); otherwise (MS_W_F32, or
+ * an F32 checkpoint under MS_W_AUTO) the decode GEMMs take every weight and input as a bf16
+ * high plane plus a bf16 low plane and sum three products (hi.hi + hi.lo + lo.hi), which
+ * keeps fp32-level accuracy, and the encoder runs fp32 CUDA-core GEMMs.  For a quantized checkpoint the clustered batch-1 kernel
  * streams the quantized codes of its row-split weights (ms_model_decode_weight_bits) except
  * under MS_W_F32, which streams them dequantized to fp32. */
 typedef enum { MS_W_AUTO = 0, MS_W_F32 = 1, MS_W_BF16 = 2 } ms_weight_dtype;
@@ -199,9 +200,10 @@ ms_status ms_model_batch_kv_pages(ms_model* model, int64_t* used, int64_t* capac
 
 /* Batched offline generation: B independent utterances decoded together (no counterpart
  * in the reference, which is batch 1).  Utterances of at most one chunk (chunk_duration)
- * are decoded in lockstep: every projection is one bf16 tensor-core GEMM over all B rows
- * (fp32 accumulation, residual stream and softmax), so logits agree with a per-utterance
- * ms_generate to bf16 precision.  Longer utterances fall back to per-utterance decoding.
+ * are decoded in lockstep: every projection is one tensor-core GEMM over all B rows (fp32
+ * accumulation, residual stream and softmax; inputs as ms_weight_dtype describes), so logits
+ * agree with a per-utterance ms_generate to bf16 precision for bf16 checkpoints and to fp32
+ * precision for fp32 ones.  Longer utterances fall back to per-utterance decoding.
  * ids_out is [B * cap], n_out [B]; teacher ids are not supported. */
 ms_status ms_generate_batch(ms_model* model, const float* const* audios,
                             const int64_t* n_samples, int32_t batch,
@@ -305,9 +307,10 @@ typedef struct {
     int32_t max_memory_frames;   /* default 100000 */
     int32_t min_segment_frames;  /* default 250 */
     int32_t batch_decode;        /* ms_stream_transcribe_batch only (default 0): 1 decodes all
-                                    streams of one model in lockstep on bf16 tensor cores;
-                                    ids then match a per-stream decode except where the top
-                                    two logits are closer than bf16 precision */
+                                    streams of one model in lockstep on tensor cores (the
+                                    batched engine; fp32 checkpoints keep fp32-level products,
+                                    bf16 ones bf16), so ids match a per-stream decode except
+                                    where the top two logits are closer than that precision */
     float temperature;           /* transcribe(temperature:) (:122-128): 0 greedy (default);
                                     > 0 draws each token from softmax(logits / temperature)
                                     (decodeMemory, :238-268) by the Gumbel-max trick */

@@ -68,6 +68,10 @@ __device__ __forceinline__ void cp16(void* s, const void* g) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(s)), "l"(g) : "memory");
 }
 
+#ifndef MSB_W0_FREE
+#define MSB_W0_FREE 0
+#endif
+
 // GEMV rows of the packed streams are stored rf + 4 floats apart (rf % 8 == 0): an odd
 // number of 16-byte units, so lanes that own consecutive rows read distinct bank groups.
 __host__ __device__ inline int row_stride(int rf) { return rf + 4; }
@@ -82,9 +86,12 @@ __device__ __noinline__ void block_gemv(const float* rows, int nr, int rf, int r
     const int c4 = rf >> 2;
     const float4* v4 = reinterpret_cast<const float4*>(vec);
     if (c4 >= 4 * NW) {
-        const int per = (c4 + NW - 1) / NW;
-        const int k0 = w * per, k1 = min(c4, k0 + per);
-        for (int i = lane; i < nr; i += 32) {
+        // MSB_W0_FREE: warp 0 (whose lane 0 issues the ring's bulk copies) takes no columns
+        constexpr int W0 = MSB_W0_FREE ? 1 : 0;
+        constexpr int NWK = NW - W0;
+        const int per = (c4 + NWK - 1) / NWK;
+        const int k0 = (w - W0) * per, k1 = w < W0 ? k0 : min(c4, k0 + per);
+        for (int i = lane; i < nr && w >= W0; i += 32) {
             const float4* row = reinterpret_cast<const float4*>(rows + (size_t)i * rs);
             float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
             int k = k0;
@@ -107,13 +114,13 @@ __device__ __noinline__ void block_gemv(const float* rows, int nr, int rf, int r
                 a2 = fmaf(x.z, u.z, a2);
                 a3 = fmaf(x.w, u.w, a3);
             }
-            part[w * 64 + i] = (a0 + a1) + (a2 + a3);
+            part[(w - W0) * 64 + i] = (a0 + a1) + (a2 + a3);
         }
         __syncthreads();
-        for (int i = tid; i < nr; i += NT) {
+        for (int i = tid - 32 * W0; i < nr && i >= 0; i += NT - 32 * W0) {
             float sum = 0.f;
 #pragma unroll
-            for (int q = 0; q < NW; ++q) sum += part[q * 64 + i];
+            for (int q = 0; q < NWK; ++q) sum += part[q * 64 + i];
             res[i] = sum;
         }
     } else {

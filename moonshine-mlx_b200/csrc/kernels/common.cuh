@@ -74,6 +74,14 @@ __device__ __forceinline__ void red_release_gpu_add(unsigned* p, unsigned v) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// bf16 of v at p[0] and, when lo_off != 0, the bf16 of its remainder v - bf16(v) at
+// p[lo_off] (the low plane of a split operand: v = hi + lo to ~2^-17 relative)
+__device__ __forceinline__ void st_bf16_split(__nv_bfloat16* p, float v, size_t lo_off) {
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    p[0] = h;
+    if (lo_off) p[lo_off] = __float2bfloat16_rn(v - __bfloat162float(h));
+}
+
 // ---------------------------------------------------------------- mbarriers and bulk copies
 constexpr uint32_t WAIT_LIMIT = 1u << 22;  // polls of a bounded mbarrier wait
 
@@ -115,12 +123,6 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
             smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
-}
-
-// Non-blocking prefetch of [src, src + bytes) into L2 (16-byte aligned, bytes % 16 == 0).
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
-                 : "memory");
 }
 
 // bulk_load with an L2 eviction-priority policy (from make_l2_policy) attached.

@@ -40,7 +40,7 @@ __global__ void embed_rows_kernel(const int* __restrict__ ids, const float* __re
 }
 
 __global__ void ln_bf16_kernel(const float* __restrict__ x, int rows, int d, const float* __restrict__ w,
-                               float w_offset, __nv_bfloat16* __restrict__ out) {
+                               float w_offset, __nv_bfloat16* __restrict__ out, size_t lo_off) {
     pdl_wait();
     pdl_trigger();
     __shared__ float red[32];
@@ -57,7 +57,7 @@ __global__ void ln_bf16_kernel(const float* __restrict__ x, int rows, int d, con
     }
     const float rstd = rsqrtf(block_sum(q, red) / (float)d + 1e-5f);
     for (int i = threadIdx.x; i < d; i += blockDim.x)
-        out[(size_t)r * d + i] = __float2bfloat16_rn((xr[i] - mean) * rstd * (w[i] + w_offset));
+        st_bf16_split(out + (size_t)r * d + i, (xr[i] - mean) * rstd * (w[i] + w_offset), lo_off);
 }
 
 // The same LayerNorm with one warp per row for d % 4 == 0, d <= 32 * 4 * LNW_V4: the row
@@ -68,7 +68,7 @@ constexpr int LNW_ROWS = 8;
 constexpr int LNW_V4 = 8;
 __global__ void __launch_bounds__(LNW_ROWS * 32) ln_bf16_warp_kernel(const float* __restrict__ x, int rows, int d,
                                                                      const float* __restrict__ w, float w_offset,
-                                                                     __nv_bfloat16* __restrict__ out) {
+                                                                     __nv_bfloat16* __restrict__ out, size_t lo_off) {
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x & 31;
@@ -100,14 +100,21 @@ __global__ void __launch_bounds__(LNW_ROWS * 32) ln_bf16_warp_kernel(const float
         const int i = lane + 32 * j;
         if (i < n4) {
             const float4 g = w4[i];
-            const __nv_bfloat162 lo = __floats2bfloat162_rn((v[j].x - mean) * rstd * (g.x + w_offset),
-                                                            (v[j].y - mean) * rstd * (g.y + w_offset));
-            const __nv_bfloat162 hi = __floats2bfloat162_rn((v[j].z - mean) * rstd * (g.z + w_offset),
-                                                            (v[j].w - mean) * rstd * (g.w + w_offset));
+            const float y0 = (v[j].x - mean) * rstd * (g.x + w_offset), y1 = (v[j].y - mean) * rstd * (g.y + w_offset);
+            const float y2 = (v[j].z - mean) * rstd * (g.z + w_offset), y3 = (v[j].w - mean) * rstd * (g.w + w_offset);
+            const __nv_bfloat162 lo = __floats2bfloat162_rn(y0, y1);
+            const __nv_bfloat162 hi = __floats2bfloat162_rn(y2, y3);
             uint2 pk;
             pk.x = *reinterpret_cast<const uint32_t*>(&lo);
             pk.y = *reinterpret_cast<const uint32_t*>(&hi);
             *reinterpret_cast<uint2*>(o2 + 2 * i) = pk;
+            if (lo_off) {  // remainders: the low plane of a split operand
+                const __nv_bfloat162 rl = __floats2bfloat162_rn(y0 - __low2float(lo), y1 - __high2float(lo));
+                const __nv_bfloat162 rh = __floats2bfloat162_rn(y2 - __low2float(hi), y3 - __high2float(hi));
+                pk.x = *reinterpret_cast<const uint32_t*>(&rl);
+                pk.y = *reinterpret_cast<const uint32_t*>(&rh);
+                *reinterpret_cast<uint2*>(o2 + 2 * i + lo_off / 2) = pk;
+            }
         }
     }
 }
@@ -122,7 +129,7 @@ __device__ __forceinline__ float load_kv(const void* base, size_t idx, int f16) 
 // skipped), key t is this step's fp32 K/V.
 __global__ void self_attn_batch_kernel(const float* __restrict__ q, const float* __restrict__ kv_new,
                                        const PagedKv kv, const int* __restrict__ pos, int B, int H, int KVH, int hd,
-                                       float scale, __nv_bfloat16* __restrict__ out) {
+                                       float scale, __nv_bfloat16* __restrict__ out, size_t lo_off) {
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x & 31;
@@ -223,8 +230,8 @@ __global__ void self_attn_batch_kernel(const float* __restrict__ q, const float*
     }
     const int c = 2 * lane;
     if (c < hd) {
-        out[(size_t)b * HD + h * hd + c] = __float2bfloat16_rn(a0 / l);
-        out[(size_t)b * HD + h * hd + c + 1] = __float2bfloat16_rn(a1 / l);
+        st_bf16_split(out + (size_t)b * HD + h * hd + c, a0 / l, lo_off);
+        st_bf16_split(out + (size_t)b * HD + h * hd + c + 1, a1 / l, lo_off);
     }
 }
 
@@ -291,7 +298,7 @@ __global__ void cross_attn_batch_kernel(const float* __restrict__ qc, const floa
 }
 
 __global__ void cross_combine_kernel(const float* __restrict__ part, int B, int H, int hd, int max_chunks,
-                                     __nv_bfloat16* __restrict__ out) {
+                                     __nv_bfloat16* __restrict__ out, size_t lo_off) {
     const int lane = threadIdx.x & 31;
     const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (item >= B * H) return;
@@ -312,7 +319,7 @@ __global__ void cross_combine_kernel(const float* __restrict__ part, int B, int 
             const float mk = base[(size_t)k * (hd + 2)];
             if (mk != -INFINITY) O += base[(size_t)k * (hd + 2) + 2 + e] * expf(mk - M);
         }
-        out[(size_t)b * H * hd + h * hd + e] = __float2bfloat16_rn(O / L);
+        st_bf16_split(out + (size_t)b * H * hd + h * hd + e, O / L, lo_off);
     }
 }
 
@@ -350,7 +357,7 @@ template <int HDT, bool F16>
 __global__ void __launch_bounds__(XS_THREADS) cross_attn_stream_kernel(
     const float* __restrict__ qc, const void* __restrict__ src, const int* __restrict__ frame_off,
     const int* __restrict__ frames, int H, int KVH, int m_cap, int layer, float scale,
-    __nv_bfloat16* __restrict__ out, unsigned* status) {
+    __nv_bfloat16* __restrict__ out, unsigned* status, size_t lo_off) {
     pdl_wait();
     pdl_trigger();
     using S = XsShape<HDT, F16>;
@@ -483,14 +490,14 @@ __global__ void __launch_bounds__(XS_THREADS) cross_attn_stream_kernel(
             L = fmaf(wl[w], f, L);
             O = fmaf(wacc[w][e], f, O);
         }
-        out[(size_t)b * H * HDT + h * HDT + e] = __float2bfloat16_rn(O / L);
+        st_bf16_split(out + (size_t)b * H * HDT + h * HDT + e, O / L, lo_off);
     }
 }
 
 template <int HDT>
 cudaError_t launch_cross_stream(bool f16, const float* qc, const void* src, const int* frame_off, const int* frames,
                                 int B, int H, int KVH, int m_cap, int layer, float scale, __nv_bfloat16* out,
-                                unsigned* status, cudaStream_t s) {
+                                unsigned* status, cudaStream_t s, size_t lo_off) {
     static bool attr_set = false;
     if (!attr_set) {  // both variants at once: the fp16 one is first launched inside a graph capture
         cudaError_t e = cudaFuncSetAttribute(cross_attn_stream_kernel<HDT, true>,
@@ -505,10 +512,10 @@ cudaError_t launch_cross_stream(bool f16, const float* qc, const void* src, cons
     if (f16)
         return launch_kernel(cross_attn_stream_kernel<HDT, true>, dim3(B * H), dim3(XS_THREADS),
                              xs_smem_bytes<HDT, true>(), s, qc, src, frame_off, frames, H, KVH, m_cap, layer, scale,
-                             out, status);
+                             out, status, lo_off);
     return launch_kernel(cross_attn_stream_kernel<HDT, false>, dim3(B * H), dim3(XS_THREADS),
                          xs_smem_bytes<HDT, false>(), s, qc, src, frame_off, frames, H, KVH, m_cap, layer, scale,
-                         out, status);
+                         out, status, lo_off);
 }
 
 // One thread per row b.  Decodes the packed argmax, applies the greedy-loop rules of
@@ -547,30 +554,33 @@ cudaError_t launch_embed_rows(const int* ids, const float* embed, int d, int B, 
 }
 
 cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv_bfloat16* out, cudaStream_t s,
-                          float w_offset) {
+                          float w_offset, size_t lo_off) {
     if (rows <= 0) return cudaSuccess;
     ++launch_counter();
     const bool warp_rows = d % 4 == 0 && d <= 32 * 4 * LNW_V4 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
-                           reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 8 == 0;
+                           reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 8 == 0 &&
+                           lo_off % 4 == 0;
     if (warp_rows)
         return launch_kernel(ln_bf16_warp_kernel, dim3((rows + LNW_ROWS - 1) / LNW_ROWS), dim3(LNW_ROWS * 32), 0, s,
-                             x, rows, d, w, w_offset, out);
-    return launch_kernel(ln_bf16_kernel, dim3(rows), dim3(128), 0, s, x, rows, d, w, w_offset, out);
+                             x, rows, d, w, w_offset, out, lo_off);
+    return launch_kernel(ln_bf16_kernel, dim3(rows), dim3(128), 0, s, x, rows, d, w, w_offset, out, lo_off);
 }
 
 cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const PagedKv& kv, const int* pos, int B,
-                                   int H, int KVH, int hd, float scale, __nv_bfloat16* out, cudaStream_t s) {
+                                   int H, int KVH, int hd, float scale, __nv_bfloat16* out, cudaStream_t s,
+                                   size_t lo_off) {
     if (hd > MAXHD_B || (hd & 7) || !kv.table || kv.page <= 0 || !kv.pool) return cudaErrorInvalidValue;
     ++launch_counter();
     const int items = B * H;
     return launch_kernel(self_attn_batch_kernel, dim3((items + 7) / 8), dim3(256), 0, s, q, kv_new, kv, pos, B, H,
-                         KVH, hd, scale, out);
+                         KVH, hd, scale, out, lo_off);
 }
 
 cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const void* cross_st, int st_f16,
                                     const int* pos, const int* frame_off, const int* frames, int B, int H, int KVH,
                                     int hd, int m_cap, int layer, int max_frames, float scale, float* part,
-                                    __nv_bfloat16* out, int first_step, unsigned* status, cudaStream_t s) {
+                                    __nv_bfloat16* out, int first_step, unsigned* status, cudaStream_t s,
+                                    size_t lo_off) {
     if (hd > MAXHD_B || (hd & 1)) return cudaErrorInvalidValue;
     if (first_step >= 0 && (hd == 32 || hd == 40 || hd == 48 || hd == 64)) {
         // one CTA per (utterance, head); the first decoder call reads the fp32 copy
@@ -579,10 +589,10 @@ cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const
         if ((reinterpret_cast<uintptr_t>(src) & 15) != 0 || !status) return cudaErrorInvalidValue;
         ++launch_counter();
         switch (hd) {
-            case 32: return launch_cross_stream<32>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s);
-            case 40: return launch_cross_stream<40>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s);
-            case 48: return launch_cross_stream<48>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s);
-            default: return launch_cross_stream<64>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s);
+            case 32: return launch_cross_stream<32>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s, lo_off);
+            case 40: return launch_cross_stream<40>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s, lo_off);
+            case 48: return launch_cross_stream<48>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s, lo_off);
+            default: return launch_cross_stream<64>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s, lo_off);
         }
     }
     // generic head_dim: chunk partials + combine, fp32/stored copy chosen on the device
@@ -591,7 +601,7 @@ cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const
     launch_counter() += 2;
     cross_attn_batch_kernel<<<(items + 7) / 8, 256, 0, s>>>(qc, cross32, cross_st, st_f16, pos, frame_off, frames, B,
                                                             H, KVH, hd, m_cap, layer, max_chunks, scale, part);
-    cross_combine_kernel<<<(B * H + 7) / 8, 256, 0, s>>>(part, B, H, hd, max_chunks, out);
+    cross_combine_kernel<<<(B * H + 7) / 8, 256, 0, s>>>(part, B, H, hd, max_chunks, out, lo_off);
     return cudaGetLastError();
 }
 
@@ -642,12 +652,12 @@ namespace {
 // dst row r = src row r (interleave == 0) or, for the SwiGLU fc1, dst row 2j = src row j
 // (value) and dst row 2j+1 = src row j + interleave (gate).
 __global__ void f32_to_bf16_rows_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, int rows,
-                                        int K, int interleave) {
+                                        int K, int interleave, size_t lo_off) {
     const int r = blockIdx.x;
     if (r >= rows) return;
     const int sr = interleave ? ((r & 1) ? interleave + (r >> 1) : (r >> 1)) : r;
     for (int k = threadIdx.x; k < K; k += blockDim.x)
-        dst[(size_t)r * K + k] = __float2bfloat16_rn(src[(size_t)sr * K + k]);
+        st_bf16_split(dst + (size_t)r * K + k, src[(size_t)sr * K + k], lo_off);
 }
 __global__ void interleave_f32_kernel(const float* __restrict__ src, float* __restrict__ dst, int n2, int half) {
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
@@ -656,9 +666,9 @@ __global__ void interleave_f32_kernel(const float* __restrict__ src, float* __re
 }  // namespace
 
 cudaError_t launch_f32_to_bf16_rows(const float* src, __nv_bfloat16* dst, int rows, int K, int interleave,
-                                    cudaStream_t s) {
+                                    cudaStream_t s, size_t lo_off) {
     ++launch_counter();
-    f32_to_bf16_rows_kernel<<<rows, 256, 0, s>>>(src, dst, rows, K, interleave);
+    f32_to_bf16_rows_kernel<<<rows, 256, 0, s>>>(src, dst, rows, K, interleave, lo_off);
     return cudaGetLastError();
 }
 

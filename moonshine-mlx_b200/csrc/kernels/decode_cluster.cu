@@ -95,9 +95,24 @@ constexpr int MAXB = 320;  // blocks per step a CTA's schedule may have (checked
 #ifndef MSB_FC2_MAXR
 #define MSB_FC2_MAXR 1024
 #endif
-#ifndef MSB_PF_AHEAD
-#define MSB_PF_AHEAD 0
+#ifndef MSB_LM_ROWS
+#define MSB_LM_ROWS 32
 #endif
+#ifndef MSB_LN_FUSED
+#define MSB_LN_FUSED 0
+#endif
+
+// Per-warp sums of the values in s and of their squares -> red[0][w], red[1][w] (the
+// LayerNorm statistics of the residual, gathered while it is written; a barrier must follow
+// before they are read).
+__device__ __forceinline__ void warp_stats(float s, float q, float* red) {
+    s = warp_sum(s);
+    q = warp_sum(q);
+    if ((threadIdx.x & 31) == 0) {
+        red[threadIdx.x >> 5] = s;
+        red[NW + (threadIdx.x >> 5)] = q;
+    }
+}
 
 struct SegPlan {
     size_t off;  // floats from the CTA's stream base
@@ -121,7 +136,7 @@ __host__ __device__ inline SegPlan seg_plan(int seg, int layer, const ClusterGeo
         case SEG_CO: return {lw + sg.co, 0, no, row_stride(hd), 1, 64};
         case SEG_FC1: return {lw + sg.fc1, d + 2 * g.gr, 2 * g.gr, sd, 2, mq};
         case SEG_FC2: return {lw + sg.fc2, sg.ro4, d, g.gr, 1, MSB_FC2_MAXR};
-        default: return {(size_t)L * sg.layer, d, nlm, lm_stride<QR>(g, d), 1, QR && g.lm_qbits ? NT : 32};
+        default: return {(size_t)L * sg.layer, d, nlm, lm_stride<QR>(g, d), 1, QR && g.lm_qbits ? NT : MSB_LM_ROWS};
     }
 }
 
@@ -161,9 +176,11 @@ __host__ __device__ inline int blocks_per_step(const ClusterGeom& g, const Segs&
 // whose four pair sums meet by shuffles in fixed order.  Ends with a barrier; returns the
 // cycles spent polling.
 __device__ __forceinline__ long long add_cluster_partials(const unsigned long long* pb, float* xs, int d, int H,
-                                                          unsigned tag, volatile int* failed, unsigned* status) {
+                                                          unsigned tag, volatile int* failed, unsigned* status,
+                                                          float* red) {
     const int tid = threadIdx.x;
     long long cyc = 0;
+    float st1 = 0.f, st2 = 0.f;  // this thread's share of sum(x), sum(x^2) (MSB_LN_FUSED)
     auto timed_out = [&](uint64_t& t0) {
         if (t0 == 0) {
             t0 = globaltimer_ns();
@@ -214,7 +231,14 @@ __device__ __forceinline__ long long add_cluster_partials(const unsigned long lo
         const float pr = (tid & 1) ? o1 + s2 : s2 + o1;  // words 0-3 / 4-7 of the element
         const float o2 = __shfl_xor_sync(FULL, pr, 2);
         const float tot = (tid & 2) ? o2 + pr : pr + o2;
-        if (hasx && (tid & 3) == 0) xs[NT + xi] += tot;
+        if (hasx && (tid & 3) == 0) {
+            const float xv = xs[NT + xi] + tot;
+            xs[NT + xi] = xv;
+            st1 += xv;
+            st2 += xv * xv;
+        }
+        st1 += v;
+        st2 += v * v;
     } else {
         for (int k = tid; k < d; k += NT) {
             unsigned long long v[16];
@@ -237,16 +261,20 @@ __device__ __forceinline__ long long add_cluster_partials(const unsigned long lo
             float a = xs[k];
             for (int q = 0; q < H; ++q) a += __uint_as_float((uint32_t)v[q]);
             xs[k] = a;
+            st1 += a;
+            st2 += a * a;
         }
     }
+    if (MSB_LN_FUSED) warp_stats(st1, st2, red);
     __syncthreads();
     return cyc;
 }
 // The same as one out-of-line copy: the quantized-row kernels (measured faster so; the fp32
 // kernel is faster with the body inlined at its three exchanges per layer).
 __device__ __noinline__ long long add_cluster_partials_call(const unsigned long long* pb, float* xs, int d, int H,
-                                                            unsigned tag, volatile int* failed, unsigned* status) {
-    return add_cluster_partials(pb, xs, d, H, tag, failed, status);
+                                                            unsigned tag, volatile int* failed, unsigned* status,
+                                                            float* red) {
+    return add_cluster_partials(pb, xs, d, H, tag, failed, status, red);
 }
 
 // xl = LN(xs) * wln over d inputs (every warp computes the statistics itself); for rows
@@ -266,6 +294,28 @@ __device__ __noinline__ void ln_vector(const float* xs, const float* wln, float*
     }
     const float rstd = rsqrtf(warp_sum(q) / (float)d + 1e-5f);
     for (int k = tid; k < d; k += NT) {
+        const float v = (xs[k] - mean) * rstd * wln[k];
+        xl[k] = v;
+        if constexpr (QB != 0)
+            if (qb) quant_input<QB>(v, k, xq, d);
+    }
+    __syncthreads();
+}
+
+// The same from statistics gathered with the residual (red: per-warp sums of x and x^2, see
+// warp_stats): mean = sum / d, variance = sum(x^2) / d - mean^2.  Ends with a barrier.
+template <int QB>
+__device__ __noinline__ void ln_apply(const float* xs, const float* wln, float* xl, int d, float* xq, int qb,
+                                      const float* red) {
+    float s = 0.f, q = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        s += red[w];
+        q += red[NW + w];
+    }
+    const float mean = s / (float)d;
+    const float rstd = rsqrtf(fmaxf(q / (float)d - mean * mean, 0.f) + 1e-5f);
+    for (int k = threadIdx.x; k < d; k += NT) {
         const float v = (xs[k] - mean) * rstd * wln[k];
         xl[k] = v;
         if constexpr (QB != 0)
@@ -381,12 +431,6 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
     auto issue_next = [&]() {
         if (n_iss >= n_total || s_failed) return;
         const BlockEnt e = n_iss < nb0 ? s_tab[0][n_iss] : s_tab[1][(n_iss - nb0) % nb1];
-        if (MSB_PF_AHEAD > 0 && n_iss + MSB_PF_AHEAD < n_total) {
-            const uint32_t f = n_iss + MSB_PF_AHEAD;
-            const BlockEnt pe = f < nb0 ? s_tab[0][f] : s_tab[1][(f - nb0) % nb1];
-            bulk_prefetch_l2(pe.s0, pe.b0);
-            if (pe.b1) bulk_prefetch_l2(pe.s1, pe.b1);
-        }
         const int slot = n_iss % NSLOT;
         mbar_expect_tx(&full[slot], e.b0 + e.b1);
         unsigned char* dst = ring + (size_t)slot * slot_bytes;
@@ -489,14 +533,18 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
     // xl = LN(xs) * wln (wln in shared memory); for rows quantized to qb bits also the
     // vector block_gemv_q reads: xl pre-scaled per input, then sums over each 16 inputs
     // (d % 64 == 0 there, so every iteration below covers whole warps)
-    auto layer_norm = [&](const float* wln, int qb) { ln_vector<QB>(xs, wln, xl, d, xq_s, qb); };
+    __shared__ float s_red[2 * NW];  // LayerNorm statistics of xs (MSB_LN_FUSED)
+    auto layer_norm = [&](const float* wln, int qb) {
+        if (MSB_LN_FUSED) ln_apply<QB>(xs, wln, xl, d, xq_s, qb, s_red);
+        else ln_vector<QB>(xs, wln, xl, d, xq_s, qb);
+    };
     int par = 0;
     // xs += sum over clusters (fixed order) of partial[par][.] of exchange `epoch`
     auto add_partials = [&]() {
         const unsigned long long* pb = gm.part + (size_t)par * H * d;
         long long cy;
-        if constexpr (QR) cy = add_cluster_partials_call(pb, xs, d, H, epoch, &s_failed, p.status);
-        else cy = add_cluster_partials(pb, xs, d, H, epoch, &s_failed, p.status);
+        if constexpr (QR) cy = add_cluster_partials_call(pb, xs, d, H, epoch, &s_failed, p.status, s_red);
+        else cy = add_cluster_partials(pb, xs, d, H, epoch, &s_failed, p.status, s_red);
         if (tr0) cyc_poll += cy;
         par ^= 1;
     };
@@ -577,7 +625,16 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
     for (; step < p.n_steps && !stop; ++step) {
         const int t = step;
         stamp();
-        for (int k = tid; k < d; k += NT) xs[k] = __ldg(p.embed + (size_t)tok * d + k);
+        {
+            float e1 = 0.f, e2 = 0.f;
+            for (int k = tid; k < d; k += NT) {
+                const float v = __ldg(p.embed + (size_t)tok * d + k);
+                xs[k] = v;
+                e1 += v;
+                e2 += v * v;
+            }
+            if (MSB_LN_FUSED) warp_stats(e1, e2, s_red);
+        }
         __syncthreads();
         for (int l = 0; l < L; ++l) {
             // ---- self-K/V prefetch of this CTA's cached keys [j0, min(j1, t))

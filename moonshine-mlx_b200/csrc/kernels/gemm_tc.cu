@@ -37,7 +37,6 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;         // bf16: 128 bytes = one 128B-swizzle row
-constexpr int STAGES = 4;
 constexpr int TC_THREADS = 128;
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
@@ -95,12 +94,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <int BN>
+// SP (split): A and B each come as a bf16 high plane and a bf16 low plane (x = hi + lo to
+// ~2^-17 relative) and every MMA step accumulates hi.hi + hi.lo + lo.hi, which gives fp32
+// checkpoints fp32-level products on the bf16 tensor pipe; 3 stages of both planes.
+template <int BN, bool SP>
 struct alignas(1024) TcSmem {
-    __nv_bfloat16 a[STAGES][BM * BK];
-    __nv_bfloat16 b[STAGES][BN * BK];
-    uint64_t full[STAGES];
-    uint64_t empty[STAGES];
+    static constexpr int ST = SP ? 3 : 4;  // ring stages
+    static constexpr int P = SP ? 2 : 1;   // planes per operand
+    __nv_bfloat16 a[ST][P][BM * BK];
+    __nv_bfloat16 b[ST][P][BN * BK];
+    uint64_t full[ST];
+    uint64_t empty[ST];
     uint64_t done;
     uint32_t tmem_base;
 };
@@ -121,6 +125,19 @@ __device__ __forceinline__ void st_bf16x4(__nv_bfloat16* p, float4 v) {
     u.x = *reinterpret_cast<uint32_t*>(&lo);
     u.y = *reinterpret_cast<uint32_t*>(&hi);
     *reinterpret_cast<uint2*>(p) = u;
+}
+
+// bf16 high part of four values, and (lo_off != 0) the bf16 of their remainders lo_off
+// elements further on
+__device__ __forceinline__ void st_bf16x4_split(__nv_bfloat16* p, float4 v, size_t lo_off) {
+    st_bf16x4(p, v);
+    if (lo_off) {
+        const float4 r = make_float4(v.x - __bfloat162float(__float2bfloat16_rn(v.x)),
+                                     v.y - __bfloat162float(__float2bfloat16_rn(v.y)),
+                                     v.z - __bfloat162float(__float2bfloat16_rn(v.z)),
+                                     v.w - __bfloat162float(__float2bfloat16_rn(v.w)));
+        st_bf16x4(p + lo_off, r);
+    }
 }
 
 __device__ __forceinline__ void st_f16x4(__half* p, float4 v) {
@@ -219,7 +236,7 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* 
                     if (ep.kv_out16) st_f16x4(reinterpret_cast<__half*>(ep.kv_out16) + idx, v);
                 } else {
                     if (ep.out) *reinterpret_cast<float4*>(ep.out + (size_t)m * ep.ldc + n) = v;
-                    if (g.out_bf16) st_bf16x4(g.out_bf16 + (size_t)m * g.ldc_bf16 + n, v);
+                    if (g.out_bf16) st_bf16x4_split(g.out_bf16 + (size_t)m * g.ldc_bf16 + n, v, g.bf16_lo_off);
                 }
             }
         } else if constexpr (MODE == TC_EPI_ACCUM) {
@@ -230,8 +247,13 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* 
         } else if constexpr (MODE == TC_EPI_SWIGLU) {
             if (ok) {  // columns (value, gate, value, gate) -> two outputs
                 v = add4(v, bias);
-                const __nv_bfloat162 o = __floats2bfloat162_rn(v.x * silu(v.y), v.z * silu(v.w));
-                *reinterpret_cast<__nv_bfloat162*>(g.out_bf16 + (size_t)m * g.ldc_bf16 + (n >> 1)) = o;
+                const float o0 = v.x * silu(v.y), o1 = v.z * silu(v.w);
+                const __nv_bfloat162 o = __floats2bfloat162_rn(o0, o1);
+                __nv_bfloat16* dst = g.out_bf16 + (size_t)m * g.ldc_bf16 + (n >> 1);
+                *reinterpret_cast<__nv_bfloat162*>(dst) = o;
+                if (g.bf16_lo_off)
+                    *reinterpret_cast<__nv_bfloat162*>(dst + g.bf16_lo_off) =
+                        __floats2bfloat162_rn(o0 - __low2float(o), o1 - __high2float(o));
             }
         } else if constexpr (MODE == TC_EPI_ROPE_KV) {
             if (ok) {
@@ -293,12 +315,15 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* 
     }
 }
 
-template <int BN, int MODE>
+template <int BN, int MODE, bool SP>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+               const __grid_constant__ CUtensorMap tmap_a_lo, const __grid_constant__ CUtensorMap tmap_b_lo,
                TcGemmArgs g) {
+    using Sm = TcSmem<BN, SP>;
+    constexpr int STAGES = Sm::ST;
     extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
-    TcSmem<BN>& s = *reinterpret_cast<TcSmem<BN>*>(
+    Sm& s = *reinterpret_cast<Sm*>(
         (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
@@ -307,7 +332,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     const int per_split = (nkb_all + g.splits - 1) / g.splits;
     const int kb_lo = blockIdx.z * per_split;
     const int nkb = max(0, min(nkb_all, kb_lo + per_split) - kb_lo);
-    constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
+    constexpr uint32_t A_BYTES = BM * BK * 2 * Sm::P, B_BYTES = BN * BK * 2 * Sm::P;
     __shared__ int s_fail;
 
     if (threadIdx.x == 0) {
@@ -339,7 +364,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             const int tap = gkb / g.kb_per_tap;
             const int k0 = (gkb - tap * g.kb_per_tap) * BK;
             mbar_expect_tx(&s.full[kb], A_BYTES + B_BYTES);
-            tma_load_2d(s.b[kb], &tmap_b, &s.full[kb], tap * g.k_per_tap + k0, n0);
+            tma_load_2d(s.b[kb][0], &tmap_b, &s.full[kb], tap * g.k_per_tap + k0, n0);
+            if constexpr (SP) tma_load_2d(s.b[kb][1], &tmap_b_lo, &s.full[kb], tap * g.k_per_tap + k0, n0);
         }
     pdl_wait();
     pdl_trigger();
@@ -358,9 +384,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             const int k0 = (gkb - tap * g.kb_per_tap) * BK;
             if (kb >= pre) {
                 mbar_expect_tx(&s.full[st], A_BYTES + B_BYTES);
-                tma_load_2d(s.b[st], &tmap_b, &s.full[st], tap * g.k_per_tap + k0, n0);
+                tma_load_2d(s.b[st][0], &tmap_b, &s.full[st], tap * g.k_per_tap + k0, n0);
+                if constexpr (SP) tma_load_2d(s.b[st][1], &tmap_b_lo, &s.full[st], tap * g.k_per_tap + k0, n0);
             }
-            tma_load_3d(s.a[st], &tmap_a, &s.full[st], k0, g.tap_y[tap], m0 + g.tap_z[tap]);
+            tma_load_3d(s.a[st][0], &tmap_a, &s.full[st], k0, g.tap_y[tap], m0 + g.tap_z[tap]);
+            if constexpr (SP) tma_load_3d(s.a[st][1], &tmap_a_lo, &s.full[st], k0, g.tap_y[tap], m0 + g.tap_z[tap]);
             issued = kb + 1;
         }
     } else if (warp == 1 && lane == 0) {
@@ -373,11 +401,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                 break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t a_addr = smem_u32(s.a[st]), b_addr = smem_u32(s.b[st]);
+            const uint32_t a_addr = smem_u32(s.a[st][0]), b_addr = smem_u32(s.b[st][0]);
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k) {  // 16 bf16 = 32 bytes per MMA along K
                 mma_bf16(tmem, smem_desc_sw128(a_addr + k * 32), smem_desc_sw128(b_addr + k * 32), idesc,
                          (kb > 0 || k > 0) ? 1u : 0u);
+                if constexpr (SP) {  // + hi.lo + lo.hi (lo.lo is below fp32 rounding of the sum)
+                    const uint32_t al = smem_u32(s.a[st][Sm::P - 1]), bl = smem_u32(s.b[st][Sm::P - 1]);
+                    mma_bf16(tmem, smem_desc_sw128(a_addr + k * 32), smem_desc_sw128(bl + k * 32), idesc, 1u);
+                    mma_bf16(tmem, smem_desc_sw128(al + k * 32), smem_desc_sw128(b_addr + k * 32), idesc, 1u);
+                }
             }
             mma_commit(&s.empty[st]);
         }
@@ -393,7 +426,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     ok = __syncthreads_and(ok && !s_fail);      // uniform: the epilogue crosses warps
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     constexpr int LDS = tile_ld<BN>();
-    float* tile = reinterpret_cast<float*>(&s.a[0][0]);
+    float* tile = reinterpret_cast<float*>(&s.a[0][0][0]);
     static_assert(sizeof(float) * BM * LDS <= sizeof(s.a) + sizeof(s.b), "epilogue tile must fit the stages");
     const int rows = min(BM, g.M - m0);
     if (warp * 32 < rows) {  // warp-uniform: lanes of rows past M hold nothing
@@ -495,32 +528,34 @@ bool tc_make_map_2d(CUtensorMap* map, const void* base, uint64_t dim_k, uint64_t
 namespace {
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
-template <int BN, int MODE>
-cudaError_t launch_tc(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcGemmArgs& g, cudaStream_t stream) {
-    const size_t smem = sizeof(TcSmem<BN>) + 1024;
+template <int BN, int MODE, bool SP>
+cudaError_t launch_tc(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_a_lo,
+                      const CUtensorMap& map_b_lo, const TcGemmArgs& g, cudaStream_t stream) {
+    const size_t smem = sizeof(TcSmem<BN, SP>) + 1024;
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e =
-            cudaFuncSetAttribute(gemm_tc_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, MODE, SP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
     const dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.splits);
     if (g.splits > 1)
-        return launch_kernel_cluster_z(gemm_tc_kernel<BN, MODE>, grid, dim3(TC_THREADS), smem, stream, g.splits,
-                                       map_a, map_b, g);
-    return launch_kernel(gemm_tc_kernel<BN, MODE>, grid, dim3(TC_THREADS), smem, stream, map_a, map_b, g);
+        return launch_kernel_cluster_z(gemm_tc_kernel<BN, MODE, SP>, grid, dim3(TC_THREADS), smem, stream, g.splits,
+                                       map_a, map_b, map_a_lo, map_b_lo, g);
+    return launch_kernel(gemm_tc_kernel<BN, MODE, SP>, grid, dim3(TC_THREADS), smem, stream, map_a, map_b, map_a_lo,
+                         map_b_lo, g);
 }
 
-template <int BN>
-cudaError_t launch_tc_mode(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcGemmArgs& g,
-                           cudaStream_t stream) {
+template <int BN, bool SP>
+cudaError_t launch_tc_mode(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_a_lo,
+                           const CUtensorMap& map_b_lo, const TcGemmArgs& g, cudaStream_t stream) {
     switch (g.mode) {
-        case TC_EPI_STD: return launch_tc<BN, TC_EPI_STD>(map_a, map_b, g, stream);
-        case TC_EPI_ROPE_KV: return launch_tc<BN, TC_EPI_ROPE_KV>(map_a, map_b, g, stream);
-        case TC_EPI_SWIGLU: return launch_tc<BN, TC_EPI_SWIGLU>(map_a, map_b, g, stream);
-        case TC_EPI_ARGMAX: return launch_tc<BN, TC_EPI_ARGMAX>(map_a, map_b, g, stream);
-        case TC_EPI_ACCUM: return launch_tc<BN, TC_EPI_ACCUM>(map_a, map_b, g, stream);
+        case TC_EPI_STD: return launch_tc<BN, TC_EPI_STD, SP>(map_a, map_b, map_a_lo, map_b_lo, g, stream);
+        case TC_EPI_ROPE_KV: return launch_tc<BN, TC_EPI_ROPE_KV, SP>(map_a, map_b, map_a_lo, map_b_lo, g, stream);
+        case TC_EPI_SWIGLU: return launch_tc<BN, TC_EPI_SWIGLU, SP>(map_a, map_b, map_a_lo, map_b_lo, g, stream);
+        case TC_EPI_ARGMAX: return launch_tc<BN, TC_EPI_ARGMAX, SP>(map_a, map_b, map_a_lo, map_b_lo, g, stream);
+        case TC_EPI_ACCUM: return launch_tc<BN, TC_EPI_ACCUM, SP>(map_a, map_b, map_a_lo, map_b_lo, g, stream);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -558,16 +593,27 @@ bool epilogue_layout_ok(const TcGemmArgs& g) {
 }
 }  // namespace
 
-cudaError_t launch_gemm_tc(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcGemmArgs& g, int bn,
-                           cudaStream_t stream) {
+cudaError_t launch_gemm_tc_split(const CUtensorMap& map_a, const CUtensorMap* map_a_lo, const CUtensorMap& map_b,
+                                 const CUtensorMap* map_b_lo, const TcGemmArgs& g, int bn, cudaStream_t stream) {
     if (g.M <= 0 || g.N <= 0) return cudaSuccess;
     if (g.taps < 1 || g.taps > 8 || g.kb_per_tap < 1 || !g.status) return cudaErrorInvalidValue;
     if (g.splits < 1 || g.splits > TC_MAX_SPLITS || g.splits > g.taps * g.kb_per_tap) return cudaErrorInvalidValue;
-    if (!epilogue_layout_ok(g)) return cudaErrorInvalidValue;
+    if ((map_a_lo == nullptr) != (map_b_lo == nullptr)) return cudaErrorInvalidValue;
+    if (!epilogue_layout_ok(g) || (g.bf16_lo_off % 4)) return cudaErrorInvalidValue;
     ++launch_counter();
-    if (bn == 128) return launch_tc_mode<128>(map_a, map_b, g, stream);
-    if (bn == 64) return launch_tc_mode<64>(map_a, map_b, g, stream);
+    if (map_a_lo) {
+        if (bn == 128) return launch_tc_mode<128, true>(map_a, map_b, *map_a_lo, *map_b_lo, g, stream);
+        if (bn == 64) return launch_tc_mode<64, true>(map_a, map_b, *map_a_lo, *map_b_lo, g, stream);
+        return cudaErrorInvalidValue;
+    }
+    if (bn == 128) return launch_tc_mode<128, false>(map_a, map_b, map_a, map_b, g, stream);
+    if (bn == 64) return launch_tc_mode<64, false>(map_a, map_b, map_a, map_b, g, stream);
     return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemm_tc(const CUtensorMap& map_a, const CUtensorMap& map_b, const TcGemmArgs& g, int bn,
+                           cudaStream_t stream) {
+    return launch_gemm_tc_split(map_a, nullptr, map_b, nullptr, g, bn, stream);
 }
 
 }  // namespace msb

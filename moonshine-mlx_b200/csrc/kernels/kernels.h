@@ -137,6 +137,8 @@ struct TcGemmArgs {
     GemmEpilogue ep;                      // fp32 outputs / scatter (as the fp32 GEMM)
     __nv_bfloat16* out_bf16 = nullptr;    // optional bf16 copy of the output [M, ldc_bf16]
     int ldc_bf16 = 0;
+    size_t bf16_lo_off = 0;               // != 0: out_bf16 (STD, SWIGLU) also gets the bf16 of the
+                                          // remainder v - bf16(v) this many elements further on
     TcRopeKv rope;
     unsigned long long* argmax = nullptr; // [M] packed (ordered value, ~column) maxima
     float inv_temp = 0.f;                 // ARGMAX: 0 greedy, else maxima of logit * inv_temp + Gumbel
@@ -155,6 +157,12 @@ bool tc_make_map_2d(CUtensorMap_st* map, const void* base, uint64_t dim_k, uint6
                     uint32_t box_rows);
 cudaError_t launch_gemm_tc(const CUtensorMap_st& map_a, const CUtensorMap_st& map_b, const TcGemmArgs& g, int bn,
                            cudaStream_t stream);
+// The same with split operands (both lo maps set): A = A_hi + A_lo and B = B_hi + B_lo as bf16
+// planes, accumulated as A_hi B_hi + A_hi B_lo + A_lo B_hi (about fp32 accuracy: each operand
+// is kept to ~2^-17 relative).  With both lo maps null it is launch_gemm_tc.
+cudaError_t launch_gemm_tc_split(const CUtensorMap_st& map_a, const CUtensorMap_st* map_a_lo,
+                                 const CUtensorMap_st& map_b, const CUtensorMap_st* map_b_lo, const TcGemmArgs& g,
+                                 int bn, cudaStream_t stream);
 
 // ---------------------------------------------------------------- encoder
 // Row LayerNorm (biased variance): out = (x-mean)/sqrt(var+eps) * (w + w_offset)
@@ -272,19 +280,23 @@ struct DecodeParams {
 // ---------------------------------------------------------------- batched decode step
 cudaError_t launch_embed_rows(const int* ids, const float* embed, int d, int B, int V, float* x, unsigned* status,
                               cudaStream_t s);
+// The bf16 outputs below take an optional lo_off: != 0 also writes the low plane of a split
+// operand (bf16 of v - bf16(v)) lo_off elements after each value.
 cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv_bfloat16* out, cudaStream_t s,
-                          float w_offset = 0.f);
+                          float w_offset = 0.f, size_t lo_off = 0);
 cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const PagedKv& kv, const int* pos, int B,
-                                   int H, int KVH, int hd, float scale, __nv_bfloat16* out, cudaStream_t s);
+                                   int H, int KVH, int hd, float scale, __nv_bfloat16* out, cudaStream_t s,
+                                   size_t lo_off = 0);
 cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const void* cross_st, int st_f16,
                                     const int* pos, const int* frame_off, const int* frames, int B, int H, int KVH,
                                     int hd, int m_cap, int layer, int max_frames, float scale, float* part,
-                                    __nv_bfloat16* out, int first_step, unsigned* status, cudaStream_t s);
+                                    __nv_bfloat16* out, int first_step, unsigned* status, cudaStream_t s,
+                                    size_t lo_off = 0);
 cudaError_t launch_step_finalize(unsigned long long* amax, int B, int* pos, int* next_ids, int* ids_out, int t_cap,
                                  int* counts, const int* limits, int* done, int* hit_eos, int eos, int forced,
                                  cudaStream_t s);
 cudaError_t launch_f32_to_bf16_rows(const float* src, __nv_bfloat16* dst, int rows, int K, int interleave,
-                                    cudaStream_t s);
+                                    cudaStream_t s, size_t lo_off = 0);
 cudaError_t launch_interleave_f32(const float* src, float* dst, int n2, int half, cudaStream_t s);
 size_t cross_batch_part_floats(int B, int H, int hd, int max_frames);
 // Per-row cross K/V ([segs][mcap[b]][hd] at src32[b] / src16[b], device pointer arrays) into

@@ -63,34 +63,34 @@ void BatchEngine::ensure_weights() {
     const Config& c = m.cfg;
     const int d = c.hidden, HD = c.heads * c.head_dim, KVD = c.kv_heads * c.head_dim, I = c.inter;
     cudaStream_t s = m.stream;
+    // fp32 checkpoints keep fp32-level GEMM products: every weight and GEMM input as a bf16
+    // high plane plus a bf16 low plane (split operands); bf16 / f16 checkpoints, or bf16 on
+    // request, use one bf16 plane
+    split = !m.enc_bf16;
+    // bf16 copy of src [rows, K] (rows interleaved value/gate when `il`), its weight map and,
+    // when split, the low plane right behind it with its own map
+    auto weight = [&](const float* src, int rows, int K, int il, int bn, CUtensorMap* hi, CUtensorMap* lo) {
+        const size_t n = (size_t)rows * K;
+        __nv_bfloat16* w = alloc<__nv_bfloat16>(split ? 2 * n : n);
+        MSB_CUDA(launch_f32_to_bf16_rows(src, w, rows, K, il, s, split ? n : 0));
+        make_b_map(hi, w, rows, K, bn);
+        if (split) make_b_map(lo, w + n, rows, K, bn);
+        return w;
+    };
     layers.resize(c.layers);
     for (int l = 0; l < c.layers; ++l) {
         const DecodeLayerW& W = m.dec[l];
         LayerB& B = layers[l];
-        B.wqkv = alloc<__nv_bfloat16>((size_t)(HD + 2 * KVD) * d);
-        B.wo = alloc<__nv_bfloat16>((size_t)d * HD);
-        B.wcq = alloc<__nv_bfloat16>((size_t)HD * d);
-        B.wco = alloc<__nv_bfloat16>((size_t)d * HD);
-        B.w1i = alloc<__nv_bfloat16>((size_t)2 * I * d);
-        B.w2 = alloc<__nv_bfloat16>((size_t)d * I);
+        B.wqkv = weight(W.wqkv, HD + 2 * KVD, d, 0, kBnNarrow, &B.m_qkv, &B.m_qkv_lo);
+        B.wo = weight(W.wo, d, HD, 0, kBnWide, &B.m_o, &B.m_o_lo);
+        B.wcq = weight(W.wcq, HD, d, 0, kBnNarrow, &B.m_cq, &B.m_cq_lo);
+        B.wco = weight(W.wco, d, HD, 0, kBnWide, &B.m_co, &B.m_co_lo);
+        B.w1i = weight(W.w1, 2 * I, d, I, kBnWide, &B.m_w1, &B.m_w1_lo);
+        B.w2 = weight(W.w2, d, I, 0, kBnWide, &B.m_w2, &B.m_w2_lo);
         B.b1i = alloc<float>((size_t)2 * I);
-        MSB_CUDA(launch_f32_to_bf16_rows(W.wqkv, B.wqkv, HD + 2 * KVD, d, 0, s));
-        MSB_CUDA(launch_f32_to_bf16_rows(W.wo, B.wo, d, HD, 0, s));
-        MSB_CUDA(launch_f32_to_bf16_rows(W.wcq, B.wcq, HD, d, 0, s));
-        MSB_CUDA(launch_f32_to_bf16_rows(W.wco, B.wco, d, HD, 0, s));
-        MSB_CUDA(launch_f32_to_bf16_rows(W.w1, B.w1i, 2 * I, d, I, s));
-        MSB_CUDA(launch_f32_to_bf16_rows(W.w2, B.w2, d, I, 0, s));
         MSB_CUDA(launch_interleave_f32(W.b1, B.b1i, 2 * I, I, s));
-        make_b_map(&B.m_qkv, B.wqkv, HD + 2 * KVD, d, kBnNarrow);
-        make_b_map(&B.m_o, B.wo, d, HD, kBnWide);
-        make_b_map(&B.m_cq, B.wcq, HD, d, kBnNarrow);
-        make_b_map(&B.m_co, B.wco, d, HD, kBnWide);
-        make_b_map(&B.m_w1, B.w1i, 2 * I, d, kBnWide);
-        make_b_map(&B.m_w2, B.w2, d, I, kBnWide);
     }
-    lm = alloc<__nv_bfloat16>((size_t)c.vocab * d);
-    MSB_CUDA(launch_f32_to_bf16_rows(m.lm_head, lm, c.vocab, d, 0, s));
-    make_b_map(&m_lm, lm, c.vocab, d, kBnWide);
+    lm = weight(m.lm_head, c.vocab, d, 0, kBnWide, &m_lm, &m_lm_lo);
     MSB_CUDA(cudaStreamSynchronize(s));
     weights_ready = true;
 }
@@ -100,13 +100,14 @@ void BatchEngine::ensure_ws(int B, int T, int Mtot, int maxM) {
     const int d = c.hidden, HD = c.heads * c.head_dim, KVD = c.kv_heads * c.head_dim, I = c.inter;
     const size_t kvsz = m.kv_f16 ? 2 : 4;
     bool remap = false;
+    const size_t P = split ? 2 : 1;  // bf16 planes of the GEMM inputs
     if (B > Bc) {
         Bc = B;
         remap = true;
         x.ensure((size_t)Bc * d * 4);
-        hb.ensure((size_t)Bc * d * 2);
-        attn.ensure((size_t)Bc * HD * 2);
-        g.ensure((size_t)Bc * I * 2);
+        hb.ensure((size_t)Bc * d * 2 * P);
+        attn.ensure((size_t)Bc * HD * 2 * P);
+        g.ensure((size_t)Bc * I * 2 * P);
         q.ensure((size_t)Bc * HD * 4);
         qc.ensure((size_t)Bc * HD * 4);
         kvnew.ensure((size_t)Bc * 2 * KVD * 4);
@@ -141,6 +142,11 @@ void BatchEngine::ensure_ws(int B, int T, int Mtot, int maxM) {
         make_a_map(&a_hb, hb.as<__nv_bfloat16>(), Bc, d);
         make_a_map(&a_attn, attn.as<__nv_bfloat16>(), Bc, HD);
         make_a_map(&a_g, g.as<__nv_bfloat16>(), Bc, I);
+        if (split) {
+            make_a_map(&a_hb_lo, hb.as<__nv_bfloat16>() + (size_t)Bc * d, Bc, d);
+            make_a_map(&a_attn_lo, attn.as<__nv_bfloat16>() + (size_t)Bc * HD, Bc, HD);
+            make_a_map(&a_g_lo, g.as<__nv_bfloat16>() + (size_t)Bc * I, Bc, I);
+        }
     }
 }
 
@@ -169,7 +175,8 @@ void BatchEngine::assign_pages(int B, int T, const std::vector<int>& limits) {
     MSB_CUDA(cudaStreamSynchronize(m.stream));
 }
 
-void BatchEngine::gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& ga, int K, int bn) {
+void BatchEngine::gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& ga, int K, int bn,
+                       const CUtensorMap* a_lo, const CUtensorMap* b_lo) {
     ga.taps = 1;
     ga.kb_per_tap = (K + 63) / 64;
     ga.k_per_tap = K;
@@ -178,7 +185,7 @@ void BatchEngine::gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& g
     // the SMs; every split keeps at least one k-block
     const int tiles = ((ga.N + bn - 1) / bn) * ((ga.M + 127) / 128);
 #ifndef MSB_SPLIT_POLICY
-#define MSB_SPLIT_POLICY 2
+#define MSB_SPLIT_POLICY 1
 #endif
     int cap_s = TC_MAX_SPLITS;
     if (MSB_SPLIT_POLICY == 2 && ga.mode != TC_EPI_ACCUM) cap_s = 1;
@@ -186,7 +193,7 @@ void BatchEngine::gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& g
     int sp = std::max(1, std::min({cap_s, ga.kb_per_tap, m.num_sms / std::max(tiles, 1)}));
     const int per = (ga.kb_per_tap + sp - 1) / sp;
     ga.splits = (ga.kb_per_tap + per - 1) / per;
-    MSB_CUDA(launch_gemm_tc(a, b, ga, bn, m.stream));
+    MSB_CUDA(launch_gemm_tc_split(a, a_lo, b, b_lo, ga, bn, m.stream));
 }
 
 namespace {
@@ -209,6 +216,13 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
     cudaStream_t s = m.stream;
     const int* posp = pos.as<int>();
     float* X = x.as<float>();
+    // split operands: low planes of the GEMM inputs (lo_* element offsets) and their maps
+    const size_t lo_hb = split ? (size_t)Bc * d : 0, lo_attn = split ? (size_t)Bc * HD : 0;
+    const size_t lo_g = split ? (size_t)Bc * I : 0;
+    const CUtensorMap* hb_lo = split ? &a_hb_lo : nullptr;
+    const CUtensorMap* attn_lo = split ? &a_attn_lo : nullptr;
+    const CUtensorMap* g_lo = split ? &a_g_lo : nullptr;
+    auto wlo = [&](const CUtensorMap& mlo) { return split ? &mlo : nullptr; };
     MSB_CUDA(launch_embed_rows(next_ids.as<int>(), m.embed, d, B, c.vocab, X, status.as<unsigned>(), s));
     for (int l = 0; l < c.layers; ++l) {
         const DecodeLayerW& W = m.dec[l];
@@ -222,7 +236,7 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
         pk.layer_off = (long long)l * 2 * KVD * kKvPage;
         pk.kv_f16 = m.kv_f16 ? 1 : 0;
         // self-attention block
-        MSB_CUDA(launch_ln_bf16(X, B, d, W.ln1, hb.as<__nv_bfloat16>(), s));
+        MSB_CUDA(launch_ln_bf16(X, B, d, W.ln1, hb.as<__nv_bfloat16>(), s, 0.f, lo_hb));
         {
             TcGemmArgs ga;
             ga.M = B;
@@ -238,10 +252,10 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
             ga.rope.q = q.as<float>();
             ga.rope.kv_new = kvnew.as<float>();
             ga.rope.kv = pk;
-            gemm(a_hb, L.m_qkv, ga, d, kBnNarrow);
+            gemm(a_hb, L.m_qkv, ga, d, kBnNarrow, hb_lo, wlo(L.m_qkv_lo));
         }
         MSB_CUDA(launch_self_attn_batch(q.as<float>(), kvnew.as<float>(), pk, posp, B, H, KVH, hd, scale,
-                                        attn.as<__nv_bfloat16>(), s));
+                                        attn.as<__nv_bfloat16>(), s, lo_attn));
         {
             TcGemmArgs ga;
             ga.M = B;
@@ -249,22 +263,22 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
             ga.mode = TC_EPI_ACCUM;
             ga.ep.out = X;
             ga.ep.ldc = d;
-            gemm(a_attn, L.m_o, ga, HD, kBnWide);
+            gemm(a_attn, L.m_o, ga, HD, kBnWide, attn_lo, wlo(L.m_o_lo));
         }
         // cross-attention block
-        MSB_CUDA(launch_ln_bf16(X, B, d, W.ln2, hb.as<__nv_bfloat16>(), s));
+        MSB_CUDA(launch_ln_bf16(X, B, d, W.ln2, hb.as<__nv_bfloat16>(), s, 0.f, lo_hb));
         {
             TcGemmArgs ga;
             ga.M = B;
             ga.N = HD;
             ga.ep.out = qc.as<float>();
             ga.ep.ldc = HD;
-            gemm(a_hb, L.m_cq, ga, d, kBnNarrow);
+            gemm(a_hb, L.m_cq, ga, d, kBnNarrow, hb_lo, wlo(L.m_cq_lo));
         }
         MSB_CUDA(launch_cross_attn_batch(qc.as<float>(), cross32.as<float>(), m.kv_f16 ? cross16.p : cross32.p,
                                          m.kv_f16 ? 1 : 0, posp, frame_off.as<int>(), frames.as<int>(), B, H, KVH,
                                          hd, Mc, l, max_frames, scale, part.as<float>(), attn.as<__nv_bfloat16>(),
-                                         first ? 1 : 0, status.as<unsigned>(), s));
+                                         first ? 1 : 0, status.as<unsigned>(), s, lo_attn));
         {
             TcGemmArgs ga;
             ga.M = B;
@@ -272,10 +286,10 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
             ga.mode = TC_EPI_ACCUM;
             ga.ep.out = X;
             ga.ep.ldc = d;
-            gemm(a_attn, L.m_co, ga, HD, kBnWide);
+            gemm(a_attn, L.m_co, ga, HD, kBnWide, attn_lo, wlo(L.m_co_lo));
         }
         // SwiGLU MLP
-        MSB_CUDA(launch_ln_bf16(X, B, d, W.ln3, hb.as<__nv_bfloat16>(), s));
+        MSB_CUDA(launch_ln_bf16(X, B, d, W.ln3, hb.as<__nv_bfloat16>(), s, 0.f, lo_hb));
         {
             TcGemmArgs ga;
             ga.M = B;
@@ -284,7 +298,8 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
             ga.ep.bias = L.b1i;
             ga.out_bf16 = g.as<__nv_bfloat16>();
             ga.ldc_bf16 = I;
-            gemm(a_hb, L.m_w1, ga, d, kBnWide);
+            ga.bf16_lo_off = lo_g;
+            gemm(a_hb, L.m_w1, ga, d, kBnWide, hb_lo, wlo(L.m_w1_lo));
         }
         {
             TcGemmArgs ga;
@@ -294,10 +309,10 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
             ga.ep.out = X;
             ga.ep.ldc = d;
             ga.ep.bias = W.b2;
-            gemm(a_g, L.m_w2, ga, I, kBnWide);
+            gemm(a_g, L.m_w2, ga, I, kBnWide, g_lo, wlo(L.m_w2_lo));
         }
     }
-    MSB_CUDA(launch_ln_bf16(X, B, d, m.dec_norm, hb.as<__nv_bfloat16>(), s));
+    MSB_CUDA(launch_ln_bf16(X, B, d, m.dec_norm, hb.as<__nv_bfloat16>(), s, 0.f, lo_hb));
     {
         TcGemmArgs ga;
         ga.M = B;
@@ -309,7 +324,7 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
         ga.inv_temp = inv_temp;
         ga.seed = seed;
         ga.step = pos.as<int>();
-        gemm(a_hb, m_lm, ga, d, kBnWide);
+        gemm(a_hb, m_lm, ga, d, kBnWide, hb_lo, wlo(m_lm_lo));
     }
     MSB_CUDA(launch_step_finalize(amax.as<unsigned long long>(), B, pos.as<int>(), next_ids.as<int>(), ids.as<int>(),
                                   Tc, counts.as<int>(), limits_d.as<int>(), done.as<int>(), hit.as<int>(), c.eos,

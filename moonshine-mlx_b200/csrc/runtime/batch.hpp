@@ -48,13 +48,15 @@ struct BatchEngine {
         __nv_bfloat16 *wqkv, *wo, *wcq, *wco, *w1i, *w2;
         float* b1i;
         CUtensorMap m_qkv, m_o, m_cq, m_co, m_w1, m_w2;
+        CUtensorMap m_qkv_lo, m_o_lo, m_cq_lo, m_co_lo, m_w1_lo, m_w2_lo;  // low planes (split)
     };
     Model& m;
+    bool split = false;  // fp32 checkpoint: split bf16 operands (fp32-level products)
     bool weights_ready = false;
     std::vector<DevBuf*> own;
     std::vector<LayerB> layers;
     __nv_bfloat16* lm = nullptr;
-    CUtensorMap m_lm;
+    CUtensorMap m_lm, m_lm_lo;
     int Bc = 0, Tc = 0, Mc = 0, Fc = 0;  // capacities: rows, steps, total frames, frames per row
     DevBuf x, hb, attn, g, q, qc, kvnew, part, amax, ids, next_ids, counts, limits_d, done, hit,
         pos, frame_off, frames, cross32, cross16, memory, status;
@@ -62,7 +64,7 @@ struct BatchEngine {
     DevBuf kvpool, ptable;
     int table_stride = 0;
     void assign_pages(int B, int T, const std::vector<int>& limits);
-    CUtensorMap a_hb, a_attn, a_g;
+    CUtensorMap a_hb, a_attn, a_g, a_hb_lo, a_attn_lo, a_g_lo;
 
     // Utterances are encoded concurrently on the model's encoder lanes.
     void encode_all(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
@@ -93,7 +95,8 @@ struct BatchEngine {
     void enqueue_step(int B, int max_frames, bool forced, bool first, float* logits);
     float inv_temp = 0.f;  // sampling state of the current run
     unsigned seed = 0;
-    void gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& g, int K, int bn);
+    void gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& g, int K, int bn,
+              const CUtensorMap* a_lo = nullptr, const CUtensorMap* b_lo = nullptr);
 };
 
 }  // namespace msb

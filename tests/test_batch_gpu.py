@@ -6,12 +6,12 @@ import numpy as np
 import pytest
 
 from moonshine_b200 import synth
-from util import BF16_LOGIT_TOL, assert_logits_close, model_dir, oracle_for, with_config
+from util import BF16_LOGIT_TOL, FP32_LOGIT_TOL, assert_logits_close, model_dir, oracle_for, with_config
 
 pytestmark = pytest.mark.gpu
 
 
-def _check_batch(path, audios, forced, kv_fp16=True, max_tokens=None, model=None):
+def _check_batch(path, audios, forced, kv_fp16=True, max_tokens=None, model=None, tol=BF16_LOGIT_TOL):
     import moonshine_b200 as mb
     m = model or mb.MoonshineModel.load(path, kv_fp16=kv_fp16)
     ids, st, logits = m.generate_batch(audios, forced_len=forced, max_tokens=max_tokens, return_logits=True)
@@ -32,9 +32,9 @@ def _check_batch(path, audios, forced, kv_fp16=True, max_tokens=None, model=None
             k = len(ref_logits) - 1
         else:
             scale = float(np.max(np.abs(ref_logits[k])))
-            assert margins[k] <= BF16_LOGIT_TOL * scale, (
+            assert margins[k] <= tol * scale, (
                 f"utterance {b}: ids part at step {k} with margin {margins[k]:.4f} (scale {scale:.3f})")
-        assert_logits_close(logits[b, : k + 1], ref_logits[: k + 1], BF16_LOGIT_TOL)
+        assert_logits_close(logits[b, : k + 1], ref_logits[: k + 1], tol)
     return st
 
 
@@ -154,3 +154,13 @@ def test_batch_kv_pages_ragged(model_root):
         assert 1 <= u <= 3 and c == cap
     for st in states:
         st.close()
+
+
+@pytest.mark.parametrize("kv_fp16", [True, False])
+def test_batch_fp32_checkpoint_split_operands(model_root, kv_fp16):
+    """An fp32 checkpoint decodes in lockstep with split bf16 operands (high + low planes,
+    three tensor-core products per step): logits within the fp32 tolerance (1e-3) of the
+    float64 oracle and ids identical to it, like the batch-1 kernels."""
+    d = model_dir(model_root, "tiny")
+    audios = [synth.synth_audio(n, 700 + i) for i, n in enumerate([16000, 48000, 30000, 80000])]
+    _check_batch(d, audios, 24, kv_fp16=kv_fp16, tol=FP32_LOGIT_TOL)

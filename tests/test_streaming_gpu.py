@@ -94,12 +94,13 @@ def test_stream_batch_equals_single(model_root):
 
 def test_stream_batch_decode_lockstep(model_root):
     """transcribe_batch with batch_decode: 4 streams fed 80 ms chunks, every call's segment
-    decoded in lockstep on bf16 tensor cores.  Per call and stream the ids follow the
-    oracle's decodeMemory (MoonshineStreaming.swift:229-276) up to the first step whose
-    top-2 logit margin is within the bf16 tolerance; the memories stay equal throughout."""
+    decoded in lockstep on the tensor cores (split bf16 operands for this fp32 checkpoint).
+    Per call and stream the ids follow the oracle's decodeMemory
+    (MoonshineStreaming.swift:229-276); they may part only at a step whose top-2 logit
+    margin is within the fp32 tolerance; the memories stay equal throughout."""
     import moonshine_b200 as mb
     from oracle.moonshine_oracle import OracleStream, StreamingConfig
-    from util import BF16_LOGIT_TOL
+    from util import FP32_LOGIT_TOL
     d = model_dir(model_root, "tiny")
     m = mb.MoonshineModel.load(d)
     o = oracle_for(d)
@@ -133,7 +134,7 @@ def test_stream_batch_decode_lockstep(model_root):
                 assert ids == ref and got[i][1] == hit, f"stream {i} chunk {k}"
             else:
                 scale = float(np.max(np.abs(ref_logits[j])))
-                assert margins[j] <= BF16_LOGIT_TOL * scale, f"stream {i} chunk {k}: ids part at step {j}"
+                assert margins[j] <= FP32_LOGIT_TOL * scale, f"stream {i} chunk {k}: ids part at step {j}"
             checked += 1
     assert checked >= n_streams * (n_chunks - 2)
 
