@@ -68,26 +68,22 @@ __device__ __forceinline__ void cp16(void* s, const void* g) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(s)), "l"(g) : "memory");
 }
 
-#ifndef MSB_W0_FREE
-#define MSB_W0_FREE 0
-#endif
-
 // GEMV rows of the packed streams are stored rf + 4 floats apart (rf % 8 == 0): an odd
 // number of 16-byte units, so lanes that own consecutive rows read distinct bank groups.
 __host__ __device__ inline int row_stride(int rf) { return rf + 4; }
 
 // res[i] = rows[i][0 : rf) . vec for i < nr (nr <= 64, row i at rows + i * rs).  Long rows
-// split their columns over the eight warps with lanes owning rows (rs / 4 odd, so the eight
-// lanes of one 128-bit phase read eight different bank groups) and a per-row sum of the
-// warp partials in fixed order; short rows take one thread each.  Ends with a barrier.
+// split their columns over warps 1-7 with lanes owning rows (rs / 4 odd, so the eight lanes
+// of one 128-bit phase read eight different bank groups) and a per-row sum of the warp
+// partials in fixed order; warp 0, whose lane 0 issues the ring's bulk copies right before,
+// takes no columns.  Short rows take one thread each.  Ends with a barrier.
 __device__ __noinline__ void block_gemv(const float* rows, int nr, int rf, int rs, const float* vec, float* part,
                                         float* res) {
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int c4 = rf >> 2;
     const float4* v4 = reinterpret_cast<const float4*>(vec);
     if (c4 >= 4 * NW) {
-        // MSB_W0_FREE: warp 0 (whose lane 0 issues the ring's bulk copies) takes no columns
-        constexpr int W0 = MSB_W0_FREE ? 1 : 0;
+        constexpr int W0 = 1;  // first column warp
         constexpr int NWK = NW - W0;
         const int per = (c4 + NWK - 1) / NWK;
         const int k0 = (w - W0) * per, k1 = w < W0 ? k0 : min(c4, k0 + per);

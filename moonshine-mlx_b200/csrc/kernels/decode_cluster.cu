@@ -92,15 +92,8 @@ __host__ __device__ inline Segs make_segs(const ClusterGeom& g, int d, int hd) {
 enum SegId { SEG_QKV = 0, SEG_O, SEG_CQ, SEG_XKV, SEG_CO, SEG_FC1, SEG_FC2, SEG_LM };
 
 constexpr int MAXB = 320;  // blocks per step a CTA's schedule may have (checked at launch)
-#ifndef MSB_FC2_MAXR
-#define MSB_FC2_MAXR 1024
-#endif
-#ifndef MSB_LM_ROWS
-#define MSB_LM_ROWS 32
-#endif
-#ifndef MSB_LN_FUSED
-#define MSB_LN_FUSED 0
-#endif
+constexpr int FC2_MAXR = 1024;  // fc2 rows per block: a CTA's whole fc2 slice is one block for tiny
+constexpr int LM_ROWS = 32;     // fp32 LM rows per block (one full lane round of block_gemv)
 
 // Per-warp sums of the values in s and of their squares -> red[0][w], red[1][w] (the
 // LayerNorm statistics of the residual, gathered while it is written; a barrier must follow
@@ -135,8 +128,8 @@ __host__ __device__ inline SegPlan seg_plan(int seg, int layer, const ClusterGeo
         case SEG_CQ: return {lw + sg.cq, d, ncq, sd, 1, mq};
         case SEG_CO: return {lw + sg.co, 0, no, row_stride(hd), 1, 64};
         case SEG_FC1: return {lw + sg.fc1, d + 2 * g.gr, 2 * g.gr, sd, 2, mq};
-        case SEG_FC2: return {lw + sg.fc2, sg.ro4, d, g.gr, 1, MSB_FC2_MAXR};
-        default: return {(size_t)L * sg.layer, d, nlm, lm_stride<QR>(g, d), 1, QR && g.lm_qbits ? NT : MSB_LM_ROWS};
+        case SEG_FC2: return {lw + sg.fc2, sg.ro4, d, g.gr, 1, FC2_MAXR};
+        default: return {(size_t)L * sg.layer, d, nlm, lm_stride<QR>(g, d), 1, QR && g.lm_qbits ? NT : LM_ROWS};
     }
 }
 
@@ -180,7 +173,7 @@ __device__ __forceinline__ long long add_cluster_partials(const unsigned long lo
                                                           float* red) {
     const int tid = threadIdx.x;
     long long cyc = 0;
-    float st1 = 0.f, st2 = 0.f;  // this thread's share of sum(x), sum(x^2) (MSB_LN_FUSED)
+    float st1 = 0.f, st2 = 0.f;  // this thread's share of sum(x), sum(x^2)
     auto timed_out = [&](uint64_t& t0) {
         if (t0 == 0) {
             t0 = globaltimer_ns();
@@ -265,7 +258,7 @@ __device__ __forceinline__ long long add_cluster_partials(const unsigned long lo
             st2 += a * a;
         }
     }
-    if (MSB_LN_FUSED) warp_stats(st1, st2, red);
+    warp_stats(st1, st2, red);
     __syncthreads();
     return cyc;
 }
@@ -277,33 +270,12 @@ __device__ __noinline__ long long add_cluster_partials_call(const unsigned long 
     return add_cluster_partials(pb, xs, d, H, tag, failed, status, red);
 }
 
-// xl = LN(xs) * wln over d inputs (every warp computes the statistics itself); for rows
-// quantized to qb (= QB) bits also the vector block_gemv_q reads (d % 64 == 0 there, so every
-// iteration covers whole warps).  One out-of-line copy serves every call site of the kernel,
-// so its instructions stay cached between the segments of a layer.  Ends with a barrier.
-template <int QB>
-__device__ __noinline__ void ln_vector(const float* xs, const float* wln, float* xl, int d, float* xq, int qb) {
-    const int tid = threadIdx.x, lane = tid & 31;
-    float s = 0.f;
-    for (int k = lane; k < d; k += 32) s += xs[k];
-    const float mean = warp_sum(s) / (float)d;
-    float q = 0.f;
-    for (int k = lane; k < d; k += 32) {
-        const float e = xs[k] - mean;
-        q += e * e;
-    }
-    const float rstd = rsqrtf(warp_sum(q) / (float)d + 1e-5f);
-    for (int k = tid; k < d; k += NT) {
-        const float v = (xs[k] - mean) * rstd * wln[k];
-        xl[k] = v;
-        if constexpr (QB != 0)
-            if (qb) quant_input<QB>(v, k, xq, d);
-    }
-    __syncthreads();
-}
-
-// The same from statistics gathered with the residual (red: per-warp sums of x and x^2, see
-// warp_stats): mean = sum / d, variance = sum(x^2) / d - mean^2.  Ends with a barrier.
+// xl = LN(xs) * wln over d inputs from statistics gathered with the residual (red: per-warp
+// sums of x and x^2, see warp_stats): mean = sum / d, variance = sum(x^2) / d - mean^2; for
+// rows quantized to qb (= QB) bits also the vector block_gemv_q reads (d % 64 == 0 there, so
+// every iteration covers whole warps).  One out-of-line copy serves every call site of the
+// kernel, so its instructions stay cached between the segments of a layer.  Ends with a
+// barrier.
 template <int QB>
 __device__ __noinline__ void ln_apply(const float* xs, const float* wln, float* xl, int d, float* xq, int qb,
                                       const float* red) {
@@ -533,11 +505,10 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
     // xl = LN(xs) * wln (wln in shared memory); for rows quantized to qb bits also the
     // vector block_gemv_q reads: xl pre-scaled per input, then sums over each 16 inputs
     // (d % 64 == 0 there, so every iteration below covers whole warps)
-    __shared__ float s_red[2 * NW];  // LayerNorm statistics of xs (MSB_LN_FUSED)
-    auto layer_norm = [&](const float* wln, int qb) {
-        if (MSB_LN_FUSED) ln_apply<QB>(xs, wln, xl, d, xq_s, qb, s_red);
-        else ln_vector<QB>(xs, wln, xl, d, xq_s, qb);
-    };
+    // LayerNorm statistics of xs, gathered where xs is written (the embedding row and every
+    // partial-sum exchange) so that the LayerNorm itself is one elementwise pass
+    __shared__ float s_red[2 * NW];
+    auto layer_norm = [&](const float* wln, int qb) { ln_apply<QB>(xs, wln, xl, d, xq_s, qb, s_red); };
     int par = 0;
     // xs += sum over clusters (fixed order) of partial[par][.] of exchange `epoch`
     auto add_partials = [&]() {
@@ -633,7 +604,7 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
                 e1 += v;
                 e2 += v * v;
             }
-            if (MSB_LN_FUSED) warp_stats(e1, e2, s_red);
+            warp_stats(e1, e2, s_red);
         }
         __syncthreads();
         for (int l = 0; l < L; ++l) {

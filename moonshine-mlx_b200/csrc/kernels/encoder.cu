@@ -96,7 +96,7 @@ constexpr int WA_MAXHD = 128;
 __global__ void window_attention_kernel(const float* __restrict__ qkv, int T, int H, int KVH,
                                         int hd, int left, int right, float scale,
                                         float* __restrict__ out, int seg_rows, const int* __restrict__ seg_len,
-                                        __nv_bfloat16* __restrict__ out_bf16) {
+                                        __nv_bfloat16* __restrict__ out_bf16, size_t lo_off) {
     const int lane = threadIdx.x & 31;
     const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (item >= T * H) return;
@@ -117,7 +117,7 @@ __global__ void window_attention_kernel(const float* __restrict__ qkv, int T, in
         if (tl >= len) {
             for (int d = lane; d < hd; d += 32) {
                 if (out) out[(size_t)t * (H * hd) + h * hd + d] = 0.f;
-                if (out_bf16) out_bf16[(size_t)t * (H * hd) + h * hd + d] = __float2bfloat16_rn(0.f);
+                if (out_bf16) st_bf16_split(out_bf16 + (size_t)t * (H * hd) + h * hd + d, 0.f, lo_off);
             }
             return;
         }
@@ -173,7 +173,7 @@ __global__ void window_attention_kernel(const float* __restrict__ qkv, int T, in
         const int d = lane + 32 * c;
         if (d < hd) {
             if (out) out[o + d] = acc[c] * inv;
-            if (out_bf16) out_bf16[o + d] = __float2bfloat16_rn(acc[c] * inv);
+            if (out_bf16) st_bf16_split(out_bf16 + o + d, acc[c] * inv, lo_off);
         }
     }
 }
@@ -184,14 +184,14 @@ __global__ void window_attention_kernel(const float* __restrict__ qkv, int T, in
 // writes exact zeros there.
 __global__ void frame_norm_rows_kernel(const float* const* __restrict__ audio, const int* __restrict__ n_frames,
                                        int rows, int seg_rows, int frame_len, const float* __restrict__ log_k,
-                                       __nv_bfloat16* __restrict__ out) {
+                                       __nv_bfloat16* __restrict__ out, size_t lo_off) {
     const int lane = threadIdx.x & 31;
     const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (r >= rows) return;
     const int sgi = r / seg_rows, f = r - sgi * seg_rows - 4;
     __nv_bfloat16* o = out + (size_t)r * frame_len;
     if (f < 0 || f >= n_frames[sgi]) {
-        for (int i = lane; i < frame_len; i += 32) o[i] = __float2bfloat16_rn(0.f);
+        for (int i = lane; i < frame_len; i += 32) st_bf16_split(o + i, 0.f, lo_off);
         return;
     }
     const float* a = audio[sgi] + (size_t)f * frame_len;
@@ -205,7 +205,7 @@ __global__ void frame_norm_rows_kernel(const float* const* __restrict__ audio, c
     }
     const float rms = sqrtf(warp_sum(v) / (float)frame_len + 1e-6f);
     const float k = expf(*log_k);
-    for (int i = lane; i < frame_len; i += 32) o[i] = __float2bfloat16_rn(asinhf(k * ((a[i] - mean) / rms)));
+    for (int i = lane; i < frame_len; i += 32) st_bf16_split(o + i, asinhf(k * ((a[i] - mean) / rms)), lo_off);
 }
 
 // Final encoder LayerNorm of segment rows (rows [s * seg_rows, s * seg_rows + len[s]) hold
@@ -214,7 +214,7 @@ __global__ void ln_gather_rows_kernel(const float* __restrict__ x, int rows, int
                                       const float* __restrict__ w, float w_offset, float eps,
                                       const float* __restrict__ pos_emb, const int* __restrict__ len,
                                       const int* __restrict__ off, float* __restrict__ out,
-                                      __nv_bfloat16* __restrict__ out_bf16) {
+                                      __nv_bfloat16* __restrict__ out_bf16, size_t lo_off) {
     const int lane = threadIdx.x & 31;
     const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (r >= rows) return;
@@ -246,7 +246,7 @@ __global__ void ln_gather_rows_kernel(const float* __restrict__ x, int rows, int
         if (i < dim) {
             const float y = (v[j] - mean) * rstd * (w[i] + w_offset) + pe[i];
             out[orow + i] = y;
-            out_bf16[orow + i] = __float2bfloat16_rn(y);
+            st_bf16_split(out_bf16 + orow + i, y, lo_off);
         }
     }
 }
@@ -290,7 +290,7 @@ cudaError_t launch_layernorm_rows(const float* x, int rows, int dim, const float
 cudaError_t launch_window_attention(const float* qkv, int T, int H, int kv_heads, int hd,
                                     int left, int right, float scale, float* out,
                                     cudaStream_t stream, int seg_rows, const int* seg_len,
-                                    __nv_bfloat16* out_bf16) {
+                                    __nv_bfloat16* out_bf16, size_t lo_off) {
     if (T <= 0) return cudaSuccess;
     if (hd > WA_MAXHD || (hd & 3) || H % kv_heads) return cudaErrorInvalidValue;
     if ((seg_rows > 0) != (seg_len != nullptr) || (!out && !out_bf16)) return cudaErrorInvalidValue;
@@ -298,30 +298,31 @@ cudaError_t launch_window_attention(const float* qkv, int T, int H, int kv_heads
     const int wpb = 8;
     const int items = T * H;
     window_attention_kernel<<<(items + wpb - 1) / wpb, wpb * 32, 0, stream>>>(
-        qkv, T, H, kv_heads, hd, left, right, scale, out, seg_rows, seg_len, out_bf16);
+        qkv, T, H, kv_heads, hd, left, right, scale, out, seg_rows, seg_len, out_bf16, lo_off);
     return cudaGetLastError();
 }
 
 cudaError_t launch_frame_norm_rows(const float* const* audio, const int* n_frames, int rows, int seg_rows,
-                                   int frame_len, const float* log_k, __nv_bfloat16* out, cudaStream_t stream) {
+                                   int frame_len, const float* log_k, __nv_bfloat16* out, cudaStream_t stream,
+                                   size_t lo_off) {
     if (rows <= 0) return cudaSuccess;
     if (seg_rows <= 4) return cudaErrorInvalidValue;
     ++launch_counter();
     const int wpb = 8;
     frame_norm_rows_kernel<<<(rows + wpb - 1) / wpb, wpb * 32, 0, stream>>>(audio, n_frames, rows, seg_rows,
-                                                                          frame_len, log_k, out);
+                                                                          frame_len, log_k, out, lo_off);
     return cudaGetLastError();
 }
 
 cudaError_t launch_ln_gather_rows(const float* x, int rows, int seg_rows, int dim, const float* w, float w_offset,
                                   float eps, const float* pos_emb, const int* len, const int* off, float* out,
-                                  __nv_bfloat16* out_bf16, cudaStream_t stream) {
+                                  __nv_bfloat16* out_bf16, cudaStream_t stream, size_t lo_off) {
     if (rows <= 0) return cudaSuccess;
     if (dim > 32 * LN_MAXV || seg_rows <= 0) return cudaErrorInvalidValue;
     ++launch_counter();
     const int wpb = 8;
     ln_gather_rows_kernel<<<(rows + wpb - 1) / wpb, wpb * 32, 0, stream>>>(x, rows, seg_rows, dim, w, w_offset, eps,
-                                                                         pos_emb, len, off, out, out_bf16);
+                                                                         pos_emb, len, off, out, out_bf16, lo_off);
     return cudaGetLastError();
 }
 

@@ -179,12 +179,15 @@ cudaError_t launch_layernorm_rows(const float* x, int rows, int dim, const float
 cudaError_t launch_window_attention(const float* qkv, int T, int H, int kv_heads, int hd,
                                     int left, int right, float scale, float* out,
                                     cudaStream_t stream, int seg_rows = 0, const int* seg_len = nullptr,
-                                    __nv_bfloat16* out_bf16 = nullptr);
+                                    __nv_bfloat16* out_bf16 = nullptr, size_t lo_off = 0);
 // CMVN + asinh of every frame of a batch into segment rows (row r: frame r % seg_rows - 4 of
 // utterance r / seg_rows, zeros where there is none), bf16 [rows][frame_len]: the input of
 // the frame Linear as one GEMM.  audio / n_frames: device arrays of the utterances.
+// (lo_off here and in the two launchers around it: the low plane of a split operand, as for
+// launch_ln_bf16.)
 cudaError_t launch_frame_norm_rows(const float* const* audio, const int* n_frames, int rows, int seg_rows,
-                                   int frame_len, const float* log_k, __nv_bfloat16* out, cudaStream_t stream);
+                                   int frame_len, const float* log_k, __nv_bfloat16* out, cudaStream_t stream,
+                                   size_t lo_off = 0);
 // Frame features written as bf16 (same math as launch_frame_features).
 cudaError_t launch_frame_features_bf16(const float* audio, int n_frames, int frame_len, const float* log_k,
                                        const float* w, int dim, __nv_bfloat16* out, int ld_out,
@@ -193,7 +196,7 @@ cudaError_t launch_frame_features_bf16(const float* audio, int n_frames, int fra
 // (fp32) and out_bf16 for t < len[s].
 cudaError_t launch_ln_gather_rows(const float* x, int rows, int seg_rows, int dim, const float* w, float w_offset,
                                   float eps, const float* pos_emb, const int* len, const int* off, float* out,
-                                  __nv_bfloat16* out_bf16, cudaStream_t stream);
+                                  __nv_bfloat16* out_bf16, cudaStream_t stream, size_t lo_off = 0);
 
 // ---------------------------------------------------------------- decoder
 struct DecodeLayerW {

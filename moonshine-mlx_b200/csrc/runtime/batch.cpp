@@ -120,20 +120,23 @@ void BatchEngine::ensure_ws(int B, int T, int Mtot, int maxM) {
         frame_off.ensure((size_t)Bc * 4);
         frames.ensure((size_t)Bc * 4);
     }
+    // capacities grow by half again at least, so a workload that grows a little per call
+    // (streams whose memories lengthen every chunk) reallocates rarely
+    auto grow = [](int cur, int need) { return need <= cur ? cur : std::max(need, cur + cur / 2); };
     if (T > Tc || remap) {
-        Tc = std::max(Tc, T);
+        Tc = grow(Tc, T);
         ids.ensure((size_t)Bc * Tc * 4);
     }
     (void)kvsz;
     if (Mtot > Mc) {
-        Mc = Mtot;
+        Mc = grow(Mc, Mtot);
         const size_t n = (size_t)c.layers * 2 * KVD * Mc;
         cross32.ensure(n * 4);
         cross16.ensure(n * 2);
         memory.ensure((size_t)Mc * d * 4);
     }
     if (maxM > Fc || remap) {
-        Fc = std::max(Fc, maxM);
+        Fc = grow(Fc, maxM);
         part.ensure(cross_batch_part_floats(Bc, c.heads, c.head_dim, Fc) * 4);
     }
     status.ensure(16);
@@ -184,13 +187,7 @@ void BatchEngine::gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& g
     // k-splits (one cluster per output tile, summed in split order) until the grid covers
     // the SMs; every split keeps at least one k-block
     const int tiles = ((ga.N + bn - 1) / bn) * ((ga.M + 127) / 128);
-#ifndef MSB_SPLIT_POLICY
-#define MSB_SPLIT_POLICY 1
-#endif
-    int cap_s = TC_MAX_SPLITS;
-    if (MSB_SPLIT_POLICY == 2 && ga.mode != TC_EPI_ACCUM) cap_s = 1;
-    if (MSB_SPLIT_POLICY == 3) cap_s = ga.mode != TC_EPI_ACCUM ? 1 : 4;
-    int sp = std::max(1, std::min({cap_s, ga.kb_per_tap, m.num_sms / std::max(tiles, 1)}));
+    int sp = std::max(1, std::min({TC_MAX_SPLITS, ga.kb_per_tap, m.num_sms / std::max(tiles, 1)}));
     const int per = (ga.kb_per_tap + sp - 1) / sp;
     ga.splits = (ga.kb_per_tap + per - 1) / per;
     MSB_CUDA(launch_gemm_tc_split(a, a_lo, b, b_lo, ga, bn, m.stream));
@@ -338,35 +335,28 @@ void BatchEngine::ensure_enc_weights() {
     const int eHD = c.e_heads * hd, QKV = (c.e_heads + 2 * c.e_kv_heads) * hd;
     const int NKV = c.layers * 2 * c.kv_heads * c.head_dim;
     cudaStream_t s = m.stream;
-    elin = alloc<__nv_bfloat16>((size_t)ed * c.frame_len());
-    MSB_CUDA(launch_f32_to_bf16_rows(m.lin_w, elin, ed, c.frame_len(), 0, s));
-    make_b_map(&m_lin, elin, ed, c.frame_len(), kBnWide);
-    econv1 = alloc<__nv_bfloat16>((size_t)2 * ed * 5 * ed);
-    econv2 = alloc<__nv_bfloat16>((size_t)ed * 10 * ed);
-    MSB_CUDA(launch_f32_to_bf16_rows(m.conv1_w, econv1, 2 * ed, 5 * ed, 0, s));
-    MSB_CUDA(launch_f32_to_bf16_rows(m.conv2_w, econv2, ed, 10 * ed, 0, s));
-    make_b_map(&m_conv1, econv1, 2 * ed, 5 * ed, kBnWide);
-    make_b_map(&m_conv2, econv2, ed, 10 * ed, kBnWide);
+    esplit = !m.enc_bf16;  // fp32 checkpoint: split operands, as in the decode
+    auto weight = [&](const float* src, int rows, int K, CUtensorMap* hi, CUtensorMap* lo) {
+        const size_t n = (size_t)rows * K;
+        __nv_bfloat16* w = alloc<__nv_bfloat16>(esplit ? 2 * n : n);
+        MSB_CUDA(launch_f32_to_bf16_rows(src, w, rows, K, 0, s, esplit ? n : 0));
+        make_b_map(hi, w, rows, K, kBnWide);
+        if (esplit) make_b_map(lo, w + n, rows, K, kBnWide);
+        return w;
+    };
+    elin = weight(m.lin_w, ed, c.frame_len(), &m_lin, &m_lin_lo);
+    econv1 = weight(m.conv1_w, 2 * ed, 5 * ed, &m_conv1, &m_conv1_lo);
+    econv2 = weight(m.conv2_w, ed, 10 * ed, &m_conv2, &m_conv2_lo);
     elayers.resize(c.e_layers);
     for (int i = 0; i < c.e_layers; ++i) {
         const EncLayer& L = m.enc[i];
         EncLayerB& E = elayers[i];
-        E.wqkv = alloc<__nv_bfloat16>((size_t)QKV * ed);
-        E.wo = alloc<__nv_bfloat16>((size_t)ed * eHD);
-        E.w1 = alloc<__nv_bfloat16>((size_t)EI * ed);
-        E.w2 = alloc<__nv_bfloat16>((size_t)ed * EI);
-        MSB_CUDA(launch_f32_to_bf16_rows(L.wqkv, E.wqkv, QKV, ed, 0, s));
-        MSB_CUDA(launch_f32_to_bf16_rows(L.wo, E.wo, ed, eHD, 0, s));
-        MSB_CUDA(launch_f32_to_bf16_rows(L.w1, E.w1, EI, ed, 0, s));
-        MSB_CUDA(launch_f32_to_bf16_rows(L.w2, E.w2, ed, EI, 0, s));
-        make_b_map(&E.m_qkv, E.wqkv, QKV, ed, kBnWide);
-        make_b_map(&E.m_o, E.wo, ed, eHD, kBnWide);
-        make_b_map(&E.m_w1, E.w1, EI, ed, kBnWide);
-        make_b_map(&E.m_w2, E.w2, ed, EI, kBnWide);
+        E.wqkv = weight(L.wqkv, QKV, ed, &E.m_qkv, &E.m_qkv_lo);
+        E.wo = weight(L.wo, ed, eHD, &E.m_o, &E.m_o_lo);
+        E.w1 = weight(L.w1, EI, ed, &E.m_w1, &E.m_w1_lo);
+        E.w2 = weight(L.w2, ed, EI, &E.m_w2, &E.m_w2_lo);
     }
-    ecross = alloc<__nv_bfloat16>((size_t)NKV * c.hidden);
-    MSB_CUDA(launch_f32_to_bf16_rows(m.cross_w, ecross, NKV, c.hidden, 0, s));
-    make_b_map(&m_ecross, ecross, NKV, c.hidden, kBnWide);
+    ecross = weight(m.cross_w, NKV, c.hidden, &m_ecross, &m_ecross_lo);
     MSB_CUDA(cudaStreamSynchronize(s));
     enc_weights_ready = true;
 }
@@ -396,22 +386,34 @@ bool BatchEngine::encode_tc(const std::vector<const float*>& audio_dev, const st
     const size_t rows1 = (size_t)B * R, rows2 = (size_t)B * R2 + 4, rows3 = (size_t)B * R3;
     ensure_enc_weights();
     cudaStream_t s = m.stream;
-    enorm.ensure(rows1 * fl * 2);
+    // bf16 GEMM inputs hold a low plane right after the high one when split (lo_* elements on)
+    const size_t P = esplit ? 2 : 1;
+    const size_t lo_norm = esplit ? rows1 * fl : 0, lo_pad1 = esplit ? rows1 * ed : 0;
+    const size_t lo_pad2 = esplit ? rows2 * 2 * ed : 0, lo_h = esplit ? rows3 * ed : 0;
+    const size_t lo_attn = esplit ? rows3 * eHD : 0, lo_f = esplit ? rows3 * EI : 0;
+    const size_t lo_mem = esplit ? (size_t)Mc * d : 0;
+    enorm.ensure(rows1 * fl * 2 * P);
     eaud.ensure((size_t)B * sizeof(float*));
-    epad1.ensure(rows1 * ed * 2);
-    epad2.ensure(rows2 * 2 * ed * 2);
+    epad1.ensure(rows1 * ed * 2 * P);
+    epad2.ensure(rows2 * 2 * ed * 2 * P);
     ex.ensure(rows3 * ed * 4);
-    eh.ensure(rows3 * ed * 2);
+    eh.ensure(rows3 * ed * 2 * P);
     eqkv.ensure(rows3 * QKV * 4);
-    eattn.ensure(rows3 * eHD * 2);
-    ef.ensure(rows3 * EI * 2);
-    emem16.ensure((size_t)Mc * d * 2);
+    eattn.ensure(rows3 * eHD * 2 * P);
+    ef.ensure(rows3 * EI * 2 * P);
+    emem16.ensure((size_t)Mc * d * 2 * P);
     eseg.ensure((size_t)3 * B * 4);
     __nv_bfloat16* pad1 = epad1.as<__nv_bfloat16>();
     __nv_bfloat16* pad2 = epad2.as<__nv_bfloat16>();
     float* X = ex.as<float>();
     int* seg_len = eseg.as<int>();
     int* seg_off = seg_len + B;
+    // A maps of a bf16 input [rows, K] at p: the high plane, and when split the low one
+    auto amap = [&](CUtensorMap* hi, CUtensorMap* lo, const __nv_bfloat16* p, size_t rows, int K, size_t lo_off) {
+        make_a_map(hi, p, (int)rows, K);
+        if (esplit) make_a_map(lo, p + lo_off, (int)rows, K);
+    };
+    auto lo_of = [&](const CUtensorMap& mlo) { return esplit ? &mlo : nullptr; };
     {
         std::vector<int> host(2 * (size_t)B);
         for (int b = 0; b < B; ++b) {
@@ -427,28 +429,34 @@ bool BatchEngine::encode_tc(const std::vector<const float*>& audio_dev, const st
         int* t1_dev = seg_len + 2 * B;
         MSB_CUDA(cudaMemcpyAsync(t1_dev, t1.data(), (size_t)B * 4, cudaMemcpyHostToDevice, s));
         MSB_CUDA(cudaMemcpyAsync(eaud.p, audio_dev.data(), (size_t)B * sizeof(float*), cudaMemcpyHostToDevice, s));
+        // the pointer array is read by the next kernel: keep the host copy alive until then
         MSB_CUDA(launch_frame_norm_rows(reinterpret_cast<const float* const*>(eaud.p), t1_dev, (int)rows1, R, fl,
-                                        m.log_k, enorm.as<__nv_bfloat16>(), s));
-        CUtensorMap a_norm;
-        if (!tc_make_map_3d(&a_norm, enorm.p, (uint64_t)fl, 1, (uint64_t)rows1, (uint64_t)fl * 2, (uint64_t)fl * 2,
-                            128))
-            throw MsError(MS_ERR_CUDA, "cuTensorMapEncodeTiled failed for the frames");
+                                        m.log_k, enorm.as<__nv_bfloat16>(), s, lo_norm));
+        CUtensorMap a_norm, a_norm_lo;
+        for (int pl = 0; pl < (int)P; ++pl) {
+            if (!tc_make_map_3d(pl ? &a_norm_lo : &a_norm, enorm.as<__nv_bfloat16>() + (pl ? lo_norm : 0),
+                                (uint64_t)fl, 1, (uint64_t)rows1, (uint64_t)fl * 2, (uint64_t)fl * 2, 128))
+                throw MsError(MS_ERR_CUDA, "cuTensorMapEncodeTiled failed for the frames");
+        }
         TcGemmArgs ga;
         ga.M = (int)rows1;
         ga.N = ed;
         ga.ep.act = ACT_SILU;
         ga.out_bf16 = pad1;
         ga.ldc_bf16 = ed;
-        gemm(a_norm, m_lin, ga, fl, kBnWide);
+        ga.bf16_lo_off = lo_pad1;
+        gemm(a_norm, m_lin, ga, fl, kBnWide, esplit ? &a_norm_lo : nullptr, lo_of(m_lin_lo));
+        MSB_CUDA(cudaStreamSynchronize(s));  // t1 and the pointer array were copied from host vectors
     }
     // causal stride-2 convs as 5-tap GEMMs: output row m reads input rows 2m + tap, i.e.
     // (y, z) = (tap & 1, m + tap / 2) of the input viewed as row pairs
-    auto conv = [&](const __nv_bfloat16* in, size_t in_rows, int cin, const CUtensorMap& wmap, int M, int N,
-                    TcGemmArgs& ga) {
-        CUtensorMap amap;
-        if (!tc_make_map_3d(&amap, in, (uint64_t)cin, 2, (uint64_t)(in_rows / 2), (uint64_t)cin * 2,
-                            (uint64_t)cin * 4, 128))
-            throw MsError(MS_ERR_CUDA, "cuTensorMapEncodeTiled failed for a conv input");
+    auto conv = [&](const __nv_bfloat16* in, size_t in_rows, int cin, size_t in_lo, const CUtensorMap& wmap,
+                    const CUtensorMap& wmap_lo, int M, int N, TcGemmArgs& ga) {
+        CUtensorMap amap, amap_lo;
+        for (int pl = 0; pl < (int)P; ++pl)
+            if (!tc_make_map_3d(pl ? &amap_lo : &amap, in + (pl ? in_lo : 0), (uint64_t)cin, 2,
+                                (uint64_t)(in_rows / 2), (uint64_t)cin * 2, (uint64_t)cin * 4, 128))
+                throw MsError(MS_ERR_CUDA, "cuTensorMapEncodeTiled failed for a conv input");
         ga.M = M;
         ga.N = N;
         ga.taps = 5;
@@ -460,7 +468,7 @@ bool BatchEngine::encode_tc(const std::vector<const float*>& audio_dev, const st
         }
         ga.mode = TC_EPI_STD;
         ga.status = status.as<unsigned>();
-        MSB_CUDA(launch_gemm_tc(amap, wmap, ga, kBnWide, s));
+        MSB_CUDA(launch_gemm_tc_split(amap, esplit ? &amap_lo : nullptr, wmap, lo_of(wmap_lo), ga, kBnWide, s));
     };
     {
         TcGemmArgs ga;
@@ -468,38 +476,44 @@ bool BatchEngine::encode_tc(const std::vector<const float*>& audio_dev, const st
         ga.ep.act = ACT_SILU;
         ga.out_bf16 = pad2 + (size_t)4 * 2 * ed;  // utterance b's conv1 outputs at rows b*R2 + 4 + t
         ga.ldc_bf16 = 2 * ed;
-        conv(pad1, rows1, ed, m_conv1, B * R2, 2 * ed, ga);
+        ga.bf16_lo_off = lo_pad2;
+        conv(pad1, rows1, ed, lo_pad1, m_conv1, m_conv1_lo, B * R2, 2 * ed, ga);
     }
     // the 4 rows in front of every utterance took the previous one's tail outputs: back to zero
-    MSB_CUDA(cudaMemset2DAsync(pad2, (size_t)R2 * 2 * ed * 2, 0, (size_t)4 * 2 * ed * 2, B, s));
+    for (int pl = 0; pl < (int)P; ++pl)
+        MSB_CUDA(cudaMemset2DAsync(pad2 + (pl ? lo_pad2 : 0), (size_t)R2 * 2 * ed * 2, 0, (size_t)4 * 2 * ed * 2, B,
+                                   s));
     {
         TcGemmArgs ga;
         ga.ep.bias = m.conv2_b;
         ga.ep.out = X;
         ga.ep.ldc = ed;
-        conv(pad2, rows2, 2 * ed, m_conv2, B * R3, ed, ga);
+        conv(pad2, rows2, 2 * ed, lo_pad2, m_conv2, m_conv2_lo, B * R3, ed, ga);
     }
     // encoder layers over all B * R3 rows; attention stays inside each utterance's rows
-    CUtensorMap a_h, a_attn, a_f;
-    make_a_map(&a_h, eh.as<__nv_bfloat16>(), (int)rows3, ed);
-    make_a_map(&a_attn, eattn.as<__nv_bfloat16>(), (int)rows3, eHD);
-    make_a_map(&a_f, ef.as<__nv_bfloat16>(), (int)rows3, EI);
+    CUtensorMap a_h, a_attn, a_f, a_h_lo, a_attn_lo, a_f_lo;
+    amap(&a_h, &a_h_lo, eh.as<__nv_bfloat16>(), rows3, ed, lo_h);
+    amap(&a_attn, &a_attn_lo, eattn.as<__nv_bfloat16>(), rows3, eHD, lo_attn);
+    amap(&a_f, &a_f_lo, ef.as<__nv_bfloat16>(), rows3, EI, lo_f);
+    const CUtensorMap* h_lo = esplit ? &a_h_lo : nullptr;
+    const CUtensorMap* attn_lo = esplit ? &a_attn_lo : nullptr;
+    const CUtensorMap* f_lo = esplit ? &a_f_lo : nullptr;
     const float scale = std::pow((float)hd, -0.5f);
     for (int i = 0; i < c.e_layers; ++i) {
         const EncLayer& L = m.enc[i];
         const EncLayerB& E = elayers[i];
-        MSB_CUDA(launch_ln_bf16(X, (int)rows3, ed, L.ln_in, eh.as<__nv_bfloat16>(), s, 1.0f));
+        MSB_CUDA(launch_ln_bf16(X, (int)rows3, ed, L.ln_in, eh.as<__nv_bfloat16>(), s, 1.0f, lo_h));
         {
             TcGemmArgs ga;
             ga.M = (int)rows3;
             ga.N = QKV;
             ga.ep.out = eqkv.as<float>();
             ga.ep.ldc = QKV;
-            gemm(a_h, E.m_qkv, ga, ed, kBnWide);
+            gemm(a_h, E.m_qkv, ga, ed, kBnWide, h_lo, lo_of(E.m_qkv_lo));
         }
         const auto w = c.window(i);
         MSB_CUDA(launch_window_attention(eqkv.as<float>(), (int)rows3, c.e_heads, c.e_kv_heads, hd, w.first, w.second,
-                                         scale, nullptr, s, R3, seg_len, eattn.as<__nv_bfloat16>()));
+                                         scale, nullptr, s, R3, seg_len, eattn.as<__nv_bfloat16>(), lo_attn));
         {
             TcGemmArgs ga;
             ga.M = (int)rows3;
@@ -508,9 +522,9 @@ bool BatchEngine::encode_tc(const std::vector<const float*>& audio_dev, const st
             ga.ep.ldc = ed;
             ga.ep.residual = X;
             ga.ep.ldr = ed;
-            gemm(a_attn, E.m_o, ga, eHD, kBnWide);
+            gemm(a_attn, E.m_o, ga, eHD, kBnWide, attn_lo, lo_of(E.m_o_lo));
         }
-        MSB_CUDA(launch_ln_bf16(X, (int)rows3, ed, L.ln_post, eh.as<__nv_bfloat16>(), s, 1.0f));
+        MSB_CUDA(launch_ln_bf16(X, (int)rows3, ed, L.ln_post, eh.as<__nv_bfloat16>(), s, 1.0f, lo_h));
         {
             TcGemmArgs ga;
             ga.M = (int)rows3;
@@ -519,7 +533,8 @@ bool BatchEngine::encode_tc(const std::vector<const float*>& audio_dev, const st
             ga.ep.act = ACT_GELU;
             ga.out_bf16 = ef.as<__nv_bfloat16>();
             ga.ldc_bf16 = EI;
-            gemm(a_h, E.m_w1, ga, ed, kBnWide);
+            ga.bf16_lo_off = lo_f;
+            gemm(a_h, E.m_w1, ga, ed, kBnWide, h_lo, lo_of(E.m_w1_lo));
         }
         {
             TcGemmArgs ga;
@@ -530,17 +545,17 @@ bool BatchEngine::encode_tc(const std::vector<const float*>& audio_dev, const st
             ga.ep.ldc = ed;
             ga.ep.residual = X;
             ga.ep.ldr = ed;
-            gemm(a_f, E.m_w2, ga, EI, kBnWide);
+            gemm(a_f, E.m_w2, ga, EI, kBnWide, f_lo, lo_of(E.m_w2_lo));
         }
     }
     // prepareMemory: final norm + positions, gathered to the batch memory rows
     MSB_CUDA(launch_ln_gather_rows(X, (int)rows3, R3, ed, m.enc_final, 1.0f, 1e-5f, m.pos_emb, seg_len, seg_off,
-                                   memory.as<float>(), emem16.as<__nv_bfloat16>(), s));
+                                   memory.as<float>(), emem16.as<__nv_bfloat16>(), s, lo_mem));
     // cross K/V of every memory row in one GEMM (scatter epilogue: fp32 copy + fp16 store)
     int Mtot = 0;
     for (int b = 0; b < B; ++b) Mtot = std::max(Mtot, off[b] + fr[b]);
-    CUtensorMap a_mem;
-    make_a_map(&a_mem, emem16.as<__nv_bfloat16>(), Mtot, d);
+    CUtensorMap a_mem, a_mem_lo;
+    amap(&a_mem, &a_mem_lo, emem16.as<__nv_bfloat16>(), Mtot, d, lo_mem);
     TcGemmArgs ga;
     ga.M = Mtot;
     ga.N = c.layers * 2 * c.kv_heads * c.head_dim;
@@ -551,7 +566,7 @@ bool BatchEngine::encode_tc(const std::vector<const float*>& audio_dev, const st
     ga.ep.head_dim = c.head_dim;
     ga.ep.frame_cap = Mc;
     ga.ep.frame_offset = 0;
-    gemm(a_mem, m_ecross, ga, d, kBnWide);
+    gemm(a_mem, m_ecross, ga, d, kBnWide, esplit ? &a_mem_lo : nullptr, lo_of(m_ecross_lo));
     return true;
 }
 
@@ -583,7 +598,7 @@ BatchEngine::Result BatchEngine::run(const std::vector<const float*>& audio_dev,
     }
     const int T = *std::max_element(limits.begin(), limits.end());
     ensure_ws(B, T, Mtot, maxM);
-    if (!(m.enc_bf16 && encode_tc(audio_dev, n_samples, off, fr))) {
+    if (!((m.enc_bf16 || m.opts.weight_dtype == MS_W_AUTO) && encode_tc(audio_dev, n_samples, off, fr))) {
         encode_all(audio_dev, n_samples, off);
         m.cross_kv_into(memory.as<float>(), Mtot, 0, cross32.as<float>(), m.kv_f16 ? cross16.p : nullptr, Mc);
     }

@@ -78,11 +78,13 @@ struct BatchEngine {
     struct EncLayerB {
         __nv_bfloat16 *wqkv, *wo, *w1, *w2;
         CUtensorMap m_qkv, m_o, m_w1, m_w2;
+        CUtensorMap m_qkv_lo, m_o_lo, m_w1_lo, m_w2_lo;
     };
     bool enc_weights_ready = false;
+    bool esplit = false;  // fp32 checkpoint: the encoder GEMMs take split operands
     std::vector<EncLayerB> elayers;
     __nv_bfloat16 *elin = nullptr, *econv1 = nullptr, *econv2 = nullptr, *ecross = nullptr;
-    CUtensorMap m_lin, m_conv1, m_conv2, m_ecross;
+    CUtensorMap m_lin, m_conv1, m_conv2, m_ecross, m_lin_lo, m_conv1_lo, m_conv2_lo, m_ecross_lo;
     DevBuf enorm, epad1, epad2, ex, eh, eqkv, eattn, ef, emem16, eseg, eaud;
     void ensure_enc_weights();
 
