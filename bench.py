@@ -79,7 +79,9 @@ KERNEL_SOURCES = {
     "cluster": ["csrc/kernels/decode_cluster.cu", "csrc/kernels/cluster_common.cuh", "csrc/kernels/common.cuh"],
     "grid": ["csrc/kernels/decode_b1.cu", "csrc/kernels/common.cuh"],
 }
-NCU_DECODE_TRAFFIC_16CALLS_1500F = {}
+NCU_DECODE_TRAFFIC_16CALLS_1500F = {
+    "cluster": {"bytes": 856079360 + 3237376, "sources_sha256": "4cf38cbb5ed3c704fa91609fc10d2fe26a5d52df23468cf10bf4b6eeab9b3a1b"},
+}
 DECODE_KERNEL_SYMBOL = {"cluster": "decode_cluster_kernel<40, 0>", "grid": "decode_b1_kernel<40>"}
 
 
@@ -347,10 +349,20 @@ def leg_streaming(mb, synth, torch, dist, barrier, rank, world, local, root, n_s
     m = mb.MoonshineModel.load(path, kv_fp16=True)
     s = torch.cuda.ExternalStream(m.cuda_stream)
     audio = {i: synth.synth_audio(n_chunks * chunk, 5000 + i) for i in mine}
+    sc = mb.StreamingConfig(batch_decode=True)
+    # warm-up on separate streams (weight planes, graph capture, first pool sizes), untimed
+    warm = [m.create_stream() for _ in mine]
+    for st in warm:
+        m.start_stream(st)
+    for k in range(3):
+        for st, i in zip(warm, mine):
+            m.add_audio(st, audio[i][k * chunk:(k + 1) * chunk])
+        m.transcribe_batch(warm, is_final=False, streaming_config=sc, max_tokens=max_tokens)
+    for st in warm:
+        st.close()
     states = [m.create_stream() for _ in mine]
     for st in states:
         m.start_stream(st)
-    sc = mb.StreamingConfig(batch_decode=True)
     lat, toks = [], 0
     barrier()
     torch.cuda.synchronize()

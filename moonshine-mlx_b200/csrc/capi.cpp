@@ -71,7 +71,18 @@ static void generate_chunk(Model& m, const float* audio, int64_t len, const ms_g
         MSB_CUDA(cudaMemcpyAsync(m.ws.audio.p, audio, (size_t)len * 4, cudaMemcpyHostToDevice, m.stream));
         audio_dev = m.ws.audio.as<float>();
     }
-    const int M = m.encode_device(audio_dev, len, 0);
+    // fp32 checkpoints under MS_W_AUTO encode on split-operand tensor-core GEMMs (the
+    // batched engine's encoder, one utterance), anything else on the CUDA-core encoder
+    const float* cross32 = nullptr;
+    const void* cross_st = nullptr;
+    int m_cap = 0;
+    int M = -1;
+    if (!m.enc_bf16 && m.opts.weight_dtype == MS_W_AUTO && len >= c.frame_len()) {
+        if (!m.batch) m.batch.reset(new BatchEngine(m));
+        M = m.batch->encode_one(audio_dev, len, &cross32, &cross_st, &m_cap);
+    }
+    const bool tc_encoded = M > 0;
+    if (!tc_encoded) M = m.encode_device(audio_dev, len, 0);
     st.memory_frames = M;
     if (M == 0) return;  // fewer samples than one frame: nothing to decode
     const double dur = (double)len / (double)c.sample_rate;
@@ -87,15 +98,20 @@ static void generate_chunk(Model& m, const float* audio, int64_t len, const ms_g
     }
     const bool want_logits = logits_out != nullptr;
     m.ensure_decode(M, n_steps, want_logits, c.vocab);
-    m.cross_kv(m.memory_ptr(), M, 0);
+    if (!tc_encoded) {
+        m.cross_kv(m.memory_ptr(), M, 0);
+        cross32 = m.ws.cross32.as<float>();
+        cross_st = m.kv_f16 ? m.ws.cross16.p : m.ws.cross32.p;
+        m_cap = m.ws.m_cap;
+    }
     if (teacher) {
         MSB_CUDA(cudaMemcpyAsync(m.ws.f.p, teacher, (size_t)n_steps * 4, cudaMemcpyHostToDevice, m.stream));
         teacher_dev = m.ws.f.as<int>();
     }
     MSB_CUDA(cudaEventRecord(m.ev[1], m.stream));
     const unsigned seed = (unsigned)gp.seed ^ (chunk_index * 0x9E3779B9u);  // chunks draw independently
-    Model::DecodeResult r = m.decode(m.ws.cross32.as<float>(), m.kv_f16 ? m.ws.cross16.p : m.ws.cross32.p,
-                                     m.ws.m_cap, M, n_steps, forced, teacher_dev, want_logits, gp.temperature, seed);
+    Model::DecodeResult r = m.decode(cross32, cross_st, m_cap, M, n_steps, forced, teacher_dev, want_logits,
+                                     gp.temperature, seed);
     MSB_CUDA(cudaEventRecord(m.ev[2], m.stream));
     const int n_ids = r.n_calls - (r.hit_eos ? 1 : 0);
     const int fit = std::max(0, std::min(n_ids, cap - out.n_ids));

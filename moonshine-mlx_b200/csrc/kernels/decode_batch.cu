@@ -202,28 +202,35 @@ __global__ void self_attn_batch_kernel(const float* __restrict__ q, const float*
         l = l * corr + warp_sum(p);
         a0 *= corr;
         a1 *= corr;
-        for (int jj = 0; jj < nk; ++jj) {
-            const float pp = __shfl_sync(FULL, p, jj);
-            const long long re = __shfl_sync(FULL, rowe, jj);
-            const int row = j0 + jj;
-            const int c = 2 * lane;
-            if (c < hd && (row == t || re >= 0)) {
-                float v0, v1;
-                if (row == t) {
-                    v0 = fv[c];
-                    v1 = fv[c + 1];
-                } else if (kv.kv_f16) {
-                    const float2 f = __half22float2(
-                        *reinterpret_cast<const __half2*>(reinterpret_cast<const __half*>(kv.pool) + voff + re + c));
-                    v0 = f.x;
-                    v1 = f.y;
+        // V rows of this chunk's keys, VU at a time: all loads of a group are issued before
+        // their products are summed (in key order), so their latencies overlap
+        constexpr int VU = 8;
+        const int c = 2 * lane;
+        for (int g0 = 0; g0 < nk; g0 += VU) {
+            float2 vv[VU];
+            float pp[VU];
+#pragma unroll
+            for (int u = 0; u < VU; ++u) {
+                const int jj = g0 + u;
+                pp[u] = __shfl_sync(FULL, p, jj & 31);
+                const long long re = __shfl_sync(FULL, rowe, jj & 31);
+                const int row = j0 + jj;
+                vv[u] = make_float2(0.f, 0.f);
+                if (jj < nk && c < hd && (row == t || re >= 0)) {
+                    if (row == t) vv[u] = make_float2(fv[c], fv[c + 1]);
+                    else if (kv.kv_f16)
+                        vv[u] = __half22float2(
+                            *reinterpret_cast<const __half2*>(reinterpret_cast<const __half*>(kv.pool) + voff + re + c));
+                    else
+                        vv[u] = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(kv.pool) + voff + re + c);
                 } else {
-                    const float2 f = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(kv.pool) + voff + re + c);
-                    v0 = f.x;
-                    v1 = f.y;
+                    pp[u] = 0.f;
                 }
-                a0 = fmaf(pp, v0, a0);
-                a1 = fmaf(pp, v1, a1);
+            }
+#pragma unroll
+            for (int u = 0; u < VU; ++u) {
+                a0 = fmaf(pp[u], vv[u].x, a0);
+                a1 = fmaf(pp[u], vv[u].y, a1);
             }
         }
         m = mn;

@@ -63,10 +63,9 @@ void BatchEngine::ensure_weights() {
     const Config& c = m.cfg;
     const int d = c.hidden, HD = c.heads * c.head_dim, KVD = c.kv_heads * c.head_dim, I = c.inter;
     cudaStream_t s = m.stream;
-    // fp32 checkpoints keep fp32-level GEMM products: every weight and GEMM input as a bf16
-    // high plane plus a bf16 low plane (split operands); bf16 / f16 checkpoints, or bf16 on
-    // request, use one bf16 plane
-    split = !m.enc_bf16;
+    // fp32 checkpoints keep fp32-level GEMM products (split): every weight and GEMM input as
+    // a bf16 high plane plus a bf16 low plane; bf16 / f16 checkpoints, or bf16 on request,
+    // use one bf16 plane
     // bf16 copy of src [rows, K] (rows interleaved value/gate when `il`), its weight map and,
     // when split, the low plane right behind it with its own map
     auto weight = [&](const float* src, int rows, int K, int il, int bn, CUtensorMap* hi, CUtensorMap* lo) {
@@ -335,7 +334,6 @@ void BatchEngine::ensure_enc_weights() {
     const int eHD = c.e_heads * hd, QKV = (c.e_heads + 2 * c.e_kv_heads) * hd;
     const int NKV = c.layers * 2 * c.kv_heads * c.head_dim;
     cudaStream_t s = m.stream;
-    esplit = !m.enc_bf16;  // fp32 checkpoint: split operands, as in the decode
     auto weight = [&](const float* src, int rows, int K, CUtensorMap* hi, CUtensorMap* lo) {
         const size_t n = (size_t)rows * K;
         __nv_bfloat16* w = alloc<__nv_bfloat16>(esplit ? 2 * n : n);
@@ -570,6 +568,27 @@ bool BatchEngine::encode_tc(const std::vector<const float*>& audio_dev, const st
     return true;
 }
 
+int BatchEngine::encode_one(const float* audio_dev, int64_t n_samples, const float** cross32_out,
+                            const void** cross16_out, int* m_cap) {
+    const Config& c = m.cfg;
+    const int fl = c.frame_len();
+    const int T1 = (int)(n_samples / fl);
+    const int T2 = T1 > 0 ? (T1 - 1) / 2 + 1 : 0;
+    const int M = T2 > 0 ? (T2 - 1) / 2 + 1 : 0;
+    if (M <= 0) return -1;
+    ensure_ws(1, 1, M, M);
+    MSB_CUDA(cudaMemsetAsync(status.p, 0, 16, m.stream));  // the split-K epilogues read it
+    if (!encode_tc({audio_dev}, {n_samples}, {0}, {M})) return -1;
+    unsigned st_word = 0;
+    MSB_CUDA(cudaMemcpyAsync(&st_word, status.p, 4, cudaMemcpyDeviceToHost, m.stream));
+    MSB_CUDA(cudaStreamSynchronize(m.stream));
+    throw_device_status(st_word, "tensor-core encoder");
+    *cross32_out = cross32.as<float>();
+    *cross16_out = m.kv_f16 ? cross16.p : cross32.p;
+    *m_cap = Mc;
+    return M;
+}
+
 BatchEngine::Result BatchEngine::run(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
                                      const std::vector<int>& limits, bool forced, bool want_logits, float temperature,
                                      unsigned seed_) {
@@ -598,6 +617,9 @@ BatchEngine::Result BatchEngine::run(const std::vector<const float*>& audio_dev,
     }
     const int T = *std::max_element(limits.begin(), limits.end());
     ensure_ws(B, T, Mtot, maxM);
+    // the status word starts at zero before any of this call's kernels (the split-K
+    // epilogues read it; the decode reports what encoder or decode recorded in it)
+    MSB_CUDA(cudaMemsetAsync(status.p, 0, 16, s));
     if (!((m.enc_bf16 || m.opts.weight_dtype == MS_W_AUTO) && encode_tc(audio_dev, n_samples, off, fr))) {
         encode_all(audio_dev, n_samples, off);
         m.cross_kv_into(memory.as<float>(), Mtot, 0, cross32.as<float>(), m.kv_f16 ? cross16.p : nullptr, Mc);
@@ -627,6 +649,7 @@ BatchEngine::Result BatchEngine::run_cross(const std::vector<CrossSrc>& src, con
     }
     const int T = *std::max_element(limits.begin(), limits.end());
     ensure_ws(B, T, Mtot, maxM);
+    MSB_CUDA(cudaMemsetAsync(status.p, 0, 16, s));
     // pointer tables: src32[B], src16[B], then mcap[B]
     std::vector<const void*> ptrs(2 * (size_t)B);
     for (int b = 0; b < B; ++b) {
@@ -666,7 +689,6 @@ BatchEngine::Result BatchEngine::decode_prepared(int B, int T, int maxM, const s
     MSB_CUDA(cudaMemsetAsync(hit.p, 0, (size_t)B * 4, s));
     MSB_CUDA(cudaMemsetAsync(amax.p, 0, (size_t)B * 8, s));
     MSB_CUDA(cudaMemsetAsync(pos.p, 0, 16, s));
-    MSB_CUDA(cudaMemsetAsync(status.p, 0, 16, s));
     DevBuf logit_buf;
     if (want_logits) logit_buf.ensure((size_t)T * B * c.vocab * 4);
     auto logits_at = [&](int step) -> float* {

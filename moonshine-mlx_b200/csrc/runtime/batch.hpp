@@ -11,7 +11,8 @@
 namespace msb {
 
 struct BatchEngine {
-    explicit BatchEngine(Model& model) : m(model) {}
+    // fp32 checkpoints (not forced to bf16) take split operands in every GEMM
+    explicit BatchEngine(Model& model) : m(model), split(!model.enc_bf16), esplit(!model.enc_bf16) {}
     ~BatchEngine();
 
     static constexpr int kKvPage = 16;  // positions per self-attention K/V page
@@ -43,6 +44,14 @@ struct BatchEngine {
     Result run_cross(const std::vector<CrossSrc>& src, const std::vector<int>& limits, bool forced,
                      float temperature = 0.f, unsigned seed = 0);
 
+    // One utterance through the tensor-core encoder (split operands for fp32 checkpoints):
+    // memory rows and cross K/V ([L][2][KVH][*m_cap][hd], fp32 and, with an fp16 KV cache,
+    // the fp16 copy) in this engine's buffers, for the batch-1 decode.  Returns the memory
+    // frames, or -1 when the dims do not fit the tensor-core encoder (the caller encodes on
+    // CUDA cores).
+    int encode_one(const float* audio_dev, int64_t n_samples, const float** cross32_out, const void** cross16_out,
+                   int* m_cap);
+
    private:
     struct LayerB {
         __nv_bfloat16 *wqkv, *wo, *wcq, *wco, *w1i, *w2;
@@ -51,7 +60,7 @@ struct BatchEngine {
         CUtensorMap m_qkv_lo, m_o_lo, m_cq_lo, m_co_lo, m_w1_lo, m_w2_lo;  // low planes (split)
     };
     Model& m;
-    bool split = false;  // fp32 checkpoint: split bf16 operands (fp32-level products)
+    bool split;  // fp32 checkpoint: split bf16 operands (fp32-level products)
     bool weights_ready = false;
     std::vector<DevBuf*> own;
     std::vector<LayerB> layers;
@@ -81,7 +90,7 @@ struct BatchEngine {
         CUtensorMap m_qkv_lo, m_o_lo, m_w1_lo, m_w2_lo;
     };
     bool enc_weights_ready = false;
-    bool esplit = false;  // fp32 checkpoint: the encoder GEMMs take split operands
+    bool esplit;  // fp32 checkpoint: the encoder GEMMs take split operands
     std::vector<EncLayerB> elayers;
     __nv_bfloat16 *elin = nullptr, *econv1 = nullptr, *econv2 = nullptr, *ecross = nullptr;
     CUtensorMap m_lin, m_conv1, m_conv2, m_ecross, m_lin_lo, m_conv1_lo, m_conv2_lo, m_ecross_lo;
