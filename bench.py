@@ -235,7 +235,7 @@ def _events(torch, stream):
     return a, b
 
 
-def leg_batched(mb, synth, root, torch, barrier, rank, reps=3):
+def leg_batched(mb, synth, root, torch, barrier, rank, local, reps=3):
     """ms_generate_batch on small bf16: 64 utterances of U(5, 15) s, 128 forced tokens each,
     host buffers in and out; CUDA events on the model's stream around the public call."""
     import numpy as np
@@ -246,7 +246,7 @@ def leg_batched(mb, synth, root, torch, barrier, rank, reps=3):
     brng = np.random.Generator(np.random.PCG64(7))
     blens = (brng.uniform(5, 15, size=64) * 16000).astype(int) // 80 * 80
     baudio = [synth.synth_audio(int(n), 100 + i) for i, n in enumerate(blens)]
-    bm = mb.MoonshineModel.load(bpath)
+    bm = mb.MoonshineModel.load(bpath, device=local)
     s = torch.cuda.ExternalStream(bm.cuda_stream)
     bm.generate_batch(baudio, forced_len=128)
     b_enc, b_dec, b_ms = [], [], []
@@ -289,7 +289,7 @@ def leg_sharded(mb, synth, root, torch, dist, barrier, rank, world, local, reps=
     order = sorted(share, key=lambda i: -int(lens[i]))
     groups = [order[k:k + sub_batch] for k in range(0, len(order), sub_batch)]
     audio = {i: synth.synth_audio(int(lens[i]), 1000 + i) for i in share}
-    m = mb.MoonshineModel.load(path)
+    m = mb.MoonshineModel.load(path, device=local)
     s = torch.cuda.ExternalStream(m.cuda_stream)
     m.generate_batch([audio[i] for i in groups[0]], forced_len=-1)   # warm-up: weights, graphs
     times, results = [], {}
@@ -346,7 +346,7 @@ def leg_streaming(mb, synth, torch, dist, barrier, rank, world, local, root, n_s
     barrier()
     path = synth.ensure_model_dir(root, ARCH, seed=WEIGHT_SEED)
     mine = list(range(rank, n_streams, world))
-    m = mb.MoonshineModel.load(path, kv_fp16=True)
+    m = mb.MoonshineModel.load(path, device=local, kv_fp16=True)
     s = torch.cuda.ExternalStream(m.cuda_stream)
     audio = {i: synth.synth_audio(n_chunks * chunk, 5000 + i) for i in mine}
     sc = mb.StreamingConfig(batch_decode=True)
@@ -579,7 +579,7 @@ def main():
         qm.close()
         barrier()
 
-    bleg = None if args.no_batched else leg_batched(mb, synth, root, torch, barrier, rank)
+    bleg = None if args.no_batched else leg_batched(mb, synth, root, torch, barrier, rank, local)
     barrier()
     sleg = None if args.no_sharded else leg_sharded(mb, synth, root, torch, dist, barrier, rank, world, local)
     barrier()

@@ -112,12 +112,24 @@ void StreamState::ensure_memory(int rows, cudaStream_t s) {
     if (rows <= mem_cap) return;
     const int cap = std::max(rows, std::max(2 * mem_cap, 256));
     grow_keep(memory, (size_t)memory_len * c.hidden * 4, (size_t)cap * c.hidden * 4, s);
-    const size_t n = (size_t)c.layers * 2 * c.kv_heads * cap * c.head_dim;
-    cross32.ensure(n * 4);
-    cross16.ensure(n * 2);
+    // the K/V layout [L][2][KVH][cap][hd] depends on the capacity: the rows kept move to the
+    // new pitch with one strided copy per buffer (no recomputation)
+    const size_t segs = (size_t)c.layers * 2 * c.kv_heads, hd = c.head_dim;
+    const size_t n = segs * cap * hd;
+    auto regrid = [&](DevBuf& b, size_t esz) {
+        void* p = nullptr;
+        MSB_CUDA(cudaMalloc(&p, n * esz));
+        if (b.p && memory_len > 0)
+            MSB_CUDA(cudaMemcpy2DAsync(p, (size_t)cap * hd * esz, b.p, (size_t)mem_cap * hd * esz,
+                                       (size_t)memory_len * hd * esz, segs, cudaMemcpyDeviceToDevice, s));
+        MSB_CUDA(cudaStreamSynchronize(s));
+        if (b.p) cudaFree(b.p);
+        b.p = p;
+        b.bytes = n * esz;
+    };
+    regrid(cross32, 4);
+    regrid(cross16, 2);
     mem_cap = cap;
-    // the K/V layout depends on the capacity: rebuild it for the rows kept
-    m.cross_kv_into(memory.as<float>(), memory_len, 0, cross32.as<float>(), cross16.p, mem_cap, s);
 }
 
 void StreamState::encode_new_frames(bool is_final, EncLane* lane) {  // MoonshineStreaming.swift:178-214

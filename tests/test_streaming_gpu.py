@@ -41,6 +41,18 @@ def test_stream_80ms_chunks_matches_oracle(model_root):
     assert em == ref_em
 
 
+@pytest.mark.parametrize("kv_fp16", [True, False])
+def test_stream_memory_growth_keeps_cross_kv(model_root, kv_fp16):
+    """7 s fed in 0.5 s chunks: the stream's memory passes its first capacity (256 frames)
+    and its cross K/V rows move to the larger layout; every call still matches the oracle."""
+    d = model_dir(model_root, "tiny")
+    audio = synth.synth_audio(16000 * 7, 35)
+    calls, em, ref_em = _run_both(d, audio, 8000, 16, {}, kv_fp16=kv_fp16, final=False)
+    for i, (g, r) in enumerate(calls):
+        assert list(g) == [r[0], r[1], r[2]], f"call {i}"
+    assert em == ref_em
+
+
 def test_stream_odd_chunks_and_fp32_kv(model_root):
     d = model_dir(model_root, "tiny")
     audio = synth.synth_audio(16000 + 777, 32)
