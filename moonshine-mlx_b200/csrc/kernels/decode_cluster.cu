@@ -94,9 +94,6 @@ enum SegId { SEG_QKV = 0, SEG_O, SEG_CQ, SEG_XKV, SEG_CO, SEG_FC1, SEG_FC2, SEG_
 constexpr int MAXB = 320;  // blocks per step a CTA's schedule may have (checked at launch)
 constexpr int FC2_MAXR = 1024;  // fc2 rows per block: a CTA's whole fc2 slice is one block for tiny
 constexpr int LM_ROWS = 32;     // fp32 LM rows per block (one full lane round of block_gemv)
-#ifndef MSB_LM_KEEP
-#define MSB_LM_KEEP -1.f
-#endif
 
 // Per-warp sums of the values in s and of their squares -> red[0][w], red[1][w] (the
 // LayerNorm statistics of the residual, gathered while it is written; a barrier must follow
@@ -389,7 +386,7 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
                         if (nr < 0) break;
                         const float* src = pbase + sp.off + (first ? 0 : sp.hdr + (size_t)row0 * sp.rf);
                         const uint32_t floats = (first ? sp.hdr : 0) + (uint32_t)nr * sp.rf;
-                        s_tab[tb][n++] = {src, nullptr, floats * 4 | (seg == SEG_LM ? 1u : 0u), 0u};
+                        s_tab[tb][n++] = {src, nullptr, floats * 4, 0u};
                         row0 += nr;
                         first = false;
                     }
@@ -403,21 +400,18 @@ __global__ void __launch_bounds__(NT, 1) decode_cluster_kernel(DecodeParams p, C
     // issue block n_iss of the whole launch (thread 0; nothing once failed or exhausted)
     const bool hint = gm.l2_keep > 0.f;
     const uint64_t l2pol = hint ? make_l2_policy(fminf(gm.l2_keep, 1.f)) : 0ull;
-    const uint64_t l2pol_lm = hint ? make_l2_policy(MSB_LM_KEEP > 0.f ? MSB_LM_KEEP : fminf(gm.l2_keep, 1.f)) : 0ull;
     auto issue_next = [&]() {
         if (n_iss >= n_total || s_failed) return;
         const BlockEnt e = n_iss < nb0 ? s_tab[0][n_iss] : s_tab[1][(n_iss - nb0) % nb1];
         const int slot = n_iss % NSLOT;
-        const uint32_t b0 = e.b0 & ~15u;  // bit 0: an LM-head block
-        const uint64_t pol = (e.b0 & 1u) ? l2pol_lm : l2pol;
-        mbar_expect_tx(&full[slot], b0 + e.b1);
+        mbar_expect_tx(&full[slot], e.b0 + e.b1);
         unsigned char* dst = ring + (size_t)slot * slot_bytes;
         if (hint) {
-            bulk_load_hint(dst, e.s0, b0, &full[slot], pol);
-            if (e.b1) bulk_load_hint(dst + b0, e.s1, e.b1, &full[slot], pol);
+            bulk_load_hint(dst, e.s0, e.b0, &full[slot], l2pol);
+            if (e.b1) bulk_load_hint(dst + e.b0, e.s1, e.b1, &full[slot], l2pol);
         } else {
-            bulk_load(dst, e.s0, b0, &full[slot]);
-            if (e.b1) bulk_load(dst + b0, e.s1, e.b1, &full[slot]);
+            bulk_load(dst, e.s0, e.b0, &full[slot]);
+            if (e.b1) bulk_load(dst + e.b0, e.s1, e.b1, &full[slot]);
         }
         ++n_iss;
     };
