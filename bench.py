@@ -336,7 +336,8 @@ def leg_streaming(mb, synth, torch, dist, barrier, rank, world, local, root, n_s
                   chunk=1280, max_tokens=16):
     """512 tiny fp32 streams (split over the ranks), 80 ms chunks, after every chunk
     transcribe(isFinal: false, maxTokens: 16) of every stream of the rank: one
-    ms_stream_transcribe_batch per chunk, whose decodes run in lockstep on the tensor cores
+    ms_stream_add_audio_batch and one ms_stream_transcribe_batch per chunk, whose encoders run
+    as one tensor-core pass and whose decodes run in lockstep on the tensor cores
     with split bf16 operands (fp32-level products for this fp32 checkpoint).  Per-chunk
     latency = the time of that call for the rank's streams (CUDA events); p50 / p99 over
     chunks and ranks."""
@@ -355,8 +356,7 @@ def leg_streaming(mb, synth, torch, dist, barrier, rank, world, local, root, n_s
     for st in warm:
         m.start_stream(st)
     for k in range(3):
-        for st, i in zip(warm, mine):
-            m.add_audio(st, audio[i][k * chunk:(k + 1) * chunk])
+        m.add_audio_batch(warm, [audio[i][k * chunk:(k + 1) * chunk] for i in mine])
         m.transcribe_batch(warm, is_final=False, streaming_config=sc, max_tokens=max_tokens)
     for st in warm:
         st.close()
@@ -371,8 +371,7 @@ def leg_streaming(mb, synth, torch, dist, barrier, rank, world, local, root, n_s
     for k in range(n_chunks):
         e0, e1 = _events(torch, s)
         e0.record(s)
-        for st, i in zip(states, mine):
-            m.add_audio(st, audio[i][k * chunk:(k + 1) * chunk])
+        m.add_audio_batch(states, [audio[i][k * chunk:(k + 1) * chunk] for i in mine])
         out = m.transcribe_batch(states, is_final=False, streaming_config=sc, max_tokens=max_tokens)
         e1.record(s)
         toks += sum(len(o[0]) for o in out)

@@ -306,10 +306,11 @@ ms_status ms_word_timings(const int32_t* jump_frames, int32_t n_jumps, const flo
 typedef struct {
     int32_t max_memory_frames;   /* default 100000 */
     int32_t min_segment_frames;  /* default 250 */
-    int32_t batch_decode;        /* ms_stream_transcribe_batch only (default 0): 1 decodes all
-                                    streams of one model in lockstep on tensor cores (the
+    int32_t batch_decode;        /* ms_stream_transcribe_batch only (default 0): 1 encodes the
+                                    new frames of all streams of one model in one tensor-core
+                                    pass and decodes them in lockstep on tensor cores (the
                                     batched engine; fp32 checkpoints keep fp32-level products,
-                                    bf16 ones bf16), so ids match a per-stream decode except
+                                    bf16 ones bf16), so ids match a per-stream call except
                                     where the top two logits are closer than that precision */
     float temperature;           /* transcribe(temperature:) (:122-128): 0 greedy (default);
                                     > 0 draws each token from softmax(logits / temperature)
@@ -329,6 +330,13 @@ ms_status ms_stream_start(ms_stream* stream);
 ms_status ms_stream_stop(ms_stream* stream);
 /* addAudio(_:chunk:) (:87-105). */
 ms_status ms_stream_add_audio(ms_stream* stream, const float* chunk, int64_t n_samples);
+
+/* addAudio of many streams at once (no counterpart in the reference, which feeds one stream
+ * per call): chunks[i] (n_samples[i] samples) goes to streams[i], with the same effect as n
+ * calls of ms_stream_add_audio.  When all streams share one model their frontends run
+ * concurrently on the model's CUDA streams, which is what serving many streams needs. */
+ms_status ms_stream_add_audio_batch(ms_stream* const* streams, int32_t n, const float* const* chunks,
+                                    const int64_t* n_samples);
 /* transcribe(_:isFinal:streamingConfig:maxTokens:temperature:) (:122-168).
  *   ids_out  ids of the current segment decode (the returned "text")
  *   hit_eos  the decode ended on EOS          (nullable)

@@ -772,6 +772,37 @@ ms_status ms_stream_add_audio(ms_stream* stream, const float* chunk, int64_t n_s
     });
 }
 
+ms_status ms_stream_add_audio_batch(ms_stream* const* streams, int32_t n, const float* const* chunks,
+                                    const int64_t* n_samples) {
+    return guarded([&]() -> ms_status {
+        if (!streams || n < 0 || (n > 0 && (!chunks || !n_samples))) return fail(MS_ERR_INVALID_ARG, "bad argument");
+        for (int32_t i = 0; i < n; ++i)
+            if (!streams[i] || n_samples[i] < 0 || (n_samples[i] > 0 && !chunks[i]))
+                return fail(MS_ERR_INVALID_ARG, "bad stream or chunk in batch");
+        Model* shared = n > 0 ? reinterpret_cast<StreamState*>(streams[0])->model : nullptr;
+        for (int32_t i = 1; i < n && shared; ++i)
+            if (reinterpret_cast<StreamState*>(streams[i])->model != shared) shared = nullptr;
+        if (!shared) {  // streams of several models: one at a time
+            for (int32_t i = 0; i < n; ++i) {
+                const ms_status st = ms_stream_add_audio(streams[i], chunks[i], n_samples[i]);
+                if (st != MS_OK) return st;
+            }
+            return MS_OK;
+        }
+        std::lock_guard<std::mutex> g(shared->mu);
+        MSB_CUDA(cudaSetDevice(shared->device));
+        // the streams' frontends run concurrently on the model's encoder lanes (each stream's
+        // buffers are its own); the model stream waits for all of them before its next work
+        const int lanes = std::min<int32_t>(n, 8);
+        shared->fork_lanes(lanes);
+        for (int32_t i = 0; i < n; ++i)
+            reinterpret_cast<StreamState*>(streams[i])->add_audio(chunks[i], n_samples[i],
+                                                                  shared->enc_lane(i % lanes).stream);
+        shared->join_lanes(lanes);
+        return MS_OK;
+    });
+}
+
 static ms_status transcribe_one(StreamState* s, int32_t is_final, const ms_streaming_config& sc,
                                 int32_t max_tokens, int32_t* ids_out, int32_t cap, int32_t* n_out,
                                 int32_t* hit_eos, int32_t* emitted) {
@@ -828,20 +859,45 @@ ms_status ms_stream_transcribe_batch(ms_stream* const* streams, int32_t n, int32
             std::vector<int64_t> lim(n);
             std::vector<BatchEngine::CrossSrc> src;
             std::vector<int> limits, rows;
-            const int lanes = std::min<int32_t>(n, 8);  // concurrent incremental encoders
-            shared->fork_lanes(lanes);
+            if (!shared->batch) shared->batch.reset(new BatchEngine(*shared));
+            BatchEngine& be = *shared->batch;
+            if (be.tc_encoder_fits() && shared->opts.weight_dtype != MS_W_F32) {
+                // every stream's new frames through one tensor-core encoder pass (split operands
+                // for fp32 checkpoints, bf16 for bf16 ones)
+                std::vector<StreamState::EncPlan> plan(n);
+                std::vector<char> has(n, 0);
+                std::vector<BatchEngine::StreamWindow> wins;
+                for (int32_t i = 0; i < n; ++i) {
+                    StreamState* s = reinterpret_cast<StreamState*>(streams[i]);
+                    s->note_call();
+                    has[i] = s->plan_new_frames(is_final != 0, &plan[i], shared->stream) ? 1 : 0;
+                    if (has[i])
+                        wins.push_back({s->window(plan[i]), plan[i].T, plan[i].off, plan[i].nnew, s->pos_offset,
+                                        s->memory_row()});
+                }
+                be.encode_windows(wins);
+                for (int32_t i = 0; i < n; ++i) {
+                    StreamState* s = reinterpret_cast<StreamState*>(streams[i]);
+                    if (has[i]) s->commit_new_frames(plan[i], shared->stream);
+                    lim[i] = s->decode_limit(is_final != 0, mt, &res[i]);
+                }
+            } else {
+                const int lanes = std::min<int32_t>(n, 8);  // concurrent incremental encoders
+                shared->fork_lanes(lanes);
+                for (int32_t i = 0; i < n; ++i)
+                    lim[i] = reinterpret_cast<StreamState*>(streams[i])
+                                 ->begin(is_final != 0, mt, &res[i], &shared->enc_lane(i % lanes));
+                shared->join_lanes(lanes);
+            }
             for (int32_t i = 0; i < n; ++i) {
                 StreamState* s = reinterpret_cast<StreamState*>(streams[i]);
-                lim[i] = s->begin(is_final != 0, mt, &res[i], &shared->enc_lane(i % lanes));
                 if (lim[i] > 0) {
                     src.push_back({s->cross32.as<float>(), s->cross16.p, s->mem_cap, s->memory_len});
                     limits.push_back((int)lim[i]);
                     rows.push_back(i);
                 }
             }
-            shared->join_lanes(lanes);
             if (!src.empty()) {
-                if (!shared->batch) shared->batch.reset(new BatchEngine(*shared));
                 // one seed for the lockstep batch: the rows (stream positions) separate the draws
                 unsigned seed = (unsigned)sc.seed;
                 if (sc.temperature > 0.f)

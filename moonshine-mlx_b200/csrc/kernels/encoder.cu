@@ -251,7 +251,80 @@ __global__ void ln_gather_rows_kernel(const float* __restrict__ x, int rows, int
     }
 }
 
+// Segment rows from per-segment sources: row t of segment b = src[b] + t * dim for t < T[b],
+// zeros for t in [T[b], seg_rows) (block (t, b), dim % 4 == 0, 16-byte aligned sources).
+__global__ void gather_seg_rows_kernel(const float* const* __restrict__ src, const int* __restrict__ T,
+                                       int seg_rows, int dim, float* __restrict__ out) {
+    const int t = blockIdx.x, b = blockIdx.y;
+    float4* o = reinterpret_cast<float4*>(out + ((size_t)b * seg_rows + t) * dim);
+    const bool has = t < T[b];
+    const float4* sr = has ? reinterpret_cast<const float4*>(src[b] + (size_t)t * dim) : nullptr;
+    for (int i = threadIdx.x; i < (dim >> 2); i += blockDim.x) o[i] = has ? sr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// Final encoder LayerNorm + positions of a window per segment, scattered to each segment's
+// own output: for i < cnt[b], row b * seg_rows + off[b] + i -> dst[b] + i * dim, adding
+// pos_emb[pos[b] + i] (one warp per (b, i); the arithmetic of ln_gather_rows_kernel).
+__global__ void ln_scatter_rows_kernel(const float* __restrict__ x, int nseg, int max_cnt, int seg_rows, int dim,
+                                       const float* __restrict__ w, float w_offset, float eps,
+                                       const float* __restrict__ pos_emb, const int* __restrict__ off,
+                                       const int* __restrict__ cnt, const int* __restrict__ pos,
+                                       float* const* __restrict__ dst) {
+    const int lane = threadIdx.x & 31;
+    const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (item >= nseg * max_cnt) return;
+    const int b = item / max_cnt, i = item - b * max_cnt;
+    if (i >= cnt[b]) return;
+    const float* xr = x + ((size_t)b * seg_rows + off[b] + i) * dim;
+    float v[LN_MAXV];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < LN_MAXV; ++j) {
+        const int k = lane + 32 * j;
+        v[j] = (k < dim) ? xr[k] : 0.f;
+        s += v[j];
+    }
+    const float mean = warp_sum(s) / (float)dim;
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < LN_MAXV; ++j) {
+        const int k = lane + 32 * j;
+        const float c = (k < dim) ? v[j] - mean : 0.f;
+        q += c * c;
+    }
+    const float rstd = rsqrtf(warp_sum(q) / (float)dim + eps);
+    float* o = dst[b] + (size_t)i * dim;
+    const float* pe = pos_emb + (size_t)(pos[b] + i) * dim;
+#pragma unroll
+    for (int j = 0; j < LN_MAXV; ++j) {
+        const int k = lane + 32 * j;
+        if (k < dim) o[k] = (v[j] - mean) * rstd * (w[k] + w_offset) + pe[k];
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_gather_seg_rows(const float* const* src, const int* T, int nseg, int seg_rows, int dim, float* out,
+                                   cudaStream_t stream) {
+    if (nseg <= 0 || seg_rows <= 0) return cudaSuccess;
+    if (dim % 4) return cudaErrorInvalidValue;
+    ++launch_counter();
+    gather_seg_rows_kernel<<<dim3(seg_rows, nseg), 128, 0, stream>>>(src, T, seg_rows, dim, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ln_scatter_rows(const float* x, int nseg, int max_cnt, int seg_rows, int dim, const float* w,
+                                   float w_offset, float eps, const float* pos_emb, const int* off, const int* cnt,
+                                   const int* pos, float* const* dst, cudaStream_t stream) {
+    if (nseg <= 0 || max_cnt <= 0) return cudaSuccess;
+    if (dim > 32 * LN_MAXV) return cudaErrorInvalidValue;
+    ++launch_counter();
+    const int wpb = 8, items = nseg * max_cnt;
+    ln_scatter_rows_kernel<<<(items + wpb - 1) / wpb, wpb * 32, 0, stream>>>(x, nseg, max_cnt, seg_rows, dim, w,
+                                                                           w_offset, eps, pos_emb, off, cnt, pos,
+                                                                           dst);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_frame_features(const float* audio, int n_frames, int frame_len,
                                   const float* log_k, const float* w, int dim, float* out,

@@ -198,6 +198,16 @@ cudaError_t launch_ln_gather_rows(const float* x, int rows, int seg_rows, int di
                                   float eps, const float* pos_emb, const int* len, const int* off, float* out,
                                   __nv_bfloat16* out_bf16, cudaStream_t stream, size_t lo_off = 0);
 
+// Segment rows gathered from per-segment device pointers (device arrays src[nseg], T[nseg]):
+// row t of segment b = src[b] + t * dim for t < T[b], zero rows up to seg_rows.
+cudaError_t launch_gather_seg_rows(const float* const* src, const int* T, int nseg, int seg_rows, int dim, float* out,
+                                   cudaStream_t stream);
+// Final encoder LayerNorm + pos_emb of cnt[b] rows of segment b starting at row off[b],
+// written to dst[b] (positions pos[b]..); device arrays of nseg entries.
+cudaError_t launch_ln_scatter_rows(const float* x, int nseg, int max_cnt, int seg_rows, int dim, const float* w,
+                                   float w_offset, float eps, const float* pos_emb, const int* off, const int* cnt,
+                                   const int* pos, float* const* dst, cudaStream_t stream);
+
 // ---------------------------------------------------------------- decoder
 struct DecodeLayerW {
     const float* wqkv;   // [3*d, d]  (q rows, k rows, v rows)

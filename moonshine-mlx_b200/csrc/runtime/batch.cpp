@@ -359,14 +359,98 @@ void BatchEngine::ensure_enc_weights() {
     enc_weights_ready = true;
 }
 
+// Encoder layers (MoonshineLayers.swift:297-310) over X = ex [rows3, e_hidden] in segments of
+// R3 rows; attention of segment s sees its first seg_len[s] rows only.  Uses eh, eqkv, eattn
+// and ef (grown here) and the encoder weights (split operands for fp32 checkpoints).
+void BatchEngine::encoder_layers_tc(size_t rows3, int R3, const int* seg_len) {
+    const Config& c = m.cfg;
+    const int ed = c.e_hidden, hd = c.e_head_dim, EI = c.e_inter;
+    const int eHD = c.e_heads * hd, QKV = (c.e_heads + 2 * c.e_kv_heads) * hd;
+    cudaStream_t s = m.stream;
+    const size_t P = esplit ? 2 : 1;
+    const size_t lo_h = esplit ? rows3 * ed : 0, lo_attn = esplit ? rows3 * eHD : 0, lo_f = esplit ? rows3 * EI : 0;
+    eh.ensure(rows3 * ed * 2 * P);
+    eqkv.ensure(rows3 * QKV * 4);
+    eattn.ensure(rows3 * eHD * 2 * P);
+    ef.ensure(rows3 * EI * 2 * P);
+    float* X = ex.as<float>();
+    auto amap = [&](CUtensorMap* hi, CUtensorMap* lo, const __nv_bfloat16* p, size_t rows, int K, size_t lo_off) {
+        make_a_map(hi, p, (int)rows, K);
+        if (esplit) make_a_map(lo, p + lo_off, (int)rows, K);
+    };
+    auto lo_of = [&](const CUtensorMap& mlo) { return esplit ? &mlo : nullptr; };
+    CUtensorMap a_h, a_attn, a_f, a_h_lo, a_attn_lo, a_f_lo;
+    amap(&a_h, &a_h_lo, eh.as<__nv_bfloat16>(), rows3, ed, lo_h);
+    amap(&a_attn, &a_attn_lo, eattn.as<__nv_bfloat16>(), rows3, eHD, lo_attn);
+    amap(&a_f, &a_f_lo, ef.as<__nv_bfloat16>(), rows3, EI, lo_f);
+    const CUtensorMap* h_lo = esplit ? &a_h_lo : nullptr;
+    const CUtensorMap* attn_lo = esplit ? &a_attn_lo : nullptr;
+    const CUtensorMap* f_lo = esplit ? &a_f_lo : nullptr;
+    const float scale = std::pow((float)hd, -0.5f);
+    for (int i = 0; i < c.e_layers; ++i) {
+        const EncLayer& L = m.enc[i];
+        const EncLayerB& E = elayers[i];
+        MSB_CUDA(launch_ln_bf16(X, (int)rows3, ed, L.ln_in, eh.as<__nv_bfloat16>(), s, 1.0f, lo_h));
+        {
+            TcGemmArgs ga;
+            ga.M = (int)rows3;
+            ga.N = QKV;
+            ga.ep.out = eqkv.as<float>();
+            ga.ep.ldc = QKV;
+            gemm(a_h, E.m_qkv, ga, ed, kBnWide, h_lo, lo_of(E.m_qkv_lo));
+        }
+        const auto w = c.window(i);
+        MSB_CUDA(launch_window_attention(eqkv.as<float>(), (int)rows3, c.e_heads, c.e_kv_heads, hd, w.first, w.second,
+                                         scale, nullptr, s, R3, seg_len, eattn.as<__nv_bfloat16>(), lo_attn));
+        {
+            TcGemmArgs ga;
+            ga.M = (int)rows3;
+            ga.N = ed;
+            ga.ep.out = X;
+            ga.ep.ldc = ed;
+            ga.ep.residual = X;
+            ga.ep.ldr = ed;
+            gemm(a_attn, E.m_o, ga, eHD, kBnWide, attn_lo, lo_of(E.m_o_lo));
+        }
+        MSB_CUDA(launch_ln_bf16(X, (int)rows3, ed, L.ln_post, eh.as<__nv_bfloat16>(), s, 1.0f, lo_h));
+        {
+            TcGemmArgs ga;
+            ga.M = (int)rows3;
+            ga.N = EI;
+            ga.ep.bias = L.b1;
+            ga.ep.act = ACT_GELU;
+            ga.out_bf16 = ef.as<__nv_bfloat16>();
+            ga.ldc_bf16 = EI;
+            ga.bf16_lo_off = lo_f;
+            gemm(a_h, E.m_w1, ga, ed, kBnWide, h_lo, lo_of(E.m_w1_lo));
+        }
+        {
+            TcGemmArgs ga;
+            ga.M = (int)rows3;
+            ga.N = ed;
+            ga.ep.bias = L.b2;
+            ga.ep.out = X;
+            ga.ep.ldc = ed;
+            ga.ep.residual = X;
+            ga.ep.ldr = ed;
+            gemm(a_f, E.m_w2, ga, EI, kBnWide, f_lo, lo_of(E.m_w2_lo));
+        }
+    }
+}
+
+bool BatchEngine::tc_encoder_fits() const {
+    const Config& c = m.cfg;
+    const int ed = c.e_hidden, fl = c.frame_len(), hd = c.e_head_dim;
+    const int eHD = c.e_heads * hd;
+    return !m.proj && ed == c.hidden && ed % 64 == 0 && eHD % 64 == 0 && c.e_inter % 64 == 0 && ed <= 1024 &&
+           hd <= 128 && hd % 4 == 0 && fl % 8 == 0 && fl <= 128;
+}
+
 bool BatchEngine::encode_tc(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
                             const std::vector<int>& off, const std::vector<int>& fr) {
     const Config& c = m.cfg;
-    const int ed = c.e_hidden, fl = c.frame_len(), d = c.hidden, hd = c.e_head_dim, EI = c.e_inter;
-    const int eHD = c.e_heads * hd, QKV = (c.e_heads + 2 * c.e_kv_heads) * hd;
-    if (m.proj || ed != d || ed % 64 || eHD % 64 || EI % 64 || ed > 1024 || hd > 128 || (hd & 3) || (fl & 7) ||
-        fl > 128)
-        return false;
+    const int ed = c.e_hidden, fl = c.frame_len(), d = c.hidden;
+    if (!tc_encoder_fits()) return false;
     const int B = (int)audio_dev.size();
     int T1max = 0;
     std::vector<int> T1(B);
@@ -387,18 +471,13 @@ bool BatchEngine::encode_tc(const std::vector<const float*>& audio_dev, const st
     // bf16 GEMM inputs hold a low plane right after the high one when split (lo_* elements on)
     const size_t P = esplit ? 2 : 1;
     const size_t lo_norm = esplit ? rows1 * fl : 0, lo_pad1 = esplit ? rows1 * ed : 0;
-    const size_t lo_pad2 = esplit ? rows2 * 2 * ed : 0, lo_h = esplit ? rows3 * ed : 0;
-    const size_t lo_attn = esplit ? rows3 * eHD : 0, lo_f = esplit ? rows3 * EI : 0;
+    const size_t lo_pad2 = esplit ? rows2 * 2 * ed : 0;
     const size_t lo_mem = esplit ? (size_t)Mc * d : 0;
     enorm.ensure(rows1 * fl * 2 * P);
     eaud.ensure((size_t)B * sizeof(float*));
     epad1.ensure(rows1 * ed * 2 * P);
     epad2.ensure(rows2 * 2 * ed * 2 * P);
     ex.ensure(rows3 * ed * 4);
-    eh.ensure(rows3 * ed * 2 * P);
-    eqkv.ensure(rows3 * QKV * 4);
-    eattn.ensure(rows3 * eHD * 2 * P);
-    ef.ensure(rows3 * EI * 2 * P);
     emem16.ensure((size_t)Mc * d * 2 * P);
     eseg.ensure((size_t)3 * B * 4);
     __nv_bfloat16* pad1 = epad1.as<__nv_bfloat16>();
@@ -489,63 +568,7 @@ bool BatchEngine::encode_tc(const std::vector<const float*>& audio_dev, const st
         conv(pad2, rows2, 2 * ed, lo_pad2, m_conv2, m_conv2_lo, B * R3, ed, ga);
     }
     // encoder layers over all B * R3 rows; attention stays inside each utterance's rows
-    CUtensorMap a_h, a_attn, a_f, a_h_lo, a_attn_lo, a_f_lo;
-    amap(&a_h, &a_h_lo, eh.as<__nv_bfloat16>(), rows3, ed, lo_h);
-    amap(&a_attn, &a_attn_lo, eattn.as<__nv_bfloat16>(), rows3, eHD, lo_attn);
-    amap(&a_f, &a_f_lo, ef.as<__nv_bfloat16>(), rows3, EI, lo_f);
-    const CUtensorMap* h_lo = esplit ? &a_h_lo : nullptr;
-    const CUtensorMap* attn_lo = esplit ? &a_attn_lo : nullptr;
-    const CUtensorMap* f_lo = esplit ? &a_f_lo : nullptr;
-    const float scale = std::pow((float)hd, -0.5f);
-    for (int i = 0; i < c.e_layers; ++i) {
-        const EncLayer& L = m.enc[i];
-        const EncLayerB& E = elayers[i];
-        MSB_CUDA(launch_ln_bf16(X, (int)rows3, ed, L.ln_in, eh.as<__nv_bfloat16>(), s, 1.0f, lo_h));
-        {
-            TcGemmArgs ga;
-            ga.M = (int)rows3;
-            ga.N = QKV;
-            ga.ep.out = eqkv.as<float>();
-            ga.ep.ldc = QKV;
-            gemm(a_h, E.m_qkv, ga, ed, kBnWide, h_lo, lo_of(E.m_qkv_lo));
-        }
-        const auto w = c.window(i);
-        MSB_CUDA(launch_window_attention(eqkv.as<float>(), (int)rows3, c.e_heads, c.e_kv_heads, hd, w.first, w.second,
-                                         scale, nullptr, s, R3, seg_len, eattn.as<__nv_bfloat16>(), lo_attn));
-        {
-            TcGemmArgs ga;
-            ga.M = (int)rows3;
-            ga.N = ed;
-            ga.ep.out = X;
-            ga.ep.ldc = ed;
-            ga.ep.residual = X;
-            ga.ep.ldr = ed;
-            gemm(a_attn, E.m_o, ga, eHD, kBnWide, attn_lo, lo_of(E.m_o_lo));
-        }
-        MSB_CUDA(launch_ln_bf16(X, (int)rows3, ed, L.ln_post, eh.as<__nv_bfloat16>(), s, 1.0f, lo_h));
-        {
-            TcGemmArgs ga;
-            ga.M = (int)rows3;
-            ga.N = EI;
-            ga.ep.bias = L.b1;
-            ga.ep.act = ACT_GELU;
-            ga.out_bf16 = ef.as<__nv_bfloat16>();
-            ga.ldc_bf16 = EI;
-            ga.bf16_lo_off = lo_f;
-            gemm(a_h, E.m_w1, ga, ed, kBnWide, h_lo, lo_of(E.m_w1_lo));
-        }
-        {
-            TcGemmArgs ga;
-            ga.M = (int)rows3;
-            ga.N = ed;
-            ga.ep.bias = L.b2;
-            ga.ep.out = X;
-            ga.ep.ldc = ed;
-            ga.ep.residual = X;
-            ga.ep.ldr = ed;
-            gemm(a_f, E.m_w2, ga, EI, kBnWide, f_lo, lo_of(E.m_w2_lo));
-        }
-    }
+    encoder_layers_tc(rows3, R3, seg_len);
     // prepareMemory: final norm + positions, gathered to the batch memory rows
     MSB_CUDA(launch_ln_gather_rows(X, (int)rows3, R3, ed, m.enc_final, 1.0f, 1e-5f, m.pos_emb, seg_len, seg_off,
                                    memory.as<float>(), emem16.as<__nv_bfloat16>(), s, lo_mem));
@@ -587,6 +610,52 @@ int BatchEngine::encode_one(const float* audio_dev, int64_t n_samples, const flo
     *cross16_out = m.kv_f16 ? cross16.p : cross32.p;
     *m_cap = Mc;
     return M;
+}
+
+bool BatchEngine::encode_windows(const std::vector<StreamWindow>& w) {
+    if (w.empty()) return true;
+    if (!tc_encoder_fits()) return false;
+    const Config& c = m.cfg;
+    const int ed = c.e_hidden, B = (int)w.size();
+    int R3 = 1, max_new = 1;
+    for (const auto& x : w) {
+        R3 = std::max(R3, x.T);
+        max_new = std::max(max_new, x.nnew);
+    }
+    const size_t rows3 = (size_t)B * R3;
+    ensure_enc_weights();
+    cudaStream_t s = m.stream;
+    ex.ensure(rows3 * ed * 4);
+    status.ensure(16);
+    // tables: src[B], dst[B] pointers, then T, off, cnt, pos
+    std::vector<unsigned char> tab((size_t)B * (2 * sizeof(void*) + 4 * sizeof(int)));
+    const void** srcp = reinterpret_cast<const void**>(tab.data());
+    void** dstp = reinterpret_cast<void**>(tab.data() + (size_t)B * sizeof(void*));
+    int* ints = reinterpret_cast<int*>(tab.data() + (size_t)2 * B * sizeof(void*));
+    for (int b = 0; b < B; ++b) {
+        srcp[b] = w[b].feat;
+        dstp[b] = w[b].dst;
+        ints[b] = w[b].T;
+        ints[B + b] = w[b].off;
+        ints[2 * B + b] = w[b].nnew;
+        ints[3 * B + b] = w[b].pos;
+    }
+    wtab.ensure(tab.size());
+    MSB_CUDA(cudaMemcpyAsync(wtab.p, tab.data(), tab.size(), cudaMemcpyHostToDevice, s));
+    MSB_CUDA(cudaMemsetAsync(status.p, 0, 16, s));
+    const char* t = reinterpret_cast<const char*>(wtab.p);
+    const float* const* src_d = reinterpret_cast<const float* const*>(t);
+    float* const* dst_d = reinterpret_cast<float* const*>(t + (size_t)B * sizeof(void*));
+    const int* T_d = reinterpret_cast<const int*>(t + (size_t)2 * B * sizeof(void*));
+    MSB_CUDA(launch_gather_seg_rows(src_d, T_d, B, R3, ed, ex.as<float>(), s));
+    encoder_layers_tc(rows3, R3, T_d);
+    MSB_CUDA(launch_ln_scatter_rows(ex.as<float>(), B, max_new, R3, ed, m.enc_final, 1.0f, 1e-5f, m.pos_emb, T_d + B,
+                                    T_d + 2 * B, T_d + 3 * B, dst_d, s));
+    unsigned st_word = 0;
+    MSB_CUDA(cudaMemcpyAsync(&st_word, status.p, 4, cudaMemcpyDeviceToHost, s));
+    MSB_CUDA(cudaStreamSynchronize(s));  // also: the host table is read
+    throw_device_status(st_word, "tensor-core stream encoder");
+    return true;
 }
 
 BatchEngine::Result BatchEngine::run(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,

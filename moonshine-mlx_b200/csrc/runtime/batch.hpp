@@ -52,6 +52,18 @@ struct BatchEngine {
     int encode_one(const float* audio_dev, int64_t n_samples, const float** cross32_out, const void** cross16_out,
                    int* m_cap);
 
+    // Incremental encoders of many streams in one pass (transcribe_batch): every stream's
+    // window of features goes through the encoder layers as one segment of the longest
+    // window's rows; the final norm + positions of its new rows land at its `dst`.  false
+    // when the dims do not fit the tensor-core encoder (the caller encodes stream by stream).
+    struct StreamWindow {
+        const float* feat;  // window rows [T, e_hidden]
+        int T, off, nnew, pos;
+        float* dst;         // the stream's memory at its current length
+    };
+    bool encode_windows(const std::vector<StreamWindow>& w);
+    bool tc_encoder_fits() const;  // the dims the tensor-core encoder supports
+
    private:
     struct LayerB {
         __nv_bfloat16 *wqkv, *wo, *wcq, *wco, *w1i, *w2;
@@ -84,6 +96,8 @@ struct BatchEngine {
     // rows.  false when the dims do not fit (the caller keeps the per-utterance path).
     bool encode_tc(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
                    const std::vector<int>& off, const std::vector<int>& fr);
+    void encoder_layers_tc(size_t rows3, int R3, const int* seg_len);
+    DevBuf wtab;  // device tables of encode_windows
     struct EncLayerB {
         __nv_bfloat16 *wqkv, *wo, *w1, *w2;
         CUtensorMap m_qkv, m_o, m_w1, m_w2;

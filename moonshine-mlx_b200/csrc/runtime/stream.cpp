@@ -37,6 +37,14 @@ StreamState::StreamState(Model* m) : model(m) {
     sample_buffer.assign((size_t)std::max(0, m->cfg.frame_len() - 1), 0.f);
 }
 
+StreamState::~StreamState() {
+    if (stage_done) {
+        cudaEventSynchronize(stage_done);
+        cudaEventDestroy(stage_done);
+    }
+    if (stage) cudaFreeHost(stage);
+}
+
 void StreamState::start() {  // MoonshineStreaming.swift:74-78
     active = true;
     reset_segment();
@@ -51,24 +59,37 @@ void StreamState::reset_segment() {  // MoonshineStreaming.swift:217-226
     last_hit_eos = false;
 }
 
-void StreamState::add_audio(const float* chunk, int64_t n) {  // MoonshineStreaming.swift:87-105
+void StreamState::add_audio(const float* chunk, int64_t n, cudaStream_t s_in) {  // MoonshineStreaming.swift:87-105
     Model& m = *model;
     const Config& c = m.cfg;
     const int fl = c.frame_len(), ed = c.e_hidden;
-    cudaStream_t s = m.stream;
-    std::vector<float> buf;
-    buf.reserve(sample_buffer.size() + (size_t)n);
-    buf.insert(buf.end(), sample_buffer.begin(), sample_buffer.end());
-    buf.insert(buf.end(), chunk, chunk + n);
-    const int64_t nf64 = (int64_t)buf.size() / fl;
-    const int64_t rem = (int64_t)buf.size() - nf64 * fl;
-    if (rem > 0) sample_buffer.assign(buf.end() - rem, buf.end());
-    else sample_buffer.clear();
-    if (nf64 == 0) return;
+    cudaStream_t s = s_in ? s_in : m.stream;
+    const size_t have = sample_buffer.size() + (size_t)n;
+    const int64_t nf64 = (int64_t)have / fl;
     if (nf64 > (1 << 24)) throw MsError(MS_ERR_INVALID_ARG, "audio chunk too long");
+    if (nf64 == 0) {  // everything stays in the remainder buffer
+        sample_buffer.insert(sample_buffer.end(), chunk, chunk + n);
+        return;
+    }
+    // leftover samples + the chunk, in page-locked memory the upload reads asynchronously
+    if (!stage_done) MSB_CUDA(cudaEventCreateWithFlags(&stage_done, cudaEventDisableTiming));
+    MSB_CUDA(cudaEventSynchronize(stage_done));  // the previous upload from it is done
+    if (have > stage_cap) {
+        if (stage) MSB_CUDA(cudaFreeHost(stage));
+        stage = nullptr;
+        const size_t cap = std::max(have, 2 * stage_cap);
+        MSB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&stage), cap * 4, cudaHostAllocDefault));
+        stage_cap = cap;
+    }
+    std::copy(sample_buffer.begin(), sample_buffer.end(), stage);
+    std::copy(chunk, chunk + n, stage + sample_buffer.size());
+    const int64_t rem = (int64_t)have - nf64 * fl;
+    sample_buffer.assign(stage + nf64 * fl, stage + have);
+    (void)rem;
     const int nf = (int)nf64;
     chunk_audio.ensure((size_t)nf * fl * 4);
-    MSB_CUDA(cudaMemcpyAsync(chunk_audio.p, buf.data(), (size_t)nf * fl * 4, cudaMemcpyHostToDevice, s));
+    MSB_CUDA(cudaMemcpyAsync(chunk_audio.p, stage, (size_t)nf * fl * 4, cudaMemcpyHostToDevice, s));
+    MSB_CUDA(cudaEventRecord(stage_done, s));
     const int T2 = (nf - 1) / 2 + 1, T3 = (T2 - 1) / 2 + 1;
     xin1.ensure((size_t)(4 + nf) * ed * 4);
     xin2.ensure((size_t)(4 + T2) * 2 * ed * 4);
@@ -132,49 +153,68 @@ void StreamState::ensure_memory(int rows, cudaStream_t s) {
     mem_cap = cap;
 }
 
-void StreamState::encode_new_frames(bool is_final, EncLane* lane) {  // MoonshineStreaming.swift:178-214
-    Model& m = *model;
-    const Config& c = m.cfg;
-    const EncBufs eb = lane ? lane->bufs() : m.own_enc_bufs();
-    const cudaStream_t s = lane ? lane->stream : m.stream;
-    if (feat_count <= 0) return;
+bool StreamState::plan_new_frames(bool is_final, EncPlan* p, cudaStream_t s) {  // MoonshineStreaming.swift:178-214
+    const Config& c = model->cfg;
+    if (feat_count <= 0) return false;
     const int total = feat_count;
     int look = 0;
     if (c.has_windows)
         for (auto& w : c.windows) look = std::max(look, w.second);
     const int stable = is_final ? total : std::max(0, total - look);
     const int nnew = stable - encoder_frames_emitted;
-    if (nnew <= 0) return;
+    if (nnew <= 0) return false;
     if (pos_offset + nnew > c.max_pos)
         throw MsError(MS_ERR_INVALID_ARG, "segment longer than the positional table");
     const int left_ctx = 16 * c.e_layers;
-    const int win_start = std::max(0, encoder_frames_emitted - left_ctx);
-    const int T = total - win_start;
-    const int ed = c.e_hidden;
-    eb.x->ensure((size_t)T * ed * 4);
-    float* x = eb.x->as<float>();
-    MSB_CUDA(cudaMemcpyAsync(x, features.as<float>() + (size_t)win_start * ed, (size_t)T * ed * 4,
-                             cudaMemcpyDeviceToDevice, s));
-    m.encoder_layers_on(eb, x, T, s);
-    const int off = encoder_frames_emitted - win_start;
+    p->win_start = std::max(0, encoder_frames_emitted - left_ctx);
+    p->T = total - p->win_start;
+    p->off = encoder_frames_emitted - p->win_start;
+    p->nnew = nnew;
+    p->stable = stable;
     ensure_memory(memory_len + nnew, s);
-    float* dst = memory.as<float>() + (size_t)memory_len * c.hidden;
+    return true;
+}
+
+const float* StreamState::window(const EncPlan& p) const {
+    return features.as<float>() + (size_t)p.win_start * model->cfg.e_hidden;
+}
+
+float* StreamState::memory_row() const { return memory.as<float>() + (size_t)memory_len * model->cfg.hidden; }
+
+void StreamState::commit_new_frames(const EncPlan& p, cudaStream_t s) {
+    Model& m = *model;
+    m.cross_kv_into(memory_row(), p.nnew, memory_len, cross32.as<float>(), cross16.p, mem_cap, s);
+    pos_offset += p.nnew;
+    encoder_frames_emitted = p.stable;
+    memory_len += p.nnew;
+}
+
+void StreamState::encode_new_frames(bool is_final, EncLane* lane) {  // MoonshineStreaming.swift:178-214
+    Model& m = *model;
+    const Config& c = m.cfg;
+    const EncBufs eb = lane ? lane->bufs() : m.own_enc_bufs();
+    const cudaStream_t s = lane ? lane->stream : m.stream;
+    EncPlan p;
+    if (!plan_new_frames(is_final, &p, s)) return;
+    const int ed = c.e_hidden;
+    eb.x->ensure((size_t)p.T * ed * 4);
+    float* x = eb.x->as<float>();
+    MSB_CUDA(cudaMemcpyAsync(x, window(p), (size_t)p.T * ed * 4, cudaMemcpyDeviceToDevice, s));
+    m.encoder_layers_on(eb, x, p.T, s);
+    float* dst = memory_row();
     if (m.proj) {
-        eb.memory->ensure((size_t)nnew * ed * 4);
-        MSB_CUDA(launch_layernorm_rows(x + (size_t)off * ed, nnew, ed, m.enc_final, 1.0f, 1e-5f, m.pos_emb,
+        eb.memory->ensure((size_t)p.nnew * ed * 4);
+        MSB_CUDA(launch_layernorm_rows(x + (size_t)p.off * ed, p.nnew, ed, m.enc_final, 1.0f, 1e-5f, m.pos_emb,
                                        pos_offset, eb.memory->as<float>(), s));
         GemmEpilogue e;
         e.out = dst;
         e.ldc = c.hidden;
-        MSB_CUDA(launch_gemm_f32(eb.memory->as<float>(), ed, m.proj, ed, nnew, c.hidden, ed, e, s));
+        MSB_CUDA(launch_gemm_f32(eb.memory->as<float>(), ed, m.proj, ed, p.nnew, c.hidden, ed, e, s));
     } else {
-        MSB_CUDA(launch_layernorm_rows(x + (size_t)off * ed, nnew, ed, m.enc_final, 1.0f, 1e-5f, m.pos_emb,
+        MSB_CUDA(launch_layernorm_rows(x + (size_t)p.off * ed, p.nnew, ed, m.enc_final, 1.0f, 1e-5f, m.pos_emb,
                                        pos_offset, dst, s));
     }
-    m.cross_kv_into(dst, nnew, memory_len, cross32.as<float>(), cross16.p, mem_cap, s);
-    pos_offset += nnew;
-    encoder_frames_emitted = stable;
-    memory_len += nnew;
+    commit_new_frames(p, s);
 }
 
 std::pair<std::vector<int32_t>, bool> StreamState::decode_memory(int32_t max_tokens, float temperature,
@@ -203,9 +243,13 @@ int64_t StreamState::begin(bool is_final, int32_t max_tokens, Result* done_early
     // MoonshineStreaming.swift:122-131
     ++calls;
     encode_new_frames(is_final, lane);
+    if (memory_len <= 0) MSB_CUDA(cudaStreamSynchronize(lane ? lane->stream : model->stream));
+    return decode_limit(is_final, max_tokens, done_early);
+}
+
+int64_t StreamState::decode_limit(bool is_final, int32_t max_tokens, Result* done_early) {
     if (memory_len <= 0) {
         if (is_final) reset_segment();
-        MSB_CUDA(cudaStreamSynchronize(lane ? lane->stream : model->stream));
         *done_early = Result();
         return 0;
     }

@@ -18,6 +18,11 @@ struct StreamState {
     bool have_conv1 = false, have_conv2 = false;
     DevBuf conv1_buf, conv2_buf;         // last 4 rows of the conv inputs
     DevBuf xin1, xin2, chunk_audio;      // per-chunk scratch
+    // page-locked staging of a chunk's frames, so its upload does not wait for the stream;
+    // stage_done marks when the last upload from it has finished
+    float* stage = nullptr;
+    size_t stage_cap = 0;
+    cudaEvent_t stage_done = nullptr;
     // accumulated encoder-input features [count, e_hidden]
     DevBuf features;
     int feat_count = 0, feat_cap = 0;
@@ -33,9 +38,13 @@ struct StreamState {
     uint32_t calls = 0;  // transcribe calls so far (separates the draws of successive calls)
 
     explicit StreamState(Model* m);
+    ~StreamState();
+    StreamState(const StreamState&) = delete;
+    StreamState& operator=(const StreamState&) = delete;
     void start();
     void stop() { active = false; }
-    void add_audio(const float* chunk, int64_t n);
+    // addAudio; `s` (nullable: the model's stream) is the CUDA stream the frontend runs on
+    void add_audio(const float* chunk, int64_t n, cudaStream_t s = nullptr);
     struct Result {
         std::vector<int32_t> ids;
         bool hit_eos = false;
@@ -47,6 +56,20 @@ struct StreamState {
     // the call is already complete); finish() applies the segment rules to the ids.
     // `lane` (nullable) runs the encoder on that lane's scratch and stream.
     int64_t begin(bool is_final, int32_t max_tokens, Result* done_early, EncLane* lane = nullptr);
+
+    // begin() split for encoding many streams' new frames in one batched pass:
+    // note_call(); plan_new_frames() (false: nothing new to encode); the caller encodes the
+    // window and writes the new memory rows at memory_row(); commit_new_frames(); then
+    // decode_limit() as begin() would return it.
+    struct EncPlan {
+        int win_start = 0, T = 0, off = 0, nnew = 0, stable = 0;
+    };
+    void note_call() { ++calls; }
+    bool plan_new_frames(bool is_final, EncPlan* p, cudaStream_t s);
+    const float* window(const EncPlan& p) const;
+    float* memory_row() const;
+    void commit_new_frames(const EncPlan& p, cudaStream_t s);
+    int64_t decode_limit(bool is_final, int32_t max_tokens, Result* done_early);
     Result finish(std::vector<int32_t> ids, bool hit_eos, bool is_final, const ms_streaming_config& sc);
 
    private:

@@ -126,6 +126,8 @@ def _load_lib() -> C.CDLL:
                                       C.POINTER(C.c_double), i32p]),
         "ms_alignment_jump_frames": (C.c_int, [f32p, C.c_int32, C.c_int32, i32p]),
         "ms_model_stream": (C.c_void_p, [P]),
+        "ms_stream_add_audio_batch": (C.c_int, [C.POINTER(C.c_void_p), C.c_int32, C.POINTER(C.POINTER(C.c_float)),
+                                          C.POINTER(C.c_int64)]),
         "ms_model_batch_kv_pages": (C.c_int, [P, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(C.c_int32)]),
         "ms_decode_memory_static": (C.c_int, [P, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
                                               i32p, i32p]),
@@ -627,6 +629,18 @@ class MoonshineModel:
     def add_audio(self, state: StreamingState, chunk) -> None:
         a = _f32(chunk)
         _check(_L().ms_stream_add_audio(state._h, _fptr(a), a.shape[0]))
+
+    def add_audio_batch(self, states: Sequence[StreamingState], chunks: Sequence) -> None:
+        """add_audio of chunks[i] to states[i] for every i in one call (the frontends of streams
+        of this model run concurrently)."""
+        arrs = [_f32(c) for c in chunks]
+        if len(arrs) != len(states):
+            raise ValueError("one chunk per stream")
+        B = len(arrs)
+        hs = (C.c_void_p * B)(*[s._h for s in states])
+        ptrs = (C.POINTER(C.c_float) * B)(*[_fptr(a) for a in arrs])
+        lens = (C.c_int64 * B)(*[a.shape[0] for a in arrs])
+        _check(_L().ms_stream_add_audio_batch(hs, B, ptrs, lens))
 
     def transcribe(self, state: StreamingState, is_final: bool = False,
                    streaming_config: Optional[StreamingConfig] = None,

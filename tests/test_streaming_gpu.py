@@ -96,9 +96,12 @@ def test_stream_batch_equals_single(model_root):
         m.start_stream(s)
     audios = [synth.synth_audio(6400, 40 + i) for i in range(3)]
     for off in range(0, 6400, 1280):
+        # the batched streams take their chunks in one add_audio_batch call (uneven sizes:
+        # the remainder buffers differ per stream), the single ones one call each
+        sizes = [1280 - 80 * i + (off // 1280) % 2 * 37 for i in range(3)]
+        m.add_audio_batch(streams, [audios[i][off:off + sizes[i]] for i in range(3)])
         for i in range(3):
-            m.add_audio(streams[i], audios[i][off:off + 1280])
-            m.add_audio(singles[i], audios[i][off:off + 1280])
+            m.add_audio(singles[i], audios[i][off:off + sizes[i]])
         got = m.transcribe_batch(streams, max_tokens=16)
         want = [m.transcribe(s, max_tokens=16) for s in singles]
         assert got == want
