@@ -364,7 +364,8 @@ template <int HDT, bool F16>
 __global__ void __launch_bounds__(XS_THREADS) cross_attn_stream_kernel(
     const float* __restrict__ qc, const void* __restrict__ src, const int* __restrict__ frame_off,
     const int* __restrict__ frames, int H, int KVH, int m_cap, int layer, float scale,
-    __nv_bfloat16* __restrict__ out, unsigned* status, size_t lo_off) {
+    __nv_bfloat16* __restrict__ out, unsigned* status, size_t lo_off, const void* const* __restrict__ rows_src,
+    const int* __restrict__ rows_cap) {
     pdl_wait();
     pdl_trigger();
     using S = XsShape<HDT, F16>;
@@ -381,10 +382,12 @@ __global__ void __launch_bounds__(XS_THREADS) cross_attn_stream_kernel(
     const int kvh = h / (H / KVH);
     const int M = frames[b];
     const int nchunks = (M + S::CH - 1) / S::CH;
-    const E* kg = reinterpret_cast<const E*>(src) +
-                  ((((size_t)layer * 2 + 0) * KVH + kvh) * m_cap + frame_off[b]) * HDT;
-    const E* vg = reinterpret_cast<const E*>(src) +
-                  ((((size_t)layer * 2 + 1) * KVH + kvh) * m_cap + frame_off[b]) * HDT;
+    // concatenated layout (frames from frame_off[b], pitch m_cap) or row b's own buffer
+    const E* base = reinterpret_cast<const E*>(rows_src ? rows_src[b] : src);
+    const size_t mc = rows_src ? (size_t)rows_cap[b] : (size_t)m_cap;
+    const size_t fo = rows_src ? 0 : (size_t)frame_off[b];
+    const E* kg = base + ((((size_t)layer * 2 + 0) * KVH + kvh) * mc + fo) * HDT;
+    const E* vg = base + ((((size_t)layer * 2 + 1) * KVH + kvh) * mc + fo) * HDT;
     auto issue = [&](int c) {
         const int st = c % XS_STAGES;
         const uint32_t bytes = (uint32_t)min(S::CH, M - c * S::CH) * S::ROWB;
@@ -504,7 +507,8 @@ __global__ void __launch_bounds__(XS_THREADS) cross_attn_stream_kernel(
 template <int HDT>
 cudaError_t launch_cross_stream(bool f16, const float* qc, const void* src, const int* frame_off, const int* frames,
                                 int B, int H, int KVH, int m_cap, int layer, float scale, __nv_bfloat16* out,
-                                unsigned* status, cudaStream_t s, size_t lo_off) {
+                                unsigned* status, cudaStream_t s, size_t lo_off, const void* const* rows_src,
+                                const int* rows_cap) {
     static bool attr_set = false;
     if (!attr_set) {  // both variants at once: the fp16 one is first launched inside a graph capture
         cudaError_t e = cudaFuncSetAttribute(cross_attn_stream_kernel<HDT, true>,
@@ -519,10 +523,10 @@ cudaError_t launch_cross_stream(bool f16, const float* qc, const void* src, cons
     if (f16)
         return launch_kernel(cross_attn_stream_kernel<HDT, true>, dim3(B * H), dim3(XS_THREADS),
                              xs_smem_bytes<HDT, true>(), s, qc, src, frame_off, frames, H, KVH, m_cap, layer, scale,
-                             out, status, lo_off);
+                             out, status, lo_off, rows_src, rows_cap);
     return launch_kernel(cross_attn_stream_kernel<HDT, false>, dim3(B * H), dim3(XS_THREADS),
                          xs_smem_bytes<HDT, false>(), s, qc, src, frame_off, frames, H, KVH, m_cap, layer, scale,
-                         out, status, lo_off);
+                         out, status, lo_off, rows_src, rows_cap);
 }
 
 // One thread per row b.  Decodes the packed argmax, applies the greedy-loop rules of
@@ -587,19 +591,23 @@ cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const
                                     const int* pos, const int* frame_off, const int* frames, int B, int H, int KVH,
                                     int hd, int m_cap, int layer, int max_frames, float scale, float* part,
                                     __nv_bfloat16* out, int first_step, unsigned* status, cudaStream_t s,
-                                    size_t lo_off) {
+                                    size_t lo_off, const CrossRows* rows) {
     if (hd > MAXHD_B || (hd & 1)) return cudaErrorInvalidValue;
-    if (first_step >= 0 && (hd == 32 || hd == 40 || hd == 48 || hd == 64)) {
+    if (rows && (first_step < 0 || !cross_rows_supported(hd) || !rows->src32 || !rows->src16 || !rows->cap))
+        return cudaErrorInvalidValue;
+    if (first_step >= 0 && cross_rows_supported(hd)) {
         // one CTA per (utterance, head); the first decoder call reads the fp32 copy
         const void* src = first_step ? (const void*)cross32 : cross_st;
         const bool f16 = !first_step && st_f16;
-        if ((reinterpret_cast<uintptr_t>(src) & 15) != 0 || !status) return cudaErrorInvalidValue;
+        const void* const* rsrc = rows ? (first_step ? rows->src32 : rows->src16) : nullptr;
+        const int* rcap = rows ? rows->cap : nullptr;
+        if ((!rows && (reinterpret_cast<uintptr_t>(src) & 15) != 0) || !status) return cudaErrorInvalidValue;
         ++launch_counter();
         switch (hd) {
-            case 32: return launch_cross_stream<32>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s, lo_off);
-            case 40: return launch_cross_stream<40>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s, lo_off);
-            case 48: return launch_cross_stream<48>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s, lo_off);
-            default: return launch_cross_stream<64>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s, lo_off);
+            case 32: return launch_cross_stream<32>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s, lo_off, rsrc, rcap);
+            case 40: return launch_cross_stream<40>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s, lo_off, rsrc, rcap);
+            case 48: return launch_cross_stream<48>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s, lo_off, rsrc, rcap);
+            default: return launch_cross_stream<64>(f16, qc, src, frame_off, frames, B, H, KVH, m_cap, layer, scale, out, status, s, lo_off, rsrc, rcap);
         }
     }
     // generic head_dim: chunk partials + combine, fp32/stored copy chosen on the device
@@ -611,6 +619,8 @@ cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const
     cross_combine_kernel<<<(B * H + 7) / 8, 256, 0, s>>>(part, B, H, hd, max_chunks, out, lo_off);
     return cudaGetLastError();
 }
+
+bool cross_rows_supported(int hd) { return hd == 32 || hd == 40 || hd == 48 || hd == 64; }
 
 cudaError_t launch_step_finalize(unsigned long long* amax, int B, int* pos, int* next_ids, int* ids_out, int t_cap,
                                  int* counts, const int* limits, int* done, int* hit_eos, int eos, int forced,

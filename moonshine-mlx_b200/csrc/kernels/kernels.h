@@ -300,11 +300,22 @@ cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv
 cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const PagedKv& kv, const int* pos, int B,
                                    int H, int KVH, int hd, float scale, __nv_bfloat16* out, cudaStream_t s,
                                    size_t lo_off = 0);
+// Per-row cross K/V read in place: row b's [layers][2][KVH][cap[b]][hd] at src32[b] (fp32) and
+// at src16[b] (the stored copy: fp16, or the fp32 rows again when the cache is fp32); device
+// tables, every pointer 16-byte aligned.  Needs a head_dim of 32, 40, 48 or 64.
+struct CrossRows {
+    const void* const* src32 = nullptr;
+    const void* const* src16 = nullptr;
+    const int* cap = nullptr;
+};
+// rows == nullptr: the concatenated layout [layers][2][KVH][m_cap][hd] at cross32 / cross_st,
+// row b's frames from frame_off[b]; otherwise rows (cross32, cross_st, frame_off, m_cap unused).
 cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const void* cross_st, int st_f16,
                                     const int* pos, const int* frame_off, const int* frames, int B, int H, int KVH,
                                     int hd, int m_cap, int layer, int max_frames, float scale, float* part,
                                     __nv_bfloat16* out, int first_step, unsigned* status, cudaStream_t s,
-                                    size_t lo_off = 0);
+                                    size_t lo_off = 0, const CrossRows* rows = nullptr);
+bool cross_rows_supported(int hd);
 cudaError_t launch_step_finalize(unsigned long long* amax, int B, int* pos, int* next_ids, int* ids_out, int t_cap,
                                  int* counts, const int* limits, int* done, int* hit_eos, int eos, int forced,
                                  cudaStream_t s);

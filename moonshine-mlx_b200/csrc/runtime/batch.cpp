@@ -274,7 +274,8 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
         MSB_CUDA(launch_cross_attn_batch(qc.as<float>(), cross32.as<float>(), m.kv_f16 ? cross16.p : cross32.p,
                                          m.kv_f16 ? 1 : 0, posp, frame_off.as<int>(), frames.as<int>(), B, H, KVH,
                                          hd, Mc, l, max_frames, scale, part.as<float>(), attn.as<__nv_bfloat16>(),
-                                         first ? 1 : 0, status.as<unsigned>(), s, lo_attn));
+                                         first ? 1 : 0, status.as<unsigned>(), s, lo_attn,
+                                         xrows_on ? &xrows : nullptr));
         {
             TcGemmArgs ga;
             ga.M = B;
@@ -717,13 +718,20 @@ BatchEngine::Result BatchEngine::run_cross(const std::vector<CrossSrc>& src, con
         maxM = std::max(maxM, fr[b]);
     }
     const int T = *std::max_element(limits.begin(), limits.end());
-    ensure_ws(B, T, Mtot, maxM);
+    // in place: the streams' buffers are read where they lie, so the engine holds no copy (the
+    // copy and its capacity would grow with the sum of every stream's memory)
+    const bool in_place = cross_rows_supported(c.head_dim);
+    for (int b = 0; b < B && in_place; ++b)
+        if ((reinterpret_cast<uintptr_t>(src[b].c32) & 15) || (m.kv_f16 && (reinterpret_cast<uintptr_t>(src[b].c16) & 15)))
+            throw MsError(MS_ERR_CUDA, "stream cross K/V not 16-byte aligned");
+    ensure_ws(B, T, in_place ? 0 : Mtot, maxM);
     MSB_CUDA(cudaMemsetAsync(status.p, 0, 16, s));
-    // pointer tables: src32[B], src16[B], then mcap[B]
+    // pointer tables: src32[B], src16[B] (the stored copy; the fp32 rows when the cache is
+    // fp32), then mcap[B]
     std::vector<const void*> ptrs(2 * (size_t)B);
     for (int b = 0; b < B; ++b) {
         ptrs[b] = src[b].c32;
-        ptrs[B + b] = m.kv_f16 ? src[b].c16 : nullptr;
+        ptrs[B + b] = m.kv_f16 ? src[b].c16 : (in_place ? src[b].c32 : nullptr);
     }
     xsrc.ensure((size_t)2 * B * sizeof(void*) + (size_t)B * 4);
     char* tab = reinterpret_cast<char*>(xsrc.p);
@@ -731,13 +739,27 @@ BatchEngine::Result BatchEngine::run_cross(const std::vector<CrossSrc>& src, con
     MSB_CUDA(cudaMemcpyAsync(tab + 2 * B * sizeof(void*), mcap.data(), (size_t)B * 4, cudaMemcpyHostToDevice, s));
     MSB_CUDA(cudaMemcpyAsync(frame_off.p, off.data(), (size_t)B * 4, cudaMemcpyHostToDevice, s));
     MSB_CUDA(cudaMemcpyAsync(frames.p, fr.data(), (size_t)B * 4, cudaMemcpyHostToDevice, s));
-    MSB_CUDA(launch_gather_cross(reinterpret_cast<const float* const*>(tab),
-                                 reinterpret_cast<const void* const*>(tab + B * sizeof(void*)),
-                                 reinterpret_cast<const int*>(tab + 2 * B * sizeof(void*)), frames.as<int>(),
-                                 frame_off.as<int>(), B, c.layers * 2 * c.kv_heads, c.head_dim, Mc,
-                                 cross32.as<float>(), m.kv_f16 ? cross16.p : nullptr, s));
+    if (in_place) {
+        xrows.src32 = reinterpret_cast<const void* const*>(tab);
+        xrows.src16 = reinterpret_cast<const void* const*>(tab + B * sizeof(void*));
+        xrows.cap = reinterpret_cast<const int*>(tab + 2 * B * sizeof(void*));
+    } else {
+        MSB_CUDA(launch_gather_cross(reinterpret_cast<const float* const*>(tab),
+                                     reinterpret_cast<const void* const*>(tab + B * sizeof(void*)),
+                                     reinterpret_cast<const int*>(tab + 2 * B * sizeof(void*)), frames.as<int>(),
+                                     frame_off.as<int>(), B, c.layers * 2 * c.kv_heads, c.head_dim, Mc,
+                                     cross32.as<float>(), m.kv_f16 ? cross16.p : nullptr, s));
+    }
     MSB_CUDA(cudaEventRecord(m.ev[1], s));
-    return decode_prepared(B, T, maxM, off, fr, limits, forced, false);
+    xrows_on = in_place;
+    try {
+        Result r = decode_prepared(B, T, maxM, off, fr, limits, forced, false);
+        xrows_on = false;
+        return r;
+    } catch (...) {
+        xrows_on = false;
+        throw;
+    }
 }
 
 BatchEngine::Result BatchEngine::decode_prepared(int B, int T, int maxM, const std::vector<int>& off,

@@ -116,6 +116,10 @@ struct BatchEngine {
     Result decode_prepared(int B, int T, int maxM, const std::vector<int>& off, const std::vector<int>& fr,
                            const std::vector<int>& limits, bool forced, bool want_logits);
     DevBuf xsrc;  // device pointer tables of run_cross
+    // run_cross: the cross attention reads every stream's own cross K/V through these tables
+    // (no copy into cross32 / cross16) when the head size has the streamed kernel
+    CrossRows xrows;
+    bool xrows_on = false;
     void ensure_ws(int B, int T, int Mtot, int maxM);
     void enqueue_step(int B, int max_frames, bool forced, bool first, float* logits);
     float inv_temp = 0.f;  // sampling state of the current run

@@ -19,13 +19,15 @@ namespace msb {
 namespace {
 
 // Grow `b` to `new_bytes`, keeping its first `keep_bytes` (device-to-device copy).
+// Growth of a stream's buffers is stream-ordered (cudaMallocAsync / cudaFreeAsync on the
+// stream that uses them): many streams growing at the same chunk neither synchronise the
+// device nor wait for fresh allocations from the driver.
 void grow_keep(DevBuf& b, size_t keep_bytes, size_t new_bytes, cudaStream_t s) {
     if (new_bytes <= b.bytes) return;
     void* p = nullptr;
-    MSB_CUDA(cudaMalloc(&p, new_bytes));
+    MSB_CUDA(cudaMallocAsync(&p, new_bytes, s));
     if (b.p && keep_bytes) MSB_CUDA(cudaMemcpyAsync(p, b.p, keep_bytes, cudaMemcpyDeviceToDevice, s));
-    MSB_CUDA(cudaStreamSynchronize(s));
-    if (b.p) cudaFree(b.p);
+    if (b.p) MSB_CUDA(cudaFreeAsync(b.p, s));
     b.p = p;
     b.bytes = new_bytes;
 }
@@ -139,12 +141,11 @@ void StreamState::ensure_memory(int rows, cudaStream_t s) {
     const size_t n = segs * cap * hd;
     auto regrid = [&](DevBuf& b, size_t esz) {
         void* p = nullptr;
-        MSB_CUDA(cudaMalloc(&p, n * esz));
+        MSB_CUDA(cudaMallocAsync(&p, n * esz, s));
         if (b.p && memory_len > 0)
             MSB_CUDA(cudaMemcpy2DAsync(p, (size_t)cap * hd * esz, b.p, (size_t)mem_cap * hd * esz,
                                        (size_t)memory_len * hd * esz, segs, cudaMemcpyDeviceToDevice, s));
-        MSB_CUDA(cudaStreamSynchronize(s));
-        if (b.p) cudaFree(b.p);
+        if (b.p) MSB_CUDA(cudaFreeAsync(b.p, s));
         b.p = p;
         b.bytes = n * esz;
     };
