@@ -12,6 +12,7 @@
 //   cross_attn_batch    generic head_dim: (b, head, 32-key chunk) partials over b's frames
 //   cross_combine       merge the chunk partials -> bf16 attention rows
 //   step_finalize       per-row argmax -> ids, EOS / limit bookkeeping, next ids, t + 1
+#include <algorithm>
 #include <type_traits>
 
 #include "common.cuh"
@@ -22,12 +23,25 @@ namespace msb {
 namespace {
 
 constexpr int CHB = 32;
+constexpr int SA_WARPS = 4;  // batched self attention: warps per (row, head), key chunks interleaved
 constexpr int MAXHD_B = 64;
 
-__global__ void embed_rows_kernel(const int* __restrict__ ids, const float* __restrict__ embed, int d, int B,
-                                  int V, float* __restrict__ x, unsigned* status) {
+// Sum over the block (128 threads) in a fixed order; every thread gets the total.
+__device__ __forceinline__ float block_sum128(float v, float* red) {
+    v = warp_sum(v);
+    __syncthreads();  // red is free (earlier readers are done)
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    return (red[0] + red[1]) + (red[2] + red[3]);
+}
+
+__global__ void __launch_bounds__(128) embed_rows_kernel(const int* __restrict__ ids, const float* __restrict__ embed,
+                                                         int d, int B, int V, float* __restrict__ x, unsigned* status,
+                                                         __nv_bfloat16* __restrict__ xb, size_t lo_off,
+                                                         float2* __restrict__ stats, int stats_ld, int tile_n) {
     pdl_wait();
     pdl_trigger();
+    __shared__ float red[4];
     const int b = blockIdx.x;
     if (b >= B) return;
     int id = ids[b];
@@ -36,7 +50,26 @@ __global__ void embed_rows_kernel(const int* __restrict__ ids, const float* __re
         id = 0;
     }
     const float* e = embed + (size_t)id * d;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) x[(size_t)b * d + i] = e[i];
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        const float v = e[i];
+        x[(size_t)b * d + i] = v;
+        if (xb) st_bf16_split(xb + (size_t)b * d + i, v, lo_off);
+    }
+    if (stats) {  // (mean, M2) per column tile, two passes (block-uniform loop)
+        for (int t0 = 0; t0 < d; t0 += tile_n) {
+            const int nc = min(tile_n, d - t0);
+            float s = 0.f;
+            for (int i = threadIdx.x; i < nc; i += blockDim.x) s += e[t0 + i];
+            const float mean = block_sum128(s, red) / (float)nc;
+            float q = 0.f;
+            for (int i = threadIdx.x; i < nc; i += blockDim.x) {
+                const float a = e[t0 + i] - mean;
+                q += a * a;
+            }
+            q = block_sum128(q, red);
+            if (threadIdx.x == 0) stats[(size_t)(t0 / tile_n) * stats_ld + b] = make_float2(mean, q);
+        }
+    }
 }
 
 __global__ void ln_bf16_kernel(const float* __restrict__ x, int rows, int d, const float* __restrict__ w,
@@ -123,18 +156,39 @@ __device__ __forceinline__ float load_kv(const void* base, size_t idx, int f16) 
     return f16 ? __half2float(reinterpret_cast<const __half*>(base)[idx]) : reinterpret_cast<const float*>(base)[idx];
 }
 
-// One warp per (b, h), eight per CTA.  Lanes own keys for the scores (each reads its key row
-// in 16-byte loads against q staged in shared memory), dims (2c, 2c+1) for the V sum.  Keys
-// 0..t-1 come from row b's pages (a key without a page -- a row past its own limit -- is
-// skipped), key t is this step's fp32 K/V.
-__global__ void self_attn_batch_kernel(const float* __restrict__ q, const float* __restrict__ kv_new,
-                                       const PagedKv kv, const int* __restrict__ pos, int B, int H, int KVH, int hd,
-                                       float scale, __nv_bfloat16* __restrict__ out, size_t lo_off) {
+// One CTA of SA_WARPS warps per (b, h).  Keys come in rounds of SaShape::KEYS: every thread
+// first copies its share of the round's cached K and V rows (from row b's pages; a key
+// without a page -- a row past its own limit -- is skipped) into shared memory with 16-byte
+// cp.async, so a round costs one memory round trip; then warp w scores keys
+// [w KW, (w + 1) KW) of the round (lanes own keys, rows read in 16-byte pieces against q
+// staged in shared memory), keeps an online softmax and accumulates V with lane c owning
+// dims (2c, 2c+1).  Key t is this step's fp32 K/V.  The warp states are merged in warp order.
+template <bool F16>
+struct SaShape {
+    static constexpr int ESZ = F16 ? 2 : 4;
+    static constexpr int KEYS = F16 ? 128 : 64;  // keys per round
+    static constexpr int KW = KEYS / SA_WARPS;   // keys per warp per round (<= 32)
+};
+// shared-memory row of hd elements: an odd number of 16-byte pieces, so the eight lanes of
+// one 128-bit phase reading eight different rows hit different bank groups
+__host__ __device__ constexpr int sa_row_pieces(int hd, int esz) { return ((hd * esz) / 16) | 1; }
+template <bool F16>
+constexpr size_t sa_smem_bytes() {
+    return (size_t)2 * SaShape<F16>::KEYS * sa_row_pieces(MAXHD_B, SaShape<F16>::ESZ) * 16;
+}
+
+template <bool F16>
+__global__ void __launch_bounds__(SA_WARPS * 32) self_attn_batch_kernel(
+    const float* __restrict__ q, const float* __restrict__ kv_new, const PagedKv kv, const int* __restrict__ pos,
+    int B, int H, int KVH, int hd, float scale, __nv_bfloat16* __restrict__ out, size_t lo_off) {
+    using S = SaShape<F16>;
+    using E = typename std::conditional<F16, __half, float>::type;
     pdl_wait();
     pdl_trigger();
-    const int lane = threadIdx.x & 31;
-    const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (item >= B * H) return;
+    extern __shared__ __align__(16) unsigned char sa_raw[];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int item = blockIdx.x;
+    if (item >= B * H) return;  // whole CTA
     const int b = item / H, h = item - b * H;
     const int kvh = h / (H / KVH);
     const int t = *pos;
@@ -146,99 +200,120 @@ __global__ void self_attn_batch_kernel(const float* __restrict__ q, const float*
     const size_t koff = (size_t)kv.layer_off + (size_t)kvh * kv.page * hd;
     const size_t voff = koff + (size_t)KVH * kv.page * hd;
     const int* tab = kv.table + (size_t)b * kv.table_stride;
-    // this head's q, staged once per warp and read back as broadcast float4s
-    __shared__ __align__(16) float qsh[8][MAXHD_B];
-    float* qw = qsh[(threadIdx.x >> 5) & 7];
-    for (int c = lane; c < hd; c += 32) qw[c] = qr[c];
-    __syncwarp();
+    const E* pool = reinterpret_cast<const E*>(kv.pool);
+    const int npc = hd * S::ESZ / 16;                 // 16-byte pieces per row
+    const int rse = sa_row_pieces(hd, S::ESZ) * 16 / S::ESZ;  // shared row stride (elements)
+    E* ks = reinterpret_cast<E*>(sa_raw);
+    E* vs = ks + (size_t)S::KEYS * rse;
+    // this head's q, staged once and read back as broadcast float4s
+    __shared__ __align__(16) float qw[MAXHD_B];
+    __shared__ float wm[SA_WARPS], wl[SA_WARPS];
+    __shared__ float wacc[SA_WARPS][MAXHD_B];
+    for (int c = threadIdx.x; c < hd; c += blockDim.x) qw[c] = qr[c];
     const float4* q4 = reinterpret_cast<const float4*>(qw);
+    // pool element offset of cached key j's row, or -1 (no page)
+    auto row_of = [&](int j) -> long long {
+        const int lp = j / kv.page;
+        const int phys = lp < kv.table_stride ? tab[lp] : -1;
+        return phys >= 0 ? (long long)phys * kv.page_elems + (long long)(j % kv.page) * hd : -1ll;
+    };
     float m = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f;
-    for (int j0 = 0; j0 <= t; j0 += CHB) {
-        const int nk = min(CHB, t + 1 - j0);
-        const int j = j0 + lane;
-        float s = -INFINITY;
-        // element offset of key j's row inside the pool (-1: no key)
-        long long rowe = -1;
-        if (lane < nk && j < t) {
-            const int lp = j / kv.page;
-            const int phys = lp < kv.table_stride ? tab[lp] : -1;
-            if (phys >= 0) rowe = (long long)phys * kv.page_elems + (long long)(j % kv.page) * hd;
+    for (int base = 0; base <= t; base += S::KEYS) {
+        const int ncached = max(0, min(S::KEYS, t - base));  // keys base .. base + ncached - 1 < t
+        __syncthreads();  // the previous round's rows are consumed (and q is staged)
+        for (int i = threadIdx.x; i < 2 * ncached * npc; i += blockDim.x) {
+            const int kvsel = i >= ncached * npc, ii = kvsel ? i - ncached * npc : i;
+            const int jj = ii / npc, pc = ii - jj * npc;
+            const long long re = row_of(base + jj);
+            if (re < 0) continue;
+            const E* src = pool + (kvsel ? voff : koff) + re + (size_t)pc * (16 / S::ESZ);
+            E* dst = (kvsel ? vs : ks) + (size_t)jj * rse + (size_t)pc * (16 / S::ESZ);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src) : "memory");
         }
-        if (lane < nk && (j == t || rowe >= 0)) {
-            // the lane's key row in 16-byte loads (hd % 8 == 0: rows start 16-byte aligned)
-            float dot = 0.f;
+        asm volatile("cp.async.commit_group;\ncp.async.wait_all;\n" ::: "memory");
+        __syncthreads();
+        const int k0 = base + w * S::KW;  // this warp's keys k0 .. k0 + KW - 1 (<= t)
+        const int nk = max(0, min(S::KW, t + 1 - k0));
+        if (nk == 0) continue;  // warp-uniform; the barrier of the next round is still taken
+        const int j = k0 + lane;
+        float s = -INFINITY;
+        bool valid = false;
+        if (lane < nk) {
             if (j == t) {
+                float dot = 0.f;
                 const float4* k4 = reinterpret_cast<const float4*>(fk);
                 for (int p = 0; p < hd / 4; ++p) {
                     const float4 kk = k4[p], qq = q4[p];
                     dot = fmaf(qq.x, kk.x, fmaf(qq.y, kk.y, fmaf(qq.z, kk.z, fmaf(qq.w, kk.w, dot))));
                 }
-            } else if (kv.kv_f16) {
-                const uint4* k8 = reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(kv.pool) + koff + rowe);
-#pragma unroll 4
-                for (int p = 0; p < hd / 8; ++p) {
-                    const uint4 u = k8[p];
-                    const __half2* h2 = reinterpret_cast<const __half2*>(&u);
-                    const float4 qa = q4[2 * p], qb = q4[2 * p + 1];
-                    const float2 f0 = __half22float2(h2[0]), f1 = __half22float2(h2[1]);
-                    const float2 f2 = __half22float2(h2[2]), f3 = __half22float2(h2[3]);
-                    dot = fmaf(qa.x, f0.x, fmaf(qa.y, f0.y, fmaf(qa.z, f1.x, fmaf(qa.w, f1.y, dot))));
-                    dot = fmaf(qb.x, f2.x, fmaf(qb.y, f2.y, fmaf(qb.z, f3.x, fmaf(qb.w, f3.y, dot))));
+                s = dot * scale;
+                valid = true;
+            } else if (row_of(j) >= 0) {
+                float dot = 0.f;
+                const E* kr = ks + (size_t)(j - base) * rse;
+                if constexpr (F16) {
+                    for (int p = 0; p < hd / 8; ++p) {
+                        const uint4 u = *reinterpret_cast<const uint4*>(kr + 8 * p);
+                        const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+                        const float4 qa = q4[2 * p], qb = q4[2 * p + 1];
+                        const float2 f0 = __half22float2(h2[0]), f1 = __half22float2(h2[1]);
+                        const float2 f2 = __half22float2(h2[2]), f3 = __half22float2(h2[3]);
+                        dot = fmaf(qa.x, f0.x, fmaf(qa.y, f0.y, fmaf(qa.z, f1.x, fmaf(qa.w, f1.y, dot))));
+                        dot = fmaf(qb.x, f2.x, fmaf(qb.y, f2.y, fmaf(qb.z, f3.x, fmaf(qb.w, f3.y, dot))));
+                    }
+                } else {
+                    for (int p = 0; p < hd / 4; ++p) {
+                        const float4 kk = *reinterpret_cast<const float4*>(kr + 4 * p), qq = q4[p];
+                        dot = fmaf(qq.x, kk.x, fmaf(qq.y, kk.y, fmaf(qq.z, kk.z, fmaf(qq.w, kk.w, dot))));
+                    }
                 }
-            } else {
-                const float4* k4 = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kv.pool) + koff + rowe);
-#pragma unroll 4
-                for (int p = 0; p < hd / 4; ++p) {
-                    const float4 kk = k4[p], qq = q4[p];
-                    dot = fmaf(qq.x, kk.x, fmaf(qq.y, kk.y, fmaf(qq.z, kk.z, fmaf(qq.w, kk.w, dot))));
-                }
+                s = dot * scale;
+                valid = true;
             }
-            s = dot * scale;
         }
-        const float mc = warp_max(s);
-        const float mn = fmaxf(m, mc);
-        const float p = (s != -INFINITY) ? expf(s - mn) : 0.f;
+        const float mn = fmaxf(m, warp_max(s));
+        const float p = valid ? expf(s - mn) : 0.f;
         const float corr = (m == -INFINITY) ? 0.f : expf(m - mn);
         l = l * corr + warp_sum(p);
         a0 *= corr;
         a1 *= corr;
-        // V rows of this chunk's keys, VU at a time: all loads of a group are issued before
-        // their products are summed (in key order), so their latencies overlap
-        constexpr int VU = 8;
         const int c = 2 * lane;
-        for (int g0 = 0; g0 < nk; g0 += VU) {
-            float2 vv[VU];
-            float pp[VU];
-#pragma unroll
-            for (int u = 0; u < VU; ++u) {
-                const int jj = g0 + u;
-                pp[u] = __shfl_sync(FULL, p, jj & 31);
-                const long long re = __shfl_sync(FULL, rowe, jj & 31);
-                const int row = j0 + jj;
-                vv[u] = make_float2(0.f, 0.f);
-                if (jj < nk && c < hd && (row == t || re >= 0)) {
-                    if (row == t) vv[u] = make_float2(fv[c], fv[c + 1]);
-                    else if (kv.kv_f16)
-                        vv[u] = __half22float2(
-                            *reinterpret_cast<const __half2*>(reinterpret_cast<const __half*>(kv.pool) + voff + re + c));
-                    else
-                        vv[u] = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(kv.pool) + voff + re + c);
-                } else {
-                    pp[u] = 0.f;
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < VU; ++u) {
-                a0 = fmaf(pp[u], vv[u].x, a0);
-                a1 = fmaf(pp[u], vv[u].y, a1);
-            }
+        for (int u = 0; u < nk; ++u) {
+            const float pu = __shfl_sync(FULL, p, u);
+            if (pu == 0.f || c >= hd) continue;
+            float2 v;
+            if (k0 + u == t) v = make_float2(fv[c], fv[c + 1]);
+            else if constexpr (F16)
+                v = __half22float2(*reinterpret_cast<const __half2*>(vs + (size_t)(k0 + u - base) * rse + c));
+            else v = *reinterpret_cast<const float2*>(vs + (size_t)(k0 + u - base) * rse + c);
+            a0 = fmaf(pu, v.x, a0);
+            a1 = fmaf(pu, v.y, a1);
         }
         m = mn;
     }
-    const int c = 2 * lane;
-    if (c < hd) {
-        st_bf16_split(out + (size_t)b * HD + h * hd + c, a0 / l, lo_off);
-        st_bf16_split(out + (size_t)b * HD + h * hd + c + 1, a1 / l, lo_off);
+    // merge the warps' softmax states in warp order
+    if (lane == 0) {
+        wm[w] = m;
+        wl[w] = l;
+    }
+    if (2 * lane < hd) {
+        wacc[w][2 * lane] = a0;
+        wacc[w][2 * lane + 1] = a1;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < hd; e += blockDim.x) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int qq = 0; qq < SA_WARPS; ++qq) mx = fmaxf(mx, wm[qq]);
+        float lsum = 0.f, o = 0.f;
+#pragma unroll
+        for (int qq = 0; qq < SA_WARPS; ++qq) {
+            if (wm[qq] == -INFINITY) continue;
+            const float f = expf(wm[qq] - mx);
+            lsum = fmaf(wl[qq], f, lsum);
+            o = fmaf(wacc[qq][e], f, o);
+        }
+        st_bf16_split(out + (size_t)b * HD + h * hd + e, o / lsum, lo_off);
     }
 }
 
@@ -559,9 +634,12 @@ __global__ void step_finalize_kernel(unsigned long long* amax, int B, int* pos, 
 }  // namespace
 
 cudaError_t launch_embed_rows(const int* ids, const float* embed, int d, int B, int V, float* x, unsigned* status,
-                              cudaStream_t s) {
+                              cudaStream_t s, __nv_bfloat16* xb, size_t lo_off, float2* stats, int stats_ld,
+                              int tile_n) {
+    if (stats && (tile_n <= 0 || stats_ld < B)) return cudaErrorInvalidValue;
     ++launch_counter();
-    return launch_kernel(embed_rows_kernel, dim3(B), dim3(128), 0, s, ids, embed, d, B, V, x, status);
+    return launch_kernel(embed_rows_kernel, dim3(B), dim3(128), 0, s, ids, embed, d, B, V, x, status, xb, lo_off,
+                         stats, stats_ld, tile_n);
 }
 
 cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv_bfloat16* out, cudaStream_t s,
@@ -582,9 +660,11 @@ cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const Pa
                                    size_t lo_off) {
     if (hd > MAXHD_B || (hd & 7) || !kv.table || kv.page <= 0 || !kv.pool) return cudaErrorInvalidValue;
     ++launch_counter();
-    const int items = B * H;
-    return launch_kernel(self_attn_batch_kernel, dim3((items + 7) / 8), dim3(256), 0, s, q, kv_new, kv, pos, B, H,
-                         KVH, hd, scale, out, lo_off);
+    if (kv.kv_f16)
+        return launch_kernel(self_attn_batch_kernel<true>, dim3(B * H), dim3(SA_WARPS * 32), sa_smem_bytes<true>(), s,
+                             q, kv_new, kv, pos, B, H, KVH, hd, scale, out, lo_off);
+    return launch_kernel(self_attn_batch_kernel<false>, dim3(B * H), dim3(SA_WARPS * 32), sa_smem_bytes<false>(), s, q,
+                         kv_new, kv, pos, B, H, KVH, hd, scale, out, lo_off);
 }
 
 cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const void* cross_st, int st_f16,
@@ -669,12 +749,33 @@ namespace {
 // dst row r = src row r (interleave == 0) or, for the SwiGLU fc1, dst row 2j = src row j
 // (value) and dst row 2j+1 = src row j + interleave (gate).
 __global__ void f32_to_bf16_rows_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, int rows,
-                                        int K, int interleave, size_t lo_off) {
+                                        int K, int interleave, size_t lo_off, const float* __restrict__ colscale) {
     const int r = blockIdx.x;
     if (r >= rows) return;
     const int sr = interleave ? ((r & 1) ? interleave + (r >> 1) : (r >> 1)) : r;
-    for (int k = threadIdx.x; k < K; k += blockDim.x)
-        st_bf16_split(dst + (size_t)r * K + k, src[(size_t)sr * K + k], lo_off);
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const float v = src[(size_t)sr * K + k];
+        st_bf16_split(dst + (size_t)r * K + k, colscale ? v * colscale[k] : v, lo_off);
+    }
+}
+// One block of 256 threads per row: strided double partial sums, then a fixed tree.
+__global__ void bf16_row_sums_kernel(const __nv_bfloat16* __restrict__ w, int K, size_t lo_off,
+                                     float* __restrict__ out) {
+    __shared__ double red[256];
+    const int r = blockIdx.x;
+    const __nv_bfloat16* row = w + (size_t)r * K;
+    double s = 0.0;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        s += (double)__bfloat162float(row[k]);
+        if (lo_off) s += (double)__bfloat162float(row[lo_off + k]);
+    }
+    red[threadIdx.x] = s;
+    __syncthreads();
+    for (int o = 128; o > 0; o >>= 1) {
+        if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) out[r] = (float)red[0];
 }
 __global__ void interleave_f32_kernel(const float* __restrict__ src, float* __restrict__ dst, int n2, int half) {
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
@@ -683,9 +784,17 @@ __global__ void interleave_f32_kernel(const float* __restrict__ src, float* __re
 }  // namespace
 
 cudaError_t launch_f32_to_bf16_rows(const float* src, __nv_bfloat16* dst, int rows, int K, int interleave,
-                                    cudaStream_t s, size_t lo_off) {
+                                    cudaStream_t s, size_t lo_off, const float* colscale) {
     ++launch_counter();
-    f32_to_bf16_rows_kernel<<<rows, 256, 0, s>>>(src, dst, rows, K, interleave, lo_off);
+    f32_to_bf16_rows_kernel<<<rows, 256, 0, s>>>(src, dst, rows, K, interleave, lo_off, colscale);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_bf16_row_sums(const __nv_bfloat16* w, int rows, int K, size_t lo_off, float* out,
+                                 cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    ++launch_counter();
+    bf16_row_sums_kernel<<<rows, 256, 0, s>>>(w, K, lo_off, out);
     return cudaGetLastError();
 }
 

@@ -38,6 +38,7 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;         // bf16: 128 bytes = one 128B-swizzle row
 constexpr int TC_THREADS = 128;
+static_assert(BM == TC_THREADS, "one thread per tile row (folded LayerNorm statistics)");
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2) {
@@ -157,10 +158,10 @@ __host__ __device__ constexpr int tile_ld() { return BN + 4; }
 // n = n0 + 4 (t mod BN/4) .. n + 3 for every row it visits, so column-only terms (bias,
 // RoPE angles, K/V scatter base) are loaded once, and the BN/4 threads of a row write one
 // contiguous row segment with 128-bit accesses.  N is a multiple of 4 (checked at launch).
-// Rows [r_lo, r_hi) of the tile.
+// Rows [r_lo, r_hi) of the tile; lnr (folded LayerNorm) holds each tile row's (mean, rstd).
 template <int BN, int MODE>
 __device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* tile, int m0, int n0, int r_lo,
-                                              int r_hi) {
+                                              int r_hi, const float2* lnr) {
     constexpr int TPR = BN / 4;            // threads per row
     constexpr int RPP = TC_THREADS / TPR;  // rows per pass
     constexpr int LDS = tile_ld<BN>();
@@ -177,6 +178,8 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* 
     if constexpr (MODE == TC_EPI_STD || MODE == TC_EPI_SWIGLU || MODE == TC_EPI_ACCUM) {
         if (ep.bias && col_ok) bias = *reinterpret_cast<const float4*>(ep.bias + n);
     }
+    float4 csum = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (lnr && col_ok) csum = *reinterpret_cast<const float4*>(g.lnf.csum + n);
     // K/V scatter: column part of the cache index (the four columns share one head)
     size_t kv_col = 0;
     if constexpr (MODE == TC_EPI_STD) {
@@ -223,6 +226,11 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* 
         const int m = m0 + r;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (ok) v = *reinterpret_cast<const float4*>(tile + (size_t)r * LDS + c);
+        if (lnr && ok) {
+            const float2 st = lnr[r];
+            v = make_float4((v.x - st.x * csum.x) * st.y, (v.y - st.x * csum.y) * st.y,
+                            (v.z - st.x * csum.z) * st.y, (v.w - st.x * csum.w) * st.y);
+        }
         if constexpr (MODE == TC_EPI_STD) {
             if (ok) {
                 v = add4(v, bias);
@@ -240,9 +248,27 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* 
                 }
             }
         } else if constexpr (MODE == TC_EPI_ACCUM) {
+            float4 nv = make_float4(0.f, 0.f, 0.f, 0.f);
             if (ok) {
                 float4* o = reinterpret_cast<float4*>(ep.out + (size_t)m * ep.ldc + n);
-                *o = add4(*o, add4(v, bias));
+                nv = add4(*o, add4(v, bias));
+                *o = nv;
+                if (g.out_bf16) st_bf16x4_split(g.out_bf16 + (size_t)m * g.ldc_bf16 + n, nv, g.bf16_lo_off);
+            }
+            if (g.stats_out) {  // (mean, M2) of the row's updated values over this tile's columns
+                float sx = (nv.x + nv.y) + (nv.z + nv.w);
+#pragma unroll
+                for (int o = TPR / 2; o > 0; o >>= 1) sx += __shfl_xor_sync(FULL, sx, o);
+                const float mean = sx / (float)min(BN, g.N - n0);
+                float q = 0.f;
+                if (ok) {
+                    const float a = nv.x - mean, b = nv.y - mean, e = nv.z - mean, f = nv.w - mean;
+                    q = (a * a + b * b) + (e * e + f * f);
+                }
+#pragma unroll
+                for (int o = TPR / 2; o > 0; o >>= 1) q += __shfl_xor_sync(FULL, q, o);
+                if ((t % TPR) == 0 && r < rows)
+                    g.stats_out[(size_t)blockIdx.x * g.stats_ld + m] = make_float2(mean, q);
             }
         } else if constexpr (MODE == TC_EPI_SWIGLU) {
             if (ok) {  // columns (value, gate, value, gate) -> two outputs
@@ -444,10 +470,33 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                 *reinterpret_cast<float4*>(my + c0 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
         }
     }
+    // folded LayerNorm: (mean, rstd) of every tile row from the producer's column-tile
+    // statistics (the producer finished before pdl_wait returned)
+    __shared__ float2 s_lnr[BM];
+    const float2* lnr = nullptr;
+    if constexpr (MODE != TC_EPI_ACCUM) {
+        if (g.lnf.stats) {
+            lnr = s_lnr;
+            const int r = threadIdx.x;
+            if (r < rows) {
+                const TcLnFold& f = g.lnf;
+                float na = 0.f, mean = 0.f, m2 = 0.f;
+                for (int q = 0; q < f.ntiles; ++q) {
+                    const float2 st = f.stats[(size_t)q * f.ld + m0 + r];
+                    const float nb = (float)min(f.tile_n, f.K - q * f.tile_n);
+                    const float nn = na + nb, delta = st.x - mean;
+                    mean += delta * (nb / nn);
+                    m2 += st.y + delta * delta * (na * nb / nn);
+                    na = nn;
+                }
+                s_lnr[r] = make_float2(mean, rsqrtf(m2 / (float)f.K + 1e-5f));
+            }
+        }
+    }
     __syncthreads();
     const int S = (int)gridDim.z;
     if (S == 1) {
-        if (ok) epilogue_tile<BN, MODE>(g, tile, m0, n0, 0, rows);
+        if (ok) epilogue_tile<BN, MODE>(g, tile, m0, n0, 0, rows, lnr);
     } else {
         // every split of the tile has staged its partial (barriers taken by all CTAs, also
         // after a failure, so none is left waiting)
@@ -470,7 +519,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             }
         }
         cluster_barrier();  // every CTA has read the partials it needs from its peers
-        if (!any_fail) epilogue_tile<BN, MODE>(g, tile, m0, n0, lo, hi);
+        if (!any_fail) epilogue_tile<BN, MODE>(g, tile, m0, n0, lo, hi, lnr);
     }
     // drain copies still in flight after a failure (bounded), then free tensor memory
     if (warp == 0 && lane == 0 && s_fail) {
@@ -561,10 +610,18 @@ cudaError_t launch_tc_mode(const CUtensorMap& map_a, const CUtensorMap& map_b, c
 }
 
 // The epilogue moves four columns per thread with 128-bit (fp32) / 64-bit (bf16, fp16)
-// accesses: every output it touches must allow that.
+// accesses: every output it touches must allow that.  A folded LayerNorm needs statistics
+// tiles that cover exactly its K inputs and a row sum per column.
 bool epilogue_layout_ok(const TcGemmArgs& g) {
     const GemmEpilogue& ep = g.ep;
     if (g.N % 4) return false;
+    if (g.stats_out && g.mode != TC_EPI_ACCUM) return false;
+    if (g.lnf.stats) {
+        const TcLnFold& f = g.lnf;
+        if (!f.csum || !aligned(f.csum, 16) || f.tile_n <= 0 || f.ntiles <= 0 || f.ld < g.M || f.K <= 0 ||
+            (f.ntiles - 1) * f.tile_n >= f.K || f.ntiles * f.tile_n < f.K)
+            return false;
+    }
     switch (g.mode) {
         case TC_EPI_STD:
             if (ep.bias && !aligned(ep.bias, 16)) return false;
@@ -576,6 +633,9 @@ bool epilogue_layout_ok(const TcGemmArgs& g) {
             if (g.out_bf16 && (g.ldc_bf16 % 4 || !aligned(g.out_bf16, 8))) return false;
             return true;
         case TC_EPI_ACCUM:
+            if (g.lnf.stats) return false;
+            if (g.stats_out && g.stats_ld < g.M) return false;
+            if (g.out_bf16 && (g.ldc_bf16 % 4 || !aligned(g.out_bf16, 8))) return false;
             return ep.out && ep.ldc % 4 == 0 && aligned(ep.out, 16) && (!ep.bias || aligned(ep.bias, 16));
         case TC_EPI_SWIGLU:
             return g.out_bf16 && g.ldc_bf16 % 2 == 0 && aligned(g.out_bf16, 4) && (!ep.bias || aligned(ep.bias, 16));

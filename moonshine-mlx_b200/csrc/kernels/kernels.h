@@ -124,6 +124,18 @@ struct TcRopeKv {
 };
 
 constexpr int TC_MAX_SPLITS = 8;  // portable cluster size
+// LayerNorm folded into the GEMM that consumes it (batched decoder): B holds W[n][k] * w[k]
+// (w the LayerNorm weight) and csum[n] is the sum of that stored row, so row m of
+// LN(x) W^T = rstd_m (x_m . W'_n - mean_m csum[n]) with A the raw residual x.  The row
+// statistics come from the kernel that last wrote the residual, as (mean, M2) pairs of
+// column tiles of tile_n columns (stats[t * ld + m]), merged here in tile order
+// (Chan, Golub and LeVeque 1979); eps 1e-5.
+struct TcLnFold {
+    const float2* stats = nullptr;
+    const float* csum = nullptr;  // [N]
+    int ntiles = 0, tile_n = 0, ld = 0, K = 0;
+};
+
 struct TcGemmArgs {
     int M = 0, N = 0;
     int taps = 1, kb_per_tap = 0, k_per_tap = 0;
@@ -140,6 +152,11 @@ struct TcGemmArgs {
     size_t bf16_lo_off = 0;               // != 0: out_bf16 (STD, SWIGLU) also gets the bf16 of the
                                           // remainder v - bf16(v) this many elements further on
     TcRopeKv rope;
+    TcLnFold lnf;                         // stats != null: LayerNorm folded in (STD, ROPE_KV,
+                                          // SWIGLU, ARGMAX), applied before the mode's epilogue
+    float2* stats_out = nullptr;          // ACCUM: (mean, M2) of each updated residual row over
+    int stats_ld = 0;                     //   this tile's columns at [blockIdx.x * stats_ld + m];
+                                          //   out_bf16 (+ bf16_lo_off) gets its bf16 planes
     unsigned long long* argmax = nullptr; // [M] packed (ordered value, ~column) maxima
     float inv_temp = 0.f;                 // ARGMAX: 0 greedy, else maxima of logit * inv_temp + Gumbel
     unsigned seed = 0;                    //   noise of (seed, step + (row << 20), column);
@@ -291,8 +308,12 @@ struct DecodeParams {
 };
 
 // ---------------------------------------------------------------- batched decode step
+// x[b] = embed[ids[b]]; with xb also its bf16 planes (xb [B][d], low plane lo_off further),
+// and with stats the (mean, M2) of each row over column tiles of tile_n at
+// stats[t * stats_ld + b] (the layout TcGemmArgs::lnf reads).
 cudaError_t launch_embed_rows(const int* ids, const float* embed, int d, int B, int V, float* x, unsigned* status,
-                              cudaStream_t s);
+                              cudaStream_t s, __nv_bfloat16* xb = nullptr, size_t lo_off = 0,
+                              float2* stats = nullptr, int stats_ld = 0, int tile_n = 0);
 // The bf16 outputs below take an optional lo_off: != 0 also writes the low plane of a split
 // operand (bf16 of v - bf16(v)) lo_off elements after each value.
 cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv_bfloat16* out, cudaStream_t s,
@@ -319,8 +340,14 @@ bool cross_rows_supported(int hd);
 cudaError_t launch_step_finalize(unsigned long long* amax, int B, int* pos, int* next_ids, int* ids_out, int t_cap,
                                  int* counts, const int* limits, int* done, int* hit_eos, int eos, int forced,
                                  cudaStream_t s);
+// colscale (optional, [K]): each row times colscale[k] before rounding (a LayerNorm weight
+// folded into the GEMM that consumes it).
 cudaError_t launch_f32_to_bf16_rows(const float* src, __nv_bfloat16* dst, int rows, int K, int interleave,
-                                    cudaStream_t s, size_t lo_off = 0);
+                                    cudaStream_t s, size_t lo_off = 0, const float* colscale = nullptr);
+// out[r] = sum over k of row r of a bf16 matrix [rows][K] (plus its low plane lo_off further,
+// when lo_off != 0), accumulated in double in a fixed order.
+cudaError_t launch_bf16_row_sums(const __nv_bfloat16* w, int rows, int K, size_t lo_off, float* out,
+                                 cudaStream_t s);
 cudaError_t launch_interleave_f32(const float* src, float* dst, int n2, int half, cudaStream_t s);
 size_t cross_batch_part_floats(int B, int H, int hd, int max_frames);
 // Per-row cross K/V ([segs][mcap[b]][hd] at src32[b] / src16[b], device pointer arrays) into

@@ -12,6 +12,7 @@ namespace msb {
 namespace {
 constexpr int kBnNarrow = 64;   // q|k|v and cross-q projections (more CTAs for small N)
 constexpr int kBnWide = 128;
+constexpr int kStatTile = kBnWide;  // residual statistics tiles: the N tiles of the ACCUM GEMMs
 
 void make_b_map(CUtensorMap* map, const __nv_bfloat16* w, int N, int K, int bn) {
     if (!tc_make_map_2d(map, w, (uint64_t)K, (uint64_t)N, (uint64_t)K * 2, (uint32_t)bn))
@@ -68,28 +69,35 @@ void BatchEngine::ensure_weights() {
     // use one bf16 plane
     // bf16 copy of src [rows, K] (rows interleaved value/gate when `il`), its weight map and,
     // when split, the low plane right behind it with its own map
-    auto weight = [&](const float* src, int rows, int K, int il, int bn, CUtensorMap* hi, CUtensorMap* lo) {
+    // With a LayerNorm weight `lnw` the rows are stored times lnw[k] (the LayerNorm folds into
+    // the GEMM) and *csum gets each stored row's sum.
+    auto weight = [&](const float* src, int rows, int K, int il, int bn, CUtensorMap* hi, CUtensorMap* lo,
+                      const float* lnw = nullptr, float** csum = nullptr) {
         const size_t n = (size_t)rows * K;
         __nv_bfloat16* w = alloc<__nv_bfloat16>(split ? 2 * n : n);
-        MSB_CUDA(launch_f32_to_bf16_rows(src, w, rows, K, il, s, split ? n : 0));
+        MSB_CUDA(launch_f32_to_bf16_rows(src, w, rows, K, il, s, split ? n : 0, lnw));
         make_b_map(hi, w, rows, K, bn);
         if (split) make_b_map(lo, w + n, rows, K, bn);
+        if (csum) {
+            *csum = alloc<float>((size_t)rows);
+            MSB_CUDA(launch_bf16_row_sums(w, rows, K, split ? n : 0, *csum, s));
+        }
         return w;
     };
     layers.resize(c.layers);
     for (int l = 0; l < c.layers; ++l) {
         const DecodeLayerW& W = m.dec[l];
         LayerB& B = layers[l];
-        B.wqkv = weight(W.wqkv, HD + 2 * KVD, d, 0, kBnNarrow, &B.m_qkv, &B.m_qkv_lo);
+        B.wqkv = weight(W.wqkv, HD + 2 * KVD, d, 0, kBnNarrow, &B.m_qkv, &B.m_qkv_lo, W.ln1, &B.cs_qkv);
         B.wo = weight(W.wo, d, HD, 0, kBnWide, &B.m_o, &B.m_o_lo);
-        B.wcq = weight(W.wcq, HD, d, 0, kBnNarrow, &B.m_cq, &B.m_cq_lo);
+        B.wcq = weight(W.wcq, HD, d, 0, kBnNarrow, &B.m_cq, &B.m_cq_lo, W.ln2, &B.cs_cq);
         B.wco = weight(W.wco, d, HD, 0, kBnWide, &B.m_co, &B.m_co_lo);
-        B.w1i = weight(W.w1, 2 * I, d, I, kBnWide, &B.m_w1, &B.m_w1_lo);
+        B.w1i = weight(W.w1, 2 * I, d, I, kBnWide, &B.m_w1, &B.m_w1_lo, W.ln3, &B.cs_w1);
         B.w2 = weight(W.w2, d, I, 0, kBnWide, &B.m_w2, &B.m_w2_lo);
         B.b1i = alloc<float>((size_t)2 * I);
         MSB_CUDA(launch_interleave_f32(W.b1, B.b1i, 2 * I, I, s));
     }
-    lm = weight(m.lm_head, c.vocab, d, 0, kBnWide, &m_lm, &m_lm_lo);
+    lm = weight(m.lm_head, c.vocab, d, 0, kBnWide, &m_lm, &m_lm_lo, m.dec_norm, &cs_lm);
     MSB_CUDA(cudaStreamSynchronize(s));
     weights_ready = true;
 }
@@ -118,6 +126,7 @@ void BatchEngine::ensure_ws(int B, int T, int Mtot, int maxM) {
         hit.ensure((size_t)Bc * 4);
         frame_off.ensure((size_t)Bc * 4);
         frames.ensure((size_t)Bc * 4);
+        lnst.ensure((size_t)((d + kStatTile - 1) / kStatTile) * Bc * sizeof(float2));
     }
     // capacities grow by half again at least, so a workload that grows a little per call
     // (streams whose memories lengthen every chunk) reallocates rarely
@@ -219,7 +228,28 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
     const CUtensorMap* attn_lo = split ? &a_attn_lo : nullptr;
     const CUtensorMap* g_lo = split ? &a_g_lo : nullptr;
     auto wlo = [&](const CUtensorMap& mlo) { return split ? &mlo : nullptr; };
-    MSB_CUDA(launch_embed_rows(next_ids.as<int>(), m.embed, d, B, c.vocab, X, status.as<unsigned>(), s));
+    // LayerNorms folded into their consumers: the GEMMs after LN1, LN2, LN3 and the final
+    // norm read the residual's bf16 planes (hb) and the statistics of its rows (lnst), which
+    // the embedding and every residual update (ACCUM GEMM) write
+    const int ntiles = (d + kStatTile - 1) / kStatTile;
+    float2* st = lnst.as<float2>();
+    auto fold = [&](TcGemmArgs& ga, const float* csum) {
+        ga.lnf.stats = st;
+        ga.lnf.csum = csum;
+        ga.lnf.ntiles = ntiles;
+        ga.lnf.tile_n = kStatTile;
+        ga.lnf.ld = Bc;
+        ga.lnf.K = d;
+    };
+    auto update = [&](TcGemmArgs& ga) {
+        ga.out_bf16 = hb.as<__nv_bfloat16>();
+        ga.ldc_bf16 = d;
+        ga.bf16_lo_off = lo_hb;
+        ga.stats_out = st;
+        ga.stats_ld = Bc;
+    };
+    MSB_CUDA(launch_embed_rows(next_ids.as<int>(), m.embed, d, B, c.vocab, X, status.as<unsigned>(), s,
+                               hb.as<__nv_bfloat16>(), lo_hb, st, Bc, kStatTile));
     for (int l = 0; l < c.layers; ++l) {
         const DecodeLayerW& W = m.dec[l];
         LayerB& L = layers[l];
@@ -232,7 +262,6 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
         pk.layer_off = (long long)l * 2 * KVD * kKvPage;
         pk.kv_f16 = m.kv_f16 ? 1 : 0;
         // self-attention block
-        MSB_CUDA(launch_ln_bf16(X, B, d, W.ln1, hb.as<__nv_bfloat16>(), s, 0.f, lo_hb));
         {
             TcGemmArgs ga;
             ga.M = B;
@@ -248,6 +277,7 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
             ga.rope.q = q.as<float>();
             ga.rope.kv_new = kvnew.as<float>();
             ga.rope.kv = pk;
+            fold(ga, L.cs_qkv);
             gemm(a_hb, L.m_qkv, ga, d, kBnNarrow, hb_lo, wlo(L.m_qkv_lo));
         }
         MSB_CUDA(launch_self_attn_batch(q.as<float>(), kvnew.as<float>(), pk, posp, B, H, KVH, hd, scale,
@@ -259,16 +289,17 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
             ga.mode = TC_EPI_ACCUM;
             ga.ep.out = X;
             ga.ep.ldc = d;
+            update(ga);
             gemm(a_attn, L.m_o, ga, HD, kBnWide, attn_lo, wlo(L.m_o_lo));
         }
         // cross-attention block
-        MSB_CUDA(launch_ln_bf16(X, B, d, W.ln2, hb.as<__nv_bfloat16>(), s, 0.f, lo_hb));
         {
             TcGemmArgs ga;
             ga.M = B;
             ga.N = HD;
             ga.ep.out = qc.as<float>();
             ga.ep.ldc = HD;
+            fold(ga, L.cs_cq);
             gemm(a_hb, L.m_cq, ga, d, kBnNarrow, hb_lo, wlo(L.m_cq_lo));
         }
         MSB_CUDA(launch_cross_attn_batch(qc.as<float>(), cross32.as<float>(), m.kv_f16 ? cross16.p : cross32.p,
@@ -283,10 +314,10 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
             ga.mode = TC_EPI_ACCUM;
             ga.ep.out = X;
             ga.ep.ldc = d;
+            update(ga);
             gemm(a_attn, L.m_co, ga, HD, kBnWide, attn_lo, wlo(L.m_co_lo));
         }
         // SwiGLU MLP
-        MSB_CUDA(launch_ln_bf16(X, B, d, W.ln3, hb.as<__nv_bfloat16>(), s, 0.f, lo_hb));
         {
             TcGemmArgs ga;
             ga.M = B;
@@ -296,6 +327,7 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
             ga.out_bf16 = g.as<__nv_bfloat16>();
             ga.ldc_bf16 = I;
             ga.bf16_lo_off = lo_g;
+            fold(ga, L.cs_w1);
             gemm(a_hb, L.m_w1, ga, d, kBnWide, hb_lo, wlo(L.m_w1_lo));
         }
         {
@@ -306,10 +338,10 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
             ga.ep.out = X;
             ga.ep.ldc = d;
             ga.ep.bias = W.b2;
+            update(ga);
             gemm(a_g, L.m_w2, ga, I, kBnWide, g_lo, wlo(L.m_w2_lo));
         }
     }
-    MSB_CUDA(launch_ln_bf16(X, B, d, m.dec_norm, hb.as<__nv_bfloat16>(), s, 0.f, lo_hb));
     {
         TcGemmArgs ga;
         ga.M = B;
@@ -321,6 +353,7 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
         ga.inv_temp = inv_temp;
         ga.seed = seed;
         ga.step = pos.as<int>();
+        fold(ga, cs_lm);
         gemm(a_hb, m_lm, ga, d, kBnWide, hb_lo, wlo(m_lm_lo));
     }
     MSB_CUDA(launch_step_finalize(amax.as<unsigned long long>(), B, pos.as<int>(), next_ids.as<int>(), ids.as<int>(),

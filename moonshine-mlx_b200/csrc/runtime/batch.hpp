@@ -68,6 +68,7 @@ struct BatchEngine {
     struct LayerB {
         __nv_bfloat16 *wqkv, *wo, *wcq, *wco, *w1i, *w2;
         float* b1i;
+        float *cs_qkv, *cs_cq, *cs_w1;  // row sums of the LayerNorm-folded weights
         CUtensorMap m_qkv, m_o, m_cq, m_co, m_w1, m_w2;
         CUtensorMap m_qkv_lo, m_o_lo, m_cq_lo, m_co_lo, m_w1_lo, m_w2_lo;  // low planes (split)
     };
@@ -77,10 +78,15 @@ struct BatchEngine {
     std::vector<DevBuf*> own;
     std::vector<LayerB> layers;
     __nv_bfloat16* lm = nullptr;
+    float* cs_lm = nullptr;
     CUtensorMap m_lm, m_lm_lo;
     int Bc = 0, Tc = 0, Mc = 0, Fc = 0;  // capacities: rows, steps, total frames, frames per row
     DevBuf x, hb, attn, g, q, qc, kvnew, part, amax, ids, next_ids, counts, limits_d, done, hit,
         pos, frame_off, frames, cross32, cross16, memory, status;
+    // LayerNorms folded into the GEMMs that consume them: hb holds the bf16 planes of the
+    // residual x, and lnst the (mean, M2) of each row over column tiles of kStatTile,
+    // written by whichever kernel last updated x ([tile][Bc])
+    DevBuf lnst;
     // paged self-attention K/V: page pool and per-row page table of the current call
     DevBuf kvpool, ptable;
     int table_stride = 0;
