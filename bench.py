@@ -250,6 +250,7 @@ def leg_batched(mb, synth, root, torch, barrier, rank, local, reps=3):
     s = torch.cuda.ExternalStream(bm.cuda_stream)
     bm.generate_batch(baudio, forced_len=128)
     b_enc, b_dec, b_ms = [], [], []
+    torch.cuda.nvtx.range_push("batched")  # profilers can select this leg's kernels (ncu --nvtx)
     for _ in range(reps):
         e0, e1 = _events(torch, s)
         e0.record(s)
@@ -260,6 +261,7 @@ def leg_batched(mb, synth, root, torch, barrier, rank, local, reps=3):
         b_ms.append(e0.elapsed_time(e1))
         b_enc.append(bst.encode_ms)
         b_dec.append(bst.decode_ms)
+    torch.cuda.nvtx.range_pop()
     bm.close()
     med = statistics.median(b_ms)
     return {"workload": "small bf16 weights, 64 utterances of U(5, 15) s, 128 forced tokens each",

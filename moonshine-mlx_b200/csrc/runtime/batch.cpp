@@ -393,6 +393,14 @@ void BatchEngine::ensure_enc_weights() {
     enc_weights_ready = true;
 }
 
+// Encoder-layer scratch rows: the capacity grows by half again at least, so stream windows
+// that lengthen a little every chunk reallocate (free + malloc, a device synchronisation)
+// only now and then.
+size_t BatchEngine::enc_rows_capacity(size_t rows3) {
+    if (rows3 > erows_cap) erows_cap = std::max(rows3, erows_cap + erows_cap / 2);
+    return erows_cap;
+}
+
 // Encoder layers (MoonshineLayers.swift:297-310) over X = ex [rows3, e_hidden] in segments of
 // R3 rows; attention of segment s sees its first seg_len[s] rows only.  Uses eh, eqkv, eattn
 // and ef (grown here) and the encoder weights (split operands for fp32 checkpoints).
@@ -402,11 +410,12 @@ void BatchEngine::encoder_layers_tc(size_t rows3, int R3, const int* seg_len) {
     const int eHD = c.e_heads * hd, QKV = (c.e_heads + 2 * c.e_kv_heads) * hd;
     cudaStream_t s = m.stream;
     const size_t P = esplit ? 2 : 1;
-    const size_t lo_h = esplit ? rows3 * ed : 0, lo_attn = esplit ? rows3 * eHD : 0, lo_f = esplit ? rows3 * EI : 0;
-    eh.ensure(rows3 * ed * 2 * P);
-    eqkv.ensure(rows3 * QKV * 4);
-    eattn.ensure(rows3 * eHD * 2 * P);
-    ef.ensure(rows3 * EI * 2 * P);
+    const size_t cap = enc_rows_capacity(rows3);  // low planes sit cap rows behind the high ones
+    const size_t lo_h = esplit ? cap * ed : 0, lo_attn = esplit ? cap * eHD : 0, lo_f = esplit ? cap * EI : 0;
+    eh.ensure(cap * ed * 2 * P);
+    eqkv.ensure(cap * QKV * 4);
+    eattn.ensure(cap * eHD * 2 * P);
+    ef.ensure(cap * EI * 2 * P);
     float* X = ex.as<float>();
     auto amap = [&](CUtensorMap* hi, CUtensorMap* lo, const __nv_bfloat16* p, size_t rows, int K, size_t lo_off) {
         make_a_map(hi, p, (int)rows, K);
@@ -511,7 +520,7 @@ bool BatchEngine::encode_tc(const std::vector<const float*>& audio_dev, const st
     eaud.ensure((size_t)B * sizeof(float*));
     epad1.ensure(rows1 * ed * 2 * P);
     epad2.ensure(rows2 * 2 * ed * 2 * P);
-    ex.ensure(rows3 * ed * 4);
+    ex.ensure(enc_rows_capacity(rows3) * ed * 4);
     emem16.ensure((size_t)Mc * d * 2 * P);
     eseg.ensure((size_t)3 * B * 4);
     __nv_bfloat16* pad1 = epad1.as<__nv_bfloat16>();
@@ -659,7 +668,7 @@ bool BatchEngine::encode_windows(const std::vector<StreamWindow>& w) {
     const size_t rows3 = (size_t)B * R3;
     ensure_enc_weights();
     cudaStream_t s = m.stream;
-    ex.ensure(rows3 * ed * 4);
+    ex.ensure(enc_rows_capacity(rows3) * ed * 4);
     status.ensure(16);
     // tables: src[B], dst[B] pointers, then T, off, cnt, pos
     std::vector<unsigned char> tab((size_t)B * (2 * sizeof(void*) + 4 * sizeof(int)));

@@ -103,6 +103,8 @@ struct BatchEngine {
     bool encode_tc(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
                    const std::vector<int>& off, const std::vector<int>& fr);
     void encoder_layers_tc(size_t rows3, int R3, const int* seg_len);
+    size_t erows_cap = 0;
+    size_t enc_rows_capacity(size_t rows3);
     DevBuf wtab;  // device tables of encode_windows
     struct EncLayerB {
         __nv_bfloat16 *wqkv, *wo, *w1, *w2;

@@ -389,10 +389,25 @@ Model::~Model() {
         cudaSetDevice(device);
         cudaStreamSynchronize(stream);
     }
+    // released by the driver once the last block allocated from it is freed
+    if (stream_pool) cudaMemPoolDestroy(stream_pool);
     for (auto* b : owned) delete b;
     for (auto& e : ev)
         if (e) cudaEventDestroy(e);
     if (stream) cudaStreamDestroy(stream);
+}
+
+cudaMemPool_t Model::streams_pool() {
+    if (!stream_pool) {
+        cudaMemPoolProps props = {};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = device;
+        MSB_CUDA(cudaMemPoolCreate(&stream_pool, &props));
+        uint64_t keep = UINT64_MAX;
+        MSB_CUDA(cudaMemPoolSetAttribute(stream_pool, cudaMemPoolAttrReleaseThreshold, &keep));
+    }
+    return stream_pool;
 }
 
 const uint32_t* Model::upload_words(const std::vector<uint32_t>& v) {

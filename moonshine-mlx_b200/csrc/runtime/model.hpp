@@ -177,6 +177,11 @@ struct Model {
     EncLane& enc_lane(int k);
     void fork_lanes(int k);
     void join_lanes(int k);
+    // Memory pool of the streams' growing buffers (stream-ordered allocations).  Freed blocks
+    // stay in the pool (no release threshold), so growth reuses memory instead of mapping
+    // new memory from the driver every time many streams grow at once.
+    cudaMemPool_t stream_pool = nullptr;
+    cudaMemPool_t streams_pool();
 };
 
 // Throws the MsError that a decode kernel's device status word stands for (no-op for DEV_OK).

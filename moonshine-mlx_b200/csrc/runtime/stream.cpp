@@ -19,13 +19,13 @@ namespace msb {
 namespace {
 
 // Grow `b` to `new_bytes`, keeping its first `keep_bytes` (device-to-device copy).
-// Growth of a stream's buffers is stream-ordered (cudaMallocAsync / cudaFreeAsync on the
-// stream that uses them): many streams growing at the same chunk neither synchronise the
-// device nor wait for fresh allocations from the driver.
-void grow_keep(DevBuf& b, size_t keep_bytes, size_t new_bytes, cudaStream_t s) {
+// Growth of a stream's buffers is stream-ordered (allocated from the model's stream pool and
+// freed with cudaFreeAsync on the stream that uses them): many streams growing at the same
+// chunk neither synchronise the device nor each map new memory from the driver.
+void grow_keep(DevBuf& b, size_t keep_bytes, size_t new_bytes, cudaStream_t s, cudaMemPool_t pool) {
     if (new_bytes <= b.bytes) return;
     void* p = nullptr;
-    MSB_CUDA(cudaMallocAsync(&p, new_bytes, s));
+    MSB_CUDA(cudaMallocFromPoolAsync(&p, new_bytes, pool, s));
     if (b.p && keep_bytes) MSB_CUDA(cudaMemcpyAsync(p, b.p, keep_bytes, cudaMemcpyDeviceToDevice, s));
     if (b.p) MSB_CUDA(cudaFreeAsync(b.p, s));
     b.p = p;
@@ -115,7 +115,7 @@ void StreamState::add_audio(const float* chunk, int64_t n, cudaStream_t s_in) { 
     have_conv1 = true;
     if (feat_count + T3 > feat_cap) {
         const int cap = std::max(feat_count + T3, std::max(2 * feat_cap, 256));
-        grow_keep(features, (size_t)feat_count * ed * 4, (size_t)cap * ed * 4, s);
+        grow_keep(features, (size_t)feat_count * ed * 4, (size_t)cap * ed * 4, s, m.streams_pool());
         feat_cap = cap;
     }
     GemmEpilogue c2;
@@ -134,14 +134,14 @@ void StreamState::ensure_memory(int rows, cudaStream_t s) {
     const Config& c = m.cfg;
     if (rows <= mem_cap) return;
     const int cap = std::max(rows, std::max(2 * mem_cap, 256));
-    grow_keep(memory, (size_t)memory_len * c.hidden * 4, (size_t)cap * c.hidden * 4, s);
+    grow_keep(memory, (size_t)memory_len * c.hidden * 4, (size_t)cap * c.hidden * 4, s, m.streams_pool());
     // the K/V layout [L][2][KVH][cap][hd] depends on the capacity: the rows kept move to the
     // new pitch with one strided copy per buffer (no recomputation)
     const size_t segs = (size_t)c.layers * 2 * c.kv_heads, hd = c.head_dim;
     const size_t n = segs * cap * hd;
     auto regrid = [&](DevBuf& b, size_t esz) {
         void* p = nullptr;
-        MSB_CUDA(cudaMallocAsync(&p, n * esz, s));
+        MSB_CUDA(cudaMallocFromPoolAsync(&p, n * esz, m.streams_pool(), s));
         if (b.p && memory_len > 0)
             MSB_CUDA(cudaMemcpy2DAsync(p, (size_t)cap * hd * esz, b.p, (size_t)mem_cap * hd * esz,
                                        (size_t)memory_len * hd * esz, segs, cudaMemcpyDeviceToDevice, s));
