@@ -513,8 +513,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             for (int e = threadIdx.x; e < (hi - lo) * C4; e += TC_THREADS) {
                 const int r = lo + e / C4, c = (e % C4) * 4;
                 const uint32_t off = (uint32_t)((r * LDS + c) * 4);
+                // every split's value is requested before the first is added (the remote loads
+                // overlap), then summed in split order
+                float4 part[TC_MAX_SPLITS];
+#pragma unroll
+                for (int q = 0; q < TC_MAX_SPLITS; ++q)
+                    if (q < S) part[q] = ld_dsmem4(mapa_rank(tile_a + off, (uint32_t)q));
                 float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int q = 0; q < S; ++q) acc = add4(acc, ld_dsmem4(mapa_rank(tile_a + off, (uint32_t)q)));
+#pragma unroll
+                for (int q = 0; q < TC_MAX_SPLITS; ++q)
+                    if (q < S) acc = add4(acc, part[q]);
                 *reinterpret_cast<float4*>(tile + (size_t)r * LDS + c) = acc;
             }
         }
