@@ -158,10 +158,11 @@ __host__ __device__ constexpr int tile_ld() { return BN + 4; }
 // n = n0 + 4 (t mod BN/4) .. n + 3 for every row it visits, so column-only terms (bias,
 // RoPE angles, K/V scatter base) are loaded once, and the BN/4 threads of a row write one
 // contiguous row segment with 128-bit accesses.  N is a multiple of 4 (checked at launch).
-// Rows [r_lo, r_hi) of the tile; lnr (folded LayerNorm) holds each tile row's (mean, rstd).
+// Rows [r_lo, r_hi) of the tile; lnr (folded LayerNorm) holds each tile row's (mean, rstd);
+// res (ACCUM, optional) the residual rows [r_lo, r_hi) read ahead, BN / 4 float4 per row.
 template <int BN, int MODE>
 __device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* tile, int m0, int n0, int r_lo,
-                                              int r_hi, const float2* lnr) {
+                                              int r_hi, const float2* lnr, const float4* res = nullptr) {
     constexpr int TPR = BN / 4;            // threads per row
     constexpr int RPP = TC_THREADS / TPR;  // rows per pass
     constexpr int LDS = tile_ld<BN>();
@@ -251,7 +252,7 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* 
             float4 nv = make_float4(0.f, 0.f, 0.f, 0.f);
             if (ok) {
                 float4* o = reinterpret_cast<float4*>(ep.out + (size_t)m * ep.ldc + n);
-                nv = add4(*o, add4(v, bias));
+                nv = add4(res ? res[(r - r_lo) * TPR + (t % TPR)] : *o, add4(v, bias));
                 *o = nv;
                 if (g.out_bf16) st_bf16x4_split(g.out_bf16 + (size_t)m * g.ldc_bf16 + n, nv, g.bf16_lo_off);
             }
@@ -360,6 +361,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     const int nkb = max(0, min(nkb_all, kb_lo + per_split) - kb_lo);
     constexpr uint32_t A_BYTES = BM * BK * 2 * Sm::P, B_BYTES = BN * BK * 2 * Sm::P;
     __shared__ int s_fail;
+    __shared__ float2 s_lnr[BM];  // folded LayerNorm: (mean, rstd) per tile row
+    // ACCUM: this CTA's residual rows, read by the idle warps while the main loop runs
+    constexpr int RES_F4 = 1024;
+    __shared__ float4 s_res[MODE == TC_EPI_ACCUM ? RES_F4 : 1];
+    const int S = (int)gridDim.z;
+    const int rows = min(BM, g.M - m0);
+    const int per_rows = (rows + S - 1) / S;  // epilogue rows of split z: [z per, (z + 1) per)
+    const int r_lo = S == 1 ? 0 : min(rows, (int)blockIdx.z * per_rows);
+    const int r_hi = S == 1 ? rows : min(rows, r_lo + per_rows);
+    const bool res_ahead = MODE == TC_EPI_ACCUM && (r_hi - r_lo) * (BN / 4) <= RES_F4;
 
     if (threadIdx.x == 0) {
         s_fail = 0;
@@ -441,9 +452,32 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             mma_commit(&s.empty[st]);
         }
         if (nkb > 0) mma_commit(&s.done);
+    } else if (warp >= 2 && res_ahead) {
+        const GemmEpilogue& ep = g.ep;
+        for (int e = threadIdx.x - 64; e < (r_hi - r_lo) * (BN / 4); e += 64) {
+            const int r = r_lo + e / (BN / 4), n = n0 + (e % (BN / 4)) * 4;
+            if (n < g.N) s_res[e] = *reinterpret_cast<const float4*>(ep.out + (size_t)(m0 + r) * ep.ldc + n);
+        }
+    } else if (warp >= 2 && MODE != TC_EPI_ACCUM && g.lnf.stats) {
+        // folded LayerNorm: (mean, rstd) of every tile row from the producer's column-tile
+        // statistics (final since pdl_wait), on the two warps the main loop leaves idle
+        const TcLnFold& f = g.lnf;
+        const int rows_here = min(BM, g.M - m0);
+        for (int r = threadIdx.x - 64; r < rows_here; r += 64) {
+            float na = 0.f, mean = 0.f, m2 = 0.f;
+            for (int q = 0; q < f.ntiles; ++q) {
+                const float2 st = f.stats[(size_t)q * f.ld + m0 + r];
+                const float nb = (float)min(f.tile_n, f.K - q * f.tile_n);
+                const float nn = na + nb, delta = st.x - mean;
+                mean += delta * (nb / nn);
+                m2 += st.y + delta * delta * (na * nb / nn);
+                na = nn;
+            }
+            s_lnr[r] = make_float2(mean, rsqrtf(m2 / (float)f.K + 1e-5f));
+        }
     }
     __syncwarp();
-    __syncthreads();  // role loops finished; s_fail is final
+    __syncthreads();  // role loops finished; s_fail and s_lnr are final
 
     // epilogue: warp w owns accumulator lanes (rows) 32w .. 32w+31.  The tile goes through
     // shared memory (the idle stage buffers) so the global side is row-contiguous.
@@ -454,7 +488,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     constexpr int LDS = tile_ld<BN>();
     float* tile = reinterpret_cast<float*>(&s.a[0][0][0]);
     static_assert(sizeof(float) * BM * LDS <= sizeof(s.a) + sizeof(s.b), "epilogue tile must fit the stages");
-    const int rows = min(BM, g.M - m0);
     if (warp * 32 < rows) {  // warp-uniform: lanes of rows past M hold nothing
         const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
         float* my = tile + (size_t)(warp * 32 + lane) * LDS;
@@ -470,40 +503,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                 *reinterpret_cast<float4*>(my + c0 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
         }
     }
-    // folded LayerNorm: (mean, rstd) of every tile row from the producer's column-tile
-    // statistics (the producer finished before pdl_wait returned)
-    __shared__ float2 s_lnr[BM];
-    const float2* lnr = nullptr;
-    if constexpr (MODE != TC_EPI_ACCUM) {
-        if (g.lnf.stats) {
-            lnr = s_lnr;
-            const int r = threadIdx.x;
-            if (r < rows) {
-                const TcLnFold& f = g.lnf;
-                float na = 0.f, mean = 0.f, m2 = 0.f;
-                for (int q = 0; q < f.ntiles; ++q) {
-                    const float2 st = f.stats[(size_t)q * f.ld + m0 + r];
-                    const float nb = (float)min(f.tile_n, f.K - q * f.tile_n);
-                    const float nn = na + nb, delta = st.x - mean;
-                    mean += delta * (nb / nn);
-                    m2 += st.y + delta * delta * (na * nb / nn);
-                    na = nn;
-                }
-                s_lnr[r] = make_float2(mean, rsqrtf(m2 / (float)f.K + 1e-5f));
-            }
-        }
-    }
-    __syncthreads();
-    const int S = (int)gridDim.z;
+    __syncthreads();  // the whole tile is staged
+    const float2* lnr = (MODE != TC_EPI_ACCUM && g.lnf.stats) ? s_lnr : nullptr;
+    const float4* res = res_ahead ? s_res : nullptr;
     if (S == 1) {
-        if (ok) epilogue_tile<BN, MODE>(g, tile, m0, n0, 0, rows, lnr);
+        if (ok) epilogue_tile<BN, MODE>(g, tile, m0, n0, 0, rows, lnr, res);
     } else {
         // every split of the tile has staged its partial (barriers taken by all CTAs, also
         // after a failure, so none is left waiting)
         cluster_barrier();
-        const int z = (int)blockIdx.z;
-        const int per = (rows + S - 1) / S;
-        const int lo = min(rows, z * per), hi = min(rows, lo + per);
+        const int lo = r_lo, hi = r_hi;
         const bool any_fail = *reinterpret_cast<volatile unsigned*>(g.status) != 0u;
         if (!any_fail) {
             // rows [lo, hi): sum of the S partials in split order, into this CTA's own tile
@@ -527,7 +536,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             }
         }
         cluster_barrier();  // every CTA has read the partials it needs from its peers
-        if (!any_fail) epilogue_tile<BN, MODE>(g, tile, m0, n0, lo, hi, lnr);
+        if (!any_fail) epilogue_tile<BN, MODE>(g, tile, m0, n0, lo, hi, lnr, res);
     }
     // drain copies still in flight after a failure (bounded), then free tensor memory
     if (warp == 0 && lane == 0 && s_fail) {
