@@ -3,10 +3,12 @@
 // and bf16 activations at the GEMM inputs; the residual stream, attention and softmax stay
 // in fp32.  Row b of every [B, ...] buffer is utterance b.
 //
-//   embed_rows          x[b] = embed[next_id[b]]
-//   ln_bf16             LayerNorm (no bias, eps 1e-5) of fp32 rows -> bf16 GEMM input
-//   self_attn_batch     one warp per (b, head): keys 0..t, cached rows below t (fp16|fp32),
-//                       this step's fp32 K/V at t (MoonshineLayers.swift:106-125)
+//   embed_rows          x[b] = embed[next_id[b]], its bf16 planes and row statistics (the
+//                       LayerNorms are folded into the GEMMs that consume them)
+//   ln_bf16             LayerNorm (no bias, eps 1e-5) of fp32 rows -> bf16 GEMM input (encoder)
+//   self_attn_batch     one 4-warp CTA per (b, head): keys 0..t in rounds staged in shared
+//                       memory from b's pages (fp16|fp32), this step's fp32 K/V at t
+//                       (MoonshineLayers.swift:106-125)
 //   cross_attn_stream   one CTA per (b, head): bulk-copy ring of K/V chunks of utterance b's
 //                       own frames through shared memory, online softmax -> bf16 rows
 //   cross_attn_batch    generic head_dim: (b, head, 32-key chunk) partials over b's frames
