@@ -18,12 +18,18 @@
 // distributed shared memory and runs the epilogue on them.  The sum order is fixed, so
 // results do not depend on which split finishes first.
 //
+// Large GEMMs with the plain epilogue (more output tiles than SMs, no k-splits) run a
+// persistent form instead: one CTA per SM walks its tiles with the producer and MMA warps
+// running ahead into a second TMEM accumulator while four epilogue warps drain the first.
+//
 // A is addressed through a 3-D tensor map (k, y, z) so a causal stride-2 convolution runs as
 // `taps` accumulated GEMMs: tap t reads A at (k, y_t, m + z_t) and B at column t*K_tap + k.
 // For a plain GEMM taps = 1, y = z = 0.
 //
 // Every mbarrier wait is bounded; a timeout records an error code and the CTA drains its
 // in-flight copies (again bounded), frees its tensor memory and exits.
+#include <algorithm>
+
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -162,11 +168,10 @@ __host__ __device__ constexpr int tile_ld() { return BN + 4; }
 // res (ACCUM, optional) the residual rows [r_lo, r_hi) read ahead, BN / 4 float4 per row.
 template <int BN, int MODE>
 __device__ __forceinline__ void epilogue_tile(const TcGemmArgs& g, const float* tile, int m0, int n0, int r_lo,
-                                              int r_hi, const float2* lnr, const float4* res = nullptr) {
+                                              int r_hi, const float2* lnr, const float4* res, int t) {
     constexpr int TPR = BN / 4;            // threads per row
     constexpr int RPP = TC_THREADS / TPR;  // rows per pass
     constexpr int LDS = tile_ld<BN>();
-    const int t = threadIdx.x;
     const int c = (t % TPR) * 4;
     const int n = n0 + c;
     const bool col_ok = n < g.N;
@@ -507,7 +512,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     const float2* lnr = (MODE != TC_EPI_ACCUM && g.lnf.stats) ? s_lnr : nullptr;
     const float4* res = res_ahead ? s_res : nullptr;
     if (S == 1) {
-        if (ok) epilogue_tile<BN, MODE>(g, tile, m0, n0, 0, rows, lnr, res);
+        if (ok) epilogue_tile<BN, MODE>(g, tile, m0, n0, 0, rows, lnr, res, threadIdx.x);
     } else {
         // every split of the tile has staged its partial (barriers taken by all CTAs, also
         // after a failure, so none is left waiting)
@@ -536,7 +541,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             }
         }
         cluster_barrier();  // every CTA has read the partials it needs from its peers
-        if (!any_fail) epilogue_tile<BN, MODE>(g, tile, m0, n0, lo, hi, lnr, res);
+        if (!any_fail) epilogue_tile<BN, MODE>(g, tile, m0, n0, lo, hi, lnr, res, threadIdx.x);
     }
     // drain copies still in flight after a failure (bounded), then free tensor memory
     if (warp == 0 && lane == 0 && s_fail) {
@@ -547,6 +552,197 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     __syncthreads();
     if (warp == 0) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN)
+                     : "memory");
+    }
+}
+
+// Persistent form for large GEMMs with the STD epilogue and no k-splits (the batched and
+// streaming encoders): one CTA per SM walks the output tiles blockIdx.x, blockIdx.x +
+// gridDim.x, ... (N fastest).  Six warps: warp 0 (one lane) the TMA producer and warp 1 (one
+// lane) the MMA issuer run ahead across tiles, warps 2-5 the epilogue.  Two TMEM accumulators
+// (2 BN columns) let the MMAs of tile i + 1 run while the epilogue drains tile i: tfull[a]
+// (MMA commit) hands accumulator a to the epilogue, tempty[a] (one arrival per epilogue warp)
+// hands it back.  The epilogue stages the accumulator in its own shared tile and runs
+// epilogue_tile with its 128 threads.  Split operands take 2 ring stages, bf16 ones 4.
+constexpr int TCP_THREADS = 192;
+// Named barrier 1 of the four epilogue warps (128 threads); the _and form also returns
+// whether every one of them passed `v`.
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ bool epi_sync_and(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 1, 128, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
+}
+template <int BN, bool SP>
+struct alignas(1024) TcPSmem {
+    static constexpr int ST = SP ? 2 : 4;
+    static constexpr int P = SP ? 2 : 1;
+    __nv_bfloat16 a[ST][P][BM * BK];
+    __nv_bfloat16 b[ST][P][BN * BK];
+    float tile[BM * tile_ld<BN>()];
+    uint64_t full[ST], empty[ST], tfull[2], tempty[2], done;
+    uint32_t tmem_base;
+};
+
+template <int BN, bool SP>
+__global__ void __launch_bounds__(TCP_THREADS, 1)
+gemm_tc_persist_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                       const __grid_constant__ CUtensorMap tmap_a_lo, const __grid_constant__ CUtensorMap tmap_b_lo,
+                       TcGemmArgs g) {
+    using Sm = TcPSmem<BN, SP>;
+    constexpr int STAGES = Sm::ST;
+    extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
+    Sm& s = *reinterpret_cast<Sm*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntn = (g.N + BN - 1) / BN, ntiles = ntn * ((g.M + BM - 1) / BM);
+    const int nkb = g.taps * g.kb_per_tap;
+    constexpr uint32_t A_BYTES = BM * BK * 2 * Sm::P, B_BYTES = BN * BK * 2 * Sm::P;
+    __shared__ int s_fail;
+    volatile int* failed = &s_fail;
+    auto fail = [&]() {
+        atomicCAS(g.status, 0u, (unsigned)DEV_WAIT_TIMEOUT);
+        *failed = 1;
+    };
+
+    if (threadIdx.x == 0) {
+        s_fail = 0;
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&s.full[i], 1);
+            mbar_init(&s.empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s.tfull[i], 1);
+            mbar_init(&s.tempty[i], 4);  // one arrival per epilogue warp
+        }
+        mbar_init(&s.done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {  // tensor memory: two accumulators of BN fp32 columns x 128 lanes
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s.tmem_base)),
+                     "r"((uint32_t)(2 * BN))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = s.tmem_base;
+    pdl_wait();
+    pdl_trigger();
+
+    int issued = 0;  // producer: k-blocks issued over all of this CTA's tiles
+    if (warp == 0 && lane == 0) {
+        for (int tile = blockIdx.x; tile < ntiles && !*failed; tile += gridDim.x) {
+            const int m0 = (tile / ntn) * BM, n0 = (tile % ntn) * BN;
+            for (int kb = 0; kb < nkb; ++kb, ++issued) {
+                const int st = issued % STAGES;
+                if (issued >= STAGES && !mbar_wait(&s.empty[st], ((issued / STAGES) - 1) & 1)) {
+                    fail();
+                    break;
+                }
+                const int tap = kb / g.kb_per_tap;
+                const int k0 = (kb - tap * g.kb_per_tap) * BK;
+                mbar_expect_tx(&s.full[st], A_BYTES + B_BYTES);
+                tma_load_2d(s.b[st][0], &tmap_b, &s.full[st], tap * g.k_per_tap + k0, n0);
+                tma_load_3d(s.a[st][0], &tmap_a, &s.full[st], k0, g.tap_y[tap], m0 + g.tap_z[tap]);
+                if constexpr (SP) {
+                    tma_load_2d(s.b[st][1], &tmap_b_lo, &s.full[st], tap * g.k_per_tap + k0, n0);
+                    tma_load_3d(s.a[st][1], &tmap_a_lo, &s.full[st], k0, g.tap_y[tap], m0 + g.tap_z[tap]);
+                }
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        const uint32_t idesc = idesc_bf16(BM, BN);
+        int used = 0, i = 0;  // k-blocks consumed, tiles started
+        for (int tile = blockIdx.x; tile < ntiles && !*failed; tile += gridDim.x, ++i) {
+            const int acc = i & 1;
+            // the epilogue has drained this accumulator's previous tile
+            if (i >= 2 && !mbar_wait(&s.tempty[acc], ((i >> 1) - 1) & 1)) {
+                fail();
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t d = tmem + (uint32_t)(acc * BN);
+            bool ok = true;
+            for (int kb = 0; kb < nkb; ++kb, ++used) {
+                const int st = used % STAGES;
+                if (!mbar_wait(&s.full[st], (used / STAGES) & 1)) {
+                    fail();
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t a_addr = smem_u32(s.a[st][0]), b_addr = smem_u32(s.b[st][0]);
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k) {
+                    mma_bf16(d, smem_desc_sw128(a_addr + k * 32), smem_desc_sw128(b_addr + k * 32), idesc,
+                             (kb > 0 || k > 0) ? 1u : 0u);
+                    if constexpr (SP) {  // + hi.lo + lo.hi
+                        const uint32_t al = smem_u32(s.a[st][Sm::P - 1]), bl = smem_u32(s.b[st][Sm::P - 1]);
+                        mma_bf16(d, smem_desc_sw128(a_addr + k * 32), smem_desc_sw128(bl + k * 32), idesc, 1u);
+                        mma_bf16(d, smem_desc_sw128(al + k * 32), smem_desc_sw128(b_addr + k * 32), idesc, 1u);
+                    }
+                }
+                mma_commit(&s.empty[st]);
+            }
+            if (!ok) break;
+            mma_commit(&s.tfull[acc]);
+        }
+        // every MMA issued here has finished before the tensor memory is freed
+        mma_commit(&s.done);
+        if (!mbar_wait(&s.done, 0)) fail();
+    } else if (warp >= 2) {
+        const int et = threadIdx.x - 64, q = warp & 3;  // warp q may read accumulator lanes 32q..32q+31
+        constexpr int LDS = tile_ld<BN>();
+        int i = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++i) {
+            const int acc = i & 1;
+            const bool ready = !*failed && mbar_wait(&s.tfull[acc], (i >> 1) & 1);
+            if (!epi_sync_and(ready)) {  // uniform over the four epilogue warps
+                fail();
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int m0 = (tile / ntn) * BM, n0 = (tile % ntn) * BN;
+            const int rows = min(BM, g.M - m0);
+            if (q * 32 < rows) {  // warp-uniform: lanes of rows past M hold nothing
+                const uint32_t lane_addr = tmem + (uint32_t)(acc * BN) + ((uint32_t)(q * 32) << 16);
+                float* my = s.tile + (size_t)(q * 32 + lane) * LDS;
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    float v[32];
+                    tmem_ld32(lane_addr + c0, v);
+#pragma unroll
+                    for (int k = 0; k < 32; k += 4)
+                        *reinterpret_cast<float4*>(my + c0 + k) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.tempty[acc]);  // the accumulator takes tile i + 2
+            epi_sync();                                   // the tile is staged
+            epilogue_tile<BN, TC_EPI_STD>(g, s.tile, m0, n0, 0, rows, nullptr, nullptr, et);
+            epi_sync();  // consumed before the next tile is staged
+        }
+    }
+    __syncwarp();
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    // drain copies still in flight after a failure (bounded), then free tensor memory (the MMA
+    // issuer waited for its last MMA)
+    if (warp == 0 && lane == 0 && *failed)
+        for (int it = (issued > STAGES ? issued - STAGES : 0); it < issued; ++it)
+            mbar_wait(&s.full[it % STAGES], (it / STAGES) & 1);
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * BN))
                      : "memory");
     }
 }
@@ -613,11 +809,43 @@ cudaError_t launch_tc(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
                          map_b_lo, g);
 }
 
+int num_sms() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            n = 1;
+    }
+    return n;
+}
+
+// The persistent form: one CTA per SM (its shared memory allows no second one).
+template <int BN, bool SP>
+cudaError_t launch_tc_persist(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_a_lo,
+                              const CUtensorMap& map_b_lo, const TcGemmArgs& g, cudaStream_t stream, int ntiles) {
+    const size_t smem = sizeof(TcPSmem<BN, SP>) + 1024;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_tc_persist_kernel<BN, SP>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    return launch_kernel(gemm_tc_persist_kernel<BN, SP>, dim3(std::min(ntiles, num_sms())), dim3(TCP_THREADS), smem,
+                         stream, map_a, map_b, map_a_lo, map_b_lo, g);
+}
+
 template <int BN, bool SP>
 cudaError_t launch_tc_mode(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_a_lo,
                            const CUtensorMap& map_b_lo, const TcGemmArgs& g, cudaStream_t stream) {
+    const int ntiles = ((g.N + BN - 1) / BN) * ((g.M + BM - 1) / BM);
     switch (g.mode) {
-        case TC_EPI_STD: return launch_tc<BN, TC_EPI_STD, SP>(map_a, map_b, map_a_lo, map_b_lo, g, stream);
+        case TC_EPI_STD:
+            // more tiles than SMs: the persistent form overlaps each tile's epilogue with the
+            // next tile's loads and MMAs
+            if (g.splits == 1 && ntiles > num_sms())
+                return launch_tc_persist<BN, SP>(map_a, map_b, map_a_lo, map_b_lo, g, stream, ntiles);
+            return launch_tc<BN, TC_EPI_STD, SP>(map_a, map_b, map_a_lo, map_b_lo, g, stream);
         case TC_EPI_ROPE_KV: return launch_tc<BN, TC_EPI_ROPE_KV, SP>(map_a, map_b, map_a_lo, map_b_lo, g, stream);
         case TC_EPI_SWIGLU: return launch_tc<BN, TC_EPI_SWIGLU, SP>(map_a, map_b, map_a_lo, map_b_lo, g, stream);
         case TC_EPI_ARGMAX: return launch_tc<BN, TC_EPI_ARGMAX, SP>(map_a, map_b, map_a_lo, map_b_lo, g, stream);
