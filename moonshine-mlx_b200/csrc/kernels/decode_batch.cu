@@ -409,7 +409,7 @@ __global__ void cross_combine_kernel(const float* __restrict__ part, int B, int 
 
 // Cross attention of one (utterance b, head h) per CTA, streamed through shared memory.
 // K rows and V rows of one head are contiguous over frames, so thread 0 keeps a ring of
-// XS_STAGES chunks of CH keys in flight as two bulk copies per chunk completing on one
+// ST chunks of CH keys in flight as two bulk copies per chunk completing on one
 // mbarrier.  Warp w scores keys [w*KW, (w+1)*KW) of each chunk with G lanes per key (16
 // bytes of the row per lane, the matching q slice in registers, shuffle sum inside the
 // group), keeps an online softmax, and accumulates V with lane c owning dims 2c, 2c+1.  The
@@ -424,17 +424,17 @@ struct XsShape {
     static constexpr int G = NE <= 4 ? 4 : (NE <= 8 ? 8 : 16);    // lanes per key
     static constexpr int KPP = 32 / G;                            // keys per warp pass
     static constexpr int CH = F16 ? 64 : 32;                      // keys per stage
+    static constexpr int ST = 3;                                  // ring stages
     static constexpr int KW = CH / 4;                             // keys per warp per stage
     static constexpr int STAGE_ELEMS = CH * HDT;                  // per tensor
     static_assert(NE * 16 == ROWB && NE <= 16, "key rows must be whole 16-byte pieces");
     static_assert(KW % KPP == 0 && KW <= 32, "warp slice must be whole passes");
 };
-constexpr int XS_STAGES = 3;
 constexpr int XS_THREADS = 128;
 
 template <int HDT, bool F16>
 constexpr size_t xs_smem_bytes() {
-    return 2 * (size_t)XS_STAGES * XsShape<HDT, F16>::STAGE_ELEMS * XsShape<HDT, F16>::ESZ;
+    return 2 * (size_t)XsShape<HDT, F16>::ST * XsShape<HDT, F16>::STAGE_ELEMS * XsShape<HDT, F16>::ESZ;
 }
 
 template <int HDT, bool F16>
@@ -449,8 +449,8 @@ __global__ void __launch_bounds__(XS_THREADS) cross_attn_stream_kernel(
     using E = typename std::conditional<F16, __half, float>::type;
     extern __shared__ __align__(128) unsigned char xs_raw[];
     E* ks = reinterpret_cast<E*>(xs_raw);
-    E* vs = ks + XS_STAGES * S::STAGE_ELEMS;
-    __shared__ __align__(8) uint64_t full[XS_STAGES];
+    E* vs = ks + S::ST * S::STAGE_ELEMS;
+    __shared__ __align__(8) uint64_t full[S::ST];
     __shared__ float sc[4][S::KW];  // scores, then probabilities, of each warp's slice
     __shared__ float wm[4], wl[4];
     __shared__ float wacc[4][HDT];
@@ -466,16 +466,16 @@ __global__ void __launch_bounds__(XS_THREADS) cross_attn_stream_kernel(
     const E* kg = base + ((((size_t)layer * 2 + 0) * KVH + kvh) * mc + fo) * HDT;
     const E* vg = base + ((((size_t)layer * 2 + 1) * KVH + kvh) * mc + fo) * HDT;
     auto issue = [&](int c) {
-        const int st = c % XS_STAGES;
+        const int st = c % S::ST;
         const uint32_t bytes = (uint32_t)min(S::CH, M - c * S::CH) * S::ROWB;
         mbar_expect_tx(&full[st], 2 * bytes);
         bulk_load(ks + (size_t)st * S::STAGE_ELEMS, kg + (size_t)c * S::STAGE_ELEMS, bytes, &full[st]);
         bulk_load(vs + (size_t)st * S::STAGE_ELEMS, vg + (size_t)c * S::STAGE_ELEMS, bytes, &full[st]);
     };
     if (threadIdx.x == 0) {
-        for (int i = 0; i < XS_STAGES; ++i) mbar_init(&full[i], 1);
+        for (int i = 0; i < S::ST; ++i) mbar_init(&full[i], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int c = 0; c < min(nchunks, XS_STAGES); ++c) issue(c);
+        for (int c = 0; c < min(nchunks, S::ST); ++c) issue(c);
     }
     __syncthreads();  // the barriers are initialised before any thread waits on them
     // q slice of this lane's piece (lanes with sub >= NE only pad their group)
@@ -488,14 +488,14 @@ __global__ void __launch_bounds__(XS_THREADS) cross_attn_stream_kernel(
     float m_run = -INFINITY, l_run = 0.f, a0 = 0.f, a1 = 0.f;
     int failed_at = -1;
     for (int c = 0; c < nchunks; ++c) {
-        const int st = c % XS_STAGES;
-        const bool ok = mbar_wait(&full[st], (c / XS_STAGES) & 1);
+        const int st = c % S::ST;
+        const bool ok = mbar_wait(&full[st], (c / S::ST) & 1);
         // every warp is past chunk c-1 here, so its stage can be refilled
         if (!__syncthreads_and(ok)) {
             failed_at = c;
             break;
         }
-        if (threadIdx.x == 0 && c >= 1 && c - 1 + XS_STAGES < nchunks) issue(c - 1 + XS_STAGES);
+        if (threadIdx.x == 0 && c >= 1 && c - 1 + S::ST < nchunks) issue(c - 1 + S::ST);
         const int nk = min(S::CH, M - c * S::CH);
         const int k0 = wid * S::KW;
         const int kw = max(0, min(S::KW, nk - k0));
@@ -551,8 +551,8 @@ __global__ void __launch_bounds__(XS_THREADS) cross_attn_stream_kernel(
     if (failed_at >= 0) {  // uniform across the CTA (decided by __syncthreads_and)
         if (threadIdx.x == 0) {
             atomicCAS(status, 0u, (unsigned)DEV_WAIT_TIMEOUT);
-            const int issued = min(nchunks, failed_at == 0 ? XS_STAGES : failed_at - 1 + XS_STAGES);
-            for (int c = failed_at; c < issued; ++c) mbar_wait(&full[c % XS_STAGES], (c / XS_STAGES) & 1);
+            const int issued = min(nchunks, failed_at == 0 ? S::ST : failed_at - 1 + S::ST);
+            for (int c = failed_at; c < issued; ++c) mbar_wait(&full[c % S::ST], (c / S::ST) & 1);
         }
         return;
     }
