@@ -273,11 +273,12 @@ def leg_batched(mb, synth, root, torch, barrier, rank, local, reps=3):
                       f"(median of {reps})"}
 
 
-def leg_sharded(mb, synth, root, torch, dist, barrier, rank, world, local, reps=2, sub_batch=64):
+def leg_sharded(mb, synth, root, torch, dist, barrier, rank, world, local, reps=2, sub_batch=256):
     """A fixed job of 256 medium bf16 utterances of U(2, 30) s, each decoding its own limit
     ceil(6.5 s) with EOS ignored, partitioned by length over the ranks (shard.py).  Each rank
     runs its share through ms_generate_batch in length-sorted groups of at most `sub_batch`
-    utterances; time per rank by CUDA events on its model stream, job time = max over ranks;
+    utterances (by default one call for the whole share: a lockstep step costs about the same
+    for 256 rows as for 64); time per rank by CUDA events on its model stream, job time = max over ranks;
     ids gathered on rank 0."""
     import numpy as np
     from moonshine_b200 import shard
