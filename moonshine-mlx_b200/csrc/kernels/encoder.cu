@@ -6,7 +6,8 @@
 //                      the encoder norms and final_norm + pos_emb (prepareMemory,
 //                      MoonshineDecoder.swift:39-47)
 //   window_attention : sliding-window MHA, keys restricted to the band instead of a
-//                      dense [T,T] additive mask (MoonshineLayers.swift:266-290)
+//                      dense [T,T] additive mask (MoonshineLayers.swift:266-290); for
+//                      windows the band of 32 query rows is staged in shared memory per CTA
 #include "common.cuh"
 #include "kernels.h"
 
@@ -174,6 +175,108 @@ __global__ void window_attention_kernel(const float* __restrict__ qkv, int T, in
         if (d < hd) {
             if (out) out[o + d] = acc[c] * inv;
             if (out_bf16) st_bf16_split(out_bf16 + o + d, acc[c] * inv, lo_off);
+        }
+    }
+}
+
+// The same attention for windows (left > 0), one CTA per (tile of WT_Q consecutive query rows
+// of one segment, head): the K and V rows of the band those queries see are staged in shared
+// memory once with coalesced loads (rows padded to hd + 4 floats, so lanes reading different
+// rows hit different banks), then each warp takes every WT_WARPS-th query with the arithmetic
+// of window_attention_kernel in the same order, so the results are the same bit for bit;
+// the per-query kernel read every key row from global memory once per query.
+constexpr int WT_Q = 32;
+constexpr int WT_WARPS = 4;
+__global__ void __launch_bounds__(WT_WARPS * 32) window_attention_tile_kernel(
+    const float* __restrict__ qkv, int T, int H, int KVH, int hd, int left, int right, float scale,
+    float* __restrict__ out, int seg_rows, const int* __restrict__ seg_len, __nv_bfloat16* __restrict__ out_bf16,
+    size_t lo_off, int tiles_per_seg, int kmax) {
+    extern __shared__ __align__(16) float wt_smem[];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int h = blockIdx.y, kvh = h / (H / KVH);
+    const int seg = blockIdx.x / tiles_per_seg, tile = blockIdx.x - seg * tiles_per_seg;
+    const int srows = seg_rows > 0 ? seg_rows : T;
+    const int base = seg * srows, len = seg_rows > 0 ? seg_len[seg] : T;
+    const int q0 = tile * WT_Q, q1 = min(srows, q0 + WT_Q);  // local rows of this tile's queries
+    const int ld = (H + 2 * KVH) * hd, rs = hd + 4, n4 = hd >> 2;
+    float* ks = wt_smem;
+    float* vs = ks + (size_t)kmax * rs;
+    float* qw = vs + (size_t)kmax * rs + wid * hd;  // this warp's query row
+    // the band of the valid queries: local keys [klo, khi) (at most kmax rows, host-checked)
+    const int qv1 = min(q1, len);
+    const int klo = q0 < qv1 ? max(0, q0 - left + 1) : 0;
+    const int khi = q0 < qv1 ? min(len, (qv1 - 1) + (right > 0 ? right : 1)) : 0;
+    const int nrows = khi - klo;
+    const float* kg = qkv + (size_t)(base + klo) * ld + H * hd + kvh * hd;
+    const float* vg = kg + KVH * hd;
+    for (int i = threadIdx.x; i < 2 * nrows * n4; i += blockDim.x) {
+        const int kv = i >= nrows * n4, ii = kv ? i - nrows * n4 : i;
+        const int r = ii / n4, c4 = ii - r * n4;
+        const float4 v = *reinterpret_cast<const float4*>((kv ? vg : kg) + (size_t)r * ld + 4 * c4);
+        *reinterpret_cast<float4*>((kv ? vs : ks) + (size_t)r * rs + 4 * c4) = v;
+    }
+    __syncthreads();
+    for (int qi = q0 + wid; qi < q1; qi += WT_WARPS) {
+        const int t = base + qi;
+        const size_t o = (size_t)t * (H * hd) + h * hd;
+        if (qi >= len) {  // rows past the segment's length are written as zeros
+            for (int d = lane; d < hd; d += 32) {
+                if (out) out[o + d] = 0.f;
+                if (out_bf16) st_bf16_split(out_bf16 + o + d, 0.f, lo_off);
+            }
+            continue;
+        }
+        __syncwarp();  // the previous query's row is no longer read
+        for (int d = lane; d < hd; d += 32) qw[d] = qkv[(size_t)t * ld + h * hd + d];
+        __syncwarp();
+        const int lo = max(0, qi - left + 1), hi = min(len, qi + (right > 0 ? right : 1));
+        float m = -INFINITY, l = 0.f;
+        float acc[WA_MAXHD / 32];
+#pragma unroll
+        for (int j = 0; j < WA_MAXHD / 32; ++j) acc[j] = 0.f;
+        for (int k0 = lo; k0 < hi; k0 += 32) {
+            const int kk = k0 + lane;
+            float s = -INFINITY;
+            if (kk < hi) {
+                const float* kr = ks + (size_t)(kk - klo) * rs;
+                float dot = 0.f;
+                for (int d = 0; d < hd; d += 4) {
+                    const float4 a = *reinterpret_cast<const float4*>(qw + d);
+                    const float4 b = *reinterpret_cast<const float4*>(kr + d);
+                    dot = fmaf(a.x, b.x, dot);
+                    dot = fmaf(a.y, b.y, dot);
+                    dot = fmaf(a.z, b.z, dot);
+                    dot = fmaf(a.w, b.w, dot);
+                }
+                s = dot * scale;
+            }
+            const float mc = warp_max(s);
+            const float mn = fmaxf(m, mc);
+            const float p = (kk < hi) ? expf(s - mn) : 0.f;
+            const float corr = expf(m - mn);  // 0 on the first chunk (m = -inf)
+            l = l * corr + warp_sum(p);
+#pragma unroll
+            for (int j = 0; j < WA_MAXHD / 32; ++j) acc[j] *= corr;
+            const int nk = min(32, hi - k0);
+            for (int j = 0; j < nk; ++j) {
+                const float pj = __shfl_sync(FULL, p, j);
+                const float* vr = vs + (size_t)(k0 + j - klo) * rs;
+#pragma unroll
+                for (int c = 0; c < WA_MAXHD / 32; ++c) {
+                    const int d = lane + 32 * c;
+                    if (d < hd) acc[c] = fmaf(pj, vr[d], acc[c]);
+                }
+            }
+            m = mn;
+        }
+        const float inv = 1.f / l;
+#pragma unroll
+        for (int c = 0; c < WA_MAXHD / 32; ++c) {
+            const int d = lane + 32 * c;
+            if (d < hd) {
+                if (out) out[o + d] = acc[c] * inv;
+                if (out_bf16) st_bf16_split(out_bf16 + o + d, acc[c] * inv, lo_off);
+            }
         }
     }
 }
@@ -368,6 +471,17 @@ cudaError_t launch_window_attention(const float* qkv, int T, int H, int kv_heads
     if (hd > WA_MAXHD || (hd & 3) || H % kv_heads) return cudaErrorInvalidValue;
     if ((seg_rows > 0) != (seg_len != nullptr) || (!out && !out_bf16)) return cudaErrorInvalidValue;
     ++launch_counter();
+    if (left > 0 && (seg_rows == 0 || T % seg_rows == 0)) {  // windows: the band staged per tile
+        const int kmax = WT_Q + left + (right > 0 ? right : 1);
+        const size_t smem = ((size_t)2 * kmax * (hd + 4) + (size_t)WT_WARPS * hd) * 4;
+        if (smem <= 48 * 1024) {
+            const int srows = seg_rows > 0 ? seg_rows : T, nseg = T / srows;
+            const int tiles = (srows + WT_Q - 1) / WT_Q;
+            window_attention_tile_kernel<<<dim3(nseg * tiles, H), WT_WARPS * 32, smem, stream>>>(
+                qkv, T, H, kv_heads, hd, left, right, scale, out, seg_rows, seg_len, out_bf16, lo_off, tiles, kmax);
+            return cudaGetLastError();
+        }
+    }
     const int wpb = 8;
     const int items = T * H;
     window_attention_kernel<<<(items + wpb - 1) / wpb, wpb * 32, 0, stream>>>(
