@@ -333,8 +333,10 @@ ms_status ms_stream_add_audio(ms_stream* stream, const float* chunk, int64_t n_s
 
 /* addAudio of many streams at once (no counterpart in the reference, which feeds one stream
  * per call): chunks[i] (n_samples[i] samples) goes to streams[i], with the same effect as n
- * calls of ms_stream_add_audio.  When all streams share one model their frontends run
- * concurrently on the model's CUDA streams, which is what serving many streams needs. */
+ * calls of ms_stream_add_audio (a stream listed twice takes its chunks in order).  When all
+ * streams share one model their frontends run as one batched pass (one upload of every
+ * stream's whole frames, five launches for all of them), which is what serving many streams
+ * needs. */
 ms_status ms_stream_add_audio_batch(ms_stream* const* streams, int32_t n, const float* const* chunks,
                                     const int64_t* n_samples);
 /* transcribe(_:isFinal:streamingConfig:maxTokens:temperature:) (:122-168).

@@ -791,14 +791,9 @@ ms_status ms_stream_add_audio_batch(ms_stream* const* streams, int32_t n, const 
         }
         std::lock_guard<std::mutex> g(shared->mu);
         MSB_CUDA(cudaSetDevice(shared->device));
-        // the streams' frontends run concurrently on the model's encoder lanes (each stream's
-        // buffers are its own); the model stream waits for all of them before its next work
-        const int lanes = std::min<int32_t>(n, 8);
-        shared->fork_lanes(lanes);
-        for (int32_t i = 0; i < n; ++i)
-            reinterpret_cast<StreamState*>(streams[i])->add_audio(chunks[i], n_samples[i],
-                                                                  shared->enc_lane(i % lanes).stream);
-        shared->join_lanes(lanes);
+        // all the streams' frontends in one pass on the model stream: one upload, five launches
+        add_audio_batch(*shared, reinterpret_cast<StreamState* const*>(streams), n, chunks, n_samples,
+                        shared->stream);
         return MS_OK;
     });
 }

@@ -21,16 +21,11 @@ constexpr int MAX_FRAME = 128;
 __device__ __forceinline__ void store_feature(float* p, float v) { *p = v; }
 __device__ __forceinline__ void store_feature(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
 
+// One frame (warp): CMVN, asinh, Linear + SiLU into the output row o; fr is the warp's
+// MAX_FRAME floats of shared memory.
 template <class OutT>
-__global__ void __launch_bounds__(FF_WARPS * 32)
-frame_features_kernel(const float* __restrict__ audio, int n_frames, int frame_len,
-                      const float* __restrict__ log_k, const float* __restrict__ w, int dim,
-                      OutT* __restrict__ out, int ld_out) {
-    __shared__ float fr[FF_WARPS][MAX_FRAME];
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int f = blockIdx.x * FF_WARPS + wid;
-    if (f >= n_frames) return;
-    const float* a = audio + (size_t)f * frame_len;
+__device__ __forceinline__ void frame_feature(const float* a, int frame_len, const float* __restrict__ log_k,
+                                              const float* __restrict__ w, int dim, OutT* o, float* fr, int lane) {
     float s = 0.f;
     for (int i = lane; i < frame_len; i += 32) s += a[i];
     const float mean = warp_sum(s) / (float)frame_len;
@@ -41,14 +36,50 @@ frame_features_kernel(const float* __restrict__ audio, int n_frames, int frame_l
     }
     const float rms = sqrtf(warp_sum(v) / (float)frame_len + 1e-6f);
     const float k = expf(*log_k);
-    for (int i = lane; i < frame_len; i += 32) fr[wid][i] = asinhf(k * ((a[i] - mean) / rms));
+    for (int i = lane; i < frame_len; i += 32) fr[i] = asinhf(k * ((a[i] - mean) / rms));
     __syncwarp();
-    for (int o = lane; o < dim; o += 32) {
-        const float* wr = w + (size_t)o * frame_len;
+    for (int j = lane; j < dim; j += 32) {
+        const float* wr = w + (size_t)j * frame_len;
         float acc = 0.f;
-        for (int i = 0; i < frame_len; ++i) acc = fmaf(fr[wid][i], __ldg(wr + i), acc);
-        store_feature(out + (size_t)f * ld_out + o, silu(acc));
+        for (int i = 0; i < frame_len; ++i) acc = fmaf(fr[i], __ldg(wr + i), acc);
+        store_feature(o + j, silu(acc));
     }
+}
+
+template <class OutT>
+__global__ void __launch_bounds__(FF_WARPS * 32)
+frame_features_kernel(const float* __restrict__ audio, int n_frames, int frame_len,
+                      const float* __restrict__ log_k, const float* __restrict__ w, int dim,
+                      OutT* __restrict__ out, int ld_out) {
+    __shared__ float fr[FF_WARPS][MAX_FRAME];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int f = blockIdx.x * FF_WARPS + wid;
+    if (f >= n_frames) return;
+    frame_feature(audio + (size_t)f * frame_len, frame_len, log_k, w, dim, out + (size_t)f * ld_out, fr[wid], lane);
+}
+
+// The same for many streams at once: stream z's nf[z] frames start at audio + aoff[z] and its
+// rows at out[z] (ld_out apart).
+__global__ void __launch_bounds__(FF_WARPS * 32)
+frame_features_batch_kernel(const float* __restrict__ audio, const long long* __restrict__ aoff,
+                            const int* __restrict__ nf, float* const* __restrict__ out, int frame_len,
+                            const float* __restrict__ log_k, const float* __restrict__ w, int dim, int ld_out) {
+    __shared__ float fr[FF_WARPS][MAX_FRAME];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int z = blockIdx.y, f = blockIdx.x * FF_WARPS + wid;
+    if (f >= nf[z]) return;
+    frame_feature(audio + aoff[z] + (size_t)f * frame_len, frame_len, log_k, w, dim,
+                  out[z] + (size_t)f * ld_out, fr[wid], lane);
+}
+
+// dst[z][0 .. n[z]) = src[z][0 .. n[z]) (zeros where src[z] is null); n[z] % 4 == 0, 16-byte
+// aligned rows.
+__global__ void copy_rows_batch_kernel(const float* const* __restrict__ src, float* const* __restrict__ dst,
+                                       const int* __restrict__ n) {
+    const int z = blockIdx.x;
+    const float4* s4 = reinterpret_cast<const float4*>(src[z]);
+    float4* d4 = reinterpret_cast<float4*>(dst[z]);
+    for (int i = threadIdx.x; i < n[z] / 4; i += blockDim.x) d4[i] = s4 ? s4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 constexpr int LN_MAXV = 32;  // up to 1024 features per row (32 per lane)
@@ -437,6 +468,25 @@ cudaError_t launch_frame_features(const float* audio, int n_frames, int frame_le
     ++launch_counter();
     frame_features_kernel<float><<<(n_frames + FF_WARPS - 1) / FF_WARPS, FF_WARPS * 32, 0, stream>>>(
         audio, n_frames, frame_len, log_k, w, dim, out, ld_out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_frame_features_batch(const float* audio, const long long* aoff, const int* nf, float* const* out,
+                                        int nb, int nf_max, int frame_len, const float* log_k, const float* w,
+                                        int dim, int ld_out, cudaStream_t stream) {
+    if (nb <= 0 || nf_max <= 0) return cudaSuccess;
+    if (frame_len > MAX_FRAME || nb > 65535) return cudaErrorInvalidValue;
+    ++launch_counter();
+    frame_features_batch_kernel<<<dim3((nf_max + FF_WARPS - 1) / FF_WARPS, nb), FF_WARPS * 32, 0, stream>>>(
+        audio, aoff, nf, out, frame_len, log_k, w, dim, ld_out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_copy_rows_batch(const float* const* src, float* const* dst, const int* n, int nb,
+                                   cudaStream_t stream) {
+    if (nb <= 0) return cudaSuccess;
+    ++launch_counter();
+    copy_rows_batch_kernel<<<nb, 128, 0, stream>>>(src, dst, n);
     return cudaGetLastError();
 }
 

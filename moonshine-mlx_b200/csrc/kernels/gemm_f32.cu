@@ -36,10 +36,10 @@ __device__ __forceinline__ void epilogue_store(const GemmEpilogue& ep, int m, in
     if (ep.kv_out16) reinterpret_cast<__half*>(ep.kv_out16)[idx] = __float2half_rn(v);
 }
 
+// One BM x BN output tile at (blockIdx.y * BM, blockIdx.x * BN).
 template <int BM>
-__global__ void __launch_bounds__(NT) gemm_f32_kernel(const float* __restrict__ A, int lda,
-                                                       const float* __restrict__ B, int ldb,
-                                                       int M, int N, int K, GemmEpilogue ep) {
+__device__ __forceinline__ void gemm_f32_tile(const float* __restrict__ A, int lda, const float* __restrict__ B,
+                                              int ldb, int M, int N, int K, const GemmEpilogue& ep) {
     constexpr int TM = BM / 16;          // rows per thread
     constexpr int A_F4 = BM * BK / 4;    // float4 per A tile
     constexpr int A_PER_T = A_F4 / NT;   // 2 (BM=128) or 1 (BM=64)
@@ -132,6 +132,26 @@ __global__ void __launch_bounds__(NT) gemm_f32_kernel(const float* __restrict__ 
     }
 }
 
+template <int BM>
+__global__ void __launch_bounds__(NT) gemm_f32_kernel(const float* __restrict__ A, int lda,
+                                                       const float* __restrict__ B, int ldb,
+                                                       int M, int N, int K, GemmEpilogue ep) {
+    gemm_f32_tile<BM>(A, lda, B, ldb, M, N, K, ep);
+}
+
+// GEMM blockIdx.z of a batch (tables in device memory); tiles past its M rows return at once.
+template <int BM>
+__global__ void __launch_bounds__(NT) gemm_f32_batch_kernel(const float* const* __restrict__ As,
+                                                             const int* __restrict__ Ms,
+                                                             float* const* __restrict__ outs, int lda,
+                                                             const float* __restrict__ B, int ldb, int N, int K,
+                                                             GemmEpilogue ep) {
+    const int z = blockIdx.z, M = Ms[z];
+    if ((int)blockIdx.y * BM >= M) return;
+    ep.out = outs[z];
+    gemm_f32_tile<BM>(As[z], lda, B, ldb, M, N, K, ep);
+}
+
 }  // namespace
 
 cudaError_t launch_gemm_f32(const float* A, int lda, const float* B, int ldb, int M, int N,
@@ -149,6 +169,25 @@ cudaError_t launch_gemm_f32(const float* A, int lda, const float* B, int ldb, in
     } else {
         dim3 grid(gx, (M + 63) / 64);
         gemm_f32_kernel<64><<<grid, NT, 0, stream>>>(A, lda, B, ldb, M, N, K, ep);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_f32_batch(const float* const* A, const int* M, float* const* out, int nb, int m_max,
+                                  int lda, const float* B, int ldb, int N, int K, const GemmEpilogue& ep,
+                                  cudaStream_t stream) {
+    if (nb <= 0 || m_max <= 0 || N <= 0) return cudaSuccess;
+    if ((K & 3) || (lda & 3) || (ldb & 3) || (reinterpret_cast<uintptr_t>(B) & 15) || ep.kv_scatter ||
+        ep.residual || nb > 65535)
+        return cudaErrorInvalidValue;
+    const int gx = (N + BN - 1) / BN;
+    ++launch_counter();
+    if (m_max > 64 && (long long)gx * ((m_max + 127) / 128) * nb >= 2 * 148) {
+        dim3 grid(gx, (m_max + 127) / 128, nb);
+        gemm_f32_batch_kernel<128><<<grid, NT, 0, stream>>>(A, M, out, lda, B, ldb, N, K, ep);
+    } else {
+        dim3 grid(gx, (m_max + 63) / 64, nb);
+        gemm_f32_batch_kernel<64><<<grid, NT, 0, stream>>>(A, M, out, lda, B, ldb, N, K, ep);
     }
     return cudaGetLastError();
 }

@@ -62,6 +62,15 @@ enum : unsigned { DEV_OK = 0, DEV_BARRIER_TIMEOUT = 1, DEV_BAD_TOKEN = 2, DEV_WA
 cudaError_t launch_frame_features(const float* audio, int n_frames, int frame_len,
                                   const float* log_k, const float* w, int dim,
                                   float* out, int ld_out, cudaStream_t stream);
+// The same for nb streams in one launch (device tables): stream z's nf[z] frames start at
+// audio + aoff[z] and its rows at out[z]; nf_max >= every nf[z].
+cudaError_t launch_frame_features_batch(const float* audio, const long long* aoff, const int* nf, float* const* out,
+                                        int nb, int nf_max, int frame_len, const float* log_k, const float* w,
+                                        int dim, int ld_out, cudaStream_t stream);
+// dst[z][0, n[z]) = src[z][0, n[z]) for z < nb (zeros where src[z] is null); device tables,
+// every n[z] a multiple of 4 floats and every row 16-byte aligned.
+cudaError_t launch_copy_rows_batch(const float* const* src, float* const* dst, const int* n, int nb,
+                                   cudaStream_t stream);
 
 // ---------------------------------------------------------------- fp32 GEMM
 // C[m, n] = epilogue( sum_k A[m*lda + k] * B[n*ldb + k] ).
@@ -83,6 +92,13 @@ struct GemmEpilogue {
 };
 cudaError_t launch_gemm_f32(const float* A, int lda, const float* B, int ldb, int M, int N,
                             int K, const GemmEpilogue& ep, cudaStream_t stream);
+// nb GEMMs sharing B, N, K and the epilogue except its output, in one launch: GEMM z reads
+// A[z] (M[z] rows, lda apart) and writes out[z] (device tables; every A[z] 16-byte aligned,
+// m_max >= every M[z]).  Each output element is the same as launch_gemm_f32's.  No K/V
+// scatter or residual.
+cudaError_t launch_gemm_f32_batch(const float* const* A, const int* M, float* const* out, int nb, int m_max,
+                                  int lda, const float* B, int ldb, int N, int K, const GemmEpilogue& ep,
+                                  cudaStream_t stream);
 
 // ---------------------------------------------------------------- bf16 tensor-core GEMM
 // C = epi(A * B^T) with A [M, K] and B [N, K] bf16 (K-major), fp32 accumulation in TMEM.

@@ -389,6 +389,8 @@ Model::~Model() {
         cudaSetDevice(device);
         cudaStreamSynchronize(stream);
     }
+    if (fe_stage_done) cudaEventDestroy(fe_stage_done);
+    if (fe_stage) cudaFreeHost(fe_stage);
     // released by the driver once the last block allocated from it is freed
     if (stream_pool) cudaMemPoolDestroy(stream_pool);
     for (auto* b : owned) delete b;

@@ -182,6 +182,13 @@ struct Model {
     // new memory from the driver every time many streams grow at once.
     cudaMemPool_t stream_pool = nullptr;
     cudaMemPool_t streams_pool();
+    // Batched streaming frontend (addAudio of many streams in one pass): page-locked staging
+    // of the chunks' frames and launch tables (fe_stage_done marks the end of the last upload
+    // from it), their device copy, and the conv inputs of all the streams.
+    char* fe_stage = nullptr;
+    size_t fe_stage_cap = 0;
+    cudaEvent_t fe_stage_done = nullptr;
+    DevBuf fe_dev, fe_x;
 };
 
 // Throws the MsError that a decode kernel's device status word stands for (no-op for DEV_OK).

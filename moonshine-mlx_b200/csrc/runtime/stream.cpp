@@ -13,6 +13,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <unordered_set>
 
 namespace msb {
 
@@ -127,6 +128,212 @@ void StreamState::add_audio(const float* chunk, int64_t n, cudaStream_t s_in) { 
                              cudaMemcpyDeviceToDevice, s));
     have_conv2 = true;
     feat_count += T3;
+}
+
+namespace {
+
+// One pass of add_audio_batch over streams that each appear once and each have whole frames.
+struct FrontJob {
+    StreamState* st;
+    const float* chunk;
+    int64_t n;
+    int nf, T2, T3;
+    size_t aoff, x1, x2;  // offsets (floats) of the frames in the upload and of the conv inputs in fe_x
+};
+
+void frontend_pass(Model& m, const std::vector<FrontJob>& jobs, size_t audio_f, size_t x_f, int nf_max, int t2_max,
+                   int t3_max, cudaStream_t s) {
+    const Config& c = m.cfg;
+    const int fl = c.frame_len(), ed = c.e_hidden, nb = (int)jobs.size();
+    const size_t tb = (audio_f * 4 + 15) & ~(size_t)15;
+    size_t off = tb;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off += (bytes + 15) & ~(size_t)15;
+        return o;
+    };
+    const size_t o_aoff = take(8 * (size_t)nb), o_ffout = take(8 * (size_t)nb);
+    const size_t o_pre_src = take(16 * (size_t)nb), o_pre_dst = take(16 * (size_t)nb);
+    const size_t o_post_src = take(16 * (size_t)nb), o_post_dst = take(16 * (size_t)nb);
+    const size_t o_g1a = take(8 * (size_t)nb), o_g1o = take(8 * (size_t)nb);
+    const size_t o_g2a = take(8 * (size_t)nb), o_g2o = take(8 * (size_t)nb);
+    const size_t o_nf = take(4 * (size_t)nb), o_cnt = take(8 * (size_t)nb);
+    const size_t o_m1 = take(4 * (size_t)nb), o_m2 = take(4 * (size_t)nb);
+    const size_t total = off;
+
+    // device scratch (grows by half again at least, so a slowly growing batch rarely reallocates)
+    auto grow = [](DevBuf& b, size_t bytes) {
+        if (bytes > b.bytes) b.ensure(std::max(bytes, b.bytes + b.bytes / 2));
+    };
+    grow(m.fe_dev, total);
+    grow(m.fe_x, x_f * 4);
+    // per-stream buffers, allocated and grown stream-ordered before the tables point at them
+    for (const FrontJob& j : jobs) {
+        StreamState& st = *j.st;
+        grow_keep(st.conv1_buf, 0, (size_t)4 * ed * 4, s, m.streams_pool());
+        grow_keep(st.conv2_buf, 0, (size_t)4 * 2 * ed * 4, s, m.streams_pool());
+        if (st.feat_count + j.T3 > st.feat_cap) {
+            const int cap = std::max(st.feat_count + j.T3, std::max(2 * st.feat_cap, 256));
+            grow_keep(st.features, (size_t)st.feat_count * ed * 4, (size_t)cap * ed * 4, s, m.streams_pool());
+            st.feat_cap = cap;
+        }
+    }
+
+    // page-locked staging, free once the previous upload from it has finished
+    if (!m.fe_stage_done) MSB_CUDA(cudaEventCreateWithFlags(&m.fe_stage_done, cudaEventDisableTiming));
+    MSB_CUDA(cudaEventSynchronize(m.fe_stage_done));
+    if (total > m.fe_stage_cap) {
+        if (m.fe_stage) MSB_CUDA(cudaFreeHost(m.fe_stage));
+        m.fe_stage = nullptr;
+        const size_t cap = std::max(total, 2 * m.fe_stage_cap);
+        MSB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&m.fe_stage), cap, cudaHostAllocDefault));
+        m.fe_stage_cap = cap;
+    }
+    char* h = m.fe_stage;
+    char* d = m.fe_dev.as<char>();
+    float* x = m.fe_x.as<float>();
+    auto hp = [&](size_t o) { return reinterpret_cast<void*>(h + o); };
+    long long* aoff = static_cast<long long*>(hp(o_aoff));
+    float** ffout = static_cast<float**>(hp(o_ffout));
+    const float** pre_src = static_cast<const float**>(hp(o_pre_src));
+    float** pre_dst = static_cast<float**>(hp(o_pre_dst));
+    const float** post_src = static_cast<const float**>(hp(o_post_src));
+    float** post_dst = static_cast<float**>(hp(o_post_dst));
+    const float** g1a = static_cast<const float**>(hp(o_g1a));
+    float** g1o = static_cast<float**>(hp(o_g1o));
+    const float** g2a = static_cast<const float**>(hp(o_g2a));
+    float** g2o = static_cast<float**>(hp(o_g2o));
+    int* nfv = static_cast<int*>(hp(o_nf));
+    int* cnt = static_cast<int*>(hp(o_cnt));
+    int* m1 = static_cast<int*>(hp(o_m1));
+    int* m2 = static_cast<int*>(hp(o_m2));
+    for (int z = 0; z < nb; ++z) {
+        const FrontJob& j = jobs[z];
+        StreamState& st = *j.st;
+        // the stream's whole frames: leftover samples, then the head of the chunk
+        float* a = reinterpret_cast<float*>(h) + j.aoff;
+        const size_t used = (size_t)j.nf * fl, sb = st.sample_buffer.size();
+        const size_t from_sb = std::min(sb, used);
+        std::copy(st.sample_buffer.begin(), st.sample_buffer.begin() + from_sb, a);
+        std::copy(j.chunk, j.chunk + (used - from_sb), a + from_sb);
+        float* x1 = x + j.x1;
+        float* x2 = x + j.x2;
+        aoff[z] = (long long)j.aoff;
+        nfv[z] = j.nf;
+        ffout[z] = x1 + 4 * ed;
+        pre_src[z] = st.have_conv1 ? st.conv1_buf.as<float>() : nullptr;
+        pre_dst[z] = x1;
+        pre_src[nb + z] = st.have_conv2 ? st.conv2_buf.as<float>() : nullptr;
+        pre_dst[nb + z] = x2;
+        // conv1Buffer / conv2Buffer = last 4 rows of [buffer; x] (MoonshineEncoder.swift:137)
+        post_src[z] = x1 + (size_t)j.nf * ed;
+        post_dst[z] = st.conv1_buf.as<float>();
+        post_src[nb + z] = x2 + (size_t)j.T2 * 2 * ed;
+        post_dst[nb + z] = st.conv2_buf.as<float>();
+        cnt[z] = 4 * ed;
+        cnt[nb + z] = 4 * 2 * ed;
+        g1a[z] = x1;
+        g1o[z] = x2 + 4 * 2 * ed;
+        m1[z] = j.T2;
+        g2a[z] = x2;
+        g2o[z] = st.features.as<float>() + (size_t)st.feat_count * ed;
+        m2[z] = j.T3;
+    }
+    MSB_CUDA(cudaMemcpyAsync(d, h, total, cudaMemcpyHostToDevice, s));
+    MSB_CUDA(cudaEventRecord(m.fe_stage_done, s));
+    auto dp = [&](size_t o) { return reinterpret_cast<void*>(d + o); };
+    MSB_CUDA(launch_copy_rows_batch(static_cast<const float* const*>(dp(o_pre_src)),
+                                    static_cast<float* const*>(dp(o_pre_dst)), static_cast<const int*>(dp(o_cnt)),
+                                    2 * nb, s));
+    MSB_CUDA(launch_frame_features_batch(reinterpret_cast<const float*>(d), static_cast<const long long*>(dp(o_aoff)),
+                                         static_cast<const int*>(dp(o_nf)), static_cast<float* const*>(dp(o_ffout)),
+                                         nb, nf_max, fl, m.log_k, m.lin_w, ed, ed, s));
+    GemmEpilogue c1;
+    c1.bias = m.conv1_b;
+    c1.act = ACT_SILU;
+    c1.ldc = 2 * ed;
+    MSB_CUDA(launch_gemm_f32_batch(static_cast<const float* const*>(dp(o_g1a)), static_cast<const int*>(dp(o_m1)),
+                                   static_cast<float* const*>(dp(o_g1o)), nb, t2_max, 2 * ed, m.conv1_w, 5 * ed,
+                                   2 * ed, 5 * ed, c1, s));
+    GemmEpilogue c2;
+    c2.bias = m.conv2_b;
+    c2.ldc = ed;
+    MSB_CUDA(launch_gemm_f32_batch(static_cast<const float* const*>(dp(o_g2a)), static_cast<const int*>(dp(o_m2)),
+                                   static_cast<float* const*>(dp(o_g2o)), nb, t3_max, 4 * ed, m.conv2_w, 10 * ed,
+                                   ed, 10 * ed, c2, s));
+    MSB_CUDA(launch_copy_rows_batch(static_cast<const float* const*>(dp(o_post_src)),
+                                    static_cast<float* const*>(dp(o_post_dst)), static_cast<const int*>(dp(o_cnt)),
+                                    2 * nb, s));
+    for (const FrontJob& j : jobs) {
+        StreamState& st = *j.st;
+        const size_t used = (size_t)j.nf * fl, sb = st.sample_buffer.size();
+        std::vector<float> rest;
+        rest.reserve(sb + (size_t)j.n - used);
+        for (size_t k = used; k < sb; ++k) rest.push_back(st.sample_buffer[k]);
+        const size_t c0 = used > sb ? used - sb : 0;
+        rest.insert(rest.end(), j.chunk + c0, j.chunk + j.n);
+        st.sample_buffer.swap(rest);
+        st.have_conv1 = st.have_conv2 = true;
+        st.feat_count += j.T3;
+    }
+}
+
+}  // namespace
+
+void add_audio_batch(Model& m, StreamState* const* ss, int n, const float* const* chunks, const int64_t* ns,
+                     cudaStream_t s) {
+    const Config& c = m.cfg;
+    const int fl = c.frame_len(), ed = c.e_hidden;
+    bool dup = false;
+    {
+        std::unordered_set<const StreamState*> seen;
+        for (int i = 0; i < n && !dup; ++i) dup = !seen.insert(ss[i]).second;
+    }
+    if (dup) {  // a stream's chunks must be taken in order: one call at a time
+        for (int i = 0; i < n; ++i) ss[i]->add_audio(chunks[i], ns[i], s);
+        return;
+    }
+    for (int i = 0; i < n; ++i)
+        if ((int64_t)(ss[i]->sample_buffer.size() + (size_t)ns[i]) / fl > (1 << 24))
+            throw MsError(MS_ERR_INVALID_ARG, "audio chunk too long");
+    constexpr int kGroup = 16384;  // streams per pass (launch grids take up to 65535 in y and z)
+    std::vector<FrontJob> jobs;
+    size_t audio_f = 0, x_f = 0;
+    int nf_max = 0, t2_max = 0, t3_max = 0;
+    auto flush = [&]() {
+        if (!jobs.empty()) frontend_pass(m, jobs, audio_f, x_f, nf_max, t2_max, t3_max, s);
+        jobs.clear();
+        audio_f = x_f = 0;
+        nf_max = t2_max = t3_max = 0;
+    };
+    for (int i = 0; i < n; ++i) {
+        StreamState& st = *ss[i];
+        const size_t have = st.sample_buffer.size() + (size_t)ns[i];
+        const int nf = (int)((int64_t)have / fl);
+        if (nf == 0) {  // everything stays in the remainder buffer
+            st.sample_buffer.insert(st.sample_buffer.end(), chunks[i], chunks[i] + ns[i]);
+            continue;
+        }
+        FrontJob j;
+        j.st = &st;
+        j.chunk = chunks[i];
+        j.n = ns[i];
+        j.nf = nf;
+        j.T2 = (nf - 1) / 2 + 1;
+        j.T3 = (j.T2 - 1) / 2 + 1;
+        j.aoff = audio_f;
+        audio_f += ((size_t)nf * fl + 3) & ~(size_t)3;
+        j.x1 = x_f;
+        x_f += (size_t)(4 + nf) * ed;
+        j.x2 = x_f;
+        x_f += (size_t)(4 + j.T2) * 2 * ed;
+        nf_max = std::max(nf_max, nf);
+        t2_max = std::max(t2_max, j.T2);
+        t3_max = std::max(t3_max, j.T3);
+        jobs.push_back(j);
+        if ((int)jobs.size() == kGroup) flush();
+    }
+    flush();
 }
 
 void StreamState::ensure_memory(int rows, cudaStream_t s) {

@@ -79,4 +79,12 @@ struct StreamState {
     std::pair<std::vector<int32_t>, bool> decode_memory(int32_t max_tokens, float temperature, unsigned seed);
 };
 
+// addAudio of n streams of model m in one pass on stream s: chunks[i] (ns[i] samples) goes to
+// ss[i], with the same results as n calls of add_audio in order (a stream that appears more
+// than once takes its chunks one after the other).  One upload of all the streams' whole
+// frames and launch tables, then five launches for the lot: the conv histories, the frame
+// features, conv1, the new histories, conv2.
+void add_audio_batch(Model& m, StreamState* const* ss, int n, const float* const* chunks, const int64_t* ns,
+                     cudaStream_t s);
+
 }  // namespace msb

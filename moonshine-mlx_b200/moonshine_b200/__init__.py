@@ -631,8 +631,8 @@ class MoonshineModel:
         _check(_L().ms_stream_add_audio(state._h, _fptr(a), a.shape[0]))
 
     def add_audio_batch(self, states: Sequence[StreamingState], chunks: Sequence) -> None:
-        """add_audio of chunks[i] to states[i] for every i in one call (the frontends of streams
-        of this model run concurrently)."""
+        """add_audio of chunks[i] to states[i] for every i in one call (the frontends of all the
+        streams of this model run as one batched pass: one upload, five launches)."""
         arrs = [_f32(c) for c in chunks]
         if len(arrs) != len(states):
             raise ValueError("one chunk per stream")

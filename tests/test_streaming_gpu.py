@@ -107,6 +107,38 @@ def test_stream_batch_equals_single(model_root):
         assert got == want
 
 
+def test_stream_batch_ragged_and_repeated(model_root):
+    """add_audio_batch with chunks shorter than a frame (they only fill the remainder buffer),
+    an empty chunk, and a stream listed twice (its chunks are taken in order) matches the same
+    chunks fed one add_audio call at a time."""
+    import moonshine_b200 as mb
+    d = model_dir(model_root, "tiny")
+    m = mb.MoonshineModel.load(d)
+    streams = [m.create_stream() for _ in range(3)]
+    singles = [m.create_stream() for _ in range(3)]
+    for s in streams + singles:
+        m.start_stream(s)
+    audios = [synth.synth_audio(8000, 50 + i) for i in range(3)]
+    pos = [0, 0, 0]
+
+    def take(i, n):
+        piece = audios[i][pos[i]:pos[i] + n]
+        pos[i] += n
+        return piece
+
+    plans = [[(0, 50), (1, 1111), (2, 0)], [(0, 2000), (1, 30), (2, 1500)],
+             [(2, 700), (0, 900), (2, 333), (1, 2100)], [(0, 1200), (1, 1200), (2, 1200)]]
+    for plan in plans:
+        pieces = [(i, take(i, n)) for i, n in plan]
+        m.add_audio_batch([streams[i] for i, _ in pieces], [p for _, p in pieces])
+        for i, p in pieces:
+            m.add_audio(singles[i], p)
+        got = m.transcribe_batch(streams, max_tokens=16)
+        want = [m.transcribe(s, max_tokens=16) for s in singles]
+        assert got == want
+        assert [s.memory_len for s in streams] == [s.memory_len for s in singles]
+
+
 def test_stream_batch_decode_lockstep(model_root):
     """transcribe_batch with batch_decode: 4 streams fed 80 ms chunks, every call's segment
     decoded in lockstep on the tensor cores (split bf16 operands for this fp32 checkpoint).
