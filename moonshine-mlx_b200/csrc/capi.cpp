@@ -871,11 +871,18 @@ ms_status ms_stream_transcribe_batch(ms_stream* const* streams, int32_t n, int32
                                         s->memory_row()});
                 }
                 be.encode_windows(wins);
-                for (int32_t i = 0; i < n; ++i) {
-                    StreamState* s = reinterpret_cast<StreamState*>(streams[i]);
-                    if (has[i]) s->commit_new_frames(plan[i], shared->stream);
-                    lim[i] = s->decode_limit(is_final != 0, mt, &res[i]);
-                }
+                // the cross K/V of every stream's new memory rows in one launch
+                std::vector<StreamState*> enc_ss;
+                std::vector<StreamState::EncPlan> enc_plans;
+                for (int32_t i = 0; i < n; ++i)
+                    if (has[i]) {
+                        enc_ss.push_back(reinterpret_cast<StreamState*>(streams[i]));
+                        enc_plans.push_back(plan[i]);
+                    }
+                commit_new_frames_batch(*shared, enc_ss.data(), enc_plans.data(), (int)enc_ss.size(),
+                                        shared->stream);
+                for (int32_t i = 0; i < n; ++i)
+                    lim[i] = reinterpret_cast<StreamState*>(streams[i])->decode_limit(is_final != 0, mt, &res[i]);
             } else {
                 const int lanes = std::min<int32_t>(n, 8);  // concurrent incremental encoders
                 shared->fork_lanes(lanes);

@@ -2,7 +2,10 @@
 // Used by the fp32 encoder path: causal convs as implicit GEMMs (strided A rows over a
 // zero-padded activation buffer), QKV / O / MLP projections with bias, activation and
 // residual fused, and the once-per-utterance cross-attention K/V projection scattered
-// straight into the decoder's KV layout (fp32 and fp16 copies).
+// straight into the decoder's KV layout (fp32 and fp16 copies).  Two batched forms for many
+// streaming states at once: GEMMs indexed by blockIdx.z through device tables (the frontend
+// convs), and one GEMM over rows gathered from anywhere with a K/V scatter per row (the cross
+// K/V of every stream's new memory rows).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -14,6 +17,22 @@ constexpr int BN = 64;
 constexpr int BK = 16;
 constexpr int NT = 256;
 
+// Column n of a cross K/V projection -> (layer, k|v, head, dim) of the decoder's layout
+// [L][2][kv_heads][frame_cap][head_dim], at frame `frame`.
+__device__ __forceinline__ void kv_store(float* out32, void* out16, int kv_heads, int head_dim, int frame_cap,
+                                         int frame, int n, float v) {
+    const int kvdim = kv_heads * head_dim;
+    const int layer = n / (2 * kvdim);
+    const int rem = n - layer * 2 * kvdim;
+    const int kv = rem / kvdim;
+    const int c = rem - kv * kvdim;
+    const int head = c / head_dim;
+    const int dim = c - head * head_dim;
+    const size_t idx = ((((size_t)layer * 2 + kv) * kv_heads + head) * frame_cap + (size_t)frame) * head_dim + dim;
+    if (out32) out32[idx] = v;
+    if (out16) reinterpret_cast<__half*>(out16)[idx] = __float2half_rn(v);
+}
+
 __device__ __forceinline__ void epilogue_store(const GemmEpilogue& ep, int m, int n, float v) {
     if (ep.bias) v += ep.bias[n];
     if (ep.act == ACT_SILU) v = silu(v);
@@ -23,23 +42,17 @@ __device__ __forceinline__ void epilogue_store(const GemmEpilogue& ep, int m, in
         ep.out[(size_t)m * ep.ldc + n] = v;
         return;
     }
-    const int kvdim = ep.kv_heads * ep.head_dim;
-    const int layer = n / (2 * kvdim);
-    const int rem = n - layer * 2 * kvdim;
-    const int kv = rem / kvdim;
-    const int c = rem - kv * kvdim;
-    const int head = c / ep.head_dim;
-    const int dim = c - head * ep.head_dim;
-    const size_t idx = ((((size_t)layer * 2 + kv) * ep.kv_heads + head) * ep.frame_cap +
-                        (size_t)(m + ep.frame_offset)) * ep.head_dim + dim;
-    if (ep.kv_out32) ep.kv_out32[idx] = v;
-    if (ep.kv_out16) reinterpret_cast<__half*>(ep.kv_out16)[idx] = __float2half_rn(v);
+    kv_store(ep.kv_out32, ep.kv_out16, ep.kv_heads, ep.head_dim, ep.frame_cap, m + ep.frame_offset, n, v);
 }
 
-// One BM x BN output tile at (blockIdx.y * BM, blockIdx.x * BN).
+// One BM x BN output tile at (blockIdx.y * BM, blockIdx.x * BN).  With a_rows, row m of A is
+// at a_rows[m] (lda unused) and the result goes through the per-row K/V scatter kv_rows[m]
+// (ep gives kv_heads and head_dim); the arithmetic is the same either way.
 template <int BM>
 __device__ __forceinline__ void gemm_f32_tile(const float* __restrict__ A, int lda, const float* __restrict__ B,
-                                              int ldb, int M, int N, int K, const GemmEpilogue& ep) {
+                                              int ldb, int M, int N, int K, const GemmEpilogue& ep,
+                                              const float* const* __restrict__ a_rows = nullptr,
+                                              const KvRowDst* __restrict__ kv_rows = nullptr) {
     constexpr int TM = BM / 16;          // rows per thread
     constexpr int A_F4 = BM * BK / 4;    // float4 per A tile
     constexpr int A_PER_T = A_F4 / NT;   // 2 (BM=128) or 1 (BM=64)
@@ -52,15 +65,21 @@ __device__ __forceinline__ void gemm_f32_tile(const float* __restrict__ A, int l
 
     float4 ra[A_PER_T];
     float4 rb;
+    const float* arow[A_PER_T];  // this thread's A rows (null past M)
+#pragma unroll
+    for (int i = 0; i < A_PER_T; ++i) {
+        const int m = m0 + ((tid + i * NT) >> 2);
+        arow[i] = m < M ? (a_rows ? a_rows[m] : A + (size_t)m * lda) : nullptr;
+    }
 
     auto load_tiles = [&](int k0) {
 #pragma unroll
         for (int i = 0; i < A_PER_T; ++i) {
             const int f = tid + i * NT;
-            const int row = f >> 2, kq = (f & 3) << 2;
-            const int m = m0 + row, k = k0 + kq;
-            ra[i] = (m < M && k < K) ? __ldg(reinterpret_cast<const float4*>(A + (size_t)m * lda + k))
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+            const int kq = (f & 3) << 2;
+            const int k = k0 + kq;
+            ra[i] = (arow[i] && k < K) ? __ldg(reinterpret_cast<const float4*>(arow[i] + k))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         {
             const int row = tid >> 2, kq = (tid & 3) << 2;
@@ -124,6 +143,15 @@ __device__ __forceinline__ void gemm_f32_tile(const float* __restrict__ A, int l
     for (int i = 0; i < TM; ++i) {
         const int m = m0 + ty * TM + i;
         if (m >= M) continue;
+        if (kv_rows) {
+            const KvRowDst d = kv_rows[m];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int n = n0 + tx * 4 + j;
+                if (n < N) kv_store(d.out32, d.out16, ep.kv_heads, ep.head_dim, d.frame_cap, d.frame_row, n, acc[i][j]);
+            }
+            continue;
+        }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int n = n0 + tx * 4 + j;
@@ -137,6 +165,14 @@ __global__ void __launch_bounds__(NT) gemm_f32_kernel(const float* __restrict__ 
                                                        const float* __restrict__ B, int ldb,
                                                        int M, int N, int K, GemmEpilogue ep) {
     gemm_f32_tile<BM>(A, lda, B, ldb, M, N, K, ep);
+}
+
+template <int BM>
+__global__ void __launch_bounds__(NT) gemm_f32_kv_rows_kernel(const float* const* __restrict__ a_rows,
+                                                               const KvRowDst* __restrict__ dst, int M,
+                                                               const float* __restrict__ B, int ldb, int N, int K,
+                                                               GemmEpilogue ep) {
+    gemm_f32_tile<BM>(nullptr, 0, B, ldb, M, N, K, ep, a_rows, dst);
 }
 
 // GEMM blockIdx.z of a batch (tables in device memory); tiles past its M rows return at once.
@@ -188,6 +224,27 @@ cudaError_t launch_gemm_f32_batch(const float* const* A, const int* M, float* co
     } else {
         dim3 grid(gx, (m_max + 63) / 64, nb);
         gemm_f32_batch_kernel<64><<<grid, NT, 0, stream>>>(A, M, out, lda, B, ldb, N, K, ep);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_f32_kv_rows(const float* const* a_rows, const KvRowDst* dst, int M, const float* B, int ldb,
+                                    int N, int K, int kv_heads, int head_dim, cudaStream_t stream) {
+    if (M <= 0 || N <= 0) return cudaSuccess;
+    if ((K & 3) || (ldb & 3) || (reinterpret_cast<uintptr_t>(B) & 15) || kv_heads <= 0 || head_dim <= 0)
+        return cudaErrorInvalidValue;
+    GemmEpilogue ep;
+    ep.kv_scatter = 1;
+    ep.kv_heads = kv_heads;
+    ep.head_dim = head_dim;
+    const int gx = (N + BN - 1) / BN;
+    ++launch_counter();
+    if ((long long)gx * ((M + 127) / 128) >= 2 * 148) {
+        dim3 grid(gx, (M + 127) / 128);
+        gemm_f32_kv_rows_kernel<128><<<grid, NT, 0, stream>>>(a_rows, dst, M, B, ldb, N, K, ep);
+    } else {
+        dim3 grid(gx, (M + 63) / 64);
+        gemm_f32_kv_rows_kernel<64><<<grid, NT, 0, stream>>>(a_rows, dst, M, B, ldb, N, K, ep);
     }
     return cudaGetLastError();
 }

@@ -99,6 +99,18 @@ cudaError_t launch_gemm_f32(const float* A, int lda, const float* B, int ldb, in
 cudaError_t launch_gemm_f32_batch(const float* const* A, const int* M, float* const* out, int nb, int m_max,
                                   int lda, const float* B, int ldb, int N, int K, const GemmEpilogue& ep,
                                   cudaStream_t stream);
+// Where row r of a gathered-rows cross K/V GEMM lands: the K/V scatter of GemmEpilogue
+// into out32 / out16 (either nullable) with frame_cap rows per segment, at frame frame_row.
+struct KvRowDst {
+    float* out32;
+    void* out16;
+    int frame_cap, frame_row;
+};
+// Cross K/V projection of M memory rows from anywhere (row r at a_rows[r], 16-byte aligned,
+// K floats) scattered per row as dst[r] says (device tables): many streams' new memory rows
+// in one launch.  Each value is the same as launch_gemm_f32 with kv_scatter gives.
+cudaError_t launch_gemm_f32_kv_rows(const float* const* a_rows, const KvRowDst* dst, int M, const float* B, int ldb,
+                                    int N, int K, int kv_heads, int head_dim, cudaStream_t stream);
 
 // ---------------------------------------------------------------- bf16 tensor-core GEMM
 // C = epi(A * B^T) with A [M, K] and B [N, K] bf16 (K-major), fp32 accumulation in TMEM.

@@ -7,6 +7,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <fstream>
@@ -35,6 +36,35 @@ ms_status to_status(const std::exception& e) {
 
 DevBuf::~DevBuf() {
     if (p) cudaFree(p);
+}
+
+TableUpload::~TableUpload() {
+    if (done) {
+        cudaEventSynchronize(done);
+        cudaEventDestroy(done);
+    }
+    if (stage) cudaFreeHost(stage);
+}
+
+char* TableUpload::host(size_t bytes) {
+    if (!done) MSB_CUDA(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+    MSB_CUDA(cudaEventSynchronize(done));
+    if (bytes > cap) {
+        if (stage) MSB_CUDA(cudaFreeHost(stage));
+        stage = nullptr;
+        const size_t c = std::max(bytes, 2 * cap);
+        MSB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&stage), c, cudaHostAllocDefault));
+        cap = c;
+    }
+    return stage;
+}
+
+char* TableUpload::upload(size_t bytes, cudaStream_t s) {
+    // grows by half again at least, so a slowly growing call rarely reallocates
+    if (bytes > dev.bytes) dev.ensure(std::max(bytes, dev.bytes + dev.bytes / 2));
+    MSB_CUDA(cudaMemcpyAsync(dev.p, stage, bytes, cudaMemcpyHostToDevice, s));
+    MSB_CUDA(cudaEventRecord(done, s));
+    return dev.as<char>();
 }
 
 void DevBuf::ensure(size_t n) {
@@ -389,8 +419,6 @@ Model::~Model() {
         cudaSetDevice(device);
         cudaStreamSynchronize(stream);
     }
-    if (fe_stage_done) cudaEventDestroy(fe_stage_done);
-    if (fe_stage) cudaFreeHost(fe_stage);
     // released by the driver once the last block allocated from it is freed
     if (stream_pool) cudaMemPoolDestroy(stream_pool);
     for (auto* b : owned) delete b;

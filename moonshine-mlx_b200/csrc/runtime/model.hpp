@@ -65,6 +65,24 @@ struct DevBuf {
     template <class T> T* as() const { return reinterpret_cast<T*>(p); }
 };
 
+// Launch tables of one call, filled on the host and uploaded on one stream: page-locked
+// staging (reused once its last upload has finished) and its device copy.  Kernels that read
+// the device copy must run on the stream of the upload, so the next upload waits for them.
+struct TableUpload {
+    char* stage = nullptr;
+    size_t cap = 0;
+    cudaEvent_t done = nullptr;
+    DevBuf dev;
+    TableUpload() = default;
+    TableUpload(const TableUpload&) = delete;
+    TableUpload& operator=(const TableUpload&) = delete;
+    ~TableUpload();
+    // Host area of at least `bytes` (waits for the previous upload from it).
+    char* host(size_t bytes);
+    // Uploads the first `bytes` on s; returns the device address of the area.
+    char* upload(size_t bytes, cudaStream_t s);
+};
+
 struct EncLayer {
     float *wqkv, *wo, *w1, *b1, *w2, *b2, *ln_in, *ln_post;
 };
@@ -182,13 +200,11 @@ struct Model {
     // new memory from the driver every time many streams grow at once.
     cudaMemPool_t stream_pool = nullptr;
     cudaMemPool_t streams_pool();
-    // Batched streaming frontend (addAudio of many streams in one pass): page-locked staging
-    // of the chunks' frames and launch tables (fe_stage_done marks the end of the last upload
-    // from it), their device copy, and the conv inputs of all the streams.
-    char* fe_stage = nullptr;
-    size_t fe_stage_cap = 0;
-    cudaEvent_t fe_stage_done = nullptr;
-    DevBuf fe_dev, fe_x;
+    // Batched streaming frontend (addAudio of many streams in one pass): the upload of the
+    // chunks' frames and launch tables, and the conv inputs of all the streams; and the
+    // tables of the streams' batched cross K/V of new memory rows.
+    TableUpload fe_tables, kv_tables;
+    DevBuf fe_x;
 };
 
 // Throws the MsError that a decode kernel's device status word stands for (no-op for DEV_OK).

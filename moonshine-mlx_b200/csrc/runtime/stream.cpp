@@ -161,12 +161,8 @@ void frontend_pass(Model& m, const std::vector<FrontJob>& jobs, size_t audio_f, 
     const size_t o_m1 = take(4 * (size_t)nb), o_m2 = take(4 * (size_t)nb);
     const size_t total = off;
 
-    // device scratch (grows by half again at least, so a slowly growing batch rarely reallocates)
-    auto grow = [](DevBuf& b, size_t bytes) {
-        if (bytes > b.bytes) b.ensure(std::max(bytes, b.bytes + b.bytes / 2));
-    };
-    grow(m.fe_dev, total);
-    grow(m.fe_x, x_f * 4);
+    // conv inputs (grow by half again at least, so a slowly growing batch rarely reallocates)
+    if (x_f * 4 > m.fe_x.bytes) m.fe_x.ensure(std::max(x_f * 4, m.fe_x.bytes + m.fe_x.bytes / 2));
     // per-stream buffers, allocated and grown stream-ordered before the tables point at them
     for (const FrontJob& j : jobs) {
         StreamState& st = *j.st;
@@ -179,18 +175,7 @@ void frontend_pass(Model& m, const std::vector<FrontJob>& jobs, size_t audio_f, 
         }
     }
 
-    // page-locked staging, free once the previous upload from it has finished
-    if (!m.fe_stage_done) MSB_CUDA(cudaEventCreateWithFlags(&m.fe_stage_done, cudaEventDisableTiming));
-    MSB_CUDA(cudaEventSynchronize(m.fe_stage_done));
-    if (total > m.fe_stage_cap) {
-        if (m.fe_stage) MSB_CUDA(cudaFreeHost(m.fe_stage));
-        m.fe_stage = nullptr;
-        const size_t cap = std::max(total, 2 * m.fe_stage_cap);
-        MSB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&m.fe_stage), cap, cudaHostAllocDefault));
-        m.fe_stage_cap = cap;
-    }
-    char* h = m.fe_stage;
-    char* d = m.fe_dev.as<char>();
+    char* h = m.fe_tables.host(total);
     float* x = m.fe_x.as<float>();
     auto hp = [&](size_t o) { return reinterpret_cast<void*>(h + o); };
     long long* aoff = static_cast<long long*>(hp(o_aoff));
@@ -239,8 +224,7 @@ void frontend_pass(Model& m, const std::vector<FrontJob>& jobs, size_t audio_f, 
         g2o[z] = st.features.as<float>() + (size_t)st.feat_count * ed;
         m2[z] = j.T3;
     }
-    MSB_CUDA(cudaMemcpyAsync(d, h, total, cudaMemcpyHostToDevice, s));
-    MSB_CUDA(cudaEventRecord(m.fe_stage_done, s));
+    char* d = m.fe_tables.upload(total, s);
     auto dp = [&](size_t o) { return reinterpret_cast<void*>(d + o); };
     MSB_CUDA(launch_copy_rows_batch(static_cast<const float* const*>(dp(o_pre_src)),
                                     static_cast<float* const*>(dp(o_pre_dst)), static_cast<const int*>(dp(o_cnt)),
@@ -392,9 +376,42 @@ float* StreamState::memory_row() const { return memory.as<float>() + (size_t)mem
 void StreamState::commit_new_frames(const EncPlan& p, cudaStream_t s) {
     Model& m = *model;
     m.cross_kv_into(memory_row(), p.nnew, memory_len, cross32.as<float>(), cross16.p, mem_cap, s);
+    advance_new_frames(p);
+}
+
+void StreamState::advance_new_frames(const EncPlan& p) {
     pos_offset += p.nnew;
     encoder_frames_emitted = p.stable;
     memory_len += p.nnew;
+}
+
+void commit_new_frames_batch(Model& m, StreamState* const* ss, const StreamState::EncPlan* plans, int n,
+                             cudaStream_t s) {
+    const Config& c = m.cfg;
+    int rows = 0;
+    for (int i = 0; i < n; ++i) rows += plans[i].nnew;
+    if (rows > 0) {
+        const size_t o_dst = ((size_t)rows * 8 + 15) & ~(size_t)15;
+        const size_t total = o_dst + (size_t)rows * sizeof(KvRowDst);
+        char* h = m.kv_tables.host(total);
+        const float** a = reinterpret_cast<const float**>(h);
+        KvRowDst* dst = reinterpret_cast<KvRowDst*>(h + o_dst);
+        int r = 0;
+        for (int i = 0; i < n; ++i) {
+            StreamState& st = *ss[i];
+            const float* mem = st.memory_row();
+            for (int j = 0; j < plans[i].nnew; ++j, ++r) {
+                a[r] = mem + (size_t)j * c.hidden;
+                dst[r] = KvRowDst{st.cross32.as<float>(), st.cross16.p, st.mem_cap, st.memory_len + j};
+            }
+        }
+        char* d = m.kv_tables.upload(total, s);
+        const int N = c.layers * 2 * c.kv_heads * c.head_dim;
+        MSB_CUDA(launch_gemm_f32_kv_rows(reinterpret_cast<const float* const*>(d),
+                                         reinterpret_cast<const KvRowDst*>(d + o_dst), rows, m.cross_w, c.hidden, N,
+                                         c.hidden, c.kv_heads, c.head_dim, s));
+    }
+    for (int i = 0; i < n; ++i) ss[i]->advance_new_frames(plans[i]);
 }
 
 void StreamState::encode_new_frames(bool is_final, EncLane* lane) {  // MoonshineStreaming.swift:178-214

@@ -69,6 +69,9 @@ struct StreamState {
     const float* window(const EncPlan& p) const;
     float* memory_row() const;
     void commit_new_frames(const EncPlan& p, cudaStream_t s);
+    // commit_new_frames without the cross K/V (computed by the caller, e.g. for many streams
+    // at once by commit_new_frames_batch)
+    void advance_new_frames(const EncPlan& p);
     int64_t decode_limit(bool is_final, int32_t max_tokens, Result* done_early);
     Result finish(std::vector<int32_t> ids, bool hit_eos, bool is_final, const ms_streaming_config& sc);
 
@@ -86,5 +89,10 @@ struct StreamState {
 // features, conv1, the new histories, conv2.
 void add_audio_batch(Model& m, StreamState* const* ss, int n, const float* const* chunks, const int64_t* ns,
                      cudaStream_t s);
+
+// commit_new_frames of n streams (plans[i] for ss[i], new memory rows already written at
+// their memory_row()) with one gathered-rows cross K/V launch for all their new rows, on s.
+void commit_new_frames_batch(Model& m, StreamState* const* ss, const StreamState::EncPlan* plans, int n,
+                             cudaStream_t s);
 
 }  // namespace msb
