@@ -158,32 +158,36 @@ __device__ __forceinline__ float load_kv(const void* base, size_t idx, int f16) 
     return f16 ? __half2float(reinterpret_cast<const __half*>(base)[idx]) : reinterpret_cast<const float*>(base)[idx];
 }
 
-// One CTA of SA_WARPS warps per (b, h).  Keys come in rounds of SaShape::KEYS: every thread
+// One CTA of SA_WARPS warps per (b, h).  Keys come in rounds of `keys` (at most SaShape::KEYS,
+// fewer when the call's positions are fewer, which shrinks the shared memory and so raises
+// the CTAs resident per SM): every thread
 // first copies its share of the round's cached K and V rows (from row b's pages; a key
 // without a page -- a row past its own limit -- is skipped) into shared memory with 16-byte
 // cp.async, so a round costs one memory round trip; then warp w scores keys
-// [w KW, (w + 1) KW) of the round (lanes own keys, rows read in 16-byte pieces against q
-// staged in shared memory), keeps an online softmax and accumulates V with lane c owning
-// dims (2c, 2c+1).  Key t is this step's fp32 K/V.  The warp states are merged in warp order.
+// [w kw, (w + 1) kw) of the round, kw = keys / SA_WARPS (lanes own keys, rows read in
+// 16-byte pieces against q staged in shared memory), keeps an online softmax and accumulates
+// V with lane c owning dims (2c, 2c+1).  Key t is this step's fp32 K/V.  The warp states are merged in warp order.
 template <bool F16>
 struct SaShape {
     static constexpr int ESZ = F16 ? 2 : 4;
-    static constexpr int KEYS = F16 ? 128 : 64;  // keys per round
-    static constexpr int KW = KEYS / SA_WARPS;   // keys per warp per round (<= 32)
+    static constexpr int KEYS = F16 ? 128 : 64;  // most keys per round (<= 32 per warp)
 };
 // shared-memory row of hd elements: an odd number of 16-byte pieces, so the eight lanes of
 // one 128-bit phase reading eight different rows hit different bank groups
 __host__ __device__ constexpr int sa_row_pieces(int hd, int esz) { return ((hd * esz) / 16) | 1; }
+// shared memory of a round of `keys` K and V rows of hd elements
 template <bool F16>
-constexpr size_t sa_smem_bytes() {
-    return (size_t)2 * SaShape<F16>::KEYS * sa_row_pieces(MAXHD_B, SaShape<F16>::ESZ) * 16;
+constexpr size_t sa_smem_bytes(int keys, int hd) {
+    return (size_t)2 * keys * sa_row_pieces(hd, SaShape<F16>::ESZ) * 16;
 }
 
-template <bool F16>
+template <bool F16, int KEYS>
 __global__ void __launch_bounds__(SA_WARPS * 32) self_attn_batch_kernel(
     const float* __restrict__ q, const float* __restrict__ kv_new, const PagedKv kv, const int* __restrict__ pos,
     int B, int H, int KVH, int hd, float scale, __nv_bfloat16* __restrict__ out, size_t lo_off) {
     using S = SaShape<F16>;
+    static_assert(KEYS % SA_WARPS == 0 && KEYS <= S::KEYS, "round of whole warp slices");
+    constexpr int keys = KEYS, kw = KEYS / SA_WARPS;  // keys per round, per warp per round
     using E = typename std::conditional<F16, __half, float>::type;
     pdl_wait();
     pdl_trigger();
@@ -206,7 +210,7 @@ __global__ void __launch_bounds__(SA_WARPS * 32) self_attn_batch_kernel(
     const int npc = hd * S::ESZ / 16;                 // 16-byte pieces per row
     const int rse = sa_row_pieces(hd, S::ESZ) * 16 / S::ESZ;  // shared row stride (elements)
     E* ks = reinterpret_cast<E*>(sa_raw);
-    E* vs = ks + (size_t)S::KEYS * rse;
+    E* vs = ks + (size_t)keys * rse;
     // this head's q, staged once and read back as broadcast float4s
     __shared__ __align__(16) float qw[MAXHD_B];
     __shared__ float wm[SA_WARPS], wl[SA_WARPS];
@@ -220,8 +224,8 @@ __global__ void __launch_bounds__(SA_WARPS * 32) self_attn_batch_kernel(
         return phys >= 0 ? (long long)phys * kv.page_elems + (long long)(j % kv.page) * hd : -1ll;
     };
     float m = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f;
-    for (int base = 0; base <= t; base += S::KEYS) {
-        const int ncached = max(0, min(S::KEYS, t - base));  // keys base .. base + ncached - 1 < t
+    for (int base = 0; base <= t; base += keys) {
+        const int ncached = max(0, min(keys, t - base));  // keys base .. base + ncached - 1 < t
         __syncthreads();  // the previous round's rows are consumed (and q is staged)
         for (int i = threadIdx.x; i < 2 * ncached * npc; i += blockDim.x) {
             const int kvsel = i >= ncached * npc, ii = kvsel ? i - ncached * npc : i;
@@ -234,8 +238,8 @@ __global__ void __launch_bounds__(SA_WARPS * 32) self_attn_batch_kernel(
         }
         asm volatile("cp.async.commit_group;\ncp.async.wait_all;\n" ::: "memory");
         __syncthreads();
-        const int k0 = base + w * S::KW;  // this warp's keys k0 .. k0 + KW - 1 (<= t)
-        const int nk = max(0, min(S::KW, t + 1 - k0));
+        const int k0 = base + w * kw;  // this warp's keys k0 .. k0 + kw - 1 (<= t)
+        const int nk = max(0, min(kw, t + 1 - k0));
         if (nk == 0) continue;  // warp-uniform; the barrier of the next round is still taken
         const int j = k0 + lane;
         float s = -INFINITY;
@@ -660,13 +664,25 @@ cudaError_t launch_ln_bf16(const float* x, int rows, int d, const float* w, __nv
 cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const PagedKv& kv, const int* pos, int B,
                                    int H, int KVH, int hd, float scale, __nv_bfloat16* out, cudaStream_t s,
                                    size_t lo_off) {
-    if (hd > MAXHD_B || (hd & 7) || !kv.table || kv.page <= 0 || !kv.pool) return cudaErrorInvalidValue;
+    if (hd > MAXHD_B || (hd & 7) || !kv.table || kv.page <= 0 || !kv.pool || kv.table_stride <= 0)
+        return cudaErrorInvalidValue;
     ++launch_counter();
-    if (kv.kv_f16)
-        return launch_kernel(self_attn_batch_kernel<true>, dim3(B * H), dim3(SA_WARPS * 32), sa_smem_bytes<true>(), s,
-                             q, kv_new, kv, pos, B, H, KVH, hd, scale, out, lo_off);
-    return launch_kernel(self_attn_batch_kernel<false>, dim3(B * H), dim3(SA_WARPS * 32), sa_smem_bytes<false>(), s, q,
-                         kv_new, kv, pos, B, H, KVH, hd, scale, out, lo_off);
+    // every position of the call is below table_stride * page: rounds of that many keys (32,
+    // 64 or 128), at most KEYS
+    const int reach = kv.table_stride * kv.page;
+    auto go = [&](auto f16, auto keys) {
+        constexpr bool F = decltype(f16)::value;
+        constexpr int KS = decltype(keys)::value;
+        return launch_kernel(self_attn_batch_kernel<F, KS>, dim3(B * H), dim3(SA_WARPS * 32), sa_smem_bytes<F>(KS, hd),
+                             s, q, kv_new, kv, pos, B, H, KVH, hd, scale, out, lo_off);
+    };
+    using T_ = std::true_type;
+    using F_ = std::false_type;
+    using K32 = std::integral_constant<int, 32>;
+    using K64 = std::integral_constant<int, 64>;
+    using K128 = std::integral_constant<int, 128>;
+    if (kv.kv_f16) return reach <= 32 ? go(T_(), K32()) : reach <= 64 ? go(T_(), K64()) : go(T_(), K128());
+    return reach <= 32 ? go(F_(), K32()) : go(F_(), K64());
 }
 
 cudaError_t launch_cross_attn_batch(const float* qc, const float* cross32, const void* cross_st, int st_f16,

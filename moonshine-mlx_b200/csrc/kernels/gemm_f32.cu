@@ -3,9 +3,9 @@
 // zero-padded activation buffer), QKV / O / MLP projections with bias, activation and
 // residual fused, and the once-per-utterance cross-attention K/V projection scattered
 // straight into the decoder's KV layout (fp32 and fp16 copies).  Two batched forms for many
-// streaming states at once: GEMMs indexed by blockIdx.z through device tables (the frontend
-// convs), and one GEMM over rows gathered from anywhere with a K/V scatter per row (the cross
-// K/V of every stream's new memory rows).
+// streaming states at once: one GEMM over rows gathered from anywhere (a row pointer each),
+// writing each row to its own place (the frontend convs of every stream) or through a K/V
+// scatter per row (the cross K/V of every stream's new memory rows).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -46,13 +46,15 @@ __device__ __forceinline__ void epilogue_store(const GemmEpilogue& ep, int m, in
 }
 
 // One BM x BN output tile at (blockIdx.y * BM, blockIdx.x * BN).  With a_rows, row m of A is
-// at a_rows[m] (lda unused) and the result goes through the per-row K/V scatter kv_rows[m]
-// (ep gives kv_heads and head_dim); the arithmetic is the same either way.
+// at a_rows[m] (lda unused) and the result goes either through the per-row K/V scatter
+// kv_rows[m] (ep gives kv_heads and head_dim) or, with bias and activation, to out_rows[m];
+// the arithmetic is the same in every form.
 template <int BM>
 __device__ __forceinline__ void gemm_f32_tile(const float* __restrict__ A, int lda, const float* __restrict__ B,
                                               int ldb, int M, int N, int K, const GemmEpilogue& ep,
                                               const float* const* __restrict__ a_rows = nullptr,
-                                              const KvRowDst* __restrict__ kv_rows = nullptr) {
+                                              const KvRowDst* __restrict__ kv_rows = nullptr,
+                                              float* const* __restrict__ out_rows = nullptr) {
     constexpr int TM = BM / 16;          // rows per thread
     constexpr int A_F4 = BM * BK / 4;    // float4 per A tile
     constexpr int A_PER_T = A_F4 / NT;   // 2 (BM=128) or 1 (BM=64)
@@ -152,6 +154,20 @@ __device__ __forceinline__ void gemm_f32_tile(const float* __restrict__ A, int l
             }
             continue;
         }
+        if (out_rows) {
+            float* o = out_rows[m];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int n = n0 + tx * 4 + j;
+                if (n >= N) continue;
+                float v = acc[i][j];
+                if (ep.bias) v += ep.bias[n];
+                if (ep.act == ACT_SILU) v = silu(v);
+                else if (ep.act == ACT_GELU) v = gelu_erf(v);
+                o[n] = v;
+            }
+            continue;
+        }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int n = n0 + tx * 4 + j;
@@ -168,24 +184,29 @@ __global__ void __launch_bounds__(NT) gemm_f32_kernel(const float* __restrict__ 
 }
 
 template <int BM>
-__global__ void __launch_bounds__(NT) gemm_f32_kv_rows_kernel(const float* const* __restrict__ a_rows,
-                                                               const KvRowDst* __restrict__ dst, int M,
-                                                               const float* __restrict__ B, int ldb, int N, int K,
-                                                               GemmEpilogue ep) {
-    gemm_f32_tile<BM>(nullptr, 0, B, ldb, M, N, K, ep, a_rows, dst);
+__global__ void __launch_bounds__(NT) gemm_f32_rows_kernel(const float* const* __restrict__ a_rows,
+                                                            const KvRowDst* __restrict__ kv_rows,
+                                                            float* const* __restrict__ out_rows, int M,
+                                                            const float* __restrict__ B, int ldb, int N, int K,
+                                                            GemmEpilogue ep) {
+    gemm_f32_tile<BM>(nullptr, 0, B, ldb, M, N, K, ep, a_rows, kv_rows, out_rows);
 }
 
-// GEMM blockIdx.z of a batch (tables in device memory); tiles past its M rows return at once.
-template <int BM>
-__global__ void __launch_bounds__(NT) gemm_f32_batch_kernel(const float* const* __restrict__ As,
-                                                             const int* __restrict__ Ms,
-                                                             float* const* __restrict__ outs, int lda,
-                                                             const float* __restrict__ B, int ldb, int N, int K,
-                                                             GemmEpilogue ep) {
-    const int z = blockIdx.z, M = Ms[z];
-    if ((int)blockIdx.y * BM >= M) return;
-    ep.out = outs[z];
-    gemm_f32_tile<BM>(As[z], lda, B, ldb, M, N, K, ep);
+cudaError_t launch_rows(const float* const* a_rows, const KvRowDst* kv_rows, float* const* out_rows, int M,
+                        const float* B, int ldb, int N, int K, const GemmEpilogue& ep, cudaStream_t stream) {
+    if (M <= 0 || N <= 0) return cudaSuccess;
+    if ((K & 3) || (ldb & 3) || (reinterpret_cast<uintptr_t>(B) & 15) || (M + 63) / 64 > 65535)
+        return cudaErrorInvalidValue;
+    const int gx = (N + BN - 1) / BN;
+    ++launch_counter();
+    if ((long long)gx * ((M + 127) / 128) >= 2 * 148) {
+        dim3 grid(gx, (M + 127) / 128);
+        gemm_f32_rows_kernel<128><<<grid, NT, 0, stream>>>(a_rows, kv_rows, out_rows, M, B, ldb, N, K, ep);
+    } else {
+        dim3 grid(gx, (M + 63) / 64);
+        gemm_f32_rows_kernel<64><<<grid, NT, 0, stream>>>(a_rows, kv_rows, out_rows, M, B, ldb, N, K, ep);
+    }
+    return cudaGetLastError();
 }
 
 }  // namespace
@@ -209,44 +230,22 @@ cudaError_t launch_gemm_f32(const float* A, int lda, const float* B, int ldb, in
     return cudaGetLastError();
 }
 
-cudaError_t launch_gemm_f32_batch(const float* const* A, const int* M, float* const* out, int nb, int m_max,
-                                  int lda, const float* B, int ldb, int N, int K, const GemmEpilogue& ep,
-                                  cudaStream_t stream) {
-    if (nb <= 0 || m_max <= 0 || N <= 0) return cudaSuccess;
-    if ((K & 3) || (lda & 3) || (ldb & 3) || (reinterpret_cast<uintptr_t>(B) & 15) || ep.kv_scatter ||
-        ep.residual || nb > 65535)
-        return cudaErrorInvalidValue;
-    const int gx = (N + BN - 1) / BN;
-    ++launch_counter();
-    if (m_max > 64 && (long long)gx * ((m_max + 127) / 128) * nb >= 2 * 148) {
-        dim3 grid(gx, (m_max + 127) / 128, nb);
-        gemm_f32_batch_kernel<128><<<grid, NT, 0, stream>>>(A, M, out, lda, B, ldb, N, K, ep);
-    } else {
-        dim3 grid(gx, (m_max + 63) / 64, nb);
-        gemm_f32_batch_kernel<64><<<grid, NT, 0, stream>>>(A, M, out, lda, B, ldb, N, K, ep);
-    }
-    return cudaGetLastError();
+cudaError_t launch_gemm_f32_rows(const float* const* a_rows, float* const* out_rows, int M, const float* B, int ldb,
+                                 int N, int K, const float* bias, int act, cudaStream_t stream) {
+    GemmEpilogue ep;
+    ep.bias = bias;
+    ep.act = act;
+    return launch_rows(a_rows, nullptr, out_rows, M, B, ldb, N, K, ep, stream);
 }
 
 cudaError_t launch_gemm_f32_kv_rows(const float* const* a_rows, const KvRowDst* dst, int M, const float* B, int ldb,
                                     int N, int K, int kv_heads, int head_dim, cudaStream_t stream) {
-    if (M <= 0 || N <= 0) return cudaSuccess;
-    if ((K & 3) || (ldb & 3) || (reinterpret_cast<uintptr_t>(B) & 15) || kv_heads <= 0 || head_dim <= 0)
-        return cudaErrorInvalidValue;
+    if (kv_heads <= 0 || head_dim <= 0) return cudaErrorInvalidValue;
     GemmEpilogue ep;
     ep.kv_scatter = 1;
     ep.kv_heads = kv_heads;
     ep.head_dim = head_dim;
-    const int gx = (N + BN - 1) / BN;
-    ++launch_counter();
-    if ((long long)gx * ((M + 127) / 128) >= 2 * 148) {
-        dim3 grid(gx, (M + 127) / 128);
-        gemm_f32_kv_rows_kernel<128><<<grid, NT, 0, stream>>>(a_rows, dst, M, B, ldb, N, K, ep);
-    } else {
-        dim3 grid(gx, (M + 63) / 64);
-        gemm_f32_kv_rows_kernel<64><<<grid, NT, 0, stream>>>(a_rows, dst, M, B, ldb, N, K, ep);
-    }
-    return cudaGetLastError();
+    return launch_rows(a_rows, dst, nullptr, M, B, ldb, N, K, ep, stream);
 }
 
 cudaError_t preload_gemm_f32() {

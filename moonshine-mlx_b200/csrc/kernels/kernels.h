@@ -92,13 +92,11 @@ struct GemmEpilogue {
 };
 cudaError_t launch_gemm_f32(const float* A, int lda, const float* B, int ldb, int M, int N,
                             int K, const GemmEpilogue& ep, cudaStream_t stream);
-// nb GEMMs sharing B, N, K and the epilogue except its output, in one launch: GEMM z reads
-// A[z] (M[z] rows, lda apart) and writes out[z] (device tables; every A[z] 16-byte aligned,
-// m_max >= every M[z]).  Each output element is the same as launch_gemm_f32's.  No K/V
-// scatter or residual.
-cudaError_t launch_gemm_f32_batch(const float* const* A, const int* M, float* const* out, int nb, int m_max,
-                                  int lda, const float* B, int ldb, int N, int K, const GemmEpilogue& ep,
-                                  cudaStream_t stream);
+// C = act(A B^T + bias) over M rows gathered from anywhere: row r of A at a_rows[r] (16-byte
+// aligned, K floats), its result at out_rows[r] (device tables).  Each value is the same as
+// launch_gemm_f32 gives.
+cudaError_t launch_gemm_f32_rows(const float* const* a_rows, float* const* out_rows, int M, const float* B, int ldb,
+                                 int N, int K, const float* bias, int act, cudaStream_t stream);
 // Where row r of a gathered-rows cross K/V GEMM lands: the K/V scatter of GemmEpilogue
 // into out32 / out16 (either nullable) with frame_cap rows per segment, at frame frame_row.
 struct KvRowDst {

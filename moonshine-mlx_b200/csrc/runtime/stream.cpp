@@ -141,8 +141,8 @@ struct FrontJob {
     size_t aoff, x1, x2;  // offsets (floats) of the frames in the upload and of the conv inputs in fe_x
 };
 
-void frontend_pass(Model& m, const std::vector<FrontJob>& jobs, size_t audio_f, size_t x_f, int nf_max, int t2_max,
-                   int t3_max, cudaStream_t s) {
+void frontend_pass(Model& m, const std::vector<FrontJob>& jobs, size_t audio_f, size_t x_f, int nf_max, int rows1,
+                   int rows2, cudaStream_t s) {
     const Config& c = m.cfg;
     const int fl = c.frame_len(), ed = c.e_hidden, nb = (int)jobs.size();
     const size_t tb = (audio_f * 4 + 15) & ~(size_t)15;
@@ -155,10 +155,10 @@ void frontend_pass(Model& m, const std::vector<FrontJob>& jobs, size_t audio_f, 
     const size_t o_aoff = take(8 * (size_t)nb), o_ffout = take(8 * (size_t)nb);
     const size_t o_pre_src = take(16 * (size_t)nb), o_pre_dst = take(16 * (size_t)nb);
     const size_t o_post_src = take(16 * (size_t)nb), o_post_dst = take(16 * (size_t)nb);
-    const size_t o_g1a = take(8 * (size_t)nb), o_g1o = take(8 * (size_t)nb);
-    const size_t o_g2a = take(8 * (size_t)nb), o_g2o = take(8 * (size_t)nb);
+    // conv1 / conv2 as implicit GEMMs over every stream's rows: A row and output row pointers
+    const size_t o_g1a = take(8 * (size_t)rows1), o_g1o = take(8 * (size_t)rows1);
+    const size_t o_g2a = take(8 * (size_t)rows2), o_g2o = take(8 * (size_t)rows2);
     const size_t o_nf = take(4 * (size_t)nb), o_cnt = take(8 * (size_t)nb);
-    const size_t o_m1 = take(4 * (size_t)nb), o_m2 = take(4 * (size_t)nb);
     const size_t total = off;
 
     // conv inputs (grow by half again at least, so a slowly growing batch rarely reallocates)
@@ -190,8 +190,7 @@ void frontend_pass(Model& m, const std::vector<FrontJob>& jobs, size_t audio_f, 
     float** g2o = static_cast<float**>(hp(o_g2o));
     int* nfv = static_cast<int*>(hp(o_nf));
     int* cnt = static_cast<int*>(hp(o_cnt));
-    int* m1 = static_cast<int*>(hp(o_m1));
-    int* m2 = static_cast<int*>(hp(o_m2));
+    int r1 = 0, r2 = 0;
     for (int z = 0; z < nb; ++z) {
         const FrontJob& j = jobs[z];
         StreamState& st = *j.st;
@@ -217,12 +216,17 @@ void frontend_pass(Model& m, const std::vector<FrontJob>& jobs, size_t audio_f, 
         post_dst[nb + z] = st.conv2_buf.as<float>();
         cnt[z] = 4 * ed;
         cnt[nb + z] = 4 * 2 * ed;
-        g1a[z] = x1;
-        g1o[z] = x2 + 4 * 2 * ed;
-        m1[z] = j.T2;
-        g2a[z] = x2;
-        g2o[z] = st.features.as<float>() + (size_t)st.feat_count * ed;
-        m2[z] = j.T3;
+        // conv1 row t reads x1 rows 2t..2t+4 (stride 2, kernel 5) and lands in x2 row 4 + t;
+        // conv2 row t reads x2 rows 2t..2t+4 and lands in feature row feat_count + t
+        for (int t = 0; t < j.T2; ++t, ++r1) {
+            g1a[r1] = x1 + (size_t)t * 2 * ed;
+            g1o[r1] = x2 + (size_t)(4 + t) * 2 * ed;
+        }
+        float* feat = st.features.as<float>() + (size_t)st.feat_count * ed;
+        for (int t = 0; t < j.T3; ++t, ++r2) {
+            g2a[r2] = x2 + (size_t)t * 4 * ed;
+            g2o[r2] = feat + (size_t)t * ed;
+        }
     }
     char* d = m.fe_tables.upload(total, s);
     auto dp = [&](size_t o) { return reinterpret_cast<void*>(d + o); };
@@ -232,19 +236,10 @@ void frontend_pass(Model& m, const std::vector<FrontJob>& jobs, size_t audio_f, 
     MSB_CUDA(launch_frame_features_batch(reinterpret_cast<const float*>(d), static_cast<const long long*>(dp(o_aoff)),
                                          static_cast<const int*>(dp(o_nf)), static_cast<float* const*>(dp(o_ffout)),
                                          nb, nf_max, fl, m.log_k, m.lin_w, ed, ed, s));
-    GemmEpilogue c1;
-    c1.bias = m.conv1_b;
-    c1.act = ACT_SILU;
-    c1.ldc = 2 * ed;
-    MSB_CUDA(launch_gemm_f32_batch(static_cast<const float* const*>(dp(o_g1a)), static_cast<const int*>(dp(o_m1)),
-                                   static_cast<float* const*>(dp(o_g1o)), nb, t2_max, 2 * ed, m.conv1_w, 5 * ed,
-                                   2 * ed, 5 * ed, c1, s));
-    GemmEpilogue c2;
-    c2.bias = m.conv2_b;
-    c2.ldc = ed;
-    MSB_CUDA(launch_gemm_f32_batch(static_cast<const float* const*>(dp(o_g2a)), static_cast<const int*>(dp(o_m2)),
-                                   static_cast<float* const*>(dp(o_g2o)), nb, t3_max, 4 * ed, m.conv2_w, 10 * ed,
-                                   ed, 10 * ed, c2, s));
+    MSB_CUDA(launch_gemm_f32_rows(static_cast<const float* const*>(dp(o_g1a)), static_cast<float* const*>(dp(o_g1o)),
+                                  rows1, m.conv1_w, 5 * ed, 2 * ed, 5 * ed, m.conv1_b, ACT_SILU, s));
+    MSB_CUDA(launch_gemm_f32_rows(static_cast<const float* const*>(dp(o_g2a)), static_cast<float* const*>(dp(o_g2o)),
+                                  rows2, m.conv2_w, 10 * ed, ed, 10 * ed, m.conv2_b, ACT_NONE, s));
     MSB_CUDA(launch_copy_rows_batch(static_cast<const float* const*>(dp(o_post_src)),
                                     static_cast<float* const*>(dp(o_post_dst)), static_cast<const int*>(dp(o_cnt)),
                                     2 * nb, s));
@@ -280,15 +275,17 @@ void add_audio_batch(Model& m, StreamState* const* ss, int n, const float* const
     for (int i = 0; i < n; ++i)
         if ((int64_t)(ss[i]->sample_buffer.size() + (size_t)ns[i]) / fl > (1 << 24))
             throw MsError(MS_ERR_INVALID_ARG, "audio chunk too long");
-    constexpr int kGroup = 16384;  // streams per pass (launch grids take up to 65535 in y and z)
+    // streams per pass (the frame-feature grid takes up to 65535 streams in y) and conv rows
+    // per pass (the conv GEMM grids take up to 65535 row tiles)
+    constexpr int kGroup = 16384, kRows = 1 << 20;
     std::vector<FrontJob> jobs;
     size_t audio_f = 0, x_f = 0;
-    int nf_max = 0, t2_max = 0, t3_max = 0;
+    int nf_max = 0, rows1 = 0, rows2 = 0;
     auto flush = [&]() {
-        if (!jobs.empty()) frontend_pass(m, jobs, audio_f, x_f, nf_max, t2_max, t3_max, s);
+        if (!jobs.empty()) frontend_pass(m, jobs, audio_f, x_f, nf_max, rows1, rows2, s);
         jobs.clear();
         audio_f = x_f = 0;
-        nf_max = t2_max = t3_max = 0;
+        nf_max = rows1 = rows2 = 0;
     };
     for (int i = 0; i < n; ++i) {
         StreamState& st = *ss[i];
@@ -312,10 +309,10 @@ void add_audio_batch(Model& m, StreamState* const* ss, int n, const float* const
         j.x2 = x_f;
         x_f += (size_t)(4 + j.T2) * 2 * ed;
         nf_max = std::max(nf_max, nf);
-        t2_max = std::max(t2_max, j.T2);
-        t3_max = std::max(t3_max, j.T3);
+        rows1 += j.T2;
+        rows2 += j.T3;
         jobs.push_back(j);
-        if ((int)jobs.size() == kGroup) flush();
+        if ((int)jobs.size() == kGroup || rows1 > kRows) flush();
     }
     flush();
 }
