@@ -111,44 +111,44 @@ void BatchEngine::ensure_ws(int B, int T, int Mtot, int maxM) {
     if (B > Bc) {
         Bc = B;
         remap = true;
-        x.ensure((size_t)Bc * d * 4);
-        hb.ensure((size_t)Bc * d * 2 * P);
-        attn.ensure((size_t)Bc * HD * 2 * P);
-        g.ensure((size_t)Bc * I * 2 * P);
-        q.ensure((size_t)Bc * HD * 4);
-        qc.ensure((size_t)Bc * HD * 4);
-        kvnew.ensure((size_t)Bc * 2 * KVD * 4);
-        amax.ensure((size_t)Bc * 8);
-        next_ids.ensure((size_t)Bc * 4);
-        counts.ensure((size_t)Bc * 4);
-        limits_d.ensure((size_t)Bc * 4);
-        done.ensure((size_t)Bc * 4);
-        hit.ensure((size_t)Bc * 4);
-        frame_off.ensure((size_t)Bc * 4);
-        frames.ensure((size_t)Bc * 4);
-        lnst.ensure((size_t)((d + kStatTile - 1) / kStatTile) * Bc * sizeof(float2));
+        grow(x, (size_t)Bc * d * 4);
+        grow(hb, (size_t)Bc * d * 2 * P);
+        grow(attn, (size_t)Bc * HD * 2 * P);
+        grow(g, (size_t)Bc * I * 2 * P);
+        grow(q, (size_t)Bc * HD * 4);
+        grow(qc, (size_t)Bc * HD * 4);
+        grow(kvnew, (size_t)Bc * 2 * KVD * 4);
+        grow(amax, (size_t)Bc * 8);
+        grow(next_ids, (size_t)Bc * 4);
+        grow(counts, (size_t)Bc * 4);
+        grow(limits_d, (size_t)Bc * 4);
+        grow(done, (size_t)Bc * 4);
+        grow(hit, (size_t)Bc * 4);
+        grow(frame_off, (size_t)Bc * 4);
+        grow(frames, (size_t)Bc * 4);
+        grow(lnst, (size_t)((d + kStatTile - 1) / kStatTile) * Bc * sizeof(float2));
     }
     // capacities grow by half again at least, so a workload that grows a little per call
     // (streams whose memories lengthen every chunk) reallocates rarely
-    auto grow = [](int cur, int need) { return need <= cur ? cur : std::max(need, cur + cur / 2); };
+    auto cap_for = [](int cur, int need) { return need <= cur ? cur : std::max(need, cur + cur / 2); };
     if (T > Tc || remap) {
-        Tc = grow(Tc, T);
-        ids.ensure((size_t)Bc * Tc * 4);
+        Tc = cap_for(Tc, T);
+        grow(ids, (size_t)Bc * Tc * 4);
     }
     (void)kvsz;
     if (Mtot > Mc) {
-        Mc = grow(Mc, Mtot);
+        Mc = cap_for(Mc, Mtot);
         const size_t n = (size_t)c.layers * 2 * KVD * Mc;
-        cross32.ensure(n * 4);
-        cross16.ensure(n * 2);
-        memory.ensure((size_t)Mc * d * 4);
+        grow(cross32, n * 4);
+        grow(cross16, n * 2);
+        grow(memory, (size_t)Mc * d * 4);
     }
     if (maxM > Fc || remap) {
-        Fc = grow(Fc, maxM);
-        part.ensure(cross_batch_part_floats(Bc, c.heads, c.head_dim, Fc) * 4);
+        Fc = cap_for(Fc, maxM);
+        grow(part, cross_batch_part_floats(Bc, c.heads, c.head_dim, Fc) * 4);
     }
-    status.ensure(16);
-    pos.ensure(16);
+    grow(status, 16);
+    grow(pos, 16);
     if (remap) {
         make_a_map(&a_hb, hb.as<__nv_bfloat16>(), Bc, d);
         make_a_map(&a_attn, attn.as<__nv_bfloat16>(), Bc, HD);
@@ -177,10 +177,10 @@ void BatchEngine::assign_pages(int B, int T, const std::vector<int>& limits) {
         for (int q = 0; q < need && q < table_stride; ++q) tab[(size_t)b * table_stride + q] = (int)next++;
     }
     const size_t page_bytes = (size_t)c.layers * 2 * KVD * kKvPage * 4;  // fp32-sized: the KV dtype may change
-    kvpool.ensure((size_t)std::max<int64_t>(next, 1) * page_bytes);
+    grow(kvpool, (size_t)std::max<int64_t>(next, 1) * page_bytes);
     pages_used = next;
     pages_capacity = (int64_t)(kvpool.bytes / page_bytes);
-    ptable.ensure(tab.size() * 4);
+    grow(ptable, tab.size() * 4);
     MSB_CUDA(cudaMemcpyAsync(ptable.p, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, m.stream));
     // the host vector goes away at return: the copy must have read it
     MSB_CUDA(cudaStreamSynchronize(m.stream));
@@ -412,10 +412,10 @@ void BatchEngine::encoder_layers_tc(size_t rows3, int R3, const int* seg_len) {
     const size_t P = esplit ? 2 : 1;
     const size_t cap = enc_rows_capacity(rows3);  // low planes sit cap rows behind the high ones
     const size_t lo_h = esplit ? cap * ed : 0, lo_attn = esplit ? cap * eHD : 0, lo_f = esplit ? cap * EI : 0;
-    eh.ensure(cap * ed * 2 * P);
-    eqkv.ensure(cap * QKV * 4);
-    eattn.ensure(cap * eHD * 2 * P);
-    ef.ensure(cap * EI * 2 * P);
+    grow(eh, cap * ed * 2 * P);
+    grow(eqkv, cap * QKV * 4);
+    grow(eattn, cap * eHD * 2 * P);
+    grow(ef, cap * EI * 2 * P);
     float* X = ex.as<float>();
     auto amap = [&](CUtensorMap* hi, CUtensorMap* lo, const __nv_bfloat16* p, size_t rows, int K, size_t lo_off) {
         make_a_map(hi, p, (int)rows, K);
@@ -516,13 +516,13 @@ bool BatchEngine::encode_tc(const std::vector<const float*>& audio_dev, const st
     const size_t lo_norm = esplit ? rows1 * fl : 0, lo_pad1 = esplit ? rows1 * ed : 0;
     const size_t lo_pad2 = esplit ? rows2 * 2 * ed : 0;
     const size_t lo_mem = esplit ? (size_t)Mc * d : 0;
-    enorm.ensure(rows1 * fl * 2 * P);
-    eaud.ensure((size_t)B * sizeof(float*));
-    epad1.ensure(rows1 * ed * 2 * P);
-    epad2.ensure(rows2 * 2 * ed * 2 * P);
-    ex.ensure(enc_rows_capacity(rows3) * ed * 4);
-    emem16.ensure((size_t)Mc * d * 2 * P);
-    eseg.ensure((size_t)3 * B * 4);
+    grow(enorm, rows1 * fl * 2 * P);
+    grow(eaud, (size_t)B * sizeof(float*));
+    grow(epad1, rows1 * ed * 2 * P);
+    grow(epad2, rows2 * 2 * ed * 2 * P);
+    grow(ex, enc_rows_capacity(rows3) * ed * 4);
+    grow(emem16, (size_t)Mc * d * 2 * P);
+    grow(eseg, (size_t)3 * B * 4);
     __nv_bfloat16* pad1 = epad1.as<__nv_bfloat16>();
     __nv_bfloat16* pad2 = epad2.as<__nv_bfloat16>();
     float* X = ex.as<float>();
@@ -668,8 +668,8 @@ bool BatchEngine::encode_windows(const std::vector<StreamWindow>& w) {
     const size_t rows3 = (size_t)B * R3;
     ensure_enc_weights();
     cudaStream_t s = m.stream;
-    ex.ensure(enc_rows_capacity(rows3) * ed * 4);
-    status.ensure(16);
+    grow(ex, enc_rows_capacity(rows3) * ed * 4);
+    grow(status, 16);
     // tables: src[B], dst[B] pointers, then T, off, cnt, pos
     std::vector<unsigned char> tab((size_t)B * (2 * sizeof(void*) + 4 * sizeof(int)));
     const void** srcp = reinterpret_cast<const void**>(tab.data());
@@ -683,7 +683,7 @@ bool BatchEngine::encode_windows(const std::vector<StreamWindow>& w) {
         ints[2 * B + b] = w[b].nnew;
         ints[3 * B + b] = w[b].pos;
     }
-    wtab.ensure(tab.size());
+    grow(wtab, tab.size());
     MSB_CUDA(cudaMemcpyAsync(wtab.p, tab.data(), tab.size(), cudaMemcpyHostToDevice, s));
     MSB_CUDA(cudaMemsetAsync(status.p, 0, 16, s));
     const char* t = reinterpret_cast<const char*>(wtab.p);
@@ -775,7 +775,7 @@ BatchEngine::Result BatchEngine::run_cross(const std::vector<CrossSrc>& src, con
         ptrs[b] = src[b].c32;
         ptrs[B + b] = m.kv_f16 ? src[b].c16 : (in_place ? src[b].c32 : nullptr);
     }
-    xsrc.ensure((size_t)2 * B * sizeof(void*) + (size_t)B * 4);
+    grow(xsrc, (size_t)2 * B * sizeof(void*) + (size_t)B * 4);
     char* tab = reinterpret_cast<char*>(xsrc.p);
     MSB_CUDA(cudaMemcpyAsync(tab, ptrs.data(), ptrs.size() * sizeof(void*), cudaMemcpyHostToDevice, s));
     MSB_CUDA(cudaMemcpyAsync(tab + 2 * B * sizeof(void*), mcap.data(), (size_t)B * 4, cudaMemcpyHostToDevice, s));

@@ -13,6 +13,9 @@ namespace msb {
 struct BatchEngine {
     // fp32 checkpoints (not forced to bf16) take split operands in every GEMM
     explicit BatchEngine(Model& model) : m(model), split(!model.enc_bf16), esplit(!model.enc_bf16) {}
+    // growth of the engine's scratch, stream-ordered on the model stream from the model's pool
+    // (a cudaFree / cudaMalloc pair in the middle of serving stalled for up to ~0.8 s)
+    void grow(DevBuf& b, size_t n) { b.ensure_on(n, m.stream, m.streams_pool()); }
     ~BatchEngine();
 
     static constexpr int kKvPage = 16;  // positions per self-attention K/V page

@@ -59,12 +59,21 @@ char* TableUpload::host(size_t bytes) {
     return stage;
 }
 
-char* TableUpload::upload(size_t bytes, cudaStream_t s) {
+char* TableUpload::upload(size_t bytes, cudaStream_t s, cudaMemPool_t pool) {
     // grows by half again at least, so a slowly growing call rarely reallocates
-    if (bytes > dev.bytes) dev.ensure(std::max(bytes, dev.bytes + dev.bytes / 2));
+    if (bytes > dev.bytes) dev.ensure_on(std::max(bytes, dev.bytes + dev.bytes / 2), s, pool);
     MSB_CUDA(cudaMemcpyAsync(dev.p, stage, bytes, cudaMemcpyHostToDevice, s));
     MSB_CUDA(cudaEventRecord(done, s));
     return dev.as<char>();
+}
+
+void DevBuf::ensure_on(size_t n, cudaStream_t s, cudaMemPool_t pool) {
+    if (n <= bytes) return;
+    if (p) MSB_CUDA(cudaFreeAsync(p, s));
+    p = nullptr;
+    bytes = 0;
+    MSB_CUDA(cudaMallocFromPoolAsync(&p, n, pool, s));
+    bytes = n;
 }
 
 void DevBuf::ensure(size_t n) {

@@ -62,6 +62,10 @@ struct DevBuf {
     DevBuf& operator=(const DevBuf&) = delete;
     ~DevBuf();
     void ensure(size_t n);
+    // ensure, stream-ordered: the old block is freed on s and the new one taken from `pool`
+    // on s (neither synchronises the device nor, once the pool holds freed blocks, maps new
+    // memory); for buffers used only on s.  The contents are not kept.
+    void ensure_on(size_t n, cudaStream_t s, cudaMemPool_t pool);
     template <class T> T* as() const { return reinterpret_cast<T*>(p); }
 };
 
@@ -79,8 +83,9 @@ struct TableUpload {
     ~TableUpload();
     // Host area of at least `bytes` (waits for the previous upload from it).
     char* host(size_t bytes);
-    // Uploads the first `bytes` on s; returns the device address of the area.
-    char* upload(size_t bytes, cudaStream_t s);
+    // Uploads the first `bytes` on s (the device copy grows stream-ordered from `pool`);
+    // returns the device address of the area.
+    char* upload(size_t bytes, cudaStream_t s, cudaMemPool_t pool);
 };
 
 struct EncLayer {

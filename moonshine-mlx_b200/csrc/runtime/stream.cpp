@@ -162,7 +162,8 @@ void frontend_pass(Model& m, const std::vector<FrontJob>& jobs, size_t audio_f, 
     const size_t total = off;
 
     // conv inputs (grow by half again at least, so a slowly growing batch rarely reallocates)
-    if (x_f * 4 > m.fe_x.bytes) m.fe_x.ensure(std::max(x_f * 4, m.fe_x.bytes + m.fe_x.bytes / 2));
+    if (x_f * 4 > m.fe_x.bytes)
+        m.fe_x.ensure_on(std::max(x_f * 4, m.fe_x.bytes + m.fe_x.bytes / 2), s, m.streams_pool());
     // per-stream buffers, allocated and grown stream-ordered before the tables point at them
     for (const FrontJob& j : jobs) {
         StreamState& st = *j.st;
@@ -228,7 +229,7 @@ void frontend_pass(Model& m, const std::vector<FrontJob>& jobs, size_t audio_f, 
             g2o[r2] = feat + (size_t)t * ed;
         }
     }
-    char* d = m.fe_tables.upload(total, s);
+    char* d = m.fe_tables.upload(total, s, m.streams_pool());
     auto dp = [&](size_t o) { return reinterpret_cast<void*>(d + o); };
     MSB_CUDA(launch_copy_rows_batch(static_cast<const float* const*>(dp(o_pre_src)),
                                     static_cast<float* const*>(dp(o_pre_dst)), static_cast<const int*>(dp(o_cnt)),
@@ -402,7 +403,7 @@ void commit_new_frames_batch(Model& m, StreamState* const* ss, const StreamState
                 dst[r] = KvRowDst{st.cross32.as<float>(), st.cross16.p, st.mem_cap, st.memory_len + j};
             }
         }
-        char* d = m.kv_tables.upload(total, s);
+        char* d = m.kv_tables.upload(total, s, m.streams_pool());
         const int N = c.layers * 2 * c.kv_heads * c.head_dim;
         MSB_CUDA(launch_gemm_f32_kv_rows(reinterpret_cast<const float* const*>(d),
                                          reinterpret_cast<const KvRowDst*>(d + o_dst), rows, m.cross_w, c.hidden, N,
