@@ -382,10 +382,12 @@ def leg_streaming(mb, synth, torch, dist, barrier, rank, world, local, root, n_s
     t_all0.record(s)
     for k in range(n_chunks):
         e0, e1 = _events(torch, s)
+        torch.cuda.nvtx.range_push(f"streaming_chunk_{k}")  # one chunk's kernels, for ncu --nvtx
         e0.record(s)
         m.add_audio_batch(states, [audio[i][k * chunk:(k + 1) * chunk] for i in mine])
         out = m.transcribe_batch(states, is_final=False, streaming_config=sc, max_tokens=max_tokens)
         e1.record(s)
+        torch.cuda.nvtx.range_pop()
         toks += sum(len(o[0]) for o in out)
         lat.append((e0, e1))
     t_all1.record(s)
