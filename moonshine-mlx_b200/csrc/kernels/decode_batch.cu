@@ -158,13 +158,14 @@ __device__ __forceinline__ float load_kv(const void* base, size_t idx, int f16) 
     return f16 ? __half2float(reinterpret_cast<const __half*>(base)[idx]) : reinterpret_cast<const float*>(base)[idx];
 }
 
-// One CTA of SA_WARPS warps per (b, h).  Keys come in rounds of `keys` (at most SaShape::KEYS,
+// One CTA of W warps per (b, h) (SA_WARPS; one warp when a round of 32 keys covers the
+// whole call).  Keys come in rounds of `keys` (at most SaShape::KEYS,
 // fewer when the call's positions are fewer, which shrinks the shared memory and so raises
 // the CTAs resident per SM): every thread
 // first copies its share of the round's cached K and V rows (from row b's pages; a key
 // without a page -- a row past its own limit -- is skipped) into shared memory with 16-byte
 // cp.async, so a round costs one memory round trip; then warp w scores keys
-// [w kw, (w + 1) kw) of the round, kw = keys / SA_WARPS (lanes own keys, rows read in
+// [w kw, (w + 1) kw) of the round, kw = keys / W (lanes own keys, rows read in
 // 16-byte pieces against q staged in shared memory), keeps an online softmax and accumulates
 // V with lane c owning dims (2c, 2c+1).  Key t is this step's fp32 K/V.  The warp states are merged in warp order.
 template <bool F16>
@@ -181,13 +182,13 @@ constexpr size_t sa_smem_bytes(int keys, int hd) {
     return (size_t)2 * keys * sa_row_pieces(hd, SaShape<F16>::ESZ) * 16;
 }
 
-template <bool F16, int KEYS>
-__global__ void __launch_bounds__(SA_WARPS * 32) self_attn_batch_kernel(
+template <bool F16, int KEYS, int W>
+__global__ void __launch_bounds__(W * 32) self_attn_batch_kernel(
     const float* __restrict__ q, const float* __restrict__ kv_new, const PagedKv kv, const int* __restrict__ pos,
     int B, int H, int KVH, int hd, float scale, __nv_bfloat16* __restrict__ out, size_t lo_off) {
     using S = SaShape<F16>;
-    static_assert(KEYS % SA_WARPS == 0 && KEYS <= S::KEYS, "round of whole warp slices");
-    constexpr int keys = KEYS, kw = KEYS / SA_WARPS;  // keys per round, per warp per round
+    static_assert(KEYS % W == 0 && KEYS / W <= 32 && KEYS <= S::KEYS, "round of whole warp slices");
+    constexpr int keys = KEYS, kw = KEYS / W;  // keys per round, per warp per round
     using E = typename std::conditional<F16, __half, float>::type;
     pdl_wait();
     pdl_trigger();
@@ -213,8 +214,8 @@ __global__ void __launch_bounds__(SA_WARPS * 32) self_attn_batch_kernel(
     E* vs = ks + (size_t)keys * rse;
     // this head's q, staged once and read back as broadcast float4s
     __shared__ __align__(16) float qw[MAXHD_B];
-    __shared__ float wm[SA_WARPS], wl[SA_WARPS];
-    __shared__ float wacc[SA_WARPS][MAXHD_B];
+    __shared__ float wm[W], wl[W];
+    __shared__ float wacc[W][MAXHD_B];
     for (int c = threadIdx.x; c < hd; c += blockDim.x) qw[c] = qr[c];
     const float4* q4 = reinterpret_cast<const float4*>(qw);
     // pool element offset of cached key j's row, or -1 (no page)
@@ -310,10 +311,10 @@ __global__ void __launch_bounds__(SA_WARPS * 32) self_attn_batch_kernel(
     for (int e = threadIdx.x; e < hd; e += blockDim.x) {
         float mx = -INFINITY;
 #pragma unroll
-        for (int qq = 0; qq < SA_WARPS; ++qq) mx = fmaxf(mx, wm[qq]);
+        for (int qq = 0; qq < W; ++qq) mx = fmaxf(mx, wm[qq]);
         float lsum = 0.f, o = 0.f;
 #pragma unroll
-        for (int qq = 0; qq < SA_WARPS; ++qq) {
+        for (int qq = 0; qq < W; ++qq) {
             if (wm[qq] == -INFINITY) continue;
             const float f = expf(wm[qq] - mx);
             lsum = fmaf(wl[qq], f, lsum);
@@ -673,7 +674,8 @@ cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const Pa
     auto go = [&](auto f16, auto keys) {
         constexpr bool F = decltype(f16)::value;
         constexpr int KS = decltype(keys)::value;
-        return launch_kernel(self_attn_batch_kernel<F, KS>, dim3(B * H), dim3(SA_WARPS * 32), sa_smem_bytes<F>(KS, hd),
+        constexpr int W = KS == 32 ? 1 : SA_WARPS;  // one round of 32 keys: one warp per (b, h)
+        return launch_kernel(self_attn_batch_kernel<F, KS, W>, dim3(B * H), dim3(W * 32), sa_smem_bytes<F>(KS, hd),
                              s, q, kv_new, kv, pos, B, H, KVH, hd, scale, out, lo_off);
     };
     using T_ = std::true_type;

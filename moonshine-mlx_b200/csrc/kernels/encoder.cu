@@ -18,7 +18,6 @@ namespace {
 constexpr int FF_WARPS = 8;
 constexpr int MAX_FRAME = 128;
 
-__device__ __forceinline__ void store_feature(float* p, float v) { *p = v; }
 __device__ __forceinline__ void store_feature(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
 
 // One frame (warp): CMVN, asinh, Linear + SiLU into the output row o; fr is the warp's
@@ -58,18 +57,75 @@ frame_features_kernel(const float* __restrict__ audio, int n_frames, int frame_l
     frame_feature(audio + (size_t)f * frame_len, frame_len, log_k, w, dim, out + (size_t)f * ld_out, fr[wid], lane);
 }
 
-// The same for many streams at once: stream z's nf[z] frames start at audio + aoff[z] and its
-// rows at out[z] (ld_out apart).
-__global__ void __launch_bounds__(FF_WARPS * 32)
-frame_features_batch_kernel(const float* __restrict__ audio, const long long* __restrict__ aoff,
-                            const int* __restrict__ nf, float* const* __restrict__ out, int frame_len,
-                            const float* __restrict__ log_k, const float* __restrict__ w, int dim, int ld_out) {
-    __shared__ float fr[FF_WARPS][MAX_FRAME];
+// Frame features of FFB_FRAMES frames per CTA (fp32 out): each warp normalises frames into
+// shared memory as frame_feature does, then thread j computes output j of every frame of the
+// CTA, so a weight row is read once per CTA instead of once per frame.  Each output is summed
+// in the same order as frame_feature's (bitwise the same values).
+constexpr int FFB_FRAMES = 16, FFB_THREADS = 256;
+
+__device__ __forceinline__ void frame_features_block(const float* __restrict__ a, int nf, int frame_len,
+                                                     const float* __restrict__ log_k, const float* __restrict__ w,
+                                                     int dim, float* __restrict__ out, int ld_out, bool w4) {
+    __shared__ __align__(16) float fr[FFB_FRAMES][MAX_FRAME];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int z = blockIdx.y, f = blockIdx.x * FF_WARPS + wid;
-    if (f >= nf[z]) return;
-    frame_feature(audio + aoff[z] + (size_t)f * frame_len, frame_len, log_k, w, dim,
-                  out[z] + (size_t)f * ld_out, fr[wid], lane);
+    const int f0 = blockIdx.x * FFB_FRAMES;
+    const int nfb = min(FFB_FRAMES, nf - f0);
+    if (nfb <= 0) return;  // whole CTA
+    for (int f = wid; f < nfb; f += FFB_THREADS / 32) {
+        const float* af = a + (size_t)(f0 + f) * frame_len;
+        float s = 0.f;
+        for (int i = lane; i < frame_len; i += 32) s += af[i];
+        const float mean = warp_sum(s) / (float)frame_len;
+        float v = 0.f;
+        for (int i = lane; i < frame_len; i += 32) {
+            const float c = af[i] - mean;
+            v += c * c;
+        }
+        const float rms = sqrtf(warp_sum(v) / (float)frame_len + 1e-6f);
+        const float k = expf(*log_k);
+        for (int i = lane; i < frame_len; i += 32) fr[f][i] = asinhf(k * ((af[i] - mean) / rms));
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < dim; j += FFB_THREADS) {
+        const float* wr = w + (size_t)j * frame_len;
+        float acc[FFB_FRAMES];
+#pragma unroll
+        for (int f = 0; f < FFB_FRAMES; ++f) acc[f] = 0.f;
+        if (w4) {  // frame_len % 4 == 0 and 16-byte aligned rows
+            for (int i = 0; i < frame_len; i += 4) {
+                const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + i));
+#pragma unroll
+                for (int f = 0; f < FFB_FRAMES; ++f) {
+                    const float4 x = *reinterpret_cast<const float4*>(&fr[f][i]);
+                    acc[f] = fmaf(x.w, wv.w, fmaf(x.z, wv.z, fmaf(x.y, wv.y, fmaf(x.x, wv.x, acc[f]))));
+                }
+            }
+        } else {
+            for (int i = 0; i < frame_len; ++i) {
+                const float wv = __ldg(wr + i);
+#pragma unroll
+                for (int f = 0; f < FFB_FRAMES; ++f) acc[f] = fmaf(fr[f][i], wv, acc[f]);
+            }
+        }
+#pragma unroll
+        for (int f = 0; f < FFB_FRAMES; ++f)
+            if (f < nfb) out[(size_t)(f0 + f) * ld_out + j] = silu(acc[f]);
+    }
+}
+
+__global__ void __launch_bounds__(FFB_THREADS)
+frame_features_block_kernel(const float* __restrict__ audio, int n_frames, int frame_len, const float* __restrict__ log_k,
+                            const float* __restrict__ w, int dim, float* __restrict__ out, int ld_out, int w4) {
+    frame_features_block(audio, n_frames, frame_len, log_k, w, dim, out, ld_out, w4 != 0);
+}
+
+__global__ void __launch_bounds__(FFB_THREADS)
+frame_features_block_batch_kernel(const float* __restrict__ audio, const long long* __restrict__ aoff,
+                                  const int* __restrict__ nf, float* const* __restrict__ out, int frame_len,
+                                  const float* __restrict__ log_k, const float* __restrict__ w, int dim, int ld_out,
+                                  int w4) {
+    const int z = blockIdx.y;
+    frame_features_block(audio + aoff[z], nf[z], frame_len, log_k, w, dim, out[z], ld_out, w4 != 0);
 }
 
 // dst[z][0 .. n[z]) = src[z][0 .. n[z]) (zeros where src[z] is null); n[z] % 4 == 0, 16-byte
@@ -466,8 +522,9 @@ cudaError_t launch_frame_features(const float* audio, int n_frames, int frame_le
     if (n_frames <= 0) return cudaSuccess;
     if (frame_len > MAX_FRAME) return cudaErrorInvalidValue;
     ++launch_counter();
-    frame_features_kernel<float><<<(n_frames + FF_WARPS - 1) / FF_WARPS, FF_WARPS * 32, 0, stream>>>(
-        audio, n_frames, frame_len, log_k, w, dim, out, ld_out);
+    const int w4 = (frame_len % 4 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) ? 1 : 0;
+    frame_features_block_kernel<<<(n_frames + FFB_FRAMES - 1) / FFB_FRAMES, FFB_THREADS, 0, stream>>>(
+        audio, n_frames, frame_len, log_k, w, dim, out, ld_out, w4);
     return cudaGetLastError();
 }
 
@@ -477,8 +534,9 @@ cudaError_t launch_frame_features_batch(const float* audio, const long long* aof
     if (nb <= 0 || nf_max <= 0) return cudaSuccess;
     if (frame_len > MAX_FRAME || nb > 65535) return cudaErrorInvalidValue;
     ++launch_counter();
-    frame_features_batch_kernel<<<dim3((nf_max + FF_WARPS - 1) / FF_WARPS, nb), FF_WARPS * 32, 0, stream>>>(
-        audio, aoff, nf, out, frame_len, log_k, w, dim, ld_out);
+    const int w4 = (frame_len % 4 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) ? 1 : 0;
+    frame_features_block_batch_kernel<<<dim3((nf_max + FFB_FRAMES - 1) / FFB_FRAMES, nb), FFB_THREADS, 0, stream>>>(
+        audio, aoff, nf, out, frame_len, log_k, w, dim, ld_out, w4);
     return cudaGetLastError();
 }
 
