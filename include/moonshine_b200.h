@@ -311,7 +311,12 @@ typedef struct {
                                     pass and decodes them in lockstep on tensor cores (the
                                     batched engine; fp32 checkpoints keep fp32-level products,
                                     bf16 ones bf16), so ids match a per-stream call except
-                                    where the top two logits are closer than that precision */
+                                    where the top two logits are closer than that precision.
+                                    The pass runs each encoder layer over the rows whose value
+                                    can have changed since the stream's previous call plus
+                                    their left attention context (the committed memory rows
+                                    are those of the reference's window); 2 re-encodes each
+                                    stream's whole window instead, as the reference does */
     float temperature;           /* transcribe(temperature:) (:122-128): 0 greedy (default);
                                     > 0 draws each token from softmax(logits / temperature)
                                     (decodeMemory, :238-268) by the Gumbel-max trick */
@@ -353,6 +358,9 @@ ms_status ms_stream_emitted(ms_stream* stream, int32_t* ids_out, int32_t cap,
                             int32_t* n_out);
 /* Frames currently in the segment's memory (StreamingState.memoryLen, :26-27). */
 int32_t ms_stream_memory_len(const ms_stream* stream);
+/* The segment's memory rows (StreamingState.memory, :24-25): memory_len x hidden floats into
+ * memory_out (cap_floats of room; MS_ERR_CAPACITY, with *rows_out set, when it is too small). */
+ms_status ms_stream_memory(ms_stream* stream, float* memory_out, int64_t cap_floats, int32_t* rows_out);
 
 /* transcribe over many streams at once (no counterpart in the reference).  Each stream's
  * new frames are encoded on its own; with config->batch_decode == 0 each stream is then

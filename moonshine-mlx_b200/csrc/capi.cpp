@@ -862,15 +862,28 @@ ms_status ms_stream_transcribe_batch(ms_stream* const* streams, int32_t n, int32
                 std::vector<StreamState::EncPlan> plan(n);
                 std::vector<char> has(n, 0);
                 std::vector<BatchEngine::StreamWindow> wins;
+                std::vector<BatchEngine::StreamIncWindow> incs;
+                // batch_decode 1: each layer over the rows that can have changed (incremental);
+                // 2: the whole window again every call, as the reference does
+                const bool incremental = sc.batch_decode != 2;
                 for (int32_t i = 0; i < n; ++i) {
                     StreamState* s = reinterpret_cast<StreamState*>(streams[i]);
                     s->note_call();
                     has[i] = s->plan_new_frames(is_final != 0, &plan[i], shared->stream) ? 1 : 0;
-                    if (has[i])
+                    if (!has[i]) continue;
+                    if (incremental && s->enc_inc) {
+                        incs.push_back({s->features.as<float>(), s->inc_buffers(shared->stream), s->feat_count,
+                                        s->enc_valid, s->encoder_frames_emitted, plan[i].nnew, s->pos_offset,
+                                        s->memory_row()});
+                        s->enc_valid = s->feat_count;
+                    } else {
                         wins.push_back({s->window(plan[i]), plan[i].T, plan[i].off, plan[i].nnew, s->pos_offset,
                                         s->memory_row()});
+                        s->enc_inc = false;
+                    }
                 }
                 be.encode_windows(wins);
+                be.encode_windows_inc(incs);
                 // the cross K/V of every stream's new memory rows in one launch
                 std::vector<StreamState*> enc_ss;
                 std::vector<StreamState::EncPlan> enc_plans;
@@ -958,6 +971,24 @@ ms_status ms_stream_emitted(ms_stream* stream, int32_t* ids_out, int32_t cap, in
 int32_t ms_stream_memory_len(const ms_stream* stream) {
     if (!stream) return 0;
     return reinterpret_cast<const StreamState*>(stream)->memory_len;
+}
+
+ms_status ms_stream_memory(ms_stream* stream, float* memory_out, int64_t cap_floats, int32_t* rows_out) {
+    return guarded([&]() -> ms_status {
+        if (!stream || !rows_out || cap_floats < 0 || (cap_floats > 0 && !memory_out))
+            return fail(MS_ERR_INVALID_ARG, "bad argument");
+        StreamState* s = reinterpret_cast<StreamState*>(stream);
+        std::lock_guard<std::mutex> g(s->model->mu);
+        MSB_CUDA(cudaSetDevice(s->model->device));
+        *rows_out = s->memory_len;
+        const int64_t need = (int64_t)s->memory_len * s->model->cfg.hidden;
+        if (need > cap_floats) return fail(MS_ERR_CAPACITY, "memory buffer too small");
+        if (need > 0)
+            MSB_CUDA(cudaMemcpyAsync(memory_out, s->memory.p, (size_t)need * 4, cudaMemcpyDeviceToHost,
+                                     s->model->stream));
+        MSB_CUDA(cudaStreamSynchronize(s->model->stream));
+        return MS_OK;
+    });
 }
 
 }  // extern "C"

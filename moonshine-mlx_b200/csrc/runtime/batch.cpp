@@ -401,10 +401,11 @@ size_t BatchEngine::enc_rows_capacity(size_t rows3) {
     return erows_cap;
 }
 
-// Encoder layers (MoonshineLayers.swift:297-310) over X = ex [rows3, e_hidden] in segments of
-// R3 rows; attention of segment s sees its first seg_len[s] rows only.  Uses eh, eqkv, eattn
+// Encoder layers l0 .. l1 - 1 (all by default; MoonshineLayers.swift:297-310) over
+// X = ex [rows3, e_hidden] in segments of R3 rows; attention of segment s sees its first
+// seg_len[s] rows only.  Uses eh, eqkv, eattn
 // and ef (grown here) and the encoder weights (split operands for fp32 checkpoints).
-void BatchEngine::encoder_layers_tc(size_t rows3, int R3, const int* seg_len) {
+void BatchEngine::encoder_layers_tc(size_t rows3, int R3, const int* seg_len, int l0, int l1) {
     const Config& c = m.cfg;
     const int ed = c.e_hidden, hd = c.e_head_dim, EI = c.e_inter;
     const int eHD = c.e_heads * hd, QKV = (c.e_heads + 2 * c.e_kv_heads) * hd;
@@ -430,7 +431,7 @@ void BatchEngine::encoder_layers_tc(size_t rows3, int R3, const int* seg_len) {
     const CUtensorMap* attn_lo = esplit ? &a_attn_lo : nullptr;
     const CUtensorMap* f_lo = esplit ? &a_f_lo : nullptr;
     const float scale = std::pow((float)hd, -0.5f);
-    for (int i = 0; i < c.e_layers; ++i) {
+    for (int i = l0; i < (l1 < 0 ? c.e_layers : l1); ++i) {
         const EncLayer& L = m.enc[i];
         const EncLayerB& E = elayers[i];
         MSB_CUDA(launch_ln_bf16(X, (int)rows3, ed, L.ln_in, eh.as<__nv_bfloat16>(), s, 1.0f, lo_h));
@@ -698,6 +699,105 @@ bool BatchEngine::encode_windows(const std::vector<StreamWindow>& w) {
     MSB_CUDA(cudaMemcpyAsync(&st_word, status.p, 4, cudaMemcpyDeviceToHost, s));
     MSB_CUDA(cudaStreamSynchronize(s));  // also: the host table is read
     throw_device_status(st_word, "tensor-core stream encoder");
+    return true;
+}
+
+bool BatchEngine::encode_windows_inc(const std::vector<StreamIncWindow>& w) {
+    if (w.empty()) return true;
+    if (!tc_encoder_fits()) return false;
+    const Config& c = m.cfg;
+    const int ed = c.e_hidden, B = (int)w.size(), L = c.e_layers;
+    ensure_enc_weights();
+    cudaStream_t s = m.stream;
+    grow(status, 16);
+    // right context summed over layers 0..l
+    std::vector<int> Ssum(L);
+    for (int l = 0, acc = 0; l < L; ++l) Ssum[l] = (acc += std::max(0, c.window(l).second));
+    // per layer and stream: rows recomputed from c (earlier ones final), segment from s0 (left
+    // attention context of row c), n = total - s0 rows
+    std::vector<int> R(L, 1);
+    std::vector<int> c0((size_t)L * B), s0((size_t)L * B);
+    int max_new = 1;
+    size_t rows_max = 0;
+    for (int l = 0; l < L; ++l) {
+        const int left = std::max(0, c.window(l).first);
+        for (int b = 0; b < B; ++b) {
+            const StreamIncWindow& x = w[b];
+            const int cl = std::max(0, std::min(x.prev, x.total) - Ssum[l]);
+            const int sl = std::max(0, cl - left);
+            c0[(size_t)l * B + b] = cl;
+            s0[(size_t)l * B + b] = sl;
+            R[l] = std::max(R[l], x.total - sl);
+        }
+        rows_max = std::max(rows_max, (size_t)B * R[l]);
+    }
+    for (const auto& x : w) {
+        max_new = std::max(max_new, x.nnew);
+        if ((int)x.layer_out.size() != L - 1 || x.emitted < 0 || x.emitted + x.nnew > x.total)
+            throw MsError(MS_ERR_INVALID_ARG, "incremental encoder: bad stream window");
+    }
+    grow(ex, enc_rows_capacity(rows_max) * ed * 4);
+    float* X = ex.as<float>();
+    // tables (each array 16-byte aligned), per layer: gather src[B], gather rows[B]; copy
+    // src[B], dst[B], floats[B] (layers but the last); then memory dst[B], off[B], cnt[B], pos[B]
+    const size_t P8 = ((size_t)B * 8 + 15) & ~(size_t)15, P4 = ((size_t)B * 4 + 15) & ~(size_t)15;
+    const size_t o_gT = P8, o_csrc = P8 + P4, o_cdst = 2 * P8 + P4, o_ccnt = 3 * P8 + P4;
+    const size_t per_layer = 3 * P8 + 2 * P4, fin = P8 + 3 * P4;
+    const size_t bytes = (size_t)L * per_layer + fin;
+    char* h = inc_tables.host(bytes);
+    for (int l = 0; l < L; ++l) {
+        char* t = h + (size_t)l * per_layer;
+        const float** gsrc = reinterpret_cast<const float**>(t);
+        int* gT = reinterpret_cast<int*>(t + o_gT);
+        const float** csrc = reinterpret_cast<const float**>(t + o_csrc);
+        float** cdst = reinterpret_cast<float**>(t + o_cdst);
+        int* ccnt = reinterpret_cast<int*>(t + o_ccnt);
+        for (int b = 0; b < B; ++b) {
+            const StreamIncWindow& x = w[b];
+            const int cl = c0[(size_t)l * B + b], sl = s0[(size_t)l * B + b];
+            gsrc[b] = (l == 0 ? x.feat : x.layer_out[l - 1]) + (size_t)sl * ed;
+            gT[b] = x.total - sl;
+            // layer l's recomputed rows c .. total of segment b into the stream's layer-l rows
+            csrc[b] = X + ((size_t)b * R[l] + (cl - sl)) * ed;
+            cdst[b] = l < L - 1 ? x.layer_out[l] + (size_t)cl * ed : nullptr;
+            ccnt[b] = (x.total - cl) * ed;
+        }
+    }
+    {
+        char* t = h + (size_t)L * per_layer;
+        float** dst = reinterpret_cast<float**>(t);
+        int* off = reinterpret_cast<int*>(t + P8);
+        int* cnt = reinterpret_cast<int*>(t + P8 + P4);
+        int* pos = reinterpret_cast<int*>(t + P8 + 2 * P4);
+        for (int b = 0; b < B; ++b) {
+            dst[b] = w[b].dst;
+            off[b] = w[b].emitted - s0[(size_t)(L - 1) * B + b];
+            cnt[b] = w[b].nnew;
+            pos[b] = w[b].pos;
+        }
+    }
+    MSB_CUDA(cudaMemsetAsync(status.p, 0, 16, s));
+    char* d = inc_tables.upload(bytes, s, m.streams_pool());
+    for (int l = 0; l < L; ++l) {
+        const char* t = d + (size_t)l * per_layer;
+        const int* gT = reinterpret_cast<const int*>(t + o_gT);
+        const size_t rows = (size_t)B * R[l];
+        MSB_CUDA(launch_gather_seg_rows(reinterpret_cast<const float* const*>(t), gT, B, R[l], ed, X, s));
+        encoder_layers_tc(rows, R[l], gT, l, l + 1);
+        if (l < L - 1)
+            MSB_CUDA(launch_copy_rows_batch(reinterpret_cast<const float* const*>(t + o_csrc),
+                                            reinterpret_cast<float* const*>(t + o_cdst),
+                                            reinterpret_cast<const int*>(t + o_ccnt), B, s));
+    }
+    const char* t = d + (size_t)L * per_layer;
+    MSB_CUDA(launch_ln_scatter_rows(X, B, max_new, R[L - 1], ed, m.enc_final, 1.0f, 1e-5f, m.pos_emb,
+                                    reinterpret_cast<const int*>(t + P8), reinterpret_cast<const int*>(t + P8 + P4),
+                                    reinterpret_cast<const int*>(t + P8 + 2 * P4),
+                                    reinterpret_cast<float* const*>(t), s));
+    unsigned st_word = 0;
+    MSB_CUDA(cudaMemcpyAsync(&st_word, status.p, 4, cudaMemcpyDeviceToHost, s));
+    MSB_CUDA(cudaStreamSynchronize(s));
+    throw_device_status(st_word, "tensor-core incremental stream encoder");
     return true;
 }
 

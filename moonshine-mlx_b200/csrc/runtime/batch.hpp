@@ -65,6 +65,23 @@ struct BatchEngine {
         float* dst;         // the stream's memory at its current length
     };
     bool encode_windows(const std::vector<StreamWindow>& w);
+    // The same result for the new rows with each layer run only over the rows whose value can
+    // have changed since the stream's previous incremental encode, plus their left attention
+    // context: a stream keeps every layer's output rows (`layer_out`, one buffer per layer but
+    // the last).  A layer-l output row r depends on features up to r + (right contexts of
+    // layers 0..l), so rows below prev - that sum were final at the previous encode (prev =
+    // the feature count then) and are kept; from there on they are recomputed with the band
+    // clipped at the current feature count, exactly as the reference's window does.  The
+    // window's left edge never reaches a committed row's receptive field (16 frames per
+    // layer of left context), so the committed rows are the window's.
+    struct StreamIncWindow {
+        const float* feat;                // the segment's features [total, e_hidden]
+        std::vector<float*> layer_out;    // [e_layers - 1] buffers of >= total rows
+        int total, prev;                  // feature count now / at the previous incremental encode
+        int emitted, nnew, pos;           // new memory rows: frames emitted .. emitted + nnew
+        float* dst;                       // the stream's memory at its current length
+    };
+    bool encode_windows_inc(const std::vector<StreamIncWindow>& w);
     bool tc_encoder_fits() const;  // the dims the tensor-core encoder supports
 
    private:
@@ -105,7 +122,8 @@ struct BatchEngine {
     // rows.  false when the dims do not fit (the caller keeps the per-utterance path).
     bool encode_tc(const std::vector<const float*>& audio_dev, const std::vector<int64_t>& n_samples,
                    const std::vector<int>& off, const std::vector<int>& fr);
-    void encoder_layers_tc(size_t rows3, int R3, const int* seg_len);
+    void encoder_layers_tc(size_t rows3, int R3, const int* seg_len, int l0 = 0, int l1 = -1);
+    TableUpload inc_tables;  // launch tables of encode_windows_inc
     size_t erows_cap = 0;
     size_t enc_rows_capacity(size_t rows3);
     DevBuf wtab;  // device tables of encode_windows

@@ -56,6 +56,8 @@ void StreamState::start() {  // MoonshineStreaming.swift:74-78
 
 void StreamState::reset_segment() {  // MoonshineStreaming.swift:217-226
     feat_count = 0;
+    enc_valid = 0;
+    enc_inc = true;
     encoder_frames_emitted = 0;
     pos_offset = 0;
     memory_len = 0;
@@ -377,6 +379,21 @@ void StreamState::commit_new_frames(const EncPlan& p, cudaStream_t s) {
     advance_new_frames(p);
 }
 
+std::vector<float*> StreamState::inc_buffers(cudaStream_t s) {
+    Model& m = *model;
+    const int L = m.cfg.e_layers, ed = m.cfg.e_hidden;
+    if (!enc_x) enc_x.reset(new DevBuf[std::max(1, L - 1)]);
+    if (feat_count > enc_rows) {
+        const int cap = std::max(feat_count, std::max(2 * enc_rows, 256));
+        for (int l = 0; l < L - 1; ++l)
+            grow_keep(enc_x[l], (size_t)enc_valid * ed * 4, (size_t)cap * ed * 4, s, m.streams_pool());
+        enc_rows = cap;
+    }
+    std::vector<float*> out((size_t)std::max(0, L - 1));
+    for (int l = 0; l < L - 1; ++l) out[l] = enc_x[l].as<float>();
+    return out;
+}
+
 void StreamState::advance_new_frames(const EncPlan& p) {
     pos_offset += p.nnew;
     encoder_frames_emitted = p.stable;
@@ -419,6 +436,7 @@ void StreamState::encode_new_frames(bool is_final, EncLane* lane) {  // Moonshin
     const cudaStream_t s = lane ? lane->stream : m.stream;
     EncPlan p;
     if (!plan_new_frames(is_final, &p, s)) return;
+    enc_inc = false;  // the incremental encoder's layer rows do not follow this encode
     const int ed = c.e_hidden;
     eb.x->ensure((size_t)p.T * ed * 4);
     float* x = eb.x->as<float>();

@@ -2,6 +2,7 @@
 // with its frontend conv buffers, features, memory and cross K/V resident on the device.
 #pragma once
 
+#include <memory>
 #include <vector>
 
 #include "model.hpp"
@@ -32,6 +33,13 @@ struct StreamState {
     DevBuf memory, cross32, cross16;
     int memory_len = 0, mem_cap = 0;
     bool cross_f16 = false;
+    // incremental encoder (batched transcribe): every encoder layer's output rows of the
+    // segment so far ([e_layers - 1] buffers of enc_rows rows), valid up to the feature count
+    // of the last incremental encode (enc_valid; rows past its final ones are recomputed);
+    // enc_inc false once another encode path has advanced the segment (until its reset)
+    std::unique_ptr<DevBuf[]> enc_x;
+    int enc_rows = 0, enc_valid = 0;
+    bool enc_inc = true;
     std::vector<std::vector<int32_t>> emitted;
     bool last_hit_eos = false;
     bool active = false;
@@ -72,6 +80,9 @@ struct StreamState {
     // commit_new_frames without the cross K/V (computed by the caller, e.g. for many streams
     // at once by commit_new_frames_batch)
     void advance_new_frames(const EncPlan& p);
+    // The incremental encoder's layer-output buffers, grown (stream-ordered on s, keeping the
+    // valid rows) to hold feat_count rows; one pointer per layer but the last.
+    std::vector<float*> inc_buffers(cudaStream_t s);
     int64_t decode_limit(bool is_final, int32_t max_tokens, Result* done_early);
     Result finish(std::vector<int32_t> ids, bool hit_eos, bool is_final, const ms_streaming_config& sc);
 

@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import weakref
 from dataclasses import dataclass, field
 from typing import Callable, List, Optional, Sequence, Tuple
 
@@ -144,6 +145,7 @@ def _load_lib() -> C.CDLL:
                                                  C.c_int32, i32p, i32p, i32p]),
         "ms_stream_emitted": (C.c_int, [P, i32p, C.c_int32, i32p]),
         "ms_stream_memory_len": (C.c_int32, [P]),
+        "ms_stream_memory": (C.c_int, [P, C.POINTER(C.c_float), C.c_int64, i32p]),
         "ms_enable_decode_trace": (C.c_int, [P, C.c_int32]),
         "ms_decode_trace": (C.c_int, [P, C.POINTER(C.c_uint64), C.c_int32, i32p]),
         "ms_last_error": (C.c_char_p, []),
@@ -296,10 +298,14 @@ class StreamingConfig:
     """StreamingConfig (MoonshineStreaming.swift:47-62)."""
     max_memory_frames: int = 100000
     min_segment_frames: int = 250
-    batch_decode: bool = False   # transcribe_batch: lockstep bf16 decode of all streams
+    # transcribe_batch: 1 (or True) encodes all streams' new frames in one tensor-core pass,
+    # each encoder layer over the rows that can have changed since the stream's previous call,
+    # and decodes in lockstep; 2 the same but re-encoding each stream's whole window, as the
+    # reference does (same memory rows to rounding)
+    batch_decode: int = 0
 
     def _c(self, temperature: float = 0.0, seed: int = 0) -> _StreamingConfig:
-        return _StreamingConfig(self.max_memory_frames, self.min_segment_frames, 1 if self.batch_decode else 0,
+        return _StreamingConfig(self.max_memory_frames, self.min_segment_frames, int(self.batch_decode),
                                 float(temperature), int(seed) & 0x7FFFFFFF)
 
 
@@ -315,10 +321,20 @@ class StreamingState:
     def memory_len(self) -> int:
         return int(_L().ms_stream_memory_len(self._h))
 
+    def memory(self) -> np.ndarray:
+        """The segment's memory rows (StreamingState.memory, MoonshineStreaming.swift:24-25),
+        [memory_len, hidden] float32."""
+        hidden = self._model.config.hidden_size
+        out = np.zeros((max(self.memory_len, 0), hidden), dtype=np.float32)
+        rows = C.c_int32()
+        _check(_L().ms_stream_memory(self._h, _fptr(out), out.size, C.byref(rows)))
+        return out[: rows.value]
+
     def close(self):
-        if self._h:
+        # a stream is freed before its model (MoonshineModel.close frees the live ones first)
+        if self._h and self._model._h:
             _L().ms_stream_free(self._h)
-            self._h = None
+        self._h = None
 
     def __del__(self):
         try:
@@ -330,6 +346,7 @@ class StreamingState:
 class MoonshineModel:
     def __init__(self, handle):
         self._h = handle
+        self._streams = weakref.WeakSet()  # live streams, freed before the model
         cfg = _ModelConfig()
         _check(_L().ms_model_get_config(self._h, C.byref(cfg)))
         self.config = cfg
@@ -368,6 +385,8 @@ class MoonshineModel:
 
     def close(self):
         if self._h:
+            for st in list(self._streams):
+                st.close()
             _L().ms_model_free(self._h)
             self._h = None
 
@@ -618,7 +637,9 @@ class MoonshineModel:
     def create_stream(self) -> StreamingState:
         h = C.c_void_p()
         _check(_L().ms_stream_create(self._h, C.byref(h)))
-        return StreamingState(h, self)
+        st = StreamingState(h, self)
+        self._streams.add(st)
+        return st
 
     def start_stream(self, state: StreamingState) -> None:
         _check(_L().ms_stream_start(state._h))

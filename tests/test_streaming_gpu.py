@@ -139,6 +139,43 @@ def test_stream_batch_ragged_and_repeated(model_root):
         assert [s.memory_len for s in streams] == [s.memory_len for s in singles]
 
 
+def test_stream_incremental_encoder_matches_window(model_root):
+    """transcribe_batch's incremental encoder (batch_decode 1: each layer recomputes only the
+    rows that can have changed since the stream's previous call, plus their left attention
+    context) against re-encoding each stream's whole window as the reference's
+    encodeNewFrames does (batch_decode 2, MoonshineStreaming.swift:178-214): the same memory
+    rows after every call, to fp32 rounding (the two passes differ only in how their GEMMs
+    split K), through the left-context limit of 16 frames per layer, ragged chunks, a call
+    with no new stable frames and the final call."""
+    import moonshine_b200 as mb
+    d = model_dir(model_root, "tiny")
+    m = mb.MoonshineModel.load(d)
+    n_streams = 3
+    inc = [m.create_stream() for _ in range(n_streams)]
+    win = [m.create_stream() for _ in range(n_streams)]
+    for s in inc + win:
+        m.start_stream(s)
+    sizes = [1280] * 30 + [320, 2000, 1280, 90, 4000] + [1280] * 12
+    audios = [synth.synth_audio(sum(sizes), 60 + i) for i in range(n_streams)]
+    sc_inc, sc_win = mb.StreamingConfig(batch_decode=1), mb.StreamingConfig(batch_decode=2)
+    off, longest = 0, 0
+    for k, n in enumerate(sizes):
+        final = k == len(sizes) - 1
+        pieces = [a[off:off + n] for a in audios]
+        off += n
+        m.add_audio_batch(inc, pieces)
+        m.add_audio_batch(win, pieces)
+        m.transcribe_batch(inc, is_final=final, streaming_config=sc_inc, max_tokens=8)
+        m.transcribe_batch(win, is_final=final, streaming_config=sc_win, max_tokens=8)
+        for a, b in zip(inc, win):
+            ma, mb_ = a.memory(), b.memory()
+            assert ma.shape == mb_.shape, (k, ma.shape, mb_.shape)
+            if ma.size:
+                assert float(np.abs(ma - mb_).max()) <= 1e-4 * max(1.0, float(np.abs(mb_).max())), k
+            longest = max(longest, ma.shape[0])
+    assert longest > 16 * 6  # past the window's left context (the final call resets the segment)
+
+
 def test_stream_batch_decode_lockstep(model_root):
     """transcribe_batch with batch_decode: 4 streams fed 80 ms chunks, every call's segment
     decoded in lockstep on the tensor cores (split bf16 operands for this fp32 checkpoint).
