@@ -842,8 +842,8 @@ cudaError_t launch_tc_mode(const CUtensorMap& map_a, const CUtensorMap& map_b, c
     switch (g.mode) {
         case TC_EPI_STD:
             // more tiles than SMs: the persistent form overlaps each tile's epilogue with the
-            // next tile's loads and MMAs
-            if (g.splits == 1 && ntiles > num_sms())
+            // next tile's loads and MMAs (its epilogue has no folded LayerNorm)
+            if (g.splits == 1 && ntiles > num_sms() && !g.lnf.stats)
                 return launch_tc_persist<BN, SP>(map_a, map_b, map_a_lo, map_b_lo, g, stream, ntiles);
             return launch_tc<BN, TC_EPI_STD, SP>(map_a, map_b, map_a_lo, map_b_lo, g, stream);
         case TC_EPI_ROPE_KV: return launch_tc<BN, TC_EPI_ROPE_KV, SP>(map_a, map_b, map_a_lo, map_b_lo, g, stream);
