@@ -358,7 +358,7 @@ ms_status ms_stream_emitted(ms_stream* stream, int32_t* ids_out, int32_t cap,
                             int32_t* n_out);
 /* Frames currently in the segment's memory (StreamingState.memoryLen, :26-27). */
 int32_t ms_stream_memory_len(const ms_stream* stream);
-/* The segment's memory rows (StreamingState.memory, :24-25): memory_len x hidden floats into
+/* The segment's memory rows (StreamingState.memory, :25-26): memory_len x hidden floats into
  * memory_out (cap_floats of room; MS_ERR_CAPACITY, with *rows_out set, when it is too small). */
 ms_status ms_stream_memory(ms_stream* stream, float* memory_out, int64_t cap_floats, int32_t* rows_out);
 

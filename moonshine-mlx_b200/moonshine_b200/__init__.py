@@ -322,7 +322,7 @@ class StreamingState:
         return int(_L().ms_stream_memory_len(self._h))
 
     def memory(self) -> np.ndarray:
-        """The segment's memory rows (StreamingState.memory, MoonshineStreaming.swift:24-25),
+        """The segment's memory rows (StreamingState.memory, MoonshineStreaming.swift:25-26),
         [memory_len, hidden] float32."""
         hidden = self._model.config.hidden_size
         out = np.zeros((max(self.memory_len, 0), hidden), dtype=np.float32)
