@@ -139,7 +139,8 @@ def test_stream_batch_ragged_and_repeated(model_root):
         assert [s.memory_len for s in streams] == [s.memory_len for s in singles]
 
 
-def test_stream_incremental_encoder_matches_window(model_root):
+@pytest.mark.parametrize("windows", [None, [[8, 2], [12, 3], [16, 0], [5, 4], [16, 1], [16, 4]]])
+def test_stream_incremental_encoder_matches_window(model_root, tmp_path, windows):
     """transcribe_batch's incremental encoder (batch_decode 1: each layer recomputes only the
     rows that can have changed since the stream's previous call, plus their left attention
     context) against re-encoding each stream's whole window as the reference's
@@ -149,6 +150,8 @@ def test_stream_incremental_encoder_matches_window(model_root):
     with no new stable frames and the final call."""
     import moonshine_b200 as mb
     d = model_dir(model_root, "tiny")
+    if windows is not None:  # right context in most layers, left windows of several sizes
+        d = with_config(d, str(tmp_path / "w"), **{"encoder_config.sliding_windows": windows})
     m = mb.MoonshineModel.load(d)
     n_streams = 3
     inc = [m.create_stream() for _ in range(n_streams)]
