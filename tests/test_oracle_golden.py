@@ -18,11 +18,13 @@ def _oracle_for(fx):
     if int(fx["overrides_maxpos"]) != 4096:
         ov["max_position_embeddings"] = int(fx["overrides_maxpos"])
     cfg = synth.make_config(arch, **ov)
+    if "rotary_factor" in fx.files:
+        cfg["rope_parameters"]["partial_rotary_factor"] = float(fx["rotary_factor"])
     w = synth.make_weights(cfg, int(fx["seed"]))
     return Oracle(ModelConfig.from_dict(cfg), sanitize_weights(w), np.float64)
 
 
-@pytest.mark.parametrize("name", ["hf_tiny", "hf_small_v2048"])
+@pytest.mark.parametrize("name", ["hf_tiny", "hf_small_v2048", "hf_small_rot48", "hf_medium_rot48"])
 def test_oracle_matches_hf_fixture(name):
     fx = np.load(os.path.join(GOLDEN, name + ".npz"))
     o = _oracle_for(fx)
