@@ -69,3 +69,39 @@ def test_load_without_gpu_reports_cuda_error(tmp_path):
     with pytest.raises(mb.MoonshineError) as ei:
         mb.MoonshineModel.load(str(tmp_path))
     assert ei.value.status in (3, 7)
+
+
+def declared_param_counts():
+    """Number of parameters of every prototype in the header (void -> 0)."""
+    txt = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    out = {}
+    for name, params in re.findall(r"\b(ms_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", txt):
+        p = " ".join(params.split())
+        out[name] = 0 if p in ("", "void") else p.count(",") + 1
+    return out
+
+
+def test_python_bindings_match_the_header_prototypes():
+    """Every function the Python mirror binds takes as many arguments as its C prototype."""
+    import moonshine_b200 as mb
+    L = mb._L()
+    counts = declared_param_counts()
+    bound = 0
+    for name, n in counts.items():
+        fn = getattr(L, name, None)
+        if fn is None or fn.argtypes is None:
+            continue
+        assert len(fn.argtypes) == n, (name, len(fn.argtypes), n)
+        bound += 1
+    assert bound >= 30
+
+
+def test_stream_batch_and_memory_argument_errors():
+    import moonshine_b200 as mb
+    L = mb._L()
+    rows = ctypes.c_int32(-1)
+    assert L.ms_stream_memory(None, None, 0, ctypes.byref(rows)) == 1
+    assert L.ms_stream_add_audio_batch(None, 1, None, None) == 1
+    assert L.ms_stream_add_audio_batch(None, 0, None, None) == 1  # null stream array
+    n = ctypes.c_int32()
+    assert L.ms_stream_transcribe_batch(None, 1, 0, None, 0, None, 0, ctypes.byref(n), None, None) == 1
