@@ -404,6 +404,10 @@ ms_status ms_decode_trace(ms_model* model, uint64_t* stamps_out, int32_t cap, in
 
 /* Library version string. */
 const char* ms_version(void);
+/* sizeof of one of this header's structs by its name ("ms_options", "ms_model_config",
+ * "ms_gen_params", "ms_gen_stats", "ms_alignment", "ms_streaming_config"), 0 for any other
+ * name: a binding in another language checks its own layouts against it at load. */
+size_t ms_struct_size(const char* name);
 
 #ifdef __cplusplus
 }

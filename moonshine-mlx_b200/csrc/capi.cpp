@@ -178,6 +178,18 @@ int64_t ms_kernel_launches(void) { return launch_counter(); }
 void ms_reset_kernel_launches(void) { launch_counter() = 0; }
 const char* ms_version(void) { return "moonshine-b200 0.1 (sm_100a)"; }
 
+size_t ms_struct_size(const char* name) {
+    if (!name) return 0;
+    const std::string n(name);
+    if (n == "ms_options") return sizeof(ms_options);
+    if (n == "ms_model_config") return sizeof(ms_model_config);
+    if (n == "ms_gen_params") return sizeof(ms_gen_params);
+    if (n == "ms_gen_stats") return sizeof(ms_gen_stats);
+    if (n == "ms_alignment") return sizeof(ms_alignment);
+    if (n == "ms_streaming_config") return sizeof(ms_streaming_config);
+    return 0;
+}
+
 ms_status ms_enable_decode_trace(ms_model* model, int32_t enabled) {
     if (!model) return fail(MS_ERR_INVALID_ARG, "null model");
     Model* m = reinterpret_cast<Model*>(model);

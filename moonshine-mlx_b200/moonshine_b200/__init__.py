@@ -152,11 +152,19 @@ def _load_lib() -> C.CDLL:
         "ms_kernel_launches": (C.c_int64, []),
         "ms_reset_kernel_launches": (None, []),
         "ms_version": (C.c_char_p, []),
+        "ms_struct_size": (C.c_size_t, [C.c_char_p]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args
+    # the structs passed by pointer must have the library's layout
+    for cname, cls in (("ms_options", _Options), ("ms_model_config", _ModelConfig), ("ms_gen_params", _GenParams),
+                       ("ms_gen_stats", _GenStats), ("ms_alignment", _Alignment),
+                       ("ms_streaming_config", _StreamingConfig)):
+        if lib.ms_struct_size(cname.encode()) != C.sizeof(cls):
+            raise ImportError(f"{cname}: {C.sizeof(cls)} bytes here, {lib.ms_struct_size(cname.encode())} in "
+                              f"{LIB_PATH} (a library built from another header)")
     return lib
 
 

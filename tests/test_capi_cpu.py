@@ -105,3 +105,14 @@ def test_stream_batch_and_memory_argument_errors():
     assert L.ms_stream_add_audio_batch(None, 0, None, None) == 1  # null stream array
     n = ctypes.c_int32()
     assert L.ms_stream_transcribe_batch(None, 1, 0, None, 0, None, 0, ctypes.byref(n), None, None) == 1
+
+
+def test_struct_layouts_match_the_library():
+    """The ctypes mirrors of the header's structs have the library's sizes (checked at load)."""
+    import moonshine_b200 as mb
+    L = mb._L()
+    for cname, cls in (("ms_options", mb._Options), ("ms_model_config", mb._ModelConfig),
+                       ("ms_gen_params", mb._GenParams), ("ms_gen_stats", mb._GenStats),
+                       ("ms_alignment", mb._Alignment), ("ms_streaming_config", mb._StreamingConfig)):
+        assert L.ms_struct_size(cname.encode()) == ctypes.sizeof(cls) > 0, cname
+    assert L.ms_struct_size(b"ms_nothing") == 0
