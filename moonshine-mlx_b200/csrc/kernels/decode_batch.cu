@@ -670,7 +670,7 @@ cudaError_t launch_self_attn_batch(const float* q, const float* kv_new, const Pa
     ++launch_counter();
     // every position of the call is below table_stride * page: rounds of that many keys (32,
     // 64 or 128), at most KEYS
-    const int reach = kv.table_stride * kv.page;
+    const int reach = kv.reach > 0 ? std::min(kv.reach, kv.table_stride * kv.page) : kv.table_stride * kv.page;
     auto go = [&](auto f16, auto keys) {
         constexpr bool F = decltype(f16)::value;
         constexpr int KS = decltype(keys)::value;

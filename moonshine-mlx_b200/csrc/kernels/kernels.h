@@ -136,6 +136,8 @@ struct PagedKv {
     long long page_elems = 0;     // elements per page (all layers, K and V)
     long long layer_off = 0;      // elements from a page's start to this layer's K
     int kv_f16 = 0;
+    int reach = 0;                // > 0: no position the launch sees reaches this (sizes the
+                                  // self-attention rounds); 0: table_stride * page
 };
 
 // Decoder q|k|v epilogue parameters (row m = batch slot b).

@@ -261,6 +261,7 @@ void BatchEngine::enqueue_step(int B, int max_frames, bool forced, bool first, f
         pk.page_elems = (long long)c.layers * 2 * KVD * kKvPage;
         pk.layer_off = (long long)l * 2 * KVD * kKvPage;
         pk.kv_f16 = m.kv_f16 ? 1 : 0;
+        pk.reach = sa_reach;
         // self-attention block
         {
             TcGemmArgs ga;
@@ -927,27 +928,56 @@ BatchEngine::Result BatchEngine::decode_prepared(int B, int T, int maxM, const s
     auto logits_at = [&](int step) -> float* {
         return want_logits ? logit_buf.as<float>() + (size_t)step * B * c.vocab : nullptr;
     };
+    // step st sees positions 0..st: its self attention needs rounds of at most st + 1 keys
+    auto reach_for = [](int st) { return st < 32 ? 32 : (st < 64 ? 64 : 0); };
+    sa_reach = reach_for(0);
     enqueue_step(B, maxM, forced, true, logits_at(0));
     if (want_logits) {
-        for (int st = 1; st < T; ++st) enqueue_step(B, maxM, forced, false, logits_at(st));
+        for (int st = 1; st < T; ++st) {
+            sa_reach = reach_for(st);
+            enqueue_step(B, maxM, forced, false, logits_at(st));
+        }
     } else if (T > 1) {
-        cudaGraph_t graph = nullptr;
-        cudaGraphExec_t exec = nullptr;
-        MSB_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        // one graph per reach bucket, each replayed for its steps; every graph lives until
+        // the stream has finished with it
+        std::vector<cudaGraph_t> graphs;
+        std::vector<cudaGraphExec_t> execs;
+        auto release = [&]() {
+            for (auto e : execs) cudaGraphExecDestroy(e);
+            for (auto g : graphs) cudaGraphDestroy(g);
+        };
         try {
-            enqueue_step(B, maxM, forced, false, nullptr);
+            for (int st = 1; st < T;) {
+                const int r = reach_for(st);
+                int end = st;
+                while (end < T && reach_for(end) == r) ++end;
+                sa_reach = r;
+                cudaGraph_t graph = nullptr;
+                MSB_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+                try {
+                    enqueue_step(B, maxM, forced, false, nullptr);
+                } catch (...) {
+                    cudaStreamEndCapture(s, &graph);
+                    if (graph) cudaGraphDestroy(graph);
+                    throw;
+                }
+                MSB_CUDA(cudaStreamEndCapture(s, &graph));
+                graphs.push_back(graph);
+                cudaGraphExec_t exec = nullptr;
+                MSB_CUDA(cudaGraphInstantiate(&exec, graph, 0));
+                execs.push_back(exec);
+                for (; st < end; ++st) MSB_CUDA(cudaGraphLaunch(exec, s));
+            }
+            MSB_CUDA(cudaStreamSynchronize(s));
         } catch (...) {
-            cudaStreamEndCapture(s, &graph);
-            if (graph) cudaGraphDestroy(graph);
+            cudaStreamSynchronize(s);
+            release();
+            sa_reach = 0;
             throw;
         }
-        MSB_CUDA(cudaStreamEndCapture(s, &graph));
-        MSB_CUDA(cudaGraphInstantiate(&exec, graph, 0));
-        for (int st = 1; st < T; ++st) MSB_CUDA(cudaGraphLaunch(exec, s));
-        MSB_CUDA(cudaStreamSynchronize(s));
-        cudaGraphExecDestroy(exec);
-        cudaGraphDestroy(graph);
+        release();
     }
+    sa_reach = 0;
     MSB_CUDA(cudaEventRecord(m.ev[2], s));
     res.t_cap = Tc;
     res.steps = T;

@@ -151,6 +151,10 @@ struct BatchEngine {
     bool xrows_on = false;
     void ensure_ws(int B, int T, int Mtot, int maxM);
     void enqueue_step(int B, int max_frames, bool forced, bool first, float* logits);
+    // positions the steps being enqueued can reach (0: the call's limit); the steps of a call
+    // are captured in up to three graphs, for positions below 32, below 64 and the rest, so
+    // that early steps run self attention in shorter rounds (less shared memory per CTA)
+    int sa_reach = 0;
     float inv_temp = 0.f;  // sampling state of the current run
     unsigned seed = 0;
     void gemm(const CUtensorMap& a, const CUtensorMap& b, TcGemmArgs& g, int K, int bn,
